@@ -1,0 +1,309 @@
+"""Generate the golden fixtures in this directory by running the reference itself.
+
+Run from the repository root, in a container where the reference's sources are
+available (they are pure Python on top of PyTorch):
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /root/reference/src
+
+The reference (Abusagit/tabpack, package `tabpackage` 0.0.1) is imported
+unmodified.  Its only source of nondeterminism on the hot path is the dropout
+draw `torch.empty_like(x).bernoulli_(p_keep)` in `DropoutPack.forward`
+(`src/tabpackage/nn.py:897-901`); for the fixtures that call is replaced by the
+counter-based Philox keep mask of `oracle.philox`, injected as the same
+`mask / p_keep` tensor the reference would have multiplied with.  Everything
+else (padded `baddbmm`, masking, depth `where`, autograd, optimizer packs,
+metrics, greedy selection) is the reference's own code path.
+
+Each fixture is an `.npz` of small arrays; `tests/test_oracle_golden.py` pins
+the numpy oracle against them and the GPU tests pin the CUDA path against the
+oracle.
+"""
+
+from __future__ import annotations
+
+import functools
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+
+
+def _import_reference(src: str):
+    sys.path.insert(0, src)
+    sys.path.insert(0, ROOT)
+    import tabpackage  # noqa: F401
+    import tabpackage.ensemble
+    import tabpackage.metrics
+    import tabpackage.nn
+    import tabpackage.optim
+
+    return tabpackage
+
+
+def _np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().numpy().copy()
+
+
+class _PhiloxDropout:
+    """Context manager replacing the Bernoulli draw of `DropoutPack.forward` by
+    the Philox keep mask; the k-th training-mode call uses offset k."""
+
+    def __init__(self, tp, seed: int):
+        self.tp = tp
+        self.seed = seed
+        self.calls = 0
+
+    def __enter__(self):
+        from oracle.layers import dropout_mask_values
+
+        DropoutPack = self.tp.nn.DropoutPack
+        self.orig = DropoutPack.forward
+        ctx = self
+
+        def forward(mod, x, pack_idx=None):
+            if isinstance(mod.p, (int, float)) or not mod.training:
+                return ctx.orig(mod, x, pack_idx)
+            p = mod.p if pack_idx is None else mod.p[pack_idx]
+            members = (np.arange(x.shape[0]) if pack_idx is None else _np(pack_idx)).astype(np.uint32)
+            mv = dropout_mask_values(
+                seed=ctx.seed, offset=ctx.calls, members=members, n_rows=x.shape[1],
+                n_cols=x.shape[2], p=_np(p), dtype=np.float64,
+            )
+            ctx.calls += 1
+            return torch.from_numpy(mv).to(x.dtype) * x
+
+        DropoutPack.forward = forward
+        return self
+
+    def __exit__(self, *exc):
+        self.tp.nn.DropoutPack.forward = self.orig
+
+
+def make_block(tp, dtype, name):
+    torch.manual_seed(1)
+    P, B, max_in, max_out = 6, 37, 40, 48
+    in_f = [40, 16, 33, 8, 24, 40]
+    out_f = [48, 16, 20, 47, 9, 32]
+    p = [0.0, 0.1, 0.25, 0.5, 0.3, 0.05]
+    blk = tp.nn.MLPBackbonePack.Block(
+        in_features=in_f, out_features=out_f, max_in_features=max_in,
+        max_out_features=max_out, activation={'type': torch.nn.ReLU}, dropout=p,
+        pack_size=P,
+    ).to(dtype)
+    blk.train()
+    x = torch.randn(P, B, max_in, dtype=dtype)
+    x = x * (torch.arange(max_in)[None] < torch.tensor(in_f)[:, None]).to(dtype)[:, None, :]
+    x.requires_grad_(True)
+    seed = 0x1234_5678_9ABC
+    with _PhiloxDropout(tp, seed) as _:
+        y = blk(x)
+    dy = torch.randn_like(y)
+    (y * dy).sum().backward()
+    np.savez_compressed(
+        os.path.join(HERE, name),
+        x=_np(x), weight=_np(blk.linear.weight), bias=_np(blk.linear.bias),
+        in_features=np.array(in_f, np.int32), out_features=np.array(out_f, np.int32),
+        p=np.array(p, np.float32), seed=np.uint64(seed), offset=np.uint32(0),
+        y=_np(y), dy=_np(dy), dx=_np(x.grad), dweight=_np(blk.linear.weight.grad),
+        dbias=_np(blk.linear.bias.grad),
+    )
+
+
+def make_tabpack(tp, dtype, name, forward_impl='dense'):
+    torch.manual_seed(2)
+    P, B = 5, 29
+    n_num, cards, d_out = 5, [3, 4], 3
+    n_blocks = [1, 3, 2, 3, 1]
+    d_block = [8, 24, 16, 32, 12]
+    dropout = [0.1, 0.0, 0.3, 0.2, 0.45]
+    model = tp.nn.TabPack(
+        n_numerical_features=n_num, categorical_cardinalities=cards, d_out=d_out,
+        n_blocks=n_blocks, d_block=d_block, dropout=dropout, pack_size=P,
+        forward_impl=forward_impl,
+    ).to(dtype)
+    model.train()
+    x_num = torch.randn(P, B, n_num, dtype=dtype)
+    x_cat = torch.stack([torch.randint(0, c + 1, (P, B)) for c in cards], -1)
+    seed = 77
+    torch.set_default_dtype(dtype)
+    try:
+        with _PhiloxDropout(tp, seed):
+            y = model(x_num, x_cat)
+    finally:
+        torch.set_default_dtype(torch.float32)
+    dy = torch.randn_like(y)
+    (y * dy).sum().backward()
+    arrays = {
+        'x_num': _np(x_num), 'x_cat': _np(x_cat), 'y': _np(y), 'dy': _np(dy),
+        'n_blocks': np.array(n_blocks, np.int32), 'd_block': np.array(d_block, np.int32),
+        'dropout': np.array(dropout, np.float32), 'cards': np.array(cards, np.int32),
+        'seed': np.uint64(seed),
+    }
+    for k, v in model.state_dict().items():
+        arrays['param.' + k] = _np(v)
+    for k, v in model.named_parameters():
+        arrays['grad.' + k] = _np(v.grad)
+    np.savez_compressed(os.path.join(HERE, name), **arrays)
+
+
+def make_adamw(tp):
+    arrays = {}
+    P = 4
+    for case, (per_member, support_replacement) in enumerate(
+        [(False, False), (True, False), (True, True), (False, True)]
+    ):
+        torch.manual_seed(10 + case)
+        w = tp.nn.ParameterPack(torch.randn(P, 6, 5))
+        b = tp.nn.ParameterPack(torch.randn(P, 6))
+        if per_member:
+            hp = dict(lr=[1e-3, 3e-3, 1e-2, 0.0], beta1=[0.9, 0.8, 0.95, 0.5],
+                      beta2=[0.999, 0.95, 0.99, 0.9], eps=[1e-8, 1e-6, 1e-7, 1e-8],
+                      weight_decay=[0.0, 1e-2, 1e-1, 1e-3])
+        else:
+            hp = dict(lr=3e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=1e-2)
+        opt = tp.optim.AdamWPack([w, b], pack_size=P, support_replacement=support_replacement, **hp)
+        arrays[f'c{case}.w0'] = _np(w)
+        arrays[f'c{case}.b0'] = _np(b)
+        for k, v in hp.items():
+            arrays[f'c{case}.hp.{k}'] = np.array(v, np.float64)
+        for s in range(3):
+            gw, gb = torch.randn_like(w) * 0.1, torch.randn_like(b) * 0.1
+            w.grad, b.grad = gw.clone(), gb.clone()
+            opt.step()
+            arrays[f'c{case}.s{s}.gw'] = _np(gw)
+            arrays[f'c{case}.s{s}.gb'] = _np(gb)
+            arrays[f'c{case}.s{s}.w'] = _np(w)
+            arrays[f'c{case}.s{s}.b'] = _np(b)
+            arrays[f'c{case}.s{s}.m_w'] = _np(opt.state[w]['exp_avg'])
+            arrays[f'c{case}.s{s}.v_w'] = _np(opt.state[w]['exp_avg_sq'])
+        arrays[f'c{case}.per_member'] = np.array(per_member)
+        arrays[f'c{case}.support_replacement'] = np.array(support_replacement)
+    np.savez_compressed(os.path.join(HERE, 'adamw.npz'), **arrays)
+
+
+def make_newton_schulz(tp):
+    torch.manual_seed(3)
+    arrays = {}
+    for j, (r, c) in enumerate([(48, 32), (32, 48), (40, 40)]):
+        G = torch.randn(3, r, c) * 0.02
+        X = tp.optim._zeropower_via_newtonschulz5(G, steps=5)
+        arrays[f'G{j}'] = _np(G)
+        arrays[f'X{j}'] = _np(X.float())
+    np.savez_compressed(os.path.join(HERE, 'newton_schulz.npz'), **arrays)
+
+
+def make_muon(tp):
+    torch.manual_seed(4)
+    P = 3
+    lin = tp.nn.LinearPack([24, 16, 32], [32, 16, 8], max_in_features=32,
+                           max_out_features=32, pack_size=P)
+    out = tp.nn.LinearPack(32, 2, pack_size=P)
+    group = tp.optim.MuonAdamWPack.make_muon_parameter_group(lin)
+    opt = tp.optim.MuonAdamWPack(
+        [group, {'params': [lin.bias, out.weight, out.bias]}],
+        adamw_lr=[1e-3, 2e-3, 5e-3], weight_decay=[1e-2, 0.0, 1e-3],
+        muon_lr=[0.02, 0.01, 0.05], muon_momentum=[0.95, 0.9, 0.8], pack_size=P,
+        allow_inplace_grad_mutation=True,
+    )
+    arrays = {'w0': _np(lin.weight), 'in_features': np.array([24, 16, 32], np.int32),
+              'out_features': np.array([32, 16, 8], np.int32)}
+    mask = (torch.arange(32)[None, :, None] < torch.tensor([32, 16, 8])[:, None, None]) & (
+        torch.arange(32)[None, None, :] < torch.tensor([24, 16, 32])[:, None, None])
+    for s in range(2):
+        g = torch.randn_like(lin.weight) * 1e-3 * mask
+        lin.weight.grad = g.clone()
+        for prm in (lin.bias, out.weight, out.bias):
+            prm.grad = torch.randn_like(prm) * 1e-3
+        opt.step()
+        arrays[f's{s}.g'] = _np(g)
+        arrays[f's{s}.w'] = _np(lin.weight)
+        arrays[f's{s}.mom'] = _np(opt.state[lin.weight]['muon_momentum_buffer'])
+    arrays['scale'] = _np(group['muon_update_scale'])
+    np.savez_compressed(os.path.join(HERE, 'muon.npz'), **arrays)
+
+
+def make_metrics(tp):
+    torch.manual_seed(5)
+    M = tp.metrics
+    P, N, C = 7, 101, 4
+    yr = torch.randn(N)
+    pr = torch.randn(P, N)
+    yb = torch.randint(0, 2, (N,))
+    pb = torch.rand(P, N).clamp(1e-6, 1 - 1e-6)
+    pb[0, :3] = 0.0  # exercises the -100 clamp
+    ym = torch.randint(0, C, (N,))
+    pm = torch.softmax(torch.randn(P, N, C), -1)
+    lab = torch.randint(0, C, (P, N))
+    sc = torch.randn(P, N).round(decimals=1)  # ties for the midranks
+    arrays = dict(yr=_np(yr), pr=_np(pr), yb=_np(yb), pb=_np(pb), ym=_np(ym), pm=_np(pm),
+                  lab=_np(lab), sc=_np(sc))
+    arrays['mse'] = _np(M.mse_pack(y_true=yr, y_pred=pr))
+    arrays['mae'] = _np(M.mae_pack(y_true=yr, y_pred=pr))
+    arrays['r2'] = _np(M.r2_pack(y_true=yr, y_pred=pr))
+    arrays['bce'] = _np(M.binary_cross_entropy_pack(y_true=yb, y_proba=pb))
+    arrays['ce'] = _np(M.multiclass_cross_entropy_pack(y_true=ym, y_proba=pm))
+    arrays['acc'] = _np(M.accuracy_pack(y_true=ym, y_pred=lab))
+    arrays['auc'] = _np(M.binary_roc_auc_pack(y_true=yb, y_score=sc))
+    np.savez_compressed(os.path.join(HERE, 'metrics.npz'), **arrays)
+
+
+def make_ensemble(tp):
+    torch.manual_seed(6)
+    E = tp.ensemble
+    M = tp.metrics
+    arrays = {}
+    C, N = 14, 83
+    y = torch.randn(N)
+    preds = y[None] + torch.randn(C, N) * torch.linspace(0.3, 1.5, C)[:, None]
+    preds[5] = preds[2]  # exact duplicate -> exact score ties
+    arrays['reg.y'] = _np(y)
+    arrays['reg.preds'] = _np(preds)
+    score = lambda p: -M.mse_pack(y_true=y, y_pred=p)  # noqa: E731
+    for j, kw in enumerate([
+        dict(), dict(init_top_k=3), dict(max_ensemble_size=4),
+        dict(with_replacement=True, max_ensemble_size=12),
+        dict(with_replacement=True, max_ensemble_size=20, init_top_k=2),
+    ]):
+        idx, w = E.greedy_ensemble(preds, score_fn=score, **kw)
+        arrays[f'reg.k{j}.idx'] = _np(idx)
+        if w is not None:
+            arrays[f'reg.k{j}.w'] = _np(w)
+    arrays['reg.top3'] = _np(E.topk_ensemble(preds, score_fn=score, k=3))
+
+    K = 3
+    yc = torch.randint(0, K, (N,))
+    logits = torch.randn(C, N, K) + 2.0 * torch.nn.functional.one_hot(yc, K)[None] * torch.rand(C, 1, 1)
+    probs = torch.softmax(logits, -1)
+    arrays['cls.y'] = _np(yc)
+    arrays['cls.probs'] = _np(probs)
+    score_ce = lambda p: -M.multiclass_cross_entropy_pack(y_true=yc, y_proba=p)  # noqa: E731
+    idx, _ = E.greedy_ensemble(probs, score_fn=score_ce, max_ensemble_size=6)
+    arrays['cls.idx'] = _np(idx)
+    wts = torch.rand(4)
+    arrays['mean.w'] = _np(wts)
+    arrays['mean.out'] = _np(E.compute_unsanitized_ensemble_predictions(probs[:4], wts))
+    arrays['mean.out_eq'] = _np(E.compute_unsanitized_ensemble_predictions(probs[:4], None))
+    np.savez_compressed(os.path.join(HERE, 'ensemble.npz'), **arrays)
+
+
+def main():
+    src = sys.argv[1] if len(sys.argv) > 1 else '/root/reference/src'
+    tp = _import_reference(src)
+    make_block(tp, torch.float64, 'block_fp64.npz')
+    make_block(tp, torch.float32, 'block_fp32.npz')
+    make_tabpack(tp, torch.float64, 'tabpack_fp64.npz')
+    make_tabpack(tp, torch.float64, 'tabpack_indexed_fp64.npz', forward_impl='indexed')
+    make_adamw(tp)
+    make_newton_schulz(tp)
+    make_muon(tp)
+    make_metrics(tp)
+    make_ensemble(tp)
+    print('fixtures written to', HERE)
+
+
+if __name__ == '__main__':
+    main()
