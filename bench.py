@@ -1,0 +1,416 @@
+"""Benchmark of the packed-ensemble hot path on B200: the ragged grouped GEMM layer.
+
+Workload (per GPU): a pack of 256 members sharing one 4096 x 512 bf16 input
+batch; member i has its own output width out_i ~ U{64, 80, ..., 1024}, weights
+U(+-1/sqrt(512)), a bias, ReLU and dropout with p_i ~ U[0, 0.5].  One step is
+the forward pass (one fused launch: GEMM + bias + ReLU + Philox dropout) and the
+backward pass (activation/bias gradient, dgrad, wgrad) of that layer, i.e.
+3 x sum_i 2 * 4096 * 512 * out_i ragged FLOPs.  Members are sharded over GPUs
+(weak scaling: every rank owns its own 256 members, keyed by global member id);
+the layer has no cross-member exchange, so the timed region has no collective.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Prints one JSON line (rank 0).  `value` is whole-job member-samples/s with all
+inputs resident in HBM; `e2e` repeats the measurement through the same C-ABI
+calls with the input batch copied from pinned host memory and the bias
+gradient read back every step; `roofline` covers the kernel with the largest
+share of the step; `cpu_baseline` times the numpy restatement of the same layer
+on a bounded member sample on this host.  `--impl reference` times that CPU
+restatement alone, with all host threads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+MEMBERS = 256
+ROWS = 4096
+D_IN = 512
+MAX_OUT = 1024
+WORKLOAD = ('packed MLP block forward+backward: 256 members/GPU sharing a 4096x512 bf16 batch, '
+            'out widths U{64..1024 step 16}, bias + ReLU + Philox dropout p~U[0,0.5], fp32 accumulation')
+
+
+def member_widths(base: int, n: int) -> np.ndarray:
+    """Per-member output widths, seeded by global member id (shard-invariant)."""
+    out = np.empty(n, np.int32)
+    for i in range(n):
+        out[i] = np.random.default_rng(1_000_003 * (base + i) + 7).integers(4, 65) * 16
+    return out
+
+
+def member_dropout(base: int, n: int) -> np.ndarray:
+    return np.array([np.random.default_rng(7_000_001 * (base + i) + 3).uniform(0, 0.5) for i in range(n)], np.float32)
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), 'measured'
+    return {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0, 'bf16_tflops_sustained': 1400.0}, 'fallback'
+
+
+# ----------------------------------------------------------------------------- CPU legs
+
+
+def cpu_layer_step(x, w, b, out_f, p, dy, seed, offset):
+    """numpy restatement (oracle) of one forward+backward of the layer."""
+    from oracle import layers as ol
+
+    P = w.shape[0]
+    mv = ol.dropout_mask_values(seed=seed, offset=offset, members=np.arange(P), n_rows=x.shape[0],
+                                n_cols=w.shape[1], p=p, dtype=np.float32)
+    y, pre = ol.block_forward(x, w, b, out_f, mask_values=mv)
+    ol.block_backward(x, w, out_f, pre, dy, mask_values=mv)
+    return y
+
+
+def cpu_sample(members: int, budget_s: float, steps: int | None = None):
+    """Times the CPU restatement on `members` members; returns (member-samples/s, threads, sample)."""
+    rng = np.random.default_rng(0)
+    out_f = member_widths(0, members)
+    max_out = int(out_f.max())
+    x = rng.standard_normal((ROWS, D_IN)).astype(np.float32)
+    w = (rng.uniform(-1, 1, (members, max_out, D_IN)) / np.sqrt(D_IN)).astype(np.float32)
+    b = (rng.uniform(-1, 1, (members, max_out)) / np.sqrt(D_IN)).astype(np.float32)
+    p = member_dropout(0, members)
+    dy = rng.standard_normal((members, ROWS, max_out)).astype(np.float32)
+    cpu_layer_step(x, w, b, out_f, p, dy, 1, 0)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_layer_step(x, w, b, out_f, p, dy, 1, n + 1)
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (steps is None and el >= budget_s):
+            break
+    try:
+        from threadpoolctl import threadpool_info
+
+        threads = max([i.get('num_threads', 1) for i in threadpool_info()] or [1])
+    except Exception:  # pragma: no cover
+        threads = os.cpu_count() or 1
+    sample = f'{members} members x {ROWS} rows x {D_IN} in (out widths {int(out_f.sum())} total), {n} fwd+bwd steps'
+    return members * ROWS * n / el, threads, sample
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    members = 4
+    vals = []
+    threads = 1
+    sample = ''
+    for _ in range(max(args.warmup, 0)):
+        cpu_sample(members, 0, steps=1)
+    for _ in range(args.steps):
+        v, threads, sample = cpu_sample(members, 0, steps=1)
+        vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        'metric': 'member-samples/sec train (packed MLP block fwd+bwd)', 'value': value,
+        'unit': 'member-samples/s', 'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+        'ms_per_step': members * ROWS / value * 1e3, 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic', 'impl': 'reference',
+        'config': {'workload': WORKLOAD, 'sample_members': members},
+        'cpu_baseline': {'value': value, 'unit': 'member-samples/s', 'cores': threads, 'kind': 'port',
+                         'sample': sample + ' per step (numpy restatement of the reference layer)'},
+        'e2e': {'value': value, 'unit': 'member-samples/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    FIELDS = ('clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, device: int) -> None:
+        self.device = device
+        self.lines: list[str] = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ['nvidia-smi', '-i', str(self.device), f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                 '-lms', '100'], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(',')]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == 'active':
+                    reasons.add(n)
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': mx or None,
+                'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+# ----------------------------------------------------------------------------- GPU leg
+
+
+def run_b200(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from tabpack_b200 import _lib
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group('nccl', device_id=dev, timeout=datetime.timedelta(seconds=120))
+    lib = _lib.load()
+
+    base = rank * MEMBERS
+    out_f = member_widths(base, MEMBERS)
+    p = member_dropout(base, MEMBERS)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    x = torch.randn(ROWS, D_IN, device=dev, generator=g).bfloat16()
+    w = ((torch.rand(MEMBERS, MAX_OUT, D_IN, device=dev, generator=g) * 2 - 1) / D_IN ** 0.5).bfloat16()
+    bias = (torch.rand(MEMBERS, MAX_OUT, device=dev, generator=g) * 2 - 1) / D_IN ** 0.5
+    dy = torch.randn(MEMBERS, ROWS, MAX_OUT, device=dev, generator=g).bfloat16()
+    of = torch.from_numpy(out_f).to(dev)
+    pd = torch.from_numpy(p).to(dev)
+    y = torch.empty(MEMBERS, ROWS, MAX_OUT, device=dev, dtype=torch.bfloat16)
+    gbuf = torch.empty_like(y)
+    dx = torch.empty(MEMBERS, ROWS, D_IN, device=dev, dtype=torch.bfloat16)
+    dw = torch.empty(MEMBERS, MAX_OUT, D_IN, device=dev, dtype=torch.float32)
+    db = torch.empty(MEMBERS, MAX_OUT, device=dev, dtype=torch.float32)
+
+    fa = _lib.LinearArgs()
+    fa.P, fa.B, fa.max_in, fa.max_out = MEMBERS, ROWS, D_IN, MAX_OUT
+    fa.dtype, fa.x_shared = _lib.TP_DTYPE_BF16, 1
+    fa.in_features, fa.out_features, fa.n_blocks = None, of.data_ptr(), None
+    fa.relu, fa.dropout_p, fa.seed, fa.member_base = 1, pd.data_ptr(), 0x5EED, base
+    fa.x, fa.w, fa.bias, fa.y = x.data_ptr(), w.data_ptr(), bias.data_ptr(), y.data_ptr()
+
+    def grad_args(**kw):
+        ga = _lib.LinearGradArgs()
+        ga.fwd = fa
+        ga.dy, ga.y, ga.g = dy.data_ptr(), y.data_ptr(), gbuf.data_ptr()
+        ga.dw_rows, ga.dw_cols, ga.db_cols = MAX_OUT, D_IN, MAX_OUT
+        for k, v in kw.items():
+            setattr(ga, k, v)
+        return ga
+
+    ga_act = grad_args(dbias=db.data_ptr())
+    ga_dx = grad_args(dx=dx.data_ptr(), g_ready=1)
+    ga_dw = grad_args(dw=dw.data_ptr(), g_ready=1)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    phases = ['fwd', 'act', 'dgrad', 'wgrad']
+
+    def check(rc, what):
+        if rc != 0:
+            raise RuntimeError(f'{what}: {lib.tp_last_error_string().decode()}')
+
+    def step(i, ev=None):
+        fa.offset = i
+        ga_act.fwd.offset = i
+        if ev is not None:
+            ev[0].record(stream)
+        check(lib.tp_linear_forward(ctypes.byref(fa), sp), 'forward')
+        if ev is not None:
+            ev[1].record(stream)
+        check(lib.tp_linear_backward(ctypes.byref(ga_act), sp), 'act')
+        if ev is not None:
+            ev[2].record(stream)
+        check(lib.tp_linear_backward(ctypes.byref(ga_dx), sp), 'dgrad')
+        if ev is not None:
+            ev[3].record(stream)
+        check(lib.tp_linear_backward(ctypes.byref(ga_dw), sp), 'wgrad')
+        if ev is not None:
+            ev[4].record(stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i, events[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = t0.elapsed_time(t1)
+    per_phase = {ph: statistics.mean(ev[j].elapsed_time(ev[j + 1]) for ev in events) for j, ph in enumerate(phases)}
+    dev_err = lib.tp_device_error()
+    if dev_err != 0:
+        raise RuntimeError(f'device-side wait timed out ({dev_err})')
+
+    # end to end: batch uploaded from pinned host memory, bias gradient read back, every step
+    x_host = x.cpu().pin_memory()
+    db_host = torch.empty(db.shape, dtype=db.dtype).pin_memory()
+    x_dev = torch.empty_like(x)
+    fa_e2e_x = x_dev.data_ptr()
+
+    def e2e_step(i):
+        x_dev.copy_(x_host, non_blocking=True)
+        fa.x = fa_e2e_x
+        ga_act.fwd.x = fa_e2e_x
+        ga_dw.fwd.x = fa_e2e_x
+        step(i)
+        db_host.copy_(db, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    if world > 1:
+        t = torch.tensor([elapsed_ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+
+    samples = world * MEMBERS * ROWS * args.steps
+    value = samples / (elapsed_ms / 1e3)
+    e2e_value = samples / (e2e_ms / 1e3)
+
+    peaks, peak_kind = load_peaks()
+    flops = 2.0 * ROWS * D_IN * float(out_f.sum())
+    # activation-gradient kernel: reads dy and y and writes g over each member's
+    # 64-column strips below out_i, bf16
+    act_bytes = 3.0 * 2 * ROWS * float(sum((o + 63) // 64 * 64 for o in out_f)) + 4.0 * MEMBERS * MAX_OUT
+    work = {'fwd': flops, 'dgrad': flops, 'wgrad': flops, 'act': act_bytes}
+    dominant = max(per_phase, key=per_phase.get)
+    if dominant == 'act':
+        ach = work['act'] / (per_phase['act'] / 1e3) / 1e9
+        roof = {'bound': 'hbm', 'achieved': ach, 'peak': peaks['hbm_gbs'], 'unit': 'GB/s'}
+    else:
+        ach = work[dominant] / (per_phase[dominant] / 1e3) / 1e12
+        roof = {'bound': 'tensor', 'achieved': ach, 'peak': peaks['bf16_tflops_sustained'], 'unit': 'TFLOP/s'}
+    roof['frac'] = roof['achieved'] / roof['peak']
+    roof['kernel'] = dominant
+    roof['traffic'] = TRAFFIC_BYTES_PER_LAUNCH.get(dominant)
+    roof['peak_source'] = f'{peak_kind} ({"sustained" if roof["bound"] == "tensor" else "copy"})'
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        v, threads, sample = cpu_sample(4, args.cpu_seconds)
+        cpu = {'value': v, 'unit': 'member-samples/s', 'cores': threads, 'kind': 'port',
+               'sample': sample + ' (numpy restatement of the reference layer, fp32)'}
+
+    tflops_step = 3 * flops * world / (elapsed_ms / args.steps / 1e3) / 1e12
+    line = {
+        'metric': 'member-samples/sec train (packed MLP block fwd+bwd)', 'value': value,
+        'unit': 'member-samples/s', 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
+        'ms_per_step': elapsed_ms / args.steps, 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
+        'config': {'workload': WORKLOAD, 'members_per_gpu': MEMBERS, 'rows': ROWS, 'd_in': D_IN,
+                   'max_out': MAX_OUT, 'ragged_tflop_per_step_per_gpu': 3 * flops / 1e12,
+                   'ragged_tflops_achieved': tflops_step, 'parallelism': f'member-sharded x{world}',
+                   'l2': 'inputs larger than L2 (weights 256 MiB, activations 2 GiB per GPU)',
+                   'per_kernel_ms': per_phase},
+        'roofline': roof,
+        'cpu_baseline': cpu,
+        'e2e': {'value': e2e_value, 'unit': 'member-samples/s', 'h2d_bytes_per_step': x.numel() * 2,
+                'd2h_bytes_per_step': db.numel() * 4},
+        'gpu_launches': 4 * args.steps,
+        'clocks': clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# DRAM bytes (read + write) per full-size launch, from the ncu capture summarised in
+# profiles/linear_block_fwd_bwd_256x4096x512.md (32-member case scaled by 256/32).
+TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
+    'fwd': (26.017536e6 + 214.157312e6) * 8,
+    'dgrad': (172.590080e6 + 91.861504e6) * 8,
+    'wgrad': (159.238912e6 + 36.017920e6) * 8,
+}
+
+
+def main() -> None:
+    global MEMBERS
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=300)
+    ap.add_argument('--warmup', type=int, default=10)
+    ap.add_argument('--impl', choices=['b200', 'reference'], default='b200')
+    ap.add_argument('--cpu-seconds', type=float, default=10.0)
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--members', type=int, default=MEMBERS, help='members per GPU (smaller for profiling)')
+    args = ap.parse_args()
+    MEMBERS = args.members
+    if args.impl == 'reference':
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == '__main__':
+    main()

@@ -1,0 +1,143 @@
+/*
+ * tabpack_b200 — C ABI of the B200 (sm_100a) packed-ensemble hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as `void*`, i.e. a `cudaStream_t`), enqueues its kernels on that
+ * stream and returns immediately.  All buffers are allocated and owned by the
+ * caller.  Return value: TP_OK (0) or a negative TP_E* code; the message for the
+ * last failure on the calling thread is available from tp_last_error_string().
+ * Errors are reported, never thrown; no kernel traps.  Kernels that wait on an
+ * mbarrier give up after a bounded time and record TP_ETIMEOUT in a device-side
+ * flag that tp_device_error() reads (and clears).
+ *
+ * Layout conventions follow the reference's pack convention (PACK_DIM = 0,
+ * BATCH_DIM = 1, src/tabpackage/nn.py:29-30): activations are padded
+ * (P, B, width), weights (P, max_out, max_in), biases (P, max_out); columns at
+ * or beyond a member's own width are exactly zero in every output.
+ */
+#ifndef TABPACK_B200_H_
+#define TABPACK_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TP_OK 0
+#define TP_EINVAL (-1)       /* bad shape, null pointer, unsupported combination */
+#define TP_EALIGN (-2)       /* pointer or leading dimension not 16-byte aligned */
+#define TP_EUNSUPPORTED (-3) /* not supported on this device / build */
+#define TP_ECUDA (-4)        /* a CUDA runtime or driver call failed */
+#define TP_ETIMEOUT (-5)     /* a device-side wait gave up (reported by tp_device_error) */
+
+#define TP_DTYPE_F32 0  /* fp32 activations and weights, fp32 CUDA-core arithmetic */
+#define TP_DTYPE_BF16 1 /* bf16 activations and weights, tcgen05 tensor cores, fp32 accumulation */
+
+/* Arguments of one packed-linear call (one LinearPack, or one MLP block =
+ * LinearPack -> ReLU -> DropoutPack).  Widths `max_in`/`max_out` are the
+ * leading dimensions of x / y / w; in BF16 mode both must be multiples of 8. */
+typedef struct tp_linear_args {
+  int32_t P;              /* members in this call */
+  int32_t B;              /* rows (batch) per member */
+  int32_t max_in;         /* padded input width  = last dim of x and w */
+  int32_t max_out;        /* padded output width = last dim of y, middle dim of w */
+  int32_t dtype;          /* TP_DTYPE_* of x, w, y, g, dx */
+  int32_t x_shared;       /* 1: x is (B, max_in), shared by every member */
+  const int32_t* in_features;  /* device (P,) real input widths, or NULL (= max_in) */
+  const int32_t* out_features; /* device (P,) real output widths, or NULL (= max_out) */
+  const int32_t* n_blocks;     /* device (P,) depths, or NULL: member m is active
+                                  iff n_blocks == NULL || n_blocks[m] > block_index */
+  int32_t block_index;
+  int32_t relu;                /* 1: ReLU after the bias */
+  const float* dropout_p;      /* device (P,) dropout probabilities, or NULL (eval) */
+  uint64_t seed;               /* Philox key */
+  uint32_t offset;             /* Philox counter word 3 (call id) */
+  uint32_t member_base;        /* global id of member 0 (counter word 2 = base + m) */
+  const void* x;               /* (P or 1, B, max_in) */
+  const void* w;               /* (P, max_out, max_in) */
+  const float* bias;           /* (P, max_out) fp32, or NULL */
+  void* y;                     /* (P, B, max_out) */
+} tp_linear_args;
+
+/* Backward of tp_linear_forward with the same `fwd` arguments. */
+typedef struct tp_linear_grad_args {
+  tp_linear_args fwd;
+  const void* dy;     /* (P, B, max_out) gradient w.r.t. y */
+  const void* y;      /* forward output (read when relu or dropout is on) */
+  void* g;            /* (P, B, max_out) workspace: gradient w.r.t. the pre-activation */
+  float* dbias;       /* (P, max_out) fp32, or NULL */
+  void* dx;           /* (P, B, max_in), or NULL (no input gradient) */
+  float* dw;          /* (P, dw_rows, dw_cols) fp32, or NULL */
+  int32_t dw_rows;    /* leading dims of dw (the parameter's real padded shape) */
+  int32_t dw_cols;
+  int32_t db_cols;    /* row length of dbias (the parameter's real max_out) */
+  int32_t g_ready;    /* 1: g (and dbias) already hold this call's activation gradient;
+                         only the requested dx / dw GEMMs run */
+} tp_linear_grad_args;
+
+/* LinearPack.forward (src/tabpackage/nn.py:792-816) fused with the ReLU and
+ * DropoutPack.forward (nn.py:886-903) of MLPBackbonePack.Block.forward
+ * (nn.py:1071-1079) and the depth gating of MLPBackbonePack._forward_dense
+ * (nn.py:1272-1288): y = dropout(relu(x w^T + b)) for active members, y = x for
+ * inactive ones (requires max_in == max_out). */
+int tp_linear_forward(const tp_linear_args* a, void* stream);
+
+/* Autograd of the same composition (replaces the BaddbmmBackward / MulBackward /
+ * ReluBackward chain the reference records at nn.py:805-816, 897-901): writes g,
+ * dbias, dx (columns >= in_features are zero) and dw (entries outside
+ * out_features x in_features are zero). */
+int tp_linear_backward(const tp_linear_grad_args* a, void* stream);
+
+/* Test hook: the Philox keep mask of the dropout above, (P, B, cols) uint8. */
+int tp_dropout_mask(uint64_t seed, uint32_t offset, uint32_t member_base,
+                    const float* dropout_p, int32_t P, int32_t B, int32_t cols,
+                    uint8_t* mask, void* stream);
+
+/* One tensor of a grouped optimizer step.  Element e of the tensor belongs to
+ * member e / inner. */
+typedef struct tp_opt_tensor {
+  float* p;
+  float* grad;
+  float* exp_avg;     /* AdamW m, or the Muon momentum buffer */
+  float* exp_avg_sq;  /* AdamW v (unused by Muon) */
+  const int64_t* step;/* per-member step counts (already incremented), or NULL */
+  int64_t numel;
+  int64_t inner;
+} tp_opt_tensor;
+
+/* Per-member hyperparameters: a device (P,) fp32 array, or NULL to use the
+ * scalar.  Mirrors the group values of OptimizerPack (src/tabpackage/optim.py:92-117). */
+typedef struct tp_hparam {
+  const float* per_member;
+  double scalar;
+} tp_hparam;
+
+#define TP_MAX_OPT_TENSORS 32
+
+typedef struct tp_adamw_args {
+  int32_t n_tensors;
+  tp_opt_tensor t[TP_MAX_OPT_TENSORS];
+  tp_hparam lr, beta1, beta2, eps, weight_decay;
+  int64_t step;       /* scalar step (already incremented) when t[i].step == NULL */
+} tp_adamw_args;
+
+/* AdamWPack.step / MuonAdamWPack._step_adamw for up to TP_MAX_OPT_TENSORS
+ * parameter packs of one group (src/tabpackage/optim.py:347-427, 776-846). */
+int tp_adamw_step(const tp_adamw_args* a, void* stream);
+
+/* Clears and returns the device-side error flag (TP_OK or TP_ETIMEOUT). */
+int tp_device_error(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* tp_last_error_string(void);
+
+/* Library version string. */
+const char* tp_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TABPACK_B200_H_ */

@@ -1,0 +1,110 @@
+"""ctypes binding of `libtabpack_b200.so` (the C ABI in `include/tabpack_b200.h`).
+
+The library is loaded lazily on first use.  There is no fallback: if the
+library is missing or fails to load, every op raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, 'libtabpack_b200.so')
+
+TP_DTYPE_F32 = 0
+TP_DTYPE_BF16 = 1
+TP_MAX_OPT_TENSORS = 32
+
+_c_int32_p = ctypes.POINTER(ctypes.c_int32)
+_c_float_p = ctypes.POINTER(ctypes.c_float)
+
+
+class LinearArgs(ctypes.Structure):
+    _fields_ = [
+        ('P', ctypes.c_int32), ('B', ctypes.c_int32), ('max_in', ctypes.c_int32),
+        ('max_out', ctypes.c_int32), ('dtype', ctypes.c_int32), ('x_shared', ctypes.c_int32),
+        ('in_features', ctypes.c_void_p), ('out_features', ctypes.c_void_p),
+        ('n_blocks', ctypes.c_void_p), ('block_index', ctypes.c_int32), ('relu', ctypes.c_int32),
+        ('dropout_p', ctypes.c_void_p), ('seed', ctypes.c_uint64), ('offset', ctypes.c_uint32),
+        ('member_base', ctypes.c_uint32), ('x', ctypes.c_void_p), ('w', ctypes.c_void_p),
+        ('bias', ctypes.c_void_p), ('y', ctypes.c_void_p),
+    ]
+
+
+class LinearGradArgs(ctypes.Structure):
+    _fields_ = [
+        ('fwd', LinearArgs), ('dy', ctypes.c_void_p), ('y', ctypes.c_void_p), ('g', ctypes.c_void_p),
+        ('dbias', ctypes.c_void_p), ('dx', ctypes.c_void_p), ('dw', ctypes.c_void_p),
+        ('dw_rows', ctypes.c_int32), ('dw_cols', ctypes.c_int32), ('db_cols', ctypes.c_int32),
+        ('g_ready', ctypes.c_int32),
+    ]
+
+
+class OptTensor(ctypes.Structure):
+    _fields_ = [
+        ('p', ctypes.c_void_p), ('grad', ctypes.c_void_p), ('exp_avg', ctypes.c_void_p),
+        ('exp_avg_sq', ctypes.c_void_p), ('step', ctypes.c_void_p), ('numel', ctypes.c_int64),
+        ('inner', ctypes.c_int64),
+    ]
+
+
+class HParam(ctypes.Structure):
+    _fields_ = [('per_member', ctypes.c_void_p), ('scalar', ctypes.c_double)]
+
+
+class AdamWArgs(ctypes.Structure):
+    _fields_ = [
+        ('n_tensors', ctypes.c_int32), ('t', OptTensor * TP_MAX_OPT_TENSORS),
+        ('lr', HParam), ('beta1', HParam), ('beta2', HParam), ('eps', HParam),
+        ('weight_decay', HParam), ('step', ctypes.c_int64),
+    ]
+
+
+# name -> (restype, argtypes); every symbol here is declared in include/tabpack_b200.h
+SIGNATURES = {
+    'tp_linear_forward': (ctypes.c_int, [ctypes.POINTER(LinearArgs), ctypes.c_void_p]),
+    'tp_linear_backward': (ctypes.c_int, [ctypes.POINTER(LinearGradArgs), ctypes.c_void_p]),
+    'tp_dropout_mask': (ctypes.c_int, [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
+                                       ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                       ctypes.c_void_p]),
+    'tp_adamw_step': (ctypes.c_int, [ctypes.POINTER(AdamWArgs), ctypes.c_void_p]),
+    'tp_device_error': (ctypes.c_int, []),
+    'tp_last_error_string': (ctypes.c_char_p, []),
+    'tp_version': (ctypes.c_char_p, []),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class TabPackError(RuntimeError):
+    """A tabpack_b200 C-ABI call returned an error code."""
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Load the library (once) and bind every declared symbol."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        p = path or LIB_PATH
+        if not os.path.exists(p):
+            raise TabPackError(
+                f'{p} is missing: build it with `python -m tabpack_b200.csrc.build` '
+                '(this package has no CPU fallback)'
+            )
+        lib = ctypes.CDLL(p)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().tp_last_error_string().decode(errors='replace')
+        raise TabPackError(f'{what} failed ({rc}): {msg}')

@@ -1,0 +1,232 @@
+// Memory-bound kernels of the packed linear layer and the AdamW optimizer pack.
+#pragma once
+
+#include "gemm_simt.cuh"
+
+namespace tp {
+
+// ---------------------------------------------------------------------------
+// Activation backward + bias gradient.
+//   g[m, r, c]  = dy * (relu ? [y > 0] : 1) * (dropout ? keep(m,r,c) / p_keep : 1)
+//                 for active members and c < out_m; 0 elsewhere (only the 64-column
+//                 strips that the dgrad kernel reads are written)
+//   dbias[m, c] = sum_r g[m, r, c]
+// With relu on, [y > 0] already implies the element was kept, so the mask is
+// only regenerated from Philox when dropout follows a plain linear layer.
+// Grid: (ceil(W / 64), P); 256 threads = 8 column groups of 8 x 32 row lanes.
+// ---------------------------------------------------------------------------
+struct ActBwdArgs {
+  int P, B, W;                // W = storage width of dy / y / g
+  const int32_t* out_f;
+  const int32_t* n_blocks;
+  int block_index;
+  int relu;
+  const float* dropout_p;
+  uint32_t k0, k1, offset, member_base;
+  const void* dy;
+  const void* y;
+  void* g;                    // nullptr: do not write g (it equals dy)
+  float* dbias;
+  int db_cols;
+};
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) act_backward_kernel(const ActBwdArgs a) {
+  __shared__ float red[32][65];
+  const int m = blockIdx.y;
+  const int strip = blockIdx.x * 64;
+  const int cg = threadIdx.x & 7;
+  const int rl = threadIdx.x >> 3;
+  const int c0 = strip + cg * 8;
+  const int out_m = a.out_f ? a.out_f[m] : a.W;
+  const bool active = a.n_blocks == nullptr || a.n_blocks[m] > a.block_index;
+  const bool live = active && strip < out_m;
+  float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (live) {
+    float scale = 1.0f;
+    uint32_t thr = 65536u;
+    if (a.dropout_p) {
+      scale = keep_scale(a.dropout_p[m]);
+      thr = keep_threshold(a.dropout_p[m]);
+    }
+    const bool regen = (!a.relu) && a.dropout_p != nullptr && thr < 65536u;
+    const T* dy = reinterpret_cast<const T*>(a.dy) + (size_t)m * a.B * a.W;
+    const T* y = reinterpret_cast<const T*>(a.y) + (size_t)m * a.B * a.W;
+    T* g = a.g ? reinterpret_cast<T*>(a.g) + (size_t)m * a.B * a.W : nullptr;
+    for (int r = rl; r < a.B; r += 32) {
+      float d[8], yy[8];
+      const size_t off = (size_t)r * a.W + c0;
+      if (VEC && c0 + 8 <= a.W) {
+        if (sizeof(T) == 2) {
+          const uint4 u = *reinterpret_cast<const uint4*>(dy + off);
+          const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) d[j] = __bfloat162float(h[j]);
+          if (a.relu) {
+            const uint4 v = *reinterpret_cast<const uint4*>(y + off);
+            const __nv_bfloat16* hy = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) yy[j] = __bfloat162float(hy[j]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; j += 4) {
+            const float4 f = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(dy) + off + j);
+            d[j] = f.x; d[j + 1] = f.y; d[j + 2] = f.z; d[j + 3] = f.w;
+            if (a.relu) {
+              const float4 fy = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(y) + off + j);
+              yy[j] = fy.x; yy[j + 1] = fy.y; yy[j + 2] = fy.z; yy[j + 3] = fy.w;
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          d[j] = (c0 + j < a.W) ? to_f32<T>(dy[off + j]) : 0.f;
+          yy[j] = (a.relu && c0 + j < a.W) ? to_f32<T>(y[off + j]) : 0.f;
+        }
+      }
+      uint32_t bits = 0xFFu;
+      if (regen) bits = dropout_bits8(a.k0, a.k1, (uint32_t)(c0 >> 3), (uint32_t)r, a.member_base + (uint32_t)m, a.offset, thr);
+      float gv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float v = d[j] * scale;
+        if (a.relu) v = yy[j] > 0.f ? v : 0.f;
+        if (!((bits >> j) & 1u)) v = 0.f;
+        if (c0 + j >= out_m) v = 0.f;
+        gv[j] = v;
+        sum[j] += v;
+      }
+      if (g) {
+        if (VEC && c0 + 8 <= a.W) {
+          if (sizeof(T) == 2) {
+            uint4 u;
+            u.x = pack_bf16x2(gv[0], gv[1]);
+            u.y = pack_bf16x2(gv[2], gv[3]);
+            u.z = pack_bf16x2(gv[4], gv[5]);
+            u.w = pack_bf16x2(gv[6], gv[7]);
+            *reinterpret_cast<uint4*>(g + off) = u;
+          } else {
+            float* gf = reinterpret_cast<float*>(g) + off;
+            *reinterpret_cast<float4*>(gf) = make_float4(gv[0], gv[1], gv[2], gv[3]);
+            *reinterpret_cast<float4*>(gf + 4) = make_float4(gv[4], gv[5], gv[6], gv[7]);
+          }
+        } else {
+          for (int j = 0; j < 8; ++j)
+            if (c0 + j < a.W) g[off + j] = from_f32<T>(gv[j]);
+        }
+      }
+    }
+  }
+  if (a.dbias == nullptr) return;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[rl][cg * 8 + j] = sum[j];
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    float s = 0.f;
+    for (int i = 0; i < 32; ++i) s += red[i][threadIdx.x];
+    const int c = strip + threadIdx.x;
+    if (c < a.db_cols) a.dbias[(size_t)m * a.db_cols + c] = s;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dropout keep mask (test hook)
+// ---------------------------------------------------------------------------
+__global__ void dropout_mask_kernel(uint32_t k0, uint32_t k1, uint32_t offset, uint32_t member_base,
+                                    const float* p, int P, int B, int C, uint8_t* mask) {
+  const long long total_groups = (long long)P * B * ((C + 7) / 8);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total_groups;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int ng = (C + 7) / 8;
+    const int grp = (int)(i % ng);
+    const long long mr = i / ng;
+    const int r = (int)(mr % B);
+    const int m = (int)(mr / B);
+    const uint32_t bits =
+        dropout_bits8(k0, k1, (uint32_t)grp, (uint32_t)r, member_base + (uint32_t)m, offset, keep_threshold(p[m]));
+    for (int j = 0; j < 8; ++j) {
+      const int c = grp * 8 + j;
+      if (c < C) mask[((size_t)m * B + r) * C + c] = (uint8_t)((bits >> j) & 1u);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// AdamW (decoupled weight decay), per-member hyperparameters.
+// ---------------------------------------------------------------------------
+struct AdamWScalars {
+  // per-member arrays (nullptr -> scalar below)
+  const float* lr;
+  const float* beta1;
+  const float* beta2;
+  const float* eps;
+  const float* wd;
+  float lr_s, beta1_s, beta2_s, eps_s, wd_s;
+  // host-precomputed values for the all-scalar case (the reference computes
+  // them in Python double precision)
+  int wd_on;               // 0: `_make_weight_decay_multiplier` returned None
+  float wd_mult_s;         // 1 - lr*wd (all scalar)
+  float one_m_b1_s, one_m_b2_s;
+  int scalar_bias_corr;    // betas scalar and step scalar
+  float bc1_s;             // 1 - beta1^step
+  float step_size_s;       // lr / (1 - beta1^step), used iff lr also scalar
+  float sqrt_bc2_s;        // sqrt(1 - beta2^step)
+  int64_t step;
+};
+
+__device__ __forceinline__ float lerp_t(float a, float b, float w) {
+  // torch's lerp: a + w (b - a) for |w| < 0.5, else b - (b - a)(1 - w)
+  const float d = b - a;
+  return fabsf(w) < 0.5f ? a + w * d : b - d * (1.0f - w);
+}
+
+struct AdamWTensors {
+  tp_opt_tensor t[TP_MAX_OPT_TENSORS];
+};
+
+__global__ void __launch_bounds__(256) adamw_kernel(const AdamWTensors ts, const AdamWScalars s) {
+  const tp_opt_tensor& T = ts.t[blockIdx.y];
+  const int64_t n = T.numel;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / T.inner);
+    const float lr = s.lr ? s.lr[m] : s.lr_s;
+    const float b1 = s.beta1 ? s.beta1[m] : s.beta1_s;
+    const float b2 = s.beta2 ? s.beta2[m] : s.beta2_s;
+    const float eps = s.eps ? s.eps[m] : s.eps_s;
+    float p = T.p[i];
+    const float g = T.grad[i];
+    float mm = T.exp_avg[i];
+    float v = T.exp_avg_sq[i];
+    if (s.wd_on) {
+      const float mult = (s.lr || s.wd) ? 1.0f - lr * (s.wd ? s.wd[m] : s.wd_s) : s.wd_mult_s;
+      p = p * mult;
+    }
+    mm = lerp_t(mm, g, s.beta1 ? 1.0f - b1 : s.one_m_b1_s);
+    if (s.beta2) {
+      v = lerp_t(v, g * g, 1.0f - b2);
+    } else {
+      v = v * b2;
+      v = v + (s.one_m_b2_s * g) * g;
+    }
+    float step_size, sqrt_bc2;
+    if (s.scalar_bias_corr && T.step == nullptr) {
+      step_size = s.lr ? lr / s.bc1_s : s.step_size_s;
+      sqrt_bc2 = s.sqrt_bc2_s;
+    } else {
+      const float st = (float)(T.step ? T.step[m] : s.step);
+      const float bc1 = 1.0f - powf(b1, st);
+      const float bc2 = 1.0f - powf(b2, st);
+      step_size = lr / bc1;
+      sqrt_bc2 = sqrtf(bc2);
+    }
+    const float denom = sqrtf(v) / sqrt_bc2 + eps;
+    p = p - step_size * (mm / denom);
+    T.p[i] = p;
+    T.exp_avg[i] = mm;
+    T.exp_avg_sq[i] = v;
+  }
+}
+
+}  // namespace tp

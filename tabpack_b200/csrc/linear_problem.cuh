@@ -1,0 +1,108 @@
+// Tile scheduling shared by the tensor-core (tcgen05) and CUDA-core paths of the
+// packed linear layer.
+//
+// One launch covers all P members of a pack.  Each member owns the same number
+// of tile slots (m_tiles x n_tiles over the padded output), so tile t maps to
+// member t / (m_tiles * n_tiles) without any prefix sums.  A slot is:
+//   MMA  - a real BMxBN block of C = A * B^T, K = the member's own reduction length
+//   ZERO - an output block that lies entirely in the member's padding (written 0)
+//   COPY - a block of a depth-inactive member: y = x (forward) / dx = dy (dgrad)
+#pragma once
+
+#include "common.cuh"
+
+namespace tp {
+
+enum : int { MODE_FWD = 0, MODE_DGRAD = 1, MODE_WGRAD = 2 };
+enum : int { KIND_MMA = 0, KIND_ZERO = 1, KIND_COPY = 2 };
+
+struct LinearProblem {
+  int mode;
+  int P, B;
+  int max_in, max_out;        // storage widths of x/w/y (multiples of 8 on the bf16 path)
+  const int32_t* in_f;        // (P,) or nullptr
+  const int32_t* out_f;       // (P,) or nullptr
+  const int32_t* n_blocks;    // (P,) or nullptr
+  int block_index;
+  int x_shared;
+  // forward epilogue
+  int relu;
+  const float* dropout_p;     // (P,) or nullptr
+  uint32_t k0, k1, offset, member_base;
+  const float* bias;          // (P, bias_ld) or nullptr
+  int bias_ld;
+  // output: rows x cols per member, leading dim out_ld, member stride out_ms
+  void* out;
+  int out_rows, out_cols, out_ld;
+  long long out_ms;
+  // COPY source (depth-inactive members), same geometry as the output
+  const void* copy_src;
+  // operand pointers for the CUDA-core path (the tensor-core path uses TMA maps)
+  const void* a_ptr;
+  const void* b_ptr;
+  int m_tiles, n_tiles;
+  int BM, BN;
+};
+
+struct TileInfo {
+  int member, mt, nt, kind, kblocks, m_valid, n_valid;
+};
+
+__device__ __forceinline__ bool member_active(const LinearProblem& p, int m) {
+  return p.n_blocks == nullptr || p.n_blocks[m] > p.block_index;
+}
+
+__device__ __forceinline__ TileInfo decode_tile(const LinearProblem& p, int t, int BK) {
+  TileInfo ti;
+  const int per_member = p.m_tiles * p.n_tiles;
+  ti.member = t / per_member;
+  const int r = t - ti.member * per_member;
+  ti.mt = r / p.n_tiles;
+  ti.nt = r - ti.mt * p.n_tiles;
+  const int m = ti.member;
+  const int in_m = p.in_f ? p.in_f[m] : p.max_in;
+  const int out_m = p.out_f ? p.out_f[m] : p.max_out;
+  const bool active = member_active(p, m);
+  int k_len;
+  if (p.mode == MODE_FWD) {
+    ti.m_valid = p.B;
+    ti.n_valid = out_m;
+    k_len = in_m;
+  } else if (p.mode == MODE_DGRAD) {
+    ti.m_valid = p.B;
+    ti.n_valid = in_m;
+    k_len = out_m;
+  } else {
+    ti.m_valid = out_m;
+    ti.n_valid = in_m;
+    k_len = p.B;
+  }
+  ti.kblocks = (k_len + BK - 1) / BK;
+  if (!active) {
+    ti.kind = (p.mode == MODE_WGRAD) ? KIND_ZERO : KIND_COPY;
+  } else if (ti.mt * p.BM >= ti.m_valid || ti.nt * p.BN >= ti.n_valid || ti.kblocks == 0) {
+    ti.kind = KIND_ZERO;
+  } else {
+    ti.kind = KIND_MMA;
+  }
+  return ti;
+}
+
+// Value written to output element (row, col) of member m given the fp32 dot product.
+// `bits` carries the dropout keep bit of this column (bit 0), `keep_scale` its scale.
+template <int MODE>
+__device__ __forceinline__ float epilogue_value(const LinearProblem& p, const TileInfo& ti, int row, int col,
+                                                float acc, float bias, bool keep, float scale) {
+  if (MODE == MODE_FWD) {
+    if (col >= ti.n_valid) return 0.0f;
+    float v = acc + bias;
+    if (p.relu) v = fmaxf(v, 0.0f);
+    return keep ? v * scale : 0.0f;
+  } else if (MODE == MODE_DGRAD) {
+    return col < ti.n_valid ? acc : 0.0f;
+  } else {
+    return (row < ti.m_valid && col < ti.n_valid) ? acc : 0.0f;
+  }
+}
+
+}  // namespace tp

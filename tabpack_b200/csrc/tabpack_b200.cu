@@ -1,0 +1,379 @@
+// C ABI of the B200 packed-ensemble hot path (declared in include/tabpack_b200.h).
+// One translation unit: host-side validation, TMA descriptor encoding and kernel
+// dispatch for every entry point.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <type_traits>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "elementwise.cuh"
+#include "gemm_sm100.cuh"
+#include "gemm_simt.cuh"
+
+namespace tp {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(TP_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define TP_CUDA_TRY(expr)                           \
+  do {                                              \
+    cudaError_t e_ = (expr);                        \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #expr); \
+  } while (0)
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0, minor = 0;
+};
+
+DeviceInfo device_info() {
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  static bool have[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev >= 0 && dev < 64 && !have[dev]) {
+    cudaDeviceGetAttribute(&cache[dev].sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&cache[dev].major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&cache[dev].minor, cudaDevAttrComputeCapabilityMinor, dev);
+    have[dev] = true;
+  }
+  return (dev >= 0 && dev < 64) ? cache[dev] : DeviceInfo{};
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor (planes, rows, inner) with 128-byte swizzled boxes (box_inner x box_rows x 1).
+int make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t rows, uint64_t planes, uint32_t box_inner,
+             uint32_t box_rows) {
+  auto enc = encode_fn();
+  if (!enc) return fail(TP_EUNSUPPORTED, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {inner, rows, planes};
+  cuuint64_t strides[2] = {inner * 2, inner * rows * 2};
+  cuuint32_t box[3] = {box_inner, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TP_EINVAL, "cuTensorMapEncodeTiled failed (%d) for dims %llu x %llu x %llu", (int)r,
+                (unsigned long long)planes, (unsigned long long)rows, (unsigned long long)inner);
+  return TP_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <int BN, int MODE>
+int launch_sm100(const LinearProblem& pr, const CUtensorMap& a, const CUtensorMap& b, cudaStream_t st) {
+  using Cfg = Sm100Cfg<BN, MODE>;
+  auto kern = linear_gemm_sm100<BN, MODE>;
+  TP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+  const long long total = (long long)pr.P * pr.m_tiles * pr.n_tiles;
+  if (total > 0x7FFFFFFFLL) return fail(TP_EINVAL, "too many tiles");
+  const int grid = (int)std::min<long long>(total, device_info().sms);
+  kern<<<grid, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, st>>>(a, b, pr);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+template <typename T, int MODE>
+int launch_simt(LinearProblem pr, cudaStream_t st) {
+  pr.BM = pr.BN = 64;
+  pr.m_tiles = (pr.out_rows + 63) / 64;
+  pr.n_tiles = (pr.out_cols + 63) / 64;
+  const long long total = (long long)pr.P * pr.m_tiles * pr.n_tiles;
+  if (total > 0x7FFFFFFFLL) return fail(TP_EINVAL, "too many tiles");
+  if (total == 0) return TP_OK;
+  linear_gemm_simt<T, MODE><<<(unsigned)total, 256, 0, st>>>(pr);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+int check_linear(const tp_linear_args* a) {
+  if (!a) return fail(TP_EINVAL, "null arguments");
+  if (a->P <= 0 || a->B <= 0 || a->max_in <= 0 || a->max_out <= 0)
+    return fail(TP_EINVAL, "P, B, max_in and max_out must be positive (got %d, %d, %d, %d)", a->P, a->B, a->max_in,
+                a->max_out);
+  if (a->dtype != TP_DTYPE_F32 && a->dtype != TP_DTYPE_BF16) return fail(TP_EINVAL, "unknown dtype %d", a->dtype);
+  if (a->n_blocks && a->max_in != a->max_out)
+    return fail(TP_EINVAL, "depth gating needs max_in == max_out (inactive members pass their input through)");
+  if (!a->w) return fail(TP_EINVAL, "w is null");
+  return TP_OK;
+}
+
+bool use_tensor_cores(const tp_linear_args* a) {
+  const DeviceInfo d = device_info();
+  return a->dtype == TP_DTYPE_BF16 && d.major == 10 && (a->max_in % 8) == 0 && (a->max_out % 8) == 0;
+}
+
+LinearProblem base_problem(const tp_linear_args* a) {
+  LinearProblem p{};
+  p.P = a->P;
+  p.B = a->B;
+  p.max_in = a->max_in;
+  p.max_out = a->max_out;
+  p.in_f = a->in_features;
+  p.out_f = a->out_features;
+  p.n_blocks = a->n_blocks;
+  p.block_index = a->block_index;
+  p.x_shared = a->x_shared;
+  p.relu = a->relu;
+  p.dropout_p = a->dropout_p;
+  p.k0 = (uint32_t)(a->seed & 0xFFFFFFFFu);
+  p.k1 = (uint32_t)(a->seed >> 32);
+  p.offset = a->offset;
+  p.member_base = a->member_base;
+  p.bias = a->bias;
+  p.bias_ld = a->max_out;
+  return p;
+}
+
+}  // namespace
+}  // namespace tp
+
+using namespace tp;
+
+extern "C" {
+
+const char* tp_version(void) { return "tabpack_b200 0.1.0 (sm_100a)"; }
+
+const char* tp_last_error_string(void) { return g_last_error.c_str(); }
+
+int tp_device_error(void) {
+  int v = 0;
+  TP_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+  const int zero = 0;
+  TP_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+  return v;
+}
+
+int tp_linear_forward(const tp_linear_args* a, void* stream) {
+  int rc = check_linear(a);
+  if (rc) return rc;
+  if (!a->x || !a->y) return fail(TP_EINVAL, "x and y must be non-null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  LinearProblem pr = base_problem(a);
+  pr.mode = MODE_FWD;
+  pr.out = a->y;
+  pr.out_rows = a->B;
+  pr.out_cols = a->max_out;
+  pr.out_ld = a->max_out;
+  pr.out_ms = (long long)a->B * a->max_out;
+  pr.copy_src = a->x;
+  pr.a_ptr = a->x;
+  pr.b_ptr = a->w;
+  if (a->n_blocks && a->x_shared) return fail(TP_EINVAL, "depth gating needs a per-member input");
+  if (use_tensor_cores(a)) {
+    if (!aligned16(a->x) || !aligned16(a->w) || !aligned16(a->y)) return fail(TP_EALIGN, "x, w, y must be 16-byte aligned");
+    constexpr int BN = 256;
+    pr.BM = 128;
+    pr.BN = BN;
+    pr.m_tiles = (a->B + 127) / 128;
+    pr.n_tiles = (a->max_out + BN - 1) / BN;
+    CUtensorMap ma, mb;
+    if ((rc = make_map(&ma, a->x, a->max_in, a->B, a->x_shared ? 1 : a->P, 64, 128))) return rc;
+    if ((rc = make_map(&mb, a->w, a->max_in, a->max_out, a->P, 64, BN))) return rc;
+    return launch_sm100<BN, MODE_FWD>(pr, ma, mb, st);
+  }
+  return a->dtype == TP_DTYPE_BF16 ? launch_simt<__nv_bfloat16, MODE_FWD>(pr, st) : launch_simt<float, MODE_FWD>(pr, st);
+}
+
+int tp_linear_backward(const tp_linear_grad_args* ga, void* stream) {
+  if (!ga) return fail(TP_EINVAL, "null arguments");
+  const tp_linear_args* a = &ga->fwd;
+  int rc = check_linear(a);
+  if (rc) return rc;
+  if (!ga->dy) return fail(TP_EINVAL, "dy must be non-null");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf16 = a->dtype == TP_DTYPE_BF16;
+  const bool need_g = a->relu || a->dropout_p || a->out_features || a->n_blocks;
+  if (need_g && !ga->g) return fail(TP_EINVAL, "g workspace is required with relu, dropout, out_features or n_blocks");
+  if ((a->relu) && !ga->y) return fail(TP_EINVAL, "y is required with relu");
+  const void* G = need_g ? ga->g : ga->dy;
+
+  // 1. g = dy * activation'(.) and dbias = sum_rows g
+  if (!ga->g_ready && (need_g || ga->dbias)) {
+    ActBwdArgs aa{};
+    aa.P = a->P;
+    aa.B = a->B;
+    aa.W = a->max_out;
+    aa.out_f = a->out_features;
+    aa.n_blocks = a->n_blocks;
+    aa.block_index = a->block_index;
+    aa.relu = a->relu;
+    aa.dropout_p = a->dropout_p;
+    aa.k0 = (uint32_t)(a->seed & 0xFFFFFFFFu);
+    aa.k1 = (uint32_t)(a->seed >> 32);
+    aa.offset = a->offset;
+    aa.member_base = a->member_base;
+    aa.dy = ga->dy;
+    aa.y = ga->y ? ga->y : ga->dy;
+    aa.g = need_g ? ga->g : nullptr;
+    aa.dbias = ga->dbias;
+    aa.db_cols = ga->db_cols > 0 ? ga->db_cols : a->max_out;
+    dim3 grid((a->max_out + 63) / 64, a->P);
+    const bool vec = (a->max_out % 8) == 0 && aligned16(ga->dy) && aligned16(aa.y) && (!aa.g || aligned16(aa.g));
+    if (bf16) {
+      if (vec) act_backward_kernel<__nv_bfloat16, true><<<grid, 256, 0, st>>>(aa);
+      else act_backward_kernel<__nv_bfloat16, false><<<grid, 256, 0, st>>>(aa);
+    } else {
+      if (vec) act_backward_kernel<float, true><<<grid, 256, 0, st>>>(aa);
+      else act_backward_kernel<float, false><<<grid, 256, 0, st>>>(aa);
+    }
+    TP_CUDA_TRY(cudaGetLastError());
+  }
+
+  const bool tc = use_tensor_cores(a);
+  // 2. dx = g w   (dx = dy for depth-inactive members)
+  if (ga->dx) {
+    LinearProblem pr = base_problem(a);
+    pr.mode = MODE_DGRAD;
+    pr.out = ga->dx;
+    pr.out_rows = a->B;
+    pr.out_cols = a->max_in;
+    pr.out_ld = a->max_in;
+    pr.out_ms = (long long)a->B * a->max_in;
+    pr.copy_src = ga->dy;
+    pr.a_ptr = G;
+    pr.b_ptr = a->w;
+    pr.dropout_p = nullptr;
+    if (tc) {
+      if (!aligned16(G) || !aligned16(a->w) || !aligned16(ga->dx)) return fail(TP_EALIGN, "g, w, dx must be 16-byte aligned");
+      constexpr int BN = 256;
+      pr.BM = 128;
+      pr.BN = BN;
+      pr.m_tiles = (a->B + 127) / 128;
+      pr.n_tiles = (a->max_in + BN - 1) / BN;
+      CUtensorMap ma, mb;
+      if ((rc = make_map(&ma, G, a->max_out, a->B, a->P, 64, 128))) return rc;
+      if ((rc = make_map(&mb, a->w, a->max_in, a->max_out, a->P, 64, 64))) return rc;
+      if ((rc = launch_sm100<BN, MODE_DGRAD>(pr, ma, mb, st))) return rc;
+    } else {
+      rc = bf16 ? launch_simt<__nv_bfloat16, MODE_DGRAD>(pr, st) : launch_simt<float, MODE_DGRAD>(pr, st);
+      if (rc) return rc;
+    }
+  }
+  // 3. dw = g^T x
+  if (ga->dw) {
+    if (!a->x) return fail(TP_EINVAL, "x is required for the weight gradient");
+    const int dw_rows = ga->dw_rows > 0 ? ga->dw_rows : a->max_out;
+    const int dw_cols = ga->dw_cols > 0 ? ga->dw_cols : a->max_in;
+    if (dw_rows > a->max_out || dw_cols > a->max_in) return fail(TP_EINVAL, "dw is larger than the weight storage");
+    LinearProblem pr = base_problem(a);
+    pr.mode = MODE_WGRAD;
+    pr.out = ga->dw;
+    pr.out_rows = dw_rows;
+    pr.out_cols = dw_cols;
+    pr.out_ld = dw_cols;
+    pr.out_ms = (long long)dw_rows * dw_cols;
+    pr.copy_src = nullptr;
+    pr.a_ptr = G;
+    pr.b_ptr = a->x;
+    pr.dropout_p = nullptr;
+    if (tc) {
+      if (!aligned16(G) || !aligned16(a->x)) return fail(TP_EALIGN, "g and x must be 16-byte aligned");
+      constexpr int BN = 256;
+      pr.BM = 128;
+      pr.BN = BN;
+      pr.m_tiles = (dw_rows + 127) / 128;
+      pr.n_tiles = (dw_cols + BN - 1) / BN;
+      CUtensorMap ma, mb;
+      if ((rc = make_map(&ma, G, a->max_out, a->B, a->P, 64, 64))) return rc;
+      if ((rc = make_map(&mb, a->x, a->max_in, a->B, a->x_shared ? 1 : a->P, 64, 64))) return rc;
+      if ((rc = launch_sm100<BN, MODE_WGRAD>(pr, ma, mb, st))) return rc;
+    } else {
+      rc = bf16 ? launch_simt<__nv_bfloat16, MODE_WGRAD>(pr, st) : launch_simt<float, MODE_WGRAD>(pr, st);
+      if (rc) return rc;
+    }
+  }
+  return TP_OK;
+}
+
+int tp_dropout_mask(uint64_t seed, uint32_t offset, uint32_t member_base, const float* dropout_p, int32_t P, int32_t B,
+                    int32_t cols, uint8_t* mask, void* stream) {
+  if (!dropout_p || !mask || P <= 0 || B <= 0 || cols <= 0) return fail(TP_EINVAL, "bad dropout mask arguments");
+  const long long groups = (long long)P * B * ((cols + 7) / 8);
+  const int blocks = (int)std::min<long long>((groups + 255) / 256, 4096);
+  dropout_mask_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      (uint32_t)(seed & 0xFFFFFFFFu), (uint32_t)(seed >> 32), offset, member_base, dropout_p, P, B, cols, mask);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+int tp_adamw_step(const tp_adamw_args* a, void* stream) {
+  if (!a || a->n_tensors <= 0 || a->n_tensors > TP_MAX_OPT_TENSORS) return fail(TP_EINVAL, "bad tensor count");
+  AdamWTensors ts{};
+  int64_t max_numel = 0;
+  for (int i = 0; i < a->n_tensors; ++i) {
+    const tp_opt_tensor& t = a->t[i];
+    if (!t.p || !t.grad || !t.exp_avg || !t.exp_avg_sq || t.numel <= 0 || t.inner <= 0)
+      return fail(TP_EINVAL, "tensor %d: null pointer or empty", i);
+    ts.t[i] = t;
+    max_numel = std::max(max_numel, t.numel);
+  }
+  AdamWScalars s{};
+  s.lr = a->lr.per_member;
+  s.beta1 = a->beta1.per_member;
+  s.beta2 = a->beta2.per_member;
+  s.eps = a->eps.per_member;
+  s.wd = a->weight_decay.per_member;
+  s.lr_s = (float)a->lr.scalar;
+  s.beta1_s = (float)a->beta1.scalar;
+  s.beta2_s = (float)a->beta2.scalar;
+  s.eps_s = (float)a->eps.scalar;
+  s.wd_s = (float)a->weight_decay.scalar;
+  const bool lr_zero = !a->lr.per_member && a->lr.scalar == 0.0;
+  const bool wd_zero = !a->weight_decay.per_member && a->weight_decay.scalar == 0.0;
+  s.wd_on = !(lr_zero || wd_zero);
+  s.wd_mult_s = (float)(1.0 - a->lr.scalar * a->weight_decay.scalar);
+  s.one_m_b1_s = (float)(1.0 - a->beta1.scalar);
+  s.one_m_b2_s = (float)(1.0 - a->beta2.scalar);
+  s.scalar_bias_corr = !a->beta1.per_member && !a->beta2.per_member;
+  s.step = a->step;
+  if (s.scalar_bias_corr) {
+    const double bc1 = 1.0 - std::pow(a->beta1.scalar, (double)a->step);
+    const double bc2 = 1.0 - std::pow(a->beta2.scalar, (double)a->step);
+    s.bc1_s = (float)bc1;
+    s.step_size_s = (float)(a->lr.scalar / bc1);
+    s.sqrt_bc2_s = (float)std::sqrt(bc2);
+  }
+  const int bx = (int)std::min<int64_t>((max_numel + 255) / 256, 2048);
+  dim3 grid(bx, a->n_tensors);
+  adamw_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(ts, s);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+}  // extern "C"

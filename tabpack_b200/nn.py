@@ -1,0 +1,753 @@
+"""Module packs whose forward and backward run on the sm_100a kernels.
+
+Drop-in counterparts of the hot-path classes of `tabpackage.nn`
+(`src/tabpackage/nn.py`): same constructors, same parameter/buffer names and
+shapes (so state dicts interchange with the reference), same `pack_idx`,
+`replace`, `remove`, `temporarily_select` and `load_state_dict_at` behaviour.
+What changes is the arithmetic:
+
+* `LinearPack.forward` and a whole `MLPBackbonePack.Block` (linear -> ReLU ->
+  dropout) are one fused kernel launch, forward and backward, on tcgen05
+  tensor cores under bf16 autocast and on CUDA cores in fp32 mode;
+* ragged widths are never computed: each member's tiles stop at its own
+  `in_features` / `out_features`, and padding is written as exact zeros;
+* depth-varying members (`n_blocks`) are gated inside the same launch
+  (inactive members pass their input through) instead of `torch.where` over a
+  fully computed block;
+* dropout draws a counter-based Philox4x32-10 mask keyed by
+  (seed, call offset, member id, row, column) inside the epilogue, so masks are
+  reproducible and independent of how members are sharded over GPUs.
+
+There is no CPU path: calling a pack on CPU tensors raises.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import enum
+import itertools
+import math
+from typing import Any, Final
+
+import torch
+import torch.nn as nn
+from torch import Tensor
+
+from tabpack_b200 import ops
+
+PACK_DIM: Final = 0
+BATCH_DIM: Final = 1
+
+KWArgs = dict[str, Any]
+
+
+# >>> tensor packs
+
+
+class ParameterPack(nn.Parameter):
+    """A trainable tensor with a leading pack dimension (`nn.py:159-163`)."""
+
+
+class BufferPack(torch.Tensor):
+    """Marker for non-trainable pack tensors (`nn.py:188-201`).
+
+    Instances are plain tensors registered as buffers; `isinstance(t, BufferPack)`
+    holds for every tensor created through `BufferPack(data)`.
+    """
+
+    def __new__(cls, data: Tensor):
+        t = data.detach() if isinstance(data, Tensor) else torch.as_tensor(data)
+        t._is_buffer_pack = True  # type: ignore[attr-defined]
+        return t
+
+    @classmethod
+    def __instancecheck__(cls, instance):  # pragma: no cover - see metaclass below
+        return isinstance(instance, Tensor) and getattr(instance, '_is_buffer_pack', False)
+
+
+class _BufferPackMeta(type(torch.Tensor)):
+    def __instancecheck__(cls, instance):
+        return isinstance(instance, Tensor) and getattr(instance, '_is_buffer_pack', False)
+
+
+BufferPack = _BufferPackMeta('BufferPack', (), {  # noqa: F811
+    '__new__': lambda cls, data: _mark_buffer(data),
+    '__doc__': BufferPack.__doc__,
+})
+
+
+def _mark_buffer(data) -> Tensor:
+    t = data.detach() if isinstance(data, Tensor) else torch.as_tensor(data)
+    t._is_buffer_pack = True  # type: ignore[attr-defined]
+    return t
+
+
+def _like(x: Tensor, data: Tensor) -> Tensor:
+    if isinstance(x, nn.Parameter):
+        return ParameterPack(data, requires_grad=x.requires_grad)
+    return _mark_buffer(data)
+
+
+def check_pack_idx(pack_idx: Tensor, pack_size: int | None) -> None:
+    """`check_pack_idx` (`nn.py:116-122`)."""
+    if pack_idx.dtype not in (torch.int32, torch.int64):
+        raise TypeError('Indices must have the data type `torch.int32` or `torch.int64`')
+    if pack_idx.ndim != 1:
+        raise ValueError('Indices must be one-dimensional')
+    if len(pack_idx) == 0:
+        raise ValueError('Indices must not be empty')
+    if pack_size is not None and len(pack_idx) > pack_size:
+        raise ValueError('The number of pack indices must not exceed the pack size')
+
+
+def make_complementary_pack_idx(pack_idx: Tensor, *, pack_size: int) -> Tensor:
+    check_pack_idx(pack_idx, pack_size)
+    mask = torch.ones(pack_size, dtype=torch.bool, device=pack_idx.device)
+    mask[pack_idx] = False
+    return torch.nonzero(mask)[:, 0]
+
+
+def _select(x: Tensor | None, pack_idx: Tensor | None) -> Tensor | None:
+    if x is None or pack_idx is None:
+        return x
+    return x.index_select(PACK_DIM, torch.where(pack_idx < 0, pack_idx + x.shape[PACK_DIM], pack_idx))
+
+
+# >>> generic modules
+
+
+class PackView(nn.Module):
+    """`PackView` (`nn.py:39-99`): a 2-D input is shared by all members.
+
+    The expansion is not materialised: packs below consume a 2-D input directly
+    (the kernels read the shared rows once per member tile from L2).
+    """
+
+    def __init__(self, *, pack_size: int) -> None:
+        super().__init__()
+        self._pack_size = pack_size
+
+    @property
+    def pack_size(self) -> int:
+        return self._pack_size
+
+    def forward(self, x: Tensor, pack_idx: Tensor | None = None) -> Tensor:
+        if pack_idx is not None:
+            check_pack_idx(pack_idx, self.pack_size)
+        pack_size = self.pack_size if pack_idx is None else len(pack_idx)
+        if x.ndim == 2:
+            return x.unsqueeze(PACK_DIM).expand(pack_size, -1, -1)
+        if x.ndim != 3:
+            raise ValueError('The input must have two or three dimensions')
+        if not self.training:
+            raise RuntimeError('Three-dimensional input requires training mode')
+        if x.shape[PACK_DIM] != pack_size:
+            raise ValueError('The pack dimension of the input must match the selected pack size')
+        return x
+
+
+class ModulePack(nn.Module):
+    """Base class of module packs (`nn.py:282-531`)."""
+
+    @property
+    def pack_size(self) -> int:  # pragma: no cover - abstract
+        raise NotImplementedError
+
+    def try_get_pack_size(self) -> int | None:
+        try:
+            return self.pack_size
+        except RuntimeError:
+            return None
+
+    def _pack_tensors(self):
+        for name, x in itertools.chain(self.named_parameters(), self.named_buffers()):
+            if isinstance(x, ParameterPack) or getattr(x, '_is_buffer_pack', False):
+                yield name, x
+
+    def _owner(self, name: str):
+        if '.' in name:
+            sub, attr = name.rsplit('.', 1)
+            return self.get_submodule(sub), attr
+        return self, name
+
+    def load_state_dict_at(self, state_dict: dict[str, Tensor], *, pack_idx: Tensor,
+                           state_dict_idx: Tensor | None = None) -> None:
+        """`ModulePack.load_state_dict_at` (`nn.py:334-397`)."""
+        check_pack_idx(pack_idx, self.pack_size)
+        if self.state_dict().keys() != state_dict.keys():
+            raise ValueError('The state dictionary has missing or unexpected keys for this module')
+        with torch.no_grad():
+            for name, x in self._pack_tensors():
+                if name not in state_dict:
+                    continue
+                v = state_dict[name]
+                if v.ndim != x.ndim or v.shape[1:] != x.shape[1:]:
+                    raise ValueError('The source and destination tensors have incompatible shapes')
+                x[pack_idx] = (v if state_dict_idx is None else v[state_dict_idx]).to(x.device, x.dtype)
+        for m in self.modules():
+            if isinstance(m, MLPBackbonePack):
+                m._invalidate()
+
+    def remove(self, *, pack_idx: Tensor) -> dict:
+        """`ModulePack.remove` (`nn.py:417-463`)."""
+        check_pack_idx(pack_idx, self.pack_size)
+        if len(pack_idx) != len(torch.unique(pack_idx)):
+            raise ValueError('Pack indices to remove must be unique')
+        keep = None
+        mapping = {}
+        for name, x in list(self._pack_tensors()):
+            if keep is None:
+                keep = make_complementary_pack_idx(pack_idx, pack_size=x.shape[PACK_DIM])
+            owner, attr = self._owner(name)
+            new_x = _like(x, x.data[keep])
+            if isinstance(x, nn.Parameter):
+                setattr(owner, attr, new_x)
+                mapping[x] = new_x
+            else:
+                owner.register_buffer(attr, new_x, persistent=attr not in owner._non_persistent_buffers_set)
+        for m in self.modules():
+            if isinstance(m, PackView):
+                m._pack_size -= len(pack_idx)
+            if isinstance(m, MLPBackbonePack):
+                m._invalidate()
+        return mapping
+
+    @contextlib.contextmanager
+    def temporarily_select(self, *, pack_idx: Tensor):
+        """`ModulePack.temporarily_select` (`nn.py:469-531`)."""
+        check_pack_idx(pack_idx, None)
+        if any(m.training for m in self.modules()):
+            raise RuntimeError('The module and all its submodules must be in evaluation mode to use this method')
+        saved, views = [], []
+        try:
+            for name, x in list(self._pack_tensors()):
+                owner, attr = self._owner(name)
+                setattr(owner, attr, _like(x, x.data[pack_idx]))
+                saved.append((owner, attr, x))
+            for m in self.modules():
+                if isinstance(m, PackView):
+                    views.append((m, m.pack_size))
+                    m._pack_size = len(pack_idx)
+                if isinstance(m, MLPBackbonePack):
+                    m._invalidate()
+            yield
+        finally:
+            for owner, attr, x in saved:
+                setattr(owner, attr, x)
+            for m, n in views:
+                m._pack_size = n
+            for m in self.modules():
+                if isinstance(m, MLPBackbonePack):
+                    m._invalidate()
+
+
+def _positive_int_pack(value, max_value, *, pack_size):
+    """`_prepare_positive_integer_pack` (`nn.py:554-587`)."""
+    if isinstance(value, list):
+        if len(value) != pack_size:
+            raise ValueError('The number of per-member hyperparameter values does not match the pack size')
+        if not all(v > 0 for v in value):
+            raise ValueError('All values must be positive')
+        if max_value is None:
+            max_value = max(value)
+        elif not all(v <= max_value for v in value):
+            raise ValueError('Values must not exceed `max_value`')
+        return _mark_buffer(torch.tensor(value)), max_value
+    if value <= 0:
+        raise ValueError('The value must be positive')
+    if max_value is None:
+        max_value = value
+    elif max_value != value:
+        raise ValueError('The configured maximum must equal the shared value')
+    return None, max_value
+
+
+# >>> compute plumbing shared by LinearPack and Block
+
+
+class _DropoutStream:
+    """Philox key and call counter of one module (masks are reproducible given
+    the module's seed, its training-forward count and the member ids)."""
+
+    def __init__(self) -> None:
+        self.seed = int(torch.randint(0, 2**62, (1,), generator=None).item())
+        self.calls = 0
+        self.member_base = 0
+
+    def next_offset(self, stride: int = 1) -> int:
+        off = self.calls * stride
+        self.calls += 1
+        return off
+
+
+class _WeightCache:
+    """bf16 copy of an fp32 weight pack, refreshed when the weight changes
+    (every optimizer step bumps the parameter's version counter)."""
+
+    def __init__(self) -> None:
+        self.key = None
+        self.value = None
+
+    def get(self, w: Tensor, dtype: torch.dtype, cols: int) -> Tensor:
+        if w.dtype == dtype and w.shape[-1] == cols:
+            return w.detach()
+        key = (w.data_ptr(), w._version, dtype, cols, tuple(w.shape))
+        if self.key != key:
+            wd = w.detach().to(dtype)
+            if cols != w.shape[-1]:
+                wd = nn.functional.pad(wd, (0, cols - w.shape[-1]))
+            self.value = wd.contiguous()
+            self.key = key
+        return self.value
+
+
+def _compute_dtype(x: Tensor) -> torch.dtype:
+    if torch.is_autocast_enabled(x.device.type) and torch.get_autocast_dtype(x.device.type) == torch.bfloat16:
+        return torch.bfloat16
+    if x.dtype == torch.bfloat16:
+        return torch.bfloat16
+    return torch.float32
+
+
+def _round8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
+class _PackedLinearFn(torch.autograd.Function):
+    """One fused launch forward, three in backward (activation grad + bias grad,
+    dgrad, wgrad); `cfg` carries the non-tensor configuration."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, w_compute, cfg):
+        y = ops.linear_forward(x, w_compute, bias, **cfg['kw'])
+        ctx.cfg = cfg
+        ctx.x_shape = x.shape
+        ctx.save_for_backward(x, w_compute, y if (cfg['kw']['relu'] or cfg['kw']['dropout_p'] is not None) else None)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w_compute, y = ctx.saved_tensors
+        cfg = ctx.cfg
+        need_dx, need_dw, need_db = ctx.needs_input_grad[0], ctx.needs_input_grad[1], ctx.needs_input_grad[2]
+        dx, dw, db = ops.linear_backward(
+            dy.contiguous().to(w_compute.dtype), x, w_compute, y, **cfg['kw'],
+            need_dx=need_dx, need_dw=need_dw, need_db=need_db,
+            dw_shape=cfg['w_shape'][1:], db_cols=cfg['w_shape'][1])
+        if dx is not None:
+            if len(ctx.x_shape) == 2:
+                dx = dx.sum(PACK_DIM)
+            if dx.shape[-1] != cfg['in_cols']:
+                dx = dx[..., : cfg['in_cols']]
+        return dx, dw, db, None, None
+
+
+def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features=None, out_features=None,
+                  n_blocks=None, block_index=0, relu=False, dropout_p=None, seed=0, offset=0,
+                  member_base=0, cache: _WeightCache | None = None) -> Tensor:
+    """Functional form of the fused packed linear layer (see module docstring)."""
+    if not x.is_cuda:
+        raise RuntimeError('tabpack_b200 packs run on CUDA devices only')
+    dtype = _compute_dtype(x)
+    in_cols = x.shape[-1]
+    cols = _round8(in_cols) if dtype == torch.bfloat16 else in_cols
+    if cols != weight.shape[-1] and weight.shape[-1] != in_cols:
+        raise ValueError('The number of input features must be equal to the maximum supported number of features')
+    xc = x.to(dtype)
+    if cols != in_cols:
+        xc = nn.functional.pad(xc, (0, cols - in_cols))
+    xc = xc.contiguous()
+    wc = (cache or _WeightCache()).get(weight, dtype, cols)
+    kw = dict(in_features=in_features, out_features=out_features, n_blocks=n_blocks, block_index=block_index,
+              relu=relu, dropout_p=dropout_p, seed=seed, offset=offset, member_base=member_base)
+    cfg = {'kw': kw, 'w_shape': tuple(weight.shape), 'in_cols': in_cols}
+    with torch.autocast(x.device.type, enabled=False):
+        return _PackedLinearFn.apply(xc, weight, bias, wc, cfg)
+
+
+def _widths(buf: Tensor | None) -> Tensor | None:
+    return None if buf is None else buf.to(torch.int32)
+
+
+# >>> module packs
+
+
+class LinearPack(ModulePack):
+    """`LinearPack` (`nn.py:598-816`) on the fused ragged grouped GEMM."""
+
+    def __init__(self, in_features, out_features, bias: bool = True, *, max_in_features=None,
+                 max_out_features=None, pack_size: int, dtype=None, device=None) -> None:
+        if pack_size <= 0:
+            raise ValueError('The pack size must be positive')
+        fk = {'dtype': dtype, 'device': device}
+        inb, max_in = _positive_int_pack(in_features, max_in_features, pack_size=pack_size)
+        outb, max_out = _positive_int_pack(out_features, max_out_features, pack_size=pack_size)
+        super().__init__()
+        self.register_buffer('in_features', None if inb is None else _mark_buffer(inb.to(device)))
+        self.register_buffer('out_features', None if outb is None else _mark_buffer(outb.to(device)))
+        self.weight = ParameterPack(torch.empty(pack_size, max_out, max_in, **fk))
+        self.bias = ParameterPack(torch.empty(pack_size, max_out, **fk)) if bias else None
+        self._cache = _WeightCache()
+        self.reset_parameters()
+
+    @property
+    def max_in_features(self) -> int:
+        return self.weight.shape[-1]
+
+    @property
+    def max_out_features(self) -> int:
+        return self.weight.shape[-2]
+
+    @property
+    def pack_size(self) -> int:
+        return self.weight.shape[PACK_DIM]
+
+    def reset_parameters(self, *, pack_idx: Tensor | None = None) -> None:
+        """Per-member U(-1/sqrt(in_i), 1/sqrt(in_i)) (`nn.py:702-747`)."""
+        if pack_idx is not None:
+            check_pack_idx(pack_idx, self.pack_size)
+        n = self.pack_size if pack_idx is None else len(pack_idx)
+        if self.in_features is None:
+            bound = torch.full((n,), self.max_in_features ** -0.5)
+        else:
+            bound = _select(self.in_features, pack_idx).float().rsqrt().cpu()
+        for p in (self.weight, self.bias):
+            if p is None:
+                continue
+            shape = (n, *p.shape[1:])
+            bnd = bound.view(-1, *([1] * (p.ndim - 1))).to(p.device, p.dtype)
+            u = torch.rand(shape, dtype=p.dtype, device=p.device)
+            init = torch.lerp(-bnd.expand(shape), bnd.expand(shape), u)
+            with torch.no_grad():
+                if pack_idx is None:
+                    p.copy_(init)
+                else:
+                    p[pack_idx] = init
+
+    def replace(self, *, pack_idx: Tensor, in_features: list[int] | None = None,
+                out_features: list[int] | None = None) -> None:
+        """`LinearPack.replace` (`nn.py:749-790`)."""
+        check_pack_idx(pack_idx, self.pack_size)
+        updates = []
+        for buf, mx, vals in ((self.in_features, self.max_in_features, in_features),
+                              (self.out_features, self.max_out_features, out_features)):
+            if vals is None:
+                continue
+            if len(vals) != len(pack_idx):
+                raise ValueError('Each provided hyperparameter list must contain one value for each selected pack member')
+            if buf is None:
+                raise RuntimeError('Cannot replace feature counts that are shared by all pack members')
+            if not all(0 < v <= mx for v in vals):
+                raise ValueError('Feature counts must be positive and must not exceed the allocated maximum')
+            updates.append((buf, torch.tensor(vals, dtype=buf.dtype, device=buf.device)))
+        for buf, v in updates:
+            buf[pack_idx] = v
+        self.reset_parameters(pack_idx=pack_idx)
+
+    def forward(self, x: Tensor, pack_idx: Tensor | None = None) -> Tensor:
+        if x.ndim != 3:
+            raise ValueError('The input must have three dimensions')
+        if x.shape[-1] != self.max_in_features:
+            raise ValueError('The number of input features must be equal to the maximum supported number of features')
+        return _linear_call(self, x, pack_idx, relu=False, dropout=None, stream=None, n_blocks=None, block_index=0)
+
+
+def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stream, n_blocks, block_index,
+                 offset_stride: int = 1, offset_add: int = 0):
+    w, b = linear.weight, linear.bias
+    inf, outf = linear.in_features, linear.out_features
+    member_base = 0 if stream is None else stream.member_base
+    if pack_idx is not None:
+        check_pack_idx(pack_idx, linear.pack_size)
+        w, b, inf, outf = (_select(t, pack_idx) for t in (w, b, inf, outf))
+        n_blocks = _select(n_blocks, pack_idx)
+        if dropout is not None:
+            raise NotImplementedError('pack_idx with training-mode dropout is not supported; '
+                                      'use temporarily_select or remove')
+    if x.ndim == 3 and x.shape[0] == 1 and w.shape[0] != 1:
+        x = x[0]
+    elif x.ndim == 3 and x.stride(0) == 0:
+        x = x[0]
+    seed = offset = 0
+    if dropout is not None and stream is not None:
+        seed = stream.seed
+        offset = stream.next_offset(offset_stride) + offset_add
+    return packed_linear(x, w, b, in_features=_widths(inf), out_features=_widths(outf), n_blocks=n_blocks,
+                         block_index=block_index, relu=relu, dropout_p=dropout, seed=seed, offset=offset,
+                         member_base=member_base, cache=linear._cache if pack_idx is None else None)
+
+
+class DropoutPack(ModulePack):
+    """`DropoutPack` (`nn.py:819-903`) with the Philox keep mask.
+
+    Inside `MLPBackbonePack.Block` the mask is applied in the GEMM epilogue; a
+    standalone `DropoutPack` applies the same mask to its input.
+    """
+
+    def __init__(self, p, *, pack_size: int) -> None:
+        if isinstance(p, (int, float)):
+            if not math.isfinite(p) or p < 0.0 or p >= 1.0:
+                raise ValueError('The dropout probability must be finite and in [0, 1)')
+        else:
+            if len(p) != pack_size:
+                raise ValueError('Provide one dropout probability per pack member')
+            if any(not math.isfinite(v) or v < 0.0 or v >= 1.0 for v in p):
+                raise ValueError('Dropout probabilities must be finite and in [0, 1)')
+        super().__init__()
+        if isinstance(p, (int, float)):
+            self.p = float(p)
+        else:
+            self.register_buffer('p', _mark_buffer(torch.tensor([float(v) for v in p])))
+        self._stream = _DropoutStream()
+
+    @property
+    def pack_size(self) -> int:
+        if isinstance(self.p, (int, float)):
+            raise RuntimeError('Cannot infer the pack size')
+        return self.p.shape[PACK_DIM]
+
+    def replace(self, *, pack_idx: Tensor, p: list[float] | None = None) -> None:
+        if p is None:
+            return
+        if isinstance(self.p, (int, float)):
+            raise RuntimeError('Cannot replace dropout probabilities when one probability is shared by all pack members')
+        check_pack_idx(pack_idx, self.pack_size)
+        if len(p) != len(pack_idx):
+            raise ValueError('Each provided hyperparameter list must contain one value for each selected pack member')
+        if any(not math.isfinite(v) or v < 0.0 or v >= 1.0 for v in p):
+            raise ValueError('Dropout probabilities must be finite and in [0, 1)')
+        self.p[pack_idx] = torch.tensor(p, dtype=self.p.dtype, device=self.p.device)
+
+    def probabilities(self, pack_size: int, device) -> Tensor:
+        if isinstance(self.p, (int, float)):
+            return torch.full((pack_size,), float(self.p), device=device)
+        return self.p.to(device=device, dtype=torch.float32)
+
+    def forward(self, x: Tensor, pack_idx: Tensor | None = None) -> Tensor:
+        if not self.training:
+            return x
+        if not x.is_cuda:
+            raise RuntimeError('tabpack_b200 packs run on CUDA devices only')
+        p = self.probabilities(x.shape[0], x.device) if pack_idx is None else _select(self.p, pack_idx).float()
+        if x.ndim != 3:
+            raise ValueError('DropoutPack expects (pack, batch, features) inputs')
+        mask = ops.dropout_mask(seed=self._stream.seed, offset=self._stream.next_offset(),
+                                member_base=self._stream.member_base, p=p.contiguous(),
+                                rows=x.shape[1], cols=x.shape[2])
+        scale = (1.0 / (1.0 - p)).to(x.dtype)
+        return x * mask.to(x.dtype) * scale.view(-1, 1, 1)
+
+
+class MLPBackbonePack(ModulePack):
+    """`MLPBackbonePack` (`nn.py:996-1428`): each block is one fused launch."""
+
+    class Block(ModulePack):
+        """`MLPBackbonePack.Block` (`nn.py:1015-1079`): linear -> ReLU -> dropout, fused."""
+
+        def __init__(self, *, activation: KWArgs, dropout, pack_size: int, **linear_kwargs) -> None:
+            super().__init__()
+            self.linear = LinearPack(pack_size=pack_size, **linear_kwargs)
+            act = dict(activation)
+            cls = act.pop('type')
+            self.activation = cls(**act) if not issubclass(cls, ModulePack) else cls(pack_size=pack_size, **act)
+            self.dropout = DropoutPack(dropout, pack_size=pack_size)
+
+        @property
+        def pack_size(self) -> int:
+            return self.linear.pack_size
+
+        def replace(self, *, pack_idx: Tensor, in_features=None, out_features=None, activation=None,
+                    dropout=None) -> None:
+            self.linear.replace(pack_idx=pack_idx, in_features=in_features, out_features=out_features)
+            if activation is not None:
+                raise RuntimeError('The activation module does not support member replacement')
+            self.dropout.replace(pack_idx=pack_idx, p=dropout)
+
+        def _fused_relu(self) -> bool:
+            if isinstance(self.activation, nn.ReLU):
+                return True
+            if isinstance(self.activation, nn.Identity):
+                return False
+            raise NotImplementedError(f'fused blocks support ReLU or Identity, not {type(self.activation)}')
+
+        def forward(self, x: Tensor, pack_idx: Tensor | None = None, *, n_blocks: Tensor | None = None,
+                    block_index: int = 0, stream: _DropoutStream | None = None, offset_stride: int = 1) -> Tensor:
+            drop = None
+            if self.training:
+                drop = self.dropout.probabilities(self.pack_size, x.device).contiguous()
+                if isinstance(self.dropout.p, float) and self.dropout.p == 0.0:
+                    drop = None
+            return _linear_call(self.linear, x, pack_idx, relu=self._fused_relu(), dropout=drop,
+                                stream=stream or self.dropout._stream, n_blocks=n_blocks, block_index=block_index,
+                                offset_stride=offset_stride, offset_add=block_index)
+
+    @enum.unique
+    class ForwardImpl(enum.StrEnum):
+        """Both reference implementations (`nn.py:1081-1116`) map to the same
+        gated kernel; the value is kept for API compatibility."""
+
+        DENSE = enum.auto()
+        INDEXED = enum.auto()
+
+    def __init__(self, *, d_in, max_d_in=None, n_blocks, d_block, activation: KWArgs | None = None, dropout,
+                 max_n_blocks=None, max_d_block=None, forward_impl='dense', pack_size: int) -> None:
+        nb, max_n_blocks = _positive_int_pack(n_blocks, max_n_blocks, pack_size=pack_size)
+        super().__init__()
+        self.blocks = nn.ModuleList([
+            type(self).Block(
+                in_features=d_in if i == 0 else d_block, out_features=d_block,
+                max_in_features=max_d_in if i == 0 else max_d_block, max_out_features=max_d_block,
+                activation={'type': nn.ReLU} if activation is None else activation,
+                dropout=dropout, pack_size=pack_size)
+            for i in range(max_n_blocks)
+        ])
+        self._max_n_blocks: Final = max_n_blocks
+        self.register_buffer('n_blocks', nb)
+        self._forward_impl = MLPBackbonePack.ForwardImpl(forward_impl)
+        self._stream = _DropoutStream()
+        self._nb_cache = None
+
+    @property
+    def pack_size(self) -> int:
+        return self.blocks[0].pack_size
+
+    @property
+    def max_n_blocks(self) -> int:
+        return self._max_n_blocks
+
+    @property
+    def forward_impl(self):
+        return self._forward_impl
+
+    def set_forward_impl(self, impl) -> None:
+        self._forward_impl = MLPBackbonePack.ForwardImpl(impl)
+
+    def set_member_base(self, base: int) -> None:
+        """Global id of member 0 (for sharded packs: masks follow global ids)."""
+        self._stream.member_base = int(base)
+        for b in self.blocks:
+            b.dropout._stream.member_base = int(base)
+
+    def _invalidate(self) -> None:
+        self._nb_cache = None
+
+    def n_blocks_index_put_(self, indices, values) -> None:
+        if self.n_blocks is None:
+            raise RuntimeError('Cannot change block counts when all pack members share a fixed depth')
+        self._invalidate()
+        self.n_blocks.index_put_(indices, values)
+
+    def replace(self, *, pack_idx: Tensor, d_in=None, n_blocks=None, d_block=None, **kwargs) -> None:
+        check_pack_idx(pack_idx, self.pack_size)
+        new_nb = None
+        if n_blocks is not None:
+            if self.n_blocks is None:
+                raise RuntimeError('Cannot change block counts when all pack members share a fixed depth')
+            if len(n_blocks) != len(pack_idx):
+                raise ValueError('Each provided hyperparameter list must contain one value for each selected pack member')
+            if not all(0 < v <= self.max_n_blocks for v in n_blocks):
+                raise ValueError('Block counts must be positive and must not exceed `max_n_blocks`')
+            new_nb = torch.tensor(n_blocks, dtype=self.n_blocks.dtype, device=self.n_blocks.device)
+        for i, block in enumerate(self.blocks):
+            block.replace(pack_idx=pack_idx, in_features=d_in if i == 0 else d_block, out_features=d_block, **kwargs)
+        if new_nb is not None:
+            self.n_blocks_index_put_((pack_idx,), new_nb)
+
+    def _n_blocks_i32(self, pack_idx):
+        if self.n_blocks is None:
+            return None
+        nb = _select(self.n_blocks, pack_idx)
+        if pack_idx is not None:
+            return nb.to(torch.int32)
+        key = (self.n_blocks.data_ptr(), self.n_blocks._version if not self.n_blocks.is_inference() else -1)
+        if self._nb_cache is None or self._nb_cache[0] != key:
+            self._nb_cache = (key, nb.to(torch.int32))
+        return self._nb_cache[1]
+
+    def forward(self, x: Tensor, pack_idx: Tensor | None = None) -> Tensor:
+        if pack_idx is not None:
+            check_pack_idx(pack_idx, self.pack_size)
+        nb = self._n_blocks_i32(pack_idx)
+        stream = self._stream
+        base_offset = None
+        for i, block in enumerate(self.blocks):
+            if block.training and base_offset is None:
+                base_offset = stream.next_offset(self.max_n_blocks)
+            sub = _OffsetView(stream, base_offset)
+            x = block(x, pack_idx, n_blocks=nb if i > 0 else None, block_index=i, stream=sub)
+        return x
+
+
+class _OffsetView:
+    """Per-forward Philox offsets of an MLP backbone: block i of the k-th
+    training forward uses offset k * max_n_blocks + i."""
+
+    def __init__(self, stream: _DropoutStream, base: int | None) -> None:
+        self.seed = stream.seed
+        self.member_base = stream.member_base
+        self._base = base or 0
+
+    def next_offset(self, stride: int = 1) -> int:
+        return self._base
+
+
+class _OneHotEncoding(nn.Module):
+    """`_OneHotEncoding` (`nn.py:1836-1871`); the value `card` encodes as zeros."""
+
+    def __init__(self, cardinalities: list[int]) -> None:
+        super().__init__()
+        self._cardinalities = cardinalities
+
+    def forward(self, x: Tensor) -> Tensor:
+        if x.shape[-1] != len(self._cardinalities):
+            raise ValueError('The input must contain one categorical feature for each entry in `cardinalities`')
+        return torch.cat([nn.functional.one_hot(x[..., i], c + 1)[..., :-1]
+                          for i, c in enumerate(self._cardinalities)], -1)
+
+
+class TabPack(ModulePack):
+    """`TabPack` (`nn.py:1883-2110`) without numerical embeddings."""
+
+    def __init__(self, *, n_numerical_features: int, categorical_cardinalities: list[int], d_out: int,
+                 n_blocks, d_block, dropout, pack_size: int, numerical_embeddings: KWArgs | None = None,
+                 **backbone_kwargs) -> None:
+        super().__init__()
+        if numerical_embeddings is not None:
+            raise NotImplementedError('numerical embeddings are not part of the B200 hot path yet')
+        self.num_module = None
+        self.cat_module = _OneHotEncoding(categorical_cardinalities) if categorical_cardinalities else None
+        d_in = n_numerical_features + sum(categorical_cardinalities)
+        self.pack_view = PackView(pack_size=pack_size)
+        self.backbone = MLPBackbonePack(d_in=d_in, n_blocks=n_blocks, d_block=d_block, dropout=dropout,
+                                        pack_size=pack_size, **backbone_kwargs)
+        self.output = LinearPack(d_block, d_out, max_in_features=backbone_kwargs.get('max_d_block'),
+                                 pack_size=pack_size)
+        self._n_numerical_features = n_numerical_features
+        self._categorical_cardinalities = categorical_cardinalities
+
+    @property
+    def pack_size(self) -> int:
+        return self.backbone.pack_size
+
+    def replace(self, *, pack_idx: Tensor, numerical_embeddings=None, d_block=None, **kwargs) -> None:
+        if numerical_embeddings is not None:
+            raise RuntimeError('Cannot replace numerical embeddings because this model has none')
+        self.backbone.replace(pack_idx=pack_idx, d_block=d_block, **kwargs)
+        self.output.replace(pack_idx=pack_idx, in_features=d_block)
+
+    def forward(self, x_num: Tensor | None, x_cat: Tensor | None, pack_idx: Tensor | None = None) -> Tensor:
+        if x_num is None and x_cat is None:
+            raise ValueError('Provide at least one of `x_num` and `x_cat`')
+        parts = []
+        if x_num is not None:
+            parts.append(x_num)
+        if x_cat is not None:
+            if self.cat_module is None:
+                raise ValueError('`x_cat` can only be provided when categorical features are configured')
+            dt = x_num.dtype if x_num is not None else torch.get_default_dtype()
+            parts.append(self.cat_module(x_cat).to(dt))
+        x = torch.cat(parts, -1) if len(parts) > 1 else parts[0]
+        if x.ndim == 3 and not self.training:
+            raise RuntimeError('Three-dimensional input requires training mode')
+        x = self.backbone(x, pack_idx)
+        return self.output(x, pack_idx)

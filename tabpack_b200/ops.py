@@ -1,0 +1,215 @@
+"""Torch-facing wrappers of the C ABI.
+
+These functions only validate tensors, allocate outputs with PyTorch's caching
+allocator and pass raw pointers plus the current CUDA stream to the library.
+All arithmetic happens in the CUDA kernels; CPU tensors are rejected.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+from torch import Tensor
+
+from tabpack_b200 import _lib
+from tabpack_b200._lib import TP_DTYPE_BF16, TP_DTYPE_F32, check, load
+
+
+def _ptr(t: Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return TP_DTYPE_BF16
+    if dt == torch.float32:
+        return TP_DTYPE_F32
+    raise TypeError(f'unsupported activation dtype {dt} (bf16 or fp32)')
+
+
+def _cuda(name: str, t: Tensor | None, dtype: torch.dtype | None = None) -> Tensor | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise RuntimeError(f'{name} must be a CUDA tensor (tabpack_b200 has no CPU path)')
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f'{name} must have dtype {dtype}, got {t.dtype}')
+    return t.contiguous()
+
+
+def _i32(name: str, t: Tensor | None) -> Tensor | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise RuntimeError(f'{name} must be a CUDA tensor')
+    return t.to(torch.int32).contiguous()
+
+
+def _linear_args(x, weight, bias, in_features, out_features, n_blocks, block_index, relu,
+                 dropout_p, seed, offset, member_base, y) -> _lib.LinearArgs:
+    P, max_out, max_in = weight.shape
+    shared = x.ndim == 2
+    B = x.shape[0] if shared else x.shape[1]
+    a = _lib.LinearArgs()
+    a.P, a.B, a.max_in, a.max_out = P, B, max_in, max_out
+    a.dtype = _dtype_code(x.dtype)
+    a.x_shared = 1 if shared else 0
+    a.in_features = _ptr(in_features)
+    a.out_features = _ptr(out_features)
+    a.n_blocks = _ptr(n_blocks)
+    a.block_index = int(block_index)
+    a.relu = 1 if relu else 0
+    a.dropout_p = _ptr(dropout_p)
+    a.seed = int(seed) & 0xFFFFFFFFFFFFFFFF
+    a.offset = int(offset) & 0xFFFFFFFF
+    a.member_base = int(member_base) & 0xFFFFFFFF
+    a.x = _ptr(x)
+    a.w = _ptr(weight)
+    a.bias = _ptr(bias)
+    a.y = _ptr(y)
+    return a
+
+
+def linear_forward(
+    x: Tensor,
+    weight: Tensor,
+    bias: Tensor | None,
+    *,
+    in_features: Tensor | None = None,
+    out_features: Tensor | None = None,
+    n_blocks: Tensor | None = None,
+    block_index: int = 0,
+    relu: bool = False,
+    dropout_p: Tensor | None = None,
+    seed: int = 0,
+    offset: int = 0,
+    member_base: int = 0,
+) -> Tensor:
+    """Packed linear (+ReLU +dropout +depth gating) forward; see `tp_linear_forward`."""
+    weight = _cuda('weight', weight)
+    x = _cuda('x', x, weight.dtype)
+    bias = _cuda('bias', bias, torch.float32)
+    dropout_p = _cuda('dropout_p', dropout_p, torch.float32)
+    in_features, out_features, n_blocks = (_i32(n, t) for n, t in (
+        ('in_features', in_features), ('out_features', out_features), ('n_blocks', n_blocks)))
+    P, max_out, _ = weight.shape
+    B = x.shape[-2]
+    y = torch.empty((P, B, max_out), dtype=x.dtype, device=x.device)
+    a = _linear_args(x, weight, bias, in_features, out_features, n_blocks, block_index, relu,
+                     dropout_p, seed, offset, member_base, y)
+    check(load().tp_linear_forward(ctypes.byref(a), _stream()), 'tp_linear_forward')
+    return y
+
+
+def linear_backward(
+    dy: Tensor,
+    x: Tensor,
+    weight: Tensor,
+    y: Tensor | None,
+    *,
+    in_features: Tensor | None = None,
+    out_features: Tensor | None = None,
+    n_blocks: Tensor | None = None,
+    block_index: int = 0,
+    relu: bool = False,
+    dropout_p: Tensor | None = None,
+    seed: int = 0,
+    offset: int = 0,
+    member_base: int = 0,
+    need_dx: bool = True,
+    need_dw: bool = True,
+    need_db: bool = True,
+    dw_shape: tuple[int, int] | None = None,
+    db_cols: int | None = None,
+) -> tuple[Tensor | None, Tensor | None, Tensor | None]:
+    """Backward of `linear_forward`: returns (dx, dw, db); dw/db are fp32."""
+    weight = _cuda('weight', weight)
+    x = _cuda('x', x, weight.dtype)
+    dy = _cuda('dy', dy, weight.dtype)
+    y = _cuda('y', y, weight.dtype)
+    dropout_p = _cuda('dropout_p', dropout_p, torch.float32)
+    in_features, out_features, n_blocks = (_i32(n, t) for n, t in (
+        ('in_features', in_features), ('out_features', out_features), ('n_blocks', n_blocks)))
+    P, max_out, max_in = weight.shape
+    B = x.shape[-2]
+    need_g = relu or dropout_p is not None or out_features is not None or n_blocks is not None
+    g = torch.empty_like(dy) if need_g else None
+    dx = torch.empty((P, B, max_in), dtype=dy.dtype, device=dy.device) if need_dx else None
+    rows, cols = dw_shape if dw_shape is not None else (max_out, max_in)
+    dw = torch.empty((P, rows, cols), dtype=torch.float32, device=dy.device) if need_dw else None
+    dbc = db_cols if db_cols is not None else max_out
+    db = torch.empty((P, dbc), dtype=torch.float32, device=dy.device) if need_db else None
+    ga = _lib.LinearGradArgs()
+    ga.fwd = _linear_args(x, weight, None, in_features, out_features, n_blocks, block_index, relu,
+                          dropout_p, seed, offset, member_base, None)
+    ga.dy, ga.y, ga.g = _ptr(dy), _ptr(y), _ptr(g)
+    ga.dbias, ga.dx, ga.dw = _ptr(db), _ptr(dx), _ptr(dw)
+    ga.dw_rows, ga.dw_cols, ga.db_cols = rows, cols, dbc
+    check(load().tp_linear_backward(ctypes.byref(ga), _stream()), 'tp_linear_backward')
+    return dx, dw, db
+
+
+def dropout_mask(*, seed: int, offset: int, member_base: int, p: Tensor, rows: int, cols: int) -> Tensor:
+    """(P, rows, cols) uint8 Philox keep mask used by the fused dropout."""
+    p = _cuda('p', p, torch.float32)
+    P = p.shape[0]
+    mask = torch.empty((P, rows, cols), dtype=torch.uint8, device=p.device)
+    check(load().tp_dropout_mask(int(seed) & 0xFFFFFFFFFFFFFFFF, int(offset) & 0xFFFFFFFF,
+                                 int(member_base) & 0xFFFFFFFF, p.data_ptr(), P, rows, cols,
+                                 mask.data_ptr(), _stream()), 'tp_dropout_mask')
+    return mask
+
+
+def _hparam(v) -> _lib.HParam:
+    h = _lib.HParam()
+    if isinstance(v, Tensor):
+        if not v.is_cuda or v.dtype != torch.float32 or v.ndim != 1:
+            raise TypeError('per-member hyperparameters must be 1-D fp32 CUDA tensors')
+        h.per_member = v.data_ptr()
+        h.scalar = 0.0
+    else:
+        h.per_member = None
+        h.scalar = float(v)
+    return h
+
+
+def adamw_step(params, grads, exp_avgs, exp_avg_sqs, *, steps=None, step: int = 0,
+               lr, beta1, beta2, eps, weight_decay) -> None:
+    """Grouped AdamW over parameter packs (each (P, ...) fp32, contiguous).
+
+    `steps` (per-tensor (P,) int64 tensors, already incremented) or the scalar
+    `step` give the bias-correction step.  Hyperparameters are floats or (P,)
+    fp32 CUDA tensors.  Tensors are chunked into launches of at most 32.
+    """
+    hp = [lr, beta1, beta2, eps, weight_decay]
+    hp = [v.contiguous() if isinstance(v, Tensor) else v for v in hp]
+    n = len(params)
+    for s in range(0, n, _lib.TP_MAX_OPT_TENSORS):
+        a = _lib.AdamWArgs()
+        chunk = range(s, min(n, s + _lib.TP_MAX_OPT_TENSORS))
+        a.n_tensors = len(chunk)
+        for j, i in enumerate(chunk):
+            p = params[i]
+            for name, t in (('param', p), ('grad', grads[i]), ('exp_avg', exp_avgs[i]),
+                            ('exp_avg_sq', exp_avg_sqs[i])):
+                if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
+                    raise TypeError(f'{name} must be a contiguous fp32 CUDA tensor')
+            ot = a.t[j]
+            ot.p, ot.grad = p.data_ptr(), grads[i].data_ptr()
+            ot.exp_avg, ot.exp_avg_sq = exp_avgs[i].data_ptr(), exp_avg_sqs[i].data_ptr()
+            ot.step = None if steps is None else steps[i].data_ptr()
+            ot.numel = p.numel()
+            ot.inner = max(1, p.numel() // p.shape[0])
+        a.lr, a.beta1, a.beta2, a.eps, a.weight_decay = (_hparam(v) for v in hp)
+        a.step = int(step)
+        check(load().tp_adamw_step(ctypes.byref(a), _stream()), 'tp_adamw_step')
+
+
+def device_error() -> int:
+    """Read and clear the device-side error flag (0 or TP_ETIMEOUT)."""
+    return load().tp_device_error()

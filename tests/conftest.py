@@ -22,3 +22,10 @@ def golden():
         return np.load(os.path.join(GOLDEN, name))
 
     return load
+
+
+def pytest_sessionstart(session):
+    # The CUDA library is built in-tree; rebuild it when a source is newer.
+    from tabpack_b200.csrc import build
+
+    build.build()

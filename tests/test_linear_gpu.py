@@ -1,0 +1,244 @@
+"""Parity of the packed-linear CUDA kernels (called through the C ABI) with the oracle.
+
+bf16 runs on tcgen05 tensor cores: inputs are bf16-exact, so the reference is the
+oracle evaluated in float64 on the same bf16 values, and the only error left is
+fp32 accumulation plus one bf16 rounding of each output (tolerance 2^-7
+relative, far inside the 2e-2 bar).  fp32 runs on CUDA cores and must agree with
+the oracle to 1e-5 relative (the bar is 1e-4).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import layers as ol
+from oracle.philox import dropout_keep_mask
+
+pytestmark = pytest.mark.gpu
+
+BF16_RTOL = 2.0 ** -7
+
+
+@pytest.fixture(scope='module', autouse=True)
+def _lib():
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+    from tabpack_b200 import _lib as L
+
+    L.load()
+
+
+def _bf16(a: np.ndarray) -> np.ndarray:
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).bfloat16().float().numpy().astype(np.float64)
+
+
+def _dev(a, dtype):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device='cuda', dtype=dtype)
+
+
+def _host(t):
+    return t.float().cpu().numpy().astype(np.float64)
+
+
+def _close(got, want, rtol, what):
+    scale = max(np.abs(want).max(), 1e-30)
+    err = np.abs(got - want)
+    bad = err > rtol * np.abs(want) + rtol * 0.25 * scale
+    assert not bad.any(), f'{what}: {bad.sum()} / {bad.size} mismatches, max err {err.max():.3e} (scale {scale:.3e})'
+
+
+def make_case(P, B, max_in, max_out, in_f=None, out_f=None, shared=False, seed=0, p_max=0.5):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((1 if shared else P, B, max_in))
+    if in_f is not None and not shared:
+        x = x * (np.arange(max_in)[None, None, :] < np.asarray(in_f)[:, None, None])
+    fan = np.asarray(in_f if in_f is not None else [max_in] * P, np.float64)
+    w = rng.uniform(-1, 1, (P, max_out, max_in)) / np.sqrt(fan)[:, None, None]
+    b = rng.uniform(-1, 1, (P, max_out)) / np.sqrt(fan)[:, None]
+    p = rng.uniform(0, p_max, P).astype(np.float32)
+    p[0] = 0.0
+    return x, w, b, p
+
+
+def oracle_forward(x, w, b, out_f, p, seed, offset, member_base, B, relu=True, dropout=True):
+    P, max_out, _ = w.shape
+    mv = None
+    if dropout:
+        mv = ol.dropout_mask_values(seed=seed, offset=offset, members=np.arange(P) + member_base,
+                                    n_rows=B, n_cols=max_out, p=p, dtype=np.float64)
+    y, _ = ol.block_forward(x if x.shape[0] == P else np.broadcast_to(x, (P, *x.shape[1:])),
+                            w, b, out_f, mask_values=mv, relu=relu)
+    return y, mv
+
+
+@pytest.mark.parametrize('P,B,cols,seed,offset,base', [(3, 37, 50, 1, 0, 0), (5, 130, 264, 2**40 + 7, 9, 1000)])
+def test_dropout_mask_bit_exact(P, B, cols, seed, offset, base):
+    from tabpack_b200 import ops
+
+    p = np.array([0.0, 0.1, 0.37, 0.5, 0.99][:P], np.float32)
+    got = ops.dropout_mask(seed=seed, offset=offset, member_base=base, p=_dev(p, torch.float32), rows=B, cols=cols)
+    want = dropout_keep_mask(seed=seed, offset=offset, members=np.arange(P) + base, n_rows=B, n_cols=cols, p=p)
+    assert np.array_equal(got.cpu().numpy().astype(bool), want)
+
+
+CASES = [
+    # P, B, max_in, max_out, in_f, out_f, shared
+    (3, 300, 72, 520, [72, 16, 40], [520, 16, 264], False),
+    (2, 128, 512, 1024, None, None, False),
+    (4, 200, 64, 256, None, [256, 8, 136, 200], True),
+    (2, 77, 24, 40, [24, 9], [40, 33], False),
+]
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize('case', range(len(CASES)))
+@pytest.mark.parametrize('dropout', [True, False])
+def test_forward(dtype, case, dropout):
+    from tabpack_b200 import ops
+
+    P, B, max_in, max_out, in_f, out_f, shared = CASES[case]
+    x, w, b, p = make_case(P, B, max_in, max_out, in_f, out_f, shared, seed=case)
+    if dtype == torch.bfloat16:
+        x, w = _bf16(x), _bf16(w)
+    seed, offset, base = 1234567 + case, 3, 17
+    y = ops.linear_forward(
+        _dev(x[0] if shared else x, dtype), _dev(w, dtype), _dev(b, torch.float32),
+        in_features=None if in_f is None else _dev(np.array(in_f), torch.int32),
+        out_features=None if out_f is None else _dev(np.array(out_f), torch.int32),
+        relu=True, dropout_p=_dev(p, torch.float32) if dropout else None,
+        seed=seed, offset=offset, member_base=base)
+    torch.cuda.synchronize()
+    want, _ = oracle_forward(x, w, b.astype(np.float32).astype(np.float64), out_f, p, seed, offset, base, B,
+                             dropout=dropout)
+    _close(_host(y), want, BF16_RTOL if dtype == torch.bfloat16 else 1e-5, f'y case {case}')
+
+
+def test_plain_gemm_matches_torch_fp32():
+    """No widths, no activation: the tcgen05 GEMM against torch's fp32 matmul."""
+    from tabpack_b200 import ops
+
+    torch.manual_seed(0)
+    P, B, K, N = 3, 384, 320, 512
+    x = torch.randn(P, B, K, device='cuda').bfloat16()
+    w = torch.randn(P, N, K, device='cuda').bfloat16() / K ** 0.5
+    y = ops.linear_forward(x, w, None)
+    ref = torch.bmm(x.float(), w.float().transpose(1, 2))
+    err = (y.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 2 ** -7, err
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize('case', range(len(CASES)))
+def test_backward(dtype, case):
+    from tabpack_b200 import ops
+
+    P, B, max_in, max_out, in_f, out_f, shared = CASES[case]
+    x, w, b, p = make_case(P, B, max_in, max_out, in_f, out_f, shared, seed=10 + case)
+    if dtype == torch.bfloat16:
+        x, w = _bf16(x), _bf16(w)
+    seed, offset, base = 99, 1, 0
+    kw = dict(in_features=None if in_f is None else _dev(np.array(in_f), torch.int32),
+              out_features=None if out_f is None else _dev(np.array(out_f), torch.int32),
+              relu=True, dropout_p=_dev(p, torch.float32), seed=seed, offset=offset, member_base=base)
+    xd, wd = _dev(x[0] if shared else x, dtype), _dev(w, dtype)
+    y = ops.linear_forward(xd, wd, _dev(b, torch.float32), **kw)
+    rng = np.random.default_rng(case)
+    dy = rng.standard_normal((P, B, max_out))
+    if dtype == torch.bfloat16:
+        dy = _bf16(dy)
+    dx, dW, db = ops.linear_backward(_dev(dy, dtype), xd, wd, y, **kw)
+    torch.cuda.synchronize()
+    # reference gradient w.r.t. the pre-activation, using the kernel's own y for the ReLU mask
+    mv = ol.dropout_mask_values(seed=seed, offset=offset, members=np.arange(P), n_rows=B, n_cols=max_out,
+                                p=p, dtype=np.float64)
+    yh = _host(y)
+    g = dy * mv * (yh > 0)
+    if out_f is not None:
+        g = g * ol.col_mask(out_f, max_out, np.float64)
+    gq = _bf16(g) if dtype == torch.bfloat16 else g
+    xb = np.broadcast_to(x, (P, B, max_in))
+    tol = BF16_RTOL if dtype == torch.bfloat16 else 1e-5
+    _close(_host(db), g.sum(1), 1e-4 if dtype == torch.bfloat16 else 1e-5, 'db')
+    _close(_host(dW), np.matmul(np.swapaxes(gq, 1, 2), xb), tol, 'dW')
+    dx_ref = np.matmul(gq, w)
+    if in_f is not None:
+        dx_ref = dx_ref * ol.col_mask(in_f, max_in, np.float64)
+    _close(_host(dx), dx_ref, tol, 'dx')
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
+def test_depth_gating(dtype):
+    """Members with n_blocks <= block_index pass x through (forward) and dy through (dgrad)."""
+    from tabpack_b200 import ops
+
+    P, B, W = 4, 150, 192
+    x, w, b, p = make_case(P, B, W, W, seed=5)
+    if dtype == torch.bfloat16:
+        x, w = _bf16(x), _bf16(w)
+    nb = np.array([1, 2, 3, 1], np.int32)
+    kw = dict(n_blocks=_dev(nb, torch.int32), block_index=1, relu=True, dropout_p=_dev(p, torch.float32),
+              seed=5, offset=2)
+    xd, wd = _dev(x, dtype), _dev(w, dtype)
+    y = ops.linear_forward(xd, wd, _dev(b, torch.float32), **kw)
+    dy = _dev(np.random.default_rng(1).standard_normal((P, B, W)), dtype)
+    dx, dW, db = ops.linear_backward(dy, xd, wd, y, **kw)
+    torch.cuda.synchronize()
+    want, _ = oracle_forward(x, w, b.astype(np.float32).astype(np.float64), None, p, 5, 2, 0, B)
+    tol = BF16_RTOL if dtype == torch.bfloat16 else 1e-5
+    for m in range(P):
+        if nb[m] > 1:
+            _close(_host(y[m]), want[m], tol, f'y[{m}]')
+        else:
+            assert torch.equal(y[m], xd[m])
+            assert torch.equal(dx[m], dy[m])
+            assert torch.count_nonzero(dW[m]) == 0 and torch.count_nonzero(db[m]) == 0
+
+
+def test_golden_block_fp32(golden):
+    """The fp32 path against the reference's own outputs and gradients."""
+    from tabpack_b200 import ops
+
+    g = golden('block_fp32.npz')
+    P, B, max_in = g['x'].shape
+    kw = dict(in_features=_dev(g['in_features'], torch.int32), out_features=_dev(g['out_features'], torch.int32),
+              relu=True, dropout_p=_dev(g['p'], torch.float32), seed=int(g['seed']), offset=int(g['offset']))
+    xd, wd = _dev(g['x'], torch.float32), _dev(g['weight'], torch.float32)
+    y = ops.linear_forward(xd, wd, _dev(g['bias'], torch.float32), **kw)
+    dx, dW, db = ops.linear_backward(_dev(g['dy'], torch.float32), xd, wd, y, **kw)
+    torch.cuda.synchronize()
+    _close(_host(y), g['y'], 1e-5, 'y')
+    _close(_host(dW), g['dweight'], 1e-5, 'dW')
+    _close(_host(db), g['dbias'], 1e-5, 'db')
+    # the reference's dx carries products with random pad weights beyond in_features;
+    # those columns are masked by the previous layer and are zero here
+    m = ol.col_mask(g['in_features'], max_in, np.float64)
+    _close(_host(dx), g['dx'] * m, 1e-5, 'dx')
+
+
+@pytest.mark.parametrize('case', [0, 1, 2, 3])
+def test_adamw_golden(golden, case):
+    from tabpack_b200 import ops
+
+    g = golden('adamw.npz')
+    pm = bool(g[f'c{case}.per_member'])
+    sr = bool(g[f'c{case}.support_replacement'])
+    hp = {}
+    for k in ('lr', 'beta1', 'beta2', 'eps', 'weight_decay'):
+        v = g[f'c{case}.hp.{k}']
+        hp[k] = _dev(v.astype(np.float32), torch.float32) if pm else float(v)
+    w = _dev(g[f'c{case}.w0'], torch.float32)
+    b = _dev(g[f'c{case}.b0'], torch.float32)
+    ms = [torch.zeros_like(w), torch.zeros_like(b)]
+    vs = [torch.zeros_like(w), torch.zeros_like(b)]
+    steps = [torch.zeros(w.shape[0], dtype=torch.int64, device='cuda') for _ in range(2)]
+    for s in range(3):
+        gw, gb = _dev(g[f'c{case}.s{s}.gw'], torch.float32), _dev(g[f'c{case}.s{s}.gb'], torch.float32)
+        for st in steps:
+            st += 1
+        ops.adamw_step([w, b], [gw, gb], ms, vs, steps=steps if sr else None, step=s + 1, **hp)
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(w.cpu().numpy(), g[f'c{case}.s{s}.w'], rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(b.cpu().numpy(), g[f'c{case}.s{s}.b'], rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(ms[0].cpu().numpy(), g[f'c{case}.s{s}.m_w'], rtol=1e-5, atol=1e-9)
+        np.testing.assert_allclose(vs[0].cpu().numpy(), g[f'c{case}.s{s}.v_w'], rtol=1e-5, atol=1e-12)
+    assert ops.device_error() == 0
