@@ -90,6 +90,31 @@ int tp_linear_forward(const tp_linear_args* a, void* stream);
  * out_features x in_features are zero). */
 int tp_linear_backward(const tp_linear_grad_args* a, void* stream);
 
+/* Size of the built-in workspace of tp_linear_backward_noalloc: 16 MiB. */
+#define TP_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* No counterpart in the reference: an addition of this library.
+ *
+ * tp_linear_backward for callers that must not allocate device memory, for
+ * example a host framework that owns all GPU memory through its own pool, or
+ * code that runs where an allocation is not allowed.  The caller passes the
+ * same arguments as for tp_linear_backward with `g` left NULL (inputs and
+ * outputs stay caller-owned); the activation-gradient workspace comes from a
+ * fixed device array inside this library, so the call allocates nothing.
+ *
+ * Limits and behaviour:
+ *  - the workspace needs P * B * max_out elements (2 bytes in BF16 mode,
+ *    4 bytes in F32 mode); larger calls are rejected with TP_EINVAL before any
+ *    kernel runs;
+ *  - every GPU that loads the library holds the TP_NOALLOC_SCRATCH_BYTES array
+ *    until the process exits;
+ *  - the first call on each device looks up the array's device address (set-up)
+ *    and should come before any CUDA stream capture;
+ *  - all calls share the one array and it keeps the last call's contents; calls
+ *    whose kernels overlap on the GPU (different streams, no ordering) race;
+ *  - `g_ready` is ignored: the activation gradient is always recomputed. */
+int tp_linear_backward_noalloc(const tp_linear_grad_args* a, void* stream);
+
 /* Test hook: the Philox keep mask of the dropout above, (P, B, cols) uint8. */
 int tp_dropout_mask(uint64_t seed, uint32_t offset, uint32_t member_base,
                     const float* dropout_p, int32_t P, int32_t B, int32_t cols,

@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(_HERE, 'libtabpack_b200.so')
 TP_DTYPE_F32 = 0
 TP_DTYPE_BF16 = 1
 TP_MAX_OPT_TENSORS = 32
+TP_NOALLOC_SCRATCH_BYTES = 16 << 20
 
 _c_int32_p = ctypes.POINTER(ctypes.c_int32)
 _c_float_p = ctypes.POINTER(ctypes.c_float)
@@ -66,6 +67,7 @@ class AdamWArgs(ctypes.Structure):
 SIGNATURES = {
     'tp_linear_forward': (ctypes.c_int, [ctypes.POINTER(LinearArgs), ctypes.c_void_p]),
     'tp_linear_backward': (ctypes.c_int, [ctypes.POINTER(LinearGradArgs), ctypes.c_void_p]),
+    'tp_linear_backward_noalloc': (ctypes.c_int, [ctypes.POINTER(LinearGradArgs), ctypes.c_void_p]),
     'tp_dropout_mask': (ctypes.c_int, [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
                                        ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
                                        ctypes.c_void_p]),

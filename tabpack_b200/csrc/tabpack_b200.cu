@@ -95,6 +95,30 @@ int make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t rows, u
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Workspace of tp_linear_backward_noalloc (device memory reserved at module load).
+// Host code must not pass this symbol to a kernel: on the host it is only a
+// stand-in, and the device address is looked up per device below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[TP_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up once per device).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  TP_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(TP_EUNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return TP_OK;
+}
+
 template <int BN, int MODE>
 int launch_sm100(const LinearProblem& pr, const CUtensorMap& a, const CUtensorMap& b, cudaStream_t st) {
   using Cfg = Sm100Cfg<BN, MODE>;
@@ -319,6 +343,31 @@ int tp_linear_backward(const tp_linear_grad_args* ga, void* stream) {
     }
   }
   return TP_OK;
+}
+
+int tp_linear_backward_noalloc(const tp_linear_grad_args* ga, void* stream) {
+  if (!ga) return fail(TP_EINVAL, "null arguments");
+  if (ga->g) return fail(TP_EINVAL, "tp_linear_backward_noalloc uses its own workspace: pass g = NULL");
+  const tp_linear_args* a = &ga->fwd;
+  int rc = check_linear(a);
+  if (rc) return rc;
+  tp_linear_grad_args b = *ga;
+  b.g_ready = 0;
+  const bool need_g = a->relu || a->dropout_p || a->out_features || a->n_blocks;
+  if (need_g) {
+    const unsigned long long elem = a->dtype == TP_DTYPE_BF16 ? 2ull : 4ull;
+    const unsigned long long bytes = (unsigned long long)a->P * (unsigned long long)a->B *
+                                     (unsigned long long)a->max_out * elem;
+    if (bytes > (unsigned long long)TP_NOALLOC_SCRATCH_BYTES)
+      return fail(TP_EINVAL,
+                  "tp_linear_backward_noalloc: P*B*max_out = %d*%d*%d elements need %llu bytes of workspace, "
+                  "more than the %u-byte built-in scratch; use tp_linear_backward with a caller-provided g",
+                  a->P, a->B, a->max_out, bytes, (unsigned)TP_NOALLOC_SCRATCH_BYTES);
+    void* scratch = nullptr;
+    if ((rc = noalloc_scratch(&scratch))) return rc;
+    b.g = scratch;
+  }
+  return tp_linear_backward(&b, stream);
 }
 
 int tp_dropout_mask(uint64_t seed, uint32_t offset, uint32_t member_base, const float* dropout_p, int32_t P, int32_t B,
