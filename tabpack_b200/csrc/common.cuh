@@ -22,15 +22,11 @@ __device__ int g_device_error = 0;
 __host__ __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
 #pragma unroll
   for (int i = 0; i < 10; ++i) {
-#ifdef __CUDA_ARCH__
-    const uint32_t hi0 = __umulhi(0xD2511F53u, c.x);
-    const uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z);
-#else
-    const uint32_t hi0 = (uint32_t)(((uint64_t)0xD2511F53u * c.x) >> 32);
-    const uint32_t hi1 = (uint32_t)(((uint64_t)0xCD9E8D57u * c.z) >> 32);
-#endif
-    const uint32_t lo0 = 0xD2511F53u * c.x;
-    const uint32_t lo1 = 0xCD9E8D57u * c.z;
+    // one 32x32->64-bit multiply per product
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c.x;
+    const uint64_t p1 = (uint64_t)0xCD9E8D57u * c.z;
+    const uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0;
+    const uint32_t hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
     c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
     k0 += 0x9E3779B9u;
     k1 += 0xBB67AE85u;

@@ -7,8 +7,10 @@
 //   MODE_DGRAD: C[B x in_m]   = G[B x out_m] * W            A K-major, B MN-major
 //   MODE_WGRAD: C[out_m x in_m] = G^T * X  (K = batch rows)  A MN-major, B MN-major
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
-// issuer, warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31).
+// Warp roles (576 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
+// issuer, warps 2..17 = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31 and
+// column quarter (w-2)/4), four epilogue warps per SM sub-partition so that TMEM
+// loads, Philox chains and stores of one warp overlap the others.
 #pragma once
 
 #include "linear_problem.cuh"
@@ -27,13 +29,113 @@ struct Sm100Cfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int NUM_THREADS = 192;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
   // stages + barriers (full, empty per stage; tfull, tempty x2; done) + tmem addr + abort
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+  // + per-warp bias slice (BN / (EPI_WARPS / 4) floats per epilogue warp)
+  static constexpr int BIAS_FLOATS_PER_WARP = BN / (EPI_WARPS / 4);
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + EPI_WARPS * BIAS_FLOATS_PER_WARP * 4;
 };
 
+// Epilogue of one 32-column chunk of one output row held in registers `r`
+// (raw fp32 accumulator bits from tcgen05.ld).
+template <int MODE>
+__device__ __forceinline__ void epi_chunk(const LinearProblem& pr, const TileInfo& ti, int m, int row, int col0,
+                                          const uint32_t (&r)[32], bool dropout_on, uint32_t thr, float scale,
+                                          const float* sbias) {
+  const int nv = ti.n_valid - col0;  // valid columns in this chunk (may be <= 0)
+  if (MODE == MODE_FWD) {
+    // streamed in groups of 8 columns: bias, ReLU, Philox keep, bf16 pack, 16-byte store
+    __nv_bfloat16* dst =
+        reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld + col0;
+    const int ncols = pr.out_cols - col0;
+    const bool drop = dropout_on && thr < 65536u;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (8 * g >= ncols) break;
+      float x[8];
+      const int gv = nv - 8 * g;  // valid columns in this group
+      if (gv <= 0) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[j] = 0.0f;
+      } else {
+        // bias slice staged in shared memory by this warp (zero beyond n_valid)
+        const float4 b0 = *reinterpret_cast<const float4*>(sbias + 8 * g);
+        const float4 b1 = *reinterpret_cast<const float4*>(sbias + 8 * g + 4);
+        const float b8[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        if (drop) {
+          // relu(t) * (keep ? scale : 0) == max(t * (keep ? scale : 0), 0) since scale > 0
+          const uint4 w = philox4x32_10(
+              make_uint4((uint32_t)(col0 >> 3) + g, (uint32_t)row, pr.member_base + (uint32_t)m, pr.offset), pr.k0,
+              pr.k1);
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t r16 = (j & 1) ? (ws[j >> 1] >> 16) : (ws[j >> 1] & 0xFFFFu);
+            const float mult = r16 < thr ? scale : 0.0f;
+            const float t = (__uint_as_float(r[8 * g + j]) + b8[j]) * mult;
+            x[j] = pr.relu ? fmaxf(t, 0.0f) : t;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float t = __uint_as_float(r[8 * g + j]) + b8[j];
+            x[j] = pr.relu ? fmaxf(t, 0.0f) : t;
+          }
+        }
+        if (gv < 8) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) x[j] = j < gv ? x[j] : 0.0f;
+        }
+      }
+      uint4 u;
+      u.x = pack_bf16x2(x[0], x[1]);
+      u.y = pack_bf16x2(x[2], x[3]);
+      u.z = pack_bf16x2(x[4], x[5]);
+      u.w = pack_bf16x2(x[6], x[7]);
+      *reinterpret_cast<uint4*>(dst + 8 * g) = u;  // out_cols is a multiple of 8 on this path
+    }
+    return;
+  }
+  float v[32];
+  if (MODE == MODE_DGRAD) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = j < nv ? __uint_as_float(r[j]) : 0.0f;
+  } else {
+    const bool rv = row < ti.m_valid;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (rv && j < nv) ? __uint_as_float(r[j]) : 0.0f;
+  }
+  const int ncols = pr.out_cols - col0;  // storable columns in this chunk (> 0)
+  if (MODE == MODE_WGRAD) {
+    float* dst = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld + col0;
+    if (ncols >= 32 && (pr.out_ld & 3) == 0) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols) dst[j] = v[j];
+    }
+  } else {
+    __nv_bfloat16* dst =
+        reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld + col0;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      if (j < ncols) {  // out_cols is a multiple of 8 on this path
+        uint4 u;
+        u.x = pack_bf16x2(v[j], v[j + 1]);
+        u.y = pack_bf16x2(v[j + 2], v[j + 3]);
+        u.z = pack_bf16x2(v[j + 4], v[j + 5]);
+        u.w = pack_bf16x2(v[j + 6], v[j + 7]);
+        *reinterpret_cast<uint4*>(dst + j) = u;
+      }
+    }
+  }
+}
+
 template <int BN, int MODE>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
     linear_gemm_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const LinearProblem pr) {
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ >= 1000)
@@ -62,7 +164,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], Cfg::EPI_WARPS);
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -121,10 +223,12 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      const uint32_t idesc = idesc_bf16_f32(BN, Cfg::A_MN, Cfg::B_MN);
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
         const TileInfo ti = decode_tile(pr, t, Cfg::BK);
         if (ti.kind != KIND_MMA) continue;
+        // the last column block of a member only multiplies its own columns (N multiple of 16)
+        const int n_mma = min(BN, (ti.n_valid - ti.nt * BN + 15) & ~15);
+        const uint32_t idesc = idesc_bf16_f32(n_mma, Cfg::A_MN, Cfg::B_MN);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -163,101 +267,70 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // Epilogue warp w drains TMEM lane quarter (w % 4) and column slice (w - 2) / 4
+    // (EPI_WARPS / 4 slices of WCOLS columns).
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int half = ew >> 2;
+    constexpr int WCOLS = BN / (Cfg::EPI_WARPS / 4);
+    constexpr int NCH = WCOLS / 32;
+    float* sbias = reinterpret_cast<float*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + 256) + ew * WCOLS;
     const int row_in_tile = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool dropout_on = (MODE == MODE_FWD) && pr.dropout_p != nullptr;
+    // tile metadata is decoded one tile ahead so its global loads overlap the current tile
+    TileInfo nti;
+    float np = 0.0f;
+    if (blockIdx.x < (unsigned)total_tiles) {
+      nti = decode_tile(pr, blockIdx.x, Cfg::BK);
+      if (dropout_on) np = pr.dropout_p[nti.member];
+    }
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const TileInfo ti = decode_tile(pr, t, Cfg::BK);
+      const TileInfo ti = nti;
+      const float p_cur = np;
+      if (t + (int)gridDim.x < total_tiles) {
+        nti = decode_tile(pr, t + gridDim.x, Cfg::BK);
+        if (dropout_on) np = pr.dropout_p[nti.member];
+      }
       const int m = ti.member;
       const int row = ti.mt * Cfg::BM + row_in_tile;
       const bool row_ok = row < pr.out_rows;
-      const int col_tile = ti.nt * BN;
+      const int cbase = ti.nt * BN + half * WCOLS;
       if (ti.kind == KIND_MMA) {
+        if (MODE == MODE_FWD) {
+          // stage this warp's bias slice (zero beyond n_valid) before waiting on the MMA
+          __syncwarp();
+          for (int j = lane; j < WCOLS; j += 32) {
+            const int col = cbase + j;
+            sbias[j] = (pr.bias != nullptr && col < ti.n_valid) ? __ldg(pr.bias + (size_t)m * pr.bias_ld + col) : 0.0f;
+          }
+          __syncwarp();
+        }
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
         tc_fence_after();
         uint32_t thr = 65536u;
         float scale = 1.0f;
         if (dropout_on) {
-          const float p = pr.dropout_p[m];
-          thr = keep_threshold(p);
-          scale = keep_scale(p);
+          thr = keep_threshold(p_cur);
+          scale = keep_scale(p_cur);
         }
-        const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+        const uint32_t t_row =
+            tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN) + (uint32_t)(half * WCOLS);
+        // chunks of 32 columns that hold storable output (warp-uniform)
+        const int nch = min(NCH, max(0, (pr.out_cols - cbase + 31) / 32));
+        uint32_t ra[32], rb[32];
+        if (nch > 0) tmem_ld_32x32b_x32(t_row, ra);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          const int col0 = col_tile + c;
-          if (col0 >= pr.out_cols) break;  // warp-uniform
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + (uint32_t)c, r);
+        for (int c = 0; c < nch; c += 2) {
           tmem_wait_ld();
-          if (!row_ok) continue;
-          const int nv = ti.n_valid - col0;  // valid columns in this chunk (may be <= 0)
-          float v[32];
-          if (MODE == MODE_FWD) {
-            uint32_t keep_bits = 0xFFFFFFFFu;
-            if (dropout_on && thr < 65536u && nv > 0) {
-              keep_bits = 0;
-#pragma unroll
-              for (int g = 0; g < 4; ++g)
-                keep_bits |= dropout_bits8(pr.k0, pr.k1, (uint32_t)(col0 >> 3) + g, (uint32_t)row,
-                                           pr.member_base + (uint32_t)m, pr.offset, thr)
-                             << (8 * g);
-            }
-            float bv[32];
-            const float* bp = pr.bias ? pr.bias + (size_t)m * pr.bias_ld + col0 : nullptr;
-            if (bp != nullptr && nv >= 32 && col0 + 32 <= pr.bias_ld) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                const float4 f = __ldg(reinterpret_cast<const float4*>(bp + j));
-                bv[j] = f.x; bv[j + 1] = f.y; bv[j + 2] = f.z; bv[j + 3] = f.w;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) bv[j] = (bp != nullptr && j < nv) ? __ldg(bp + j) : 0.0f;
-            }
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float x = __uint_as_float(r[j]) + bv[j];
-              if (pr.relu) x = fmaxf(x, 0.0f);
-              x = ((keep_bits >> j) & 1u) ? x * scale : 0.0f;
-              v[j] = j < nv ? x : 0.0f;
-            }
-          } else if (MODE == MODE_DGRAD) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = j < nv ? __uint_as_float(r[j]) : 0.0f;
-          } else {
-            const bool rv = row < ti.m_valid;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = (rv && j < nv) ? __uint_as_float(r[j]) : 0.0f;
-          }
-          const int ncols = pr.out_cols - col0;  // storable columns in this chunk (> 0)
-          if (MODE == MODE_WGRAD) {
-            float* dst = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld + col0;
-            if (ncols >= 32 && (pr.out_ld & 3) == 0) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < ncols) dst[j] = v[j];
-            }
-          } else {
-            __nv_bfloat16* dst =
-                reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld + col0;
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              if (j < ncols) {  // out_cols is a multiple of 8 on this path
-                uint4 u;
-                u.x = pack_bf16x2(v[j], v[j + 1]);
-                u.y = pack_bf16x2(v[j + 2], v[j + 3]);
-                u.z = pack_bf16x2(v[j + 4], v[j + 5]);
-                u.w = pack_bf16x2(v[j + 6], v[j + 7]);
-                *reinterpret_cast<uint4*>(dst + j) = u;
-              }
-            }
+          if (c + 1 < nch) tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * (c + 1)), rb);
+          if (row_ok) epi_chunk<MODE>(pr, ti, m, row, cbase + 32 * c, ra, dropout_on, thr, scale, sbias + 32 * c);
+          if (c + 1 < nch) {
+            tmem_wait_ld();
+            if (c + 2 < nch) tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * (c + 2)), ra);
+            if (row_ok)
+              epi_chunk<MODE>(pr, ti, m, row, cbase + 32 * (c + 1), rb, dropout_on, thr, scale, sbias + 32 * (c + 1));
           }
         }
         tc_fence_before();
@@ -266,26 +339,26 @@ __global__ void __launch_bounds__(192, 1)
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       } else if (row_ok) {
-        // ZERO or COPY block: this thread's row, columns [col_tile, col_tile + BN)
-        const int c_end = min(col_tile + BN, pr.out_cols);
+        // ZERO or COPY block: this thread's row, this warp's column half
+        const int c_end = min(cbase + WCOLS, pr.out_cols);
         if (MODE == MODE_WGRAD) {
           float* dst = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld;
           if ((pr.out_ld & 3) == 0) {
-            int c = col_tile;
+            int c = cbase;
             for (; c + 4 <= c_end; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(0.f, 0.f, 0.f, 0.f);
             for (; c < c_end; ++c) dst[c] = 0.0f;
           } else {
-            for (int c = col_tile; c < c_end; ++c) dst[c] = 0.0f;
+            for (int c = cbase; c < c_end; ++c) dst[c] = 0.0f;
           }
         } else {
           __nv_bfloat16* dst =
               reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld;
           if (ti.kind == KIND_ZERO) {
-            for (int c = col_tile; c < c_end; c += 8) *reinterpret_cast<uint4*>(dst + c) = make_uint4(0, 0, 0, 0);
+            for (int c = cbase; c < c_end; c += 8) *reinterpret_cast<uint4*>(dst + c) = make_uint4(0, 0, 0, 0);
           } else {
             const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(pr.copy_src) +
                                        (size_t)m * pr.out_ms + (size_t)row * pr.out_ld;
-            for (int c = col_tile; c < c_end; c += 8)
+            for (int c = cbase; c < c_end; c += 8)
               *reinterpret_cast<uint4*>(dst + c) = *reinterpret_cast<const uint4*>(src + c);
           }
         }

@@ -54,11 +54,15 @@ __device__ __forceinline__ bool member_active(const LinearProblem& p, int m) {
 
 __device__ __forceinline__ TileInfo decode_tile(const LinearProblem& p, int t, int BK) {
   TileInfo ti;
+  // Slot order (member, n-tile, m-tile): consecutive slots of one member walk down the
+  // rows of one column block, so a persistent CTA that strides through the slots sees
+  // every n-tile (a row-major order would pin a CTA to n-tile (cta % n_tiles) whenever
+  // the grid is a multiple of n_tiles, and padding-only n-tiles would idle those CTAs).
   const int per_member = p.m_tiles * p.n_tiles;
   ti.member = t / per_member;
   const int r = t - ti.member * per_member;
-  ti.mt = r / p.n_tiles;
-  ti.nt = r - ti.mt * p.n_tiles;
+  ti.nt = r / p.m_tiles;
+  ti.mt = r - ti.nt * p.m_tiles;
   const int m = ti.member;
   const int in_m = p.in_f ? p.in_f[m] : p.max_in;
   const int out_m = p.out_f ? p.out_f[m] : p.max_out;

@@ -126,7 +126,20 @@ int launch_sm100(const LinearProblem& pr, const CUtensorMap& a, const CUtensorMa
   TP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
   const long long total = (long long)pr.P * pr.m_tiles * pr.n_tiles;
   if (total > 0x7FFFFFFFLL) return fail(TP_EINVAL, "too many tiles");
-  const int grid = (int)std::min<long long>(total, device_info().sms);
+  int grid = (int)std::min<long long>(total, device_info().sms);
+  // A persistent CTA takes slots c, c + grid, ...  With the (member, n-tile, m-tile) slot
+  // order its n-tile advances by (grid mod slots_per_member) / m_tiles per step; avoid
+  // grids for which that step leaves a CTA on a subset of the column blocks.
+  const int spm = pr.m_tiles * pr.n_tiles;
+  auto gcd = [](int x, int y) { while (y) { const int r = x % y; x = y; y = r; } return x; };
+  for (int g = grid; g > grid / 2 && pr.n_tiles > 1 && total > grid; --g) {
+    const int step = g % spm;
+    const bool pinned = step == 0 || (step % pr.m_tiles == 0 && gcd(step / pr.m_tiles, pr.n_tiles) > 1);
+    if (!pinned) {
+      grid = g;
+      break;
+    }
+  }
   kern<<<grid, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, st>>>(a, b, pr);
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;

@@ -48,38 +48,26 @@ class ParameterPack(nn.Parameter):
     """A trainable tensor with a leading pack dimension (`nn.py:159-163`)."""
 
 
-class BufferPack(torch.Tensor):
-    """Marker for non-trainable pack tensors (`nn.py:188-201`).
-
-    Instances are plain tensors registered as buffers; `isinstance(t, BufferPack)`
-    holds for every tensor created through `BufferPack(data)`.
-    """
-
-    def __new__(cls, data: Tensor):
-        t = data.detach() if isinstance(data, Tensor) else torch.as_tensor(data)
-        t._is_buffer_pack = True  # type: ignore[attr-defined]
-        return t
-
-    @classmethod
-    def __instancecheck__(cls, instance):  # pragma: no cover - see metaclass below
-        return isinstance(instance, Tensor) and getattr(instance, '_is_buffer_pack', False)
-
-
-class _BufferPackMeta(type(torch.Tensor)):
-    def __instancecheck__(cls, instance):
-        return isinstance(instance, Tensor) and getattr(instance, '_is_buffer_pack', False)
-
-
-BufferPack = _BufferPackMeta('BufferPack', (), {  # noqa: F811
-    '__new__': lambda cls, data: _mark_buffer(data),
-    '__doc__': BufferPack.__doc__,
-})
-
-
 def _mark_buffer(data) -> Tensor:
     t = data.detach() if isinstance(data, Tensor) else torch.as_tensor(data)
     t._is_buffer_pack = True  # type: ignore[attr-defined]
     return t
+
+
+class _BufferPackMeta(type):
+    def __instancecheck__(cls, instance):
+        return isinstance(instance, Tensor) and getattr(instance, '_is_buffer_pack', False)
+
+
+class BufferPack(metaclass=_BufferPackMeta):
+    """Marker for non-trainable pack tensors (`nn.py:188-201`).
+
+    `BufferPack(data)` returns `data` as a plain tensor tagged as a buffer pack, and
+    `isinstance(t, BufferPack)` holds exactly for tagged tensors.
+    """
+
+    def __new__(cls, data):
+        return _mark_buffer(data)
 
 
 def _like(x: Tensor, data: Tensor) -> Tensor:
@@ -146,8 +134,23 @@ class PackView(nn.Module):
         return x
 
 
+class _PackBuffers(dict):
+    """Buffer dict of module packs: a buffer pack stays a buffer pack when it is
+    reassigned (e.g. by `Module.to`), like `_ModulePackBuffers` (`nn.py:259-279`)."""
+
+    def __setitem__(self, key, value):
+        cur = self.get(key)
+        if value is not None and cur is not None and getattr(cur, '_is_buffer_pack', False):
+            value._is_buffer_pack = True
+        super().__setitem__(key, value)
+
+
 class ModulePack(nn.Module):
     """Base class of module packs (`nn.py:282-531`)."""
+
+    def __init__(self, *args, **kwargs) -> None:
+        super().__init__(*args, **kwargs)
+        self._buffers = _PackBuffers()
 
     @property
     def pack_size(self) -> int:  # pragma: no cover - abstract

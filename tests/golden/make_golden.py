@@ -150,6 +150,64 @@ def make_tabpack(tp, dtype, name, forward_impl='dense'):
     np.savez_compressed(os.path.join(HERE, name), **arrays)
 
 
+def make_tabpack_large(tp, name):
+    """A larger batch for the bf16 comparison (statistics over 384 rows), computed by
+    the reference in fp64 and stored as fp32."""
+    torch.manual_seed(8)
+    P, B = 4, 384
+    n_num, cards, d_out = 24, [6, 9], 2
+    n_blocks = [3, 2, 3, 1]
+    d_block = [64, 48, 32, 56]
+    dropout = [0.1, 0.2, 0.0, 0.3]
+    model = tp.nn.TabPack(
+        n_numerical_features=n_num, categorical_cardinalities=cards, d_out=d_out,
+        n_blocks=n_blocks, d_block=d_block, dropout=dropout, pack_size=P,
+    )
+    with torch.no_grad():  # parameters exactly representable in fp32
+        for prm in model.parameters():
+            prm.copy_(prm.float())
+    model = model.to(torch.float64)
+    model.train()
+    x_num = torch.randn(P, B, n_num).double()
+    x_cat = torch.stack([torch.randint(0, c + 1, (P, B)) for c in cards], -1)
+    seed = 91
+    torch.set_default_dtype(torch.float64)
+    try:
+        with _PhiloxDropout(tp, seed):
+            y = model(x_num, x_cat)
+    finally:
+        torch.set_default_dtype(torch.float32)
+    dy = torch.randn_like(y).float().double()
+    (y * dy).sum().backward()
+    arrays = {
+        'x_num': _np(x_num).astype(np.float32), 'x_cat': _np(x_cat), 'y': _np(y).astype(np.float32),
+        'dy': _np(dy).astype(np.float32), 'n_blocks': np.array(n_blocks, np.int32),
+        'd_block': np.array(d_block, np.int32), 'dropout': np.array(dropout, np.float32),
+        'cards': np.array(cards, np.int32), 'seed': np.uint64(seed),
+    }
+    for k, v in model.state_dict().items():
+        v = _np(v)
+        arrays['param.' + k] = v.astype(np.float32) if v.dtype == np.float64 else v
+    for k, v in model.named_parameters():
+        arrays['grad.' + k] = _np(v.grad).astype(np.float32)
+
+    # The same step through the reference's own bf16 path (CPU autocast), the accuracy a
+    # bf16 implementation is held to.
+    ref16 = tp.nn.TabPack(
+        n_numerical_features=n_num, categorical_cardinalities=cards, d_out=d_out,
+        n_blocks=n_blocks, d_block=d_block, dropout=dropout, pack_size=P,
+    )
+    ref16.load_state_dict({k: v.float() if v.is_floating_point() else v for k, v in model.state_dict().items()})
+    ref16.train()
+    with _PhiloxDropout(tp, seed), torch.autocast('cpu', dtype=torch.bfloat16):
+        y16 = ref16(x_num.float(), x_cat)
+    (y16.float() * dy.float()).sum().backward()
+    arrays['bf16ref.y'] = _np(y16.float())
+    for k, v in ref16.named_parameters():
+        arrays['bf16ref.grad.' + k] = _np(v.grad).astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, name), **arrays)
+
+
 def make_adamw(tp):
     arrays = {}
     P = 4
@@ -297,6 +355,7 @@ def main():
     make_block(tp, torch.float32, 'block_fp32.npz')
     make_tabpack(tp, torch.float64, 'tabpack_fp64.npz')
     make_tabpack(tp, torch.float64, 'tabpack_indexed_fp64.npz', forward_impl='indexed')
+    make_tabpack_large(tp, 'tabpack_large.npz')
     make_adamw(tp)
     make_newton_schulz(tp)
     make_muon(tp)
