@@ -152,6 +152,35 @@ typedef struct tp_adamw_args {
  * parameter packs of one group (src/tabpackage/optim.py:347-427, 776-846). */
 int tp_adamw_step(const tp_adamw_args* a, void* stream);
 
+/* One Muon parameter group: a packed weight (P, max_out, max_in) fp32 with its
+ * gradient and momentum buffer.  Follows MuonAdamWPack._step_muon
+ * (src/tabpackage/optim.py:682-774) with _zeropower_via_newtonschulz5
+ * (optim.py:464-490): decoupled weight decay, momentum lerp, Nesterov, ns_steps
+ * quintic Newton-Schulz iterations in bf16 (fp32 accumulation) on tensor cores,
+ * p -= lr * scale * update.  Each member iterates on its own out x in block,
+ * oriented so its Gram matrix is min(out, in) square; members whose update is all
+ * zero skip the iterations (decided on the device, no host synchronisation).  The
+ * padding of p / grad / momentum outside out_features x in_features is not touched. */
+typedef struct tp_muon_args {
+  int32_t P, max_out, max_in;
+  float* p;
+  float* grad;
+  float* momentum_buffer;
+  const int32_t* out_features;  /* (P,) or NULL (= max_out) */
+  const int32_t* in_features;   /* (P,) or NULL (= max_in) */
+  tp_hparam lr, momentum, weight_decay;
+  const float* update_scale;    /* (P,) or NULL: sqrt(max(1, max_out / max_in)) */
+  int32_t nesterov;
+  int32_t mutate_grad;          /* 1: grad receives the Nesterov update (as the reference
+                                   does with allow_inplace_grad_mutation=True) */
+  int32_t ns_steps;
+  void* workspace;              /* >= tp_muon_workspace_size(P, max_out, max_in) bytes */
+  size_t workspace_bytes;
+} tp_muon_args;
+
+size_t tp_muon_workspace_size(int32_t P, int32_t max_out, int32_t max_in);
+int tp_muon_step(const tp_muon_args* a, void* stream);
+
 /* Clears and returns the device-side error flag (TP_OK or TP_ETIMEOUT). */
 int tp_device_error(void);
 

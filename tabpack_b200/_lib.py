@@ -63,6 +63,17 @@ class AdamWArgs(ctypes.Structure):
     ]
 
 
+class MuonArgs(ctypes.Structure):
+    _fields_ = [
+        ('P', ctypes.c_int32), ('max_out', ctypes.c_int32), ('max_in', ctypes.c_int32),
+        ('p', ctypes.c_void_p), ('grad', ctypes.c_void_p), ('momentum_buffer', ctypes.c_void_p),
+        ('out_features', ctypes.c_void_p), ('in_features', ctypes.c_void_p),
+        ('lr', HParam), ('momentum', HParam), ('weight_decay', HParam),
+        ('update_scale', ctypes.c_void_p), ('nesterov', ctypes.c_int32), ('mutate_grad', ctypes.c_int32),
+        ('ns_steps', ctypes.c_int32), ('workspace', ctypes.c_void_p), ('workspace_bytes', ctypes.c_size_t),
+    ]
+
+
 # name -> (restype, argtypes); every symbol here is declared in include/tabpack_b200.h
 SIGNATURES = {
     'tp_linear_forward': (ctypes.c_int, [ctypes.POINTER(LinearArgs), ctypes.c_void_p]),
@@ -72,6 +83,8 @@ SIGNATURES = {
                                        ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
                                        ctypes.c_void_p]),
     'tp_adamw_step': (ctypes.c_int, [ctypes.POINTER(AdamWArgs), ctypes.c_void_p]),
+    'tp_muon_workspace_size': (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+    'tp_muon_step': (ctypes.c_int, [ctypes.POINTER(MuonArgs), ctypes.c_void_p]),
     'tp_device_error': (ctypes.c_int, []),
     'tp_last_error_string': (ctypes.c_char_p, []),
     'tp_version': (ctypes.c_char_p, []),

@@ -23,7 +23,7 @@ struct Sm100Cfg {
   static constexpr int BN = BN_;
   static constexpr int BK = 64;  // one 128-byte swizzle atom of bf16 along K
   static constexpr bool A_MN = (MODE == MODE_WGRAD);
-  static constexpr bool B_MN = (MODE != MODE_FWD);
+  static constexpr bool B_MN = (MODE == MODE_DGRAD || MODE == MODE_WGRAD || MODE == MODE_NS_BMN);
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
@@ -98,7 +98,26 @@ __device__ __forceinline__ void epi_chunk(const LinearProblem& pr, const TileInf
     return;
   }
   float v[32];
-  if (MODE == MODE_DGRAD) {
+  if (MODE == MODE_NS || MODE == MODE_NS_BMN) {
+    // alpha * acc + beta * D inside the member's r x (r|c) block, exact zeros around it
+    const bool rv = row < ti.m_valid;
+    const __nv_bfloat16* dp = pr.D ? reinterpret_cast<const __nv_bfloat16*>(pr.D) + (size_t)m * pr.out_ms +
+                                         (size_t)row * pr.out_ld + col0
+                                   : nullptr;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float d[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (dp != nullptr && rv && j < nv) {
+        const uint4 u = *reinterpret_cast<const uint4*>(dp + j);
+        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d[e] = __bfloat162float(h[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        v[j + e] = (rv && j + e < nv) ? pr.alpha * __uint_as_float(r[j + e]) + pr.beta * d[e] : 0.0f;
+    }
+  } else if (MODE == MODE_DGRAD) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = j < nv ? __uint_as_float(r[j]) : 0.0f;
   } else {
@@ -186,7 +205,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
         const TileInfo ti = decode_tile(pr, t, Cfg::BK);
         if (ti.kind != KIND_MMA) continue;
-        const int zA = (MODE == MODE_FWD && pr.x_shared) ? 0 : ti.member;
+        const int zA = (MODE == MODE_FWD && pr.x_shared) ? 0 : ti.member;  // NS operands are per member
         const int zB = (MODE == MODE_WGRAD && pr.x_shared) ? 0 : ti.member;
         for (int kb = 0; kb < ti.kblocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
@@ -338,7 +357,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
         if (lane == 0) mbar_arrive(&tempty[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
-      } else if (row_ok) {
+      } else if (row_ok && ti.kind != KIND_SKIP) {
         // ZERO or COPY block: this thread's row, this warp's column half
         const int c_end = min(cbase + WCOLS, pr.out_cols);
         if (MODE == MODE_WGRAD) {

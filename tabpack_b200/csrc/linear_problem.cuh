@@ -13,8 +13,10 @@
 
 namespace tp {
 
-enum : int { MODE_FWD = 0, MODE_DGRAD = 1, MODE_WGRAD = 2 };
-enum : int { KIND_MMA = 0, KIND_ZERO = 1, KIND_COPY = 2 };
+// MODE_NS / MODE_NS_BMN: one Newton-Schulz GEMM, C = alpha * A B^T + beta * D, with
+// per-member shapes taken from (ns_rows, ns_cols) and B read K-major / MN-major.
+enum : int { MODE_FWD = 0, MODE_DGRAD = 1, MODE_WGRAD = 2, MODE_NS = 3, MODE_NS_BMN = 4 };
+enum : int { KIND_MMA = 0, KIND_ZERO = 1, KIND_COPY = 2, KIND_SKIP = 3 };
 
 struct LinearProblem {
   int mode;
@@ -42,6 +44,15 @@ struct LinearProblem {
   const void* b_ptr;
   int m_tiles, n_tiles;
   int BM, BN;
+  // Newton-Schulz GEMMs: member m multiplies r = ns_rows[m], c = ns_cols[m] matrices;
+  // ns_shape 1: (M, N, K) = (r, r, c), 2: (r, r, r), 3: (r, c, r); members with
+  // active[m] == 0 are skipped.
+  const int32_t* ns_rows;
+  const int32_t* ns_cols;
+  const int32_t* active;
+  int ns_shape;
+  float alpha, beta;
+  const void* D;  // (optional) addend with the output's geometry
 };
 
 struct TileInfo {
@@ -64,6 +75,17 @@ __device__ __forceinline__ TileInfo decode_tile(const LinearProblem& p, int t, i
   ti.nt = r / p.m_tiles;
   ti.mt = r - ti.nt * p.m_tiles;
   const int m = ti.member;
+  if (p.mode >= MODE_NS) {
+    const int r = p.ns_rows[m], c = p.ns_cols[m];
+    ti.m_valid = r;
+    ti.n_valid = (p.ns_shape == 3) ? c : r;
+    const int k_len = (p.ns_shape == 1) ? c : r;
+    ti.kblocks = (k_len + BK - 1) / BK;
+    const bool act = p.active == nullptr || p.active[m] != 0;
+    ti.kind = (!act || ti.mt * p.BM >= ti.m_valid || ti.nt * p.BN >= ti.n_valid || ti.kblocks == 0) ? KIND_SKIP
+                                                                                                     : KIND_MMA;
+    return ti;
+  }
   const int in_m = p.in_f ? p.in_f[m] : p.max_in;
   const int out_m = p.out_f ? p.out_f[m] : p.max_out;
   const bool active = member_active(p, m);

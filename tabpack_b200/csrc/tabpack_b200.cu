@@ -15,6 +15,7 @@
 #include "elementwise.cuh"
 #include "gemm_sm100.cuh"
 #include "gemm_simt.cuh"
+#include "muon.cuh"
 
 namespace tp {
 namespace {
@@ -195,6 +196,66 @@ LinearProblem base_problem(const tp_linear_args* a) {
   p.bias = a->bias;
   p.bias_ld = a->max_out;
   return p;
+}
+
+struct MuonLayout {
+  int R_s, C_s;
+  size_t off_x0, off_x1, off_a, off_b, off_norm, off_rows, off_cols, off_trans, off_active, total;
+};
+
+MuonLayout muon_layout(int P, int max_out, int max_in) {
+  auto up = [](size_t v, size_t a) { return (v + a - 1) / a * a; };
+  MuonLayout L{};
+  L.R_s = (int)up((size_t)std::min(max_out, max_in), 128);
+  L.C_s = (int)up((size_t)std::max(max_out, max_in), 256);
+  size_t o = 0;
+  auto take = [&](size_t bytes) { const size_t at = o; o = up(o + bytes, 256); return at; };
+  L.off_x0 = take((size_t)P * L.R_s * L.C_s * 2);
+  L.off_x1 = take((size_t)P * L.R_s * L.C_s * 2);
+  L.off_a = take((size_t)P * L.R_s * L.R_s * 2);
+  L.off_b = take((size_t)P * L.R_s * L.R_s * 2);
+  L.off_norm = take((size_t)P * 4);
+  L.off_rows = take((size_t)P * 4);
+  L.off_cols = take((size_t)P * 4);
+  L.off_trans = take((size_t)P * 4);
+  L.off_active = take((size_t)P * 4);
+  L.total = o;
+  return L;
+}
+
+// One Newton-Schulz GEMM over the pack: out = alpha * A_op B_op^T + beta * D.
+template <int MODE>
+int ns_gemm(const MuonArgs& ma, int shape, const void* a_op, int a_cols, const void* b_op, int b_cols,
+            void* out, int out_cols, const void* d, float alpha, float beta, cudaStream_t st) {
+  constexpr int BN = 256;
+  LinearProblem pr{};
+  pr.mode = MODE;
+  pr.P = ma.P;
+  pr.ns_rows = ma.rows;
+  pr.ns_cols = ma.cols;
+  pr.active = ma.active;
+  pr.ns_shape = shape;
+  pr.alpha = alpha;
+  pr.beta = beta;
+  pr.D = d;
+  pr.out = out;
+  pr.out_rows = ma.R_s;
+  pr.out_cols = out_cols;
+  pr.out_ld = out_cols;
+  pr.out_ms = (long long)ma.R_s * out_cols;
+  pr.BM = 128;
+  pr.BN = BN;
+  pr.m_tiles = ma.R_s / 128;
+  pr.n_tiles = (out_cols + BN - 1) / BN;
+  CUtensorMap mapA, mapB;
+  int rc;
+  if ((rc = make_map(&mapA, a_op, a_cols, ma.R_s, ma.P, 64, 128))) return rc;
+  if (MODE == MODE_NS) {
+    if ((rc = make_map(&mapB, b_op, b_cols, ma.R_s, ma.P, 64, BN))) return rc;
+  } else {
+    if ((rc = make_map(&mapB, b_op, b_cols, ma.R_s, ma.P, 64, 64))) return rc;
+  }
+  return launch_sm100<BN, MODE>(pr, mapA, mapB, st);
 }
 
 }  // namespace
@@ -381,6 +442,86 @@ int tp_linear_backward_noalloc(const tp_linear_grad_args* ga, void* stream) {
     b.g = scratch;
   }
   return tp_linear_backward(&b, stream);
+}
+
+size_t tp_muon_workspace_size(int32_t P, int32_t max_out, int32_t max_in) {
+  if (P <= 0 || max_out <= 0 || max_in <= 0) return 0;
+  return muon_layout(P, max_out, max_in).total;
+}
+
+int tp_muon_step(const tp_muon_args* a, void* stream) {
+  if (!a || a->P <= 0 || a->max_out <= 0 || a->max_in <= 0) return fail(TP_EINVAL, "bad Muon shapes");
+  if (!a->p || !a->grad || !a->momentum_buffer || !a->workspace) return fail(TP_EINVAL, "null Muon tensor");
+  if (a->ns_steps < 0) return fail(TP_EINVAL, "negative Newton-Schulz step count");
+  const DeviceInfo dinfo = device_info();
+  if (dinfo.major != 10) return fail(TP_EUNSUPPORTED, "Newton-Schulz GEMMs need an sm_100 device");
+  const MuonLayout L = muon_layout(a->P, a->max_out, a->max_in);
+  if (a->workspace_bytes < L.total)
+    return fail(TP_EINVAL, "Muon workspace holds %zu bytes, needs %zu", a->workspace_bytes, L.total);
+  if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return fail(TP_EALIGN, "workspace must be 256-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  MuonArgs m{};
+  m.P = a->P;
+  m.max_out = a->max_out;
+  m.max_in = a->max_in;
+  m.p = a->p;
+  m.g = a->grad;
+  m.m = a->momentum_buffer;
+  m.out_f = a->out_features;
+  m.in_f = a->in_features;
+  m.lr_pm = a->lr.per_member;
+  m.lr_s = (float)a->lr.scalar;
+  m.mu_pm = a->momentum.per_member;
+  m.mu_s = (float)a->momentum.scalar;
+  m.wd_pm = a->weight_decay.per_member;
+  m.wd_s = (float)a->weight_decay.scalar;
+  const bool lr_zero = !a->lr.per_member && a->lr.scalar == 0.0;
+  const bool wd_zero = !a->weight_decay.per_member && a->weight_decay.scalar == 0.0;
+  m.wd_on = !(lr_zero || wd_zero);
+  m.wd_mult_s = (float)(1.0 - a->lr.scalar * a->weight_decay.scalar);
+  m.one_m_mu_s = (float)(1.0 - a->momentum.scalar);
+  m.scale_pm = a->update_scale;
+  m.scale_s = (float)std::sqrt(std::max(1.0, (double)a->max_out / (double)a->max_in));
+  m.nesterov = a->nesterov;
+  m.mutate_grad = a->mutate_grad;
+  m.R_s = L.R_s;
+  m.C_s = L.C_s;
+  m.norm2 = reinterpret_cast<float*>(ws + L.off_norm);
+  m.rows = reinterpret_cast<int32_t*>(ws + L.off_rows);
+  m.cols = reinterpret_cast<int32_t*>(ws + L.off_cols);
+  m.trans = reinterpret_cast<int32_t*>(ws + L.off_trans);
+  m.active = reinterpret_cast<int32_t*>(ws + L.off_active);
+  void* x0 = ws + L.off_x0;
+  void* x1 = ws + L.off_x1;
+  void* A = ws + L.off_a;
+  void* Bm = ws + L.off_b;
+  m.x = reinterpret_cast<__nv_bfloat16*>(x0);
+
+  muon_geometry_kernel<<<(a->P + 255) / 256, 256, 0, st>>>(m);
+  TP_CUDA_TRY(cudaGetLastError());
+  if (a->P > 65535) return fail(TP_EINVAL, "at most 65535 members per Muon call");
+  dim3 tiles((a->max_in + 31) / 32, (a->max_out + 31) / 32, a->P);
+  muon_prologue_kernel<<<tiles, 256, 0, st>>>(m);
+  TP_CUDA_TRY(cudaGetLastError());
+  dim3 ngrid((L.C_s + 255) / 256, L.R_s / 8, a->P);
+  muon_normalize_kernel<<<ngrid, 256, 0, st>>>(m, 128, 256);
+  TP_CUDA_TRY(cudaGetLastError());
+  // quintic Newton-Schulz, coefficients of optim.py:477
+  const float ca = 3.4445f, cb = -4.7750f, cc = 2.0315f;
+  void* X = x0;
+  void* Xn = x1;
+  int rc;
+  for (int it = 0; it < a->ns_steps; ++it) {
+    if ((rc = ns_gemm<MODE_NS>(m, 1, X, L.C_s, X, L.C_s, A, L.R_s, nullptr, 1.0f, 0.0f, st))) return rc;
+    if ((rc = ns_gemm<MODE_NS>(m, 2, A, L.R_s, A, L.R_s, Bm, L.R_s, A, cc, cb, st))) return rc;
+    if ((rc = ns_gemm<MODE_NS_BMN>(m, 3, Bm, L.R_s, X, L.C_s, Xn, L.C_s, X, 1.0f, ca, st))) return rc;
+    std::swap(X, Xn);
+  }
+  m.x = reinterpret_cast<__nv_bfloat16*>(X);
+  muon_apply_kernel<<<tiles, 256, 0, st>>>(m);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
 }
 
 int tp_dropout_mask(uint64_t seed, uint32_t offset, uint32_t member_base, const float* dropout_p, int32_t P, int32_t B,

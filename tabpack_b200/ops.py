@@ -210,6 +210,35 @@ def adamw_step(params, grads, exp_avgs, exp_avg_sqs, *, steps=None, step: int = 
         check(load().tp_adamw_step(ctypes.byref(a), _stream()), 'tp_adamw_step')
 
 
+def muon_workspace_size(P: int, max_out: int, max_in: int) -> int:
+    """Bytes of scratch one `muon_step` call on a (P, max_out, max_in) pack needs."""
+    return int(load().tp_muon_workspace_size(P, max_out, max_in))
+
+
+def muon_step(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=None, in_features=None, lr,
+              momentum, weight_decay, update_scale=None, nesterov: bool = True, mutate_grad: bool = True,
+              ns_steps: int = 5, workspace: Tensor | None = None) -> None:
+    """One Muon group step on a packed (P, max_out, max_in) fp32 weight; see `tp_muon_step`."""
+    for name, t in (('p', p), ('grad', grad), ('momentum_buffer', momentum_buffer)):
+        if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous() or t.ndim != 3:
+            raise TypeError(f'{name} must be a contiguous 3-D fp32 CUDA tensor')
+    P, mo, mi = p.shape
+    need = muon_workspace_size(P, mo, mi)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=p.device)
+    a = _lib.MuonArgs()
+    a.P, a.max_out, a.max_in = P, mo, mi
+    a.p, a.grad, a.momentum_buffer = p.data_ptr(), grad.data_ptr(), momentum_buffer.data_ptr()
+    a.out_features = _ptr(_i32('out_features', out_features))
+    a.in_features = _ptr(_i32('in_features', in_features))
+    a.lr, a.momentum, a.weight_decay = _hparam(lr), _hparam(momentum), _hparam(weight_decay)
+    a.update_scale = _ptr(_cuda('update_scale', update_scale, torch.float32))
+    a.nesterov, a.mutate_grad, a.ns_steps = int(nesterov), int(mutate_grad), int(ns_steps)
+    a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    keep = (out_features, in_features, update_scale)  # noqa: F841  (alive until the launch is queued)
+    check(load().tp_muon_step(ctypes.byref(a), _stream()), 'tp_muon_step')
+
+
 def device_error() -> int:
     """Read and clear the device-side error flag (0 or TP_ETIMEOUT)."""
     return load().tp_device_error()

@@ -1,0 +1,127 @@
+"""Optimizer packs on the GPU (through the C ABI) against the reference and the oracle.
+
+Newton-Schulz runs in bf16 on tcgen05 tensor cores with each member oriented on its
+own min(out, in) side; it must agree with the reference's bf16 iteration within
+2e-2 (relative to the largest entry).  Momentum buffers (fp32) agree to 1e-5.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import optim as oo
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module', autouse=True)
+def _gpu():
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+
+
+def _ns_via_muon(G: np.ndarray, out_f=None, in_f=None, steps=5) -> np.ndarray:
+    """NS(G) through tp_muon_step: momentum 0, no weight decay, lr 1, scale 1, p = 0."""
+    from tabpack_b200 import ops
+
+    g = torch.tensor(G, dtype=torch.float32, device='cuda').contiguous()
+    p = torch.zeros_like(g)
+    m = torch.zeros_like(g)
+    P = g.shape[0]
+    ops.muon_step(p, g, m, out_features=None if out_f is None else torch.tensor(out_f, device='cuda'),
+                  in_features=None if in_f is None else torch.tensor(in_f, device='cuda'),
+                  lr=1.0, momentum=0.0, weight_decay=0.0, update_scale=torch.ones(P, device='cuda'),
+                  nesterov=True, ns_steps=steps)
+    torch.cuda.synchronize()
+    return -p.cpu().numpy()
+
+
+def test_newton_schulz_matches_reference(golden):
+    g = golden('newton_schulz.npz')
+    for j in range(3):
+        got = _ns_via_muon(g[f'G{j}'])
+        want = g[f'X{j}']
+        err = np.abs(got - want).max() / np.abs(want).max()
+        assert err < 2e-2, (j, err)
+
+
+def test_newton_schulz_ragged_multi_tile():
+    """Members spanning several 128-row / 256-column tiles, tall and wide, one all-zero."""
+    rng = np.random.default_rng(3)
+    out_f = np.array([300, 72, 16, 200, 520, 64], np.int32)
+    in_f = np.array([140, 520, 16, 200, 96, 40], np.int32)
+    P, mo, mi = len(out_f), int(out_f.max()), int(in_f.max())
+    G = np.zeros((P, mo, mi), np.float32)
+    for i in range(P):
+        G[i, :out_f[i], :in_f[i]] = rng.standard_normal((out_f[i], in_f[i])) * 0.02
+    G[2] = 0.0  # all-zero update: skipped, stays zero
+    got = _ns_via_muon(G, out_f, in_f)
+    want = oo.newton_schulz5_ragged(G, out_f, in_f)
+    assert np.all(got[2] == 0)
+    for i in range(P):
+        if i == 2:
+            continue
+        a, b = got[i, :out_f[i], :in_f[i]], want[i, :out_f[i], :in_f[i]]
+        err = np.linalg.norm(a - b) / np.linalg.norm(b)
+        assert err < 2e-2, (i, err)
+        # padding of the update stays exactly zero
+        assert np.all(got[i, out_f[i]:, :] == 0) and np.all(got[i, :, in_f[i]:] == 0)
+
+
+def test_muon_adamw_pack_matches_reference(golden):
+    from tabpack_b200 import nn as bnn
+    from tabpack_b200 import optim as bopt
+
+    g = golden('muon.npz')
+    P = 3
+    lin = bnn.LinearPack([24, 16, 32], [32, 16, 8], max_in_features=32, max_out_features=32, pack_size=P).cuda()
+    out = bnn.LinearPack(32, 2, pack_size=P).cuda()
+    with torch.no_grad():
+        lin.weight.copy_(torch.from_numpy(g['w0']))
+    group = bopt.MuonAdamWPack.make_muon_parameter_group(lin)
+    np.testing.assert_allclose(group['muon_update_scale'].cpu().numpy(), g['scale'], rtol=1e-7)
+    opt = bopt.MuonAdamWPack(
+        [group, {'params': [lin.bias, out.weight, out.bias]}],
+        adamw_lr=[1e-3, 2e-3, 5e-3], weight_decay=[1e-2, 0.0, 1e-3], muon_lr=[0.02, 0.01, 0.05],
+        muon_momentum=[0.95, 0.9, 0.8], pack_size=P, allow_inplace_grad_mutation=True)
+    w_prev_ref = g['w0']
+    for s in range(2):
+        w_prev = lin.weight.detach().cpu().numpy()
+        lin.weight.grad = torch.from_numpy(g[f's{s}.g']).cuda()
+        for prm in (lin.bias, out.weight, out.bias):
+            prm.grad = torch.zeros_like(prm)
+        opt.step()
+        torch.cuda.synchronize()
+        mom = opt.state[lin.weight]['muon_momentum_buffer'].cpu().numpy()
+        np.testing.assert_allclose(mom, g[f's{s}.mom'], rtol=1e-5, atol=1e-12)
+        # the applied update (bf16 Newton-Schulz) against the reference's, relative Frobenius
+        w = lin.weight.detach().cpu().numpy()
+        delta, delta_ref = w - w_prev, g[f's{s}.w'] - w_prev_ref
+        err = np.linalg.norm(delta - delta_ref) / np.linalg.norm(delta_ref)
+        assert err < 2e-2, err
+        w_prev_ref = g[f's{s}.w']
+
+
+@pytest.mark.parametrize('case', [0, 1, 2, 3])
+def test_adamw_pack_class_matches_reference(golden, case):
+    from tabpack_b200 import nn as bnn  # noqa: F401
+    from tabpack_b200 import optim as bopt
+    from tabpack_b200.nn import ParameterPack
+
+    g = golden('adamw.npz')
+    pm = bool(g[f'c{case}.per_member'])
+    sr = bool(g[f'c{case}.support_replacement'])
+    hp = {}
+    for k in ('lr', 'beta1', 'beta2', 'eps', 'weight_decay'):
+        v = g[f'c{case}.hp.{k}']
+        hp[k] = [float(x) for x in v] if pm else float(v)
+    w = ParameterPack(torch.from_numpy(g[f'c{case}.w0']).cuda())
+    b = ParameterPack(torch.from_numpy(g[f'c{case}.b0']).cuda())
+    opt = bopt.AdamWPack([w, b], pack_size=4, support_replacement=sr, **hp)
+    for s in range(3):
+        w.grad = torch.from_numpy(g[f'c{case}.s{s}.gw']).cuda()
+        b.grad = torch.from_numpy(g[f'c{case}.s{s}.gb']).cuda()
+        opt.step()
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(w.detach().cpu().numpy(), g[f'c{case}.s{s}.w'], rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(b.detach().cpu().numpy(), g[f'c{case}.s{s}.b'], rtol=1e-5, atol=1e-6)
