@@ -181,6 +181,61 @@ typedef struct tp_muon_args {
 size_t tp_muon_workspace_size(int32_t P, int32_t max_out, int32_t max_in);
 int tp_muon_step(const tp_muon_args* a, void* stream);
 
+#define TP_METRIC_MSE 0
+#define TP_METRIC_MAE 1
+#define TP_METRIC_ACCURACY 2        /* int64 predicted labels (P, N) vs int64 labels */
+#define TP_METRIC_BCE 3             /* probabilities (P, N) vs int64 {0, 1} labels */
+#define TP_METRIC_CE 4              /* probabilities (P, N, C) vs int64 class labels */
+#define TP_METRIC_ACCURACY_ARGMAX 5 /* scores (P, N, C): accuracy of the argmax class */
+#define TP_METRIC_R2 6
+
+/* Per-member metrics with labels shared by every member: mse_pack, mae_pack,
+ * accuracy_pack, binary_cross_entropy_pack, multiclass_cross_entropy_pack and
+ * r2_pack of src/tabpackage/metrics.py:76-253.  Terms in fp32, sums in fp64. */
+typedef struct tp_metric_args {
+  int32_t metric;
+  int32_t P;              /* number of predictions */
+  int64_t N;              /* rows */
+  int32_t C;              /* classes (CE, argmax accuracy), else 1 */
+  const void* y_pred;     /* fp32 (P, N[, C]), or int64 (P, N) for TP_METRIC_ACCURACY */
+  const void* y_true;     /* fp32 (N,) for MSE / MAE / R2, int64 (N,) otherwise */
+  float* out;             /* (P,) */
+} tp_metric_args;
+int tp_metric_pack(const tp_metric_args* a, void* stream);
+
+/* Greedy ensemble selection, greedy_ensemble (src/tabpackage/ensemble.py:95-263),
+ * for the metrics above: candidates (C_pred, N, C) fp32, scores = metric
+ * (maximize = 1) or -metric, top-k initialisation, forward selection with or
+ * without replacement, stop at no improvement or the size limit.  The whole loop
+ * runs on the device; `counts[c]` receives how often prediction c was selected, and
+ * `status` (host memory) {iterations, distinct members, error} once the stream
+ * reaches the end of the call.  error = 1 means a NaN score (the reference raises). */
+typedef struct tp_greedy_args {
+  int32_t metric;
+  int32_t maximize;
+  int32_t n_pred;                /* candidate predictions */
+  int64_t N;                     /* rows */
+  int32_t C;                     /* classes per row */
+  const float* predictions;      /* (n_pred, N, C) */
+  const void* y_true;
+  int32_t init_top_k;
+  int32_t max_ensemble_size;     /* <= 0: no limit (only without replacement) */
+  int32_t with_replacement;
+  int32_t* counts;               /* (n_pred,) device */
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t* status;               /* (3,) device: iterations, distinct members, error */
+} tp_greedy_args;
+size_t tp_greedy_workspace_size(int32_t n_pred, int64_t N, int32_t C);
+int tp_greedy_ensemble(const tp_greedy_args* a, void* stream);
+
+/* (Weighted) mean of selected member predictions: compute_unsanitized_ensemble_predictions
+ * (src/tabpackage/ensemble.py:25-61) and TabPackPredictor.EnsembleHead.forward
+ * (src/tabpackage/_training.py:1955-1958).  pred (P, n), idx (K,) device, weights (K,)
+ * device or NULL, out (n,). */
+int tp_ensemble_mean(const float* pred, const int32_t* idx, const float* weights, int32_t K, int64_t n,
+                     float* out, void* stream);
+
 /* Clears and returns the device-side error flag (TP_OK or TP_ETIMEOUT). */
 int tp_device_error(void);
 

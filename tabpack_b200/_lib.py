@@ -74,6 +74,26 @@ class MuonArgs(ctypes.Structure):
     ]
 
 
+class MetricArgs(ctypes.Structure):
+    _fields_ = [
+        ('metric', ctypes.c_int32), ('P', ctypes.c_int32), ('N', ctypes.c_int64), ('C', ctypes.c_int32),
+        ('y_pred', ctypes.c_void_p), ('y_true', ctypes.c_void_p), ('out', ctypes.c_void_p),
+    ]
+
+
+class GreedyArgs(ctypes.Structure):
+    _fields_ = [
+        ('metric', ctypes.c_int32), ('maximize', ctypes.c_int32), ('n_pred', ctypes.c_int32),
+        ('N', ctypes.c_int64), ('C', ctypes.c_int32), ('predictions', ctypes.c_void_p), ('y_true', ctypes.c_void_p),
+        ('init_top_k', ctypes.c_int32), ('max_ensemble_size', ctypes.c_int32), ('with_replacement', ctypes.c_int32),
+        ('counts', ctypes.c_void_p), ('workspace', ctypes.c_void_p), ('workspace_bytes', ctypes.c_size_t),
+        ('status', ctypes.c_void_p),
+    ]
+
+
+TP_METRIC = {'mse': 0, 'mae': 1, 'accuracy': 2, 'bce': 3, 'ce': 4, 'accuracy_argmax': 5, 'r2': 6}
+
+
 # name -> (restype, argtypes); every symbol here is declared in include/tabpack_b200.h
 SIGNATURES = {
     'tp_linear_forward': (ctypes.c_int, [ctypes.POINTER(LinearArgs), ctypes.c_void_p]),
@@ -85,6 +105,11 @@ SIGNATURES = {
     'tp_adamw_step': (ctypes.c_int, [ctypes.POINTER(AdamWArgs), ctypes.c_void_p]),
     'tp_muon_workspace_size': (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     'tp_muon_step': (ctypes.c_int, [ctypes.POINTER(MuonArgs), ctypes.c_void_p]),
+    'tp_metric_pack': (ctypes.c_int, [ctypes.POINTER(MetricArgs), ctypes.c_void_p]),
+    'tp_greedy_workspace_size': (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32]),
+    'tp_greedy_ensemble': (ctypes.c_int, [ctypes.POINTER(GreedyArgs), ctypes.c_void_p]),
+    'tp_ensemble_mean': (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                        ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
     'tp_device_error': (ctypes.c_int, []),
     'tp_last_error_string': (ctypes.c_char_p, []),
     'tp_version': (ctypes.c_char_p, []),

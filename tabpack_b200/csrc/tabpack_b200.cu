@@ -16,6 +16,7 @@
 #include "gemm_sm100.cuh"
 #include "gemm_simt.cuh"
 #include "muon.cuh"
+#include "metrics.cuh"
 
 namespace tp {
 namespace {
@@ -520,6 +521,120 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
   }
   m.x = reinterpret_cast<__nv_bfloat16*>(X);
   muon_apply_kernel<<<tiles, 256, 0, st>>>(m);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+int tp_metric_pack(const tp_metric_args* a, void* stream) {
+  if (!a || a->P <= 0 || a->N <= 0 || !a->y_pred || !a->y_true || !a->out) return fail(TP_EINVAL, "bad metric arguments");
+  if (a->metric < TP_METRIC_MSE || a->metric > TP_METRIC_R2) return fail(TP_EINVAL, "unknown metric %d", a->metric);
+  MetricSrc s{};
+  s.metric = a->metric;
+  s.N = a->N;
+  s.C = (a->metric == TP_METRIC_CE || a->metric == TP_METRIC_ACCURACY_ARGMAX) ? std::max(1, a->C) : 1;
+  const bool float_labels = a->metric == TP_METRIC_MSE || a->metric == TP_METRIC_MAE || a->metric == TP_METRIC_R2;
+  s.yf = float_labels ? static_cast<const float*>(a->y_true) : nullptr;
+  s.yi = float_labels ? nullptr : static_cast<const int64_t*>(a->y_true);
+  const bool int_pred = a->metric == TP_METRIC_ACCURACY;
+  metric_pack_kernel<<<a->P, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      s, int_pred ? nullptr : static_cast<const float*>(a->y_pred),
+      int_pred ? static_cast<const int64_t*>(a->y_pred) : nullptr, a->out);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+static size_t greedy_layout(int32_t n_pred, int64_t N, int32_t C, size_t* off_ens, size_t* off_sc, size_t* off_ind,
+                            size_t* off_st, size_t* off_init, size_t* off_metric) {
+  auto up = [](size_t v) { return (v + 255) / 256 * 256; };
+  size_t o = 0;
+  *off_ens = o;
+  o = up(o + (size_t)N * C * 4);
+  *off_sc = o;
+  o = up(o + (size_t)n_pred * 8);
+  *off_ind = o;
+  o = up(o + (size_t)n_pred * 8);
+  *off_st = o;
+  o = up(o + sizeof(GreedyState));
+  *off_init = o;
+  o = up(o + (size_t)n_pred * 4);
+  *off_metric = o;
+  o = up(o + (size_t)n_pred * 4);
+  return o;
+}
+
+size_t tp_greedy_workspace_size(int32_t n_pred, int64_t N, int32_t C) {
+  if (n_pred <= 0 || N <= 0 || C <= 0) return 0;
+  size_t a, b, c, d, e, f;
+  return greedy_layout(n_pred, N, C, &a, &b, &c, &d, &e, &f);
+}
+
+int tp_greedy_ensemble(const tp_greedy_args* a, void* stream) {
+  if (!a || a->n_pred <= 0 || a->N <= 0 || !a->predictions || !a->y_true || !a->counts || !a->workspace || !a->status)
+    return fail(TP_EINVAL, "bad greedy arguments");
+  if (a->metric == TP_METRIC_ACCURACY || a->metric == TP_METRIC_R2 || a->metric < 0 || a->metric > TP_METRIC_R2)
+    return fail(TP_EINVAL, "metric %d is not supported by the fused greedy selection", a->metric);
+  if (a->init_top_k <= 0) return fail(TP_EINVAL, "`init_top_k` must be positive to initialize the ensemble with at least one member");
+  if (a->with_replacement && a->max_ensemble_size <= 0)
+    return fail(TP_EINVAL, "Set `max_ensemble_size` to limit the number of ensemble members when `with_replacement=True`");
+  if (a->max_ensemble_size > 0 && a->init_top_k > a->max_ensemble_size)
+    return fail(TP_EINVAL, "`init_top_k` must not exceed `max_ensemble_size`");
+  const int C = std::max(1, a->C);
+  size_t o_ens, o_sc, o_ind, o_st, o_init, o_met;
+  const size_t need = greedy_layout(a->n_pred, a->N, C, &o_ens, &o_sc, &o_ind, &o_st, &o_init, &o_met);
+  if (a->workspace_bytes < need) return fail(TP_EINVAL, "greedy workspace holds %zu bytes, needs %zu", a->workspace_bytes, need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  GreedyArgs g{};
+  g.s.metric = a->metric;
+  g.s.N = a->N;
+  g.s.C = (a->metric == TP_METRIC_CE || a->metric == TP_METRIC_ACCURACY_ARGMAX) ? C : 1;
+  const bool float_labels = a->metric == TP_METRIC_MSE || a->metric == TP_METRIC_MAE;
+  g.s.yf = float_labels ? static_cast<const float*>(a->y_true) : nullptr;
+  g.s.yi = float_labels ? nullptr : static_cast<const int64_t*>(a->y_true);
+  g.Cand = a->n_pred;
+  g.pred = a->predictions;
+  g.sign = a->maximize ? 1 : -1;
+  g.with_replacement = a->with_replacement;
+  g.limit = a->max_ensemble_size <= 0 ? a->n_pred
+            : a->with_replacement   ? a->max_ensemble_size
+                                    : std::min(a->n_pred, a->max_ensemble_size);
+  g.counts = a->counts;
+  g.ens = reinterpret_cast<float*>(ws + o_ens);
+  g.scores = reinterpret_cast<double*>(ws + o_sc);
+  g.ind_scores = reinterpret_cast<double*>(ws + o_ind);
+  g.st = reinterpret_cast<GreedyState*>(ws + o_st);
+  int* init_idx = reinterpret_cast<int*>(ws + o_init);
+  float* metric = reinterpret_cast<float*>(ws + o_met);
+  const int k = std::min(a->init_top_k, a->n_pred);
+  TP_CUDA_TRY(cudaMemsetAsync(a->counts, 0, (size_t)a->n_pred * 4, st));
+  // individual scores
+  metric_pack_kernel<<<a->n_pred, 256, 0, st>>>(g.s, a->predictions, nullptr, metric);
+  greedy_sign_kernel<<<(a->n_pred + 255) / 256, 256, 0, st>>>(metric, g.ind_scores, a->n_pred, g.sign);
+  greedy_init_select_kernel<<<1, 32, 0, st>>>(g, k, init_idx);
+  const int64_t n = a->N * (int64_t)g.s.C;
+  const int eb = (int)std::min<int64_t>((n + 255) / 256, 1184);
+  greedy_init_mean_kernel<<<eb, 256, 0, st>>>(g, k, init_idx);
+  greedy_init_score_kernel<<<1, 256, 0, st>>>(g);
+  TP_CUDA_TRY(cudaGetLastError());
+  for (int it = k; it < g.limit; ++it) {
+    greedy_score_kernel<<<a->n_pred, 256, 0, st>>>(g);
+    greedy_select_kernel<<<1, 1024, 0, st>>>(g);
+    greedy_update_kernel<<<eb, 256, 0, st>>>(g);
+    greedy_advance_kernel<<<1, 1, 0, st>>>(g);
+  }
+  TP_CUDA_TRY(cudaGetLastError());
+  // status: iterations, distinct members, error
+  TP_CUDA_TRY(cudaMemcpyAsync(a->status, &g.st->iters, 4, cudaMemcpyDeviceToDevice, st));
+  TP_CUDA_TRY(cudaMemcpyAsync(a->status + 1, &g.st->size, 4, cudaMemcpyDeviceToDevice, st));
+  TP_CUDA_TRY(cudaMemcpyAsync(a->status + 2, &g.st->error, 4, cudaMemcpyDeviceToDevice, st));
+  return TP_OK;
+}
+
+int tp_ensemble_mean(const float* pred, const int32_t* idx, const float* weights, int32_t K, int64_t n, float* out,
+                     void* stream) {
+  if (!pred || !idx || !out || K <= 0 || n <= 0) return fail(TP_EINVAL, "bad ensemble-mean arguments");
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4096);
+  ensemble_mean_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(pred, idx, weights, K, n, out);
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;
 }

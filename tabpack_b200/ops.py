@@ -239,6 +239,61 @@ def muon_step(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=
     check(load().tp_muon_step(ctypes.byref(a), _stream()), 'tp_muon_step')
 
 
+def metric_pack(metric: str, y_pred: Tensor, y_true: Tensor, classes: int = 1) -> Tensor:
+    """(P,) metric values; y_pred (P, N[, classes]); see `tp_metric_pack`."""
+    code = _lib.TP_METRIC[metric]
+    y_pred = _cuda('y_pred', y_pred)
+    y_true = _cuda('y_true', y_true)
+    if code == _lib.TP_METRIC['accuracy']:
+        y_pred, y_true = y_pred.to(torch.int64), y_true.to(torch.int64)
+    elif code in (_lib.TP_METRIC['mse'], _lib.TP_METRIC['mae'], _lib.TP_METRIC['r2']):
+        y_pred, y_true = y_pred.to(torch.float32), y_true.to(torch.float32)
+    else:
+        y_pred, y_true = y_pred.to(torch.float32), y_true.to(torch.int64)
+    y_pred, y_true = y_pred.contiguous(), y_true.contiguous()
+    P = y_pred.shape[0]
+    N = y_true.numel()
+    out = torch.empty(P, dtype=torch.float32, device=y_pred.device)
+    a = _lib.MetricArgs(metric=code, P=P, N=N, C=classes, y_pred=y_pred.data_ptr(), y_true=y_true.data_ptr(),
+                        out=out.data_ptr())
+    check(load().tp_metric_pack(ctypes.byref(a), _stream()), 'tp_metric_pack')
+    return out
+
+
+def greedy_ensemble(predictions: Tensor, y_true: Tensor, *, metric: str, maximize: bool, classes: int = 1,
+                    init_top_k: int = 1, max_ensemble_size: int | None = None,
+                    with_replacement: bool = False) -> tuple[Tensor, Tensor]:
+    """Fused greedy selection; returns (counts (n_pred,) int32, status (3,) int32) on the device."""
+    code = _lib.TP_METRIC[metric]
+    pred = _cuda('predictions', predictions).to(torch.float32).contiguous()
+    yt = _cuda('y_true', y_true)
+    yt = (yt.to(torch.float32) if metric in ('mse', 'mae') else yt.to(torch.int64)).contiguous()
+    n_pred = pred.shape[0]
+    N = yt.numel()
+    ws = torch.empty(int(load().tp_greedy_workspace_size(n_pred, N, classes)), dtype=torch.uint8, device=pred.device)
+    counts = torch.empty(n_pred, dtype=torch.int32, device=pred.device)
+    status = torch.zeros(3, dtype=torch.int32, device=pred.device)
+    a = _lib.GreedyArgs(metric=code, maximize=int(maximize), n_pred=n_pred, N=N, C=classes,
+                        predictions=pred.data_ptr(), y_true=yt.data_ptr(), init_top_k=init_top_k,
+                        max_ensemble_size=0 if max_ensemble_size is None else int(max_ensemble_size),
+                        with_replacement=int(with_replacement), counts=counts.data_ptr(), workspace=ws.data_ptr(),
+                        workspace_bytes=ws.numel(), status=status.data_ptr())
+    check(load().tp_greedy_ensemble(ctypes.byref(a), _stream()), 'tp_greedy_ensemble')
+    return counts, status
+
+
+def ensemble_mean(pred: Tensor, idx: Tensor, weights: Tensor | None = None) -> Tensor:
+    """(Weighted) mean of pred[idx] over the first dimension; see `tp_ensemble_mean`."""
+    pred = _cuda('pred', pred, torch.float32)
+    idx = _i32('idx', idx)
+    weights = None if weights is None else _cuda('weights', weights).to(torch.float32).contiguous()
+    out = torch.empty(pred.shape[1:], dtype=torch.float32, device=pred.device)
+    n = out.numel()
+    check(load().tp_ensemble_mean(pred.data_ptr(), idx.data_ptr(), _ptr(weights), idx.numel(), n, out.data_ptr(),
+                                  _stream()), 'tp_ensemble_mean')
+    return out
+
+
 def device_error() -> int:
     """Read and clear the device-side error flag (0 or TP_ETIMEOUT)."""
     return load().tp_device_error()
