@@ -236,6 +236,19 @@ int tp_greedy_ensemble(const tp_greedy_args* a, void* stream);
 int tp_ensemble_mean(const float* pred, const int32_t* idx, const float* weights, int32_t K, int64_t n,
                      float* out, void* stream);
 
+/* Row-wise softmax over the last dimension: the classification prediction transform
+ * (torch.softmax(x, -1)) applied to packed outputs before metrics and ensembling
+ * (_training.py:170-181).  x, out: (rows, C) fp32. */
+int tp_softmax_rows(const float* x, int64_t rows, int32_t C, float* out, void* stream);
+
+/* Per-member batch-order keys for make_shuffled_batch_indices_pack
+ * (src/tabpackage/_training.py:323-338), whose `rand(P, N).argsort` draws from a global
+ * RNG: here keys[m][i] is 31 bits of a Philox word of (seed, epoch, member_base + m, i), so sorting a
+ * member's keys (stable) yields the same permutation on any number of GPUs.  keys: (P, N)
+ * int32 in [0, 2^31). */
+int tp_permutation_keys(uint64_t seed, uint32_t epoch, uint32_t member_base, int32_t P, int64_t N, int32_t* keys,
+                        void* stream);
+
 /* Clears and returns the device-side error flag (TP_OK or TP_ETIMEOUT). */
 int tp_device_error(void);
 

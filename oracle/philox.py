@@ -98,3 +98,14 @@ def dropout_keep_mask(
     r16 = halves.reshape(n_members, n_rows, n_groups * 8)[:, :, :n_cols]
     thr = keep_threshold(p)[:, None, None]
     return r16 < thr
+
+
+def permutation_keys(*, seed: int, epoch: int, members: np.ndarray, n_rows: int) -> np.ndarray:
+    """(len(members), n_rows) int32 batch-order keys: 31 bits of Philox4x32-10 word 0 with
+    key = seed and counter = (row, member, epoch, 0x9E3779B9).  A member's stable argsort
+    of its keys is its batch order in every epoch, whatever the sharding."""
+    members = np.asarray(members, dtype=np.uint32)
+    r = np.arange(n_rows, dtype=np.uint32)[None, :]
+    w = philox4x32_10(r, members[:, None], np.uint32(epoch), np.uint32(0x9E3779B9),
+                      seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF)[0]
+    return (w >> np.uint32(1)).astype(np.int32)

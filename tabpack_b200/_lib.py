@@ -110,6 +110,10 @@ SIGNATURES = {
     'tp_greedy_ensemble': (ctypes.c_int, [ctypes.POINTER(GreedyArgs), ctypes.c_void_p]),
     'tp_ensemble_mean': (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                         ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
+    'tp_softmax_rows': (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
+                                       ctypes.c_void_p]),
+    'tp_permutation_keys': (ctypes.c_int, [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int32,
+                                           ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
     'tp_device_error': (ctypes.c_int, []),
     'tp_last_error_string': (ctypes.c_char_p, []),
     'tp_version': (ctypes.c_char_p, []),

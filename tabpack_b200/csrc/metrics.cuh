@@ -326,4 +326,35 @@ __global__ void ensemble_mean_kernel(const float* pred, const int32_t* idx, cons
   }
 }
 
+// Row-wise softmax over the last dimension (C classes), fp32: the prediction transform
+// `functools.partial(torch.softmax, dim=-1)` of classification runs.  One warp per row.
+__global__ void softmax_rows_kernel(const float* x, int64_t rows, int C, float* out) {
+  const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* r = x + row * C;
+  float mx = -INFINITY;
+  for (int c = lane; c < C; c += 32) mx = fmaxf(mx, r[c]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+  float s = 0.0f;
+  for (int c = lane; c < C; c += 32) s += expf(r[c] - mx);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, off);
+  for (int c = lane; c < C; c += 32) out[row * C + c] = expf(r[c] - mx) / s;
+}
+
+// keys[m][i] = (word 0 >> 1) of Philox4x32-10 with key = seed and counter
+// (i, member_base + m, epoch, 0x9E3779B9): sorting each member's row keys gives a
+// batch order that depends only on (seed, epoch, global member id).
+__global__ void permutation_keys_kernel(uint32_t k0, uint32_t k1, uint32_t epoch, uint32_t member_base, int P,
+                                        int64_t N, int32_t* keys) {
+  const int64_t total = (int64_t)P * N;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(t / N);
+    const uint32_t i = (uint32_t)(t - (int64_t)m * N);
+    keys[t] = (int32_t)(philox4x32_10(make_uint4(i, member_base + (uint32_t)m, epoch, 0x9E3779B9u), k0, k1).x >> 1);
+  }
+}
+
 }  // namespace tp

@@ -36,6 +36,8 @@ struct MuonArgs {
   __nv_bfloat16* x;      // (P, R_s, C_s) oriented operand
   int R_s, C_s;
   float* norm2;          // (P,)
+  float* partial;        // (P, tiles) per-32x32-tile sums of squares (fixed-order reduction)
+  int tiles;             // ceil(max_out / 32) * ceil(max_in / 32)
   int32_t* rows;         // (P,) r_m
   int32_t* cols;         // (P,) c_m
   int32_t* trans;        // (P,) 1: X = U^T
@@ -50,7 +52,6 @@ __global__ void muon_geometry_kernel(MuonArgs a) {
   a.rows[m] = min(o, n);
   a.cols[m] = max(o, n);
   a.trans[m] = o > n ? 1 : 0;
-  a.norm2[m] = 0.0f;
 }
 
 // 32x32 source tiles (o, n) of member blockIdx.z; 256 threads = 32 columns x 8 row lanes.
@@ -95,7 +96,7 @@ __global__ void __launch_bounds__(256) muon_prologue_kernel(MuonArgs a) {
   if (threadIdx.x == 0) {
     float t = 0.0f;
     for (int i = 0; i < 8; ++i) t += red[i];
-    if (t != 0.0f) atomicAdd(a.norm2 + mem, t);
+    a.partial[(size_t)mem * a.tiles + blockIdx.y * gridDim.x + blockIdx.x] = t;
   }
   // oriented bf16 operand
   const bool tr = out_m > in_m;
@@ -111,6 +112,31 @@ __global__ void __launch_bounds__(256) muon_prologue_kernel(MuonArgs a) {
   }
 }
 
+// norm2[m] = sum of the member's tile partials in a fixed order (deterministic),
+// active[m] = norm2[m] > 0.  One block per member.
+__global__ void __launch_bounds__(256) muon_norm_kernel(MuonArgs a, int tiles_x) {
+  __shared__ float red[256];
+  const int mem = blockIdx.x;
+  const int out_m = a.out_f ? a.out_f[mem] : a.max_out;
+  const int in_m = a.in_f ? a.in_f[mem] : a.max_in;
+  const int ty_n = (out_m + 31) / 32, tx_n = (in_m + 31) / 32;  // tiles the prologue wrote
+  float s = 0.0f;
+  for (int t = threadIdx.x; t < ty_n * tx_n; t += blockDim.x) {
+    const int ty = t / tx_n, tx = t - ty * tx_n;
+    s += a.partial[(size_t)mem * a.tiles + ty * tiles_x + tx];
+  }
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    a.norm2[mem] = red[0];
+    a.active[mem] = red[0] > 0.0f ? 1 : 0;
+  }
+}
+
 // X <- bf16(X / bf16(bf16(||X||_F) + 1e-7)) on the member's r x c block and exact zeros
 // on [0, R_s-tile) x [0, C_s-tile) around it (the Newton-Schulz GEMMs read those pads
 // along K).  Grid: (ceil(C_s / 256), R_s / 8, P), 256 threads, 8 rows x 32 x 8 columns.
@@ -120,7 +146,6 @@ __global__ void __launch_bounds__(256) muon_normalize_kernel(MuonArgs a, int row
   const int rr = min(a.R_s, (r + row_pad - 1) / row_pad * row_pad);
   const int cc = min(a.C_s, (c + col_pad - 1) / col_pad * col_pad);
   const float nrm2 = a.norm2[mem];
-  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) a.active[mem] = nrm2 > 0.0f ? 1 : 0;
   if (nrm2 == 0.0f) return;  // all-zero update: Newton-Schulz is skipped for this member
   const float nrm = __bfloat162float(__float2bfloat16_rn(sqrtf(nrm2)));
   const float den = __bfloat162float(__float2bfloat16_rn(nrm + 1e-7f));

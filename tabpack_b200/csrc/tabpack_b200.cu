@@ -200,8 +200,8 @@ LinearProblem base_problem(const tp_linear_args* a) {
 }
 
 struct MuonLayout {
-  int R_s, C_s;
-  size_t off_x0, off_x1, off_a, off_b, off_norm, off_rows, off_cols, off_trans, off_active, total;
+  int R_s, C_s, tiles;
+  size_t off_x0, off_x1, off_a, off_b, off_norm, off_rows, off_cols, off_trans, off_active, off_partial, total;
 };
 
 MuonLayout muon_layout(int P, int max_out, int max_in) {
@@ -220,6 +220,8 @@ MuonLayout muon_layout(int P, int max_out, int max_in) {
   L.off_cols = take((size_t)P * 4);
   L.off_trans = take((size_t)P * 4);
   L.off_active = take((size_t)P * 4);
+  L.tiles = ((max_out + 31) / 32) * ((max_in + 31) / 32);
+  L.off_partial = take((size_t)P * L.tiles * 4);
   L.total = o;
   return L;
 }
@@ -493,6 +495,8 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
   m.cols = reinterpret_cast<int32_t*>(ws + L.off_cols);
   m.trans = reinterpret_cast<int32_t*>(ws + L.off_trans);
   m.active = reinterpret_cast<int32_t*>(ws + L.off_active);
+  m.partial = reinterpret_cast<float*>(ws + L.off_partial);
+  m.tiles = L.tiles;
   void* x0 = ws + L.off_x0;
   void* x1 = ws + L.off_x1;
   void* A = ws + L.off_a;
@@ -504,6 +508,7 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
   if (a->P > 65535) return fail(TP_EINVAL, "at most 65535 members per Muon call");
   dim3 tiles((a->max_in + 31) / 32, (a->max_out + 31) / 32, a->P);
   muon_prologue_kernel<<<tiles, 256, 0, st>>>(m);
+  muon_norm_kernel<<<a->P, 256, 0, st>>>(m, (int)tiles.x);
   TP_CUDA_TRY(cudaGetLastError());
   dim3 ngrid((L.C_s + 255) / 256, L.R_s / 8, a->P);
   muon_normalize_kernel<<<ngrid, 256, 0, st>>>(m, 128, 256);
@@ -635,6 +640,26 @@ int tp_ensemble_mean(const float* pred, const int32_t* idx, const float* weights
   if (!pred || !idx || !out || K <= 0 || n <= 0) return fail(TP_EINVAL, "bad ensemble-mean arguments");
   const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4096);
   ensemble_mean_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(pred, idx, weights, K, n, out);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+int tp_softmax_rows(const float* x, int64_t rows, int32_t C, float* out, void* stream) {
+  if (!x || !out || rows <= 0 || C <= 0) return fail(TP_EINVAL, "bad softmax arguments");
+  const int64_t threads = rows * 32;
+  const int blocks = (int)std::min<int64_t>((threads + 255) / 256, 1 << 20);
+  if ((int64_t)blocks * 256 < threads) return fail(TP_EINVAL, "too many rows for one softmax call");
+  softmax_rows_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, rows, C, out);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+int tp_permutation_keys(uint64_t seed, uint32_t epoch, uint32_t member_base, int32_t P, int64_t N, int32_t* keys,
+                        void* stream) {
+  if (!keys || P <= 0 || N <= 0) return fail(TP_EINVAL, "bad permutation-key arguments");
+  const int blocks = (int)std::min<int64_t>(((int64_t)P * N + 255) / 256, 8192);
+  permutation_keys_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      (uint32_t)(seed & 0xFFFFFFFFu), (uint32_t)(seed >> 32), epoch, member_base, P, N, keys);
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;
 }

@@ -294,6 +294,24 @@ def ensemble_mean(pred: Tensor, idx: Tensor, weights: Tensor | None = None) -> T
     return out
 
 
+def softmax_rows(x: Tensor) -> Tensor:
+    """Softmax over the last dimension (fp32); see `tp_softmax_rows`."""
+    x = _cuda('x', x).to(torch.float32).contiguous()
+    out = torch.empty_like(x)
+    C = x.shape[-1]
+    check(load().tp_softmax_rows(x.data_ptr(), x.numel() // C, C, out.data_ptr(), _stream()), 'tp_softmax_rows')
+    return out
+
+
+def permutation_keys(*, seed: int, epoch: int, member_base: int, P: int, N: int, device) -> Tensor:
+    """(P, N) int32 Philox keys whose per-row stable argsort is each member's batch order."""
+    keys = torch.empty((P, N), dtype=torch.int32, device=device)
+    check(load().tp_permutation_keys(int(seed) & 0xFFFFFFFFFFFFFFFF, int(epoch) & 0xFFFFFFFF,
+                                     int(member_base) & 0xFFFFFFFF, P, N, keys.data_ptr(), _stream()),
+          'tp_permutation_keys')
+    return keys
+
+
 def device_error() -> int:
     """Read and clear the device-side error flag (0 or TP_ETIMEOUT)."""
     return load().tp_device_error()

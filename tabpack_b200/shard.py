@@ -1,0 +1,77 @@
+"""Member sharding over the GPUs of one box (one process per GPU, torch.distributed).
+
+Members of a pack are independent (the training loss is a sum of per-member losses,
+`src/tabpackage/_training.py:2679-2682`), so a pack shards by member with no gradient
+exchange: rank r owns the contiguous global member range `ranges[r]`, dropout masks
+and batch orders are keyed by global member id (shard-invariant), and the only
+exchanges are the once-per-epoch all-gather of per-member validation predictions
+(before greedy selection) and, at inference, a sum all-reduce of ensemble
+probabilities.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+
+def member_ranges(n_members: int, world: int, cost: list[float] | None = None) -> list[tuple[int, int]]:
+    """Contiguous member ranges, one per rank, in global member order.
+
+    With `cost` (one number per member, e.g. its FLOPs per step) the cut points follow
+    the cost prefix sums so that every rank gets about the same work; otherwise the
+    counts differ by at most one.
+    """
+    if world <= 0 or n_members < 0:
+        raise ValueError('world must be positive and n_members non-negative')
+    if cost is None:
+        base, extra = divmod(n_members, world)
+        out, start = [], 0
+        for r in range(world):
+            n = base + (1 if r < extra else 0)
+            out.append((start, start + n))
+            start += n
+        return out
+    if len(cost) != n_members:
+        raise ValueError('one cost per member is required')
+    total = float(sum(cost))
+    cuts, acc, r = [0], 0.0, 1
+    for i, c in enumerate(cost):
+        acc += float(c)
+        while r < world and acc >= total * r / world and len(cuts) <= r:
+            cuts.append(i + 1)
+            r += 1
+    while len(cuts) < world:
+        cuts.append(n_members)
+    cuts.append(n_members)
+    return [(cuts[k], cuts[k + 1]) for k in range(world)]
+
+
+def gather_members(local: Tensor, counts: list[int], group=None) -> Tensor:
+    """All-gather tensors with a leading member dimension from every rank and return
+    them concatenated in global member order (ranks may own different counts)."""
+    world = dist.get_world_size(group)
+    if len(counts) != world:
+        raise ValueError('one member count per rank is required')
+    rank = dist.get_rank(group)
+    if local.shape[0] != counts[rank]:
+        raise ValueError('the local tensor does not match this rank\'s member count')
+    maxc = max(counts)
+    padded = local.new_zeros((maxc, *local.shape[1:]))
+    padded[: local.shape[0]] = local
+    if dist.get_backend(group) == 'nccl':
+        out = local.new_empty((world * maxc, *local.shape[1:]))
+        dist.all_gather_into_tensor(out, padded.contiguous(), group=group)
+        parts = [out[r * maxc: r * maxc + counts[r]] for r in range(world)]
+    else:
+        bufs = [torch.empty_like(padded) for _ in range(world)]
+        dist.all_gather(bufs, padded.contiguous(), group=group)
+        parts = [bufs[r][: counts[r]] for r in range(world)]
+    return torch.cat(parts, 0)
+
+
+def allreduce_sum_(t: Tensor, group=None) -> Tensor:
+    """In-place sum over ranks (ensemble probability partial sums)."""
+    dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+    return t

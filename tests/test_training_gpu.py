@@ -1,0 +1,96 @@
+"""Member-sharded training on one GPU: shard invariance, training progress, prediction.
+
+Members are keyed by global id everywhere (initialisation, batch order, dropout) and
+the kernels are deterministic, so training the pack as one shard or as two shards must
+give bit-identical members.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.philox import permutation_keys
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module', autouse=True)
+def _gpu():
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+
+
+def test_permutation_keys_match_oracle():
+    from tabpack_b200 import ops
+
+    got = ops.permutation_keys(seed=2**40 + 5, epoch=3, member_base=17, P=5, N=1031, device='cuda')
+    want = permutation_keys(seed=2**40 + 5, epoch=3, members=np.arange(17, 22), n_rows=1031)
+    assert np.array_equal(got.cpu().numpy(), want)
+
+
+def _data(n, seed, dev):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(n, 12, generator=g)
+    c = torch.randint(0, 4, (n, 2), generator=g)
+    w = torch.randn(12, generator=g)
+    y = torch.tanh(x @ w / 3) + 0.3 * (c[:, 0] == 1).float() + 0.1 * torch.randn(n, generator=g)
+    return {'x_num': x.to(dev), 'x_cat': c.to(dev), 'y': y.to(dev)}
+
+
+MODEL = dict(n_numerical_features=12, categorical_cardinalities=[3, 3], d_out=1, max_d_block=96, max_n_blocks=3)
+PER_MEMBER = [dict(n_blocks=nb, d_block=db, dropout=p) for nb, db, p in
+              [(1, 64, 0.1), (3, 96, 0.2), (2, 32, 0.0), (3, 48, 0.3), (2, 96, 0.1), (1, 16, 0.05)]]
+
+
+def _trainer(member_range, opt='muon'):
+    from tabpack_b200.training import PackTrainer
+
+    optim = (dict(type='muon', adamw_lr=3e-3, weight_decay=1e-4, muon_lr=2e-2) if opt == 'muon'
+             else dict(type='adamw', lr=3e-3, weight_decay=1e-4))
+    per_opt = [dict(**({'muon_lr': lr} if opt == 'muon' else {'lr': lr * 0.2}))
+               for lr in (1e-2, 2e-2, 5e-3, 1e-2, 3e-2, 2e-2)]
+    return PackTrainer(n_members=6, model=MODEL, per_member_model=PER_MEMBER, optimizer=optim,
+                       per_member_optimizer=per_opt, loss='mse', seed=99, device='cuda', autocast_bf16=True,
+                       member_range=member_range)
+
+
+@pytest.mark.parametrize('opt', ['muon', 'adamw'])
+def test_sharding_is_bit_invariant(opt):
+    data = _data(640, 0, 'cuda')
+    val = _data(300, 1, 'cuda')
+    full = _trainer((0, 6), opt)
+    a, b = _trainer((0, 4), opt), _trainer((4, 6), opt)
+    for epoch in range(2):
+        for t in (full, a, b):
+            t.fit_epoch(data, batch_size=64, epoch=epoch)
+    sd_full = full.model.state_dict()
+    for shard, lo in ((a, 0), (b, 4)):
+        for k, v in shard.model.state_dict().items():
+            w = sd_full[k]
+            if v.ndim == 0 or w.shape[1:] != v.shape[1:]:
+                continue  # pack maxima (e.g. max widths) differ between shards
+            assert torch.equal(v, w[lo: lo + v.shape[0]]), k
+    pf = full.predict_local(val)
+    pa, pb = a.predict_local(val), b.predict_local(val)
+    assert torch.equal(torch.cat([pa, pb]), pf)
+
+
+def test_training_reduces_loss_and_ensembles():
+    from tabpack_b200.training import PackPredictor
+
+    data = _data(2048, 2, 'cuda')
+    val = _data(512, 3, 'cuda')
+    t = _trainer((0, 6), 'muon')
+    first = None
+    for epoch in range(4):
+        loss = t.fit_epoch(data, batch_size=128, epoch=epoch)
+        first = loss if first is None else first
+    res = t.evaluate_and_ensemble(val, epoch=3, train_loss=loss, max_ensemble_size=4)
+    assert torch.all(loss < first)
+    assert torch.isfinite(res.val_metric).all()
+    assert 1 <= len(res.ensemble_idx) <= 4
+    assert res.ensemble_score <= float(res.val_metric.min()) + 1e-6
+    pred = PackPredictor(t, {'greedy': res.ensemble_idx})
+    y_pack, heads = pred(val['x_num'], val['x_cat'])
+    want = y_pack[res.ensemble_idx].mean(0)
+    torch.testing.assert_close(heads['greedy'], want, rtol=1e-6, atol=1e-6)
