@@ -394,6 +394,74 @@ TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
 }
 
 
+def run_optimizer(args) -> None:
+    """Grouped optimizer step: `members` x 3 weight matrices with rows and cols ~ U{64..1024
+    step 16} (entries N(0, 0.02^2), gradients N(0, 1e-3^2)), one Muon group per matrix with
+    5 Newton-Schulz iterations, per-member lr / weight decay / momentum."""
+    import torch
+
+    from tabpack_b200 import ops
+
+    dev = torch.device('cuda', 0)
+    torch.cuda.set_device(dev)
+    P = args.members
+    rng = np.random.default_rng(5)
+    groups = []
+    flops = 0.0
+    elems = 0
+    for j in range(3):
+        outs = rng.integers(4, 65, P).astype(np.int32) * 16
+        ins = rng.integers(4, 65, P).astype(np.int32) * 16
+        mo, mi = int(outs.max()), int(ins.max())
+        g = torch.Generator(device=dev).manual_seed(j)
+        p = torch.zeros(P, mo, mi, device=dev)
+        grad = torch.zeros_like(p)
+        mask = ((torch.arange(mo, device=dev)[None, :, None] < torch.from_numpy(outs).to(dev)[:, None, None]) &
+                (torch.arange(mi, device=dev)[None, None, :] < torch.from_numpy(ins).to(dev)[:, None, None]))
+        p.copy_(torch.randn(P, mo, mi, device=dev, generator=g) * 0.02 * mask)
+        grad.copy_(torch.randn(P, mo, mi, device=dev, generator=g) * 1e-3 * mask)
+        del mask
+        r = np.minimum(outs, ins).astype(np.float64)
+        c = np.maximum(outs, ins).astype(np.float64)
+        flops += float(np.sum(5 * (4 * r * r * c + 2 * r ** 3)))
+        elems += int(np.sum(outs.astype(np.int64) * ins))
+        groups.append(dict(p=p, grad=grad, m=torch.zeros_like(p), outf=torch.from_numpy(outs).to(dev),
+                           inf=torch.from_numpy(ins).to(dev), ws=torch.empty(ops.muon_workspace_size(P, mo, mi),
+                                                                             dtype=torch.uint8, device=dev)))
+    lr = torch.from_numpy(np.exp(rng.uniform(np.log(1e-4), np.log(1e-2), P)).astype(np.float32)).to(dev)
+    wd = torch.from_numpy(np.exp(rng.uniform(np.log(1e-6), np.log(1e-2), P)).astype(np.float32)).to(dev)
+    mu = torch.full((P,), 0.95, device=dev)
+
+    def step():
+        for gr in groups:
+            ops.muon_step(gr['p'], gr['grad'], gr['m'], out_features=gr['outf'], in_features=gr['inf'], lr=lr,
+                          momentum=mu, weight_decay=wd, nesterov=True, mutate_grad=False, ns_steps=5,
+                          workspace=gr['ws'])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    peaks, kind = load_peaks()
+    ach = flops / (ms / 1e3) / 1e12
+    print(json.dumps({
+        'metric': 'grouped Muon optimizer step (3 ragged matrices per member)', 'value': 3 * P / (ms / 1e3),
+        'unit': 'matrices/s', 'ms_per_step': ms, 'steps': args.steps, 'warmup': args.warmup,
+        'config': {'workload': f'{P} members x 3 matrices, rows/cols U{{64..1024 step 16}}, 5 Newton-Schulz iterations',
+                   'ns_tflop_per_step': flops / 1e12, 'elements': elems},
+        'roofline': {'bound': 'tensor', 'achieved': ach, 'peak': peaks['bf16_tflops_sustained'], 'unit': 'TFLOP/s',
+                     'frac': ach / peaks['bf16_tflops_sustained'], 'peak_source': f'{kind} (sustained)',
+                     'note': 'whole step (elementwise + Newton-Schulz) time against Newton-Schulz FLOPs'},
+        'clocks': clocks.summary()}), flush=True)
+
+
 def main() -> None:
     global MEMBERS
     ap = argparse.ArgumentParser()
@@ -404,8 +472,13 @@ def main() -> None:
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--members', type=int, default=MEMBERS, help='members per GPU (smaller for profiling)')
+    ap.add_argument('--workload', choices=['layer', 'optimizer'], default='layer',
+                    help='layer: the packed-block fwd+bwd benchmark (default); optimizer: grouped Muon step')
     args = ap.parse_args()
     MEMBERS = args.members
+    if args.workload == 'optimizer':
+        run_optimizer(args)
+        return
     if args.impl == 'reference':
         run_reference(args)
     else:

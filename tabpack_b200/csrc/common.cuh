@@ -34,6 +34,29 @@ __host__ __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, ui
   return c;
 }
 
+// Philox4x32-10 with a precomputed key schedule ks[2*i], ks[2*i+1] = key words of round i
+// (held in kernel parameters, i.e. constant-bank operands of the XORs).
+__device__ __forceinline__ uint4 philox4x32_10_ks(uint4 c, const uint32_t* ks) {
+#pragma unroll
+  for (int i = 0; i < 10; ++i) {
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c.x;
+    const uint64_t p1 = (uint64_t)0xCD9E8D57u * c.z;
+    const uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0;
+    const uint32_t hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+    c = make_uint4(hi1 ^ c.y ^ ks[2 * i], lo1, hi0 ^ c.w ^ ks[2 * i + 1], lo0);
+  }
+  return c;
+}
+
+__host__ __device__ inline void philox_key_schedule(uint32_t k0, uint32_t k1, uint32_t* ks) {
+  for (int i = 0; i < 10; ++i) {
+    ks[2 * i] = k0;
+    ks[2 * i + 1] = k1;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+}
+
 // floor(float32(1 - p) * 2^16): an element is kept iff its 16-bit draw is below it.
 __device__ __forceinline__ uint32_t keep_threshold(float p) {
   const float keep = 1.0f - p;
@@ -84,20 +107,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps (without issuing) until the phase
+// completes or the hint expires, instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(0x989680u)  // 10 ms
+      : "memory");
+  return ok != 0;
+}
+
 // Returns false on timeout or when *abort is already set.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const uint32_t b = smem_u32(bar);
   if (mbar_try_wait(b, parity)) return true;
   const long long t0 = clock64();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(b, parity)) return true;
-    if ((it & 63u) == 0) {
-      if (*abort) return false;
-      if ((unsigned long long)(clock64() - t0) > TP_WAIT_CYCLES) {
-        *abort = 1;
-        atomicExch(&g_device_error, TP_ETIMEOUT);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_sleep(b, parity)) return true;
+    if (*abort) return false;
+    if ((unsigned long long)(clock64() - t0) > TP_WAIT_CYCLES) {
+      *abort = 1;
+      atomicExch(&g_device_error, TP_ETIMEOUT);
+      return false;
     }
   }
 }

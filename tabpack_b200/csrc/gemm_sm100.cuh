@@ -34,7 +34,11 @@ struct Sm100Cfg {
   // stages + barriers (full, empty per stage; tfull, tempty x2; done) + tmem addr + abort
   // + per-warp bias slice (BN / (EPI_WARPS / 4) floats per epilogue warp)
   static constexpr int BIAS_FLOATS_PER_WARP = BN / (EPI_WARPS / 4);
-  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + EPI_WARPS * BIAS_FLOATS_PER_WARP * 4;
+  // + per-warp staging tile for coalesced bf16 stores (32 rows x 32 columns, rows padded to 80 B)
+  static constexpr int STAGE_ROW_BYTES = 80;
+  static constexpr int STORE_STAGE_BYTES = 32 * STAGE_ROW_BYTES;
+  static constexpr int SMEM_BYTES =
+      1024 + STAGES * STAGE_BYTES + 256 + EPI_WARPS * BIAS_FLOATS_PER_WARP * 4 + EPI_WARPS * STORE_STAGE_BYTES;
 };
 
 // Epilogue of one 32-column chunk of one output row held in registers `r`
@@ -42,58 +46,47 @@ struct Sm100Cfg {
 template <int MODE>
 __device__ __forceinline__ void epi_chunk(const LinearProblem& pr, const TileInfo& ti, int m, int row, int col0,
                                           const uint32_t (&r)[32], bool dropout_on, uint32_t thr, float scale,
-                                          const float* sbias) {
+                                          const float* sbias, uint8_t* stage, float* wg_out = nullptr) {
   const int nv = ti.n_valid - col0;  // valid columns in this chunk (may be <= 0)
   if (MODE == MODE_FWD) {
-    // streamed in groups of 8 columns: bias, ReLU, Philox keep, bf16 pack, 16-byte store
-    __nv_bfloat16* dst =
-        reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld + col0;
+    // Groups of 8 columns: bias, ReLU, keep mask, bf16 pack into the staging tile.  The
+    // chunk's four Philox chains are computed up front so they interleave (each is a
+    // 10-round dependent sequence).
     const int ncols = pr.out_cols - col0;
-    const bool drop = dropout_on && thr < 65536u;
+    const bool drop = dropout_on && thr < 65536u && nv > 0;
+    uint4 q4[4];
+    if (drop) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+        q4[g] = philox4x32_10_ks(
+            make_uint4((uint32_t)(col0 >> 3) + g, (uint32_t)row, pr.member_base + (uint32_t)m, pr.offset), pr.ks);
+    }
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      if (8 * g >= ncols) break;
-      float x[8];
       const int gv = nv - 8 * g;  // valid columns in this group
-      if (gv <= 0) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) x[j] = 0.0f;
-      } else {
-        // bias slice staged in shared memory by this warp (zero beyond n_valid)
+      uint4 u = make_uint4(0, 0, 0, 0);
+      if (gv > 0) {
         const float4 b0 = *reinterpret_cast<const float4*>(sbias + 8 * g);
         const float4 b1 = *reinterpret_cast<const float4*>(sbias + 8 * g + 4);
         const float b8[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-        if (drop) {
-          // relu(t) * (keep ? scale : 0) == max(t * (keep ? scale : 0), 0) since scale > 0
-          const uint4 w = philox4x32_10(
-              make_uint4((uint32_t)(col0 >> 3) + g, (uint32_t)row, pr.member_base + (uint32_t)m, pr.offset), pr.k0,
-              pr.k1);
-          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const uint32_t w[4] = {q4[g].x, q4[g].y, q4[g].z, q4[g].w};
+        float x[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint32_t r16 = (j & 1) ? (ws[j >> 1] >> 16) : (ws[j >> 1] & 0xFFFFu);
-            const float mult = r16 < thr ? scale : 0.0f;
-            const float t = (__uint_as_float(r[8 * g + j]) + b8[j]) * mult;
-            x[j] = pr.relu ? fmaxf(t, 0.0f) : t;
+        for (int j = 0; j < 8; ++j) {
+          float t = __uint_as_float(r[8 * g + j]) + b8[j];
+          if (pr.relu) t = fmaxf(t, 0.0f);
+          if (drop) {
+            const uint32_t r16 = (j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xFFFFu);
+            t = r16 < thr ? t * scale : 0.0f;
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float t = __uint_as_float(r[8 * g + j]) + b8[j];
-            x[j] = pr.relu ? fmaxf(t, 0.0f) : t;
-          }
+          x[j] = j < gv ? t : 0.0f;
         }
-        if (gv < 8) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) x[j] = j < gv ? x[j] : 0.0f;
-        }
+        u.x = pack_bf16x2(x[0], x[1]);
+        u.y = pack_bf16x2(x[2], x[3]);
+        u.z = pack_bf16x2(x[4], x[5]);
+        u.w = pack_bf16x2(x[6], x[7]);
       }
-      uint4 u;
-      u.x = pack_bf16x2(x[0], x[1]);
-      u.y = pack_bf16x2(x[2], x[3]);
-      u.z = pack_bf16x2(x[4], x[5]);
-      u.w = pack_bf16x2(x[6], x[7]);
-      *reinterpret_cast<uint4*>(dst + 8 * g) = u;  // out_cols is a multiple of 8 on this path
+      if (8 * g < ncols) *reinterpret_cast<uint4*>(stage + 16 * g) = u;
     }
     return;
   }
@@ -125,31 +118,62 @@ __device__ __forceinline__ void epi_chunk(const LinearProblem& pr, const TileInf
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = (rv && j < nv) ? __uint_as_float(r[j]) : 0.0f;
   }
-  const int ncols = pr.out_cols - col0;  // storable columns in this chunk (> 0)
   if (MODE == MODE_WGRAD) {
-    float* dst = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld + col0;
-    if (ncols >= 32 && (pr.out_ld & 3) == 0) {
+    // fp32: the caller flushes the chunk in two 16-column halves through the staging tile
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (j < ncols) dst[j] = v[j];
-    }
+    for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(wg_out + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
   } else {
-    __nv_bfloat16* dst =
-        reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld + col0;
 #pragma unroll
     for (int j = 0; j < 32; j += 8) {
-      if (j < ncols) {  // out_cols is a multiple of 8 on this path
-        uint4 u;
-        u.x = pack_bf16x2(v[j], v[j + 1]);
-        u.y = pack_bf16x2(v[j + 2], v[j + 3]);
-        u.z = pack_bf16x2(v[j + 4], v[j + 5]);
-        u.w = pack_bf16x2(v[j + 6], v[j + 7]);
-        *reinterpret_cast<uint4*>(dst + j) = u;
-      }
+      uint4 u;
+      u.x = pack_bf16x2(v[j], v[j + 1]);
+      u.y = pack_bf16x2(v[j + 2], v[j + 3]);
+      u.z = pack_bf16x2(v[j + 4], v[j + 5]);
+      u.w = pack_bf16x2(v[j + 6], v[j + 7]);
+      *reinterpret_cast<uint4*>(stage + j * 2) = u;
     }
+  }
+}
+
+// Writes a warp's 32 x 16 fp32 half-chunk (row r's 64 bytes at stage_warp + r * row_bytes)
+// to columns col0.. of the fp32 output, 4 lanes per row.
+__device__ __forceinline__ void stage_flush_f32(const LinearProblem& pr, int m, int row_base, int col0,
+                                                const uint8_t* stage_warp, int lane, int row_bytes) {
+  const int c = lane & 3;
+  float* base = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms;
+  const bool vec = (pr.out_ld & 3) == 0 && col0 + 4 * c + 4 <= pr.out_cols;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = (lane >> 2) + 8 * k;
+    const int grow = row_base + r;
+    if (grow >= pr.out_rows) continue;
+    const float4 v = *reinterpret_cast<const float4*>(stage_warp + r * row_bytes + c * 16);
+    float* d = base + (size_t)grow * pr.out_ld + col0 + 4 * c;
+    if (vec) {
+      *reinterpret_cast<float4*>(d) = v;
+    } else {
+      const float e[4] = {v.x, v.y, v.z, v.w};
+      for (int j = 0; j < 4; ++j)
+        if (col0 + 4 * c + j < pr.out_cols) d[j] = e[j];
+    }
+  }
+}
+
+// Writes a warp's staged 32 x 32 bf16 chunk (rows row_base.., columns col0..) to global
+// memory with 4 lanes per row (64 contiguous bytes), so one store instruction covers
+// 8 rows instead of 32 scattered 16-byte pieces.
+__device__ __forceinline__ void stage_flush(const LinearProblem& pr, int m, int row_base, int col0,
+                                            const uint8_t* stage_warp, int lane, int row_bytes) {
+  const int c = lane & 3;
+  if (col0 + 8 * c >= pr.out_cols) return;  // out_cols is a multiple of 8 on this path
+  __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms + col0 + 8 * c;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = (lane >> 2) + 8 * k;
+    const int grow = row_base + r;
+    if (grow < pr.out_rows)
+      *reinterpret_cast<uint4*>(base + (size_t)grow * pr.out_ld) =
+          *reinterpret_cast<const uint4*>(stage_warp + r * row_bytes + c * 16);
   }
 }
 
@@ -294,6 +318,9 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
     constexpr int WCOLS = BN / (Cfg::EPI_WARPS / 4);
     constexpr int NCH = WCOLS / 32;
     float* sbias = reinterpret_cast<float*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + 256) + ew * WCOLS;
+    uint8_t* stage_warp = smem + Cfg::STAGES * Cfg::STAGE_BYTES + 256 + Cfg::EPI_WARPS * Cfg::BIAS_FLOATS_PER_WARP * 4 +
+                          ew * Cfg::STORE_STAGE_BYTES;
+    uint8_t* stage_row = stage_warp + lane * Cfg::STAGE_ROW_BYTES;
     const int row_in_tile = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -338,18 +365,40 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
             tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN) + (uint32_t)(half * WCOLS);
         // chunks of 32 columns that hold storable output (warp-uniform)
         const int nch = min(NCH, max(0, (pr.out_cols - cbase + 31) / 32));
+        const int row_base = ti.mt * Cfg::BM + q * 32;
+        auto emit_chunk = [&](int col0, const uint32_t(&rr)[32], const float* sb) {
+          if (MODE == MODE_WGRAD) {
+            float vals[32];
+            epi_chunk<MODE>(pr, ti, m, row, col0, rr, dropout_on, thr, scale, sb, nullptr, vals);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<float4*>(stage_row + j * 4) =
+                    make_float4(vals[16 * h + j], vals[16 * h + j + 1], vals[16 * h + j + 2], vals[16 * h + j + 3]);
+              __syncwarp();
+              if (col0 + 16 * h < pr.out_cols)
+                stage_flush_f32(pr, m, row_base, col0 + 16 * h, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
+              __syncwarp();
+            }
+          } else {
+            epi_chunk<MODE>(pr, ti, m, row, col0, rr, dropout_on, thr, scale, sb, stage_row);
+            __syncwarp();
+            stage_flush(pr, m, row_base, col0, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
+            __syncwarp();
+          }
+        };
         uint32_t ra[32], rb[32];
         if (nch > 0) tmem_ld_32x32b_x32(t_row, ra);
 #pragma unroll 1
         for (int c = 0; c < nch; c += 2) {
           tmem_wait_ld();
           if (c + 1 < nch) tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * (c + 1)), rb);
-          if (row_ok) epi_chunk<MODE>(pr, ti, m, row, cbase + 32 * c, ra, dropout_on, thr, scale, sbias + 32 * c);
+          emit_chunk(cbase + 32 * c, ra, sbias + 32 * c);
           if (c + 1 < nch) {
             tmem_wait_ld();
             if (c + 2 < nch) tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * (c + 2)), ra);
-            if (row_ok)
-              epi_chunk<MODE>(pr, ti, m, row, cbase + 32 * (c + 1), rb, dropout_on, thr, scale, sbias + 32 * (c + 1));
+            emit_chunk(cbase + 32 * (c + 1), rb, sbias + 32 * (c + 1));
           }
         }
         tc_fence_before();
@@ -357,28 +406,37 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
         if (lane == 0) mbar_arrive(&tempty[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
-      } else if (row_ok && ti.kind != KIND_SKIP) {
-        // ZERO or COPY block: this thread's row, this warp's column half
+      } else if (ti.kind != KIND_SKIP) {
+        // ZERO or COPY block: this warp's 32 rows x column slice, lanes along the columns
+        const int row_base = ti.mt * Cfg::BM + q * 32;
         const int c_end = min(cbase + WCOLS, pr.out_cols);
         if (MODE == MODE_WGRAD) {
-          float* dst = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld;
-          if ((pr.out_ld & 3) == 0) {
-            int c = cbase;
-            for (; c + 4 <= c_end; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (; c < c_end; ++c) dst[c] = 0.0f;
+          float* base = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms;
+          const int ncol = c_end - cbase;
+          if ((pr.out_ld & 3) == 0 && (ncol & 3) == 0) {
+            const int nq = ncol / 4;
+            for (int i = lane; i < 32 * nq; i += 32) {
+              const int r = i / nq, cc = cbase + 4 * (i - r * nq);
+              if (row_base + r < pr.out_rows)
+                *reinterpret_cast<float4*>(base + (size_t)(row_base + r) * pr.out_ld + cc) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
           } else {
-            for (int c = cbase; c < c_end; ++c) dst[c] = 0.0f;
+            for (int i = lane; i < 32 * ncol; i += 32) {
+              const int r = i / ncol, cc = cbase + (i - r * ncol);
+              if (row_base + r < pr.out_rows) base[(size_t)(row_base + r) * pr.out_ld + cc] = 0.0f;
+            }
           }
         } else {
-          __nv_bfloat16* dst =
-              reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld;
-          if (ti.kind == KIND_ZERO) {
-            for (int c = cbase; c < c_end; c += 8) *reinterpret_cast<uint4*>(dst + c) = make_uint4(0, 0, 0, 0);
-          } else {
-            const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(pr.copy_src) +
-                                       (size_t)m * pr.out_ms + (size_t)row * pr.out_ld;
-            for (int c = cbase; c < c_end; c += 8)
-              *reinterpret_cast<uint4*>(dst + c) = *reinterpret_cast<const uint4*>(src + c);
+          __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms;
+          const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(pr.copy_src) + (size_t)m * pr.out_ms;
+          const int nq = (c_end - cbase) / 8;  // 16-byte pieces per row (out_cols multiple of 8)
+          for (int i = lane; i < 32 * nq; i += 32) {
+            const int r = (nq == WCOLS / 8) ? i / (WCOLS / 8) : i / nq;
+            const int cc = cbase + 8 * (i - r * nq);
+            if (row_base + r >= pr.out_rows) continue;
+            const size_t off = (size_t)(row_base + r) * pr.out_ld + cc;
+            *reinterpret_cast<uint4*>(base + off) =
+                ti.kind == KIND_ZERO ? make_uint4(0, 0, 0, 0) : *reinterpret_cast<const uint4*>(src + off);
           }
         }
       }

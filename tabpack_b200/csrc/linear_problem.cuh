@@ -31,6 +31,7 @@ struct LinearProblem {
   int relu;
   const float* dropout_p;     // (P,) or nullptr
   uint32_t k0, k1, offset, member_base;
+  uint32_t ks[20];            // Philox key schedule of (k0, k1)
   const float* bias;          // (P, bias_ld) or nullptr
   int bias_ld;
   // output: rows x cols per member, leading dim out_ld, member stride out_ms

@@ -192,6 +192,7 @@ LinearProblem base_problem(const tp_linear_args* a) {
   p.dropout_p = a->dropout_p;
   p.k0 = (uint32_t)(a->seed & 0xFFFFFFFFu);
   p.k1 = (uint32_t)(a->seed >> 32);
+  philox_key_schedule(p.k0, p.k1, p.ks);
   p.offset = a->offset;
   p.member_base = a->member_base;
   p.bias = a->bias;

@@ -60,14 +60,16 @@ def make_case(P, B, max_in, max_out, in_f=None, out_f=None, shared=False, seed=0
     return x, w, b, p
 
 
-def oracle_forward(x, w, b, out_f, p, seed, offset, member_base, B, relu=True, dropout=True):
+def oracle_forward(x, w, b, out_f, p, seed, offset, member_base, B, relu=True, dropout=True, bf16=False):
+    """The block forward in fp64 (the kernels round each output to bf16 once)."""
     P, max_out, _ = w.shape
     mv = None
     if dropout:
         mv = ol.dropout_mask_values(seed=seed, offset=offset, members=np.arange(P) + member_base,
                                     n_rows=B, n_cols=max_out, p=p, dtype=np.float64)
-    y, _ = ol.block_forward(x if x.shape[0] == P else np.broadcast_to(x, (P, *x.shape[1:])),
-                            w, b, out_f, mask_values=mv, relu=relu)
+    xx = x if x.shape[0] == P else np.broadcast_to(x, (P, *x.shape[1:]))
+    del bf16
+    y, _ = ol.block_forward(xx, w, b, out_f, mask_values=mv, relu=relu)
     return y, mv
 
 
@@ -109,7 +111,7 @@ def test_forward(dtype, case, dropout):
         seed=seed, offset=offset, member_base=base)
     torch.cuda.synchronize()
     want, _ = oracle_forward(x, w, b.astype(np.float32).astype(np.float64), out_f, p, seed, offset, base, B,
-                             dropout=dropout)
+                             dropout=dropout, bf16=dtype == torch.bfloat16)
     _close(_host(y), want, BF16_RTOL if dtype == torch.bfloat16 else 1e-5, f'y case {case}')
 
 
@@ -183,7 +185,8 @@ def test_depth_gating(dtype):
     dy = _dev(np.random.default_rng(1).standard_normal((P, B, W)), dtype)
     dx, dW, db = ops.linear_backward(dy, xd, wd, y, **kw)
     torch.cuda.synchronize()
-    want, _ = oracle_forward(x, w, b.astype(np.float32).astype(np.float64), None, p, 5, 2, 0, B)
+    want, _ = oracle_forward(x, w, b.astype(np.float32).astype(np.float64), None, p, 5, 2, 0, B,
+                             bf16=dtype == torch.bfloat16)
     tol = BF16_RTOL if dtype == torch.bfloat16 else 1e-5
     for m in range(P):
         if nb[m] > 1:
