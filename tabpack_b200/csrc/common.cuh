@@ -97,35 +97,53 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 
+// CLUSTER: acquire at cluster scope (arrivals released by the peer CTA of a pair).
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
+  if (CLUSTER)
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+  else
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
   return ok != 0;
 }
 
 // try_wait with a suspend-time hint: the thread sleeps (without issuing) until the phase
 // completes or the hint expires, instead of spinning.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(0x989680u)  // 10 ms
-      : "memory");
+  if (CLUSTER)
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(0x989680u)  // 10 ms
+        : "memory");
+  else
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(0x989680u)  // 10 ms
+        : "memory");
   return ok != 0;
 }
 
 // Returns false on timeout or when *abort is already set.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const uint32_t b = smem_u32(bar);
-  if (mbar_try_wait(b, parity)) return true;
+  if (mbar_try_wait<CLUSTER>(b, parity)) return true;
   const long long t0 = clock64();
   for (;;) {
-    if (mbar_try_wait_sleep(b, parity)) return true;
+    if (mbar_try_wait_sleep<CLUSTER>(b, parity)) return true;
     if (*abort) return false;
     if ((unsigned long long)(clock64() - t0) > TP_WAIT_CYCLES) {
       *abort = 1;
@@ -160,6 +178,67 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// CTA-pair form (cta_group::2): the data lands in this CTA's shared memory and the
+// transaction bytes are counted on `bar_cluster`, a shared::cluster address that may
+// name the mbarrier of the pair's leader CTA (no multicast).
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                                                 int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Division by a kernel-invariant divisor (Granlund & Montgomery, "Division by invariant
+// integers using multiplication", PLDI 1994): for 0 <= n < 2^31 and d >= 1,
+// n / d == (umulhi(n, m) + n) >> l with l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1.
+// ---------------------------------------------------------------------------
+struct FastDiv {
+  uint32_t d, m, l;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f;
+  f.d = d;
+  f.l = 0;
+  while ((1ull << f.l) < d) ++f.l;
+  f.m = (uint32_t)((((1ull << f.l) - d) << 32) / d + 1);
+  return f;
+}
+
+__device__ __forceinline__ uint32_t fastdiv(uint32_t n, const FastDiv& f) { return (__umulhi(n, f.m) + n) >> f.l; }
+
+// ---------------------------------------------------------------------------
+// Thread-block clusters (CTA pairs)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the variable at shared::cta address `addr` in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Every thread of both CTAs; orders shared-memory writes (barrier init) before the peer's use.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (own or peer CTA).  CTA-scope
+// release: it only has to follow this thread's completed TMEM reads (ordered by the
+// tcgen05 fences around it), not make its global stores visible cluster-wide, which
+// would make it wait for every outstanding store.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -178,6 +257,19 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+// CTA-pair TMEM allocation: one warp with the same warp index in each CTA of the pair
+// issues it, with the same shared-memory slot; both CTAs receive the same column base.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -191,6 +283,24 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// CTA-pair MMA, issued by the leader CTA: M = 256 rows, A rows 0..127 from the
+// leader's and 128..255 from the peer's shared memory (same offsets), B columns split
+// in halves the same way, D rows 0..127 into the leader's TMEM and 128..255 into the peer's.
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Pair form of umma_commit: the mbarrier may be in either CTA (shared::cluster address).
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
 }
 
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread complete.
@@ -213,6 +323,16 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version bits.
@@ -230,13 +350,13 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
 }
 
 // Instruction descriptor: kind::f16, A = B = bf16, D = f32, M = 128.
-__host__ __device__ __forceinline__ uint32_t idesc_bf16_f32(int n, bool a_mn_major, bool b_mn_major) {
+__host__ __device__ __forceinline__ uint32_t idesc_bf16_f32(int n, bool a_mn_major, bool b_mn_major, int m = 128) {
   return (1u << 4)                     // D format f32
          | (1u << 7)                   // A format bf16
          | (1u << 10)                  // B format bf16
          | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
          ((uint32_t)(n >> 3) << 17)    // N / 8
-         | ((uint32_t)(128 >> 4) << 24);  // M / 16
+         | ((uint32_t)(m >> 4) << 24);    // M / 16
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {

@@ -1,16 +1,17 @@
 // Persistent, warp-specialised ragged grouped GEMM for the packed linear layer on
 // sm_100a: TMA (no multicast) fills a ring of shared-memory stages, one thread
-// issues tcgen05.mma into a double-buffered TMEM accumulator, and four epilogue
+// issues tcgen05.mma into a double-buffered TMEM accumulator, and the epilogue
 // warps drain TMEM with tcgen05.ld, apply the fused epilogue and store.
 //
 //   MODE_FWD  : C[B x out_m]  = X[B x in_m]  * W^T          A K-major, B K-major
 //   MODE_DGRAD: C[B x in_m]   = G[B x out_m] * W            A K-major, B MN-major
 //   MODE_WGRAD: C[out_m x in_m] = G^T * X  (K = batch rows)  A MN-major, B MN-major
 //
-// Warp roles (576 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
-// issuer, warps 2..17 = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31 and
-// column quarter (w-2)/4), four epilogue warps per SM sub-partition so that TMEM
-// loads, Philox chains and stores of one warp overlap the others.
+// Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer, warps 2.. =
+// epilogue (warp w reads TMEM lanes 32*(w%4) .. +31 and column slice (w-2)/4).  The
+// forward runs 16 epilogue warps (four per SM sub-partition: its bias + ReLU + Philox
+// epilogue is latency-bound, so four warps per scheduler hide each other's dependency
+// stalls) over a 3-stage ring; the other modes run 8 epilogue warps over 4 stages.
 #pragma once
 
 #include "linear_problem.cuh"
@@ -19,17 +20,23 @@ namespace tp {
 
 template <int BN_, int MODE>
 struct Sm100Cfg {
-  static constexpr int BM = 128;
+  static constexpr int BM = 128;  // accumulator rows per CTA (TMEM lanes)
   static constexpr int BN = BN_;
   static constexpr int BK = 64;  // one 128-byte swizzle atom of bf16 along K
+  // CTA pairs (cta_group::2) for the batch-row GEMMs: the pair computes a 256 x BN tile,
+  // each CTA stages its own 128 rows of A and half of B's columns, so the operand bytes
+  // a CTA loads and its tensor core reads per MMA drop by a third.
+  static constexpr bool PAIR = (MODE == MODE_FWD || MODE == MODE_DGRAD) && BN_ == 256;
+  static constexpr int TILE_M = PAIR ? 2 * BM : BM;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B columns staged per CTA
   static constexpr bool A_MN = (MODE == MODE_WGRAD);
   static constexpr bool B_MN = (MODE == MODE_DGRAD || MODE == MODE_WGRAD || MODE == MODE_NS_BMN);
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int STAGES = PAIR ? (MODE == MODE_FWD ? 5 : 6) : (BN == 256) ? 4 : 6;
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = B_ROWS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int EPI_WARPS = 8;
+  static constexpr int EPI_WARPS = (MODE == MODE_FWD) ? 16 : 8;
   static constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
   // stages + barriers (full, empty per stage; tfull, tempty x2; done) + tmem addr + abort
   // + per-warp bias slice (BN / (EPI_WARPS / 4) floats per epilogue warp)
@@ -40,6 +47,51 @@ struct Sm100Cfg {
   static constexpr int SMEM_BYTES =
       1024 + STAGES * STAGE_BYTES + 256 + EPI_WARPS * BIAS_FLOATS_PER_WARP * 4 + EPI_WARPS * STORE_STAGE_BYTES;
 };
+
+// Forward epilogue of one 16-column chunk (columns col0.., col0 a multiple of 16) of one
+// output row: bias, ReLU, Philox keep mask and scale, bf16 pack into 32 bytes of the
+// row's staging slot.  The chunk's two Philox chains are independent and interleave.
+__device__ __forceinline__ void epi_fwd16(const LinearProblem& pr, int m, int row, int col0, const uint32_t (&r)[16],
+                                          int nv, bool drop, uint32_t thr, float scale, const float* sbias,
+                                          uint8_t* stage) {
+  uint4 q2[2];
+  if (drop) {
+#pragma unroll
+    for (int g = 0; g < 2; ++g)
+      q2[g] = philox4x32_10_ks(
+          make_uint4((uint32_t)(col0 >> 3) + g, (uint32_t)row, pr.member_base + (uint32_t)m, pr.offset), pr.ks);
+  }
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const int gv = nv - 8 * g;  // valid columns in this group of 8
+    const float4 b0 = *reinterpret_cast<const float4*>(sbias + 8 * g);
+    const float4 b1 = *reinterpret_cast<const float4*>(sbias + 8 * g + 4);
+    const float b8[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    const uint32_t w[4] = {q2[g].x, q2[g].y, q2[g].z, q2[g].w};
+    float x[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float t = __uint_as_float(r[8 * g + j]) + b8[j];
+      if (pr.relu) t = fmaxf(t, 0.0f);
+      if (drop) {
+        const uint32_t r16 = (j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xFFFFu);
+        t = r16 < thr ? t * scale : 0.0f;
+      }
+      x[j] = t;
+    }
+    if (gv < 8) {  // ragged last group (warp-uniform): zeros beyond the member's columns
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j >= gv) x[j] = 0.0f;
+    }
+    uint4 u;
+    u.x = pack_bf16x2(x[0], x[1]);
+    u.y = pack_bf16x2(x[2], x[3]);
+    u.z = pack_bf16x2(x[4], x[5]);
+    u.w = pack_bf16x2(x[6], x[7]);
+    *reinterpret_cast<uint4*>(stage + 16 * g) = u;
+  }
+}
 
 // Epilogue of one 32-column chunk of one output row held in registers `r`
 // (raw fp32 accumulator bits from tcgen05.ld).
@@ -177,6 +229,13 @@ __device__ __forceinline__ void stage_flush(const LinearProblem& pr, int m, int 
   }
 }
 
+// Columns a CTA pair multiplies in tile `ti`: the member's remaining columns rounded up
+// to 32 (each CTA's half a multiple of 16), at most BN.
+template <int BN>
+__device__ __forceinline__ int pair_n_mma(const TileInfo& ti) {
+  return min(BN, (ti.n_valid - ti.nt * BN + 31) & ~31);
+}
+
 template <int BN, int MODE>
 __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
     linear_gemm_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -199,6 +258,11 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
   const int warp = warp_id();
   const int lane = lane_id();
   const int total_tiles = pr.P * pr.m_tiles * pr.n_tiles;
+  constexpr bool PAIR = Cfg::PAIR;
+  // persistent tile loop over clusters: a CTA pair takes the same tiles
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::STAGES; ++s) {
@@ -207,7 +271,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], Cfg::EPI_WARPS);
+      mbar_init(&tempty[i], PAIR ? 2 * Cfg::EPI_WARPS : Cfg::EPI_WARPS);  // the leader's counts both CTAs
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -215,9 +279,15 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    else
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -226,30 +296,47 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      for (int t = tile0; t < total_tiles; t += tile_step) {
         const TileInfo ti = decode_tile(pr, t, Cfg::BK);
         if (ti.kind != KIND_MMA) continue;
         const int zA = (MODE == MODE_FWD && pr.x_shared) ? 0 : ti.member;  // NS operands are per member
         const int zB = (MODE == MODE_WGRAD && pr.x_shared) ? 0 : ti.member;
+        // this CTA's A rows and B columns: in a pair the leader takes rows 0..127 and the
+        // first half of the (trimmed) columns, the peer rows 128..255 and the second half
+        const int a_row = ti.mt * Cfg::TILE_M + (int)rank * Cfg::BM;
+        const int b_col = ti.nt * BN + (PAIR ? (int)rank * (pair_n_mma<BN>(ti) / 2) : 0);
         for (int kb = 0; kb < ti.kblocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
-          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
           uint8_t* a = smA + stage * Cfg::A_BYTES;
           uint8_t* b = smB + stage * Cfg::B_BYTES;
           const int k0 = kb * Cfg::BK;
+          if constexpr (PAIR) {
+            // both CTAs' bytes complete on the leader's full barrier
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_3d_pair(a, &tmA, fb, k0, a_row, zA);
+            if (!Cfg::B_MN) {
+              tma_load_3d_pair(b, &tmB, fb, k0, b_col, zB);
+            } else {
+#pragma unroll
+              for (int c = 0; c < Cfg::B_ROWS / 64; ++c) tma_load_3d_pair(b + c * 64 * 128, &tmB, fb, b_col + c * 64, k0, zB);
+            }
+          } else {
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
           if (!Cfg::A_MN) {
-            tma_load_3d(a, &tmA, &full[stage], k0, ti.mt * Cfg::BM, zA);
+            tma_load_3d(a, &tmA, &full[stage], k0, a_row, zA);
           } else {
 #pragma unroll
             for (int c = 0; c < Cfg::BM / 64; ++c)
-              tma_load_3d(a + c * 64 * 128, &tmA, &full[stage], ti.mt * Cfg::BM + c * 64, k0, zA);
+              tma_load_3d(a + c * 64 * 128, &tmA, &full[stage], a_row + c * 64, k0, zA);
           }
           if (!Cfg::B_MN) {
-            tma_load_3d(b, &tmB, &full[stage], k0, ti.nt * BN, zB);
+            tma_load_3d(b, &tmB, &full[stage], k0, b_col, zB);
           } else {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)
-              tma_load_3d(b + c * 64 * 128, &tmB, &full[stage], ti.nt * BN + c * 64, k0, zB);
+              tma_load_3d(b + c * 64 * 128, &tmB, &full[stage], b_col + c * 64, k0, zB);
+          }
           }
           if (++stage == Cfg::STAGES) {
             stage = 0;
@@ -261,17 +348,19 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // (in a pair only the leader CTA issues; its MMAs fill both CTAs' TMEM)
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      for (int t = tile0; t < total_tiles; t += tile_step) {
         const TileInfo ti = decode_tile(pr, t, Cfg::BK);
         if (ti.kind != KIND_MMA) continue;
-        // the last column block of a member only multiplies its own columns (N multiple of 16)
-        const int n_mma = min(BN, (ti.n_valid - ti.nt * BN + 15) & ~15);
-        const uint32_t idesc = idesc_bf16_f32(n_mma, Cfg::A_MN, Cfg::B_MN);
+        // the last column block of a member only multiplies its own columns (N multiple of
+        // 16, of 32 for a pair so that each CTA's half is a multiple of 16)
+        const int n_mma = PAIR ? pair_n_mma<BN>(ti) : min(BN, (ti.n_valid - ti.nt * BN + 15) & ~15);
+        const uint32_t idesc = idesc_bf16_f32(n_mma, Cfg::A_MN, Cfg::B_MN, Cfg::TILE_M);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -290,21 +379,37 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
                                              : smem_desc_sw128(a_base + k * 32, 16, 1024);
             const uint64_t bdesc = Cfg::B_MN ? smem_desc_sw128(b_base + k * 2048, 64 * 128, 1024)
                                              : smem_desc_sw128(b_base + k * 32, 16, 1024);
-            umma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            if constexpr (PAIR)
+              umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            else
+              umma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          if constexpr (PAIR) {  // frees the stage in both CTAs
+            umma_commit_pair(smem_u32(&empty[stage]));
+            umma_commit_pair(mapa_shared(smem_u32(&empty[stage]), 1));
+          } else {
+            umma_commit(&empty[stage]);
+          }
           if (++stage == Cfg::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (aborted) break;
-        umma_commit(&tfull[acc]);
+        if constexpr (PAIR) {
+          umma_commit_pair(smem_u32(&tfull[acc]));
+          umma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 1));
+        } else {
+          umma_commit(&tfull[acc]);
+        }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
       // Every MMA issued by this thread has completed once done_bar flips.
-      umma_commit(done_bar);
+      if constexpr (PAIR)
+        umma_commit_pair(smem_u32(done_bar));
+      else
+        umma_commit(done_bar);
       volatile int no_abort = 0;
       mbar_wait(done_bar, 0, &no_abort);
     }
@@ -321,37 +426,48 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
     uint8_t* stage_warp = smem + Cfg::STAGES * Cfg::STAGE_BYTES + 256 + Cfg::EPI_WARPS * Cfg::BIAS_FLOATS_PER_WARP * 4 +
                           ew * Cfg::STORE_STAGE_BYTES;
     uint8_t* stage_row = stage_warp + lane * Cfg::STAGE_ROW_BYTES;
-    const int row_in_tile = q * 32 + lane;
+    const int row_in_tile = (int)rank * Cfg::BM + q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool dropout_on = (MODE == MODE_FWD) && pr.dropout_p != nullptr;
     // tile metadata is decoded one tile ahead so its global loads overlap the current tile
     TileInfo nti;
     float np = 0.0f;
-    if (blockIdx.x < (unsigned)total_tiles) {
-      nti = decode_tile(pr, blockIdx.x, Cfg::BK);
-      if (dropout_on) np = pr.dropout_p[nti.member];
+    // the bias slice of the next MMA tile is loaded into registers one tile ahead
+    float bnext[NCH];
+    auto load_bias = [&](const TileInfo& x) {
+      const int cb = x.nt * BN + half * WCOLS;
+#pragma unroll
+      for (int i = 0; i < NCH; ++i) {
+        const int col = cb + 32 * i + lane;
+        bnext[i] = (MODE == MODE_FWD && x.kind == KIND_MMA && pr.bias != nullptr && col < x.n_valid)
+                       ? __ldg(pr.bias + (size_t)x.member * pr.bias_ld + col)
+                       : 0.0f;
+      }
+    };
+    if (tile0 < total_tiles) {
+      nti = decode_tile(pr, tile0, Cfg::BK);
+      if (dropout_on) np = __ldg(pr.dropout_p + nti.member);
+      if (MODE == MODE_FWD) load_bias(nti);
     }
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+    for (int t = tile0; t < total_tiles; t += tile_step) {
       const TileInfo ti = nti;
       const float p_cur = np;
-      if (t + (int)gridDim.x < total_tiles) {
-        nti = decode_tile(pr, t + gridDim.x, Cfg::BK);
-        if (dropout_on) np = pr.dropout_p[nti.member];
+      if (t + tile_step < total_tiles) {
+        nti = decode_tile(pr, t + tile_step, Cfg::BK);
+        if (dropout_on) np = __ldg(pr.dropout_p + nti.member);
       }
       const int m = ti.member;
-      const int row = ti.mt * Cfg::BM + row_in_tile;
-      const bool row_ok = row < pr.out_rows;
+      const int row = ti.mt * Cfg::TILE_M + row_in_tile;
       const int cbase = ti.nt * BN + half * WCOLS;
       if (ti.kind == KIND_MMA) {
         if (MODE == MODE_FWD) {
-          // stage this warp's bias slice (zero beyond n_valid) before waiting on the MMA
+          // this tile's bias slice (zero beyond n_valid) to smem, then prefetch the next one
           __syncwarp();
-          for (int j = lane; j < WCOLS; j += 32) {
-            const int col = cbase + j;
-            sbias[j] = (pr.bias != nullptr && col < ti.n_valid) ? __ldg(pr.bias + (size_t)m * pr.bias_ld + col) : 0.0f;
-          }
+#pragma unroll
+          for (int i = 0; i < NCH; ++i) sbias[32 * i + lane] = bnext[i];
           __syncwarp();
+          if (t + tile_step < total_tiles) load_bias(nti);
         }
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
         tc_fence_after();
@@ -365,7 +481,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
             tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN) + (uint32_t)(half * WCOLS);
         // chunks of 32 columns that hold storable output (warp-uniform)
         const int nch = min(NCH, max(0, (pr.out_cols - cbase + 31) / 32));
-        const int row_base = ti.mt * Cfg::BM + q * 32;
+        const int row_base = ti.mt * Cfg::TILE_M + (int)rank * Cfg::BM + q * 32;
         auto emit_chunk = [&](int col0, const uint32_t(&rr)[32], const float* sb) {
           if (MODE == MODE_WGRAD) {
             float vals[32];
@@ -388,6 +504,26 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
             __syncwarp();
           }
         };
+        if constexpr (MODE == MODE_FWD) {
+          // 16-column TMEM loads (four warps per scheduler cover their latency); the staged
+          // 32-column slot is flushed after every second chunk
+          const int n16 = 2 * nch;
+          const bool drop = dropout_on && thr < 65536u;
+          uint32_t fa[16];
+#pragma unroll 1
+          for (int c = 0; c < n16; ++c) {
+            const int col0 = cbase + 16 * c;
+            tmem_ld_32x32b_x16(t_row + (uint32_t)(16 * c), fa);
+            tmem_wait_ld();
+            const int nv = ti.n_valid - col0;
+            epi_fwd16(pr, m, row, col0, fa, nv, drop && nv > 0, thr, scale, sbias + 16 * c, stage_row + 32 * (c & 1));
+            if (c & 1) {
+              __syncwarp();
+              stage_flush(pr, m, row_base, col0 - 16, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
+              __syncwarp();
+            }
+          }
+        } else {
         uint32_t ra[32], rb[32];
         if (nch > 0) tmem_ld_32x32b_x32(t_row, ra);
 #pragma unroll 1
@@ -401,14 +537,20 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
             emit_chunk(cbase + 32 * (c + 1), rb, sbias + 32 * (c + 1));
           }
         }
+        }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);
+        if (lane == 0) {
+          if constexpr (PAIR)
+            mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));  // the leader's MMA waits on it
+          else
+            mbar_arrive(&tempty[acc]);
+        }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       } else if (ti.kind != KIND_SKIP) {
         // ZERO or COPY block: this warp's 32 rows x column slice, lanes along the columns
-        const int row_base = ti.mt * Cfg::BM + q * 32;
+        const int row_base = ti.mt * Cfg::TILE_M + (int)rank * Cfg::BM + q * 32;
         const int c_end = min(cbase + WCOLS, pr.out_cols);
         if (MODE == MODE_WGRAD) {
           float* base = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms;
@@ -445,8 +587,14 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // neither CTA leaves while the other may still signal it
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
 #endif
 }
 

@@ -45,6 +45,8 @@ struct LinearProblem {
   const void* b_ptr;
   int m_tiles, n_tiles;
   int BM, BN;
+  FastDiv div_member;  // by m_tiles * n_tiles (tiles per member)
+  FastDiv div_mt;      // by m_tiles
   // Newton-Schulz GEMMs: member m multiplies r = ns_rows[m], c = ns_cols[m] matrices;
   // ns_shape 1: (M, N, K) = (r, r, c), 2: (r, r, r), 3: (r, c, r); members with
   // active[m] == 0 are skipped.
@@ -61,7 +63,7 @@ struct TileInfo {
 };
 
 __device__ __forceinline__ bool member_active(const LinearProblem& p, int m) {
-  return p.n_blocks == nullptr || p.n_blocks[m] > p.block_index;
+  return p.n_blocks == nullptr || __ldg(p.n_blocks + m) > p.block_index;
 }
 
 __device__ __forceinline__ TileInfo decode_tile(const LinearProblem& p, int t, int BK) {
@@ -71,24 +73,24 @@ __device__ __forceinline__ TileInfo decode_tile(const LinearProblem& p, int t, i
   // every n-tile (a row-major order would pin a CTA to n-tile (cta % n_tiles) whenever
   // the grid is a multiple of n_tiles, and padding-only n-tiles would idle those CTAs).
   const int per_member = p.m_tiles * p.n_tiles;
-  ti.member = t / per_member;
+  ti.member = (int)fastdiv((uint32_t)t, p.div_member);
   const int r = t - ti.member * per_member;
-  ti.nt = r / p.m_tiles;
+  ti.nt = (int)fastdiv((uint32_t)r, p.div_mt);
   ti.mt = r - ti.nt * p.m_tiles;
   const int m = ti.member;
   if (p.mode >= MODE_NS) {
-    const int r = p.ns_rows[m], c = p.ns_cols[m];
+    const int r = __ldg(p.ns_rows + m), c = __ldg(p.ns_cols + m);
     ti.m_valid = r;
     ti.n_valid = (p.ns_shape == 3) ? c : r;
     const int k_len = (p.ns_shape == 1) ? c : r;
     ti.kblocks = (k_len + BK - 1) / BK;
-    const bool act = p.active == nullptr || p.active[m] != 0;
+    const bool act = p.active == nullptr || __ldg(p.active + m) != 0;
     ti.kind = (!act || ti.mt * p.BM >= ti.m_valid || ti.nt * p.BN >= ti.n_valid || ti.kblocks == 0) ? KIND_SKIP
                                                                                                      : KIND_MMA;
     return ti;
   }
-  const int in_m = p.in_f ? p.in_f[m] : p.max_in;
-  const int out_m = p.out_f ? p.out_f[m] : p.max_out;
+  const int in_m = p.in_f ? __ldg(p.in_f + m) : p.max_in;
+  const int out_m = p.out_f ? __ldg(p.out_f + m) : p.max_out;
   const bool active = member_active(p, m);
   int k_len;
   if (p.mode == MODE_FWD) {

@@ -122,13 +122,44 @@ int noalloc_scratch(void** out) {
 }
 
 template <int BN, int MODE>
-int launch_sm100(const LinearProblem& pr, const CUtensorMap& a, const CUtensorMap& b, cudaStream_t st) {
+int launch_sm100(const LinearProblem& pr_in, const CUtensorMap& a, const CUtensorMap& b, cudaStream_t st) {
+  LinearProblem pr = pr_in;
+  pr.div_member = make_fastdiv((uint32_t)std::max(1, pr.m_tiles * pr.n_tiles));
+  pr.div_mt = make_fastdiv((uint32_t)std::max(1, pr.m_tiles));
   using Cfg = Sm100Cfg<BN, MODE>;
   auto kern = linear_gemm_sm100<BN, MODE>;
   TP_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
   const long long total = (long long)pr.P * pr.m_tiles * pr.n_tiles;
   if (total > 0x7FFFFFFFLL) return fail(TP_EINVAL, "too many tiles");
-  int grid = (int)std::min<long long>(total, device_info().sms);
+  if (total == 0) return TP_OK;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(Cfg::NUM_THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = st;
+  // persistent workers: CTAs, or CTA pairs (clusters of 2) for the pair modes
+  int workers = device_info().sms;
+  if constexpr (Cfg::PAIR) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    static int max_clusters[64] = {};
+    int dev = 0;
+    TP_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(TP_EUNSUPPORTED, "device index %d out of range", dev);
+    if (max_clusters[dev] == 0) {
+      cfg.gridDim = dim3(2 * (device_info().sms / 2));
+      int n = 0;
+      TP_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+      if (n <= 0) return fail(TP_EUNSUPPORTED, "no CTA pair of this kernel fits on the device");
+      max_clusters[dev] = n;
+    }
+    workers = max_clusters[dev];
+  }
+  int grid = (int)std::min<long long>(total, workers);
   // A persistent CTA takes slots c, c + grid, ...  With the (member, n-tile, m-tile) slot
   // order its n-tile advances by (grid mod slots_per_member) / m_tiles per step; avoid
   // grids for which that step leaves a CTA on a subset of the column blocks.
@@ -142,8 +173,8 @@ int launch_sm100(const LinearProblem& pr, const CUtensorMap& a, const CUtensorMa
       break;
     }
   }
-  kern<<<grid, Cfg::NUM_THREADS, Cfg::SMEM_BYTES, st>>>(a, b, pr);
-  TP_CUDA_TRY(cudaGetLastError());
+  cfg.gridDim = dim3(Cfg::PAIR ? 2 * grid : grid);
+  TP_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a, b, pr));
   return TP_OK;
 }
 
@@ -152,6 +183,8 @@ int launch_simt(LinearProblem pr, cudaStream_t st) {
   pr.BM = pr.BN = 64;
   pr.m_tiles = (pr.out_rows + 63) / 64;
   pr.n_tiles = (pr.out_cols + 63) / 64;
+  pr.div_member = make_fastdiv((uint32_t)std::max(1, pr.m_tiles * pr.n_tiles));
+  pr.div_mt = make_fastdiv((uint32_t)std::max(1, pr.m_tiles));
   const long long total = (long long)pr.P * pr.m_tiles * pr.n_tiles;
   if (total > 0x7FFFFFFFLL) return fail(TP_EINVAL, "too many tiles");
   if (total == 0) return TP_OK;
@@ -300,13 +333,14 @@ int tp_linear_forward(const tp_linear_args* a, void* stream) {
   if (use_tensor_cores(a)) {
     if (!aligned16(a->x) || !aligned16(a->w) || !aligned16(a->y)) return fail(TP_EALIGN, "x, w, y must be 16-byte aligned");
     constexpr int BN = 256;
-    pr.BM = 128;
+    using Cfg = Sm100Cfg<BN, MODE_FWD>;
+    pr.BM = Cfg::TILE_M;
     pr.BN = BN;
-    pr.m_tiles = (a->B + 127) / 128;
+    pr.m_tiles = (a->B + Cfg::TILE_M - 1) / Cfg::TILE_M;
     pr.n_tiles = (a->max_out + BN - 1) / BN;
     CUtensorMap ma, mb;
-    if ((rc = make_map(&ma, a->x, a->max_in, a->B, a->x_shared ? 1 : a->P, 64, 128))) return rc;
-    if ((rc = make_map(&mb, a->w, a->max_in, a->max_out, a->P, 64, BN))) return rc;
+    if ((rc = make_map(&ma, a->x, a->max_in, a->B, a->x_shared ? 1 : a->P, 64, Cfg::BM))) return rc;
+    if ((rc = make_map(&mb, a->w, a->max_in, a->max_out, a->P, 64, Cfg::B_ROWS))) return rc;
     return launch_sm100<BN, MODE_FWD>(pr, ma, mb, st);
   }
   return a->dtype == TP_DTYPE_BF16 ? launch_simt<__nv_bfloat16, MODE_FWD>(pr, st) : launch_simt<float, MODE_FWD>(pr, st);
@@ -374,12 +408,13 @@ int tp_linear_backward(const tp_linear_grad_args* ga, void* stream) {
     if (tc) {
       if (!aligned16(G) || !aligned16(a->w) || !aligned16(ga->dx)) return fail(TP_EALIGN, "g, w, dx must be 16-byte aligned");
       constexpr int BN = 256;
-      pr.BM = 128;
+      using Cfg = Sm100Cfg<BN, MODE_DGRAD>;
+      pr.BM = Cfg::TILE_M;
       pr.BN = BN;
-      pr.m_tiles = (a->B + 127) / 128;
+      pr.m_tiles = (a->B + Cfg::TILE_M - 1) / Cfg::TILE_M;
       pr.n_tiles = (a->max_in + BN - 1) / BN;
       CUtensorMap ma, mb;
-      if ((rc = make_map(&ma, G, a->max_out, a->B, a->P, 64, 128))) return rc;
+      if ((rc = make_map(&ma, G, a->max_out, a->B, a->P, 64, Cfg::BM))) return rc;
       if ((rc = make_map(&mb, a->w, a->max_in, a->max_out, a->P, 64, 64))) return rc;
       if ((rc = launch_sm100<BN, MODE_DGRAD>(pr, ma, mb, st))) return rc;
     } else {
