@@ -6,6 +6,9 @@
 //   MODE_FWD  : C[B x out_m]  = X[B x in_m]  * W^T          A K-major, B K-major
 //   MODE_DGRAD: C[B x in_m]   = G[B x out_m] * W            A K-major, B MN-major
 //   MODE_WGRAD: C[out_m x in_m] = G^T * X  (K = batch rows)  A MN-major, B MN-major
+//   MODE_WGRAD_T: C^T[in_m x out_m] = X^T * G, stored into C (K = batch rows), A and B
+//               MN-major; a warp's 32 lanes hold 32 consecutive input features, so each
+//               output feature's column is one coalesced 128-byte fp32 store
 //
 // Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer, warps 2.. =
 // epilogue (warp w reads TMEM lanes 32*(w%4) .. +31 and column slice (w-2)/4).  The
@@ -26,11 +29,11 @@ struct Sm100Cfg {
   // CTA pairs (cta_group::2) for the batch-row GEMMs: the pair computes a 256 x BN tile,
   // each CTA stages its own 128 rows of A and half of B's columns, so the operand bytes
   // a CTA loads and its tensor core reads per MMA drop by a third.
-  static constexpr bool PAIR = (MODE == MODE_FWD || MODE == MODE_DGRAD) && BN_ == 256;
+  static constexpr bool PAIR = (MODE == MODE_FWD || MODE == MODE_DGRAD || MODE == MODE_WGRAD_T) && BN_ == 256;
   static constexpr int TILE_M = PAIR ? 2 * BM : BM;
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B columns staged per CTA
-  static constexpr bool A_MN = (MODE == MODE_WGRAD);
-  static constexpr bool B_MN = (MODE == MODE_DGRAD || MODE == MODE_WGRAD || MODE == MODE_NS_BMN);
+  static constexpr bool A_MN = (MODE == MODE_WGRAD || MODE == MODE_WGRAD_T);
+  static constexpr bool B_MN = (MODE == MODE_DGRAD || MODE == MODE_WGRAD || MODE == MODE_WGRAD_T || MODE == MODE_NS_BMN);
   static constexpr int STAGES = PAIR ? (MODE == MODE_FWD ? 5 : 6) : (BN == 256) ? 4 : 6;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = B_ROWS * BK * 2;
@@ -299,7 +302,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
       for (int t = tile0; t < total_tiles; t += tile_step) {
         const TileInfo ti = decode_tile(pr, t, Cfg::BK);
         if (ti.kind != KIND_MMA) continue;
-        const int zA = (MODE == MODE_FWD && pr.x_shared) ? 0 : ti.member;  // NS operands are per member
+        const int zA = ((MODE == MODE_FWD || MODE == MODE_WGRAD_T) && pr.x_shared) ? 0 : ti.member;  // NS operands are per member
         const int zB = (MODE == MODE_WGRAD && pr.x_shared) ? 0 : ti.member;
         // this CTA's A rows and B columns: in a pair the leader takes rows 0..127 and the
         // first half of the (trimmed) columns, the peer rows 128..255 and the second half
@@ -314,7 +317,12 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
             // both CTAs' bytes complete on the leader's full barrier
             if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
             const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
-            tma_load_3d_pair(a, &tmA, fb, k0, a_row, zA);
+            if (!Cfg::A_MN) {
+              tma_load_3d_pair(a, &tmA, fb, k0, a_row, zA);
+            } else {
+#pragma unroll
+              for (int c = 0; c < Cfg::BM / 64; ++c) tma_load_3d_pair(a + c * 64 * 128, &tmA, fb, a_row + c * 64, k0, zA);
+            }
             if (!Cfg::B_MN) {
               tma_load_3d_pair(b, &tmB, fb, k0, b_col, zB);
             } else {
@@ -504,7 +512,27 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
             __syncwarp();
           }
         };
-        if constexpr (MODE == MODE_FWD) {
+        if constexpr (MODE == MODE_WGRAD_T) {
+          // lane = input feature `row`, register j = output feature col0 + j:
+          // dW[o][row] for fixed o is 32 consecutive floats across the warp
+          float* base = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms;
+          const bool in_store = row < pr.out_cols;
+          const bool in_valid = row < ti.m_valid;
+          const int nco = min(NCH, max(0, (pr.out_rows - cbase + 31) / 32));
+          uint32_t wa[32];
+#pragma unroll 1
+          for (int c = 0; c < nco; ++c) {
+            const int o0 = cbase + 32 * c;
+            tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * c), wa);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int o = o0 + j;
+              if (in_store && o < pr.out_rows)
+                base[(size_t)o * pr.out_ld + row] = (in_valid && o < ti.n_valid) ? __uint_as_float(wa[j]) : 0.0f;
+            }
+          }
+        } else if constexpr (MODE == MODE_FWD) {
           // 16-column TMEM loads (four warps per scheduler cover their latency); the staged
           // 32-column slot is flushed after every second chunk
           const int n16 = 2 * nch;
@@ -552,7 +580,14 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
         // ZERO or COPY block: this warp's 32 rows x column slice, lanes along the columns
         const int row_base = ti.mt * Cfg::TILE_M + (int)rank * Cfg::BM + q * 32;
         const int c_end = min(cbase + WCOLS, pr.out_cols);
-        if (MODE == MODE_WGRAD) {
+        if (MODE == MODE_WGRAD_T) {
+          // zero block, transposed: output features cbase.. x input features row_base + lane
+          float* base = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms;
+          const int i = row_base + lane;
+          const int o_end = min(cbase + WCOLS, pr.out_rows);
+          if (i < pr.out_cols)
+            for (int o = cbase; o < o_end; ++o) base[(size_t)o * pr.out_ld + i] = 0.0f;
+        } else if (MODE == MODE_WGRAD) {
           float* base = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms;
           const int ncol = c_end - cbase;
           if ((pr.out_ld & 3) == 0 && (ncol & 3) == 0) {

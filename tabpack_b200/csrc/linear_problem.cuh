@@ -15,7 +15,7 @@ namespace tp {
 
 // MODE_NS / MODE_NS_BMN: one Newton-Schulz GEMM, C = alpha * A B^T + beta * D, with
 // per-member shapes taken from (ns_rows, ns_cols) and B read K-major / MN-major.
-enum : int { MODE_FWD = 0, MODE_DGRAD = 1, MODE_WGRAD = 2, MODE_NS = 3, MODE_NS_BMN = 4 };
+enum : int { MODE_FWD = 0, MODE_DGRAD = 1, MODE_WGRAD = 2, MODE_NS = 3, MODE_NS_BMN = 4, MODE_WGRAD_T = 5 };
 enum : int { KIND_MMA = 0, KIND_ZERO = 1, KIND_COPY = 2, KIND_SKIP = 3 };
 
 struct LinearProblem {
@@ -78,7 +78,7 @@ __device__ __forceinline__ TileInfo decode_tile(const LinearProblem& p, int t, i
   ti.nt = (int)fastdiv((uint32_t)r, p.div_mt);
   ti.mt = r - ti.nt * p.m_tiles;
   const int m = ti.member;
-  if (p.mode >= MODE_NS) {
+  if (p.mode == MODE_NS || p.mode == MODE_NS_BMN) {
     const int r = __ldg(p.ns_rows + m), c = __ldg(p.ns_cols + m);
     ti.m_valid = r;
     ti.n_valid = (p.ns_shape == 3) ? c : r;
@@ -101,6 +101,10 @@ __device__ __forceinline__ TileInfo decode_tile(const LinearProblem& p, int t, i
     ti.m_valid = p.B;
     ti.n_valid = in_m;
     k_len = out_m;
+  } else if (p.mode == MODE_WGRAD_T) {  // dW^T = X^T G: rows are input features
+    ti.m_valid = in_m;
+    ti.n_valid = out_m;
+    k_len = p.B;
   } else {
     ti.m_valid = out_m;
     ti.n_valid = in_m;
@@ -108,7 +112,7 @@ __device__ __forceinline__ TileInfo decode_tile(const LinearProblem& p, int t, i
   }
   ti.kblocks = (k_len + BK - 1) / BK;
   if (!active) {
-    ti.kind = (p.mode == MODE_WGRAD) ? KIND_ZERO : KIND_COPY;
+    ti.kind = (p.mode == MODE_WGRAD || p.mode == MODE_WGRAD_T) ? KIND_ZERO : KIND_COPY;
   } else if (ti.mt * p.BM >= ti.m_valid || ti.nt * p.BN >= ti.n_valid || ti.kblocks == 0) {
     ti.kind = KIND_ZERO;
   } else {

@@ -441,15 +441,19 @@ int tp_linear_backward(const tp_linear_grad_args* ga, void* stream) {
     pr.dropout_p = nullptr;
     if (tc) {
       if (!aligned16(G) || !aligned16(a->x)) return fail(TP_EALIGN, "g and x must be 16-byte aligned");
+      // transposed on CTA pairs: rows of the tile are input features (the full input width
+      // in 256-row pair tiles), columns the member's output features (trimmed to 32)
       constexpr int BN = 256;
-      pr.BM = 128;
+      using Cfg = Sm100Cfg<BN, MODE_WGRAD_T>;
+      pr.mode = MODE_WGRAD_T;
+      pr.BM = Cfg::TILE_M;
       pr.BN = BN;
-      pr.m_tiles = (dw_rows + 127) / 128;
-      pr.n_tiles = (dw_cols + BN - 1) / BN;
+      pr.m_tiles = (dw_cols + Cfg::TILE_M - 1) / Cfg::TILE_M;
+      pr.n_tiles = (dw_rows + BN - 1) / BN;
       CUtensorMap ma, mb;
-      if ((rc = make_map(&ma, G, a->max_out, a->B, a->P, 64, 64))) return rc;
-      if ((rc = make_map(&mb, a->x, a->max_in, a->B, a->x_shared ? 1 : a->P, 64, 64))) return rc;
-      if ((rc = launch_sm100<BN, MODE_WGRAD>(pr, ma, mb, st))) return rc;
+      if ((rc = make_map(&ma, a->x, a->max_in, a->B, a->x_shared ? 1 : a->P, 64, 64))) return rc;
+      if ((rc = make_map(&mb, G, a->max_out, a->B, a->P, 64, 64))) return rc;
+      if ((rc = launch_sm100<BN, MODE_WGRAD_T>(pr, ma, mb, st))) return rc;
     } else {
       rc = bf16 ? launch_simt<__nv_bfloat16, MODE_WGRAD>(pr, st) : launch_simt<float, MODE_WGRAD>(pr, st);
       if (rc) return rc;
