@@ -42,6 +42,7 @@ __global__ void __launch_bounds__(256) act_backward_kernel(const ActBwdArgs a) {
   const bool active = a.n_blocks == nullptr || a.n_blocks[m] > a.block_index;
   const bool live = active && strip < out_m;
   float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  int a_rows_done = rl;  // first row of this thread's generic loop
   if (live) {
     float scale = 1.0f;
     uint32_t thr = 65536u;
@@ -53,7 +54,47 @@ __global__ void __launch_bounds__(256) act_backward_kernel(const ActBwdArgs a) {
     const T* dy = reinterpret_cast<const T*>(a.dy) + (size_t)m * a.B * a.W;
     const T* y = reinterpret_cast<const T*>(a.y) + (size_t)m * a.B * a.W;
     T* g = a.g ? reinterpret_cast<T*>(a.g) + (size_t)m * a.B * a.W : nullptr;
-    for (int r = rl; r < a.B; r += 32) {
+    if constexpr (VEC && sizeof(T) == 2) {
+      if (a.relu && c0 + 8 <= a.W) {
+        // bf16 + ReLU (the mask is implied by y > 0): four rows of 16-byte loads in flight
+        // per thread before any use, streaming dy / y past L1
+        constexpr int U = 4;
+        int r0 = rl;
+        for (; r0 + 32 * (U - 1) < a.B; r0 += 32 * U) {
+          uint4 ud[U], uy[U];
+#pragma unroll
+          for (int i = 0; i < U; ++i) {
+            const size_t off = (size_t)(r0 + 32 * i) * a.W + c0;
+            ud[i] = __ldcs(reinterpret_cast<const uint4*>(dy + off));
+            uy[i] = __ldcs(reinterpret_cast<const uint4*>(y + off));
+          }
+#pragma unroll
+          for (int i = 0; i < U; ++i) {
+            const __nv_bfloat16* hd = reinterpret_cast<const __nv_bfloat16*>(&ud[i]);
+            const __nv_bfloat16* hy = reinterpret_cast<const __nv_bfloat16*>(&uy[i]);
+            float gv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float v = __bfloat162float(hy[j]) > 0.f ? __bfloat162float(hd[j]) * scale : 0.f;
+              if (c0 + j >= out_m) v = 0.f;
+              gv[j] = v;
+              sum[j] += v;
+            }
+            if (g) {
+              uint4 u;
+              u.x = pack_bf16x2(gv[0], gv[1]);
+              u.y = pack_bf16x2(gv[2], gv[3]);
+              u.z = pack_bf16x2(gv[4], gv[5]);
+              u.w = pack_bf16x2(gv[6], gv[7]);
+              *reinterpret_cast<uint4*>(g + (size_t)(r0 + 32 * i) * a.W + c0) = u;
+            }
+          }
+        }
+        // remaining rows fall through to the generic loop below
+        a_rows_done = r0;
+      }
+    }
+    for (int r = a_rows_done; r < a.B; r += 32) {
       float d[8], yy[8];
       const size_t off = (size_t)r * a.W + c0;
       if (VEC && c0 + 8 <= a.W) {
