@@ -26,15 +26,17 @@ struct Sm100Cfg {
   static constexpr int BM = 128;  // accumulator rows per CTA (TMEM lanes)
   static constexpr int BN = BN_;
   static constexpr int BK = 64;  // one 128-byte swizzle atom of bf16 along K
-  // CTA pairs (cta_group::2) for the batch-row GEMMs: the pair computes a 256 x BN tile,
+  // CTA pairs (cta_group::2) for the gradient GEMMs: the pair computes a 256 x BN tile,
   // each CTA stages its own 128 rows of A and half of B's columns, so the operand bytes
-  // a CTA loads and its tensor core reads per MMA drop by a third.
-  static constexpr bool PAIR = (MODE == MODE_FWD || MODE == MODE_DGRAD || MODE == MODE_WGRAD_T) && BN_ == 256;
+  // a CTA loads and its tensor core reads per MMA drop by a third.  The forward, whose
+  // time goes to its bias / ReLU / dropout epilogue rather than to operand traffic, runs
+  // on single CTAs (measured a few percent faster than on pairs).
+  static constexpr bool PAIR = (MODE == MODE_DGRAD || MODE == MODE_WGRAD_T) && BN_ == 256;
   static constexpr int TILE_M = PAIR ? 2 * BM : BM;
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B columns staged per CTA
   static constexpr bool A_MN = (MODE == MODE_WGRAD || MODE == MODE_WGRAD_T);
   static constexpr bool B_MN = (MODE == MODE_DGRAD || MODE == MODE_WGRAD || MODE == MODE_WGRAD_T || MODE == MODE_NS_BMN);
-  static constexpr int STAGES = PAIR ? (MODE == MODE_FWD ? 5 : 6) : (BN == 256) ? 4 : 6;
+  static constexpr int STAGES = PAIR ? 6 : (BN == 256) ? (MODE == MODE_FWD ? 3 : 4) : 6;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = B_ROWS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -237,6 +239,19 @@ __device__ __forceinline__ void stage_flush(const LinearProblem& pr, int m, int 
 template <int BN>
 __device__ __forceinline__ int pair_n_mma(const TileInfo& ti) {
   return min(BN, (ti.n_valid - ti.nt * BN + 31) & ~31);
+}
+
+// Zeros in columns [c_begin, c_end) of the warp's 32 output rows (bf16, c_begin and c_end
+// multiples of 8), lanes along 16-byte pieces so that a store instruction covers whole rows.
+__device__ __forceinline__ void zero_fill_bf16(const LinearProblem& pr, int m, int row_base, int c_begin, int c_end,
+                                               int lane) {
+  __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms;
+  const int nq = (c_end - c_begin) / 8;
+  for (int i = lane; i < 32 * nq; i += 32) {
+    const int r = i / nq, cc = c_begin + 8 * (i - r * nq);
+    if (row_base + r < pr.out_rows)
+      *reinterpret_cast<uint4*>(base + (size_t)(row_base + r) * pr.out_ld + cc) = make_uint4(0, 0, 0, 0);
+  }
 }
 
 template <int BN, int MODE>
@@ -534,8 +549,11 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
           }
         } else if constexpr (MODE == MODE_FWD) {
           // 16-column TMEM loads (four warps per scheduler cover their latency); the staged
-          // 32-column slot is flushed after every second chunk
-          const int n16 = 2 * nch;
+          // 32-column slot is flushed after every second chunk.  Only the 32-column chunks
+          // that hold some of the member's columns run the epilogue; the padding after them
+          // is written as plain zeros.
+          const int ncomp = min(nch, max(0, (ti.n_valid - cbase + 31) / 32));
+          const int n16 = 2 * ncomp;
           const bool drop = dropout_on && thr < 65536u;
           uint32_t fa[16];
 #pragma unroll 1
@@ -551,6 +569,8 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
               __syncwarp();
             }
           }
+          const int z0 = cbase + 32 * ncomp, z1 = min(cbase + WCOLS, pr.out_cols);
+          if (z0 < z1) zero_fill_bf16(pr, m, row_base, z0, z1, lane);
         } else {
         uint32_t ra[32], rb[32];
         if (nch > 0) tmem_ld_32x32b_x32(t_row, ra);
