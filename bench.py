@@ -397,7 +397,9 @@ TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
 def run_optimizer(args) -> None:
     """Grouped optimizer step: `members` x 3 weight matrices with rows and cols ~ U{64..1024
     step 16} (entries N(0, 0.02^2), gradients N(0, 1e-3^2)), one Muon group per matrix with
-    5 Newton-Schulz iterations, per-member lr / weight decay / momentum."""
+    5 Newton-Schulz iterations and the update scale sqrt(max(1, out/in)), plus one grouped
+    AdamW launch over the matrices' bias vectors; per-member lr log-U[1e-4, 1e-2], weight
+    decay log-U[1e-6, 1e-2], beta2 U[0.95, 0.999]."""
     import torch
 
     from tabpack_b200 import ops
@@ -430,32 +432,55 @@ def run_optimizer(args) -> None:
                                                                              dtype=torch.uint8, device=dev)))
     lr = torch.from_numpy(np.exp(rng.uniform(np.log(1e-4), np.log(1e-2), P)).astype(np.float32)).to(dev)
     wd = torch.from_numpy(np.exp(rng.uniform(np.log(1e-6), np.log(1e-2), P)).astype(np.float32)).to(dev)
+    beta2 = torch.from_numpy(rng.uniform(0.95, 0.999, P).astype(np.float32)).to(dev)
     mu = torch.full((P,), 0.95, device=dev)
+    for gr in groups:
+        gr['scale'] = torch.sqrt(torch.clamp(gr['outf'].float() / gr['inf'].float(), min=1.0))
+    # AdamW state of the biases (P, max_out) of the three matrices
+    biases = [dict(p=torch.randn(P, gr['p'].shape[1], device=dev) * 0.02,
+                   g=torch.randn(P, gr['p'].shape[1], device=dev) * 1e-3) for gr in groups]
+    for b in biases:
+        b['m'], b['v'] = torch.zeros_like(b['p']), torch.zeros_like(b['p'])
+    adamw_elems = sum(b['p'].numel() for b in biases)
+    adamw_ms = []
 
-    def step():
+    def step(i=0, ev=None):
         for gr in groups:
             ops.muon_step(gr['p'], gr['grad'], gr['m'], out_features=gr['outf'], in_features=gr['inf'], lr=lr,
-                          momentum=mu, weight_decay=wd, nesterov=True, mutate_grad=False, ns_steps=5,
-                          workspace=gr['ws'])
+                          momentum=mu, weight_decay=wd, update_scale=gr['scale'], nesterov=True,
+                          mutate_grad=False, ns_steps=5, workspace=gr['ws'])
+        if ev is not None:
+            ev[0].record()
+        ops.adamw_step([b['p'] for b in biases], [b['g'] for b in biases], [b['m'] for b in biases],
+                       [b['v'] for b in biases], step=i + 1, lr=lr, beta1=0.9, beta2=beta2, eps=1e-8,
+                       weight_decay=wd)
+        if ev is not None:
+            ev[1].record()
 
-    for _ in range(args.warmup):
-        step()
+    for i in range(args.warmup):
+        step(i)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    aev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
     with ClockSampler(0) as clocks:
         e0.record()
-        for _ in range(args.steps):
-            step()
+        for i in range(args.steps):
+            step(args.warmup + i, aev[i])
         e1.record()
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
+    adamw_ms = statistics.mean(a.elapsed_time(b) for a, b in aev)
     peaks, kind = load_peaks()
     ach = flops / (ms / 1e3) / 1e12
     print(json.dumps({
         'metric': 'grouped Muon optimizer step (3 ragged matrices per member)', 'value': 3 * P / (ms / 1e3),
         'unit': 'matrices/s', 'ms_per_step': ms, 'steps': args.steps, 'warmup': args.warmup,
-        'config': {'workload': f'{P} members x 3 matrices, rows/cols U{{64..1024 step 16}}, 5 Newton-Schulz iterations',
-                   'ns_tflop_per_step': flops / 1e12, 'elements': elems},
+        'config': {'workload': f'{P} members x 3 matrices, rows/cols U{{64..1024 step 16}}, 5 Newton-Schulz '
+                               'iterations; AdamW on the 3 bias vectors',
+                   'ns_tflop_per_step': flops / 1e12, 'elements': elems,
+                   'adamw': {'ms': adamw_ms, 'elements': adamw_elems,
+                             'gbs': 28.0 * adamw_elems / (adamw_ms / 1e3) / 1e9,
+                             'hbm_frac': 28.0 * adamw_elems / (adamw_ms / 1e3) / 1e9 / peaks['hbm_gbs']}},
         'roofline': {'bound': 'tensor', 'achieved': ach, 'peak': peaks['bf16_tflops_sustained'], 'unit': 'TFLOP/s',
                      'frac': ach / peaks['bf16_tflops_sustained'], 'peak_source': f'{kind} (sustained)',
                      'note': 'whole step (elementwise + Newton-Schulz) time against Newton-Schulz FLOPs'},
@@ -471,10 +496,13 @@ def main() -> None:
     ap.add_argument('--impl', choices=['b200', 'reference'], default='b200')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--members', type=int, default=MEMBERS, help='members per GPU (smaller for profiling)')
+    ap.add_argument('--members', type=int, default=None,
+                    help='members per GPU (default 256 for the layer workload, 1024 for the optimizer)')
     ap.add_argument('--workload', choices=['layer', 'optimizer'], default='layer',
                     help='layer: the packed-block fwd+bwd benchmark (default); optimizer: grouped Muon step')
     args = ap.parse_args()
+    if args.members is None:
+        args.members = 1024 if args.workload == 'optimizer' else MEMBERS
     MEMBERS = args.members
     if args.workload == 'optimizer':
         run_optimizer(args)

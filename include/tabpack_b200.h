@@ -34,6 +34,7 @@ extern "C" {
 
 #define TP_DTYPE_F32 0  /* fp32 activations and weights, fp32 CUDA-core arithmetic */
 #define TP_DTYPE_BF16 1 /* bf16 activations and weights, tcgen05 tensor cores, fp32 accumulation */
+#define TP_DTYPE_F64 2  /* fp64 scores (tp_binary_roc_auc only) */
 
 /* Arguments of one packed-linear call (one LinearPack, or one MLP block =
  * LinearPack -> ReLU -> DropoutPack).  Widths `max_in`/`max_out` are the
@@ -248,6 +249,18 @@ int tp_softmax_rows(const float* x, int64_t rows, int32_t C, float* out, void* s
  * int32 in [0, 2^31). */
 int tp_permutation_keys(uint64_t seed, uint32_t epoch, uint32_t member_base, int32_t P, int64_t N, int32_t* keys,
                         void* stream);
+
+/* Per-member binary ROC AUC: binary_roc_auc_pack (src/tabpackage/metrics.py:117-150), the
+ * Mann-Whitney U statistic with midranks for ties (_midranks_pack, metrics.py:85-114).
+ * scores (P, N) fp32 (dtype TP_DTYPE_F32) or fp64 (TP_DTYPE_F64); labels (N,) int64, shared by
+ * every member, nonzero = positive; out (P,) in the scores' type, NaN when one class is absent.
+ * Ties and NaNs follow the reference: equal scores (-0.0 == +0.0) share their average rank,
+ * NaNs rank last and are never tied.  The rank sum is exact (integer), where the reference
+ * accumulates it in the scores' type.  One CTA per member sorts its scores (stable radix sort
+ * in the workspace); N < 2^31. */
+size_t tp_roc_auc_workspace_size(int32_t P, int64_t N, int32_t dtype);
+int tp_binary_roc_auc(const void* scores, const int64_t* labels, int32_t P, int64_t N, int32_t dtype, void* out,
+                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* Clears and returns the device-side error flag (TP_OK or TP_ETIMEOUT). */
 int tp_device_error(void);

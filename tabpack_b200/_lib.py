@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(_HERE, 'libtabpack_b200.so')
 
 TP_DTYPE_F32 = 0
 TP_DTYPE_BF16 = 1
+TP_DTYPE_F64 = 2
 TP_MAX_OPT_TENSORS = 32
 TP_NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -114,6 +115,10 @@ SIGNATURES = {
                                        ctypes.c_void_p]),
     'tp_permutation_keys': (ctypes.c_int, [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int32,
                                            ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
+    'tp_roc_auc_workspace_size': (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32]),
+    'tp_binary_roc_auc': (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
+                                         ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                         ctypes.c_void_p]),
     'tp_device_error': (ctypes.c_int, []),
     'tp_last_error_string': (ctypes.c_char_p, []),
     'tp_version': (ctypes.c_char_p, []),

@@ -54,8 +54,9 @@ struct Sm100Cfg {
 };
 
 // Forward epilogue of one 16-column chunk (columns col0.., col0 a multiple of 16) of one
-// output row: bias, ReLU, Philox keep mask and scale, bf16 pack into 32 bytes of the
-// row's staging slot.  The chunk's two Philox chains are independent and interleave.
+// output row: (acc + b) * scale as one fma with the staged b * scale, ReLU (which commutes
+// with the positive scale), Philox keep mask, bf16 pack into 32 bytes of the row's staging
+// slot.  The chunk's two Philox chains are independent and interleave.
 __device__ __forceinline__ void epi_fwd16(const LinearProblem& pr, int m, int row, int col0, const uint32_t (&r)[16],
                                           int nv, bool drop, uint32_t thr, float scale, const float* sbias,
                                           uint8_t* stage) {
@@ -76,11 +77,11 @@ __device__ __forceinline__ void epi_fwd16(const LinearProblem& pr, int m, int ro
     float x[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      float t = __uint_as_float(r[8 * g + j]) + b8[j];
+      float t = fmaf(__uint_as_float(r[8 * g + j]), scale, b8[j]);
       if (pr.relu) t = fmaxf(t, 0.0f);
       if (drop) {
         const uint32_t r16 = (j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xFFFFu);
-        t = r16 < thr ? t * scale : 0.0f;
+        t = r16 < thr ? t : 0.0f;
       }
       x[j] = t;
     }
@@ -105,48 +106,6 @@ __device__ __forceinline__ void epi_chunk(const LinearProblem& pr, const TileInf
                                           const uint32_t (&r)[32], bool dropout_on, uint32_t thr, float scale,
                                           const float* sbias, uint8_t* stage, float* wg_out = nullptr) {
   const int nv = ti.n_valid - col0;  // valid columns in this chunk (may be <= 0)
-  if (MODE == MODE_FWD) {
-    // Groups of 8 columns: bias, ReLU, keep mask, bf16 pack into the staging tile.  The
-    // chunk's four Philox chains are computed up front so they interleave (each is a
-    // 10-round dependent sequence).
-    const int ncols = pr.out_cols - col0;
-    const bool drop = dropout_on && thr < 65536u && nv > 0;
-    uint4 q4[4];
-    if (drop) {
-#pragma unroll
-      for (int g = 0; g < 4; ++g)
-        q4[g] = philox4x32_10_ks(
-            make_uint4((uint32_t)(col0 >> 3) + g, (uint32_t)row, pr.member_base + (uint32_t)m, pr.offset), pr.ks);
-    }
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const int gv = nv - 8 * g;  // valid columns in this group
-      uint4 u = make_uint4(0, 0, 0, 0);
-      if (gv > 0) {
-        const float4 b0 = *reinterpret_cast<const float4*>(sbias + 8 * g);
-        const float4 b1 = *reinterpret_cast<const float4*>(sbias + 8 * g + 4);
-        const float b8[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-        const uint32_t w[4] = {q4[g].x, q4[g].y, q4[g].z, q4[g].w};
-        float x[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float t = __uint_as_float(r[8 * g + j]) + b8[j];
-          if (pr.relu) t = fmaxf(t, 0.0f);
-          if (drop) {
-            const uint32_t r16 = (j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xFFFFu);
-            t = r16 < thr ? t * scale : 0.0f;
-          }
-          x[j] = j < gv ? t : 0.0f;
-        }
-        u.x = pack_bf16x2(x[0], x[1]);
-        u.y = pack_bf16x2(x[2], x[3]);
-        u.z = pack_bf16x2(x[4], x[5]);
-        u.w = pack_bf16x2(x[6], x[7]);
-      }
-      if (8 * g < ncols) *reinterpret_cast<uint4*>(stage + 16 * g) = u;
-    }
-    return;
-  }
   float v[32];
   if (MODE == MODE_NS || MODE == MODE_NS_BMN) {
     // alpha * acc + beta * D inside the member's r x (r|c) block, exact zeros around it
@@ -484,22 +443,23 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
       const int row = ti.mt * Cfg::TILE_M + row_in_tile;
       const int cbase = ti.nt * BN + half * WCOLS;
       if (ti.kind == KIND_MMA) {
+        uint32_t thr = 65536u;
+        float scale = 1.0f;  // 1 / (1 - p): kept elements are (acc + b) * scale
+        if (dropout_on) {
+          thr = keep_threshold(p_cur);
+          scale = keep_scale(p_cur);
+        }
         if (MODE == MODE_FWD) {
-          // this tile's bias slice (zero beyond n_valid) to smem, then prefetch the next one
+          // this tile's bias slice times the keep scale (zero beyond n_valid) to smem, then
+          // prefetch the next one; the epilogue forms (acc + b) * scale as fma(acc, scale, b * scale)
           __syncwarp();
 #pragma unroll
-          for (int i = 0; i < NCH; ++i) sbias[32 * i + lane] = bnext[i];
+          for (int i = 0; i < NCH; ++i) sbias[32 * i + lane] = bnext[i] * scale;
           __syncwarp();
           if (t + tile_step < total_tiles) load_bias(nti);
         }
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
         tc_fence_after();
-        uint32_t thr = 65536u;
-        float scale = 1.0f;
-        if (dropout_on) {
-          thr = keep_threshold(p_cur);
-          scale = keep_scale(p_cur);
-        }
         const uint32_t t_row =
             tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN) + (uint32_t)(half * WCOLS);
         // chunks of 32 columns that hold storable output (warp-uniform)

@@ -17,6 +17,7 @@
 #include "gemm_simt.cuh"
 #include "muon.cuh"
 #include "metrics.cuh"
+#include "roc_auc.cuh"
 
 namespace tp {
 namespace {
@@ -690,6 +691,30 @@ int tp_softmax_rows(const float* x, int64_t rows, int32_t C, float* out, void* s
   const int blocks = (int)std::min<int64_t>((threads + 255) / 256, 1 << 20);
   if ((int64_t)blocks * 256 < threads) return fail(TP_EINVAL, "too many rows for one softmax call");
   softmax_rows_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, rows, C, out);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+size_t tp_roc_auc_workspace_size(int32_t P, int64_t N, int32_t dtype) {
+  if (P <= 0 || N <= 0 || (dtype != TP_DTYPE_F32 && dtype != TP_DTYPE_F64)) return 0;
+  return roc_auc_workspace_bytes(P, N, dtype == TP_DTYPE_F64 ? 8 : 4);
+}
+
+int tp_binary_roc_auc(const void* scores, const int64_t* labels, int32_t P, int64_t N, int32_t dtype, void* out,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  if (!scores || !labels || !out || !workspace) return fail(TP_EINVAL, "null ROC AUC argument");
+  if (P <= 0 || N <= 0) return fail(TP_EINVAL, "ROC AUC needs P > 0 and N > 0 (got %d, %lld)", P, (long long)N);
+  if (N >= (int64_t)1 << 31) return fail(TP_EINVAL, "ROC AUC supports N < 2^31");
+  if (dtype != TP_DTYPE_F32 && dtype != TP_DTYPE_F64) return fail(TP_EINVAL, "ROC AUC scores must be fp32 or fp64");
+  const size_t need = tp_roc_auc_workspace_size(P, N, dtype);
+  if (workspace_bytes < need)
+    return fail(TP_EINVAL, "ROC AUC workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
+  AucArgs a{P, (long long)N, scores, labels, out, workspace};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TP_DTYPE_F64)
+    roc_auc_kernel<uint64_t><<<P, AUC_THREADS, 0, st>>>(a);
+  else
+    roc_auc_kernel<uint32_t><<<P, AUC_THREADS, 0, st>>>(a);
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;
 }

@@ -117,7 +117,9 @@ def greedy_ensemble(predictions: Tensor, *, score_fn, init_top_k: int = 1, max_e
         raise ValueError('`init_top_k` must not exceed `max_ensemble_size`')
     if not predictions.is_cuda:
         raise RuntimeError('tabpack_b200 ensembling runs on CUDA devices only')
-    if not isinstance(score_fn, PackScore):
+    if not isinstance(score_fn, PackScore) or score_fn.metric == 'roc_auc':
+        # no fused candidate scoring for ROC AUC: each iteration ranks its candidate blends
+        # with the per-member sort kernel
         return _greedy_reference_loop(predictions, score_fn, init_top_k, max_ensemble_size, with_replacement)
     k = score_fn.classes(predictions)
     counts, status = ops.greedy_ensemble(

@@ -104,6 +104,25 @@ def multiclass_cross_entropy_pack(*, y_true: Tensor, y_proba: Tensor) -> Tensor:
     return ops.metric_pack('ce', y_proba.reshape(P, rows, y_proba.shape[-1]), yt, y_proba.shape[-1]).to(y_proba.dtype)
 
 
+def binary_roc_auc_pack(*, y_true: Tensor, y_score: Tensor) -> Tensor:
+    """`binary_roc_auc_pack` (`metrics.py:117-150`): per-member ROC AUC as the Mann-Whitney U
+    statistic with midranks, one sort per member on the device (`tp_binary_roc_auc`).
+    Labels are {0, 1}; a nonzero label counts as positive."""
+    if y_true.dtype != torch.int64:
+        raise TypeError('Labels must have the data type `torch.int64`')
+    if y_score.dtype not in (torch.float32, torch.float64):
+        raise TypeError('Scores must have the data type `torch.float32` or `torch.float64`')
+    if y_true.ndim != 1:
+        raise ValueError('The label tensor must have one dimension')
+    if y_score.ndim != 2:
+        raise ValueError('The score tensor must have two dimensions')
+    if y_true.shape[-1] != y_score.shape[-1]:
+        raise ValueError('Labels and scores must have the same batch size')
+    if y_score.numel() == 0:
+        raise ValueError('Scores must not be empty')
+    return ops.binary_roc_auc(y_score, y_true)
+
+
 _PACK_FNS = {'mse': mse_pack, 'mae': mae_pack, 'bce': binary_cross_entropy_pack, 'ce': multiclass_cross_entropy_pack}
 
 
@@ -111,12 +130,14 @@ class PackScore:
     """A higher-is-better score function over stacked predictions, as `greedy_ensemble`
     and `topk_ensemble` take it (`ensemble.py:9-12`), backed by a fused metric.
 
-    metric: 'mse', 'mae', 'bce', 'ce' or 'accuracy_argmax'; `y_true` shared labels;
-    `maximize`: whether larger metric values are better (the score is -metric otherwise).
+    metric: 'mse', 'mae', 'bce', 'ce', 'accuracy_argmax' or 'roc_auc' (binary scores, scored
+    by `binary_roc_auc_pack`; greedy selection then scores each iteration's candidate blends
+    with it instead of the fused scoring kernel); `y_true` shared labels; `maximize`: whether
+    larger metric values are better (the score is -metric otherwise).
     """
 
     def __init__(self, metric: str, y_true: Tensor, *, maximize: bool) -> None:
-        if metric not in ('mse', 'mae', 'bce', 'ce', 'accuracy_argmax'):
+        if metric not in ('mse', 'mae', 'bce', 'ce', 'accuracy_argmax', 'roc_auc'):
             raise ValueError(f'unsupported fused metric {metric!r}')
         self.metric = metric
         self.y_true = y_true
@@ -127,6 +148,9 @@ class PackScore:
 
     def __call__(self, predictions: Tensor) -> Tensor:
         C = predictions.shape[0]
+        if self.metric == 'roc_auc':
+            v = ops.binary_roc_auc(predictions.reshape(C, -1).float(), self.y_true.reshape(-1).to(torch.int64))
+            return v if self.maximize else -v
         k = self.classes(predictions)
         flat = predictions.reshape(C, -1, k) if k > 1 else predictions.reshape(C, -1)
         v = ops.metric_pack(self.metric, flat, self.y_true.reshape(-1), k)

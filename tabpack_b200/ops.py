@@ -312,6 +312,25 @@ def permutation_keys(*, seed: int, epoch: int, member_base: int, P: int, N: int,
     return keys
 
 
+def binary_roc_auc(scores: Tensor, labels: Tensor, workspace: Tensor | None = None) -> Tensor:
+    """(P,) ROC AUC of each row of `scores` (P, N) fp32/fp64 against int64 labels (N,);
+    see `tp_binary_roc_auc`.  The result has the scores' dtype."""
+    scores = _cuda('scores', scores).contiguous()
+    labels = _cuda('labels', labels, torch.int64).contiguous()
+    if scores.dtype not in (torch.float32, torch.float64):
+        raise TypeError('scores must be float32 or float64')
+    P, N = scores.shape
+    dtype = _lib.TP_DTYPE_F64 if scores.dtype == torch.float64 else _lib.TP_DTYPE_F32
+    need = int(load().tp_roc_auc_workspace_size(P, N, dtype))
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=scores.device)
+    out = torch.empty(P, dtype=scores.dtype, device=scores.device)
+    check(load().tp_binary_roc_auc(scores.data_ptr(), labels.data_ptr(), P, N, dtype, out.data_ptr(),
+                                   workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream()),
+          'tp_binary_roc_auc')
+    return out
+
+
 def device_error() -> int:
     """Read and clear the device-side error flag (0 or TP_ETIMEOUT)."""
     return load().tp_device_error()

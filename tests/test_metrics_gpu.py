@@ -110,3 +110,65 @@ def test_greedy_large_matches_oracle(metric):
     np.testing.assert_array_equal(idx.cpu().numpy(), want_idx)
     if want_w is not None:
         np.testing.assert_array_equal(w.cpu().numpy(), want_w)
+
+
+def test_roc_auc_matches_reference(golden):
+    """Golden vectors of the reference's binary_roc_auc_pack (scores rounded to 0.1: ties)."""
+    from tabpack_b200 import metrics as M
+
+    g = golden('metrics.npz')
+    got = M.binary_roc_auc_pack(y_true=_t(g['yb']), y_score=_t(g['sc']))
+    assert got.dtype == torch.float32
+    np.testing.assert_allclose(got.cpu().numpy(), g['auc'], rtol=1e-6)
+
+
+@pytest.mark.parametrize('dtype', [np.float32, np.float64])
+def test_roc_auc_large_with_ties_nans_and_signed_zeros(dtype):
+    """Against the oracle at 50 003 rows: coarse scores (large tie groups), a constant member
+    (AUC 0.5), NaN scores (ranked last, never tied), -0.0 next to +0.0 (tied)."""
+    from tabpack_b200 import metrics as M
+
+    rng = np.random.default_rng(11)
+    N = 50003
+    y = (rng.random(N) < 0.3).astype(np.int64)
+    sc = np.stack([
+        rng.standard_normal(N) + y,                      # distinct scores, informative
+        np.round(rng.standard_normal(N) + 0.5 * y, 1),   # ~80 tie groups
+        np.full(N, 0.25),                                # one group: AUC = 0.5
+        np.where(rng.random(N) < 0.01, np.nan, rng.standard_normal(N) - y),
+        np.where(rng.random(N) < 0.3 + 0.4 * y, 1.0, np.where(rng.random(N) < 0.5, -0.0, 0.0)),
+    ]).astype(dtype)
+    got = M.binary_roc_auc_pack(y_true=_t(y), y_score=_t(sc))
+    want = om.binary_roc_auc_pack(y, sc)
+    assert got.dtype == torch.from_numpy(sc).dtype
+    np.testing.assert_allclose(got.cpu().numpy(), want, rtol=1e-6 if dtype == np.float32 else 1e-12)
+    assert abs(float(got[2]) - 0.5) < 1e-12
+
+
+def test_roc_auc_absent_class_is_nan_and_errors():
+    from tabpack_b200 import metrics as M
+
+    sc = torch.randn(3, 17, device='cuda')
+    out = M.binary_roc_auc_pack(y_true=torch.zeros(17, dtype=torch.int64, device='cuda'), y_score=sc)
+    assert torch.isnan(out).all()
+    with pytest.raises(TypeError):
+        M.binary_roc_auc_pack(y_true=torch.zeros(17, dtype=torch.int32, device='cuda'), y_score=sc)
+    with pytest.raises(ValueError):
+        M.binary_roc_auc_pack(y_true=torch.zeros(16, dtype=torch.int64, device='cuda'), y_score=sc)
+
+
+def test_greedy_with_roc_auc_matches_oracle():
+    """Greedy selection scored by ROC AUC (the reference's loop order, the AUC kernel as the
+    score function) selects the same members as the oracle's greedy with the oracle's AUC."""
+    from tabpack_b200.ensemble import greedy_ensemble
+    from tabpack_b200.metrics import PackScore
+
+    rng = np.random.default_rng(3)
+    C, N = 12, 4000
+    y = (rng.random(N) < 0.4).astype(np.int64)
+    preds = (y[None] + rng.standard_normal((C, N)) * np.linspace(0.6, 2.0, C)[:, None]).astype(np.float32)
+    idx, _ = greedy_ensemble(_t(preds), score_fn=PackScore('roc_auc', _t(y), maximize=True), init_top_k=2,
+                             max_ensemble_size=6)
+    want, _ = oe.greedy_ensemble(preds, lambda p: om.binary_roc_auc_pack(y, p).astype(np.float64), init_top_k=2,
+                                 max_ensemble_size=6)
+    assert sorted(idx.cpu().tolist()) == sorted(np.asarray(want).tolist())
