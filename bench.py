@@ -487,6 +487,66 @@ def run_optimizer(args) -> None:
         'clocks': clocks.summary()}), flush=True)
 
 
+def run_metrics(args) -> None:
+    """Per-epoch evaluation of the full-training configuration's validation split: `members`
+    binary-classification members x 100 000 rows.  Times the fused per-member BCE reduction,
+    the per-member ROC AUC (sort-based) and the fused greedy ensemble selection (BCE, init top-1,
+    at most 32 members), each as its own launch(es) with CUDA events; reports achieved GB/s
+    against the measured HBM copy bandwidth."""
+    import torch
+
+    from tabpack_b200 import ops
+
+    dev = torch.device('cuda', 0)
+    torch.cuda.set_device(dev)
+    P, N = args.members, 100_000
+    g = torch.Generator(device=dev).manual_seed(7)
+    y = (torch.rand(N, device=dev, generator=g) < 0.3).to(torch.int64)
+    logits = torch.randn(P, N, device=dev, generator=g) + y.float() * torch.rand(P, 1, device=dev, generator=g) * 2
+    proba = torch.sigmoid(logits)
+    auc_ws = torch.empty(int(ops.load().tp_roc_auc_workspace_size(P, N, 0)), dtype=torch.uint8, device=dev)
+
+    def timed(fn, reps):
+        for _ in range(max(1, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            out = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps, out
+
+    peaks, kind = load_peaks()
+    with ClockSampler(0) as clocks:
+        bce_ms, _ = timed(lambda: ops.metric_pack('bce', proba, y), args.steps)
+        auc_ms, _ = timed(lambda: ops.binary_roc_auc(proba, y, auc_ws), max(1, args.steps // 4))
+        greedy_ms, (counts, status) = timed(
+            lambda: ops.greedy_ensemble(proba, y, metric='bce', maximize=False, max_ensemble_size=32),
+            max(1, args.steps // 10))
+    st = status.cpu().tolist()
+    bce_bytes = 4.0 * P * N + 8.0 * N
+    # the AUC sort moves each element's 4-byte key and 1-byte label: key build (read 4, write 5),
+    # 4 radix passes (read 4 to count, read 5 + write 5 to scatter), one read of 5 for the ranks
+    auc_bytes = P * N * (4.0 + 5.0 + 4 * 14.0 + 5.0)
+    greedy_bytes = 4.0 * P * N * (st[0] + 1)  # every iteration scores all candidates once
+    gbs = lambda b, ms: b / (ms / 1e3) / 1e9  # noqa: E731
+    print(json.dumps({
+        'metric': f'validation metrics + greedy ensemble ({P} members x {N} rows)',
+        'value': bce_ms + auc_ms + greedy_ms, 'unit': 'ms', 'higher_is_better': False,
+        'steps': args.steps, 'warmup': args.warmup,
+        'config': {'workload': f'binary classification, {P} members x {N} validation rows, fp32 probabilities',
+                   'bce': {'ms': bce_ms, 'gbs': gbs(bce_bytes, bce_ms), 'hbm_frac': gbs(bce_bytes, bce_ms) / peaks['hbm_gbs']},
+                   'roc_auc': {'ms': auc_ms, 'gbs': gbs(auc_bytes, auc_ms),
+                               'hbm_frac': gbs(auc_bytes, auc_ms) / peaks['hbm_gbs'],
+                               'bytes_note': '75 B per element: key build + 4 radix passes + rank pass'},
+                   'greedy': {'ms': greedy_ms, 'iterations': st[0], 'members': st[1],
+                              'gbs': gbs(greedy_bytes, greedy_ms), 'hbm_frac': gbs(greedy_bytes, greedy_ms) / peaks['hbm_gbs']},
+                   'peak_source': f'{kind} (copy)'},
+        'clocks': clocks.summary()}), flush=True)
+
+
 def main() -> None:
     global MEMBERS
     ap = argparse.ArgumentParser()
@@ -498,14 +558,18 @@ def main() -> None:
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--members', type=int, default=None,
                     help='members per GPU (default 256 for the layer workload, 1024 for the optimizer)')
-    ap.add_argument('--workload', choices=['layer', 'optimizer'], default='layer',
-                    help='layer: the packed-block fwd+bwd benchmark (default); optimizer: grouped Muon step')
+    ap.add_argument('--workload', choices=['layer', 'optimizer', 'metrics'], default='layer',
+                    help='layer: the packed-block fwd+bwd benchmark (default); optimizer: grouped Muon step; '
+                         'metrics: validation metrics, ROC AUC and greedy selection')
     args = ap.parse_args()
     if args.members is None:
-        args.members = 1024 if args.workload == 'optimizer' else MEMBERS
+        args.members = {'optimizer': 1024, 'metrics': 512}.get(args.workload, MEMBERS)
     MEMBERS = args.members
     if args.workload == 'optimizer':
         run_optimizer(args)
+        return
+    if args.workload == 'metrics':
+        run_metrics(args)
         return
     if args.impl == 'reference':
         run_reference(args)

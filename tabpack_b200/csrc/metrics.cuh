@@ -52,57 +52,88 @@ __device__ __forceinline__ double block_sum(double v, double* sh) {
   return t;  // valid in thread 0
 }
 
-// Sum over rows of the metric's per-row term for one prediction `row(i, c)`.
-template <typename RowVal>
-__device__ __forceinline__ double metric_row_sum(const MetricSrc& s, RowVal val) {
-  double acc = 0.0;
-  for (int64_t i = threadIdx.x; i < s.N; i += blockDim.x) {
-    float t = 0.0f;
-    if (s.metric == MET_MSE || s.metric == MET_R2) {
-      const float d = val(i, 0) - s.yf[i];
-      t = d * d;
-    } else if (s.metric == MET_MAE) {
-      t = fabsf(val(i, 0) - s.yf[i]);
-    } else if (s.metric == MET_BCE) {
-      const float p = val(i, 0);
-      const float y = (float)s.yi[i];
-      t = -(y * log_clamped(p) + (1.0f - y) * log_clamped(1.0f - p));
-    } else if (s.metric == MET_CE) {
-      const int64_t y = s.yi[i];  // a label outside [0, C) poisons the metric (the reference raises)
-      t = (y >= 0 && y < s.C) ? -log_clamped(val(i, (int)y)) : __int_as_float(0x7fc00000);
-    } else if (s.metric == MET_ACCURACY_ARGMAX) {
-      int best = 0;
-      float bv = val(i, 0);
-      for (int c = 1; c < s.C; ++c) {
-        const float v = val(i, c);
-        if (v > bv || (v != v && bv == bv)) {  // first maximum; NaN wins like torch.argmax
-          bv = v;
-          best = c;
-        }
-      }
-      t = (best == (int)s.yi[i]) ? 1.0f : 0.0f;
-    }
-    acc += (double)t;
+// Per-row term of the single-output metrics for prediction value p of row i.
+template <int MET>
+__device__ __forceinline__ float metric_term(const MetricSrc& s, float p, int64_t i) {
+  if (MET == MET_MSE || MET == MET_R2) {
+    const float d = p - s.yf[i];
+    return d * d;
+  } else if (MET == MET_MAE) {
+    return fabsf(p - s.yf[i]);
+  } else {  // MET_BCE: torch's (t - 1) max(log(1 - p), -100) - t max(log(p), -100)
+    const int64_t y = s.yi[i];
+    if (y == 0 || y == 1) return -log_clamped(y ? p : 1.0f - p);  // the other term is exactly 0
+    const float yf = (float)y;
+    return -(yf * log_clamped(p) + (1.0f - yf) * log_clamped(1.0f - p));
   }
-  return acc;
+}
+
+// Sum over rows [r0, r1) of the metric's per-row term for one prediction `val(i, c)`
+// (this thread's share; the caller reduces over the block).  The single-output metrics read
+// four rows per thread before any arithmetic (loads in flight) and keep two fp64
+// accumulators.
+template <int MET, typename RowVal>
+__device__ __forceinline__ double metric_row_sum(const MetricSrc& s, RowVal val, int64_t r0, int64_t r1) {
+  double acc0 = 0.0, acc1 = 0.0;
+  const int64_t st = blockDim.x;
+  int64_t i = r0 + threadIdx.x;
+  if constexpr (MET == MET_MSE || MET == MET_R2 || MET == MET_MAE || MET == MET_BCE) {
+    constexpr int U = 4;
+    for (; i + (U - 1) * st < r1; i += U * st) {
+      float p[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) p[u] = val(i + u * st, 0);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const double t = (double)metric_term<MET>(s, p[u], i + u * st);
+        if (u & 1)
+          acc1 += t;
+        else
+          acc0 += t;
+      }
+    }
+    for (; i < r1; i += st) acc0 += (double)metric_term<MET>(s, val(i, 0), i);
+  } else {
+    for (; i < r1; i += st) {
+      float t = 0.0f;
+      if (MET == MET_CE) {
+        const int64_t y = s.yi[i];  // a label outside [0, C) poisons the metric (the reference raises)
+        t = (y >= 0 && y < s.C) ? -log_clamped(val(i, (int)y)) : __int_as_float(0x7fc00000);
+      } else {  // MET_ACCURACY_ARGMAX
+        int best = 0;
+        float bv = val(i, 0);
+        for (int c = 1; c < s.C; ++c) {
+          const float v = val(i, c);
+          if (v > bv || (v != v && bv == bv)) {  // first maximum; NaN wins like torch.argmax
+            bv = v;
+            best = c;
+          }
+        }
+        t = (best == (int)s.yi[i]) ? 1.0f : 0.0f;
+      }
+      acc0 += (double)t;
+    }
+  }
+  return acc0 + acc1;
 }
 
 // One block per prediction: out[p] = metric of y_pred[p].
-__global__ void __launch_bounds__(256) metric_pack_kernel(MetricSrc s, const float* yp, const int64_t* yp_int,
-                                                          float* out) {
+template <int MET>
+__global__ void __launch_bounds__(1024) metric_pack_kernel(MetricSrc s, const float* yp, const int64_t* yp_int,
+                                                           float* out) {
   __shared__ double sh[32];
   const int p = blockIdx.x;
   double total;
-  if (s.metric == MET_ACCURACY) {
+  if (MET == MET_ACCURACY) {
     double acc = 0.0;
     const int64_t* q = yp_int + (size_t)p * s.N;
     for (int64_t i = threadIdx.x; i < s.N; i += blockDim.x) acc += (q[i] == s.yi[i]) ? 1.0 : 0.0;
     total = block_sum(acc, sh);
   } else {
     const float* q = yp + (size_t)p * s.N * s.C;
-    total = block_sum(metric_row_sum(s, [&](int64_t i, int c) { return q[i * s.C + c]; }), sh);
+    total = block_sum(metric_row_sum<MET>(s, [&](int64_t i, int c) { return q[i * s.C + c]; }, 0, s.N), sh);
   }
-  if (s.metric == MET_R2) {
+  if (MET == MET_R2) {
     // denominator: sum (y - mean(y))^2 over the shared labels (two passes, fp64)
     double sy = 0.0;
     for (int64_t i = threadIdx.x; i < s.N; i += blockDim.x) sy += (double)s.yf[i];
@@ -148,6 +179,9 @@ struct GreedyArgs {
   int limit;               // stop once wsum reaches it
   int* counts;             // (Cand,)
   float* ens;              // (N, C)
+  int S;                   // row segments per candidate in the scoring launch
+  int64_t seg;             // rows per segment
+  double* partials;        // (Cand, S) fp64 metric sums of the segments
   double* scores;          // (Cand,)
   double* ind_scores;      // (Cand,)
   GreedyState* st;
@@ -155,21 +189,25 @@ struct GreedyArgs {
 
 __device__ __forceinline__ float greedy_weight(int wsum) { return (float)((double)wsum / (double)(wsum + 1)); }
 
-// scores[c] = sign * metric(lerp(pred_c, ens, w)) for every candidate c.
+// partials[c][s] = sum over the rows of segment s of the metric terms of lerp(pred_c, ens, w)
+// for every candidate c (grid: candidates x segments; greedy_select_kernel adds the
+// segments of a candidate in order).
+template <int MET>
 __global__ void __launch_bounds__(256) greedy_score_kernel(GreedyArgs g) {
   __shared__ double sh[32];
   if (g.st->stop) return;
   const int c = blockIdx.x;
+  const int64_t r0 = (int64_t)blockIdx.y * g.seg, r1 = min(g.s.N, r0 + g.seg);
   if (!g.with_replacement && g.counts[c] > 0) return;
   const float w = greedy_weight(g.st->wsum);
   const float* q = g.pred + (size_t)c * g.s.N * g.s.C;
   const float* e = g.ens;
   const int C = g.s.C;
-  const double tot = block_sum(metric_row_sum(g.s, [&](int64_t i, int k) {
+  const double tot = block_sum(metric_row_sum<MET>(g.s, [&](int64_t i, int k) {
                                  return lerp_t(q[i * C + k], e[i * C + k], w);
-                               }),
+                               }, r0, r1),
                                sh);
-  if (threadIdx.x == 0) g.scores[c] = (double)g.sign * (double)(float)(tot / (double)g.s.N);
+  if (threadIdx.x == 0) g.partials[(size_t)c * g.S + blockIdx.y] = tot;
 }
 
 // Pick the best candidate (single block), stop if it does not improve the ensemble.
@@ -185,7 +223,9 @@ __global__ void __launch_bounds__(1024) greedy_select_kernel(GreedyArgs g) {
   int bx = 0x7FFFFFFF;
   for (int c = threadIdx.x; c < g.Cand; c += blockDim.x) {
     if (!g.with_replacement && g.counts[c] > 0) continue;
-    const double s = g.scores[c], is = g.ind_scores[c];
+    double tot = 0.0;
+    for (int k = 0; k < g.S; ++k) tot += g.partials[(size_t)c * g.S + k];
+    const double s = (double)g.sign * (double)(float)(tot / (double)g.s.N), is = g.ind_scores[c];
     if (s != s) {
       nan_seen = 1;
       continue;
@@ -294,11 +334,12 @@ __global__ void greedy_init_mean_kernel(GreedyArgs g, int k, const int* init_idx
   }
 }
 
-__global__ void __launch_bounds__(256) greedy_init_score_kernel(GreedyArgs g) {
+template <int MET>
+__global__ void __launch_bounds__(1024) greedy_init_score_kernel(GreedyArgs g) {
   __shared__ double sh[32];
   const float* e = g.ens;
   const int C = g.s.C;
-  const double tot = block_sum(metric_row_sum(g.s, [&](int64_t i, int k) { return e[i * C + k]; }), sh);
+  const double tot = block_sum(metric_row_sum<MET>(g.s, [&](int64_t i, int k) { return e[i * C + k]; }, 0, g.s.N), sh);
   if (threadIdx.x == 0) g.st->ens_score = (double)g.sign * (double)(float)(tot / (double)g.s.N);
 }
 

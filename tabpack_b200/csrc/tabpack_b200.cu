@@ -301,6 +301,21 @@ int ns_gemm(const MuonArgs& ma, int shape, const void* a_op, int a_cols, const v
 
 using namespace tp;
 
+// Calls f(std::integral_constant<int, metric>) for a runtime metric code (kernels are
+// specialised per metric).
+template <typename F>
+static void metric_dispatch(int metric, F f) {
+  switch (metric) {
+    case MET_MSE: f(std::integral_constant<int, MET_MSE>{}); break;
+    case MET_MAE: f(std::integral_constant<int, MET_MAE>{}); break;
+    case MET_ACCURACY: f(std::integral_constant<int, MET_ACCURACY>{}); break;
+    case MET_BCE: f(std::integral_constant<int, MET_BCE>{}); break;
+    case MET_CE: f(std::integral_constant<int, MET_CE>{}); break;
+    case MET_ACCURACY_ARGMAX: f(std::integral_constant<int, MET_ACCURACY_ARGMAX>{}); break;
+    default: f(std::integral_constant<int, MET_R2>{}); break;
+  }
+}
+
 extern "C" {
 
 const char* tp_version(void) { return "tabpack_b200 0.1.0 (sm_100a)"; }
@@ -582,15 +597,21 @@ int tp_metric_pack(const tp_metric_args* a, void* stream) {
   s.yf = float_labels ? static_cast<const float*>(a->y_true) : nullptr;
   s.yi = float_labels ? nullptr : static_cast<const int64_t*>(a->y_true);
   const bool int_pred = a->metric == TP_METRIC_ACCURACY;
-  metric_pack_kernel<<<a->P, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      s, int_pred ? nullptr : static_cast<const float*>(a->y_pred),
-      int_pred ? static_cast<const int64_t*>(a->y_pred) : nullptr, a->out);
+  metric_dispatch(a->metric, [&](auto tag) {
+    metric_pack_kernel<decltype(tag)::value><<<a->P, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
+        s, int_pred ? nullptr : static_cast<const float*>(a->y_pred),
+        int_pred ? static_cast<const int64_t*>(a->y_pred) : nullptr, a->out);
+  });
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;
 }
 
+constexpr int64_t GREEDY_SEG_ROWS = 16384;  // rows per block of the candidate scoring launch
+
+static int greedy_segments(int64_t N) { return (int)((N + GREEDY_SEG_ROWS - 1) / GREEDY_SEG_ROWS); }
+
 static size_t greedy_layout(int32_t n_pred, int64_t N, int32_t C, size_t* off_ens, size_t* off_sc, size_t* off_ind,
-                            size_t* off_st, size_t* off_init, size_t* off_metric) {
+                            size_t* off_st, size_t* off_init, size_t* off_metric, size_t* off_part) {
   auto up = [](size_t v) { return (v + 255) / 256 * 256; };
   size_t o = 0;
   *off_ens = o;
@@ -605,13 +626,15 @@ static size_t greedy_layout(int32_t n_pred, int64_t N, int32_t C, size_t* off_en
   o = up(o + (size_t)n_pred * 4);
   *off_metric = o;
   o = up(o + (size_t)n_pred * 4);
+  *off_part = o;
+  o = up(o + (size_t)n_pred * greedy_segments(N) * 8);
   return o;
 }
 
 size_t tp_greedy_workspace_size(int32_t n_pred, int64_t N, int32_t C) {
   if (n_pred <= 0 || N <= 0 || C <= 0) return 0;
-  size_t a, b, c, d, e, f;
-  return greedy_layout(n_pred, N, C, &a, &b, &c, &d, &e, &f);
+  size_t a, b, c, d, e, f, h;
+  return greedy_layout(n_pred, N, C, &a, &b, &c, &d, &e, &f, &h);
 }
 
 int tp_greedy_ensemble(const tp_greedy_args* a, void* stream) {
@@ -625,8 +648,8 @@ int tp_greedy_ensemble(const tp_greedy_args* a, void* stream) {
   if (a->max_ensemble_size > 0 && a->init_top_k > a->max_ensemble_size)
     return fail(TP_EINVAL, "`init_top_k` must not exceed `max_ensemble_size`");
   const int C = std::max(1, a->C);
-  size_t o_ens, o_sc, o_ind, o_st, o_init, o_met;
-  const size_t need = greedy_layout(a->n_pred, a->N, C, &o_ens, &o_sc, &o_ind, &o_st, &o_init, &o_met);
+  size_t o_ens, o_sc, o_ind, o_st, o_init, o_met, o_part;
+  const size_t need = greedy_layout(a->n_pred, a->N, C, &o_ens, &o_sc, &o_ind, &o_st, &o_init, &o_met, &o_part);
   if (a->workspace_bytes < need) return fail(TP_EINVAL, "greedy workspace holds %zu bytes, needs %zu", a->workspace_bytes, need);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(a->workspace);
@@ -647,6 +670,9 @@ int tp_greedy_ensemble(const tp_greedy_args* a, void* stream) {
   g.counts = a->counts;
   g.ens = reinterpret_cast<float*>(ws + o_ens);
   g.scores = reinterpret_cast<double*>(ws + o_sc);
+  g.S = greedy_segments(a->N);
+  g.seg = GREEDY_SEG_ROWS;
+  g.partials = reinterpret_cast<double*>(ws + o_part);
   g.ind_scores = reinterpret_cast<double*>(ws + o_ind);
   g.st = reinterpret_cast<GreedyState*>(ws + o_st);
   int* init_idx = reinterpret_cast<int*>(ws + o_init);
@@ -654,16 +680,20 @@ int tp_greedy_ensemble(const tp_greedy_args* a, void* stream) {
   const int k = std::min(a->init_top_k, a->n_pred);
   TP_CUDA_TRY(cudaMemsetAsync(a->counts, 0, (size_t)a->n_pred * 4, st));
   // individual scores
-  metric_pack_kernel<<<a->n_pred, 256, 0, st>>>(g.s, a->predictions, nullptr, metric);
+  metric_dispatch(g.s.metric, [&](auto tag) {
+    metric_pack_kernel<decltype(tag)::value><<<a->n_pred, 1024, 0, st>>>(g.s, a->predictions, nullptr, metric);
+  });
   greedy_sign_kernel<<<(a->n_pred + 255) / 256, 256, 0, st>>>(metric, g.ind_scores, a->n_pred, g.sign);
   greedy_init_select_kernel<<<1, 32, 0, st>>>(g, k, init_idx);
   const int64_t n = a->N * (int64_t)g.s.C;
   const int eb = (int)std::min<int64_t>((n + 255) / 256, 1184);
   greedy_init_mean_kernel<<<eb, 256, 0, st>>>(g, k, init_idx);
-  greedy_init_score_kernel<<<1, 256, 0, st>>>(g);
+  metric_dispatch(g.s.metric, [&](auto tag) { greedy_init_score_kernel<decltype(tag)::value><<<1, 1024, 0, st>>>(g); });
   TP_CUDA_TRY(cudaGetLastError());
   for (int it = k; it < g.limit; ++it) {
-    greedy_score_kernel<<<a->n_pred, 256, 0, st>>>(g);
+    metric_dispatch(g.s.metric, [&](auto tag) {
+      greedy_score_kernel<decltype(tag)::value><<<dim3(a->n_pred, g.S), 256, 0, st>>>(g);
+    });
     greedy_select_kernel<<<1, 1024, 0, st>>>(g);
     greedy_update_kernel<<<eb, 256, 0, st>>>(g);
     greedy_advance_kernel<<<1, 1, 0, st>>>(g);
