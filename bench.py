@@ -385,12 +385,13 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
-# DRAM bytes (read + write) per full-size launch, from the ncu capture summarised in
+# DRAM bytes (read + write) per full-size launch, from the ncu captures summarised in
 # profiles/linear_block_fwd_bwd_256x4096x512.md (32-member case scaled by 256/32).
 TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
-    'fwd': (26.017536e6 + 214.157312e6) * 8,
-    'dgrad': (172.590080e6 + 91.861504e6) * 8,
-    'wgrad': (159.238912e6 + 36.017920e6) * 8,
+    'fwd': (25.804544e6 + 211.742720e6) * 8,
+    'act': (293.636608e6 + 98.083072e6) * 8,
+    'dgrad': (173.277184e6 + 100.588032e6) * 8,
+    'wgrad': (179.476736e6 + 45.408256e6) * 8,
 }
 
 
