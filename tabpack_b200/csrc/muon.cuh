@@ -69,19 +69,30 @@ __global__ void __launch_bounds__(256) muon_prologue_kernel(MuonArgs a) {
   const float mult = (a.lr_pm || a.wd_pm) ? 1.0f - lr * (a.wd_pm ? a.wd_pm[mem] : a.wd_s) : a.wd_mult_s;
   const float one_m_mu = a.mu_pm ? 1.0f - mu : a.one_m_mu_s;
   float ss = 0.0f;
-  for (int i = ty; i < 32; i += 8) {
-    const int o = o0 + i, n = n0 + tx;
+  // rows ty, ty + 8, ty + 16, ty + 24: all loads issued before any use
+  float pv[4], gv[4], mv[4];
+  bool ok[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int o = o0 + ty + 8 * k, n = n0 + tx;
+    ok[k] = o < out_m && n < in_m;
+    const size_t idx = ((size_t)mem * a.max_out + o) * a.max_in + n;
+    pv[k] = ok[k] ? a.p[idx] : 0.0f;
+    gv[k] = ok[k] ? a.g[idx] : 0.0f;
+    mv[k] = ok[k] ? a.m[idx] : 0.0f;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = ty + 8 * k;
     float u = 0.0f;
-    if (o < out_m && n < in_m) {
-      const size_t idx = ((size_t)mem * a.max_out + o) * a.max_in + n;
-      float pv = a.p[idx];
-      const float gv = a.g[idx];
-      float mv = a.m[idx];
-      if (a.wd_on) pv *= mult;
-      mv = lerp_t(mv, gv, one_m_mu);
-      u = a.nesterov ? lerp_t(gv, mv, mu) : mv;
-      a.p[idx] = pv;
-      a.m[idx] = mv;
+    if (ok[k]) {
+      const size_t idx = ((size_t)mem * a.max_out + (o0 + i)) * a.max_in + (n0 + tx);
+      float p = pv[k];
+      if (a.wd_on) p *= mult;
+      const float m = lerp_t(mv[k], gv[k], one_m_mu);
+      u = a.nesterov ? lerp_t(gv[k], m, mu) : m;
+      a.p[idx] = p;
+      a.m[idx] = m;
       if (a.nesterov && a.mutate_grad) a.g[idx] = u;
       u = __bfloat162float(__float2bfloat16_rn(u));
       ss += u * u;
@@ -176,7 +187,16 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(MuonArgs a) {
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const bool tr = out_m > in_m;
   const __nv_bfloat16* x = a.x + (size_t)mem * a.R_s * a.C_s;
-  for (int i = ty; i < 32; i += 8) {
+  // the four rows' weights are loaded together with the update tile
+  float pv[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int o = o0 + ty + 8 * k, n = n0 + tx;
+    pv[k] = (o < out_m && n < in_m) ? a.p[((size_t)mem * a.max_out + o) * a.max_in + n] : 0.0f;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = ty + 8 * k;
     if (!tr) {
       const int o = o0 + i, n = n0 + tx;
       tile[i][tx] = (o < out_m && n < in_m) ? __bfloat162float(x[(size_t)o * a.C_s + n]) : 0.0f;
@@ -189,12 +209,11 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(MuonArgs a) {
   const float lr = a.lr_pm ? a.lr_pm[mem] : a.lr_s;
   const float sc = a.scale_pm ? a.scale_pm[mem] : a.scale_s;
   const float slr = lr * sc;
-  for (int i = ty; i < 32; i += 8) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int i = ty + 8 * k;
     const int o = o0 + i, n = n0 + tx;
-    if (o < out_m && n < in_m) {
-      const size_t idx = ((size_t)mem * a.max_out + o) * a.max_in + n;
-      a.p[idx] = a.p[idx] - tile[i][tx] * slr;
-    }
+    if (o < out_m && n < in_m) a.p[((size_t)mem * a.max_out + o) * a.max_in + n] = pv[k] - tile[i][tx] * slr;
   }
 }
 
