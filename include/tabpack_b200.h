@@ -262,6 +262,40 @@ size_t tp_roc_auc_workspace_size(int32_t P, int64_t N, int32_t dtype);
 int tp_binary_roc_auc(const void* scores, const int64_t* labels, int32_t P, int64_t N, int32_t dtype, void* out,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* Cosine numerical-feature embeddings: CosineEmbeddingsPack (src/tabpackage/nn.py:1627-1833,
+ * forward nn.py:1783-1833) with concat_input.  Member m, feature f, slot k < D (D =
+ * max_d_embedding): slot 0 is the raw value, slot k >= 1 is cos(2pi b[k-1] + 2pi w[k-1] x), then the
+ * elementwise affine ab_k + aw_k * slot_k with aw, ab zero at k >= d_embedding[m].  The output
+ * is written at column f * D + k of each row of `out` (leading dimension out_ld >= F * D), i.e.
+ * the flattened embedding the first linear layer consumes.  Backward gives the parameter
+ * gradients from the upstream gradient of that output (sums over the batch in fp64, fixed order;
+ * the input x takes no gradient).  x: (P, B, F) fp32, or (B, F) when x_shared. */
+typedef struct tp_cos_emb_args {
+  int32_t P, B, F, D;
+  int32_t x_shared;
+  const float* x;
+  const float* weight;           /* (P, F, D - 1) */
+  const float* bias;             /* (P, F, D - 1) */
+  const float* affine_weight;    /* (P, F, D) */
+  const float* affine_bias;      /* (P, F, D) */
+  const int32_t* d_embedding;    /* (P,) or NULL: every slot active */
+  void* out;                     /* forward: (P, B, out_ld) */
+  int32_t out_ld;
+  int32_t out_dtype;             /* TP_DTYPE_F32 or TP_DTYPE_BF16 */
+  const void* grad_out;          /* backward: (P, B, grad_ld) */
+  int32_t grad_ld;
+  int32_t grad_dtype;            /* TP_DTYPE_F32 or TP_DTYPE_BF16 */
+  float* dweight;                /* (P, F, D - 1) */
+  float* dbias;                  /* (P, F, D - 1) */
+  float* daffine_weight;         /* (P, F, D) */
+  float* daffine_bias;           /* (P, F, D) */
+  void* workspace;               /* backward: >= tp_cos_emb_workspace_size(P, B, F, D) bytes */
+  size_t workspace_bytes;
+} tp_cos_emb_args;
+size_t tp_cos_emb_workspace_size(int32_t P, int32_t B, int32_t F, int32_t D);
+int tp_cos_emb_forward(const tp_cos_emb_args* a, void* stream);
+int tp_cos_emb_backward(const tp_cos_emb_args* a, void* stream);
+
 /* Clears and returns the device-side error flag (TP_OK or TP_ETIMEOUT). */
 int tp_device_error(void);
 

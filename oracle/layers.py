@@ -138,3 +138,40 @@ def one_hot_encode(x_cat: np.ndarray, cardinalities, dtype) -> np.ndarray:
         oh = (v[..., None] == np.arange(card)[None]).astype(dtype)
         parts.append(oh)
     return np.concatenate(parts, axis=-1)
+
+
+def cosine_embeddings_forward(x, weight, bias, aw, ab, d_embedding=None):
+    """`CosineEmbeddingsPack.forward` (`nn.py:1783-1833`), concat_input=True.
+
+    x (P, B, F); weight, bias (P, F, D-1); aw, ab (P, F, D) (the elementwise affine);
+    d_embedding (P,) or None.  out[..., 0] = ab0 + aw0 x, out[..., k] = ab_k + aw_k
+    cos(2 pi b_{k-1} + 2 pi w_{k-1} x), with aw, ab zero at k >= d_embedding.  The
+    factor 2 pi multiplies the parameters in their own dtype (`weight * (2 * torch.pi)`).
+    Returns (y (P, B, F, D), cache).
+    """
+    dt = x.dtype
+    D = aw.shape[-1]
+    mask = None
+    if d_embedding is not None:
+        mask = (np.arange(D)[None] < np.asarray(d_embedding)[:, None]).astype(dt)[:, None, :]
+        aw, ab = aw * mask, ab * mask
+    two_pi = dt.type(2 * np.pi)
+    w2, b2 = weight * two_pi, bias * two_pi
+    z = b2[:, None] + w2[:, None] * x[..., None]
+    cat = np.concatenate([x[..., None], np.cos(z)], -1)
+    y = ab[:, None] + aw[:, None] * cat
+    return y, (x, z, cat, aw, mask)
+
+
+def cosine_embeddings_backward(cache, dy):
+    """Autograd of `cosine_embeddings_forward` w.r.t. (weight, bias, aw, ab)."""
+    x, z, cat, aw_m, mask = cache
+    two_pi = x.dtype.type(2 * np.pi)
+    dab = dy.sum(1)
+    daw = (dy * cat).sum(1)
+    if mask is not None:
+        dab, daw = dab * mask, daw * mask
+    dz = (dy * aw_m[:, None])[..., 1:] * -np.sin(z)
+    dweight = (dz * x[..., None]).sum(1) * two_pi
+    dbias = dz.sum(1) * two_pi
+    return dweight, dbias, daw, dab

@@ -82,6 +82,18 @@ class MetricArgs(ctypes.Structure):
     ]
 
 
+class CosEmbArgs(ctypes.Structure):
+    _fields_ = [
+        ('P', ctypes.c_int32), ('B', ctypes.c_int32), ('F', ctypes.c_int32), ('D', ctypes.c_int32),
+        ('x_shared', ctypes.c_int32), ('x', ctypes.c_void_p), ('weight', ctypes.c_void_p), ('bias', ctypes.c_void_p),
+        ('affine_weight', ctypes.c_void_p), ('affine_bias', ctypes.c_void_p), ('d_embedding', ctypes.c_void_p),
+        ('out', ctypes.c_void_p), ('out_ld', ctypes.c_int32), ('out_dtype', ctypes.c_int32),
+        ('grad_out', ctypes.c_void_p), ('grad_ld', ctypes.c_int32), ('grad_dtype', ctypes.c_int32),
+        ('dweight', ctypes.c_void_p), ('dbias', ctypes.c_void_p), ('daffine_weight', ctypes.c_void_p),
+        ('daffine_bias', ctypes.c_void_p), ('workspace', ctypes.c_void_p), ('workspace_bytes', ctypes.c_size_t),
+    ]
+
+
 class GreedyArgs(ctypes.Structure):
     _fields_ = [
         ('metric', ctypes.c_int32), ('maximize', ctypes.c_int32), ('n_pred', ctypes.c_int32),
@@ -115,6 +127,9 @@ SIGNATURES = {
                                        ctypes.c_void_p]),
     'tp_permutation_keys': (ctypes.c_int, [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int32,
                                            ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
+    'tp_cos_emb_workspace_size': (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
+    'tp_cos_emb_forward': (ctypes.c_int, [ctypes.POINTER(CosEmbArgs), ctypes.c_void_p]),
+    'tp_cos_emb_backward': (ctypes.c_int, [ctypes.POINTER(CosEmbArgs), ctypes.c_void_p]),
     'tp_roc_auc_workspace_size': (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32]),
     'tp_binary_roc_auc': (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
                                          ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,

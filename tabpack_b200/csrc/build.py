@@ -18,7 +18,7 @@ PKG = os.path.dirname(HERE)
 ROOT = os.path.dirname(PKG)
 LIB = os.path.join(PKG, 'libtabpack_b200.so')
 SOURCES = ['tabpack_b200.cu']
-HEADERS = ['common.cuh', 'linear_problem.cuh', 'gemm_sm100.cuh', 'gemm_simt.cuh', 'elementwise.cuh', 'muon.cuh', 'metrics.cuh', 'roc_auc.cuh']
+HEADERS = ['common.cuh', 'linear_problem.cuh', 'gemm_sm100.cuh', 'gemm_simt.cuh', 'elementwise.cuh', 'muon.cuh', 'metrics.cuh', 'roc_auc.cuh', 'embeddings.cuh']
 
 
 def nvcc_path() -> str:

@@ -1,0 +1,165 @@
+// Cosine numerical-feature embeddings (CosineEmbeddingsPack, src/tabpackage/nn.py:1627-1833,
+// concat_input = True), forward and parameter gradients.
+//
+// Member m, feature f, embedding slot k < D (D = max_d_embedding):
+//   cat_0 = x,  cat_k = cos(z_k),  z_k = 2pi*b[k-1] + 2pi*w[k-1] * x   (2pi*w, 2pi*b in fp32)
+//   out_k = ab'_k + aw'_k * cat_k,  aw' / ab' = aw / ab where k < d_embedding[m], else 0
+// written at column f * D + k of the member's output row, so the flattened embedding lands
+// directly in the first layer's input (the one-hot block can follow in the same buffer).
+//
+// Backward, per (m, f, k), sums over the batch rows in fp64:
+//   dab_k = [k < d] sum g,  daw_k = [k < d] sum g cat_k,
+//   dz_k = g aw'_k (-sin z_k),  dw[k-1] = 2pi sum dz_k x,  db[k-1] = 2pi sum dz_k.
+// Threads own one column (f, k) each and walk the rows, so parameter loads happen once per
+// thread and the loads / stores of a warp are contiguous along the columns.
+#pragma once
+
+#include "common.cuh"
+
+namespace tp {
+
+constexpr float COS_EMB_TWO_PI = 6.28318530717958647692f;
+constexpr int COS_EMB_THREADS = 128;
+
+struct CosEmbArgs {
+  int P, B, F, D;
+  int x_shared;            // x is (B, F) for every member, else (P, B, F)
+  const float* x;
+  const float* w;          // (P, F, D - 1)
+  const float* b;          // (P, F, D - 1)
+  const float* aw;         // (P, F, D)
+  const float* ab;         // (P, F, D)
+  const int32_t* d_emb;    // (P,) or nullptr (every slot active)
+  void* out;               // (P, B, out_ld), fp32 or bf16
+  int out_ld, out_bf16;
+  const void* g;           // (P, B, g_ld) upstream gradient, fp32 or bf16
+  int g_ld, g_bf16;
+  int rows_per_block;      // rows of one block (the grid's z dimension covers B)
+  double* partial;         // (4, gridDim.z, P, F * D) or nullptr when gridDim.z == 1
+  float* dw;               // (P, F, D - 1)
+  float* db;
+  float* daw;              // (P, F, D)
+  float* dab;
+};
+
+struct CosEmbCol {
+  int f, k;
+  bool valid;
+  float aw, ab, w2, b2;
+};
+
+__device__ __forceinline__ CosEmbCol cos_emb_col(const CosEmbArgs& a, int m, int j) {
+  CosEmbCol c;
+  c.valid = j < a.F * a.D;
+  c.f = c.valid ? j / a.D : 0;
+  c.k = c.valid ? j - c.f * a.D : 0;
+  const bool on = c.valid && (a.d_emb == nullptr || c.k < a.d_emb[m]);
+  const size_t pa = ((size_t)m * a.F + c.f) * a.D + c.k;
+  c.aw = on ? a.aw[pa] : 0.0f;
+  c.ab = on ? a.ab[pa] : 0.0f;
+  c.w2 = c.b2 = 0.0f;
+  if (c.valid && c.k > 0) {
+    const size_t pw = ((size_t)m * a.F + c.f) * (a.D - 1) + (c.k - 1);
+    c.w2 = a.w[pw] * COS_EMB_TWO_PI;
+    c.b2 = a.b[pw] * COS_EMB_TWO_PI;
+  }
+  return c;
+}
+
+__device__ __forceinline__ float cos_emb_x(const CosEmbArgs& a, int m, int r, int f) {
+  return a.x[(a.x_shared ? (size_t)r : ((size_t)m * a.B + r)) * a.F + f];
+}
+
+// Grid: (ceil(F * D / COS_EMB_THREADS), P, ceil(B / rows_per_block)).
+__global__ void __launch_bounds__(COS_EMB_THREADS) cos_emb_forward_kernel(const CosEmbArgs a) {
+  const int m = blockIdx.y;
+  const int j = blockIdx.x * COS_EMB_THREADS + threadIdx.x;
+  const CosEmbCol c = cos_emb_col(a, m, j);
+  if (!c.valid) return;
+  const int r0 = blockIdx.z * a.rows_per_block, r1 = min(a.B, r0 + a.rows_per_block);
+  for (int r = r0; r < r1; ++r) {
+    const float x = cos_emb_x(a, m, r, c.f);
+    const float cat = c.k == 0 ? x : cosf(c.b2 + c.w2 * x);
+    const float v = c.ab + c.aw * cat;
+    const size_t o = ((size_t)m * a.B + r) * a.out_ld + j;
+    if (a.out_bf16)
+      reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(v);
+    else
+      reinterpret_cast<float*>(a.out)[o] = v;
+  }
+}
+
+// Grid as the forward.  One block row segment per z; with gridDim.z == 1 the sums are final,
+// otherwise they go to `partial` and cos_emb_finish_kernel adds the segments in order.
+__global__ void __launch_bounds__(COS_EMB_THREADS) cos_emb_backward_kernel(const CosEmbArgs a) {
+  const int m = blockIdx.y;
+  const int j = blockIdx.x * COS_EMB_THREADS + threadIdx.x;
+  const CosEmbCol c = cos_emb_col(a, m, j);
+  if (!c.valid) return;
+  const int r0 = blockIdx.z * a.rows_per_block, r1 = min(a.B, r0 + a.rows_per_block);
+  double s_ab = 0.0, s_aw = 0.0, s_w = 0.0, s_b = 0.0;
+  for (int r = r0; r < r1; ++r) {
+    const size_t gi = ((size_t)m * a.B + r) * a.g_ld + j;
+    const float g = a.g_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.g)[gi])
+                             : reinterpret_cast<const float*>(a.g)[gi];
+    const float x = cos_emb_x(a, m, r, c.f);
+    s_ab += (double)g;
+    if (c.k == 0) {
+      s_aw += (double)g * (double)x;
+    } else {
+      float sn, cs;
+      sincosf(c.b2 + c.w2 * x, &sn, &cs);
+      s_aw += (double)g * (double)cs;
+      const double dz = -(double)g * (double)c.aw * (double)sn;
+      s_w += dz * (double)x;
+      s_b += dz;
+    }
+  }
+  const size_t FD = (size_t)a.F * a.D;
+  if (gridDim.z > 1) {
+    const size_t slot = ((size_t)blockIdx.z * a.P + m) * FD + j;
+    const size_t plane = (size_t)gridDim.z * a.P * FD;
+    a.partial[slot] = s_ab;
+    a.partial[plane + slot] = s_aw;
+    a.partial[2 * plane + slot] = s_w;
+    a.partial[3 * plane + slot] = s_b;
+    return;
+  }
+  const bool on = a.d_emb == nullptr || c.k < a.d_emb[m];
+  const size_t pa = ((size_t)m * a.F + c.f) * a.D + c.k;
+  a.dab[pa] = on ? (float)s_ab : 0.0f;
+  a.daw[pa] = on ? (float)s_aw : 0.0f;
+  if (c.k > 0) {
+    const size_t pw = ((size_t)m * a.F + c.f) * (a.D - 1) + (c.k - 1);
+    a.dw[pw] = (float)s_w * COS_EMB_TWO_PI;
+    a.db[pw] = (float)s_b * COS_EMB_TWO_PI;
+  }
+}
+
+// Adds the row segments' partial sums in segment order (deterministic).  Grid:
+// (ceil(F * D / COS_EMB_THREADS), P).
+__global__ void __launch_bounds__(COS_EMB_THREADS) cos_emb_finish_kernel(const CosEmbArgs a, int segments) {
+  const int m = blockIdx.y;
+  const int j = blockIdx.x * COS_EMB_THREADS + threadIdx.x;
+  const size_t FD = (size_t)a.F * a.D;
+  if (j >= (int)FD) return;
+  const size_t plane = (size_t)segments * a.P * FD;
+  double s[4] = {0.0, 0.0, 0.0, 0.0};
+  for (int z = 0; z < segments; ++z) {
+    const size_t slot = ((size_t)z * a.P + m) * FD + j;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) s[q] += a.partial[q * plane + slot];
+  }
+  const int f = j / a.D, k = j - f * a.D;
+  const bool on = a.d_emb == nullptr || k < a.d_emb[m];
+  const size_t pa = ((size_t)m * a.F + f) * a.D + k;
+  a.dab[pa] = on ? (float)s[0] : 0.0f;
+  a.daw[pa] = on ? (float)s[1] : 0.0f;
+  if (k > 0) {
+    const size_t pw = ((size_t)m * a.F + f) * (a.D - 1) + (k - 1);
+    a.dw[pw] = (float)s[2] * COS_EMB_TWO_PI;
+    a.db[pw] = (float)s[3] * COS_EMB_TWO_PI;
+  }
+}
+
+}  // namespace tp

@@ -18,6 +18,7 @@
 #include "muon.cuh"
 #include "metrics.cuh"
 #include "roc_auc.cuh"
+#include "embeddings.cuh"
 
 namespace tp {
 namespace {
@@ -721,6 +722,96 @@ int tp_softmax_rows(const float* x, int64_t rows, int32_t C, float* out, void* s
   const int blocks = (int)std::min<int64_t>((threads + 255) / 256, 1 << 20);
   if ((int64_t)blocks * 256 < threads) return fail(TP_EINVAL, "too many rows for one softmax call");
   softmax_rows_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, rows, C, out);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+// Row segments of the embedding backward: enough blocks for two waves of 148 SMs, at least
+// 64 rows per segment.
+static int cos_emb_segments(int P, int B, int F, int D) {
+  const long long cols = ((long long)F * D + COS_EMB_THREADS - 1) / COS_EMB_THREADS;
+  const long long base = cols * P;
+  long long s = (296 + base - 1) / base;
+  s = std::min<long long>(s, (B + 63) / 64);
+  return (int)std::max<long long>(1, s);
+}
+
+static int check_cos_emb(const tp_cos_emb_args* a) {
+  if (!a) return fail(TP_EINVAL, "null embedding arguments");
+  if (a->P <= 0 || a->B <= 0 || a->F <= 0 || a->D <= 0)
+    return fail(TP_EINVAL, "embedding needs P, B, F, D > 0 (got %d, %d, %d, %d)", a->P, a->B, a->F, a->D);
+  if (!a->x || !a->affine_weight || !a->affine_bias || (a->D > 1 && (!a->weight || !a->bias)))
+    return fail(TP_EINVAL, "null embedding parameter");
+  return TP_OK;
+}
+
+static CosEmbArgs cos_emb_args(const tp_cos_emb_args* a) {
+  CosEmbArgs k{};
+  k.P = a->P;
+  k.B = a->B;
+  k.F = a->F;
+  k.D = a->D;
+  k.x_shared = a->x_shared;
+  k.x = a->x;
+  k.w = a->weight;
+  k.b = a->bias;
+  k.aw = a->affine_weight;
+  k.ab = a->affine_bias;
+  k.d_emb = a->d_embedding;
+  k.out = a->out;
+  k.out_ld = a->out_ld;
+  k.out_bf16 = a->out_dtype == TP_DTYPE_BF16;
+  k.g = a->grad_out;
+  k.g_ld = a->grad_ld;
+  k.g_bf16 = a->grad_dtype == TP_DTYPE_BF16;
+  k.dw = a->dweight;
+  k.db = a->dbias;
+  k.daw = a->daffine_weight;
+  k.dab = a->daffine_bias;
+  return k;
+}
+
+size_t tp_cos_emb_workspace_size(int32_t P, int32_t B, int32_t F, int32_t D) {
+  if (P <= 0 || B <= 0 || F <= 0 || D <= 0) return 0;
+  const int s = cos_emb_segments(P, B, F, D);
+  return s > 1 ? (size_t)4 * s * P * (size_t)F * D * sizeof(double) : 0;
+}
+
+int tp_cos_emb_forward(const tp_cos_emb_args* a, void* stream) {
+  int rc = check_cos_emb(a);
+  if (rc) return rc;
+  if (!a->out || a->out_ld < a->F * a->D) return fail(TP_EINVAL, "embedding output needs out_ld >= F * D");
+  if (a->out_dtype != TP_DTYPE_F32 && a->out_dtype != TP_DTYPE_BF16) return fail(TP_EINVAL, "bad output dtype");
+  CosEmbArgs k = cos_emb_args(a);
+  k.rows_per_block = 64;
+  const dim3 grid((a->F * a->D + COS_EMB_THREADS - 1) / COS_EMB_THREADS, a->P, (a->B + 63) / 64);
+  if (grid.z > 65535) return fail(TP_EINVAL, "batch too large for one embedding call");
+  cos_emb_forward_kernel<<<grid, COS_EMB_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(k);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+int tp_cos_emb_backward(const tp_cos_emb_args* a, void* stream) {
+  int rc = check_cos_emb(a);
+  if (rc) return rc;
+  if (!a->grad_out || a->grad_ld < a->F * a->D) return fail(TP_EINVAL, "embedding gradient needs grad_ld >= F * D");
+  if (a->grad_dtype != TP_DTYPE_F32 && a->grad_dtype != TP_DTYPE_BF16) return fail(TP_EINVAL, "bad gradient dtype");
+  if (!a->dweight || !a->dbias || !a->daffine_weight || !a->daffine_bias)
+    return fail(TP_EINVAL, "null embedding gradient output");
+  CosEmbArgs k = cos_emb_args(a);
+  const int s = cos_emb_segments(a->P, a->B, a->F, a->D);
+  k.rows_per_block = (a->B + s - 1) / s;
+  const size_t need = tp_cos_emb_workspace_size(a->P, a->B, a->F, a->D);
+  if (need > 0) {
+    if (!a->workspace || a->workspace_bytes < need)
+      return fail(TP_EINVAL, "embedding backward workspace of %zu bytes is smaller than the %zu needed",
+                  a->workspace_bytes, need);
+    k.partial = static_cast<double*>(a->workspace);
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned cols = (a->F * a->D + COS_EMB_THREADS - 1) / COS_EMB_THREADS;
+  cos_emb_backward_kernel<<<dim3(cols, a->P, s), COS_EMB_THREADS, 0, st>>>(k);
+  if (s > 1) cos_emb_finish_kernel<<<dim3(cols, a->P), COS_EMB_THREADS, 0, st>>>(k, s);
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;
 }

@@ -340,8 +340,8 @@ class _PackedLinearFn(torch.autograd.Function):
         if dx is not None:
             if len(ctx.x_shape) == 2:
                 dx = dx.sum(PACK_DIM)
-            if dx.shape[-1] != cfg['in_cols']:
-                dx = dx[..., : cfg['in_cols']]
+            if dx.shape[-1] != ctx.x_shape[-1]:  # the gradient of this function's (padded) input
+                dx = dx[..., : ctx.x_shape[-1]]
         return dx, dw, db, None, None
 
 
@@ -475,6 +475,8 @@ def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stre
     if dropout is not None and stream is not None:
         seed = stream.seed
         offset = stream.next_offset(offset_stride) + offset_add
+    if getattr(linear, 'full_width_input', False):
+        inf = None  # the whole padded input width takes part (first layer of a TabPack with embeddings)
     return packed_linear(x, w, b, in_features=_widths(inf), out_features=_widths(outf), n_blocks=n_blocks,
                          block_index=block_index, relu=relu, dropout_p=dropout, seed=seed, offset=offset,
                          member_base=member_base, cache=linear._cache if pack_idx is None else None)
@@ -694,6 +696,134 @@ class _OffsetView:
         return self._base
 
 
+class _CosineEmbeddingFn(torch.autograd.Function):
+    """One launch forward (`tp_cos_emb_forward`), one (or two) backward: parameter gradients
+    from the gradient of the flattened embedding; the input takes no gradient."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, affine_weight, affine_bias, d_embedding):
+        y = ops.cos_emb_forward(x, weight, bias, affine_weight, affine_bias, d_embedding)
+        ctx.save_for_backward(x, weight, bias, affine_weight, affine_bias)
+        ctx.d_embedding = d_embedding
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, w, b, aw, ab = ctx.saved_tensors
+        dw, db, daw, dab = ops.cos_emb_backward(x, w, b, aw, ab, ctx.d_embedding, gy)
+        return None, dw, db, daw, dab, None
+
+
+class CosineEmbeddingsPack(ModulePack):
+    """`CosineEmbeddingsPack` (`nn.py:1627-1833`): per feature the raw value and
+    `cos(2 pi (w x + b))`, then an elementwise affine masked to each member's
+    `d_embedding`, computed by `tp_cos_emb_forward` / `tp_cos_emb_backward`.
+
+    Input `(pack_size, batch, n_features)` (or a shared `(batch, n_features)`), output
+    `(pack_size, batch, n_features, max_d_embedding)`.
+    """
+
+    def __init__(self, n_features: int, d_embedding: int | list[int], *, max_d_embedding: int | None = None,
+                 init_scale: float | list[float], pack_size: int) -> None:
+        d_buf, max_d = _positive_int_pack(d_embedding, max_d_embedding, pack_size=pack_size)
+        super().__init__()
+        self.weight = ParameterPack(torch.empty(pack_size, n_features, max_d - 1))
+        self.bias = ParameterPack(torch.empty(self.weight.shape))
+        self.elementwise_affine_weight = ParameterPack(torch.empty(pack_size, n_features, max_d))
+        self.elementwise_affine_bias = ParameterPack(torch.empty(self.elementwise_affine_weight.shape))
+        self.register_buffer('d_embedding', d_buf)
+        if isinstance(init_scale, (int, float)):
+            self.init_scale = float(init_scale)
+        else:
+            self.register_buffer('init_scale', _mark_buffer(torch.tensor([float(v) for v in init_scale])))
+        self._concat_input = True
+        self.reset_parameters()
+
+    @property
+    def pack_size(self) -> int:
+        return self.weight.shape[PACK_DIM]
+
+    @property
+    def max_d_embedding(self) -> int:
+        return self.weight.shape[-1] + 1
+
+    def get_output_shape(self) -> torch.Size:
+        return torch.Size((self.weight.shape[1], self.weight.shape[2] + 1))
+
+    def reset_parameters(self, *, pack_idx: Tensor | None = None) -> None:
+        """Truncated N(0, 1) on [-3, 3] times the init scale for `weight`, zeros for the rest
+        (`nn.py:1706-1753`)."""
+        if pack_idx is not None:
+            check_pack_idx(pack_idx, self.pack_size)
+        n = self.pack_size if pack_idx is None else len(pack_idx)
+        w = torch.empty(n, *self.weight.shape[1:], dtype=self.weight.dtype, device=self.weight.device)
+        nn.init.trunc_normal_(w, a=-3.0, b=3.0)
+        with torch.no_grad():
+            if isinstance(self.init_scale, float):
+                w *= self.init_scale
+            else:
+                w *= _select(self.init_scale, pack_idx).to(w)[:, None, None]
+            if pack_idx is None:
+                self.weight.copy_(w)
+            else:
+                self.weight[pack_idx] = w
+            for p in (self.bias, self.elementwise_affine_weight, self.elementwise_affine_bias):
+                if pack_idx is None:
+                    p.zero_()
+                else:
+                    p[pack_idx] = 0.0
+
+    def replace(self, *, pack_idx: Tensor, d_embedding: list[int] | None = None,
+                init_scale: list[float] | None = None) -> None:
+        """`CosineEmbeddingsPack.replace` (`nn.py:1755-1781`)."""
+        check_pack_idx(pack_idx, self.pack_size)
+        updates = []
+        for vals in (d_embedding, init_scale):
+            if vals is not None and len(vals) != len(pack_idx):
+                raise ValueError('Each provided hyperparameter list must contain one value for each selected pack member')
+        if d_embedding is not None:
+            if self.d_embedding is None:
+                raise RuntimeError('Cannot replace embedding sizes that are shared by all pack members')
+            if not all(0 < v <= self.max_d_embedding for v in d_embedding):
+                raise ValueError('Embedding sizes must be positive and must not exceed `max_d_embedding`')
+            updates.append((self.d_embedding, d_embedding))
+        if init_scale is not None:
+            if isinstance(self.init_scale, float):
+                raise RuntimeError('Cannot replace initialization scales that are shared by all pack members')
+            updates.append((self.init_scale, init_scale))
+        for buf, vals in updates:
+            buf[pack_idx] = torch.tensor(vals, dtype=buf.dtype, device=buf.device)
+        self.reset_parameters(pack_idx=pack_idx)
+
+    def _flat(self, x: Tensor, pack_idx: Tensor | None) -> Tensor:
+        """(P, B, n_features * max_d_embedding) embedding, the layout the first layer reads."""
+        if x.ndim not in (2, 3):
+            raise ValueError('The input must have three dimensions')
+        if x.shape[-1] != self.weight.shape[-2]:
+            raise ValueError('The number of input features must match the number of features configured for the '
+                             'embeddings')
+        if not x.is_cuda:
+            raise RuntimeError('tabpack_b200 packs run on CUDA devices only')
+        prm = [self.weight, self.bias, self.elementwise_affine_weight, self.elementwise_affine_bias]
+        d = self.d_embedding
+        if pack_idx is not None:
+            check_pack_idx(pack_idx, self.pack_size)
+            prm = [p[pack_idx] for p in prm]
+            d = _select(d, pack_idx)
+        if x.ndim == 3 and x.stride(0) == 0:
+            x = x[0]
+        xf = x.float().contiguous()
+        d32 = None if d is None else d.to(torch.int32)
+        with torch.autocast(x.device.type, enabled=False):
+            return _CosineEmbeddingFn.apply(xf, *[p.contiguous() for p in prm], d32)
+
+    def forward(self, x: Tensor, pack_idx: Tensor | None = None) -> Tensor:
+        if x.ndim != 3:
+            raise ValueError('The input must have three dimensions')
+        y = self._flat(x, pack_idx)
+        return y.view(y.shape[0], y.shape[1], *self.get_output_shape())
+
+
 class _OneHotEncoding(nn.Module):
     """`_OneHotEncoding` (`nn.py:1836-1871`); the value `card` encodes as zeros."""
 
@@ -708,21 +838,52 @@ class _OneHotEncoding(nn.Module):
                           for i, c in enumerate(self._cardinalities)], -1)
 
 
+def _embedding_class(kind):
+    """The embedding class of `numerical_embeddings['type']`: this package's class, or the
+    reference's class of the same name (configurations written for the reference work)."""
+    name = kind if isinstance(kind, str) else getattr(kind, '__name__', '')
+    if name == 'CosineEmbeddingsPack':
+        return CosineEmbeddingsPack
+    raise NotImplementedError(f'numerical embeddings of type {name!r} are not implemented on the B200 path '
+                              '(CosineEmbeddingsPack is)')
+
+
 class TabPack(ModulePack):
-    """`TabPack` (`nn.py:1883-2110`) without numerical embeddings."""
+    """`TabPack` (`nn.py:1883-2110`); numerical embeddings: `CosineEmbeddingsPack`."""
 
     def __init__(self, *, n_numerical_features: int, categorical_cardinalities: list[int], d_out: int,
                  n_blocks, d_block, dropout, pack_size: int, numerical_embeddings: KWArgs | None = None,
                  **backbone_kwargs) -> None:
         super().__init__()
-        if numerical_embeddings is not None:
-            raise NotImplementedError('numerical embeddings are not part of the B200 hot path yet')
-        self.num_module = None
+        max_d_in = None
+        if numerical_embeddings is None:
+            self.num_module = None
+            d_in_num = n_numerical_features
+        else:
+            kw = dict(numerical_embeddings)
+            cls = _embedding_class(kw.pop('type'))
+            self.num_module = cls(n_numerical_features, pack_size=pack_size, **kw)
+            d_emb = numerical_embeddings['d_embedding']
+            if isinstance(d_emb, int):
+                d_in_num = d_emb * n_numerical_features
+            else:
+                if not isinstance(d_emb, list):
+                    raise TypeError('The `d_embedding` setting in `numerical_embeddings` must be an integer or a list')
+                max_d_emb = numerical_embeddings.get('max_d_embedding') or max(d_emb)
+                d_in_num = [v * n_numerical_features for v in d_emb]
+                max_d_in = max_d_emb * n_numerical_features
         self.cat_module = _OneHotEncoding(categorical_cardinalities) if categorical_cardinalities else None
-        d_in = n_numerical_features + sum(categorical_cardinalities)
+        d_in_cat = sum(categorical_cardinalities)
+        d_in = d_in_num + d_in_cat if isinstance(d_in_num, int) else [v + d_in_cat for v in d_in_num]
         self.pack_view = PackView(pack_size=pack_size)
-        self.backbone = MLPBackbonePack(d_in=d_in, n_blocks=n_blocks, d_block=d_block, dropout=dropout,
+        self.backbone = MLPBackbonePack(d_in=d_in, max_d_in=None if max_d_in is None else max_d_in + d_in_cat,
+                                        n_blocks=n_blocks, d_block=d_block, dropout=dropout,
                                         pack_size=pack_size, **backbone_kwargs)
+        # With per-member embedding sizes the first layer's input is not a prefix of valid
+        # columns (member m's embedding slots sit at f * max_d + k, the one-hot block after
+        # all of them); the reference's first layer multiplies the whole padded width
+        # (`nn.py:792-816` uses in_features only for initialisation), so this one does too.
+        self.backbone.blocks[0].linear.full_width_input = isinstance(d_in, list)
         self.output = LinearPack(d_block, d_out, max_in_features=backbone_kwargs.get('max_d_block'),
                                  pack_size=pack_size)
         self._n_numerical_features = n_numerical_features
@@ -733,9 +894,15 @@ class TabPack(ModulePack):
         return self.backbone.pack_size
 
     def replace(self, *, pack_idx: Tensor, numerical_embeddings=None, d_block=None, **kwargs) -> None:
-        if numerical_embeddings is not None:
+        """`TabPack.replace` (`nn.py:1986-2024`)."""
+        if numerical_embeddings is not None and self.num_module is None:
             raise RuntimeError('Cannot replace numerical embeddings because this model has none')
-        self.backbone.replace(pack_idx=pack_idx, d_block=d_block, **kwargs)
+        if self.num_module is not None:
+            self.num_module.replace(pack_idx=pack_idx, **({} if numerical_embeddings is None else numerical_embeddings))
+        d_emb = None if numerical_embeddings is None else numerical_embeddings.get('d_embedding')
+        d_in = None if d_emb is None else [v * self._n_numerical_features + sum(self._categorical_cardinalities)
+                                           for v in d_emb]
+        self.backbone.replace(pack_idx=pack_idx, d_in=d_in, d_block=d_block, **kwargs)
         self.output.replace(pack_idx=pack_idx, in_features=d_block)
 
     def forward(self, x_num: Tensor | None, x_cat: Tensor | None, pack_idx: Tensor | None = None) -> Tensor:
@@ -743,12 +910,22 @@ class TabPack(ModulePack):
             raise ValueError('Provide at least one of `x_num` and `x_cat`')
         parts = []
         if x_num is not None:
-            parts.append(x_num)
+            if self.num_module is None:
+                parts.append(x_num)
+            else:
+                if x_num.ndim == 2:
+                    x_num = x_num.expand(self.pack_size, *x_num.shape)
+                parts.append(self.num_module._flat(x_num, pack_idx))
+        elif self.num_module is not None:
+            raise ValueError('`x_num` is required when numerical embeddings are configured')
         if x_cat is not None:
             if self.cat_module is None:
                 raise ValueError('`x_cat` can only be provided when categorical features are configured')
-            dt = x_num.dtype if x_num is not None else torch.get_default_dtype()
-            parts.append(self.cat_module(x_cat).to(dt))
+            dt = parts[0].dtype if parts else torch.get_default_dtype()
+            oh = self.cat_module(x_cat).to(dt)
+            if parts and parts[0].ndim == 3 and oh.ndim == 2:
+                oh = oh.expand(parts[0].shape[0], *oh.shape)
+            parts.append(oh)
         x = torch.cat(parts, -1) if len(parts) > 1 else parts[0]
         if x.ndim == 3 and not self.training:
             raise RuntimeError('Three-dimensional input requires training mode')

@@ -312,6 +312,67 @@ def permutation_keys(*, seed: int, epoch: int, member_base: int, P: int, N: int,
     return keys
 
 
+def _cos_emb_args(x, weight, bias, affine_weight, affine_bias, d_embedding):
+    P, F, D = affine_weight.shape
+    for name, t in (('weight', weight), ('bias', bias), ('affine_weight', affine_weight),
+                    ('affine_bias', affine_bias)):
+        if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
+            raise TypeError(f'{name} must be a contiguous fp32 CUDA tensor')
+    x = _cuda('x', x, torch.float32)
+    if x.ndim == 2:
+        B, shared = x.shape[0], 1
+    else:
+        B, shared = x.shape[1], 0
+    if x.shape[-1] != F:
+        raise ValueError('The number of input features must match the number of features configured for the embeddings')
+    d = _i32('d_embedding', d_embedding)
+    a = _lib.CosEmbArgs(P=P, B=B, F=F, D=D, x_shared=shared, x=x.data_ptr(), weight=weight.data_ptr(),
+                        bias=bias.data_ptr(), affine_weight=affine_weight.data_ptr(),
+                        affine_bias=affine_bias.data_ptr(), d_embedding=_ptr(d))
+    return a, (x, d)
+
+
+def cos_emb_forward(x: Tensor, weight: Tensor, bias: Tensor, affine_weight: Tensor, affine_bias: Tensor,
+                    d_embedding: Tensor | None = None, *, out: Tensor | None = None,
+                    dtype: torch.dtype = torch.float32) -> Tensor:
+    """Cosine embeddings of x (P, B, F) or shared (B, F) into the first F * D columns of `out`
+    (P, B, >= F * D; allocated (P, B, F * D) of `dtype` when None); see `tp_cos_emb_forward`."""
+    a, keep = _cos_emb_args(x, weight, bias, affine_weight, affine_bias, d_embedding)
+    if out is None:
+        out = torch.empty(a.P, a.B, a.F * a.D, dtype=dtype, device=weight.device)
+    if out.stride(-1) != 1 or out.stride(0) != out.shape[1] * out.stride(1) or out.dtype not in (torch.float32,
+                                                                                                   torch.bfloat16):
+        raise TypeError('out must be a row-major fp32 or bf16 (P, B, width) tensor')
+    a.out, a.out_ld = out.data_ptr(), out.stride(1)
+    a.out_dtype = TP_DTYPE_BF16 if out.dtype == torch.bfloat16 else TP_DTYPE_F32
+    check(load().tp_cos_emb_forward(ctypes.byref(a), _stream()), 'tp_cos_emb_forward')
+    del keep
+    return out
+
+
+def cos_emb_backward(x: Tensor, weight: Tensor, bias: Tensor, affine_weight: Tensor, affine_bias: Tensor,
+                     d_embedding: Tensor | None, grad_out: Tensor):
+    """Parameter gradients (dweight, dbias, daffine_weight, daffine_bias) from the gradient of the
+    flattened embedding (its first F * D columns); see `tp_cos_emb_backward`."""
+    a, keep = _cos_emb_args(x, weight, bias, affine_weight, affine_bias, d_embedding)
+    if grad_out.stride(-1) != 1 or grad_out.stride(0) != grad_out.shape[1] * grad_out.stride(1):
+        grad_out = grad_out.contiguous()
+    if grad_out.dtype not in (torch.float32, torch.bfloat16):
+        grad_out = grad_out.float()
+    a.grad_out, a.grad_ld = grad_out.data_ptr(), grad_out.stride(1)
+    a.grad_dtype = TP_DTYPE_BF16 if grad_out.dtype == torch.bfloat16 else TP_DTYPE_F32
+    dweight, dbias = torch.empty_like(weight), torch.empty_like(bias)
+    daw, dab = torch.empty_like(affine_weight), torch.empty_like(affine_bias)
+    a.dweight, a.dbias = dweight.data_ptr(), dbias.data_ptr()
+    a.daffine_weight, a.daffine_bias = daw.data_ptr(), dab.data_ptr()
+    need = int(load().tp_cos_emb_workspace_size(a.P, a.B, a.F, a.D))
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=weight.device)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), need
+    check(load().tp_cos_emb_backward(ctypes.byref(a), _stream()), 'tp_cos_emb_backward')
+    del keep
+    return dweight, dbias, daw, dab
+
+
 def binary_roc_auc(scores: Tensor, labels: Tensor, workspace: Tensor | None = None) -> Tensor:
     """(P,) ROC AUC of each row of `scores` (P, N) fp32/fp64 against int64 labels (N,);
     see `tp_binary_roc_auc`.  The result has the scores' dtype."""

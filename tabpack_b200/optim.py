@@ -365,6 +365,18 @@ def optimizer_pack_reset_state(optimizer, *, pack_idx: Tensor) -> None:
 
 
 def should_skip_weight_decay(module_name: str, module, parameter_name: str, parameter) -> bool:
-    """`should_skip_weight_decay` (`optim.py:929-943`) for the packs of this package."""
-    del module_name, module, parameter
-    return parameter_name.endswith('bias')
+    """`should_skip_weight_decay` (`optim.py:929-943`) for the packs of this package: biases
+    and the frequencies of cosine embeddings take no weight decay."""
+    del module_name
+    from tabpack_b200.nn import CosineEmbeddingsPack
+
+    return parameter_name.endswith('bias') or (isinstance(module, CosineEmbeddingsPack) and parameter is module.weight)
+
+
+def split_weight_decay(model) -> tuple[list, list]:
+    """(parameters with weight decay, parameters without) by `should_skip_weight_decay`."""
+    decay, no_decay = [], []
+    for mname, mod in model.named_modules():
+        for pname, p in mod.named_parameters(recurse=False):
+            (no_decay if should_skip_weight_decay(mname, mod, pname, p) else decay).append(p)
+    return decay, no_decay

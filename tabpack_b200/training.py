@@ -26,8 +26,8 @@ from torch import Tensor
 from tabpack_b200 import ops
 from tabpack_b200.ensemble import greedy_ensemble
 from tabpack_b200.metrics import PackScore
-from tabpack_b200.nn import LinearPack, TabPack
-from tabpack_b200.optim import AdamWPack, MuonAdamWPack
+from tabpack_b200.nn import CosineEmbeddingsPack, LinearPack, TabPack
+from tabpack_b200.optim import AdamWPack, MuonAdamWPack, split_weight_decay
 from tabpack_b200.shard import allreduce_sum_, gather_members, member_ranges
 
 _LOSSES = ('mse', 'bce', 'ce')
@@ -44,12 +44,23 @@ def _mix(*xs: int) -> int:
 
 @torch.no_grad()
 def init_member_parameters_(model: torch.nn.Module, *, seed: int, member_ids: list[int]) -> None:
-    """Re-initialise every LinearPack member from its own generator.
+    """Re-initialise every LinearPack (and CosineEmbeddingsPack) member from its own generator.
 
     Same distribution as `LinearPack.reset_parameters` (`nn.py:702-747`), U(+-1/sqrt(in_i))
     for weights and biases, but member m of the j-th LinearPack draws from a generator
     seeded by (seed, global member id, j): initial weights do not depend on sharding.
     """
+    for j, emb in enumerate(m for m in model.modules() if isinstance(m, CosineEmbeddingsPack)):
+        # CosineEmbeddingsPack.reset_parameters (`nn.py:1706-1753`): truncated N(0, 1) on
+        # [-3, 3] times the member's init scale, the affine parts zero
+        for m, gid in enumerate(member_ids):
+            g = torch.Generator(device=emb.weight.device).manual_seed(_mix(seed, gid, 0xE0 + j))
+            w = torch.empty(emb.weight.shape[1:], device=emb.weight.device, dtype=emb.weight.dtype)
+            torch.nn.init.trunc_normal_(w, a=-3.0, b=3.0, generator=g)
+            scale = emb.init_scale if isinstance(emb.init_scale, float) else float(emb.init_scale[m])
+            emb.weight[m].copy_(w * scale)
+            for p in (emb.bias, emb.elementwise_affine_weight, emb.elementwise_affine_bias):
+                p[m].zero_()
     linears = [m for m in model.modules() if isinstance(m, LinearPack)]
     for j, lin in enumerate(linears):
         inf = lin.in_features.tolist() if lin.in_features is not None else [lin.max_in_features] * lin.pack_size
@@ -72,6 +83,14 @@ def _transpose(per_member: list[dict]) -> dict:
             out[k] = _transpose([d[k] for d in per_member])
         else:
             out[k] = [d[k] for d in per_member]
+    return out
+
+
+def _merge(base: dict, update: dict) -> dict:
+    """`base` with `update` merged in, nested dicts (e.g. `numerical_embeddings`) key by key."""
+    out = dict(base)
+    for k, v in update.items():
+        out[k] = _merge(out[k], v) if isinstance(v, dict) and isinstance(out.get(k), dict) else v
     return out
 
 
@@ -130,8 +149,7 @@ class PackTrainer:
         self.autocast = autocast_bf16
         self.device = torch.device(device)
         local = per_member_model[lo:hi]
-        kw = dict(model)
-        kw.update(_transpose(local))
+        kw = _merge(model, _transpose(local))
         self.model = TabPack(pack_size=hi - lo, **kw).to(self.device)
         self.model.backbone.set_member_base(lo)
         self.model.backbone._stream.seed = _mix(self.seed, 0xD0)  # one Philox key on every rank
@@ -143,14 +161,12 @@ class PackTrainer:
         if otype == 'muon':
             groups = [MuonAdamWPack.make_muon_parameter_group(b.linear) for b in self.model.backbone.blocks]
             muon_params = {id(g['params'][0]) for g in groups}
-            rest_nd = [p for n, p in self.model.named_parameters() if id(p) not in muon_params and n.endswith('bias')]
-            rest = [p for n, p in self.model.named_parameters() if id(p) not in muon_params and not n.endswith('bias')]
-            groups.append({'params': rest_nd, 'weight_decay': 0.0})
-            groups.append({'params': rest})
+            decay, no_decay = split_weight_decay(self.model)
+            groups.append({'params': [p for p in no_decay if id(p) not in muon_params], 'weight_decay': 0.0})
+            groups.append({'params': [p for p in decay if id(p) not in muon_params]})
             self.opt = MuonAdamWPack(groups, pack_size=hi - lo, allow_inplace_grad_mutation=True, **okw)
         elif otype == 'adamw':
-            nd = [p for n, p in self.model.named_parameters() if n.endswith('bias')]
-            wd = [p for n, p in self.model.named_parameters() if not n.endswith('bias')]
+            wd, nd = split_weight_decay(self.model)
             self.opt = AdamWPack([{'params': nd, 'weight_decay': 0.0}, {'params': wd}], pack_size=hi - lo, **okw)
         else:
             raise ValueError("optimizer type must be 'muon' or 'adamw'")

@@ -150,6 +150,68 @@ def make_tabpack(tp, dtype, name, forward_impl='dense'):
     np.savez_compressed(os.path.join(HERE, name), **arrays)
 
 
+def _randomize_cosine(emb, gen):
+    """The affine parameters start at zero (`nn.py:1742-1753`), which would make the
+    embedding output and most gradients vanish; give them random values."""
+    with torch.no_grad():
+        for prm in (emb.bias, emb.elementwise_affine_weight, emb.elementwise_affine_bias):
+            prm.copy_(torch.randn(prm.shape, generator=gen, dtype=prm.dtype))
+
+
+def make_cosine(tp, dtype, name):
+    """`CosineEmbeddingsPack` forward/backward with per-member embedding sizes."""
+    torch.manual_seed(8)
+    gen = torch.Generator().manual_seed(9)
+    P, B, F = 4, 23, 6
+    emb = tp.nn.CosineEmbeddingsPack(F, [3, 5, 8, 2], max_d_embedding=8, init_scale=[0.01, 0.1, 1.0, 0.3],
+                                     pack_size=P).to(dtype)
+    _randomize_cosine(emb, gen)
+    x = torch.randn(P, B, F, dtype=dtype, generator=gen)
+    y = emb(x)
+    dy = torch.randn(y.shape, dtype=dtype, generator=gen)
+    (y * dy).sum().backward()
+    arrays = {'x': _np(x), 'y': _np(y), 'dy': _np(dy), 'd_embedding': _np(emb.d_embedding).astype(np.int32)}
+    for k in ('weight', 'bias', 'elementwise_affine_weight', 'elementwise_affine_bias'):
+        arrays['param.' + k] = _np(getattr(emb, k))
+        arrays['grad.' + k] = _np(getattr(emb, k).grad)
+    np.savez_compressed(os.path.join(HERE, name), **arrays)
+
+
+def make_tabpack_cosine(tp, dtype, name):
+    """`TabPack` with cosine numerical embeddings of per-member size and one-hot
+    categorical features: the first layer's input is not a masked prefix (each member's
+    embedding columns sit at f * max_d + k, the one-hot block after them)."""
+    torch.manual_seed(10)
+    gen = torch.Generator().manual_seed(11)
+    P, B = 3, 31
+    n_num, cards, d_out = 4, [3, 2], 2
+    model = tp.nn.TabPack(
+        n_numerical_features=n_num, categorical_cardinalities=cards, d_out=d_out,
+        n_blocks=[2, 1, 2], d_block=[16, 8, 12], dropout=[0.1, 0.0, 0.2], pack_size=P,
+        numerical_embeddings={'type': tp.nn.CosineEmbeddingsPack, 'd_embedding': [4, 6, 3], 'max_d_embedding': 6,
+                              'init_scale': [0.1, 0.05, 0.2]},
+    ).to(dtype)
+    _randomize_cosine(model.num_module, gen)
+    model.train()
+    x_num = torch.randn(P, B, n_num, dtype=dtype, generator=gen)
+    x_cat = torch.stack([torch.randint(0, c + 1, (P, B), generator=gen) for c in cards], -1)
+    seed = 91
+    torch.set_default_dtype(dtype)
+    try:
+        with _PhiloxDropout(tp, seed):
+            y = model(x_num, x_cat)
+    finally:
+        torch.set_default_dtype(torch.float32)
+    dy = torch.randn(y.shape, dtype=dtype, generator=gen)
+    (y * dy).sum().backward()
+    arrays = {'x_num': _np(x_num), 'x_cat': _np(x_cat), 'y': _np(y), 'dy': _np(dy), 'seed': np.uint64(seed)}
+    for k, v in model.state_dict().items():
+        arrays['param.' + k] = _np(v)
+    for k, v in model.named_parameters():
+        arrays['grad.' + k] = _np(v.grad)
+    np.savez_compressed(os.path.join(HERE, name), **arrays)
+
+
 def make_tabpack_large(tp, name):
     """A larger batch for the bf16 comparison (statistics over 384 rows), computed by
     the reference in fp64 and stored as fp32."""
@@ -356,6 +418,9 @@ def main():
     make_tabpack(tp, torch.float64, 'tabpack_fp64.npz')
     make_tabpack(tp, torch.float64, 'tabpack_indexed_fp64.npz', forward_impl='indexed')
     make_tabpack_large(tp, 'tabpack_large.npz')
+    make_cosine(tp, torch.float64, 'cosine_fp64.npz')
+    make_cosine(tp, torch.float32, 'cosine_fp32.npz')
+    make_tabpack_cosine(tp, torch.float64, 'tabpack_cosine_fp64.npz')
     make_adamw(tp)
     make_newton_schulz(tp)
     make_muon(tp)

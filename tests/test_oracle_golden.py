@@ -176,3 +176,50 @@ def test_ensemble(golden):
     np.testing.assert_array_equal(idx, g['cls.idx'])
     np.testing.assert_allclose(oe.ensemble_mean(probs[:4], g['mean.w']), g['mean.out'], rtol=1e-6)
     np.testing.assert_allclose(oe.ensemble_mean(probs[:4]), g['mean.out_eq'], rtol=1e-6)
+
+
+@pytest.mark.parametrize('name, rtol', [('cosine_fp64.npz', 1e-12), ('cosine_fp32.npz', 2e-5)])
+def test_cosine_embeddings(golden, name, rtol):
+    g = golden(name)
+    prm = [g['param.' + k] for k in ('weight', 'bias', 'elementwise_affine_weight', 'elementwise_affine_bias')]
+    y, cache = ol.cosine_embeddings_forward(g['x'], *prm, g['d_embedding'])
+    np.testing.assert_allclose(y, g['y'], rtol=rtol, atol=rtol * np.abs(g['y']).max())
+    grads = ol.cosine_embeddings_backward(cache, g['dy'])
+    for got, k in zip(grads, ('weight', 'bias', 'elementwise_affine_weight', 'elementwise_affine_bias')):
+        want = g['grad.' + k]
+        np.testing.assert_allclose(got, want, rtol=rtol * 10, atol=rtol * 10 * np.abs(want).max(), err_msg=k)
+
+
+def test_tabpack_cosine_forward_backward(golden):
+    """TabPack with per-member cosine embedding sizes and one-hot features: the first
+    layer multiplies its full padded input width (`nn.py:792-816` ignores in_features)."""
+    g = golden('tabpack_cosine_fp64.npz')
+    P = g['x_num'].shape[0]
+    pre = 'param.num_module.'
+    prm = [g[pre + k] for k in ('weight', 'bias', 'elementwise_affine_weight', 'elementwise_affine_bias')]
+    emb, cache = ol.cosine_embeddings_forward(g['x_num'], *prm, g[pre + 'd_embedding'])
+    cards = [3, 2]
+    x = np.concatenate([emb.reshape(*emb.shape[:2], -1), ol.one_hot_encode(g['x_cat'], cards, np.float64)], -1)
+    nb = g['param.backbone.n_blocks']
+    blocks, masks = [], []
+    for i in range(int(nb.max())):
+        p = f'param.backbone.blocks.{i}.'
+        w = g[p + 'linear.weight']
+        blocks.append((w, g[p + 'linear.bias'], g[p + 'linear.out_features']))
+        masks.append(ol.dropout_mask_values(seed=int(g['seed']), offset=i, members=np.arange(P), n_rows=x.shape[1],
+                                            n_cols=w.shape[1], p=g[f'param.backbone.blocks.{i}.dropout.p'],
+                                            dtype=np.float64))
+    h, bcache = ol.mlp_forward_dense(x, blocks, nb, masks=masks)
+    y = ol.linear_forward(h, g['param.output.weight'], g['param.output.bias'])
+    np.testing.assert_allclose(y, g['y'], rtol=1e-12, atol=1e-12)
+    dh, _, _ = ol.linear_backward(h, g['param.output.weight'], None, g['dy'])
+    dx, grads = ol.mlp_backward_dense(blocks, bcache, dh, nb)
+    for i, (dW, db) in enumerate(grads):
+        p = f'grad.backbone.blocks.{i}.linear.'
+        np.testing.assert_allclose(dW, g[p + 'weight'], rtol=1e-10, atol=1e-10)
+        np.testing.assert_allclose(db, g[p + 'bias'], rtol=1e-10, atol=1e-10)
+    F, D = prm[2].shape[1:]
+    demb = dx[..., :F * D].reshape(P, -1, F, D)
+    for got, k in zip(ol.cosine_embeddings_backward(cache, demb),
+                      ('weight', 'bias', 'elementwise_affine_weight', 'elementwise_affine_bias')):
+        np.testing.assert_allclose(got, g['grad.num_module.' + k], rtol=1e-10, atol=1e-10, err_msg=k)

@@ -94,3 +94,36 @@ def test_training_reduces_loss_and_ensembles():
     y_pack, heads = pred(val['x_num'], val['x_cat'])
     want = y_pack[res.ensemble_idx].mean(0)
     torch.testing.assert_close(heads['greedy'], want, rtol=1e-6, atol=1e-6)
+
+
+def test_sharding_is_bit_invariant_with_cosine_embeddings():
+    """Per-member embedding sizes and init scales from per-member configs (merged into the
+    shared `numerical_embeddings` entry); sharded training equals the unsharded run."""
+    from tabpack_b200.nn import CosineEmbeddingsPack
+    from tabpack_b200.training import PackTrainer
+
+    model = dict(MODEL, numerical_embeddings={'type': CosineEmbeddingsPack, 'max_d_embedding': 8})
+    per = [dict(pm, numerical_embeddings={'d_embedding': d, 'init_scale': s})
+           for pm, d, s in zip(PER_MEMBER, [4, 8, 2, 6, 3, 8], [0.1, 0.05, 0.2, 0.1, 0.3, 0.02])]
+
+    def trainer(rng):
+        return PackTrainer(n_members=6, model=model, per_member_model=per,
+                           optimizer=dict(type='muon', adamw_lr=3e-3, weight_decay=1e-4, muon_lr=2e-2),
+                           loss='mse', seed=5, device='cuda', autocast_bf16=True, member_range=rng)
+
+    data = _data(512, 4, 'cuda')
+    full, a, b = trainer((0, 6)), trainer((0, 2)), trainer((2, 6))
+    first = None
+    for epoch in range(2):
+        for t in (full, a, b):
+            loss = t.fit_epoch(data, batch_size=64, epoch=epoch)
+            if t is full:
+                first = loss if first is None else first
+    sd = full.model.state_dict()
+    for shard, lo in ((a, 0), (b, 2)):
+        for k, v in shard.model.state_dict().items():
+            if v.ndim == 0 or sd[k].shape[1:] != v.shape[1:]:
+                continue
+            assert torch.equal(v, sd[k][lo: lo + v.shape[0]]), k
+    assert torch.isfinite(loss).all()
+    assert full.model.num_module.elementwise_affine_weight.abs().sum() > 0  # the embeddings train
