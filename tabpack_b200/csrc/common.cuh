@@ -167,7 +167,7 @@ __device__ __forceinline__ void fence_barrier_init() {
 }
 
 // ---------------------------------------------------------------------------
-// TMA: tiled 3-D load into shared memory, completion on an mbarrier (no multicast).
+// TMA: tiled 3-D load into this CTA's shared memory, completion on an mbarrier.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
                                             int z) {
@@ -180,7 +180,7 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
 
 // CTA-pair form (cta_group::2): the data lands in this CTA's shared memory and the
 // transaction bytes are counted on `bar_cluster`, a shared::cluster address that may
-// name the mbarrier of the pair's leader CTA (no multicast).
+// name the mbarrier of the pair's leader CTA; the data goes to this CTA only.
 __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
                                                  int y, int z) {
   asm volatile(

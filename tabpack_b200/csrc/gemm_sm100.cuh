@@ -1,5 +1,5 @@
 // Persistent, warp-specialised ragged grouped GEMM for the packed linear layer on
-// sm_100a: TMA (no multicast) fills a ring of shared-memory stages, one thread
+// sm_100a: TMA (one destination CTA per load) fills a ring of shared-memory stages, one thread
 // issues tcgen05.mma into a double-buffered TMEM accumulator, and the epilogue
 // warps drain TMEM with tcgen05.ld, apply the fused epilogue and store.
 //
