@@ -548,6 +548,63 @@ def run_metrics(args) -> None:
         'clocks': clocks.summary()}), flush=True)
 
 
+def run_train(args) -> None:
+    """Training steps of the full-training configuration: binary classification over
+    1 000 000 synthetic rows (100 numerical features N(0, 1), 10 % of rows heavy-tailed
+    Student-t(3); 10 categorical features with cardinalities log-U[2, 1000]; labels
+    Bernoulli(sigmoid(random teacher MLP))); `members` members per GPU with depth U{1..4},
+    width U{128..1024 step 8}, dropout U[0, 0.5], Muon + AdamW, batch 1024, bf16 autocast.
+    One step = batch gather, one-hot encoding, forward, loss, backward and optimizer step of
+    every member; value = member-samples/s (members x 1024 / step time)."""
+    import torch
+
+    from tabpack_b200.training import PackTrainer
+
+    dev = torch.device('cuda', 0)
+    torch.cuda.set_device(dev)
+    rng = np.random.default_rng(21)
+    N, n_num, batch = 1_000_000, 100, 1024
+    cards = [int(c) for c in np.exp(rng.uniform(np.log(2), np.log(1000), 10)).round()]
+    g = torch.Generator(device=dev).manual_seed(21)
+    x = torch.randn(N, n_num, device=dev, generator=g)
+    heavy = torch.rand(N, device=dev, generator=g) < 0.1
+    t3 = torch.distributions.StudentT(3.0).sample((int(heavy.sum()), n_num)).to(dev)
+    x[heavy] = t3
+    xc = torch.stack([torch.randint(0, c, (N,), device=dev, generator=g) for c in cards], 1)
+    w1 = torch.randn(n_num, 64, device=dev, generator=g) / n_num ** 0.5
+    y = (torch.rand(N, device=dev, generator=g) < torch.sigmoid(torch.relu(x @ w1).sum(1) / 8 - 1)).to(torch.int64)
+    data = {'x_num': x, 'x_cat': xc, 'y': y}
+    P = args.members
+    per = [dict(n_blocks=int(rng.integers(1, 5)), d_block=int(rng.integers(16, 129)) * 8,
+                dropout=float(rng.uniform(0, 0.5))) for _ in range(P)]
+    model = dict(n_numerical_features=n_num, categorical_cardinalities=cards, d_out=1, max_d_block=1024,
+                 max_n_blocks=4)
+    trainer = PackTrainer(n_members=P, model=model, per_member_model=per,
+                          optimizer=dict(type='muon', adamw_lr=1e-3, weight_decay=1e-5, muon_lr=2e-2),
+                          loss='bce', seed=0, device=dev, autocast_bf16=True, member_range=(0, P))
+    steps = args.steps
+    trainer.fit_epoch({k: v[: batch * args.warmup] for k, v in data.items()}, batch_size=batch, epoch=0)
+    torch.cuda.synchronize()
+    sub = {k: v[: batch * steps] for k, v in data.items()}
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        torch.cuda.nvtx.range_push('timed')  # lets a profiler keep only the timed steps
+        e0.record()
+        loss = trainer.fit_epoch(sub, batch_size=batch, epoch=1)
+        e1.record()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    print(json.dumps({
+        'metric': 'member-samples/sec train (full TabPack training step)', 'value': P * batch / (ms / 1e3),
+        'unit': 'member-samples/s', 'n_gpus': 1, 'steps': steps, 'warmup': args.warmup, 'ms_per_step': ms,
+        'higher_is_better': True, 'dtype': 'bf16', 'data': 'synthetic',
+        'config': {'workload': f'{P} members, depth U{{1..4}}, width U{{128..1024}}, 100 numerical + 10 categorical '
+                               f'(sum of cardinalities {sum(cards)}), batch 1024, Muon + AdamW, bf16',
+                   'mean_train_loss': float(loss.mean())},
+        'clocks': clocks.summary()}), flush=True)
+
+
 def main() -> None:
     global MEMBERS
     ap = argparse.ArgumentParser()
@@ -559,18 +616,21 @@ def main() -> None:
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--members', type=int, default=None,
                     help='members per GPU (default 256 for the layer workload, 1024 for the optimizer)')
-    ap.add_argument('--workload', choices=['layer', 'optimizer', 'metrics'], default='layer',
+    ap.add_argument('--workload', choices=['layer', 'optimizer', 'metrics', 'train'], default='layer',
                     help='layer: the packed-block fwd+bwd benchmark (default); optimizer: grouped Muon step; '
                          'metrics: validation metrics, ROC AUC and greedy selection')
     args = ap.parse_args()
     if args.members is None:
-        args.members = {'optimizer': 1024, 'metrics': 512}.get(args.workload, MEMBERS)
+        args.members = {'optimizer': 1024, 'metrics': 512, 'train': 512}.get(args.workload, MEMBERS)
     MEMBERS = args.members
     if args.workload == 'optimizer':
         run_optimizer(args)
         return
     if args.workload == 'metrics':
         run_metrics(args)
+        return
+    if args.workload == 'train':
+        run_train(args)
         return
     if args.impl == 'reference':
         run_reference(args)

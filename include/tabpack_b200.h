@@ -293,6 +293,26 @@ typedef struct tp_cos_emb_args {
   size_t workspace_bytes;
 } tp_cos_emb_args;
 size_t tp_cos_emb_workspace_size(int32_t P, int32_t B, int32_t F, int32_t D);
+
+/* First-layer input of a TabPack without numerical embeddings, in one pass: row r gets its
+ * n_num numerical values, then the one-hot encoding of each categorical feature
+ * (_OneHotEncoding, src/tabpackage/nn.py:1836-1871; the value `cardinality` is the unknown
+ * category and encodes as zeros; torch.cat of both parts, nn.py:2071-2107), converted to
+ * out_dtype, then zeros up to out_ld.  cat_offsets: (n_cat + 1,) device int32 prefix sums of
+ * the cardinalities.  out_ld must be a multiple of 8 (bf16) or 4 (fp32) and at least
+ * n_num + cat_offsets[n_cat]. */
+typedef struct tp_input_args {
+  int64_t rows;
+  int32_t n_num;
+  int32_t n_cat;
+  const float* x_num;            /* (rows, n_num) or NULL */
+  const int64_t* x_cat;          /* (rows, n_cat) or NULL */
+  const int32_t* cat_offsets;    /* (n_cat + 1,) */
+  void* out;                     /* (rows, out_ld) */
+  int32_t out_ld;
+  int32_t out_dtype;             /* TP_DTYPE_F32 or TP_DTYPE_BF16 */
+} tp_input_args;
+int tp_tabpack_input(const tp_input_args* a, void* stream);
 int tp_cos_emb_forward(const tp_cos_emb_args* a, void* stream);
 int tp_cos_emb_backward(const tp_cos_emb_args* a, void* stream);
 

@@ -94,6 +94,14 @@ class CosEmbArgs(ctypes.Structure):
     ]
 
 
+class InputArgs(ctypes.Structure):
+    _fields_ = [
+        ('rows', ctypes.c_int64), ('n_num', ctypes.c_int32), ('n_cat', ctypes.c_int32), ('x_num', ctypes.c_void_p),
+        ('x_cat', ctypes.c_void_p), ('cat_offsets', ctypes.c_void_p), ('out', ctypes.c_void_p),
+        ('out_ld', ctypes.c_int32), ('out_dtype', ctypes.c_int32),
+    ]
+
+
 class GreedyArgs(ctypes.Structure):
     _fields_ = [
         ('metric', ctypes.c_int32), ('maximize', ctypes.c_int32), ('n_pred', ctypes.c_int32),
@@ -130,6 +138,7 @@ SIGNATURES = {
     'tp_cos_emb_workspace_size': (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     'tp_cos_emb_forward': (ctypes.c_int, [ctypes.POINTER(CosEmbArgs), ctypes.c_void_p]),
     'tp_cos_emb_backward': (ctypes.c_int, [ctypes.POINTER(CosEmbArgs), ctypes.c_void_p]),
+    'tp_tabpack_input': (ctypes.c_int, [ctypes.POINTER(InputArgs), ctypes.c_void_p]),
     'tp_roc_auc_workspace_size': (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32]),
     'tp_binary_roc_auc': (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
                                          ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,

@@ -777,6 +777,28 @@ size_t tp_cos_emb_workspace_size(int32_t P, int32_t B, int32_t F, int32_t D) {
   return s > 1 ? (size_t)4 * s * P * (size_t)F * D * sizeof(double) : 0;
 }
 
+int tp_tabpack_input(const tp_input_args* a, void* stream) {
+  if (!a || a->rows <= 0 || a->n_num < 0 || a->n_cat < 0 || !a->out) return fail(TP_EINVAL, "bad input arguments");
+  if (a->n_num > 0 && !a->x_num) return fail(TP_EINVAL, "x_num is null");
+  if (a->n_cat > 0 && (!a->x_cat || !a->cat_offsets)) return fail(TP_EINVAL, "x_cat or cat_offsets is null");
+  const bool bf16 = a->out_dtype == TP_DTYPE_BF16;
+  if (!bf16 && a->out_dtype != TP_DTYPE_F32) return fail(TP_EINVAL, "bad output dtype");
+  if (a->out_ld % (bf16 ? 8 : 4) != 0 || a->out_ld < a->n_num)
+    return fail(TP_EINVAL, "out_ld must be a multiple of %d covering the columns", bf16 ? 8 : 4);
+  if (!aligned16(a->out)) return fail(TP_EALIGN, "out must be 16-byte aligned");
+  InputArgs k{a->rows, a->n_num, a->n_cat, a->n_num > 0 ? a->x_num : nullptr, a->n_cat > 0 ? a->x_cat : nullptr,
+              a->cat_offsets, a->out, a->out_ld, bf16 ? 1 : 0};
+  const long long blocks = (a->rows + 7) / 8;
+  if (blocks > 0x7FFFFFFFLL) return fail(TP_EINVAL, "too many rows");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (bf16)
+    tabpack_input_kernel<true><<<(unsigned)blocks, 256, 0, st>>>(k);
+  else
+    tabpack_input_kernel<false><<<(unsigned)blocks, 256, 0, st>>>(k);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
 int tp_cos_emb_forward(const tp_cos_emb_args* a, void* stream) {
   int rc = check_cos_emb(a);
   if (rc) return rc;

@@ -354,7 +354,8 @@ def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features
     dtype = _compute_dtype(x)
     in_cols = x.shape[-1]
     cols = _round8(in_cols) if dtype == torch.bfloat16 else in_cols
-    if cols != weight.shape[-1] and weight.shape[-1] != in_cols:
+    # bf16 inputs may arrive already padded to the 8-column multiple the tensor-core path uses
+    if weight.shape[-1] != in_cols and not (dtype == torch.bfloat16 and in_cols == _round8(weight.shape[-1])):
         raise ValueError('The number of input features must be equal to the maximum supported number of features')
     xc = x.to(dtype)
     if cols != in_cols:
@@ -888,10 +889,39 @@ class TabPack(ModulePack):
                                  pack_size=pack_size)
         self._n_numerical_features = n_numerical_features
         self._categorical_cardinalities = categorical_cardinalities
+        # prefix sums of the cardinalities: the one-hot block of each feature (tp_tabpack_input)
+        offs = [0]
+        for c in categorical_cardinalities:
+            offs.append(offs[-1] + c)
+        self.register_buffer('_cat_offsets', torch.tensor(offs, dtype=torch.int32), persistent=False)
 
     @property
     def pack_size(self) -> int:
         return self.backbone.pack_size
+
+    def _fused_input(self, x_num: Tensor | None, x_cat: Tensor) -> Tensor | None:
+        """[x_num | one-hot(x_cat)] built by one kernel in the first layer's dtype (already
+        padded to the tensor-core width), or None when the generic path has to run (input
+        gradients, numerical embeddings, CPU tensors, an fp32 width the kernel cannot pad)."""
+        if self.num_module is not None or self.cat_module is None or not x_cat.is_cuda:
+            return None
+        if x_num is not None and (x_num.requires_grad or not x_num.is_cuda or x_num.shape[:-1] != x_cat.shape[:-1]
+                                  or x_num.shape[-1] != self._n_numerical_features):
+            return None
+        if x_cat.shape[-1] != len(self._categorical_cardinalities):
+            return None
+        if torch.is_autocast_enabled('cuda') and torch.get_autocast_dtype('cuda') == torch.bfloat16:
+            dtype = torch.bfloat16
+        else:
+            dtype = x_num.dtype if x_num is not None else torch.get_default_dtype()
+        d_in = self._n_numerical_features + sum(self._categorical_cardinalities)
+        if dtype == torch.bfloat16:
+            width = _round8(d_in)
+        elif dtype == torch.float32 and d_in % 4 == 0:
+            width = d_in
+        else:
+            return None
+        return ops.tabpack_input(x_num, x_cat, self._cat_offsets, width, dtype)
 
     def replace(self, *, pack_idx: Tensor, numerical_embeddings=None, d_block=None, **kwargs) -> None:
         """`TabPack.replace` (`nn.py:1986-2024`)."""
@@ -908,6 +938,11 @@ class TabPack(ModulePack):
     def forward(self, x_num: Tensor | None, x_cat: Tensor | None, pack_idx: Tensor | None = None) -> Tensor:
         if x_num is None and x_cat is None:
             raise ValueError('Provide at least one of `x_num` and `x_cat`')
+        fused = None if x_cat is None else self._fused_input(x_num, x_cat)
+        if fused is not None:
+            if fused.ndim == 3 and not self.training:
+                raise RuntimeError('Three-dimensional input requires training mode')
+            return self.output(self.backbone(fused, pack_idx), pack_idx)
         parts = []
         if x_num is not None:
             if self.num_module is None:

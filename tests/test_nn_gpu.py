@@ -101,3 +101,27 @@ def test_eval_forward_shared_input_and_state_dict_keys(golden):
     h, _ = ol.mlp_forward_dense(np.broadcast_to(x, (P, *x.shape)), blocks, g['n_blocks'])
     want = ol.linear_forward(h, g['param.output.weight'], g['param.output.bias'])
     assert _rel(y, want) < 1e-4
+
+
+@pytest.mark.parametrize('dtype,shared', [(torch.float32, False), (torch.bfloat16, False), (torch.bfloat16, True)])
+def test_fused_first_layer_input_matches_one_hot_concat(dtype, shared):
+    """tp_tabpack_input equals torch.cat([x_num, one_hot(x_cat)]) (unknown category = zeros),
+    cast to the first layer's dtype and zero-padded to its width; 37 categorical features
+    exercise the per-piece feature search."""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+    from tabpack_b200 import ops
+
+    g = torch.Generator(device='cuda').manual_seed(3)
+    cards = [int(c) for c in torch.randint(1, 40, (37,), generator=torch.Generator().manual_seed(4))]
+    lead = (300,) if shared else (3, 100)
+    x_num = torch.randn(*lead, 6, device='cuda', generator=g)
+    x_cat = torch.stack([torch.randint(0, c + 1, lead, device='cuda', generator=g) for c in cards], -1)
+    offs = torch.tensor([0] + list(np.cumsum(cards)), dtype=torch.int32, device='cuda')
+    d_in = 6 + sum(cards)
+    width = (d_in + 7) // 8 * 8
+    got = ops.tabpack_input(x_num, x_cat, offs, width, dtype)
+    oh = torch.cat([torch.nn.functional.one_hot(x_cat[..., i], c + 1)[..., :-1] for i, c in enumerate(cards)], -1)
+    want = torch.nn.functional.pad(torch.cat([x_num, oh.float()], -1), (0, width - d_in)).to(dtype)
+    assert got.shape == want.shape and got.dtype == dtype
+    assert torch.equal(got, want)
