@@ -291,14 +291,15 @@ class _WeightCache:
         self.key = None
         self.value = None
 
-    def get(self, w: Tensor, dtype: torch.dtype, cols: int) -> Tensor:
-        if w.dtype == dtype and w.shape[-1] == cols:
+    def get(self, w: Tensor, dtype: torch.dtype, cols: int, rows: int | None = None) -> Tensor:
+        rows = w.shape[-2] if rows is None else rows
+        if w.dtype == dtype and w.shape[-1] == cols and w.shape[-2] == rows:
             return w.detach()
-        key = (w.data_ptr(), w._version, dtype, cols, tuple(w.shape))
+        key = (w.data_ptr(), w._version, dtype, cols, rows, tuple(w.shape))
         if self.key != key:
             wd = w.detach().to(dtype)
-            if cols != w.shape[-1]:
-                wd = nn.functional.pad(wd, (0, cols - w.shape[-1]))
+            if cols != w.shape[-1] or rows != w.shape[-2]:
+                wd = nn.functional.pad(wd, (0, cols - w.shape[-1], 0, rows - w.shape[-2]))
             self.value = wd.contiguous()
             self.key = key
         return self.value
@@ -321,8 +322,8 @@ class _PackedLinearFn(torch.autograd.Function):
     dgrad, wgrad); `cfg` carries the non-tensor configuration."""
 
     @staticmethod
-    def forward(ctx, x, weight, bias, w_compute, cfg):
-        y = ops.linear_forward(x, w_compute, bias, **cfg['kw'])
+    def forward(ctx, x, weight, bias, w_compute, b_compute, cfg):
+        y = ops.linear_forward(x, w_compute, b_compute, **cfg['kw'])
         ctx.cfg = cfg
         ctx.x_shape = x.shape
         ctx.save_for_backward(x, w_compute, y if (cfg['kw']['relu'] or cfg['kw']['dropout_p'] is not None) else None)
@@ -342,7 +343,7 @@ class _PackedLinearFn(torch.autograd.Function):
                 dx = dx.sum(PACK_DIM)
             if dx.shape[-1] != ctx.x_shape[-1]:  # the gradient of this function's (padded) input
                 dx = dx[..., : ctx.x_shape[-1]]
-        return dx, dw, db, None, None
+        return dx, dw, db, None, None, None
 
 
 def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features=None, out_features=None,
@@ -361,12 +362,20 @@ def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features
     if cols != in_cols:
         xc = nn.functional.pad(xc, (0, cols - in_cols))
     xc = xc.contiguous()
-    wc = (cache or _WeightCache()).get(weight, dtype, cols)
+    # bf16 output widths that are not a multiple of 8 (e.g. a 1-wide output head) run on the
+    # tensor cores over zero-padded weight rows and bias; the padded columns are sliced off
+    max_out = weight.shape[-2]
+    rows = _round8(max_out) if dtype == torch.bfloat16 else max_out
+    wc = (cache or _WeightCache()).get(weight, dtype, cols, rows)
+    bc = bias
+    if bias is not None and rows != max_out:
+        bc = nn.functional.pad(bias.detach(), (0, rows - max_out))
     kw = dict(in_features=in_features, out_features=out_features, n_blocks=n_blocks, block_index=block_index,
               relu=relu, dropout_p=dropout_p, seed=seed, offset=offset, member_base=member_base)
     cfg = {'kw': kw, 'w_shape': tuple(weight.shape), 'in_cols': in_cols}
     with torch.autocast(x.device.type, enabled=False):
-        return _PackedLinearFn.apply(xc, weight, bias, wc, cfg)
+        y = _PackedLinearFn.apply(xc, weight, bias, wc, bc, cfg)
+    return y if rows == max_out else y[..., :max_out]
 
 
 def _widths(buf: Tensor | None) -> Tensor | None:
