@@ -99,6 +99,34 @@ __device__ __forceinline__ void epi_fwd16(const LinearProblem& pr, int m, int ro
   }
 }
 
+// Newton-Schulz addend D (bf16) of one 32-column chunk of one row, zeros outside the
+// member's valid columns (`drow` null outside its valid rows or without D).
+__device__ __forceinline__ void ns_load_d(const __nv_bfloat16* drow, int col0, int nv, uint4 (&d)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    d[j] = (drow != nullptr && 8 * j < nv) ? *reinterpret_cast<const uint4*>(drow + col0 + 8 * j) : make_uint4(0, 0, 0, 0);
+}
+
+// alpha * acc + beta * D of one 32-column chunk (D preloaded), exact zeros outside the
+// member's r x (r|c) block, bf16 into the row's staging slot.
+__device__ __forceinline__ void ns_chunk(const LinearProblem& pr, bool rv, int nv, const uint32_t (&r)[32],
+                                         const uint4 (&d)[4], uint8_t* stage) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&d[j]);
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      v[e] = (rv && 8 * j + e < nv) ? pr.alpha * __uint_as_float(r[8 * j + e]) + pr.beta * __bfloat162float(h[e]) : 0.0f;
+    uint4 u;
+    u.x = pack_bf16x2(v[0], v[1]);
+    u.y = pack_bf16x2(v[2], v[3]);
+    u.z = pack_bf16x2(v[4], v[5]);
+    u.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(stage + 16 * j) = u;
+  }
+}
+
 // Epilogue of one 32-column chunk of one output row held in registers `r`
 // (raw fp32 accumulator bits from tcgen05.ld).
 template <int MODE>
@@ -229,8 +257,11 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
   uint64_t* tfull = bars + 2 * Cfg::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* done_bar = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  uint64_t* tr_full = done_bar + 1;   // tile-id ring (dynamic scheduling): published
+  uint64_t* tr_empty = tr_full + 4;   //   read by the MMA thread and every epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tr_empty + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* tile_ring = abort_flag + 1;
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -240,6 +271,21 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  // Dynamic scheduling (single CTAs with a counter): the producer claims the k-th tile
+  // (k > 0) with an atomic on the counter and publishes its id in ring slot k % 4; the MMA
+  // thread and the epilogue warps read the ids in the same order.  Tiles of ragged members
+  // differ a lot in cost, so claiming them as CTAs free up balances the launch.
+  const bool dyn = !PAIR && pr.tile_counter != nullptr;
+  // k-th tile of this CTA for a consumer (MMA thread or an epilogue warp); total_tiles ends
+  auto consume_tile = [&](int k, bool arrive) -> int {
+    if (!dyn) return tile0 + k * tile_step;
+    const int s = k & 3;
+    if (!mbar_wait(&tr_full[s], (uint32_t)(k >> 2) & 1u, abort_flag)) return total_tiles;
+    const int t = tile_ring[s];
+    __syncwarp(__activemask());
+    if (arrive) mbar_arrive(&tr_empty[s]);
+    return t;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::STAGES; ++s) {
@@ -251,6 +297,10 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
       mbar_init(&tempty[i], PAIR ? 2 * Cfg::EPI_WARPS : Cfg::EPI_WARPS);  // the leader's counts both CTAs
     }
     mbar_init(done_bar, 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&tr_full[i], 1);
+      mbar_init(&tr_empty[i], 1 + Cfg::EPI_WARPS);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&tmA);
@@ -273,7 +323,16 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = tile0; t < total_tiles; t += tile_step) {
+      for (int k = 0;; ++k) {
+        int t = tile0 + k * tile_step;
+        if (dyn) {  // claim and publish the k-th tile
+          if (k > 0) t = min(total_tiles, (int)gridDim.x + atomicAdd(pr.tile_counter, 1));
+          const int s = k & 3;
+          if (!mbar_wait(&tr_empty[s], ((uint32_t)(k >> 2) & 1u) ^ 1u, abort_flag)) goto producer_done;
+          tile_ring[s] = min(t, total_tiles);
+          mbar_arrive(&tr_full[s]);
+        }
+        if (t >= total_tiles) break;
         const TileInfo ti = decode_tile(pr, t, Cfg::BK);
         if (ti.kind != KIND_MMA) continue;
         const int zA = ((MODE == MODE_FWD || MODE == MODE_WGRAD_T) && pr.x_shared) ? 0 : ti.member;  // NS operands are per member
@@ -336,7 +395,9 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int t = tile0; t < total_tiles; t += tile_step) {
+      for (int k = 0;; ++k) {
+        const int t = consume_tile(k, true);
+        if (t >= total_tiles) break;
         const TileInfo ti = decode_tile(pr, t, Cfg::BK);
         if (ti.kind != KIND_MMA) continue;
         // the last column block of a member only multiplies its own columns (N multiple of
@@ -427,16 +488,19 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
                        : 0.0f;
       }
     };
-    if (tile0 < total_tiles) {
-      nti = decode_tile(pr, tile0, Cfg::BK);
+    int t = consume_tile(0, lane == 0);
+    if (t < total_tiles) {
+      nti = decode_tile(pr, t, Cfg::BK);
       if (dropout_on) np = __ldg(pr.dropout_p + nti.member);
       if (MODE == MODE_FWD) load_bias(nti);
     }
-    for (int t = tile0; t < total_tiles; t += tile_step) {
+    int t_next = total_tiles;
+    for (int k = 0; t < total_tiles; ++k, t = t_next) {
       const TileInfo ti = nti;
       const float p_cur = np;
-      if (t + tile_step < total_tiles) {
-        nti = decode_tile(pr, t + tile_step, Cfg::BK);
+      t_next = consume_tile(k + 1, lane == 0);
+      if (t_next < total_tiles) {
+        nti = decode_tile(pr, t_next, Cfg::BK);
         if (dropout_on) np = __ldg(pr.dropout_p + nti.member);
       }
       const int m = ti.member;
@@ -456,7 +520,15 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < NCH; ++i) sbias[32 * i + lane] = bnext[i] * scale;
           __syncwarp();
-          if (t + tile_step < total_tiles) load_bias(nti);
+          if (t_next < total_tiles) load_bias(nti);
+        }
+        // Newton-Schulz: the addend of the first chunk is loaded before the accumulator wait
+        [[maybe_unused]] uint4 d_a[4], d_b[4];
+        [[maybe_unused]] const __nv_bfloat16* d_row = nullptr;
+        if constexpr (MODE == MODE_NS || MODE == MODE_NS_BMN) {
+          if (pr.D != nullptr && row < ti.m_valid)
+            d_row = reinterpret_cast<const __nv_bfloat16*>(pr.D) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld;
+          ns_load_d(d_row, cbase, ti.n_valid - cbase, d_a);
         }
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
         tc_fence_after();
@@ -487,7 +559,31 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
             __syncwarp();
           }
         };
-        if constexpr (MODE == MODE_WGRAD_T) {
+        if constexpr (MODE == MODE_NS || MODE == MODE_NS_BMN) {
+          // the addend of chunk c + 1 is loaded while chunk c is computed
+          const bool rv = row < ti.m_valid;
+          uint32_t na[32];
+#pragma unroll 1
+          for (int c = 0; c < nch; c += 2) {
+            const int col0 = cbase + 32 * c;
+            tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * c), na);
+            if (c + 1 < nch) ns_load_d(d_row, col0 + 32, ti.n_valid - col0 - 32, d_b);
+            tmem_wait_ld();
+            ns_chunk(pr, rv, ti.n_valid - col0, na, d_a, stage_row);
+            __syncwarp();
+            stage_flush(pr, m, row_base, col0, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
+            __syncwarp();
+            if (c + 1 < nch) {
+              tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * (c + 1)), na);
+              if (c + 2 < nch) ns_load_d(d_row, col0 + 64, ti.n_valid - col0 - 64, d_a);
+              tmem_wait_ld();
+              ns_chunk(pr, rv, ti.n_valid - col0 - 32, na, d_b, stage_row);
+              __syncwarp();
+              stage_flush(pr, m, row_base, col0 + 32, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
+              __syncwarp();
+            }
+          }
+        } else if constexpr (MODE == MODE_WGRAD_T) {
           // lane = input feature `row`, register j = output feature col0 + j:
           // dW[o][row] for fixed o is 32 consecutive floats across the warp
           float* base = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms;

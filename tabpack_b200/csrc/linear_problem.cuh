@@ -47,6 +47,9 @@ struct LinearProblem {
   int BM, BN;
   FastDiv div_member;  // by m_tiles * n_tiles (tiles per member)
   FastDiv div_mt;      // by m_tiles
+  // zeroed counter for dynamic tile scheduling (single-CTA launches), or nullptr: CTA c
+  // takes tiles c, c + grid, ...
+  int* tile_counter;
   // Newton-Schulz GEMMs: member m multiplies r = ns_rows[m], c = ns_cols[m] matrices;
   // ns_shape 1: (M, N, K) = (r, r, c), 2: (r, r, r), 3: (r, c, r); members with
   // active[m] == 0 are skipped.

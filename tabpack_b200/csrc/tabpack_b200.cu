@@ -237,8 +237,11 @@ LinearProblem base_problem(const tp_linear_args* a) {
 
 struct MuonLayout {
   int R_s, C_s, tiles;
-  size_t off_x0, off_x1, off_a, off_b, off_norm, off_rows, off_cols, off_trans, off_active, off_partial, total;
+  size_t off_x0, off_x1, off_a, off_b, off_norm, off_rows, off_cols, off_trans, off_active, off_partial, off_counter,
+      total;
 };
+
+constexpr int MUON_COUNTERS = 64;
 
 MuonLayout muon_layout(int P, int max_out, int max_in) {
   auto up = [](size_t v, size_t a) { return (v + a - 1) / a * a; };
@@ -258,6 +261,7 @@ MuonLayout muon_layout(int P, int max_out, int max_in) {
   L.off_active = take((size_t)P * 4);
   L.tiles = ((max_out + 31) / 32) * ((max_in + 31) / 32);
   L.off_partial = take((size_t)P * L.tiles * 4);
+  L.off_counter = take(MUON_COUNTERS * 4);  // tile counters of the Newton-Schulz launches
   L.total = o;
   return L;
 }
@@ -265,9 +269,10 @@ MuonLayout muon_layout(int P, int max_out, int max_in) {
 // One Newton-Schulz GEMM over the pack: out = alpha * A_op B_op^T + beta * D.
 template <int MODE>
 int ns_gemm(const MuonArgs& ma, int shape, const void* a_op, int a_cols, const void* b_op, int b_cols,
-            void* out, int out_cols, const void* d, float alpha, float beta, cudaStream_t st) {
+            void* out, int out_cols, const void* d, float alpha, float beta, int* counter, cudaStream_t st) {
   constexpr int BN = 256;
   LinearProblem pr{};
+  pr.tile_counter = counter;  // zeroed: tiles of ragged members are claimed dynamically
   pr.mode = MODE;
   pr.P = ma.P;
   pr.ns_rows = ma.rows;
@@ -282,15 +287,16 @@ int ns_gemm(const MuonArgs& ma, int shape, const void* a_op, int a_cols, const v
   pr.out_cols = out_cols;
   pr.out_ld = out_cols;
   pr.out_ms = (long long)ma.R_s * out_cols;
-  pr.BM = 128;
+  using Cfg = Sm100Cfg<BN, MODE>;
+  pr.BM = Cfg::TILE_M;
   pr.BN = BN;
-  pr.m_tiles = ma.R_s / 128;
+  pr.m_tiles = (ma.R_s + Cfg::TILE_M - 1) / Cfg::TILE_M;
   pr.n_tiles = (out_cols + BN - 1) / BN;
   CUtensorMap mapA, mapB;
   int rc;
-  if ((rc = make_map(&mapA, a_op, a_cols, ma.R_s, ma.P, 64, 128))) return rc;
+  if ((rc = make_map(&mapA, a_op, a_cols, ma.R_s, ma.P, 64, Cfg::BM))) return rc;
   if (MODE == MODE_NS) {
-    if ((rc = make_map(&mapB, b_op, b_cols, ma.R_s, ma.P, 64, BN))) return rc;
+    if ((rc = make_map(&mapB, b_op, b_cols, ma.R_s, ma.P, 64, Cfg::B_ROWS))) return rc;
   } else {
     if ((rc = make_map(&mapB, b_op, b_cols, ma.R_s, ma.P, 64, 64))) return rc;
   }
@@ -575,10 +581,23 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
   void* X = x0;
   void* Xn = x1;
   int rc;
+  // one zeroed tile counter per Newton-Schulz launch (the block is re-zeroed when it wraps;
+  // stream order keeps the earlier launches' use of a counter before its memset)
+  int* counters = reinterpret_cast<int*>(ws + L.off_counter);
+  int launch = 0;
+  auto counter = [&]() -> int* {
+    if (launch % MUON_COUNTERS == 0 && cudaMemsetAsync(counters, 0, MUON_COUNTERS * 4, st) != cudaSuccess)
+      return nullptr;
+    return counters + (launch++ % MUON_COUNTERS);
+  };
   for (int it = 0; it < a->ns_steps; ++it) {
-    if ((rc = ns_gemm<MODE_NS>(m, 1, X, L.C_s, X, L.C_s, A, L.R_s, nullptr, 1.0f, 0.0f, st))) return rc;
-    if ((rc = ns_gemm<MODE_NS>(m, 2, A, L.R_s, A, L.R_s, Bm, L.R_s, A, cc, cb, st))) return rc;
-    if ((rc = ns_gemm<MODE_NS_BMN>(m, 3, Bm, L.R_s, X, L.C_s, Xn, L.C_s, X, 1.0f, ca, st))) return rc;
+    int* c1 = counter();
+    int* c2 = counter();
+    int* c3 = counter();
+    if (!c1 || !c2 || !c3) return fail(TP_ECUDA, "cudaMemsetAsync of the tile counters failed");
+    if ((rc = ns_gemm<MODE_NS>(m, 1, X, L.C_s, X, L.C_s, A, L.R_s, nullptr, 1.0f, 0.0f, c1, st))) return rc;
+    if ((rc = ns_gemm<MODE_NS>(m, 2, A, L.R_s, A, L.R_s, Bm, L.R_s, A, cc, cb, c2, st))) return rc;
+    if ((rc = ns_gemm<MODE_NS_BMN>(m, 3, Bm, L.R_s, X, L.C_s, Xn, L.C_s, X, 1.0f, ca, c3, st))) return rc;
     std::swap(X, Xn);
   }
   m.x = reinterpret_cast<__nv_bfloat16*>(X);
