@@ -579,6 +579,14 @@ def run_train(args) -> None:
                 dropout=float(rng.uniform(0, 0.5))) for _ in range(P)]
     model = dict(n_numerical_features=n_num, categorical_cardinalities=cards, d_out=1, max_d_block=1024,
                  max_n_blocks=4)
+    if args.embeddings == 'cosine':
+        # the reference's default model: cosine numerical embeddings of per-member size
+        from tabpack_b200.nn import CosineEmbeddingsPack
+
+        model['numerical_embeddings'] = {'type': CosineEmbeddingsPack, 'max_d_embedding': 32}
+        for pm in per:
+            pm['numerical_embeddings'] = {'d_embedding': int(rng.integers(8, 33)),
+                                          'init_scale': float(np.exp(rng.uniform(np.log(0.01), np.log(1.0))))}
     trainer = PackTrainer(n_members=P, model=model, per_member_model=per,
                           optimizer=dict(type='muon', adamw_lr=1e-3, weight_decay=1e-5, muon_lr=2e-2),
                           loss='bce', seed=0, device=dev, autocast_bf16=True, member_range=(0, P))
@@ -600,7 +608,8 @@ def run_train(args) -> None:
         'unit': 'member-samples/s', 'n_gpus': 1, 'steps': steps, 'warmup': args.warmup, 'ms_per_step': ms,
         'higher_is_better': True, 'dtype': 'bf16', 'data': 'synthetic',
         'config': {'workload': f'{P} members, depth U{{1..4}}, width U{{128..1024}}, 100 numerical + 10 categorical '
-                               f'(sum of cardinalities {sum(cards)}), batch 1024, Muon + AdamW, bf16',
+                               f'(sum of cardinalities {sum(cards)}), batch 1024, Muon + AdamW, bf16'
+                               + (', cosine numerical embeddings d U{8..32}' if args.embeddings == 'cosine' else ''),
                    'mean_train_loss': float(loss.mean())},
         'clocks': clocks.summary()}), flush=True)
 
@@ -619,6 +628,8 @@ def main() -> None:
     ap.add_argument('--workload', choices=['layer', 'optimizer', 'metrics', 'train'], default='layer',
                     help='layer: the packed-block fwd+bwd benchmark (default); optimizer: grouped Muon step; '
                          'metrics: validation metrics, ROC AUC and greedy selection')
+    ap.add_argument('--embeddings', choices=['none', 'cosine'], default='none',
+                    help='train workload: numerical features raw or through cosine embeddings')
     args = ap.parse_args()
     if args.members is None:
         args.members = {'optimizer': 1024, 'metrics': 512, 'train': 512}.get(args.workload, MEMBERS)
