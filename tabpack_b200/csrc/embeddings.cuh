@@ -171,8 +171,8 @@ namespace tp {
 // followed by the one-hot encoding of each categorical feature (_OneHotEncoding,
 // src/tabpackage/nn.py:1836-1871: value `card` is the unknown category and encodes as
 // zeros), converted to the first layer's dtype and zero-padded to out_ld, in one pass.
-// A warp writes one row, 16 bytes (8 bf16 or 4 fp32 values) per lane and store; each
-// 16-byte piece checks which features' one-hot columns fall inside it.
+// A warp writes one row: the numerical values and zeros as 16-byte stores (8 bf16 or 4 fp32
+// values per lane and store), then one store per categorical feature for its 1.
 // ---------------------------------------------------------------------------
 struct InputArgs {
   long long rows;
@@ -190,39 +190,12 @@ __global__ void __launch_bounds__(256) tabpack_input_kernel(const InputArgs a) {
   const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= a.rows) return;
+  // pass 1: numerical columns and zeros, 16-byte stores
   const float* xr = a.x_num ? a.x_num + row * a.n_num : nullptr;
-  const int64_t* cr = a.x_cat ? a.x_cat + row * a.n_cat : nullptr;
-  const int total = a.n_cat > 0 ? a.offsets[a.n_cat] : 0;
   for (int c0 = lane * V; c0 < a.out_ld; c0 += 32 * V) {
     float val[V];
 #pragma unroll
-    for (int e = 0; e < V; ++e) {
-      const int c = c0 + e;
-      val[e] = (xr != nullptr && c < a.n_num) ? xr[c] : 0.0f;
-    }
-    // one-hot columns [lo, hi) of this piece, relative to the first one-hot column
-    const int lo = max(c0 - a.n_num, 0), hi = min(c0 + V - a.n_num, total);
-    if (cr != nullptr && lo < hi) {
-      // first feature whose block ends after lo (offsets are increasing)
-      int f0 = 0, f1 = a.n_cat - 1;
-      while (f0 < f1) {
-        const int mid = (f0 + f1) >> 1;
-        if (a.offsets[mid + 1] <= lo)
-          f0 = mid + 1;
-        else
-          f1 = mid;
-      }
-      for (int f = f0; f < a.n_cat && a.offsets[f] < hi; ++f) {
-        const int64_t v = cr[f];
-        const int start = a.offsets[f], card = a.offsets[f + 1] - start;
-        if (v >= 0 && v < card) {  // the unknown category `card` stays all zeros
-          const int col = a.n_num + start + (int)v;
-#pragma unroll
-          for (int e = 0; e < V; ++e)
-            if (col == c0 + e) val[e] = 1.0f;
-        }
-      }
-    }
+    for (int e = 0; e < V; ++e) val[e] = (xr != nullptr && c0 + e < a.n_num) ? xr[c0 + e] : 0.0f;
     if (BF16) {
       uint4 u;
       u.x = pack_bf16x2(val[0], val[1]);
@@ -234,6 +207,19 @@ __global__ void __launch_bounds__(256) tabpack_input_kernel(const InputArgs a) {
       *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + row * a.out_ld + c0) =
           make_float4(val[0], val[1], val[2], val[3]);
     }
+  }
+  // pass 2: one 1 per categorical feature (the warp's stores above precede it)
+  __syncwarp();
+  if (a.x_cat == nullptr) return;
+  for (int f = lane; f < a.n_cat; f += 32) {
+    const int64_t v = a.x_cat[row * a.n_cat + f];
+    const int start = a.offsets[f], card = a.offsets[f + 1] - start;
+    if (v < 0 || v >= card) continue;  // the unknown category `card` stays all zeros
+    const size_t o = row * a.out_ld + a.n_num + start + (int)v;
+    if (BF16)
+      reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(1.0f);
+    else
+      reinterpret_cast<float*>(a.out)[o] = 1.0f;
   }
 }
 

@@ -745,12 +745,12 @@ int tp_softmax_rows(const float* x, int64_t rows, int32_t C, float* out, void* s
   return TP_OK;
 }
 
-// Row segments of the embedding backward: enough blocks for two waves of 148 SMs, at least
-// 64 rows per segment.
+// Row segments of the embedding backward: enough blocks to fill 148 SMs (16 blocks of 128
+// threads each), at least 64 rows per segment.
 static int cos_emb_segments(int P, int B, int F, int D) {
   const long long cols = ((long long)F * D + COS_EMB_THREADS - 1) / COS_EMB_THREADS;
   const long long base = cols * P;
-  long long s = (296 + base - 1) / base;
+  long long s = (148 * 16 + base - 1) / base;
   s = std::min<long long>(s, (B + 63) / 64);
   return (int)std::max<long long>(1, s);
 }
