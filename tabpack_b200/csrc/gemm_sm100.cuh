@@ -57,16 +57,21 @@ struct Sm100Cfg {
 // output row: (acc + b) * scale as one fma with the staged b * scale, ReLU (which commutes
 // with the positive scale), Philox keep mask, bf16 pack into 32 bytes of the row's staging
 // slot.  The chunk's two Philox chains are independent and interleave.
-__device__ __forceinline__ void epi_fwd16(const LinearProblem& pr, int m, int row, int col0, const uint32_t (&r)[16],
-                                          int nv, bool drop, uint32_t thr, float scale, const float* sbias,
-                                          uint8_t* stage) {
-  uint4 q2[2];
+// The chunk's two Philox draws (independent of the accumulator: computed while its TMEM load
+// is in flight).
+__device__ __forceinline__ void fwd16_draws(const LinearProblem& pr, int m, int row, int col0, bool drop,
+                                            uint4 (&q2)[2]) {
   if (drop) {
 #pragma unroll
     for (int g = 0; g < 2; ++g)
       q2[g] = philox4x32_10_ks(
           make_uint4((uint32_t)(col0 >> 3) + g, (uint32_t)row, pr.member_base + (uint32_t)m, pr.offset), pr.ks);
   }
+}
+
+__device__ __forceinline__ void epi_fwd16(const LinearProblem& pr, const uint32_t (&r)[16], const uint4 (&q2)[2],
+                                          int nv, bool drop, uint32_t thr, float scale, const float* sbias,
+                                          uint8_t* stage) {
 #pragma unroll
   for (int g = 0; g < 2; ++g) {
     const int gv = nv - 8 * g;  // valid columns in this group of 8
@@ -616,9 +621,11 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
           for (int c = 0; c < n16; ++c) {
             const int col0 = cbase + 16 * c;
             tmem_ld_32x32b_x16(t_row + (uint32_t)(16 * c), fa);
-            tmem_wait_ld();
             const int nv = ti.n_valid - col0;
-            epi_fwd16(pr, m, row, col0, fa, nv, drop && nv > 0, thr, scale, sbias + 16 * c, stage_row + 32 * (c & 1));
+            uint4 q2[2];
+            fwd16_draws(pr, m, row, col0, drop && nv > 0, q2);
+            tmem_wait_ld();
+            epi_fwd16(pr, fa, q2, nv, drop && nv > 0, thr, scale, sbias + 16 * c, stage_row + 32 * (c & 1));
             if (c & 1) {
               __syncwarp();
               stage_flush(pr, m, row_base, col0 - 16, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
