@@ -300,13 +300,16 @@ size_t tp_cos_emb_workspace_size(int32_t P, int32_t B, int32_t F, int32_t D);
  * category and encodes as zeros; torch.cat of both parts, nn.py:2071-2107), converted to
  * out_dtype, then zeros up to out_ld.  cat_offsets: (n_cat + 1,) device int32 prefix sums of
  * the cardinalities.  out_ld must be a multiple of 8 (bf16) or 4 (fp32) and at least
- * n_num + cat_offsets[n_cat]. */
+ * n_num + cat_offsets[n_cat].  With row_index, output row r is built from dataset row
+ * row_index[r]: the per-step batch gather of the training loop (`v[batch_idx]`,
+ * src/tabpackage/_training.py:2667-2669) without materialising the gathered batch. */
 typedef struct tp_input_args {
   int64_t rows;
   int32_t n_num;
   int32_t n_cat;
-  const float* x_num;            /* (rows, n_num) or NULL */
-  const int64_t* x_cat;          /* (rows, n_cat) or NULL */
+  const float* x_num;            /* (rows, n_num), or (dataset rows, n_num) with row_index; or NULL */
+  const int64_t* x_cat;          /* (rows, n_cat), or (dataset rows, n_cat) with row_index; or NULL */
+  const int64_t* row_index;      /* (rows,) dataset row of each output row, or NULL */
   const int32_t* cat_offsets;    /* (n_cat + 1,) */
   void* out;                     /* (rows, out_ld) */
   int32_t out_ld;

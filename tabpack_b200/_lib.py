@@ -97,7 +97,8 @@ class CosEmbArgs(ctypes.Structure):
 class InputArgs(ctypes.Structure):
     _fields_ = [
         ('rows', ctypes.c_int64), ('n_num', ctypes.c_int32), ('n_cat', ctypes.c_int32), ('x_num', ctypes.c_void_p),
-        ('x_cat', ctypes.c_void_p), ('cat_offsets', ctypes.c_void_p), ('out', ctypes.c_void_p),
+        ('x_cat', ctypes.c_void_p), ('row_index', ctypes.c_void_p), ('cat_offsets', ctypes.c_void_p),
+        ('out', ctypes.c_void_p),
         ('out_ld', ctypes.c_int32), ('out_dtype', ctypes.c_int32),
     ]
 

@@ -179,6 +179,7 @@ struct InputArgs {
   int n_num, n_cat;
   const float* x_num;       // (rows, n_num) or nullptr
   const int64_t* x_cat;     // (rows, n_cat) or nullptr
+  const int64_t* row_index; // (rows,) source row of each output row, or nullptr
   const int32_t* offsets;   // (n_cat + 1,): first one-hot column of each feature (relative to n_num), total last
   void* out;                // (rows, out_ld)
   int out_ld, out_bf16;
@@ -190,8 +191,9 @@ __global__ void __launch_bounds__(256) tabpack_input_kernel(const InputArgs a) {
   const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= a.rows) return;
+  const long long src = a.row_index ? a.row_index[row] : row;  // the batch gather
   // pass 1: numerical columns and zeros, 16-byte stores
-  const float* xr = a.x_num ? a.x_num + row * a.n_num : nullptr;
+  const float* xr = a.x_num ? a.x_num + src * a.n_num : nullptr;
   for (int c0 = lane * V; c0 < a.out_ld; c0 += 32 * V) {
     float val[V];
 #pragma unroll
@@ -212,7 +214,7 @@ __global__ void __launch_bounds__(256) tabpack_input_kernel(const InputArgs a) {
   __syncwarp();
   if (a.x_cat == nullptr) return;
   for (int f = lane; f < a.n_cat; f += 32) {
-    const int64_t v = a.x_cat[row * a.n_cat + f];
+    const int64_t v = a.x_cat[src * a.n_cat + f];
     const int start = a.offsets[f], card = a.offsets[f + 1] - start;
     if (v < 0 || v >= card) continue;  // the unknown category `card` stays all zeros
     const size_t o = row * a.out_ld + a.n_num + start + (int)v;

@@ -805,8 +805,8 @@ int tp_tabpack_input(const tp_input_args* a, void* stream) {
   if (a->out_ld % (bf16 ? 8 : 4) != 0 || a->out_ld < a->n_num)
     return fail(TP_EINVAL, "out_ld must be a multiple of %d covering the columns", bf16 ? 8 : 4);
   if (!aligned16(a->out)) return fail(TP_EALIGN, "out must be 16-byte aligned");
-  InputArgs k{a->rows, a->n_num, a->n_cat, a->n_num > 0 ? a->x_num : nullptr, a->n_cat > 0 ? a->x_cat : nullptr,
-              a->cat_offsets, a->out, a->out_ld, bf16 ? 1 : 0};
+  InputArgs k{a->rows,     a->n_num,   a->n_cat, a->n_num > 0 ? a->x_num : nullptr, a->n_cat > 0 ? a->x_cat : nullptr,
+              a->row_index, a->cat_offsets, a->out, a->out_ld, bf16 ? 1 : 0};
   const long long blocks = (a->rows + 7) / 8;
   if (blocks > 0x7FFFFFFFLL) return fail(TP_EINVAL, "too many rows");
   cudaStream_t st = static_cast<cudaStream_t>(stream);

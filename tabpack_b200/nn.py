@@ -908,13 +908,18 @@ class TabPack(ModulePack):
     def pack_size(self) -> int:
         return self.backbone.pack_size
 
-    def _fused_input(self, x_num: Tensor | None, x_cat: Tensor) -> Tensor | None:
+    def _fused_input(self, x_num: Tensor | None, x_cat: Tensor, row_index: Tensor | None = None) -> Tensor | None:
         """[x_num | one-hot(x_cat)] built by one kernel in the first layer's dtype (already
         padded to the tensor-core width), or None when the generic path has to run (input
-        gradients, numerical embeddings, CPU tensors, an fp32 width the kernel cannot pad)."""
+        gradients, numerical embeddings, CPU tensors, an fp32 width the kernel cannot pad).
+        With `row_index`, x_num / x_cat are whole datasets and the rows are gathered too."""
         if self.num_module is not None or self.cat_module is None or not x_cat.is_cuda:
             return None
-        if x_num is not None and (x_num.requires_grad or not x_num.is_cuda or x_num.shape[:-1] != x_cat.shape[:-1]
+        if row_index is not None and (not row_index.is_cuda or x_cat.ndim != 2
+                                      or (x_num is not None and (x_num.ndim != 2 or x_num.shape[0] != x_cat.shape[0]))):
+            return None
+        lead_ok = row_index is not None or x_num is None or x_num.shape[:-1] == x_cat.shape[:-1]
+        if x_num is not None and (x_num.requires_grad or not x_num.is_cuda or not lead_ok
                                   or x_num.shape[-1] != self._n_numerical_features):
             return None
         if x_cat.shape[-1] != len(self._categorical_cardinalities):
@@ -930,7 +935,19 @@ class TabPack(ModulePack):
             width = d_in
         else:
             return None
-        return ops.tabpack_input(x_num, x_cat, self._cat_offsets, width, dtype)
+        return ops.tabpack_input(x_num, x_cat, self._cat_offsets, width, dtype, row_index=row_index)
+
+    def forward_rows(self, x_num: Tensor | None, x_cat: Tensor | None, row_index: Tensor,
+                     pack_idx: Tensor | None = None) -> Tensor:
+        """`forward(x_num[row_index], x_cat[row_index])`: the per-step batch gather of the
+        training loop (`_training.py:2667-2669`), fused into the first-layer input build when
+        the model has one-hot features and no numerical embeddings (otherwise gathered first).
+        `row_index`: (pack_size, batch) dataset rows of every member."""
+        fused = None if x_cat is None else self._fused_input(x_num, x_cat, row_index)
+        if fused is None:
+            return self(None if x_num is None else x_num[row_index], None if x_cat is None else x_cat[row_index],
+                        pack_idx)
+        return self.output(self.backbone(fused, pack_idx), pack_idx)
 
     def replace(self, *, pack_idx: Tensor, numerical_embeddings=None, d_block=None, **kwargs) -> None:
         """`TabPack.replace` (`nn.py:1986-2024`)."""

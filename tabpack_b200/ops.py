@@ -374,17 +374,20 @@ def cos_emb_backward(x: Tensor, weight: Tensor, bias: Tensor, affine_weight: Ten
 
 
 def tabpack_input(x_num: Tensor | None, x_cat: Tensor | None, cat_offsets: Tensor, width: int,
-                  dtype: torch.dtype) -> Tensor:
+                  dtype: torch.dtype, row_index: Tensor | None = None) -> Tensor:
     """[x_num | one-hot(x_cat)] in `dtype`, zero-padded to `width` columns; leading dimensions
-    of the inputs are kept; see `tp_tabpack_input`."""
+    of the inputs are kept, or with `row_index` (any shape, int64) output row r is built from
+    dataset row row_index[r] and the output takes row_index's shape; see `tp_tabpack_input`."""
     ref = x_num if x_num is not None else x_cat
-    lead = ref.shape[:-1]
-    rows = ref[..., 0].numel()
+    ri = None if row_index is None else _cuda('row_index', row_index).to(torch.int64).contiguous()
+    lead = ref.shape[:-1] if ri is None else ri.shape
+    rows = ref[..., 0].numel() if ri is None else ri.numel()
     xn = None if x_num is None else _cuda('x_num', x_num).to(torch.float32).contiguous()
     xc = None if x_cat is None else _cuda('x_cat', x_cat).to(torch.int64).contiguous()
     out = torch.empty(*lead, width, dtype=dtype, device=ref.device)
     a = _lib.InputArgs(rows=rows, n_num=0 if xn is None else xn.shape[-1], n_cat=0 if xc is None else xc.shape[-1],
-                       x_num=_ptr(xn), x_cat=_ptr(xc), cat_offsets=cat_offsets.data_ptr(), out=out.data_ptr(),
+                       x_num=_ptr(xn), x_cat=_ptr(xc), row_index=_ptr(ri), cat_offsets=cat_offsets.data_ptr(),
+                       out=out.data_ptr(),
                        out_ld=width, out_dtype=TP_DTYPE_BF16 if dtype == torch.bfloat16 else TP_DTYPE_F32)
     check(load().tp_tabpack_input(ctypes.byref(a), _stream()), 'tp_tabpack_input')
     return out

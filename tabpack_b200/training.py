@@ -186,11 +186,10 @@ class PackTrainer:
         total = torch.zeros(self.hi - self.lo, device=self.device)
         steps = 0
         for idx in self._batches(n, batch_size, epoch):
-            xn = data['x_num'][idx] if 'x_num' in data else None
-            xc = data['x_cat'][idx] if 'x_cat' in data else None
             y = data['y'][idx]
             with torch.autocast('cuda', dtype=torch.bfloat16, enabled=self.autocast):
-                out = self.model(xn, xc)
+                # the batch gather runs inside the first-layer input build where it can
+                out = self.model.forward_rows(data.get('x_num'), data.get('x_cat'), idx)
             losses = member_loss(self.loss, out.float(), y)
             losses.sum().backward()
             self.opt.step()

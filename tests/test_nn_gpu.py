@@ -125,3 +125,27 @@ def test_fused_first_layer_input_matches_one_hot_concat(dtype, shared):
     want = torch.nn.functional.pad(torch.cat([x_num, oh.float()], -1), (0, width - d_in)).to(dtype)
     assert got.shape == want.shape and got.dtype == dtype
     assert torch.equal(got, want)
+
+
+def test_forward_rows_equals_gathered_forward():
+    """TabPack.forward_rows (batch gather fused into the first-layer input) gives the same
+    output as gathering the batch first, in training mode with dropout."""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+    from tabpack_b200 import nn as bnn
+
+    torch.manual_seed(0)
+    P, N, B = 4, 500, 64
+    model = bnn.TabPack(n_numerical_features=6, categorical_cardinalities=[5, 3, 11], d_out=2, n_blocks=[1, 2, 3, 2],
+                        d_block=[32, 16, 48, 24], dropout=[0.1, 0.2, 0.0, 0.3], pack_size=P, max_d_block=48).cuda().train()
+    g = torch.Generator(device='cuda').manual_seed(1)
+    x_num = torch.randn(N, 6, device='cuda', generator=g)
+    x_cat = torch.stack([torch.randint(0, c + 1, (N,), device='cuda', generator=g) for c in (5, 3, 11)], 1)
+    idx = torch.randint(0, N, (P, B), device='cuda', generator=g)
+    for autocast in (False, True):
+        with torch.autocast('cuda', dtype=torch.bfloat16, enabled=autocast):
+            model.backbone._stream.seed, model.backbone._stream.calls = 7, 0
+            a = model.forward_rows(x_num, x_cat, idx)
+            model.backbone._stream.seed, model.backbone._stream.calls = 7, 0  # the same dropout masks
+            b = model(x_num[idx], x_cat[idx])
+        assert torch.equal(a, b), autocast
