@@ -1,20 +1,22 @@
-// Persistent, warp-specialised ragged grouped GEMM for the packed linear layer on
-// sm_100a: TMA (one destination CTA per load) fills a ring of shared-memory stages, one thread
-// issues tcgen05.mma into a double-buffered TMEM accumulator, and the epilogue
-// warps drain TMEM with tcgen05.ld, apply the fused epilogue and store.
+// Persistent, warp-specialised ragged grouped GEMM for the packed linear layer and the
+// Newton-Schulz iterations of Muon on sm_100a: TMA (one destination CTA per load) fills a ring
+// of shared-memory stages, one thread issues tcgen05.mma into a double-buffered TMEM
+// accumulator, and the epilogue warps drain TMEM with tcgen05.ld, apply the fused epilogue
+// and store.
 //
-//   MODE_FWD  : C[B x out_m]  = X[B x in_m]  * W^T          A K-major, B K-major
-//   MODE_DGRAD: C[B x in_m]   = G[B x out_m] * W            A K-major, B MN-major
-//   MODE_WGRAD: C[out_m x in_m] = G^T * X  (K = batch rows)  A MN-major, B MN-major
-//   MODE_WGRAD_T: C^T[in_m x out_m] = X^T * G, stored into C (K = batch rows), A and B
-//               MN-major; a warp's 32 lanes hold 32 consecutive input features, so each
-//               output feature's column is one coalesced 128-byte fp32 store
+//   MODE_FWD    : C[B x out_m] = X[B x in_m] * W^T, + bias, ReLU, Philox dropout; A, B K-major
+//   MODE_DGRAD  : C[B x in_m] = G[B x out_m] * W; A K-major, B MN-major; CTA pairs
+//   MODE_WGRAD_T: C^T[in_m x out_m] = X^T * G stored into C (K = batch rows), A and B MN-major;
+//                 a warp's 32 lanes hold 32 consecutive input features, so each output
+//                 feature's column is one coalesced 128-byte fp32 store; CTA pairs
+//   MODE_NS / MODE_NS_BMN: C = alpha * A B^T + beta * D over each member's r x (r|c) block
+//                 (B K-major / MN-major); tiles claimed dynamically
 //
-// Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer, warps 2.. =
-// epilogue (warp w reads TMEM lanes 32*(w%4) .. +31 and column slice (w-2)/4).  The
-// forward runs 16 epilogue warps (four per SM sub-partition: its bias + ReLU + Philox
-// epilogue is latency-bound, so four warps per scheduler hide each other's dependency
-// stalls) over a 3-stage ring; the other modes run 8 epilogue warps over 4 stages.
+// Warp roles: warp 0 = TMA producer (and, with a tile counter, the tile claimer), warp 1 =
+// TMEM owner + MMA issuer, warps 2.. = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31 and
+// column slice (w-2)/4).  The forward runs 16 epilogue warps (four per SM sub-partition: its
+// bias + ReLU + Philox epilogue is latency-bound, so four warps per scheduler hide each
+// other's dependency stalls) over a 3-stage ring; the other modes run 8 epilogue warps.
 #pragma once
 
 #include "linear_problem.cuh"
@@ -34,8 +36,8 @@ struct Sm100Cfg {
   static constexpr bool PAIR = (MODE == MODE_DGRAD || MODE == MODE_WGRAD_T) && BN_ == 256;
   static constexpr int TILE_M = PAIR ? 2 * BM : BM;
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B columns staged per CTA
-  static constexpr bool A_MN = (MODE == MODE_WGRAD || MODE == MODE_WGRAD_T);
-  static constexpr bool B_MN = (MODE == MODE_DGRAD || MODE == MODE_WGRAD || MODE == MODE_WGRAD_T || MODE == MODE_NS_BMN);
+  static constexpr bool A_MN = (MODE == MODE_WGRAD_T);
+  static constexpr bool B_MN = (MODE == MODE_DGRAD || MODE == MODE_WGRAD_T || MODE == MODE_NS_BMN);
   static constexpr int STAGES = PAIR ? 6 : (BN == 256) ? (MODE == MODE_FWD ? 3 : 4) : 6;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = B_ROWS * BK * 2;
@@ -132,79 +134,22 @@ __device__ __forceinline__ void ns_chunk(const LinearProblem& pr, bool rv, int n
   }
 }
 
-// Epilogue of one 32-column chunk of one output row held in registers `r`
-// (raw fp32 accumulator bits from tcgen05.ld).
-template <int MODE>
-__device__ __forceinline__ void epi_chunk(const LinearProblem& pr, const TileInfo& ti, int m, int row, int col0,
-                                          const uint32_t (&r)[32], bool dropout_on, uint32_t thr, float scale,
-                                          const float* sbias, uint8_t* stage, float* wg_out = nullptr) {
+// dgrad epilogue of one 32-column chunk of one output row held in registers `r` (raw fp32
+// accumulator bits from tcgen05.ld): bf16 into the row's staging slot, zeros beyond the
+// member's columns.
+__device__ __forceinline__ void dgrad_chunk(const TileInfo& ti, int col0, const uint32_t (&r)[32], uint8_t* stage) {
   const int nv = ti.n_valid - col0;  // valid columns in this chunk (may be <= 0)
-  float v[32];
-  if (MODE == MODE_NS || MODE == MODE_NS_BMN) {
-    // alpha * acc + beta * D inside the member's r x (r|c) block, exact zeros around it
-    const bool rv = row < ti.m_valid;
-    const __nv_bfloat16* dp = pr.D ? reinterpret_cast<const __nv_bfloat16*>(pr.D) + (size_t)m * pr.out_ms +
-                                         (size_t)row * pr.out_ld + col0
-                                   : nullptr;
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      float d[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      if (dp != nullptr && rv && j < nv) {
-        const uint4 u = *reinterpret_cast<const uint4*>(dp + j);
-        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+  for (int j = 0; j < 32; j += 8) {
+    float v[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) d[e] = __bfloat162float(h[e]);
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        v[j + e] = (rv && j + e < nv) ? pr.alpha * __uint_as_float(r[j + e]) + pr.beta * d[e] : 0.0f;
-    }
-  } else if (MODE == MODE_DGRAD) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = j < nv ? __uint_as_float(r[j]) : 0.0f;
-  } else {
-    const bool rv = row < ti.m_valid;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = (rv && j < nv) ? __uint_as_float(r[j]) : 0.0f;
-  }
-  if (MODE == MODE_WGRAD) {
-    // fp32: the caller flushes the chunk in two 16-column halves through the staging tile
-#pragma unroll
-    for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(wg_out + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      uint4 u;
-      u.x = pack_bf16x2(v[j], v[j + 1]);
-      u.y = pack_bf16x2(v[j + 2], v[j + 3]);
-      u.z = pack_bf16x2(v[j + 4], v[j + 5]);
-      u.w = pack_bf16x2(v[j + 6], v[j + 7]);
-      *reinterpret_cast<uint4*>(stage + j * 2) = u;
-    }
-  }
-}
-
-// Writes a warp's 32 x 16 fp32 half-chunk (row r's 64 bytes at stage_warp + r * row_bytes)
-// to columns col0.. of the fp32 output, 4 lanes per row.
-__device__ __forceinline__ void stage_flush_f32(const LinearProblem& pr, int m, int row_base, int col0,
-                                                const uint8_t* stage_warp, int lane, int row_bytes) {
-  const int c = lane & 3;
-  float* base = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms;
-  const bool vec = (pr.out_ld & 3) == 0 && col0 + 4 * c + 4 <= pr.out_cols;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int r = (lane >> 2) + 8 * k;
-    const int grow = row_base + r;
-    if (grow >= pr.out_rows) continue;
-    const float4 v = *reinterpret_cast<const float4*>(stage_warp + r * row_bytes + c * 16);
-    float* d = base + (size_t)grow * pr.out_ld + col0 + 4 * c;
-    if (vec) {
-      *reinterpret_cast<float4*>(d) = v;
-    } else {
-      const float e[4] = {v.x, v.y, v.z, v.w};
-      for (int j = 0; j < 4; ++j)
-        if (col0 + 4 * c + j < pr.out_cols) d[j] = e[j];
-    }
+    for (int e = 0; e < 8; ++e) v[e] = j + e < nv ? __uint_as_float(r[j + e]) : 0.0f;
+    uint4 u;
+    u.x = pack_bf16x2(v[0], v[1]);
+    u.y = pack_bf16x2(v[2], v[3]);
+    u.z = pack_bf16x2(v[4], v[5]);
+    u.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(stage + j * 2) = u;
   }
 }
 
@@ -341,7 +286,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
         const TileInfo ti = decode_tile(pr, t, Cfg::BK);
         if (ti.kind != KIND_MMA) continue;
         const int zA = ((MODE == MODE_FWD || MODE == MODE_WGRAD_T) && pr.x_shared) ? 0 : ti.member;  // NS operands are per member
-        const int zB = (MODE == MODE_WGRAD && pr.x_shared) ? 0 : ti.member;
+        const int zB = ti.member;
         // this CTA's A rows and B columns: in a pair the leader takes rows 0..127 and the
         // first half of the (trimmed) columns, the peer rows 128..255 and the second half
         const int a_row = ti.mt * Cfg::TILE_M + (int)rank * Cfg::BM;
@@ -542,27 +487,11 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
         // chunks of 32 columns that hold storable output (warp-uniform)
         const int nch = min(NCH, max(0, (pr.out_cols - cbase + 31) / 32));
         const int row_base = ti.mt * Cfg::TILE_M + (int)rank * Cfg::BM + q * 32;
-        auto emit_chunk = [&](int col0, const uint32_t(&rr)[32], const float* sb) {
-          if (MODE == MODE_WGRAD) {
-            float vals[32];
-            epi_chunk<MODE>(pr, ti, m, row, col0, rr, dropout_on, thr, scale, sb, nullptr, vals);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-#pragma unroll
-              for (int j = 0; j < 16; j += 4)
-                *reinterpret_cast<float4*>(stage_row + j * 4) =
-                    make_float4(vals[16 * h + j], vals[16 * h + j + 1], vals[16 * h + j + 2], vals[16 * h + j + 3]);
-              __syncwarp();
-              if (col0 + 16 * h < pr.out_cols)
-                stage_flush_f32(pr, m, row_base, col0 + 16 * h, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
-              __syncwarp();
-            }
-          } else {
-            epi_chunk<MODE>(pr, ti, m, row, col0, rr, dropout_on, thr, scale, sb, stage_row);
-            __syncwarp();
-            stage_flush(pr, m, row_base, col0, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
-            __syncwarp();
-          }
+        auto emit_chunk = [&](int col0, const uint32_t(&rr)[32]) {
+          dgrad_chunk(ti, col0, rr, stage_row);
+          __syncwarp();
+          stage_flush(pr, m, row_base, col0, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
+          __syncwarp();
         };
         if constexpr (MODE == MODE_NS || MODE == MODE_NS_BMN) {
           // the addend of chunk c + 1 is loaded while chunk c is computed
@@ -641,11 +570,11 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
         for (int c = 0; c < nch; c += 2) {
           tmem_wait_ld();
           if (c + 1 < nch) tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * (c + 1)), rb);
-          emit_chunk(cbase + 32 * c, ra, sbias + 32 * c);
+          emit_chunk(cbase + 32 * c, ra);
           if (c + 1 < nch) {
             tmem_wait_ld();
             if (c + 2 < nch) tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * (c + 2)), ra);
-            emit_chunk(cbase + 32 * (c + 1), rb, sbias + 32 * (c + 1));
+            emit_chunk(cbase + 32 * (c + 1), rb);
           }
         }
         }
@@ -670,22 +599,6 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
           const int o_end = min(cbase + WCOLS, pr.out_rows);
           if (i < pr.out_cols)
             for (int o = cbase; o < o_end; ++o) base[(size_t)o * pr.out_ld + i] = 0.0f;
-        } else if (MODE == MODE_WGRAD) {
-          float* base = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms;
-          const int ncol = c_end - cbase;
-          if ((pr.out_ld & 3) == 0 && (ncol & 3) == 0) {
-            const int nq = ncol / 4;
-            for (int i = lane; i < 32 * nq; i += 32) {
-              const int r = i / nq, cc = cbase + 4 * (i - r * nq);
-              if (row_base + r < pr.out_rows)
-                *reinterpret_cast<float4*>(base + (size_t)(row_base + r) * pr.out_ld + cc) = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-          } else {
-            for (int i = lane; i < 32 * ncol; i += 32) {
-              const int r = i / ncol, cc = cbase + (i - r * ncol);
-              if (row_base + r < pr.out_rows) base[(size_t)(row_base + r) * pr.out_ld + cc] = 0.0f;
-            }
-          }
         } else {
           __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms;
           const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(pr.copy_src) + (size_t)m * pr.out_ms;
