@@ -319,6 +319,29 @@ int tp_tabpack_input(const tp_input_args* a, void* stream);
 int tp_cos_emb_forward(const tp_cos_emb_args* a, void* stream);
 int tp_cos_emb_backward(const tp_cos_emb_args* a, void* stream);
 
+/* bf16 compute copy of an fp32 weight pack for the tensor-core GEMMs: the weight cast of
+ * torch.autocast at LinearPack.forward (src/tabpackage/nn.py:806-808, autocast region
+ * src/tabpackage/_training.py:161-167), done once per weight update and only over what the
+ * GEMMs read.  For every member m with n_blocks[m] > block_index (all members when n_blocks is
+ * NULL) and every row r < min(out_features[m], src_rows): dst[m, r, c] = bf16(src[m, r, c])
+ * (round to nearest even) for c < min(in_features[m], src_cols) and 0 for the other c <
+ * dst_cols.  Other rows of dst are left as they are: a caller that starts from a zeroed dst
+ * (or one written by an earlier call) hands the GEMMs finite values everywhere.  NULL widths
+ * mean the full source extent. */
+typedef struct tp_weight_cast_args {
+  int32_t P;
+  int32_t src_rows, src_cols;   /* fp32 source (P, src_rows, src_cols), contiguous */
+  int32_t dst_rows, dst_cols;   /* bf16 destination (P, dst_rows, dst_cols); dst_cols % 8 == 0,
+                                   dst_rows >= src_rows, dst_cols >= src_cols */
+  const int32_t* out_features;  /* device (P,) or NULL */
+  const int32_t* in_features;   /* device (P,) or NULL */
+  const int32_t* n_blocks;      /* device (P,) or NULL */
+  int32_t block_index;
+  const float* src;
+  void* dst;                    /* 16-byte aligned */
+} tp_weight_cast_args;
+int tp_weight_cast(const tp_weight_cast_args* a, void* stream);
+
 /* Clears and returns the device-side error flag (TP_OK or TP_ETIMEOUT). */
 int tp_device_error(void);
 

@@ -103,6 +103,15 @@ class InputArgs(ctypes.Structure):
     ]
 
 
+class WeightCastArgs(ctypes.Structure):
+    _fields_ = [
+        ('P', ctypes.c_int32), ('src_rows', ctypes.c_int32), ('src_cols', ctypes.c_int32),
+        ('dst_rows', ctypes.c_int32), ('dst_cols', ctypes.c_int32), ('out_features', ctypes.c_void_p),
+        ('in_features', ctypes.c_void_p), ('n_blocks', ctypes.c_void_p), ('block_index', ctypes.c_int32),
+        ('src', ctypes.c_void_p), ('dst', ctypes.c_void_p),
+    ]
+
+
 class GreedyArgs(ctypes.Structure):
     _fields_ = [
         ('metric', ctypes.c_int32), ('maximize', ctypes.c_int32), ('n_pred', ctypes.c_int32),
@@ -140,6 +149,7 @@ SIGNATURES = {
     'tp_cos_emb_forward': (ctypes.c_int, [ctypes.POINTER(CosEmbArgs), ctypes.c_void_p]),
     'tp_cos_emb_backward': (ctypes.c_int, [ctypes.POINTER(CosEmbArgs), ctypes.c_void_p]),
     'tp_tabpack_input': (ctypes.c_int, [ctypes.POINTER(InputArgs), ctypes.c_void_p]),
+    'tp_weight_cast': (ctypes.c_int, [ctypes.POINTER(WeightCastArgs), ctypes.c_void_p]),
     'tp_roc_auc_workspace_size': (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32]),
     'tp_binary_roc_auc': (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
                                          ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,

@@ -270,4 +270,47 @@ __global__ void __launch_bounds__(256) adamw_kernel(const AdamWTensors ts, const
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// bf16 compute copy of an fp32 weight pack: the cast autocast applies to the weight of
+// LinearPack.forward (src/tabpackage/nn.py:806-808 under _training.py:161-167), restricted to
+// what the grouped GEMMs read.  Member m's rows r < out_m get bf16(w) in the columns c < in_m
+// and zeros in [in_m, dst_cols); rows at or beyond out_m and depth-inactive members are not
+// written (the GEMMs read them only against exact zeros, so any finite contents do).  A warp
+// converts one row: 8 columns per lane, one 16-byte store.
+// ---------------------------------------------------------------------------
+struct WeightCastArgs {
+  int src_rows, src_cols, dst_rows, dst_cols;
+  const int32_t* out_f;
+  const int32_t* in_f;
+  const int32_t* n_blocks;
+  int block_index;
+  const float* src;
+  __nv_bfloat16* dst;
+};
+
+// Grid: (ceil(src_rows / 8), P), 256 threads.
+__global__ void __launch_bounds__(256) weight_cast_kernel(const WeightCastArgs a) {
+  const int m = blockIdx.y;
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (a.n_blocks != nullptr && __ldg(a.n_blocks + m) <= a.block_index) return;
+  const int rows = a.out_f != nullptr ? min(__ldg(a.out_f + m), a.src_rows) : a.src_rows;
+  if (r >= rows) return;
+  const int cols = a.in_f != nullptr ? min(__ldg(a.in_f + m), a.src_cols) : a.src_cols;
+  const float* s = a.src + ((size_t)m * a.src_rows + r) * a.src_cols;
+  __nv_bfloat16* d = a.dst + ((size_t)m * a.dst_rows + r) * a.dst_cols;
+  for (int c0 = lane * 8; c0 < a.dst_cols; c0 += 256) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = c0 + e < cols ? __ldg(s + c0 + e) : 0.0f;
+    uint4 u;
+    u.x = pack_bf16x2(v[0], v[1]);
+    u.y = pack_bf16x2(v[2], v[3]);
+    u.z = pack_bf16x2(v[4], v[5]);
+    u.w = pack_bf16x2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(d + c0) = u;
+  }
+}
+
 }  // namespace tp

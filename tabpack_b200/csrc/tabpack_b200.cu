@@ -902,6 +902,22 @@ int tp_dropout_mask(uint64_t seed, uint32_t offset, uint32_t member_base, const 
   return TP_OK;
 }
 
+int tp_weight_cast(const tp_weight_cast_args* a, void* stream) {
+  if (!a || a->P <= 0 || a->src_rows <= 0 || a->src_cols <= 0 || !a->src || !a->dst)
+    return fail(TP_EINVAL, "bad weight cast arguments");
+  if (a->dst_rows < a->src_rows || a->dst_cols < a->src_cols || a->dst_cols % 8 != 0)
+    return fail(TP_EINVAL, "destination (%d, %d) must cover the source (%d, %d) with a multiple of 8 columns",
+                a->dst_rows, a->dst_cols, a->src_rows, a->src_cols);
+  if (!aligned16(a->dst)) return fail(TP_EALIGN, "dst must be 16-byte aligned");
+  if (a->P > 65535) return fail(TP_EINVAL, "too many members for one call");
+  WeightCastArgs k{a->src_rows, a->src_cols, a->dst_rows, a->dst_cols, a->out_features, a->in_features,
+                   a->n_blocks, a->block_index, a->src, static_cast<__nv_bfloat16*>(a->dst)};
+  const dim3 grid((a->src_rows + 7) / 8, a->P);
+  weight_cast_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(k);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
 int tp_adamw_step(const tp_adamw_args* a, void* stream) {
   if (!a || a->n_tensors <= 0 || a->n_tensors > TP_MAX_OPT_TENSORS) return fail(TP_EINVAL, "bad tensor count");
   AdamWTensors ts{};

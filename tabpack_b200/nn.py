@@ -284,23 +284,46 @@ class _DropoutStream:
 
 
 class _WeightCache:
-    """bf16 copy of an fp32 weight pack, refreshed when the weight changes
-    (every optimizer step bumps the parameter's version counter)."""
+    """bf16 copy of an fp32 weight pack, refreshed when the weight changes (optimizer steps
+    and in-place updates bump the parameter's version counter).
+
+    With the layer's widths the copy comes from `tp_weight_cast`: one pass that reads only
+    each active member's rows and columns; the other rows of the copy keep earlier (finite)
+    contents, which the GEMMs only multiply by exact zeros.  The copy is refreshed in place
+    unless something else (a pending backward) still holds it."""
 
     def __init__(self) -> None:
         self.key = None
         self.value = None
 
-    def get(self, w: Tensor, dtype: torch.dtype, cols: int, rows: int | None = None) -> Tensor:
+    @staticmethod
+    def _tag(t):
+        return None if t is None else (t.data_ptr(), t._version, tuple(t.shape))
+
+    def get(self, w: Tensor, dtype: torch.dtype, cols: int, rows: int | None = None, widths=None) -> Tensor:
         rows = w.shape[-2] if rows is None else rows
         if w.dtype == dtype and w.shape[-1] == cols and w.shape[-2] == rows:
             return w.detach()
-        key = (w.data_ptr(), w._version, dtype, cols, rows, tuple(w.shape))
+        out_f, in_f, nb, bi = widths if widths is not None else (None, None, None, 0)
+        key = (w.data_ptr(), w._version, dtype, cols, rows, tuple(w.shape),
+               self._tag(out_f), self._tag(in_f), self._tag(nb), bi)
         if self.key != key:
-            wd = w.detach().to(dtype)
-            if cols != w.shape[-1] or rows != w.shape[-2]:
-                wd = nn.functional.pad(wd, (0, cols - w.shape[-1], 0, rows - w.shape[-2]))
-            self.value = wd.contiguous()
+            self.key = None
+            if dtype == torch.bfloat16 and w.dtype == torch.float32 and w.is_cuda and w.is_contiguous():
+                shape = (w.shape[0], rows, cols)
+                buf = self.value
+                use_count = getattr(buf, '_use_count', None)
+                if (buf is None or tuple(buf.shape) != shape or buf.dtype != dtype or buf.device != w.device
+                        or use_count is None or use_count() != 1):
+                    buf = torch.zeros(shape, dtype=dtype, device=w.device)
+                self.value = None
+                ops.weight_cast(w.detach(), buf, out_features=out_f, in_features=in_f, n_blocks=nb, block_index=bi)
+                self.value = buf
+            else:
+                wd = w.detach().to(dtype)
+                if cols != w.shape[-1] or rows != w.shape[-2]:
+                    wd = nn.functional.pad(wd, (0, cols - w.shape[-1], 0, rows - w.shape[-2]))
+                self.value = wd.contiguous()
             self.key = key
         return self.value
 
@@ -366,7 +389,8 @@ def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features
     # tensor cores over zero-padded weight rows and bias; the padded columns are sliced off
     max_out = weight.shape[-2]
     rows = _round8(max_out) if dtype == torch.bfloat16 else max_out
-    wc = (cache or _WeightCache()).get(weight, dtype, cols, rows)
+    wc = (cache or _WeightCache()).get(weight, dtype, cols, rows,
+                                       widths=(out_features, in_features, n_blocks, block_index))
     bc = bias
     if bias is not None and rows != max_out:
         bc = nn.functional.pad(bias.detach(), (0, rows - max_out))
@@ -380,6 +404,20 @@ def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features
 
 def _widths(buf: Tensor | None) -> Tensor | None:
     return None if buf is None else buf.to(torch.int32)
+
+
+def _widths_cached(module: nn.Module, name: str, buf: Tensor | None) -> Tensor | None:
+    """int32 copy of a width buffer, kept while the buffer is unchanged: one tensor per buffer
+    state, so caches may key on its identity."""
+    if buf is None:
+        return None
+    cache = module.__dict__.setdefault('_widths_i32', {})
+    key = (buf.data_ptr(), buf._version, buf.dtype, tuple(buf.shape))
+    hit = cache.get(name)
+    if hit is None or hit[0] != key:
+        hit = (key, buf.to(torch.int32))
+        cache[name] = hit
+    return hit[1]
 
 
 # >>> module packs
@@ -487,7 +525,11 @@ def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stre
         offset = stream.next_offset(offset_stride) + offset_add
     if getattr(linear, 'full_width_input', False):
         inf = None  # the whole padded input width takes part (first layer of a TabPack with embeddings)
-    return packed_linear(x, w, b, in_features=_widths(inf), out_features=_widths(outf), n_blocks=n_blocks,
+    if pack_idx is None:
+        inf, outf = _widths_cached(linear, 'in', inf), _widths_cached(linear, 'out', outf)
+    else:
+        inf, outf = _widths(inf), _widths(outf)
+    return packed_linear(x, w, b, in_features=inf, out_features=outf, n_blocks=n_blocks,
                          block_index=block_index, relu=relu, dropout_p=dropout, seed=seed, offset=offset,
                          member_base=member_base, cache=linear._cache if pack_idx is None else None)
 

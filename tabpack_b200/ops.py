@@ -11,6 +11,7 @@ import ctypes
 
 import torch
 from torch import Tensor
+from torch.autograd.graph import increment_version
 
 from tabpack_b200 import _lib
 from tabpack_b200._lib import TP_DTYPE_BF16, TP_DTYPE_F32, check, load
@@ -208,6 +209,9 @@ def adamw_step(params, grads, exp_avgs, exp_avg_sqs, *, steps=None, step: int = 
         a.lr, a.beta1, a.beta2, a.eps, a.weight_decay = (_hparam(v) for v in hp)
         a.step = int(step)
         check(load().tp_adamw_step(ctypes.byref(a), _stream()), 'tp_adamw_step')
+    # the kernel updated these in place: bump their version counters as torch's in-place ops do
+    # (caches keyed on a parameter's version, e.g. its bf16 copy, see the new values)
+    increment_version(list(params) + list(exp_avgs) + list(exp_avg_sqs))
 
 
 def muon_workspace_size(P: int, max_out: int, max_in: int) -> int:
@@ -237,6 +241,7 @@ def muon_step(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=
     a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     keep = (out_features, in_features, update_scale)  # noqa: F841  (alive until the launch is queued)
     check(load().tp_muon_step(ctypes.byref(a), _stream()), 'tp_muon_step')
+    increment_version([p, momentum_buffer] + ([grad] if mutate_grad else []))
 
 
 def metric_pack(metric: str, y_pred: Tensor, y_true: Tensor, classes: int = 1) -> Tensor:
@@ -391,6 +396,28 @@ def tabpack_input(x_num: Tensor | None, x_cat: Tensor | None, cat_offsets: Tenso
                        out_ld=width, out_dtype=TP_DTYPE_BF16 if dtype == torch.bfloat16 else TP_DTYPE_F32)
     check(load().tp_tabpack_input(ctypes.byref(a), _stream()), 'tp_tabpack_input')
     return out
+
+
+def weight_cast(src: Tensor, dst: Tensor, *, out_features: Tensor | None = None, in_features: Tensor | None = None,
+                n_blocks: Tensor | None = None, block_index: int = 0) -> Tensor:
+    """Write bf16(src) into `dst` (P, dst_rows, dst_cols) over each active member's rows
+    r < out_features[m], zero beyond in_features[m]; other rows of `dst` keep their contents
+    (see `tp_weight_cast`).  Returns `dst`."""
+    src = _cuda('src', src, torch.float32)
+    dst = _cuda('dst', dst, torch.bfloat16)
+    if not src.is_contiguous() or not dst.is_contiguous():
+        raise ValueError('weight_cast needs contiguous tensors')
+    P, R, C = src.shape
+    if dst.shape[0] != P:
+        raise ValueError('src and dst differ in their pack size')
+    outf, inf, nb = (_i32(n, t) for n, t in (('out_features', out_features), ('in_features', in_features),
+                                             ('n_blocks', n_blocks)))
+    a = _lib.WeightCastArgs(P=P, src_rows=R, src_cols=C, dst_rows=dst.shape[1], dst_cols=dst.shape[2],
+                            out_features=_ptr(outf), in_features=_ptr(inf), n_blocks=_ptr(nb),
+                            block_index=block_index, src=src.data_ptr(), dst=dst.data_ptr())
+    check(load().tp_weight_cast(ctypes.byref(a), _stream()), 'tp_weight_cast')
+    increment_version(dst)
+    return dst
 
 
 def binary_roc_auc(scores: Tensor, labels: Tensor, workspace: Tensor | None = None) -> Tensor:

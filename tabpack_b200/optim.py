@@ -156,7 +156,9 @@ def _adamw_group(opt: torch.optim.Optimizer, params, *, lr, beta1, beta2, eps, w
             st['exp_avg_sq'] = torch.zeros_like(p.data)
         st['step'] += 1
         key = 'tensor' if isinstance(st['step'], Tensor) else int(st['step'])
-        batches.setdefault(key, []).append((p.data, p.grad.data.contiguous(), st['exp_avg'], st['exp_avg_sq'],
+        # the parameter itself (not `.data`, whose version counter is separate): the launch bumps
+        # its version like an in-place update
+        batches.setdefault(key, []).append((p, p.grad.data.contiguous(), st['exp_avg'], st['exp_avg_sq'],
                                             st['step']))
     hp = dict(lr=_hp(lr), beta1=_hp(beta1), beta2=_hp(beta2), eps=_hp(eps), weight_decay=_hp(weight_decay))
     for key, items in batches.items():
@@ -300,7 +302,7 @@ class MuonAdamWPack(OptimizerPack):
         if not self._allow_inplace_grad_mutation:
             grad = grad.clone()
         scale = g.get('muon_update_scale')
-        ops.muon_step(p.data, grad, st['muon_momentum_buffer'], out_features=g.get('muon_out_features'),
+        ops.muon_step(p, grad, st['muon_momentum_buffer'], out_features=g.get('muon_out_features'),
                       in_features=g.get('muon_in_features'), lr=_hp(g['muon_lr']), momentum=_hp(g['muon_momentum']),
                       weight_decay=_hp(g['weight_decay']),
                       update_scale=None if scale is None else scale.to(torch.float32).contiguous(),

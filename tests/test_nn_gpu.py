@@ -149,3 +149,71 @@ def test_forward_rows_equals_gathered_forward():
             model.backbone._stream.seed, model.backbone._stream.calls = 7, 0  # the same dropout masks
             b = model(x_num[idx], x_cat[idx])
         assert torch.equal(a, b), autocast
+
+
+def test_weight_cast_writes_active_rows_only():
+    """tp_weight_cast: bf16 (round to nearest even, as torch's cast) over rows < out_features
+    of active members, zeros from in_features to the padded width; the other rows and the
+    depth-inactive members keep what the destination held."""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+    from tabpack_b200 import ops
+
+    g = torch.Generator(device='cuda').manual_seed(11)
+    P, R, C = 5, 70, 203
+    src = torch.randn(P, R, C, device='cuda', generator=g) * 3
+    outf = torch.tensor([70, 1, 33, 64, 17], dtype=torch.int32, device='cuda')
+    inf = torch.tensor([203, 5, 100, 8, 1], dtype=torch.int32, device='cuda')
+    nb = torch.tensor([2, 3, 1, 2, 2], dtype=torch.int32, device='cuda')  # member 2 inactive at block 1
+    sentinel = torch.tensor(7.0, dtype=torch.bfloat16)
+    dst = torch.full((P, 72, 208), float(sentinel), dtype=torch.bfloat16, device='cuda')
+    ops.weight_cast(src, dst, out_features=outf, in_features=inf, n_blocks=nb, block_index=1)
+    want = torch.full_like(dst, float(sentinel))
+    cast = src.to(torch.bfloat16)
+    for m in range(P):
+        if int(nb[m]) <= 1:
+            continue
+        o, i = int(outf[m]), int(inf[m])
+        want[m, :o, :] = 0
+        want[m, :o, :i] = cast[m, :o, :i]
+    assert torch.equal(dst, want)
+
+
+@pytest.mark.parametrize('opt', ['muon', 'adamw'])
+def test_bf16_weight_copy_follows_optimizer_steps(opt):
+    """The optimizers update parameters in place through the C ABI and bump their version
+    counters, so the cached bf16 weight copy is refreshed: after a step, the forward equals
+    that of a fresh model holding the updated state."""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+    from tabpack_b200 import nn as bnn
+    from tabpack_b200 import optim as bopt
+
+    torch.manual_seed(2)
+    P = 4
+    kw = dict(n_numerical_features=6, categorical_cardinalities=[5, 3], d_out=2, n_blocks=[1, 2, 3, 2],
+              d_block=[32, 16, 48, 24], dropout=[0.0] * P, pack_size=P, max_d_block=48)
+    model = bnn.TabPack(**kw).cuda()
+    if opt == 'muon':
+        groups = [bopt.MuonAdamWPack.make_muon_parameter_group(b.linear) for b in model.backbone.blocks]
+        muon_ids = {id(g['params'][0]) for g in groups}
+        groups.append({'params': [p for p in model.parameters() if id(p) not in muon_ids], 'muon': False})
+        o = bopt.MuonAdamWPack(groups, adamw_lr=1e-2, weight_decay=1e-3, muon_lr=5e-2, pack_size=P,
+                               allow_inplace_grad_mutation=True)
+    else:
+        o = bopt.AdamWPack(model.parameters(), lr=1e-2, weight_decay=1e-3, pack_size=P)
+    g = torch.Generator(device='cuda').manual_seed(3)
+    x_num = torch.randn(64, 6, device='cuda', generator=g)  # shared by the members (eval mode)
+    x_cat = torch.stack([torch.randint(0, c, (64,), device='cuda', generator=g) for c in (5, 3)], -1)
+    model.eval()
+    for _ in range(2):
+        with torch.autocast('cuda', dtype=torch.bfloat16):
+            y = model(x_num, x_cat)
+        y.float().square().mean().backward()
+        o.step()
+        o.zero_grad(set_to_none=True)
+    fresh = bnn.TabPack(**kw).cuda().eval()
+    fresh.load_state_dict(model.state_dict())
+    with torch.autocast('cuda', dtype=torch.bfloat16):
+        a, b = model(x_num, x_cat), fresh(x_num, x_cat)
+    assert torch.equal(a, b)
