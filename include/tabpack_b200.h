@@ -330,7 +330,8 @@ int tp_cos_emb_backward(const tp_cos_emb_args* a, void* stream);
  * mean the full source extent. */
 typedef struct tp_weight_cast_args {
   int32_t P;
-  int32_t src_rows, src_cols;   /* fp32 source (P, src_rows, src_cols), contiguous */
+  int32_t src_rows, src_cols;   /* fp32 source (P, src_rows, src_cols) */
+  int32_t src_ld;               /* row stride of src in elements (0: src_cols), e.g. a column block */
   int32_t dst_rows, dst_cols;   /* bf16 destination (P, dst_rows, dst_cols); dst_cols % 8 == 0,
                                    dst_rows >= src_rows, dst_cols >= src_cols */
   const int32_t* out_features;  /* device (P,) or NULL */
@@ -341,6 +342,66 @@ typedef struct tp_weight_cast_args {
   void* dst;                    /* 16-byte aligned */
 } tp_weight_cast_args;
 int tp_weight_cast(const tp_weight_cast_args* a, void* stream);
+
+/* Transposed bf16 copy of the column block [col0, col0 + ncols) of an fp32 weight pack:
+ * dst[m, j, n] = bf16(src[m, n, col0 + j]) for n < min(out_features[m], src_rows) and 0 for
+ * the n up to the next multiple of 8; the rest of each dst row is left as it is.  This is the
+ * operand of tp_onehot_linear_forward (the one-hot block of a TabPack's first-layer weight,
+ * whose rows the forward gathers).  dst_ld must be even and at least src_rows rounded up to 8. */
+typedef struct tp_weight_cast_t_args {
+  int32_t P;
+  int32_t src_rows, src_ld;     /* fp32 source (P, src_rows, src_ld) */
+  int32_t col0, ncols;          /* the column block */
+  int32_t dst_ld;               /* bf16 destination (P, ncols, dst_ld) */
+  const int32_t* out_features;  /* device (P,) or NULL */
+  const float* src;
+  void* dst;                    /* 16-byte aligned */
+} tp_weight_cast_t_args;
+int tp_weight_cast_transposed(const tp_weight_cast_t_args* a, void* stream);
+
+/* First layer of a TabPack over one-hot categorical features as a gather-sum (bf16, tensor
+ * cores).  The reference one-hot encodes each categorical feature (_OneHotEncoding,
+ * src/tabpackage/nn.py:1836-1871), concatenates the blocks after the dense columns
+ * (nn.py:2071-2107) and multiplies the whole width in its first LinearPack (nn.py:792-816).
+ * Here the layer's weight W (P, max_out, n_dense + n_onehot) is split: the dense columns
+ * (bf16 copy, tp_weight_cast with src_ld) multiply the dense input on the tensor cores with
+ * K = n_dense, and the one-hot columns are gathered: one W column per feature and row, added
+ * to the accumulator before the bias, ReLU and dropout.  Category values outside
+ * [0, cardinality) (the unknown category `cardinality` included) contribute nothing, as
+ * their one-hot rows are zero.
+ *
+ * tp_onehot_linear_forward: `a` is the forward of the dense part (x: (P or 1, B, max_in) dense
+ * input, w: the bf16 dense weight copy (P, max_out, max_in), bias/relu/dropout as in
+ * tp_linear_forward, dtype TP_DTYPE_BF16).  Writes y, and sorted_keys when it is non-NULL
+ * (kept for the backward; a forward without a backward passes NULL and skips the sort), and
+ * uses addend as scratch.
+ * tp_onehot_linear_backward: as tp_linear_backward for the same `a` and `oh` (after the
+ * forward wrote sorted_keys); dw is the full weight gradient (P, dw_rows, dw_cols)
+ * with dw_cols = n_dense + n_onehot: the dense columns come from the tensor-core wgrad and
+ * the one-hot columns from segmented sums of the pre-activation gradient over the rows of
+ * each category, in ascending row order.  dx, when requested, is the dense input's gradient
+ * (P, B, max_in). */
+/* At most 16384 batch rows per call (TP_EUNSUPPORTED beyond). */
+typedef struct tp_onehot_args {
+  int32_t n_dense;               /* weight columns before the one-hot block (<= max_in of `a`) */
+  int32_t n_cat;                 /* categorical features */
+  int32_t n_onehot;              /* one-hot columns (= cat_offsets[n_cat]) */
+  const int32_t* cat_offsets;    /* device (n_cat + 1,): first one-hot column of each feature */
+  const int64_t* x_cat;          /* categories; batch row r of member m reads x_cat row
+                                    (row_index ? row_index[m * row_index_member_stride + r] : r)
+                                    + m * x_cat_member_stride */
+  int64_t x_cat_member_stride;
+  const int64_t* row_index;      /* device or NULL */
+  int64_t row_index_member_stride;
+  const void* w_onehot_t;        /* bf16 (P, n_onehot, wt_ld) from tp_weight_cast_transposed */
+  int32_t wt_ld;                 /* >= max_out rounded up to 8 */
+  void* sorted_keys;             /* (P, n_cat, B) uint64: (category << 32 | batch row), ascending per
+                                    feature; the unknown category sorts last */
+  float* addend;                 /* forward scratch (P, B, addend_ld), 16-byte aligned */
+  int32_t addend_ld;             /* multiple of 16, >= max_out */
+} tp_onehot_args;
+int tp_onehot_linear_forward(const tp_linear_args* a, const tp_onehot_args* oh, void* stream);
+int tp_onehot_linear_backward(const tp_linear_grad_args* ga, const tp_onehot_args* oh, void* stream);
 
 /* Clears and returns the device-side error flag (TP_OK or TP_ETIMEOUT). */
 int tp_device_error(void);

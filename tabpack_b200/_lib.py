@@ -106,9 +106,27 @@ class InputArgs(ctypes.Structure):
 class WeightCastArgs(ctypes.Structure):
     _fields_ = [
         ('P', ctypes.c_int32), ('src_rows', ctypes.c_int32), ('src_cols', ctypes.c_int32),
-        ('dst_rows', ctypes.c_int32), ('dst_cols', ctypes.c_int32), ('out_features', ctypes.c_void_p),
+        ('src_ld', ctypes.c_int32), ('dst_rows', ctypes.c_int32), ('dst_cols', ctypes.c_int32), ('out_features', ctypes.c_void_p),
         ('in_features', ctypes.c_void_p), ('n_blocks', ctypes.c_void_p), ('block_index', ctypes.c_int32),
         ('src', ctypes.c_void_p), ('dst', ctypes.c_void_p),
+    ]
+
+
+class WeightCastTArgs(ctypes.Structure):
+    _fields_ = [
+        ('P', ctypes.c_int32), ('src_rows', ctypes.c_int32), ('src_ld', ctypes.c_int32), ('col0', ctypes.c_int32),
+        ('ncols', ctypes.c_int32), ('dst_ld', ctypes.c_int32), ('out_features', ctypes.c_void_p),
+        ('src', ctypes.c_void_p), ('dst', ctypes.c_void_p),
+    ]
+
+
+class OneHotArgs(ctypes.Structure):
+    _fields_ = [
+        ('n_dense', ctypes.c_int32), ('n_cat', ctypes.c_int32), ('n_onehot', ctypes.c_int32),
+        ('cat_offsets', ctypes.c_void_p), ('x_cat', ctypes.c_void_p), ('x_cat_member_stride', ctypes.c_int64),
+        ('row_index', ctypes.c_void_p), ('row_index_member_stride', ctypes.c_int64),
+        ('w_onehot_t', ctypes.c_void_p), ('wt_ld', ctypes.c_int32), ('sorted_keys', ctypes.c_void_p),
+        ('addend', ctypes.c_void_p), ('addend_ld', ctypes.c_int32),
     ]
 
 
@@ -150,6 +168,11 @@ SIGNATURES = {
     'tp_cos_emb_backward': (ctypes.c_int, [ctypes.POINTER(CosEmbArgs), ctypes.c_void_p]),
     'tp_tabpack_input': (ctypes.c_int, [ctypes.POINTER(InputArgs), ctypes.c_void_p]),
     'tp_weight_cast': (ctypes.c_int, [ctypes.POINTER(WeightCastArgs), ctypes.c_void_p]),
+    'tp_weight_cast_transposed': (ctypes.c_int, [ctypes.POINTER(WeightCastTArgs), ctypes.c_void_p]),
+    'tp_onehot_linear_forward': (ctypes.c_int, [ctypes.POINTER(LinearArgs), ctypes.POINTER(OneHotArgs),
+                                                ctypes.c_void_p]),
+    'tp_onehot_linear_backward': (ctypes.c_int, [ctypes.POINTER(LinearGradArgs), ctypes.POINTER(OneHotArgs),
+                                                 ctypes.c_void_p]),
     'tp_roc_auc_workspace_size': (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32]),
     'tp_binary_roc_auc': (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
                                          ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,

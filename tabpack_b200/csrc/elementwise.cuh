@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(256) adamw_kernel(const AdamWTensors ts, const
 // converts one row: 8 columns per lane, one 16-byte store.
 // ---------------------------------------------------------------------------
 struct WeightCastArgs {
-  int src_rows, src_cols, dst_rows, dst_cols;
+  int src_rows, src_cols, src_ld, dst_rows, dst_cols;
   const int32_t* out_f;
   const int32_t* in_f;
   const int32_t* n_blocks;
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(256) weight_cast_kernel(const WeightCastArgs a
   const int rows = a.out_f != nullptr ? min(__ldg(a.out_f + m), a.src_rows) : a.src_rows;
   if (r >= rows) return;
   const int cols = a.in_f != nullptr ? min(__ldg(a.in_f + m), a.src_cols) : a.src_cols;
-  const float* s = a.src + ((size_t)m * a.src_rows + r) * a.src_cols;
+  const float* s = a.src + ((size_t)m * a.src_rows + r) * a.src_ld;
   __nv_bfloat16* d = a.dst + ((size_t)m * a.dst_rows + r) * a.dst_cols;
   for (int c0 = lane * 8; c0 < a.dst_cols; c0 += 256) {
     float v[8];
@@ -310,6 +310,57 @@ __global__ void __launch_bounds__(256) weight_cast_kernel(const WeightCastArgs a
     u.z = pack_bf16x2(v[4], v[5]);
     u.w = pack_bf16x2(v[6], v[7]);
     *reinterpret_cast<uint4*>(d + c0) = u;
+  }
+}
+
+
+// Transposed bf16 copy of a column block of an fp32 weight pack (the one-hot columns of a
+// TabPack's first layer, gathered row-wise by onehot_gather_kernel):
+// dst[m, j, n] = bf16(src[m, n, col0 + j]) for n < out_m, 0 for out_m <= n < round8(out_m);
+// the rest of each dst row is not written (never read).  Tiles of 64 n x 128 j go through
+// shared memory so that both the fp32 reads (128-byte pieces along j, 32 loads in flight per
+// thread) and the bf16 writes (128-byte pieces along n) are contiguous.
+struct WeightCastTArgs {
+  int src_rows, src_ld, col0, ncols, dst_ld;
+  const int32_t* out_f;
+  const float* src;
+  __nv_bfloat16* dst;
+};
+
+constexpr int CAST_T_N = 64, CAST_T_J = 128;
+
+// Grid: (ceil(ncols / 128), ceil(src_rows / 64), P), 256 threads, 33 KB of dynamic shared memory.
+__global__ void __launch_bounds__(256) weight_cast_t_kernel(const WeightCastTArgs a) {
+  extern __shared__ float ct_tile[];  // [CAST_T_N][CAST_T_J + 1]
+  const int m = blockIdx.z;
+  const int j0 = blockIdx.x * CAST_T_J, n0 = blockIdx.y * CAST_T_N;
+  const int rows = a.out_f != nullptr ? min(__ldg(a.out_f + m), a.src_rows) : a.src_rows;
+  const int rows8 = (rows + 7) & ~7;
+  if (n0 >= rows8) return;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const float* s = a.src + (size_t)m * a.src_rows * a.src_ld + a.col0;
+  float v[CAST_T_N / 8][CAST_T_J / 32];
+#pragma unroll
+  for (int ii = 0; ii < CAST_T_N / 8; ++ii) {
+    const int n = n0 + w + 8 * ii;
+#pragma unroll
+    for (int jj = 0; jj < CAST_T_J / 32; ++jj) {
+      const int j = j0 + lane + 32 * jj;
+      v[ii][jj] = (n < rows && j < a.ncols) ? __ldg(s + (size_t)n * a.src_ld + j) : 0.0f;
+    }
+  }
+#pragma unroll
+  for (int ii = 0; ii < CAST_T_N / 8; ++ii)
+#pragma unroll
+    for (int jj = 0; jj < CAST_T_J / 32; ++jj) ct_tile[(w + 8 * ii) * (CAST_T_J + 1) + lane + 32 * jj] = v[ii][jj];
+  __syncthreads();
+  __nv_bfloat16* d = a.dst + (size_t)m * a.ncols * a.dst_ld;
+  const int n = n0 + 2 * lane;
+  for (int jr = w; jr < CAST_T_J; jr += 8) {
+    const int j = j0 + jr;
+    if (j < a.ncols && n < rows8)
+      *reinterpret_cast<uint32_t*>(d + (size_t)j * a.dst_ld + n) =
+          pack_bf16x2(ct_tile[2 * lane * (CAST_T_J + 1) + jr], ct_tile[(2 * lane + 1) * (CAST_T_J + 1) + jr]);
   }
 }
 

@@ -5,6 +5,7 @@
 // and store.
 //
 //   MODE_FWD    : C[B x out_m] = X[B x in_m] * W^T, + bias, ReLU, Philox dropout; A, B K-major
+//   MODE_FWD_ADD: the forward with an fp32 addend E[B x out_m] summed before the bias
 //   MODE_DGRAD  : C[B x in_m] = G[B x out_m] * W; A K-major, B MN-major; CTA pairs
 //   MODE_WGRAD_T: C^T[in_m x out_m] = X^T * G stored into C (K = batch rows), A and B MN-major;
 //                 a warp's 32 lanes hold 32 consecutive input features, so each output
@@ -34,16 +35,17 @@ struct Sm100Cfg {
   // time goes to its bias / ReLU / dropout epilogue rather than to operand traffic, runs
   // on single CTAs (measured a few percent faster than on pairs).
   static constexpr bool PAIR = (MODE == MODE_DGRAD || MODE == MODE_WGRAD_T) && BN_ == 256;
+  static constexpr bool FWDK = (MODE == MODE_FWD || MODE == MODE_FWD_ADD);  // forward epilogue
   static constexpr int TILE_M = PAIR ? 2 * BM : BM;
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B columns staged per CTA
   static constexpr bool A_MN = (MODE == MODE_WGRAD_T);
   static constexpr bool B_MN = (MODE == MODE_DGRAD || MODE == MODE_WGRAD_T || MODE == MODE_NS_BMN);
-  static constexpr int STAGES = PAIR ? 6 : (BN == 256) ? (MODE == MODE_FWD ? 3 : 4) : 6;
+  static constexpr int STAGES = PAIR ? 6 : (BN == 256) ? (FWDK ? 3 : 4) : 6;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = B_ROWS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int EPI_WARPS = (MODE == MODE_FWD) ? 16 : 8;
+  static constexpr int EPI_WARPS = FWDK ? 16 : 8;
   static constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
   // stages + barriers (full, empty per stage; tfull, tempty x2; done) + tmem addr + abort
   // + per-warp bias slice (BN / (EPI_WARPS / 4) floats per epilogue warp)
@@ -285,7 +287,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
         if (t >= total_tiles) break;
         const TileInfo ti = decode_tile(pr, t, Cfg::BK);
         if (ti.kind != KIND_MMA) continue;
-        const int zA = ((MODE == MODE_FWD || MODE == MODE_WGRAD_T) && pr.x_shared) ? 0 : ti.member;  // NS operands are per member
+        const int zA = ((Cfg::FWDK || MODE == MODE_WGRAD_T) && pr.x_shared) ? 0 : ti.member;  // NS operands are per member
         const int zB = ti.member;
         // this CTA's A rows and B columns: in a pair the leader takes rows 0..127 and the
         // first half of the (trimmed) columns, the peer rows 128..255 and the second half
@@ -422,7 +424,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
     const int row_in_tile = (int)rank * Cfg::BM + q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    const bool dropout_on = (MODE == MODE_FWD) && pr.dropout_p != nullptr;
+    const bool dropout_on = Cfg::FWDK && pr.dropout_p != nullptr;
     // tile metadata is decoded one tile ahead so its global loads overlap the current tile
     TileInfo nti;
     float np = 0.0f;
@@ -433,7 +435,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
 #pragma unroll
       for (int i = 0; i < NCH; ++i) {
         const int col = cb + 32 * i + lane;
-        bnext[i] = (MODE == MODE_FWD && x.kind == KIND_MMA && pr.bias != nullptr && col < x.n_valid)
+        bnext[i] = (Cfg::FWDK && x.kind == KIND_MMA && pr.bias != nullptr && col < x.n_valid)
                        ? __ldg(pr.bias + (size_t)x.member * pr.bias_ld + col)
                        : 0.0f;
       }
@@ -442,7 +444,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
     if (t < total_tiles) {
       nti = decode_tile(pr, t, Cfg::BK);
       if (dropout_on) np = __ldg(pr.dropout_p + nti.member);
-      if (MODE == MODE_FWD) load_bias(nti);
+      if (Cfg::FWDK) load_bias(nti);
     }
     int t_next = total_tiles;
     for (int k = 0; t < total_tiles; ++k, t = t_next) {
@@ -463,7 +465,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
           thr = keep_threshold(p_cur);
           scale = keep_scale(p_cur);
         }
-        if (MODE == MODE_FWD) {
+        if (Cfg::FWDK) {
           // this tile's bias slice times the keep scale (zero beyond n_valid) to smem, then
           // prefetch the next one; the epilogue forms (acc + b) * scale as fma(acc, scale, b * scale)
           __syncwarp();
@@ -537,7 +539,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
                 base[(size_t)o * pr.out_ld + row] = (in_valid && o < ti.n_valid) ? __uint_as_float(wa[j]) : 0.0f;
             }
           }
-        } else if constexpr (MODE == MODE_FWD) {
+        } else if constexpr (Cfg::FWDK) {
           // 16-column TMEM loads (four warps per scheduler cover their latency); the staged
           // 32-column slot is flushed after every second chunk.  Only the 32-column chunks
           // that hold some of the member's columns run the epilogue; the padding after them
@@ -553,7 +555,24 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
             const int nv = ti.n_valid - col0;
             uint4 q2[2];
             fwd16_draws(pr, m, row, col0, drop && nv > 0, q2);
+            [[maybe_unused]] float4 ea[4];
+            if constexpr (MODE == MODE_FWD_ADD) {
+              // the gathered addend of this row's 16 columns (the ragged tail is zeroed below)
+              const bool ev = nv > 0 && row < pr.B;
+              const float4* ep = reinterpret_cast<const float4*>(pr.addend + ((size_t)m * pr.B + row) * pr.add_ld + col0);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) ea[i] = ev ? __ldg(ep + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
             tmem_wait_ld();
+            if constexpr (MODE == MODE_FWD_ADD) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                fa[4 * i] = __float_as_uint(__uint_as_float(fa[4 * i]) + ea[i].x);
+                fa[4 * i + 1] = __float_as_uint(__uint_as_float(fa[4 * i + 1]) + ea[i].y);
+                fa[4 * i + 2] = __float_as_uint(__uint_as_float(fa[4 * i + 2]) + ea[i].z);
+                fa[4 * i + 3] = __float_as_uint(__uint_as_float(fa[4 * i + 3]) + ea[i].w);
+              }
+            }
             epi_fwd16(pr, fa, q2, nv, drop && nv > 0, thr, scale, sbias + 16 * c, stage_row + 32 * (c & 1));
             if (c & 1) {
               __syncwarp();

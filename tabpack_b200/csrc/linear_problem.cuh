@@ -16,6 +16,10 @@ namespace tp {
 // MODE_NS / MODE_NS_BMN: one Newton-Schulz GEMM, C = alpha * A B^T + beta * D, with
 // per-member shapes taken from (ns_rows, ns_cols) and B read K-major / MN-major.
 enum : int { MODE_FWD = 0, MODE_DGRAD = 1, MODE_WGRAD = 2, MODE_NS = 3, MODE_NS_BMN = 4, MODE_WGRAD_T = 5 };
+// Kernel instantiation of the forward whose epilogue also adds a per-element fp32 addend
+// (the gathered one-hot columns of a TabPack's first layer); its problems carry
+// mode = MODE_FWD, so tiles decode as the forward's.
+enum : int { MODE_FWD_ADD = 6 };
 enum : int { KIND_MMA = 0, KIND_ZERO = 1, KIND_COPY = 2, KIND_SKIP = 3 };
 
 struct LinearProblem {
@@ -59,6 +63,9 @@ struct LinearProblem {
   int ns_shape;
   float alpha, beta;
   const void* D;  // (optional) addend with the output's geometry
+  // MODE_FWD_ADD: fp32 addend (P, B, add_ld) added to the accumulator before the bias
+  const float* addend;
+  int add_ld;
 };
 
 struct TileInfo {

@@ -36,8 +36,8 @@ struct MuonArgs {
   __nv_bfloat16* x;      // (P, R_s, C_s) oriented operand
   int R_s, C_s;
   float* norm2;          // (P,)
-  float* partial;        // (P, tiles) per-32x32-tile sums of squares (fixed-order reduction)
-  int tiles;             // ceil(max_out / 32) * ceil(max_in / 32)
+  float* partial;        // (P, tiles) per-tile sums of squares (fixed-order reduction)
+  int tiles;             // ceil(max_out / 32) * ceil(max_in / 128)
   int32_t* rows;         // (P,) r_m
   int32_t* cols;         // (P,) c_m
   int32_t* trans;        // (P,) 1: X = U^T
@@ -54,73 +54,115 @@ __global__ void muon_geometry_kernel(MuonArgs a) {
   a.trans[m] = o > n ? 1 : 0;
 }
 
-// 32x32 source tiles (o, n) of member blockIdx.z; 256 threads = 32 columns x 8 row lanes.
+// Tiles of the Muon elementwise kernels: 32 weight rows (o) x 128 weight columns (n), 256
+// threads; warp w takes rows w, w + 8, w + 16, w + 24 and lane l columns l, l + 32, l + 64,
+// l + 96, so each load instruction covers 128 contiguous bytes and a thread has 16 elements
+// (32 loads in the prologue) in flight.
+constexpr int MUON_TM = 32, MUON_TN = 128;
+constexpr int MUON_UB_LD = MUON_TN + 8;  // bf16 staging row (16-byte aligned rows)
+
+// The oriented operand X of the tile (o0, n0) from / to the staged bf16 update ub[o][n]:
+// X[o][n] = U when the member is not transposed (rows of 8-byte pieces), X[n][o] = U otherwise
+// (rows of 64 bytes, two 32-byte halves per thread).
+__device__ __forceinline__ void muon_store_x(__nv_bfloat16* x, int C_s, bool tr, int o0, int n0,
+                                             const __nv_bfloat16 (*ub)[MUON_UB_LD]) {
+  const int t = threadIdx.x;
+  if (!tr) {
+    const int c4 = 4 * (t & 31);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = (t >> 5) + 8 * i;
+      *reinterpret_cast<uint2*>(x + (size_t)(o0 + r) * C_s + n0 + c4) = *reinterpret_cast<const uint2*>(&ub[r][c4]);
+    }
+  } else {
+    const int nl = t >> 1, h = 16 * (t & 1);
+    __align__(16) __nv_bfloat16 v[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[e] = ub[h + e][nl];
+    uint4* dst = reinterpret_cast<uint4*>(x + (size_t)(n0 + nl) * C_s + o0 + h);
+    dst[0] = reinterpret_cast<const uint4*>(v)[0];
+    dst[1] = reinterpret_cast<const uint4*>(v)[1];
+  }
+}
+
+__device__ __forceinline__ void muon_load_x(const __nv_bfloat16* x, int C_s, bool tr, int o0, int n0,
+                                            __nv_bfloat16 (*ub)[MUON_UB_LD]) {
+  const int t = threadIdx.x;
+  if (!tr) {
+    const int c4 = 4 * (t & 31);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = (t >> 5) + 8 * i;
+      *reinterpret_cast<uint2*>(&ub[r][c4]) = *reinterpret_cast<const uint2*>(x + (size_t)(o0 + r) * C_s + n0 + c4);
+    }
+  } else {
+    const int nl = t >> 1, h = 16 * (t & 1);
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(n0 + nl) * C_s + o0 + h);
+    __align__(16) __nv_bfloat16 v[16];
+    reinterpret_cast<uint4*>(v)[0] = src[0];
+    reinterpret_cast<uint4*>(v)[1] = src[1];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) ub[h + e][nl] = v[e];
+  }
+}
+
+// Grid: (ceil(max_in / 128), ceil(max_out / 32), P).  Momentum (lerp toward the gradient),
+// Nesterov, the bf16 update into the oriented operand (tiles wholly outside the member's
+// out x in block are never read nor written; the rest of a partly covered tile gets zeros,
+// which the normalisation keeps), and the tile's sum of squares of the bf16 update.  Weight
+// decay is applied with the update in muon_apply_kernel.
 __global__ void __launch_bounds__(256) muon_prologue_kernel(MuonArgs a) {
-  __shared__ float tile[32][33];
+  __shared__ __align__(16) __nv_bfloat16 ub[MUON_TM][MUON_UB_LD];
   __shared__ float red[8];
   const int mem = blockIdx.z;
-  const int o0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  const int o0 = blockIdx.y * MUON_TM, n0 = blockIdx.x * MUON_TN;
   const int out_m = a.out_f ? a.out_f[mem] : a.max_out;
   const int in_m = a.in_f ? a.in_f[mem] : a.max_in;
   if (o0 >= out_m || n0 >= in_m) return;  // padding: never read, never written
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const float lr = a.lr_pm ? a.lr_pm[mem] : a.lr_s;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const float mu = a.mu_pm ? a.mu_pm[mem] : a.mu_s;
-  const float mult = (a.lr_pm || a.wd_pm) ? 1.0f - lr * (a.wd_pm ? a.wd_pm[mem] : a.wd_s) : a.wd_mult_s;
   const float one_m_mu = a.mu_pm ? 1.0f - mu : a.one_m_mu_s;
-  float ss = 0.0f;
-  // rows ty, ty + 8, ty + 16, ty + 24: all loads issued before any use
-  float pv[4], gv[4], mv[4];
-  bool ok[4];
+  float gv[4][4], mv[4][4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int o = o0 + ty + 8 * k, n = n0 + tx;
-    ok[k] = o < out_m && n < in_m;
-    const size_t idx = ((size_t)mem * a.max_out + o) * a.max_in + n;
-    pv[k] = ok[k] ? a.p[idx] : 0.0f;
-    gv[k] = ok[k] ? a.g[idx] : 0.0f;
-    mv[k] = ok[k] ? a.m[idx] : 0.0f;
-  }
+  for (int i = 0; i < 4; ++i)
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int i = ty + 8 * k;
-    float u = 0.0f;
-    if (ok[k]) {
-      const size_t idx = ((size_t)mem * a.max_out + (o0 + i)) * a.max_in + (n0 + tx);
-      float p = pv[k];
-      if (a.wd_on) p *= mult;
-      const float m = lerp_t(mv[k], gv[k], one_m_mu);
-      u = a.nesterov ? lerp_t(gv[k], m, mu) : m;
-      a.p[idx] = p;
-      a.m[idx] = m;
-      if (a.nesterov && a.mutate_grad) a.g[idx] = u;
-      u = __bfloat162float(__float2bfloat16_rn(u));
-      ss += u * u;
+    for (int c = 0; c < 4; ++c) {
+      const int o = o0 + w + 8 * i, n = n0 + lane + 32 * c;
+      const bool ok = o < out_m && n < in_m;
+      const size_t idx = ((size_t)mem * a.max_out + o) * a.max_in + n;
+      gv[i][c] = ok ? a.g[idx] : 0.0f;
+      mv[i][c] = ok ? a.m[idx] : 0.0f;
     }
-    tile[i][tx] = u;
-  }
-  // Frobenius norm of the bf16 update, per member
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int o = o0 + w + 8 * i, n = n0 + lane + 32 * c;
+      __nv_bfloat16 ubv = __float2bfloat16_rn(0.0f);
+      if (o < out_m && n < in_m) {
+        const size_t idx = ((size_t)mem * a.max_out + o) * a.max_in + n;
+        const float m = lerp_t(mv[i][c], gv[i][c], one_m_mu);
+        const float u = a.nesterov ? lerp_t(gv[i][c], m, mu) : m;
+        a.m[idx] = m;
+        if (a.nesterov && a.mutate_grad) a.g[idx] = u;
+        ubv = __float2bfloat16_rn(u);
+        const float ub_f = __bfloat162float(ubv);
+        ss += ub_f * ub_f;
+      }
+      ub[w + 8 * i][lane + 32 * c] = ubv;
+    }
+  // Frobenius norm of the bf16 update: this tile's partial, reduced in a fixed order
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
-  if (tx == 0) red[ty] = ss;
+  if (lane == 0) red[w] = ss;
   __syncthreads();
   if (threadIdx.x == 0) {
     float t = 0.0f;
     for (int i = 0; i < 8; ++i) t += red[i];
     a.partial[(size_t)mem * a.tiles + blockIdx.y * gridDim.x + blockIdx.x] = t;
   }
-  // oriented bf16 operand
-  const bool tr = out_m > in_m;
-  __nv_bfloat16* x = a.x + (size_t)mem * a.R_s * a.C_s;
-  for (int i = ty; i < 32; i += 8) {
-    if (!tr) {
-      const int o = o0 + i, n = n0 + tx;
-      if (o < out_m && n < in_m) x[(size_t)o * a.C_s + n] = __float2bfloat16_rn(tile[i][tx]);
-    } else {
-      const int n = n0 + i, o = o0 + tx;  // X[n][o] = U[o][n]
-      if (o < out_m && n < in_m) x[(size_t)n * a.C_s + o] = __float2bfloat16_rn(tile[tx][i]);
-    }
-  }
+  muon_store_x(a.x + (size_t)mem * a.R_s * a.C_s, a.C_s, out_m > in_m, o0, n0, ub);
 }
 
 // norm2[m] = sum of the member's tile partials in a fixed order (deterministic),
@@ -130,7 +172,7 @@ __global__ void __launch_bounds__(256) muon_norm_kernel(MuonArgs a, int tiles_x)
   const int mem = blockIdx.x;
   const int out_m = a.out_f ? a.out_f[mem] : a.max_out;
   const int in_m = a.in_f ? a.in_f[mem] : a.max_in;
-  const int ty_n = (out_m + 31) / 32, tx_n = (in_m + 31) / 32;  // tiles the prologue wrote
+  const int ty_n = (out_m + MUON_TM - 1) / MUON_TM, tx_n = (in_m + MUON_TN - 1) / MUON_TN;  // tiles the prologue wrote
   float s = 0.0f;
   for (int t = threadIdx.x; t < ty_n * tx_n; t += blockDim.x) {
     const int ty = t / tx_n, tx = t - ty * tx_n;
@@ -150,71 +192,79 @@ __global__ void __launch_bounds__(256) muon_norm_kernel(MuonArgs a, int tiles_x)
 
 // X <- bf16(X / bf16(bf16(||X||_F) + 1e-7)) on the member's r x c block and exact zeros
 // on [0, R_s-tile) x [0, C_s-tile) around it (the Newton-Schulz GEMMs read those pads
-// along K).  Grid: (ceil(C_s / 256), R_s / 8, P), 256 threads, 8 rows x 32 x 8 columns.
+// along K).  Grid: (ceil(C_s / 256), ceil(R_s / 32), P), 256 threads; a warp covers rows
+// w, w + 8, w + 16, w + 24 of the block's 32, a lane 8 columns (16 bytes) of each.
 __global__ void __launch_bounds__(256) muon_normalize_kernel(MuonArgs a, int row_pad, int col_pad) {
   const int mem = blockIdx.z;
   const int r = a.rows[mem], c = a.cols[mem];
   const int rr = min(a.R_s, (r + row_pad - 1) / row_pad * row_pad);
   const int cc = min(a.C_s, (c + col_pad - 1) / col_pad * col_pad);
+  const int row0 = blockIdx.y * 32;
+  const int col = blockIdx.x * 256 + (threadIdx.x & 31) * 8;
+  if (row0 >= rr || col >= cc) return;
   const float nrm2 = a.norm2[mem];
   if (nrm2 == 0.0f) return;  // all-zero update: Newton-Schulz is skipped for this member
   const float nrm = __bfloat162float(__float2bfloat16_rn(sqrtf(nrm2)));
   const float den = __bfloat162float(__float2bfloat16_rn(nrm + 1e-7f));
-  const int row = blockIdx.y * 8 + (threadIdx.x >> 5);
-  const int col = blockIdx.x * 256 + (threadIdx.x & 31) * 8;
-  if (row >= rr || col >= cc) return;
-  __nv_bfloat16* x = a.x + (size_t)mem * a.R_s * a.C_s + (size_t)row * a.C_s + col;
-  uint4 u = make_uint4(0, 0, 0, 0);
-  if (row < r && col < c) {
-    u = *reinterpret_cast<const uint4*>(x);
-    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&u);
+  uint4 u[4];
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      h[e] = (col + e < c) ? __float2bfloat16_rn(__bfloat162float(h[e]) / den) : __float2bfloat16_rn(0.0f);
+  for (int i = 0; i < 4; ++i) {
+    const int row = row0 + (threadIdx.x >> 5) + 8 * i;
+    u[i] = make_uint4(0, 0, 0, 0);
+    if (row < r && col < c) u[i] = *reinterpret_cast<const uint4*>(a.x + (size_t)mem * a.R_s * a.C_s + (size_t)row * a.C_s + col);
   }
-  *reinterpret_cast<uint4*>(x) = u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int row = row0 + (threadIdx.x >> 5) + 8 * i;
+    if (row >= rr) continue;
+    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&u[i]);
+    if (row < r) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        h[e] = (col + e < c) ? __float2bfloat16_rn(__bfloat162float(h[e]) / den) : __float2bfloat16_rn(0.0f);
+    }
+    *reinterpret_cast<uint4*>(a.x + (size_t)mem * a.R_s * a.C_s + (size_t)row * a.C_s + col) = u[i];
+  }
 }
 
-// p[o][n] -= lr * scale * U[o][n] for the member's out x in block (U read back through
-// the orientation).  Same tiling as the prologue.
+// p <- p * (1 - lr wd) - lr * scale * U over the member's out x in block (weight decay first,
+// rounded, as the reference's separate in-place steps; U read back through the orientation;
+// members whose update was all zero take the weight decay alone).  Same tiling as the
+// prologue.
 __global__ void __launch_bounds__(256) muon_apply_kernel(MuonArgs a) {
-  __shared__ float tile[32][33];
+  __shared__ __align__(16) __nv_bfloat16 ub[MUON_TM][MUON_UB_LD];
   const int mem = blockIdx.z;
-  const int o0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  const int o0 = blockIdx.y * MUON_TM, n0 = blockIdx.x * MUON_TN;
   const int out_m = a.out_f ? a.out_f[mem] : a.max_out;
   const int in_m = a.in_f ? a.in_f[mem] : a.max_in;
-  if (o0 >= out_m || n0 >= in_m || a.active[mem] == 0) return;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const bool tr = out_m > in_m;
-  const __nv_bfloat16* x = a.x + (size_t)mem * a.R_s * a.C_s;
-  // the four rows' weights are loaded together with the update tile
-  float pv[4];
+  if (o0 >= out_m || n0 >= in_m) return;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const bool active = a.active[mem] != 0;
+  float pv[4][4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int o = o0 + ty + 8 * k, n = n0 + tx;
-    pv[k] = (o < out_m && n < in_m) ? a.p[((size_t)mem * a.max_out + o) * a.max_in + n] : 0.0f;
-  }
+  for (int i = 0; i < 4; ++i)
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int i = ty + 8 * k;
-    if (!tr) {
-      const int o = o0 + i, n = n0 + tx;
-      tile[i][tx] = (o < out_m && n < in_m) ? __bfloat162float(x[(size_t)o * a.C_s + n]) : 0.0f;
-    } else {
-      const int n = n0 + i, o = o0 + tx;
-      tile[tx][i] = (o < out_m && n < in_m) ? __bfloat162float(x[(size_t)n * a.C_s + o]) : 0.0f;
+    for (int c = 0; c < 4; ++c) {
+      const int o = o0 + w + 8 * i, n = n0 + lane + 32 * c;
+      pv[i][c] = (o < out_m && n < in_m) ? a.p[((size_t)mem * a.max_out + o) * a.max_in + n] : 0.0f;
     }
-  }
+  if (active) muon_load_x(a.x + (size_t)mem * a.R_s * a.C_s, a.C_s, out_m > in_m, o0, n0, ub);
   __syncthreads();
   const float lr = a.lr_pm ? a.lr_pm[mem] : a.lr_s;
+  const float mult = (a.lr_pm || a.wd_pm) ? 1.0f - lr * (a.wd_pm ? a.wd_pm[mem] : a.wd_s) : a.wd_mult_s;
   const float sc = a.scale_pm ? a.scale_pm[mem] : a.scale_s;
   const float slr = lr * sc;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int i = ty + 8 * k;
-    const int o = o0 + i, n = n0 + tx;
-    if (o < out_m && n < in_m) a.p[((size_t)mem * a.max_out + o) * a.max_in + n] = pv[k] - tile[i][tx] * slr;
-  }
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int o = o0 + w + 8 * i, n = n0 + lane + 32 * c;
+      if (o < out_m && n < in_m) {
+        const float pw = a.wd_on ? __fmul_rn(pv[i][c], mult) : pv[i][c];
+        const float u = active ? __bfloat162float(ub[w + 8 * i][lane + 32 * c]) : 0.0f;
+        a.p[((size_t)mem * a.max_out + o) * a.max_in + n] = fmaf(-u, slr, pw);
+      }
+    }
 }
 
 }  // namespace tp

@@ -19,6 +19,7 @@
 #include "metrics.cuh"
 #include "roc_auc.cuh"
 #include "embeddings.cuh"
+#include "onehot.cuh"
 
 namespace tp {
 namespace {
@@ -259,7 +260,7 @@ MuonLayout muon_layout(int P, int max_out, int max_in) {
   L.off_cols = take((size_t)P * 4);
   L.off_trans = take((size_t)P * 4);
   L.off_active = take((size_t)P * 4);
-  L.tiles = ((max_out + 31) / 32) * ((max_in + 31) / 32);
+  L.tiles = ((max_out + MUON_TM - 1) / MUON_TM) * ((max_in + MUON_TN - 1) / MUON_TN);
   L.off_partial = take((size_t)P * L.tiles * 4);
   L.off_counter = take(MUON_COUNTERS * 4);  // tile counters of the Newton-Schulz launches
   L.total = o;
@@ -323,6 +324,13 @@ static void metric_dispatch(int metric, F f) {
   }
 }
 
+namespace tp {
+namespace {
+int linear_forward_impl(const tp_linear_args* a, const float* addend, int add_ld, void* stream);
+int linear_backward_impl(const tp_linear_grad_args* ga, int dw_ld, void* stream);
+}  // namespace
+}  // namespace tp
+
 extern "C" {
 
 const char* tp_version(void) { return "tabpack_b200 0.1.0 (sm_100a)"; }
@@ -338,11 +346,24 @@ int tp_device_error(void) {
 }
 
 int tp_linear_forward(const tp_linear_args* a, void* stream) {
+  return linear_forward_impl(a, nullptr, 0, stream);
+}
+
+}  // extern "C"
+
+namespace tp {
+namespace {
+
+// The forward of tp_linear_forward; with `addend` (fp32 (P, B, add_ld)) the tensor-core
+// forward adds it to the accumulator before the bias.
+int linear_forward_impl(const tp_linear_args* a, const float* addend, int add_ld, void* stream) {
   int rc = check_linear(a);
   if (rc) return rc;
   if (!a->x || !a->y) return fail(TP_EINVAL, "x and y must be non-null");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   LinearProblem pr = base_problem(a);
+  pr.addend = addend;
+  pr.add_ld = add_ld;
   pr.mode = MODE_FWD;
   pr.out = a->y;
   pr.out_rows = a->B;
@@ -364,12 +385,30 @@ int tp_linear_forward(const tp_linear_args* a, void* stream) {
     CUtensorMap ma, mb;
     if ((rc = make_map(&ma, a->x, a->max_in, a->B, a->x_shared ? 1 : a->P, 64, Cfg::BM))) return rc;
     if ((rc = make_map(&mb, a->w, a->max_in, a->max_out, a->P, 64, Cfg::B_ROWS))) return rc;
+    static_assert(Sm100Cfg<BN, MODE_FWD_ADD>::TILE_M == Cfg::TILE_M && Sm100Cfg<BN, MODE_FWD_ADD>::B_ROWS == Cfg::B_ROWS,
+                  "the forward with an addend shares the forward's tiling");
+    if (addend != nullptr) return launch_sm100<BN, MODE_FWD_ADD>(pr, ma, mb, st);
     return launch_sm100<BN, MODE_FWD>(pr, ma, mb, st);
   }
+  if (addend != nullptr) return fail(TP_EUNSUPPORTED, "the gathered first layer runs on the sm_100 tensor-core path only");
   return a->dtype == TP_DTYPE_BF16 ? launch_simt<__nv_bfloat16, MODE_FWD>(pr, st) : launch_simt<float, MODE_FWD>(pr, st);
 }
 
-int tp_linear_backward(const tp_linear_grad_args* ga, void* stream) {
+}  // namespace
+}  // namespace tp
+
+extern "C" {
+
+int tp_linear_backward(const tp_linear_grad_args* ga, void* stream) { return linear_backward_impl(ga, 0, stream); }
+
+}  // extern "C"
+
+namespace tp {
+namespace {
+
+// tp_linear_backward with the row stride of dw given separately (dw_ld > dw_cols writes the
+// first dw_cols columns of wider rows, e.g. the dense columns of a one-hot first layer).
+int linear_backward_impl(const tp_linear_grad_args* ga, int dw_ld_in, void* stream) {
   if (!ga) return fail(TP_EINVAL, "null arguments");
   const tp_linear_args* a = &ga->fwd;
   int rc = check_linear(a);
@@ -450,14 +489,16 @@ int tp_linear_backward(const tp_linear_grad_args* ga, void* stream) {
     if (!a->x) return fail(TP_EINVAL, "x is required for the weight gradient");
     const int dw_rows = ga->dw_rows > 0 ? ga->dw_rows : a->max_out;
     const int dw_cols = ga->dw_cols > 0 ? ga->dw_cols : a->max_in;
+    const int dw_ld = dw_ld_in > 0 ? dw_ld_in : dw_cols;
     if (dw_rows > a->max_out || dw_cols > a->max_in) return fail(TP_EINVAL, "dw is larger than the weight storage");
+    if (dw_ld < dw_cols) return fail(TP_EINVAL, "dw row stride below its columns");
     LinearProblem pr = base_problem(a);
     pr.mode = MODE_WGRAD;
     pr.out = ga->dw;
     pr.out_rows = dw_rows;
     pr.out_cols = dw_cols;
-    pr.out_ld = dw_cols;
-    pr.out_ms = (long long)dw_rows * dw_cols;
+    pr.out_ld = dw_ld;
+    pr.out_ms = (long long)dw_rows * dw_ld;
     pr.copy_src = nullptr;
     pr.a_ptr = G;
     pr.b_ptr = a->x;
@@ -484,6 +525,11 @@ int tp_linear_backward(const tp_linear_grad_args* ga, void* stream) {
   }
   return TP_OK;
 }
+
+}  // namespace
+}  // namespace tp
+
+extern "C" {
 
 int tp_linear_backward_noalloc(const tp_linear_grad_args* ga, void* stream) {
   if (!ga) return fail(TP_EINVAL, "null arguments");
@@ -569,11 +615,11 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
   muon_geometry_kernel<<<(a->P + 255) / 256, 256, 0, st>>>(m);
   TP_CUDA_TRY(cudaGetLastError());
   if (a->P > 65535) return fail(TP_EINVAL, "at most 65535 members per Muon call");
-  dim3 tiles((a->max_in + 31) / 32, (a->max_out + 31) / 32, a->P);
+  dim3 tiles((a->max_in + MUON_TN - 1) / MUON_TN, (a->max_out + MUON_TM - 1) / MUON_TM, a->P);
   muon_prologue_kernel<<<tiles, 256, 0, st>>>(m);
   muon_norm_kernel<<<a->P, 256, 0, st>>>(m, (int)tiles.x);
   TP_CUDA_TRY(cudaGetLastError());
-  dim3 ngrid((L.C_s + 255) / 256, L.R_s / 8, a->P);
+  dim3 ngrid((L.C_s + 255) / 256, (L.R_s + 31) / 32, a->P);
   muon_normalize_kernel<<<ngrid, 256, 0, st>>>(m, 128, 256);
   TP_CUDA_TRY(cudaGetLastError());
   // quintic Newton-Schulz, coefficients of optim.py:477
@@ -910,10 +956,135 @@ int tp_weight_cast(const tp_weight_cast_args* a, void* stream) {
                 a->dst_rows, a->dst_cols, a->src_rows, a->src_cols);
   if (!aligned16(a->dst)) return fail(TP_EALIGN, "dst must be 16-byte aligned");
   if (a->P > 65535) return fail(TP_EINVAL, "too many members for one call");
-  WeightCastArgs k{a->src_rows, a->src_cols, a->dst_rows, a->dst_cols, a->out_features, a->in_features,
+  const int src_ld = a->src_ld > 0 ? a->src_ld : a->src_cols;
+  if (src_ld < a->src_cols) return fail(TP_EINVAL, "src_ld %d is below src_cols %d", src_ld, a->src_cols);
+  WeightCastArgs k{a->src_rows, a->src_cols, src_ld, a->dst_rows, a->dst_cols, a->out_features, a->in_features,
                    a->n_blocks, a->block_index, a->src, static_cast<__nv_bfloat16*>(a->dst)};
   const dim3 grid((a->src_rows + 7) / 8, a->P);
   weight_cast_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(k);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+int tp_weight_cast_transposed(const tp_weight_cast_t_args* a, void* stream) {
+  if (!a || a->P <= 0 || a->src_rows <= 0 || a->ncols <= 0 || a->col0 < 0 || !a->src || !a->dst)
+    return fail(TP_EINVAL, "bad transposed weight cast arguments");
+  if (a->src_ld < a->col0 + a->ncols) return fail(TP_EINVAL, "column block beyond the source rows");
+  if (a->dst_ld % 2 != 0 || a->dst_ld < (a->src_rows + 7) / 8 * 8)
+    return fail(TP_EINVAL, "dst_ld must be even and cover the source rows rounded up to 8");
+  if (!aligned16(a->dst)) return fail(TP_EALIGN, "dst must be 16-byte aligned");
+  if (a->P > 65535) return fail(TP_EINVAL, "too many members for one call");
+  WeightCastTArgs k{a->src_rows, a->src_ld, a->col0, a->ncols, a->dst_ld, a->out_features, a->src,
+                    static_cast<__nv_bfloat16*>(a->dst)};
+  const dim3 grid((a->ncols + CAST_T_J - 1) / CAST_T_J, (a->src_rows + CAST_T_N - 1) / CAST_T_N, a->P);
+  if (grid.y > 65535) return fail(TP_EINVAL, "too many rows for one call");
+  constexpr int smem = CAST_T_N * (CAST_T_J + 1) * 4;
+  TP_CUDA_TRY(cudaFuncSetAttribute(weight_cast_t_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  weight_cast_t_kernel<<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(k);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+}  // extern "C"
+
+namespace tp {
+namespace {
+
+constexpr int ONEHOT_MAX_ROWS = 16384;  // batch rows one sort CTA holds (128 KB of keys)
+
+int check_onehot(const tp_linear_args* a, const tp_onehot_args* oh) {
+  if (!oh) return fail(TP_EINVAL, "null one-hot arguments");
+  if (oh->n_cat <= 0 || oh->n_onehot <= 0 || !oh->cat_offsets || !oh->x_cat)
+    return fail(TP_EINVAL, "one-hot features, offsets and categories are required");
+  if (oh->n_dense < 0 || oh->n_dense > a->max_in) return fail(TP_EINVAL, "n_dense must lie in [0, max_in]");
+  if (a->B > ONEHOT_MAX_ROWS) return fail(TP_EUNSUPPORTED, "at most %d batch rows per gathered first layer", ONEHOT_MAX_ROWS);
+
+  if (a->P > 65535 || oh->n_cat > 65535) return fail(TP_EINVAL, "too many members or features for one call");
+  if (a->n_blocks) return fail(TP_EINVAL, "the first layer has no depth gating");
+  return TP_OK;
+}
+
+OneHotArgs onehot_args(const tp_linear_args* a, const tp_onehot_args* oh) {
+  OneHotArgs k{};
+  k.P = a->P;
+  k.B = a->B;
+  k.n_cat = oh->n_cat;
+  k.n_onehot = oh->n_onehot;
+  k.offsets = oh->cat_offsets;
+  k.x_cat = oh->x_cat;
+  k.x_cat_ms = oh->x_cat_member_stride;
+  k.row_index = oh->row_index;
+  k.row_index_ms = oh->row_index_member_stride;
+  k.sorted_keys = static_cast<uint64_t*>(oh->sorted_keys);
+  k.wt = static_cast<const __nv_bfloat16*>(oh->w_onehot_t);
+  k.wt_ld = oh->wt_ld;
+  k.out_f = a->out_features;
+  k.max_out = a->max_out;
+  k.addend = oh->addend;
+  k.add_ld = oh->addend_ld;
+  return k;
+}
+
+}  // namespace
+}  // namespace tp
+
+extern "C" {
+
+int tp_onehot_linear_forward(const tp_linear_args* a, const tp_onehot_args* oh, void* stream) {
+  int rc = check_linear(a);
+  if (rc) return rc;
+  if ((rc = check_onehot(a, oh))) return rc;
+  if (!use_tensor_cores(a)) return fail(TP_EUNSUPPORTED, "the gathered first layer runs on the sm_100 bf16 path only");
+  if (!oh->w_onehot_t || oh->wt_ld < (a->max_out + 7) / 8 * 8 || oh->wt_ld % 8 != 0 || !aligned16(oh->w_onehot_t))
+    return fail(TP_EINVAL, "w_onehot_t must be 16-byte aligned with wt_ld a multiple of 8 covering max_out");
+  if (!oh->addend || oh->addend_ld % 16 != 0 || oh->addend_ld < a->max_out || !aligned16(oh->addend))
+    return fail(TP_EINVAL, "addend must be 16-byte aligned with addend_ld a multiple of 16 covering max_out");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const OneHotArgs k = onehot_args(a, oh);
+  if (oh->sorted_keys) {  // the category sort the backward reads
+    int pow2 = 1;
+    while (pow2 < a->B) pow2 <<= 1;
+    const int smem = pow2 * 8;
+    TP_CUDA_TRY(cudaFuncSetAttribute(onehot_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    onehot_sort_kernel<<<dim3(oh->n_cat, a->P), std::min(1024, std::max(32, pow2 / 2)), smem, st>>>(k, pow2);
+    TP_CUDA_TRY(cudaGetLastError());
+  }
+  onehot_gather_kernel<<<dim3((a->B + 7) / 8, a->P), 256, 0, st>>>(k);
+  TP_CUDA_TRY(cudaGetLastError());
+  return linear_forward_impl(a, oh->addend, oh->addend_ld, stream);
+}
+
+int tp_onehot_linear_backward(const tp_linear_grad_args* ga, const tp_onehot_args* oh, void* stream) {
+  if (!ga) return fail(TP_EINVAL, "null arguments");
+  const tp_linear_args* a = &ga->fwd;
+  int rc = check_linear(a);
+  if (rc) return rc;
+  if ((rc = check_onehot(a, oh))) return rc;
+  if (!use_tensor_cores(a)) return fail(TP_EUNSUPPORTED, "the gathered first layer runs on the sm_100 bf16 path only");
+  const int dw_rows = ga->dw_rows > 0 ? ga->dw_rows : a->max_out;
+  if (ga->dw && !oh->sorted_keys) return fail(TP_EINVAL, "the weight gradient needs the forward's sorted_keys");
+  if (ga->dw && (ga->dw_cols != oh->n_dense + oh->n_onehot || dw_rows > a->max_out))
+    return fail(TP_EINVAL, "dw must be (P, <= max_out, n_dense + n_onehot)");
+  // activation gradient, dx and the dense columns of dw
+  tp_linear_grad_args d = *ga;
+  d.dw_cols = oh->n_dense;
+  if (d.dw && oh->n_dense == 0) d.dw = nullptr;
+  if ((rc = linear_backward_impl(&d, ga->dw_cols, stream))) return rc;
+  if (!ga->dw) return TP_OK;
+  // the one-hot columns: segmented sums of g over each category's rows
+  const bool need_g = a->relu || a->dropout_p || a->out_features || a->n_blocks;
+  OneHotArgs k = onehot_args(a, oh);
+  k.g = need_g ? ga->g : ga->dy;
+  k.g_ld = a->max_out;
+  k.g_bf16 = 1;
+  k.dw = ga->dw;
+  k.dw_rows = dw_rows;
+  k.dw_ld = ga->dw_cols;
+  k.dw_col0 = oh->n_dense;
+  const int nb_count = (dw_rows + ONEHOT_WG_N - 1) / ONEHOT_WG_N;
+  const long long blocks = ((long long)a->P * nb_count + ONEHOT_WG_WARPS - 1) / ONEHOT_WG_WARPS;
+  if (blocks > 0x7FFFFFFFLL) return fail(TP_EINVAL, "too many one-hot gradient tasks");
+  onehot_wgrad_kernel<<<(unsigned)blocks, 32 * ONEHOT_WG_WARPS, 0, static_cast<cudaStream_t>(stream)>>>(k, nb_count);
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;
 }

@@ -328,6 +328,47 @@ class _WeightCache:
         return self.value
 
 
+def _reusable(buf: Tensor | None, shape, dtype: torch.dtype, device) -> bool:
+    """True when `buf` has this geometry and nothing but its cache holds it (a pending
+    backward that saved it would see an in-place refresh)."""
+    if buf is None or tuple(buf.shape) != tuple(shape) or buf.dtype != dtype or buf.device != device:
+        return False
+    use_count = getattr(buf, '_use_count', None)
+    return use_count is not None and use_count() == 1
+
+
+class _OneHotWeightCache:
+    """bf16 copies of a first-layer weight (P, max_out, n_dense + n_onehot) for the gathered
+    one-hot path: the dense columns (tp_weight_cast, padded to `dense_cols`) and the one-hot
+    columns transposed, (P, n_onehot, rows) (tp_weight_cast_transposed), refreshed when the
+    weight or its widths change."""
+
+    def __init__(self) -> None:
+        self.key = None
+        self.dense = None
+        self.onehot_t = None
+
+    def get(self, w: Tensor, out_f: Tensor | None, n_dense: int, rows: int, dense_cols: int) -> tuple[Tensor, Tensor]:
+        key = (w.data_ptr(), w._version, tuple(w.shape), _WeightCache._tag(out_f), n_dense, rows, dense_cols)
+        if self.key != key:
+            self.key = None
+            P, _, C = w.shape
+            n_onehot = C - n_dense
+            dense, wt = self.dense, self.onehot_t
+            self.dense = self.onehot_t = None
+            if not _reusable(dense, (P, rows, dense_cols), torch.bfloat16, w.device):
+                dense = torch.zeros((P, rows, dense_cols), dtype=torch.bfloat16, device=w.device)
+            if not _reusable(wt, (P, n_onehot, rows), torch.bfloat16, w.device):
+                wt = torch.empty((P, n_onehot, rows), dtype=torch.bfloat16, device=w.device)
+            src = w.detach()
+            if n_dense > 0:
+                ops.weight_cast(src, dense, out_features=out_f, src_cols=n_dense)
+            ops.weight_cast_transposed(src, wt, col0=n_dense, ncols=n_onehot, out_features=out_f)
+            self.dense, self.onehot_t = dense, wt
+            self.key = key
+        return self.dense, self.onehot_t
+
+
 def _compute_dtype(x: Tensor) -> torch.dtype:
     if torch.is_autocast_enabled(x.device.type) and torch.get_autocast_dtype(x.device.type) == torch.bfloat16:
         return torch.bfloat16
@@ -399,6 +440,69 @@ def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features
     cfg = {'kw': kw, 'w_shape': tuple(weight.shape), 'in_cols': in_cols}
     with torch.autocast(x.device.type, enabled=False):
         y = _PackedLinearFn.apply(xc, weight, bias, wc, bc, cfg)
+    return y if rows == max_out else y[..., :max_out]
+
+
+class _OneHotLinearFn(torch.autograd.Function):
+    """First layer with gathered one-hot columns: one sort + gather + tensor-core launch
+    forward (`tp_onehot_linear_forward`), activation grad + dense dgrad/wgrad + one-hot
+    segmented sums backward (`tp_onehot_linear_backward`)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, w_dense, w_t, b_compute, cfg):
+        kw = cfg['kw']
+        y, state = ops.onehot_linear_forward(x, w_dense, b_compute, w_onehot_t=w_t, **cfg['onehot'], **kw,
+                                             need_sort=cfg['need_sort'])
+        ctx.cfg, ctx.state = cfg, state
+        ctx.save_for_backward(x, w_dense, y)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w_dense, y = ctx.saved_tensors
+        cfg = ctx.cfg
+        need_dx, need_dw, need_db = ctx.needs_input_grad[0], ctx.needs_input_grad[1], ctx.needs_input_grad[2]
+        dx, dw, db = ops.onehot_linear_backward(
+            dy.contiguous().to(torch.bfloat16), x, w_dense, y, ctx.state, **cfg['kw'], need_dx=need_dx,
+            need_db=need_db, dw_rows=cfg['w_shape'][1], db_cols=cfg['w_shape'][1])
+        if dx is not None and x.ndim == 2:
+            dx = dx.sum(PACK_DIM)
+        return dx, (dw if need_dw else None), db, None, None, None, None
+
+
+def _onehot_linear_call(linear: LinearPack, x: Tensor, onehot: dict, *, relu, dropout, stream,
+                        offset_stride: int = 1, offset_add: int = 0) -> Tensor:
+    """The first layer over [x | one-hot(categories)] with the one-hot columns gathered from
+    the weight instead of multiplied (bf16 tensor-core path).  `x`: the dense columns (the
+    numerical features or their embeddings), (B, n_dense) shared or (P, B, n_dense);
+    `onehot`: x_cat / cat_offsets / n_dense / row_index as `ops.onehot_linear_forward` takes
+    them."""
+    w, b = linear.weight, linear.bias
+    outf = _widths_cached(linear, 'out', linear.out_features)
+    member_base = 0 if stream is None else stream.member_base
+    seed = offset = 0
+    if dropout is not None and stream is not None:
+        seed = stream.seed
+        offset = stream.next_offset(offset_stride) + offset_add
+    max_out = w.shape[-2]
+    rows = _round8(max_out)
+    n_dense = int(onehot['n_dense'])
+    dense_cols = _round8(max(n_dense, 1))
+    xd = x.to(torch.bfloat16)
+    if xd.shape[-1] != dense_cols:
+        xd = nn.functional.pad(xd, (0, dense_cols - xd.shape[-1]))
+    xd = xd.contiguous()
+    cache = linear.__dict__.setdefault('_onehot_cache', _OneHotWeightCache())
+    wd, wt = cache.get(w, outf, n_dense, rows, dense_cols)
+    bc = b
+    if b is not None and rows != max_out:
+        bc = nn.functional.pad(b.detach(), (0, rows - max_out))
+    kw = dict(out_features=outf, relu=relu, dropout_p=dropout, seed=seed, offset=offset, member_base=member_base)
+    # the category sort serves the backward only
+    need_sort = torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (xd, w, b))
+    cfg = {'kw': kw, 'onehot': onehot, 'w_shape': tuple(w.shape), 'need_sort': need_sort}
+    with torch.autocast(x.device.type, enabled=False):
+        y = _OneHotLinearFn.apply(xd, w, b, wd, wt, bc, cfg)
     return y if rows == max_out else y[..., :max_out]
 
 
@@ -628,12 +732,17 @@ class MLPBackbonePack(ModulePack):
             raise NotImplementedError(f'fused blocks support ReLU or Identity, not {type(self.activation)}')
 
         def forward(self, x: Tensor, pack_idx: Tensor | None = None, *, n_blocks: Tensor | None = None,
-                    block_index: int = 0, stream: _DropoutStream | None = None, offset_stride: int = 1) -> Tensor:
+                    block_index: int = 0, stream: _DropoutStream | None = None, offset_stride: int = 1,
+                    onehot: dict | None = None) -> Tensor:
             drop = None
             if self.training:
                 drop = self.dropout.probabilities(self.pack_size, x.device).contiguous()
                 if isinstance(self.dropout.p, float) and self.dropout.p == 0.0:
                     drop = None
+            if onehot is not None:
+                return _onehot_linear_call(self.linear, x, onehot, relu=self._fused_relu(), dropout=drop,
+                                           stream=stream or self.dropout._stream, offset_stride=offset_stride,
+                                           offset_add=block_index)
             return _linear_call(self.linear, x, pack_idx, relu=self._fused_relu(), dropout=drop,
                                 stream=stream or self.dropout._stream, n_blocks=n_blocks, block_index=block_index,
                                 offset_stride=offset_stride, offset_add=block_index)
@@ -721,9 +830,13 @@ class MLPBackbonePack(ModulePack):
             self._nb_cache = (key, nb.to(torch.int32))
         return self._nb_cache[1]
 
-    def forward(self, x: Tensor, pack_idx: Tensor | None = None) -> Tensor:
+    def forward(self, x: Tensor, pack_idx: Tensor | None = None, *, onehot: dict | None = None) -> Tensor:
+        """`onehot`: the first block's one-hot columns, gathered instead of multiplied (`x` then
+        holds only the dense columns; see `_onehot_linear_call`)."""
         if pack_idx is not None:
             check_pack_idx(pack_idx, self.pack_size)
+            if onehot is not None:
+                raise ValueError('the gathered one-hot first layer runs on the whole pack')
         nb = self._n_blocks_i32(pack_idx)
         stream = self._stream
         base_offset = None
@@ -731,7 +844,8 @@ class MLPBackbonePack(ModulePack):
             if block.training and base_offset is None:
                 base_offset = stream.next_offset(self.max_n_blocks)
             sub = _OffsetView(stream, base_offset)
-            x = block(x, pack_idx, n_blocks=nb if i > 0 else None, block_index=i, stream=sub)
+            x = block(x, pack_idx, n_blocks=nb if i > 0 else None, block_index=i, stream=sub,
+                      **({'onehot': onehot} if i == 0 and onehot is not None else {}))
         return x
 
 
@@ -979,12 +1093,78 @@ class TabPack(ModulePack):
             return None
         return ops.tabpack_input(x_num, x_cat, self._cat_offsets, width, dtype, row_index=row_index)
 
+    # batch rows one gathered first-layer call sorts in shared memory (tp_onehot_linear_forward)
+    _GATHER_MAX_ROWS = 16384
+
+    # The gathered first layer in training too.  Off by default: its backward forms the one-hot
+    # columns' weight gradient as segmented sums on the CUDA cores, which measured slower on a
+    # B200 than the dense tensor-core weight gradient over the one-hot input (both write the
+    # same dW); forwards without a backward (evaluation, prediction) always gather.
+    gather_one_hot_in_training = False
+
+    def _gathered(self, x_num: Tensor | None, x_cat: Tensor | None, row_index: Tensor | None,
+                  pack_idx: Tensor | None) -> Tensor | None:
+        """The model output with the first layer's one-hot columns gathered from the weight
+        (one W column per feature and row) instead of multiplied, or None when this path does
+        not apply: it needs bf16 autocast on a CUDA device (the tensor-core path), categorical
+        features, the whole pack, inputs whose gradient is not requested, and no backward
+        (unless `gather_one_hot_in_training`)."""
+        if pack_idx is not None or self.cat_module is None or x_cat is None or not x_cat.is_cuda:
+            return None
+        if (torch.is_grad_enabled() and not self.gather_one_hot_in_training
+                and any(p.requires_grad for p in self.parameters())):
+            return None
+        if not (torch.is_autocast_enabled('cuda') and torch.get_autocast_dtype('cuda') == torch.bfloat16):
+            return None
+        if x_cat.shape[-1] != len(self._categorical_cardinalities) or x_cat.ndim not in (2, 3):
+            return None
+        if x_num is not None and (x_num.requires_grad or not x_num.is_cuda
+                                  or x_num.shape[-1] != self._n_numerical_features):
+            return None
+        P = self.pack_size
+        if row_index is not None:
+            if (not row_index.is_cuda or row_index.ndim != 2 or row_index.shape[0] != P or x_cat.ndim != 2
+                    or (x_num is not None and (x_num.ndim != 2 or x_num.shape[0] != x_cat.shape[0]))):
+                return None
+            B = row_index.shape[1]
+        else:
+            if x_num is not None and x_num.shape[:-1] != x_cat.shape[:-1]:
+                return None
+            if x_cat.ndim == 3 and x_cat.shape[0] != P:
+                return None
+            B = x_cat.shape[-2]
+        if B > self._GATHER_MAX_ROWS or B == 0:
+            return None
+        if (row_index is not None or x_cat.ndim == 3) and not self.training:
+            raise RuntimeError('Three-dimensional input requires training mode')
+        linear = self.backbone.blocks[0].linear
+        n_dense = linear.max_in_features - sum(self._categorical_cardinalities)
+        if self.num_module is None:
+            lead = (B,) if row_index is None and x_cat.ndim == 2 else (P, B)
+            if x_num is None:
+                dense = torch.zeros(*lead, 8, dtype=torch.bfloat16, device=x_cat.device)
+            else:
+                dense = ops.tabpack_input(x_num, None, self._cat_offsets, _round8(max(n_dense, 1)), torch.bfloat16,
+                                          row_index=row_index)
+        else:
+            if x_num is None:
+                raise ValueError('`x_num` is required when numerical embeddings are configured')
+            xn = x_num[row_index] if row_index is not None else x_num
+            if xn.ndim == 2:
+                xn = xn.expand(P, *xn.shape)
+            dense = self.num_module._flat(xn, None)
+        onehot = {'x_cat': x_cat, 'cat_offsets': self._cat_offsets, 'n_dense': n_dense, 'row_index': row_index}
+        return self.output(self.backbone(dense, None, onehot=onehot), None)
+
     def forward_rows(self, x_num: Tensor | None, x_cat: Tensor | None, row_index: Tensor,
                      pack_idx: Tensor | None = None) -> Tensor:
         """`forward(x_num[row_index], x_cat[row_index])`: the per-step batch gather of the
         training loop (`_training.py:2667-2669`), fused into the first-layer input build when
         the model has one-hot features and no numerical embeddings (otherwise gathered first).
         `row_index`: (pack_size, batch) dataset rows of every member."""
+        y = self._gathered(x_num, x_cat, row_index, pack_idx)
+        if y is not None:
+            return y
         fused = None if x_cat is None else self._fused_input(x_num, x_cat, row_index)
         if fused is None:
             return self(None if x_num is None else x_num[row_index], None if x_cat is None else x_cat[row_index],
@@ -1006,6 +1186,9 @@ class TabPack(ModulePack):
     def forward(self, x_num: Tensor | None, x_cat: Tensor | None, pack_idx: Tensor | None = None) -> Tensor:
         if x_num is None and x_cat is None:
             raise ValueError('Provide at least one of `x_num` and `x_cat`')
+        y = self._gathered(x_num, x_cat, None, pack_idx)
+        if y is not None:
+            return y
         fused = None if x_cat is None else self._fused_input(x_num, x_cat)
         if fused is not None:
             if fused.ndim == 3 and not self.training:

@@ -399,25 +399,139 @@ def tabpack_input(x_num: Tensor | None, x_cat: Tensor | None, cat_offsets: Tenso
 
 
 def weight_cast(src: Tensor, dst: Tensor, *, out_features: Tensor | None = None, in_features: Tensor | None = None,
-                n_blocks: Tensor | None = None, block_index: int = 0) -> Tensor:
+                n_blocks: Tensor | None = None, block_index: int = 0, src_cols: int | None = None) -> Tensor:
     """Write bf16(src) into `dst` (P, dst_rows, dst_cols) over each active member's rows
     r < out_features[m], zero beyond in_features[m]; other rows of `dst` keep their contents
-    (see `tp_weight_cast`).  Returns `dst`."""
+    (see `tp_weight_cast`).  `src_cols` takes only the first columns of each source row.
+    Returns `dst`."""
     src = _cuda('src', src, torch.float32)
     dst = _cuda('dst', dst, torch.bfloat16)
     if not src.is_contiguous() or not dst.is_contiguous():
         raise ValueError('weight_cast needs contiguous tensors')
-    P, R, C = src.shape
+    P, R, ld = src.shape
+    C = ld if src_cols is None else int(src_cols)
     if dst.shape[0] != P:
         raise ValueError('src and dst differ in their pack size')
     outf, inf, nb = (_i32(n, t) for n, t in (('out_features', out_features), ('in_features', in_features),
                                              ('n_blocks', n_blocks)))
-    a = _lib.WeightCastArgs(P=P, src_rows=R, src_cols=C, dst_rows=dst.shape[1], dst_cols=dst.shape[2],
+    a = _lib.WeightCastArgs(P=P, src_rows=R, src_cols=C, src_ld=ld, dst_rows=dst.shape[1], dst_cols=dst.shape[2],
                             out_features=_ptr(outf), in_features=_ptr(inf), n_blocks=_ptr(nb),
                             block_index=block_index, src=src.data_ptr(), dst=dst.data_ptr())
     check(load().tp_weight_cast(ctypes.byref(a), _stream()), 'tp_weight_cast')
     increment_version(dst)
     return dst
+
+
+def weight_cast_transposed(src: Tensor, dst: Tensor, *, col0: int, ncols: int,
+                           out_features: Tensor | None = None) -> Tensor:
+    """dst[m, j, n] = bf16(src[m, n, col0 + j]) over each member's rows n < out_features[m]
+    (zeros up to the next multiple of 8); see `tp_weight_cast_transposed`.  Returns `dst`."""
+    src = _cuda('src', src, torch.float32)
+    dst = _cuda('dst', dst, torch.bfloat16)
+    if not src.is_contiguous() or not dst.is_contiguous():
+        raise ValueError('weight_cast_transposed needs contiguous tensors')
+    P, R, ld = src.shape
+    if tuple(dst.shape[:2]) != (P, ncols):
+        raise ValueError('dst must be (P, ncols, dst_ld)')
+    outf = _i32('out_features', out_features)
+    a = _lib.WeightCastTArgs(P=P, src_rows=R, src_ld=ld, col0=int(col0), ncols=int(ncols), dst_ld=dst.shape[2],
+                             out_features=_ptr(outf), src=src.data_ptr(), dst=dst.data_ptr())
+    check(load().tp_weight_cast_transposed(ctypes.byref(a), _stream()), 'tp_weight_cast_transposed')
+    increment_version(dst)
+    return dst
+
+
+def _round(n: int, k: int) -> int:
+    return (n + k - 1) // k * k
+
+
+def _onehot_args(oh: dict) -> _lib.OneHotArgs:
+    a = _lib.OneHotArgs()
+    a.n_dense, a.n_cat, a.n_onehot = oh['n_dense'], oh['n_cat'], oh['n_onehot']
+    a.cat_offsets = oh['cat_offsets'].data_ptr()
+    a.x_cat = oh['x_cat'].data_ptr()
+    a.x_cat_member_stride = oh['x_cat_member_stride']
+    a.row_index = _ptr(oh.get('row_index'))
+    a.row_index_member_stride = oh.get('row_index_member_stride', 0)
+    a.w_onehot_t = _ptr(oh.get('w_onehot_t'))
+    a.wt_ld = 0 if oh.get('w_onehot_t') is None else oh['w_onehot_t'].shape[-1]
+    a.sorted_keys = _ptr(oh.get('sorted_keys'))
+    a.addend = _ptr(oh.get('addend'))
+    a.addend_ld = 0 if oh.get('addend') is None else oh['addend'].shape[-1]
+    return a
+
+
+def onehot_linear_forward(x: Tensor, weight: Tensor, bias: Tensor | None, *, x_cat: Tensor, cat_offsets: Tensor,
+                          n_dense: int, w_onehot_t: Tensor, row_index: Tensor | None = None,
+                          out_features: Tensor | None = None, relu: bool = False, dropout_p: Tensor | None = None,
+                          seed: int = 0, offset: int = 0, member_base: int = 0,
+                          need_sort: bool = True) -> tuple[Tensor, dict]:
+    """First layer over [dense | one-hot(x_cat)] with the one-hot columns gathered (bf16);
+    see `tp_onehot_linear_forward`.  x: dense input (P or 1, B, max_in) bf16; weight: the bf16
+    dense weight copy (P, max_out, max_in); w_onehot_t: (P, n_onehot, >= max_out) bf16.
+    x_cat: (B, n_cat) shared, (P, B, n_cat) per member, or dataset rows with row_index (P, B).
+    Returns (y, state) where state holds the category sort the backward needs (skipped with
+    need_sort=False: a forward that no backward follows)."""
+    weight = _cuda('weight', weight, torch.bfloat16)
+    x = _cuda('x', x, torch.bfloat16)
+    bias = _cuda('bias', bias, torch.float32)
+    dropout_p = _cuda('dropout_p', dropout_p, torch.float32)
+    outf = _i32('out_features', out_features)
+    xc = _cuda('x_cat', x_cat, torch.int64).contiguous()
+    P, max_out, _ = weight.shape
+    B = x.shape[-2]
+    n_cat = xc.shape[-1]
+    ri = None
+    if row_index is not None:
+        ri = _cuda('row_index', row_index, torch.int64).contiguous()
+        if ri.shape[-1] != B or (ri.ndim == 2 and ri.shape[0] not in (1, P)):
+            raise ValueError('row_index must be (B,) or (P, B)')
+        xcs, ris = 0, (B if ri.ndim == 2 and ri.shape[0] == P else 0)
+    else:
+        if xc.shape[-2] != B:
+            raise ValueError('x_cat rows must match the batch')
+        xcs, ris = (B if xc.ndim == 3 else 0), 0
+    n_onehot = int(w_onehot_t.shape[1])
+    dev = x.device
+    state = {
+        'n_dense': int(n_dense), 'n_cat': n_cat, 'n_onehot': n_onehot, 'cat_offsets': cat_offsets, 'x_cat': xc,
+        'x_cat_member_stride': xcs, 'row_index': ri, 'row_index_member_stride': ris, 'w_onehot_t': w_onehot_t,
+        'sorted_keys': torch.empty((P, n_cat, B), dtype=torch.int64, device=dev) if need_sort else None,
+        'addend': torch.empty((P, B, _round(max_out, 16)), dtype=torch.float32, device=dev),
+    }
+    y = torch.empty((P, B, max_out), dtype=torch.bfloat16, device=dev)
+    a = _linear_args(x, weight, bias, None, outf, None, 0, relu, dropout_p, seed, offset, member_base, y)
+    oa = _onehot_args(state)
+    check(load().tp_onehot_linear_forward(ctypes.byref(a), ctypes.byref(oa), _stream()), 'tp_onehot_linear_forward')
+    state['addend'] = state['w_onehot_t'] = None  # used by the forward only
+    return y, state
+
+
+def onehot_linear_backward(dy: Tensor, x: Tensor, weight: Tensor, y: Tensor, state: dict, *,
+                           out_features: Tensor | None = None, relu: bool = False, dropout_p: Tensor | None = None,
+                           seed: int = 0, offset: int = 0, member_base: int = 0, need_dx: bool = False,
+                           need_db: bool = True, dw_rows: int, db_cols: int) -> tuple[Tensor | None, Tensor, Tensor | None]:
+    """Backward of `onehot_linear_forward`: (dx of the dense input or None, dw (P, dw_rows,
+    n_dense + n_onehot) fp32, db fp32); see `tp_onehot_linear_backward`."""
+    weight = _cuda('weight', weight, torch.bfloat16)
+    dy = _cuda('dy', dy, torch.bfloat16)
+    dropout_p = _cuda('dropout_p', dropout_p, torch.float32)
+    outf = _i32('out_features', out_features)
+    P, max_out, max_in = weight.shape
+    B = x.shape[-2]
+    g = torch.empty_like(dy)
+    dx = torch.empty((P, B, max_in), dtype=torch.bfloat16, device=dy.device) if need_dx else None
+    cols = state['n_dense'] + state['n_onehot']
+    dw = torch.empty((P, dw_rows, cols), dtype=torch.float32, device=dy.device)
+    db = torch.empty((P, db_cols), dtype=torch.float32, device=dy.device) if need_db else None
+    ga = _lib.LinearGradArgs()
+    ga.fwd = _linear_args(x, weight, None, None, outf, None, 0, relu, dropout_p, seed, offset, member_base, None)
+    ga.dy, ga.y, ga.g = _ptr(dy), _ptr(y), _ptr(g)
+    ga.dbias, ga.dx, ga.dw = _ptr(db), _ptr(dx), _ptr(dw)
+    ga.dw_rows, ga.dw_cols, ga.db_cols = dw_rows, cols, db_cols
+    oa = _onehot_args(state)
+    check(load().tp_onehot_linear_backward(ctypes.byref(ga), ctypes.byref(oa), _stream()), 'tp_onehot_linear_backward')
+    return dx, dw, db
 
 
 def binary_roc_auc(scores: Tensor, labels: Tensor, workspace: Tensor | None = None) -> Tensor:
