@@ -541,7 +541,7 @@ def run_metrics(args) -> None:
                    'bce': {'ms': bce_ms, 'gbs': gbs(bce_bytes, bce_ms), 'hbm_frac': gbs(bce_bytes, bce_ms) / peaks['hbm_gbs']},
                    'roc_auc': {'ms': auc_ms, 'gbs': gbs(auc_bytes, auc_ms),
                                'hbm_frac': gbs(auc_bytes, auc_ms) / peaks['hbm_gbs'],
-                               'bytes_note': '75 B per element: key build + 4 radix passes + rank pass'},
+                               'bytes_note': '70 B per element: key build (9) + 4 radix passes (14 each) + rank pass (5)'},
                    'greedy': {'ms': greedy_ms, 'iterations': st[0], 'members': st[1],
                               'gbs': gbs(greedy_bytes, greedy_ms), 'hbm_frac': gbs(greedy_bytes, greedy_ms) / peaks['hbm_gbs']},
                    'peak_source': f'{kind} (copy)'},

@@ -76,6 +76,9 @@ typedef struct tp_linear_grad_args {
   int32_t db_cols;    /* row length of dbias (the parameter's real max_out) */
   int32_t g_ready;    /* 1: g (and dbias) already hold this call's activation gradient;
                          only the requested dx / dw GEMMs run */
+  int32_t dx_cols;    /* > 0: dx only for input columns < dx_cols (zeros beyond), e.g. the
+                         embedding columns of a first layer whose one-hot columns take no
+                         gradient; 0: every column */
 } tp_linear_grad_args;
 
 /* LinearPack.forward (src/tabpackage/nn.py:792-816) fused with the ReLU and
@@ -314,6 +317,11 @@ typedef struct tp_input_args {
   void* out;                     /* (rows, out_ld) */
   int32_t out_ld;
   int32_t out_dtype;             /* TP_DTYPE_F32 or TP_DTYPE_BF16 */
+  int32_t out_col0;              /* columns [out_col0, out_ld) of each row are written (the
+                                    numerical values start there); columns before it are left
+                                    as they are, e.g. an embedding written by
+                                    tp_cos_emb_forward.  out_col0 * element size must be a
+                                    multiple of 16 */
 } tp_input_args;
 int tp_tabpack_input(const tp_input_args* a, void* stream);
 int tp_cos_emb_forward(const tp_cos_emb_args* a, void* stream);

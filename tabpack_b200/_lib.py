@@ -40,7 +40,7 @@ class LinearGradArgs(ctypes.Structure):
         ('fwd', LinearArgs), ('dy', ctypes.c_void_p), ('y', ctypes.c_void_p), ('g', ctypes.c_void_p),
         ('dbias', ctypes.c_void_p), ('dx', ctypes.c_void_p), ('dw', ctypes.c_void_p),
         ('dw_rows', ctypes.c_int32), ('dw_cols', ctypes.c_int32), ('db_cols', ctypes.c_int32),
-        ('g_ready', ctypes.c_int32),
+        ('g_ready', ctypes.c_int32), ('dx_cols', ctypes.c_int32),
     ]
 
 
@@ -99,7 +99,7 @@ class InputArgs(ctypes.Structure):
         ('rows', ctypes.c_int64), ('n_num', ctypes.c_int32), ('n_cat', ctypes.c_int32), ('x_num', ctypes.c_void_p),
         ('x_cat', ctypes.c_void_p), ('row_index', ctypes.c_void_p), ('cat_offsets', ctypes.c_void_p),
         ('out', ctypes.c_void_p),
-        ('out_ld', ctypes.c_int32), ('out_dtype', ctypes.c_int32),
+        ('out_ld', ctypes.c_int32), ('out_dtype', ctypes.c_int32), ('out_col0', ctypes.c_int32),
     ]
 
 

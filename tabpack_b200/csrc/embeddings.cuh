@@ -183,6 +183,7 @@ struct InputArgs {
   const int32_t* offsets;   // (n_cat + 1,): first one-hot column of each feature (relative to n_num), total last
   void* out;                // (rows, out_ld)
   int out_ld, out_bf16;
+  int out_col0;             // first column written
 };
 
 template <bool BF16>
@@ -194,10 +195,11 @@ __global__ void __launch_bounds__(256) tabpack_input_kernel(const InputArgs a) {
   const long long src = a.row_index ? a.row_index[row] : row;  // the batch gather
   // pass 1: numerical columns and zeros, 16-byte stores
   const float* xr = a.x_num ? a.x_num + src * a.n_num : nullptr;
-  for (int c0 = lane * V; c0 < a.out_ld; c0 += 32 * V) {
+  for (int c0 = a.out_col0 + lane * V; c0 < a.out_ld; c0 += 32 * V) {
+    const int k0 = c0 - a.out_col0;  // numerical feature of column c0
     float val[V];
 #pragma unroll
-    for (int e = 0; e < V; ++e) val[e] = (xr != nullptr && c0 + e < a.n_num) ? xr[c0 + e] : 0.0f;
+    for (int e = 0; e < V; ++e) val[e] = (xr != nullptr && k0 + e < a.n_num) ? xr[k0 + e] : 0.0f;
     if (BF16) {
       uint4 u;
       u.x = pack_bf16x2(val[0], val[1]);
@@ -217,7 +219,7 @@ __global__ void __launch_bounds__(256) tabpack_input_kernel(const InputArgs a) {
     const int64_t v = a.x_cat[src * a.n_cat + f];
     const int start = a.offsets[f], card = a.offsets[f + 1] - start;
     if (v < 0 || v >= card) continue;  // the unknown category `card` stays all zeros
-    const size_t o = row * a.out_ld + a.n_num + start + (int)v;
+    const size_t o = row * a.out_ld + a.out_col0 + a.n_num + start + (int)v;
     if (BF16)
       reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(1.0f);
     else

@@ -454,9 +454,15 @@ int linear_backward_impl(const tp_linear_grad_args* ga, int dw_ld_in, void* stre
   }
 
   const bool tc = use_tensor_cores(a);
-  // 2. dx = g w   (dx = dy for depth-inactive members)
+  // 2. dx = g w   (dx = dy for depth-inactive members); with dx_cols, the input columns from
+  // dx_cols on are written as zeros without their GEMM tiles
   if (ga->dx) {
+    if (ga->dx_cols < 0 || (ga->dx_cols > 0 && (a->in_features || a->n_blocks)))
+      return fail(TP_EINVAL, "dx_cols needs a layer without per-member input widths or depth gating");
     LinearProblem pr = base_problem(a);
+    const bool dx_part = ga->dx_cols > 0 && ga->dx_cols < a->max_in;
+    // tensor cores: the members' input width (tiles past it are zero tiles)
+    if (dx_part && tc) pr.max_in = ga->dx_cols;
     pr.mode = MODE_DGRAD;
     pr.out = ga->dx;
     pr.out_rows = a->B;
@@ -482,6 +488,11 @@ int linear_backward_impl(const tp_linear_grad_args* ga, int dw_ld_in, void* stre
     } else {
       rc = bf16 ? launch_simt<__nv_bfloat16, MODE_DGRAD>(pr, st) : launch_simt<float, MODE_DGRAD>(pr, st);
       if (rc) return rc;
+      if (dx_part) {  // the CUDA-core path computes every column: clear the tail
+        const size_t es = bf16 ? 2 : 4;
+        TP_CUDA_TRY(cudaMemset2DAsync(static_cast<char*>(ga->dx) + ga->dx_cols * es, a->max_in * es, 0,
+                                      (a->max_in - ga->dx_cols) * es, (size_t)a->P * a->B, st));
+      }
     }
   }
   // 3. dw = g^T x
@@ -848,11 +859,12 @@ int tp_tabpack_input(const tp_input_args* a, void* stream) {
   if (a->n_cat > 0 && (!a->x_cat || !a->cat_offsets)) return fail(TP_EINVAL, "x_cat or cat_offsets is null");
   const bool bf16 = a->out_dtype == TP_DTYPE_BF16;
   if (!bf16 && a->out_dtype != TP_DTYPE_F32) return fail(TP_EINVAL, "bad output dtype");
-  if (a->out_ld % (bf16 ? 8 : 4) != 0 || a->out_ld < a->n_num)
-    return fail(TP_EINVAL, "out_ld must be a multiple of %d covering the columns", bf16 ? 8 : 4);
+  if (a->out_ld % (bf16 ? 8 : 4) != 0 || a->out_col0 < 0 || a->out_col0 % (bf16 ? 8 : 4) != 0 ||
+      a->out_ld < a->out_col0 + a->n_num)
+    return fail(TP_EINVAL, "out_ld and out_col0 must be multiples of %d with the columns inside a row", bf16 ? 8 : 4);
   if (!aligned16(a->out)) return fail(TP_EALIGN, "out must be 16-byte aligned");
   InputArgs k{a->rows,     a->n_num,   a->n_cat, a->n_num > 0 ? a->x_num : nullptr, a->n_cat > 0 ? a->x_cat : nullptr,
-              a->row_index, a->cat_offsets, a->out, a->out_ld, bf16 ? 1 : 0};
+              a->row_index, a->cat_offsets, a->out, a->out_ld, bf16 ? 1 : 0, a->out_col0};
   const long long blocks = (a->rows + 7) / 8;
   if (blocks > 0x7FFFFFFFLL) return fail(TP_EINVAL, "too many rows");
   cudaStream_t st = static_cast<cudaStream_t>(stream);

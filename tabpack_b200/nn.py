@@ -401,7 +401,7 @@ class _PackedLinearFn(torch.autograd.Function):
         dx, dw, db = ops.linear_backward(
             dy.contiguous().to(w_compute.dtype), x, w_compute, y, **cfg['kw'],
             need_dx=need_dx, need_dw=need_dw, need_db=need_db,
-            dw_shape=cfg['w_shape'][1:], db_cols=cfg['w_shape'][1])
+            dw_shape=cfg['w_shape'][1:], db_cols=cfg['w_shape'][1], dx_cols=cfg.get('dx_cols', 0))
         if dx is not None:
             if len(ctx.x_shape) == 2:
                 dx = dx.sum(PACK_DIM)
@@ -412,8 +412,9 @@ class _PackedLinearFn(torch.autograd.Function):
 
 def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features=None, out_features=None,
                   n_blocks=None, block_index=0, relu=False, dropout_p=None, seed=0, offset=0,
-                  member_base=0, cache: _WeightCache | None = None) -> Tensor:
-    """Functional form of the fused packed linear layer (see module docstring)."""
+                  member_base=0, cache: _WeightCache | None = None, dx_cols: int = 0) -> Tensor:
+    """Functional form of the fused packed linear layer (see module docstring).  `dx_cols` > 0:
+    the input's gradient is needed in its first dx_cols columns only (zeros beyond)."""
     if not x.is_cuda:
         raise RuntimeError('tabpack_b200 packs run on CUDA devices only')
     dtype = _compute_dtype(x)
@@ -437,7 +438,7 @@ def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features
         bc = nn.functional.pad(bias.detach(), (0, rows - max_out))
     kw = dict(in_features=in_features, out_features=out_features, n_blocks=n_blocks, block_index=block_index,
               relu=relu, dropout_p=dropout_p, seed=seed, offset=offset, member_base=member_base)
-    cfg = {'kw': kw, 'w_shape': tuple(weight.shape), 'in_cols': in_cols}
+    cfg = {'kw': kw, 'w_shape': tuple(weight.shape), 'in_cols': in_cols, 'dx_cols': int(dx_cols)}
     with torch.autocast(x.device.type, enabled=False):
         y = _PackedLinearFn.apply(xc, weight, bias, wc, bc, cfg)
     return y if rows == max_out else y[..., :max_out]
@@ -608,7 +609,7 @@ class LinearPack(ModulePack):
 
 
 def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stream, n_blocks, block_index,
-                 offset_stride: int = 1, offset_add: int = 0):
+                 offset_stride: int = 1, offset_add: int = 0, dx_cols: int = 0):
     w, b = linear.weight, linear.bias
     inf, outf = linear.in_features, linear.out_features
     member_base = 0 if stream is None else stream.member_base
@@ -635,7 +636,8 @@ def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stre
         inf, outf = _widths(inf), _widths(outf)
     return packed_linear(x, w, b, in_features=inf, out_features=outf, n_blocks=n_blocks,
                          block_index=block_index, relu=relu, dropout_p=dropout, seed=seed, offset=offset,
-                         member_base=member_base, cache=linear._cache if pack_idx is None else None)
+                         member_base=member_base, cache=linear._cache if pack_idx is None else None,
+                         dx_cols=dx_cols)
 
 
 class DropoutPack(ModulePack):
@@ -733,7 +735,7 @@ class MLPBackbonePack(ModulePack):
 
         def forward(self, x: Tensor, pack_idx: Tensor | None = None, *, n_blocks: Tensor | None = None,
                     block_index: int = 0, stream: _DropoutStream | None = None, offset_stride: int = 1,
-                    onehot: dict | None = None) -> Tensor:
+                    onehot: dict | None = None, dx_cols: int = 0) -> Tensor:
             drop = None
             if self.training:
                 drop = self.dropout.probabilities(self.pack_size, x.device).contiguous()
@@ -745,7 +747,7 @@ class MLPBackbonePack(ModulePack):
                                            offset_add=block_index)
             return _linear_call(self.linear, x, pack_idx, relu=self._fused_relu(), dropout=drop,
                                 stream=stream or self.dropout._stream, n_blocks=n_blocks, block_index=block_index,
-                                offset_stride=offset_stride, offset_add=block_index)
+                                offset_stride=offset_stride, offset_add=block_index, dx_cols=dx_cols)
 
     @enum.unique
     class ForwardImpl(enum.StrEnum):
@@ -830,9 +832,11 @@ class MLPBackbonePack(ModulePack):
             self._nb_cache = (key, nb.to(torch.int32))
         return self._nb_cache[1]
 
-    def forward(self, x: Tensor, pack_idx: Tensor | None = None, *, onehot: dict | None = None) -> Tensor:
+    def forward(self, x: Tensor, pack_idx: Tensor | None = None, *, onehot: dict | None = None,
+                dx_cols: int = 0) -> Tensor:
         """`onehot`: the first block's one-hot columns, gathered instead of multiplied (`x` then
-        holds only the dense columns; see `_onehot_linear_call`)."""
+        holds only the dense columns; see `_onehot_linear_call`).  `dx_cols`: the input's
+        gradient is needed in its first dx_cols columns only."""
         if pack_idx is not None:
             check_pack_idx(pack_idx, self.pack_size)
             if onehot is not None:
@@ -844,8 +848,12 @@ class MLPBackbonePack(ModulePack):
             if block.training and base_offset is None:
                 base_offset = stream.next_offset(self.max_n_blocks)
             sub = _OffsetView(stream, base_offset)
-            x = block(x, pack_idx, n_blocks=nb if i > 0 else None, block_index=i, stream=sub,
-                      **({'onehot': onehot} if i == 0 and onehot is not None else {}))
+            first = {}
+            if i == 0 and onehot is not None:
+                first['onehot'] = onehot
+            if i == 0 and dx_cols:
+                first['dx_cols'] = dx_cols
+            x = block(x, pack_idx, n_blocks=nb if i > 0 else None, block_index=i, stream=sub, **first)
         return x
 
 
@@ -878,6 +886,31 @@ class _CosineEmbeddingFn(torch.autograd.Function):
         x, w, b, aw, ab = ctx.saved_tensors
         dw, db, daw, dab = ops.cos_emb_backward(x, w, b, aw, ab, ctx.d_embedding, gy)
         return None, dw, db, daw, dab, None
+
+
+class _EmbeddedInputFn(torch.autograd.Function):
+    """The first layer's bf16 input [cosine embeddings | one-hot | zeros] built in one buffer:
+    `tp_cos_emb_forward` writes the embedding columns, `tp_tabpack_input` the one-hot block
+    after them.  Backward: the parameter gradients from the embedding columns of the input's
+    gradient, read in place."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, affine_weight, affine_bias, d_embedding, cfg):
+        P, F, D = affine_weight.shape
+        B = x.shape[-2]
+        out = torch.empty(P, B, cfg['width'], dtype=torch.bfloat16, device=x.device)
+        ops.cos_emb_forward(x, weight, bias, affine_weight, affine_bias, d_embedding, out=out)
+        ops.tabpack_input(None, cfg['x_cat'], cfg['cat_offsets'], cfg['width'], torch.bfloat16,
+                          row_index=cfg['row_index'], out=out, col0=F * D)
+        ctx.save_for_backward(x, weight, bias, affine_weight, affine_bias)
+        ctx.d_embedding = d_embedding
+        return out
+
+    @staticmethod
+    def backward(ctx, gx):
+        x, w, b, aw, ab = ctx.saved_tensors
+        dw, db, daw, dab = ops.cos_emb_backward(x, w, b, aw, ab, ctx.d_embedding, gx)
+        return None, dw, db, daw, dab, None, None
 
 
 class CosineEmbeddingsPack(ModulePack):
@@ -1049,7 +1082,9 @@ class TabPack(ModulePack):
         # columns (member m's embedding slots sit at f * max_d + k, the one-hot block after
         # all of them); the reference's first layer multiplies the whole padded width
         # (`nn.py:792-816` uses in_features only for initialisation), so this one does too.
-        self.backbone.blocks[0].linear.full_width_input = isinstance(d_in, list)
+        # (with embeddings of one size for all members the input widths all equal the maximum,
+        # so the whole width is the same computation)
+        self.backbone.blocks[0].linear.full_width_input = isinstance(d_in, list) or self.num_module is not None
         self.output = LinearPack(d_block, d_out, max_in_features=backbone_kwargs.get('max_d_block'),
                                  pack_size=pack_size)
         self._n_numerical_features = n_numerical_features
@@ -1156,6 +1191,44 @@ class TabPack(ModulePack):
         onehot = {'x_cat': x_cat, 'cat_offsets': self._cat_offsets, 'n_dense': n_dense, 'row_index': row_index}
         return self.output(self.backbone(dense, None, onehot=onehot), None)
 
+    def _embedded_input(self, x_num: Tensor | None, x_cat: Tensor | None, row_index: Tensor | None,
+                        pack_idx: Tensor | None) -> tuple[Tensor, int] | None:
+        """(bf16 first-layer input [cosine embeddings | one-hot], embedding columns) built in one
+        buffer (`_EmbeddedInputFn`), or None when the generic path has to run: it needs cosine
+        numerical embeddings, categorical features, bf16 autocast on a CUDA device, the whole
+        pack and an embedding width that keeps the one-hot block 16-byte aligned."""
+        if (not isinstance(self.num_module, CosineEmbeddingsPack) or self.cat_module is None or x_num is None
+                or x_cat is None or pack_idx is not None or not x_cat.is_cuda or not x_num.is_cuda):
+            return None
+        if not (torch.is_autocast_enabled('cuda') and torch.get_autocast_dtype('cuda') == torch.bfloat16):
+            return None
+        emb = self.num_module
+        P, F, D = emb.elementwise_affine_weight.shape
+        if (F * D) % 8 != 0 or x_cat.shape[-1] != len(self._categorical_cardinalities) or x_num.shape[-1] != F:
+            return None
+        if row_index is not None:
+            if row_index.ndim != 2 or row_index.shape[0] != P or x_cat.ndim != 2 or x_num.ndim != 2:
+                return None
+            x = x_num[row_index]
+            ri = row_index
+        else:
+            if x_num.shape[:-1] != x_cat.shape[:-1] or (x_cat.ndim == 3 and x_cat.shape[0] != P):
+                return None
+            x = x_num
+            B = x_cat.shape[-2]
+            # one-hot rows per member: the shared batch's rows for every member
+            ri = None if x_cat.ndim == 3 else torch.arange(B, device=x_cat.device).expand(P, B)
+        if x.ndim == 3 and x.stride(0) == 0:
+            x = x[0]
+        width = self.backbone.blocks[0].linear.max_in_features
+        width = _round8(width)
+        cfg = {'x_cat': x_cat, 'cat_offsets': self._cat_offsets, 'row_index': ri, 'width': width}
+        prm = [emb.weight, emb.bias, emb.elementwise_affine_weight, emb.elementwise_affine_bias]
+        d32 = None if emb.d_embedding is None else emb.d_embedding.to(torch.int32)
+        with torch.autocast(x.device.type, enabled=False):
+            buf = _EmbeddedInputFn.apply(x.float().contiguous(), *[p.contiguous() for p in prm], d32, cfg)
+        return buf, F * D
+
     def forward_rows(self, x_num: Tensor | None, x_cat: Tensor | None, row_index: Tensor,
                      pack_idx: Tensor | None = None) -> Tensor:
         """`forward(x_num[row_index], x_cat[row_index])`: the per-step batch gather of the
@@ -1165,6 +1238,9 @@ class TabPack(ModulePack):
         y = self._gathered(x_num, x_cat, row_index, pack_idx)
         if y is not None:
             return y
+        emb = self._embedded_input(x_num, x_cat, row_index, pack_idx)
+        if emb is not None:
+            return self.output(self.backbone(emb[0], pack_idx, dx_cols=emb[1]), pack_idx)
         fused = None if x_cat is None else self._fused_input(x_num, x_cat, row_index)
         if fused is None:
             return self(None if x_num is None else x_num[row_index], None if x_cat is None else x_cat[row_index],
@@ -1186,13 +1262,18 @@ class TabPack(ModulePack):
     def forward(self, x_num: Tensor | None, x_cat: Tensor | None, pack_idx: Tensor | None = None) -> Tensor:
         if x_num is None and x_cat is None:
             raise ValueError('Provide at least one of `x_num` and `x_cat`')
+        # per-member batches are a training-time input (PackView, `nn.py:88-131`); a shared batch
+        # may still become per-member inside (numerical embeddings)
+        if not self.training and any(t is not None and t.ndim == 3 for t in (x_num, x_cat)):
+            raise RuntimeError('Three-dimensional input requires training mode')
         y = self._gathered(x_num, x_cat, None, pack_idx)
         if y is not None:
             return y
+        emb = self._embedded_input(x_num, x_cat, None, pack_idx)
+        if emb is not None:
+            return self.output(self.backbone(emb[0], pack_idx, dx_cols=emb[1]), pack_idx)
         fused = None if x_cat is None else self._fused_input(x_num, x_cat)
         if fused is not None:
-            if fused.ndim == 3 and not self.training:
-                raise RuntimeError('Three-dimensional input requires training mode')
             return self.output(self.backbone(fused, pack_idx), pack_idx)
         parts = []
         if x_num is not None:
@@ -1213,7 +1294,5 @@ class TabPack(ModulePack):
                 oh = oh.expand(parts[0].shape[0], *oh.shape)
             parts.append(oh)
         x = torch.cat(parts, -1) if len(parts) > 1 else parts[0]
-        if x.ndim == 3 and not self.training:
-            raise RuntimeError('Three-dimensional input requires training mode')
         x = self.backbone(x, pack_idx)
         return self.output(x, pack_idx)

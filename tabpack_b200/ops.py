@@ -127,8 +127,10 @@ def linear_backward(
     need_db: bool = True,
     dw_shape: tuple[int, int] | None = None,
     db_cols: int | None = None,
+    dx_cols: int = 0,
 ) -> tuple[Tensor | None, Tensor | None, Tensor | None]:
-    """Backward of `linear_forward`: returns (dx, dw, db); dw/db are fp32."""
+    """Backward of `linear_forward`: returns (dx, dw, db); dw/db are fp32.  With dx_cols > 0
+    only dx's first dx_cols columns are computed (the rest are zeros)."""
     weight = _cuda('weight', weight)
     x = _cuda('x', x, weight.dtype)
     dy = _cuda('dy', dy, weight.dtype)
@@ -151,6 +153,7 @@ def linear_backward(
     ga.dy, ga.y, ga.g = _ptr(dy), _ptr(y), _ptr(g)
     ga.dbias, ga.dx, ga.dw = _ptr(db), _ptr(dx), _ptr(dw)
     ga.dw_rows, ga.dw_cols, ga.db_cols = rows, cols, dbc
+    ga.dx_cols = int(dx_cols)
     check(load().tp_linear_backward(ctypes.byref(ga), _stream()), 'tp_linear_backward')
     return dx, dw, db
 
@@ -379,21 +382,29 @@ def cos_emb_backward(x: Tensor, weight: Tensor, bias: Tensor, affine_weight: Ten
 
 
 def tabpack_input(x_num: Tensor | None, x_cat: Tensor | None, cat_offsets: Tensor, width: int,
-                  dtype: torch.dtype, row_index: Tensor | None = None) -> Tensor:
+                  dtype: torch.dtype, row_index: Tensor | None = None, *, out: Tensor | None = None,
+                  col0: int = 0) -> Tensor:
     """[x_num | one-hot(x_cat)] in `dtype`, zero-padded to `width` columns; leading dimensions
     of the inputs are kept, or with `row_index` (any shape, int64) output row r is built from
-    dataset row row_index[r] and the output takes row_index's shape; see `tp_tabpack_input`."""
+    dataset row row_index[r] and the output takes row_index's shape; see `tp_tabpack_input`.
+    With `out` (contiguous, last dimension `width`) the columns from `col0` on are written into
+    it and the columns before are left as they are."""
     ref = x_num if x_num is not None else x_cat
     ri = None if row_index is None else _cuda('row_index', row_index).to(torch.int64).contiguous()
     lead = ref.shape[:-1] if ri is None else ri.shape
     rows = ref[..., 0].numel() if ri is None else ri.numel()
     xn = None if x_num is None else _cuda('x_num', x_num).to(torch.float32).contiguous()
     xc = None if x_cat is None else _cuda('x_cat', x_cat).to(torch.int64).contiguous()
-    out = torch.empty(*lead, width, dtype=dtype, device=ref.device)
+    if out is None:
+        out = torch.empty(*lead, width, dtype=dtype, device=ref.device)
+    elif (out.dtype != dtype or out.shape[-1] != width or not out.is_contiguous()
+          or out.numel() != rows * width):
+        raise ValueError('out must be a contiguous tensor of the rows x width output')
     a = _lib.InputArgs(rows=rows, n_num=0 if xn is None else xn.shape[-1], n_cat=0 if xc is None else xc.shape[-1],
                        x_num=_ptr(xn), x_cat=_ptr(xc), row_index=_ptr(ri), cat_offsets=cat_offsets.data_ptr(),
                        out=out.data_ptr(),
-                       out_ld=width, out_dtype=TP_DTYPE_BF16 if dtype == torch.bfloat16 else TP_DTYPE_F32)
+                       out_ld=width, out_dtype=TP_DTYPE_BF16 if dtype == torch.bfloat16 else TP_DTYPE_F32,
+                       out_col0=int(col0))
     check(load().tp_tabpack_input(ctypes.byref(a), _stream()), 'tp_tabpack_input')
     return out
 

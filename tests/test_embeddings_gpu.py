@@ -123,3 +123,65 @@ def test_tabpack_with_cosine_embeddings_matches_reference(golden):
     (y * torch.from_numpy(g['dy']).float().cuda()).sum().backward()
     for k, p in model.named_parameters():
         assert _rel(p.grad.cpu().numpy(), g['grad.' + k]) < 1e-4, k
+
+
+def _cosine_model(P=4):
+    from tabpack_b200 import nn as bnn
+
+    return bnn.TabPack(
+        n_numerical_features=6, categorical_cardinalities=[5, 3, 9], d_out=2, n_blocks=[1, 2, 3, 2][:P],
+        d_block=[32, 16, 48, 24][:P], dropout=[0.1, 0.2, 0.0, 0.3][:P], pack_size=P, max_d_block=48,
+        numerical_embeddings={'type': bnn.CosineEmbeddingsPack, 'd_embedding': [4, 8, 3, 6][:P], 'max_d_embedding': 8,
+                              'init_scale': [0.1, 0.05, 0.2, 0.1][:P]}).cuda()
+
+
+@pytest.mark.parametrize('rows', [False, True])
+def test_embedded_first_layer_input_equals_concat(rows):
+    """Under bf16 autocast the first layer's input [embeddings | one-hot] is built in one bf16
+    buffer and the embedding gradient is read from the input's gradient in place; outputs and
+    every gradient equal the generic path (embedding, one-hot, concat, cast) bit for bit."""
+    torch.manual_seed(2)
+    model = _cosine_model().train()
+    g = torch.Generator(device='cuda').manual_seed(4)
+    N, B = 300, 200
+    x_num = torch.randn(N, 6, device='cuda', generator=g)
+    x_cat = torch.stack([torch.randint(0, c + 1, (N,), device='cuda', generator=g) for c in (5, 3, 9)], -1)
+    idx = torch.randint(0, N, (4, B), device='cuda', generator=g)
+    dy = torch.randn(4, B if rows else N, 2, device='cuda', generator=g)
+
+    def run(embedded):
+        model.zero_grad(set_to_none=True)
+        model.backbone._stream.seed, model.backbone._stream.calls = 11, 0
+        if not embedded:
+            model._embedded_input = lambda *a, **k: None
+        try:
+            with torch.autocast('cuda', dtype=torch.bfloat16):
+                y = model.forward_rows(x_num, x_cat, idx) if rows else model(x_num, x_cat)
+            (y.float() * dy).sum().backward()
+        finally:
+            model.__dict__.pop('_embedded_input', None)
+        return y.detach(), {k: p.grad.clone() for k, p in model.named_parameters() if p.grad is not None}
+
+    y1, g1 = run(True)
+    y0, g0 = run(False)
+    assert torch.equal(y1, y0)
+    assert set(g1) == set(g0)
+    for k in g0:
+        assert torch.equal(g1[k], g0[k]), k
+
+
+def test_cosine_embeddings_model_predicts_in_eval_mode():
+    """A shared 2-D batch is a valid evaluation input with numerical embeddings (the
+    per-member embedding is internal); a per-member 3-D batch still needs training mode."""
+    model = _cosine_model().eval()
+    g = torch.Generator(device='cuda').manual_seed(7)
+    x_num = torch.randn(50, 6, device='cuda', generator=g)
+    x_cat = torch.stack([torch.randint(0, c, (50,), device='cuda', generator=g) for c in (5, 3, 9)], -1)
+    with torch.autocast('cuda', dtype=torch.bfloat16):
+        y = model(x_num, x_cat)
+    assert y.shape == (4, 50, 2) and torch.isfinite(y).all()
+    with torch.no_grad():
+        y32 = model(x_num, x_cat)
+    assert (y.float() - y32).abs().max() < 5e-2 * y32.abs().max()
+    with pytest.raises(RuntimeError, match='training mode'):
+        model(x_num.expand(4, 50, 6), x_cat.expand(4, 50, 3))
