@@ -591,6 +591,9 @@ def run_train(args) -> None:
                           optimizer=dict(type='muon', adamw_lr=1e-3, weight_decay=1e-5, muon_lr=2e-2),
                           loss='bce', seed=0, device=dev, autocast_bf16=True, member_range=(0, P))
     steps = args.steps
+    # backward on the calling thread (kernels are asynchronous either way), so that the NVTX
+    # range below also holds the backward launches
+    torch.autograd.set_multithreading_enabled(False)
     trainer.fit_epoch({k: v[: batch * args.warmup] for k, v in data.items()}, batch_size=batch, epoch=0)
     torch.cuda.synchronize()
     sub = {k: v[: batch * steps] for k, v in data.items()}

@@ -283,6 +283,15 @@ class _DropoutStream:
         return off
 
 
+def _reusable(buf: Tensor | None, shape, dtype: torch.dtype, device) -> bool:
+    """True when `buf` has this geometry and nothing but its cache holds it (a pending
+    backward that saved it would see an in-place refresh)."""
+    if buf is None or tuple(buf.shape) != tuple(shape) or buf.dtype != dtype or buf.device != device:
+        return False
+    use_count = getattr(buf, '_use_count', None)
+    return use_count is not None and use_count() == 1
+
+
 class _WeightCache:
     """bf16 copy of an fp32 weight pack, refreshed when the weight changes (optimizer steps
     and in-place updates bump the parameter's version counter).
@@ -312,9 +321,7 @@ class _WeightCache:
             if dtype == torch.bfloat16 and w.dtype == torch.float32 and w.is_cuda and w.is_contiguous():
                 shape = (w.shape[0], rows, cols)
                 buf = self.value
-                use_count = getattr(buf, '_use_count', None)
-                if (buf is None or tuple(buf.shape) != shape or buf.dtype != dtype or buf.device != w.device
-                        or use_count is None or use_count() != 1):
+                if not _reusable(buf, shape, dtype, w.device):
                     buf = torch.zeros(shape, dtype=dtype, device=w.device)
                 self.value = None
                 ops.weight_cast(w.detach(), buf, out_features=out_f, in_features=in_f, n_blocks=nb, block_index=bi)
@@ -326,15 +333,6 @@ class _WeightCache:
                 self.value = wd.contiguous()
             self.key = key
         return self.value
-
-
-def _reusable(buf: Tensor | None, shape, dtype: torch.dtype, device) -> bool:
-    """True when `buf` has this geometry and nothing but its cache holds it (a pending
-    backward that saved it would see an in-place refresh)."""
-    if buf is None or tuple(buf.shape) != tuple(shape) or buf.dtype != dtype or buf.device != device:
-        return False
-    use_count = getattr(buf, '_use_count', None)
-    return use_count is not None and use_count() == 1
 
 
 class _OneHotWeightCache:
