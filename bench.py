@@ -617,6 +617,105 @@ def run_train(args) -> None:
         'clocks': clocks.summary()}), flush=True)
 
 
+def run_inference(args) -> None:
+    """Inference of the packed-ensemble inference configuration: `members` members over all
+    ranks (1024 by default; rank r predicts its share), depth U{2,3}, width U{256..1024 step
+    8}, 200 numerical features N(0, 1), a 10-class head, batches of 65 536 rows in bf16.  A step
+    is every member's class probabilities for one batch (members run in groups of 128) and the
+    ensemble head, the mean of 64 seeded members' probabilities, summed over ranks with an
+    NCCL all-reduce.  value = rows/s (strong scaling: the pack is fixed); e2e copies each
+    batch from pinned host memory and reads the ensemble head back."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from tabpack_b200.training import PackPredictor, PackTrainer
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        dist.init_process_group('nccl', device_id=dev, timeout=datetime.timedelta(seconds=120))
+    total, B, n_num, C = args.members, 65536, 200, 10
+    rng = np.random.default_rng(31)
+    per = [dict(n_blocks=int(rng.integers(2, 4)), d_block=int(rng.integers(32, 129)) * 8, dropout=0.0)
+           for _ in range(total)]
+    model = dict(n_numerical_features=n_num, categorical_cardinalities=[], d_out=C, max_d_block=1024, max_n_blocks=3)
+    trainer = PackTrainer(n_members=total, model=model, per_member_model=per,
+                          optimizer=dict(type='adamw', lr=1e-3, weight_decay=0.0), loss='ce', seed=0, device=dev,
+                          autocast_bf16=True)
+    ens = torch.from_numpy(np.random.default_rng(7).choice(total, 64, replace=False)).to(dev)
+    predictor = PackPredictor(trainer, {'ensemble': ens})
+    # ragged GEMM FLOPs per row of this rank's members (first layer, hidden blocks, head)
+    flops_row = 0.0
+    for pm in per[trainer.lo: trainer.hi]:
+        w = pm['d_block']
+        flops_row += 2.0 * (n_num * w + (pm['n_blocks'] - 1) * w * w + w * C)
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    x = torch.randn(B, n_num, device=dev, generator=g)
+    x_host = x.cpu().pin_memory()
+    chunk = 128
+
+    def step():
+        return predictor(x, None, eval_batch_size=B, member_chunk=chunk)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    # end to end: batch from pinned host memory, ensemble head back to the host
+    xd = torch.empty_like(x)
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        xd.copy_(x_host, non_blocking=True)
+        _, heads = predictor(xd, None, eval_batch_size=B, member_chunk=chunk)
+        head = heads['ensemble'].cpu()
+    t1.record()
+    barrier()
+    e2e_ms = t0.elapsed_time(t1) / args.steps
+    t = torch.tensor([ms, e2e_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(t[0]), float(t[1])
+    flops = torch.tensor([flops_row * B], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(flops)
+    peaks, kind = load_peaks()
+    tflops = float(flops[0]) / (ms / 1e3) / 1e12
+    if rank == 0:
+        print(json.dumps({
+            'metric': 'rows/sec inference (every member of the pack, ensemble head)', 'value': B / (ms / 1e3),
+            'unit': 'rows/s', 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms,
+            'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
+            'config': {'workload': f'{total} members, depth U{{2,3}}, width U{{256..1024}}, 200 numerical features, '
+                                   f'10 classes, batch {B} rows, ensemble of 64 members, members in groups of {chunk}',
+                       'member_rows_per_s': total * B / (ms / 1e3), 'ragged_tflops': tflops,
+                       'frac_of_sustained_bf16': tflops / peaks['bf16_tflops_sustained'], 'peak_source': kind,
+                       'head_checksum': float(head.double().sum())},
+            'e2e': {'value': B / (e2e_ms / 1e3), 'unit': 'rows/s', 'h2d_bytes_per_step': x.numel() * 4,
+                    'd2h_bytes_per_step': B * C * 4},
+            'clocks': clocks.summary()}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main() -> None:
     global MEMBERS
     ap = argparse.ArgumentParser()
@@ -628,14 +727,14 @@ def main() -> None:
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--members', type=int, default=None,
                     help='members per GPU (default 256 for the layer workload, 1024 for the optimizer)')
-    ap.add_argument('--workload', choices=['layer', 'optimizer', 'metrics', 'train'], default='layer',
+    ap.add_argument('--workload', choices=['layer', 'optimizer', 'metrics', 'train', 'inference'], default='layer',
                     help='layer: the packed-block fwd+bwd benchmark (default); optimizer: grouped Muon step; '
                          'metrics: validation metrics, ROC AUC and greedy selection')
     ap.add_argument('--embeddings', choices=['none', 'cosine'], default='none',
                     help='train workload: numerical features raw or through cosine embeddings')
     args = ap.parse_args()
     if args.members is None:
-        args.members = {'optimizer': 1024, 'metrics': 512, 'train': 512}.get(args.workload, MEMBERS)
+        args.members = {'optimizer': 1024, 'metrics': 512, 'train': 512, 'inference': 1024}.get(args.workload, MEMBERS)
     MEMBERS = args.members
     if args.workload == 'optimizer':
         run_optimizer(args)
@@ -645,6 +744,9 @@ def main() -> None:
         return
     if args.workload == 'train':
         run_train(args)
+        return
+    if args.workload == 'inference':
+        run_inference(args)
         return
     if args.impl == 'reference':
         run_reference(args)

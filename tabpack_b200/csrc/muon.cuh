@@ -206,6 +206,10 @@ __global__ void __launch_bounds__(256) muon_normalize_kernel(MuonArgs a, int row
   if (nrm2 == 0.0f) return;  // all-zero update: Newton-Schulz is skipped for this member
   const float nrm = __bfloat162float(__float2bfloat16_rn(sqrtf(nrm2)));
   const float den = __bfloat162float(__float2bfloat16_rn(nrm + 1e-7f));
+  // x / den per element from one division per thread: q = x * (1 / den) and one correction
+  // step q + (x - q den) / den with fused multiply-adds (Markstein's method for a correctly
+  // rounded quotient from the correctly rounded reciprocal)
+  const float rcp = 1.0f / den;
   uint4 u[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -221,7 +225,14 @@ __global__ void __launch_bounds__(256) muon_normalize_kernel(MuonArgs a, int row
     if (row < r) {
 #pragma unroll
       for (int e = 0; e < 8; ++e)
-        h[e] = (col + e < c) ? __float2bfloat16_rn(__bfloat162float(h[e]) / den) : __float2bfloat16_rn(0.0f);
+        if (col + e < c) {
+          const float xv = __bfloat162float(h[e]);
+          float q = xv * rcp;
+          q = fmaf(fmaf(-q, den, xv), rcp, q);
+          h[e] = __float2bfloat16_rn(q);
+        } else {
+          h[e] = __float2bfloat16_rn(0.0f);
+        }
     }
     *reinterpret_cast<uint4*>(a.x + (size_t)mem * a.R_s * a.C_s + (size_t)row * a.C_s + col) = u[i];
   }

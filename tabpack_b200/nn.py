@@ -613,8 +613,8 @@ def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stre
     member_base = 0 if stream is None else stream.member_base
     if pack_idx is not None:
         check_pack_idx(pack_idx, linear.pack_size)
+        # (n_blocks comes from the backbone already selected to the same members)
         w, b, inf, outf = (_select(t, pack_idx) for t in (w, b, inf, outf))
-        n_blocks = _select(n_blocks, pack_idx)
         if dropout is not None:
             raise NotImplementedError('pack_idx with training-mode dropout is not supported; '
                                       'use temporarily_select or remove')

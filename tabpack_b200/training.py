@@ -201,17 +201,25 @@ class PackTrainer:
 
     # ------------------------------------------------------------------ evaluation
     @torch.no_grad()
-    def predict_local(self, data: dict, *, eval_batch_size: int = 32768) -> Tensor:
-        """Transformed predictions of this rank's members on a shared dataset."""
+    def predict_local(self, data: dict, *, eval_batch_size: int = 32768, member_chunk: int | None = None) -> Tensor:
+        """Transformed predictions of this rank's members on a shared dataset.  `member_chunk`
+        runs the members in groups of that size (bounds the activations of wide packs on large
+        batches: each group is a `pack_idx` selection of the pack)."""
         self.model.eval()
         n = len(data['y']) if 'y' in data else len(next(iter(data.values())))
+        P = self.hi - self.lo
+        chunks = [None] if member_chunk is None or member_chunk >= P else [
+            torch.arange(c, min(P, c + member_chunk), device=self.device) for c in range(0, P, member_chunk)]
         parts = []
         for i in range(0, n, eval_batch_size):
             xn = data['x_num'][i: i + eval_batch_size] if 'x_num' in data else None
             xc = data['x_cat'][i: i + eval_batch_size] if 'x_cat' in data else None
-            with torch.autocast('cuda', dtype=torch.bfloat16, enabled=self.autocast):
-                out = self.model(xn, xc)
-            parts.append(transform(self.loss, out.float()))
+            outs = []
+            for idx in chunks:
+                with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16, enabled=self.autocast):
+                    out = self.model(xn, xc, idx)
+                outs.append(transform(self.loss, out.float()))
+            parts.append(outs[0] if len(outs) == 1 else torch.cat(outs, 0))
         return torch.cat(parts, 1)
 
     def _score(self, y_val: Tensor) -> PackScore:
@@ -241,14 +249,15 @@ class PackPredictor(torch.nn.Module):
         self.ensembles = {k: v.to(trainer.device, torch.int64) for k, v in ensembles.items()}
 
     @torch.no_grad()
-    def forward(self, x_num: Tensor | None, x_cat: Tensor | None) -> tuple[Tensor, dict[str, Tensor]]:
+    def forward(self, x_num: Tensor | None, x_cat: Tensor | None, *, eval_batch_size: int = 32768,
+                member_chunk: int | None = None) -> tuple[Tensor, dict[str, Tensor]]:
         t = self.trainer
         data = {}
         if x_num is not None:
             data['x_num'] = x_num
         if x_cat is not None:
             data['x_cat'] = x_cat
-        local = t.predict_local(data)  # (P_local, B[, C])
+        local = t.predict_local(data, eval_batch_size=eval_batch_size, member_chunk=member_chunk)  # (P_local, B[, C])
         flat = local.reshape(local.shape[0], -1).contiguous()
         heads = {}
         for name, gidx in self.ensembles.items():

@@ -217,3 +217,24 @@ def test_bf16_weight_copy_follows_optimizer_steps(opt):
     with torch.autocast('cuda', dtype=torch.bfloat16):
         a, b = model(x_num, x_cat), fresh(x_num, x_cat)
     assert torch.equal(a, b)
+
+
+def test_pack_idx_forward_selects_members():
+    """A forward over selected members (non-prefix, unordered: depth gating and widths are
+    selected once) equals those members' rows of the whole pack's forward."""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+    from tabpack_b200 import nn as bnn
+
+    torch.manual_seed(5)
+    P = 5
+    model = bnn.TabPack(n_numerical_features=4, categorical_cardinalities=[3, 6], d_out=2, n_blocks=[1, 3, 2, 3, 1],
+                        d_block=[16, 48, 24, 32, 40], dropout=[0.1] * P, pack_size=P, max_d_block=48).cuda().eval()
+    g = torch.Generator(device='cuda').manual_seed(2)
+    x_num = torch.randn(64, 4, device='cuda', generator=g)
+    x_cat = torch.stack([torch.randint(0, c, (64,), device='cuda', generator=g) for c in (3, 6)], -1)
+    with torch.no_grad():
+        whole = model(x_num, x_cat)
+        for idx in ([4, 1], [3], [2, 0, 4]):
+            part = model(x_num, x_cat, torch.tensor(idx, device='cuda'))
+            assert torch.equal(part, whole[idx]), idx

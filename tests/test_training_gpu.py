@@ -127,3 +127,23 @@ def test_sharding_is_bit_invariant_with_cosine_embeddings():
             assert torch.equal(v, sd[k][lo: lo + v.shape[0]]), k
     assert torch.isfinite(loss).all()
     assert full.model.num_module.elementwise_affine_weight.abs().sum() > 0  # the embeddings train
+
+
+def test_member_chunked_prediction_equals_whole_pack():
+    """predict_local in member groups (pack_idx selections, bounded activations for wide packs
+    on large batches): every grouping gives the same predictions bit for bit, and they agree
+    with the whole pack's (whose first layer gathers its one-hot columns) to the bf16
+    tolerance; the predictor's ensemble head is the mean of the selected members."""
+    from tabpack_b200.training import PackPredictor
+
+    val = _data(300, 3, 'cuda')
+    t = _trainer((0, 6), 'muon')
+    t.fit_epoch(_data(256, 2, 'cuda'), batch_size=64, epoch=0)
+    whole = t.predict_local(val)
+    one = t.predict_local(val, member_chunk=1)
+    assert torch.equal(t.predict_local(val, member_chunk=4), one)
+    assert float((one - whole).abs().max()) < 2e-2 * float(whole.abs().max())
+    pred = PackPredictor(t, {'h': torch.tensor([1, 4, 5])})
+    y_pack, heads = pred(val['x_num'], val['x_cat'], member_chunk=4)
+    assert torch.equal(y_pack, one)
+    torch.testing.assert_close(heads['h'], one[[1, 4, 5]].mean(0), rtol=1e-6, atol=1e-6)
