@@ -6,6 +6,7 @@
 //
 //   MODE_FWD    : C[B x out_m] = X[B x in_m] * W^T, + bias, ReLU, Philox dropout; A, B K-major
 //   MODE_FWD_ADD: the forward with an fp32 addend E[B x out_m] summed before the bias
+//   MODE_FWD_PAIR: the forward without dropout, on CTA pairs
 //   MODE_DGRAD  : C[B x in_m] = G[B x out_m] * W; A K-major, B MN-major; CTA pairs
 //   MODE_WGRAD_T: C^T[in_m x out_m] = X^T * G stored into C (K = batch rows), A and B MN-major;
 //                 a warp's 32 lanes hold 32 consecutive input features, so each output
@@ -34,13 +35,13 @@ struct Sm100Cfg {
   // a CTA loads and its tensor core reads per MMA drop by a third.  The forward, whose
   // time goes to its bias / ReLU / dropout epilogue rather than to operand traffic, runs
   // on single CTAs (measured a few percent faster than on pairs).
-  static constexpr bool PAIR = (MODE == MODE_DGRAD || MODE == MODE_WGRAD_T) && BN_ == 256;
-  static constexpr bool FWDK = (MODE == MODE_FWD || MODE == MODE_FWD_ADD);  // forward epilogue
+  static constexpr bool PAIR = (MODE == MODE_DGRAD || MODE == MODE_WGRAD_T || MODE == MODE_FWD_PAIR) && BN_ == 256;
+  static constexpr bool FWDK = (MODE == MODE_FWD || MODE == MODE_FWD_ADD || MODE == MODE_FWD_PAIR);  // forward epilogue
   static constexpr int TILE_M = PAIR ? 2 * BM : BM;
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B columns staged per CTA
   static constexpr bool A_MN = (MODE == MODE_WGRAD_T);
   static constexpr bool B_MN = (MODE == MODE_DGRAD || MODE == MODE_WGRAD_T || MODE == MODE_NS_BMN);
-  static constexpr int STAGES = PAIR ? 6 : (BN == 256) ? (FWDK ? 3 : 4) : 6;
+  static constexpr int STAGES = PAIR ? (FWDK ? 5 : 6) : (BN == 256) ? (FWDK ? 3 : 4) : 6;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = B_ROWS * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;

@@ -388,6 +388,14 @@ int linear_forward_impl(const tp_linear_args* a, const float* addend, int add_ld
     static_assert(Sm100Cfg<BN, MODE_FWD_ADD>::TILE_M == Cfg::TILE_M && Sm100Cfg<BN, MODE_FWD_ADD>::B_ROWS == Cfg::B_ROWS,
                   "the forward with an addend shares the forward's tiling");
     if (addend != nullptr) return launch_sm100<BN, MODE_FWD_ADD>(pr, ma, mb, st);
+    if (a->dropout_p == nullptr) {  // no Philox draws: the forward on CTA pairs (256-row tiles)
+      using CfgP = Sm100Cfg<BN, MODE_FWD_PAIR>;
+      pr.BM = CfgP::TILE_M;
+      pr.m_tiles = (a->B + CfgP::TILE_M - 1) / CfgP::TILE_M;
+      CUtensorMap mbp;
+      if ((rc = make_map(&mbp, a->w, a->max_in, a->max_out, a->P, 64, CfgP::B_ROWS))) return rc;
+      return launch_sm100<BN, MODE_FWD_PAIR>(pr, ma, mbp, st);
+    }
     return launch_sm100<BN, MODE_FWD>(pr, ma, mb, st);
   }
   if (addend != nullptr) return fail(TP_EUNSUPPORTED, "the gathered first layer runs on the sm_100 tensor-core path only");
