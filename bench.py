@@ -716,6 +716,86 @@ def run_inference(args) -> None:
         dist.destroy_process_group()
 
 
+def run_onehot(args) -> None:
+    """The first layer of the full-training configuration over one-hot categoricals, piece by
+    piece, gathered against dense: `members` members, batch 1024 gathered from 1 000 000 rows,
+    100 numerical features, 10 categorical features with cardinalities log-U[2, 1000] (the
+    full-training draw), output widths U{128..1024 step 8}, bf16, ReLU and dropout
+    p ~ U[0, 0.5].  Each piece: median of `steps` CUDA-event timings after `warmup` calls.
+    value = the gathered forward (category sort, gather, dense-column GEMM with the addend)."""
+    import statistics
+
+    import torch
+
+    from tabpack_b200 import ops
+
+    dev = torch.device('cuda', 0)
+    torch.cuda.set_device(dev)
+    P, B, n_num, N, max_out = args.members, 1024, 100, 1_000_000, 1024
+    rng = np.random.default_rng(21)
+    cards = [int(c) for c in np.exp(rng.uniform(np.log(2), np.log(1000), 10)).round()]
+    offs = torch.tensor([0] + list(np.cumsum(cards)), dtype=torch.int32, device=dev)
+    n_oh = int(offs[-1])
+    d_in = n_num + n_oh
+    outs = torch.from_numpy(rng.integers(16, 129, P).astype(np.int32) * 8).to(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    W = torch.randn(P, max_out, d_in, device=dev, generator=g) * 0.02
+    b = torch.zeros(P, max_out, device=dev)
+    xn = torch.randn(N, n_num, device=dev, generator=g)
+    xc = torch.stack([torch.randint(0, c, (N,), device=dev, generator=g) for c in cards], 1)
+    idx = torch.randint(0, N, (P, B), device=dev, generator=g)
+    p = torch.rand(P, device=dev, generator=g) * 0.5
+    dense_cols, full_cols = (n_num + 7) // 8 * 8, (d_in + 7) // 8 * 8
+    wd = torch.zeros(P, max_out, dense_cols, dtype=torch.bfloat16, device=dev)
+    wt = torch.empty(P, n_oh, max_out, dtype=torch.bfloat16, device=dev)
+    wf = torch.zeros(P, max_out, full_cols, dtype=torch.bfloat16, device=dev)
+    kw = dict(out_features=outs, relu=True, dropout_p=p, seed=3, offset=1)
+    res = {}
+
+    def timed(name, fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        res[name] = statistics.median(ts)
+
+    with ClockSampler(0) as clocks:
+        timed('cast_dense_columns', lambda: ops.weight_cast(W, wd, out_features=outs, src_cols=n_num))
+        timed('cast_onehot_transposed', lambda: ops.weight_cast_transposed(W, wt, col0=n_num, ncols=n_oh,
+                                                                           out_features=outs))
+        timed('cast_whole_weight', lambda: ops.weight_cast(W, wf, out_features=outs))
+        timed('input_dense', lambda: ops.tabpack_input(xn, None, offs, dense_cols, torch.bfloat16, row_index=idx))
+        timed('input_with_onehot', lambda: ops.tabpack_input(xn, xc, offs, full_cols, torch.bfloat16, row_index=idx))
+        xd = ops.tabpack_input(xn, None, offs, dense_cols, torch.bfloat16, row_index=idx)
+        xf = ops.tabpack_input(xn, xc, offs, full_cols, torch.bfloat16, row_index=idx)
+        out = {}
+        timed('gathered_forward', lambda: out.__setitem__('g', ops.onehot_linear_forward(
+            xd, wd, b, x_cat=xc, cat_offsets=offs, n_dense=n_num, w_onehot_t=wt, row_index=idx, **kw)))
+        timed('dense_forward', lambda: out.__setitem__('d', ops.linear_forward(xf, wf, b, **kw)))
+        (yg, st), yd = out['g'], out['d']
+        dy = torch.randn(P, B, max_out, device=dev, generator=g).bfloat16()
+        timed('gathered_backward', lambda: ops.onehot_linear_backward(dy, xd, wd, yg, st, **kw, dw_rows=max_out,
+                                                                      db_cols=max_out))
+        timed('dense_backward', lambda: ops.linear_backward(dy, xf, wf, yd, **kw, need_dx=False,
+                                                            dw_shape=(max_out, d_in), db_cols=max_out))
+    diff = float((yg.float() - yd.float()).abs().max() / yd.float().abs().max())
+    print(json.dumps({
+        'metric': 'first-layer forward over one-hot categoricals (gathered)', 'value': res['gathered_forward'],
+        'unit': 'ms', 'higher_is_better': False, 'steps': args.steps, 'warmup': args.warmup, 'dtype': 'bf16',
+        'data': 'synthetic',
+        'config': {'workload': f'{P} members, batch {B} gathered from {N} rows, {n_num} numerical + 10 categorical '
+                               f'features ({n_oh} one-hot columns), widths U{{128..1024}}, ReLU + dropout',
+                   'ms': res, 'gathered_vs_dense_max_rel_diff': diff},
+        'clocks': clocks.summary()}), flush=True)
+
+
 def main() -> None:
     global MEMBERS
     ap = argparse.ArgumentParser()
@@ -727,14 +807,16 @@ def main() -> None:
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--members', type=int, default=None,
                     help='members per GPU (default 256 for the layer workload, 1024 for the optimizer)')
-    ap.add_argument('--workload', choices=['layer', 'optimizer', 'metrics', 'train', 'inference'], default='layer',
+    ap.add_argument('--workload', choices=['layer', 'optimizer', 'metrics', 'train', 'inference', 'onehot'],
+                    default='layer',
                     help='layer: the packed-block fwd+bwd benchmark (default); optimizer: grouped Muon step; '
                          'metrics: validation metrics, ROC AUC and greedy selection')
     ap.add_argument('--embeddings', choices=['none', 'cosine'], default='none',
                     help='train workload: numerical features raw or through cosine embeddings')
     args = ap.parse_args()
     if args.members is None:
-        args.members = {'optimizer': 1024, 'metrics': 512, 'train': 512, 'inference': 1024}.get(args.workload, MEMBERS)
+        args.members = {'optimizer': 1024, 'metrics': 512, 'train': 512, 'inference': 1024,
+                        'onehot': 512}.get(args.workload, MEMBERS)
     MEMBERS = args.members
     if args.workload == 'optimizer':
         run_optimizer(args)
@@ -747,6 +829,9 @@ def main() -> None:
         return
     if args.workload == 'inference':
         run_inference(args)
+        return
+    if args.workload == 'onehot':
+        run_onehot(args)
         return
     if args.impl == 'reference':
         run_reference(args)
