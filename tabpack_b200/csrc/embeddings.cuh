@@ -21,6 +21,15 @@ namespace tp {
 constexpr float COS_EMB_TWO_PI = 6.28318530717958647692f;
 constexpr int COS_EMB_THREADS = 128;
 
+// z reduced to about [-pi, pi] by z - k 2pi, k = rint(z / 2pi), with 2pi split into a head of
+// 12 significant bits (3217 / 512, so that k * head is exact for |k| < 4096) and an fp32 tail
+// (Cody and Waite's argument reduction); the hardware cosine and sine are accurate to about
+// 4e-7 absolute on that range.
+__device__ __forceinline__ float cos_emb_reduce(float z) {
+  const float k = rintf(z * 0.159154936671f);
+  return fmaf(-k, -1.781781975e-05f, fmaf(-k, 6.283203125f, z));
+}
+
 struct CosEmbArgs {
   int P, B, F, D;
   int x_shared;            // x is (B, F) for every member, else (P, B, F)
@@ -79,7 +88,7 @@ __global__ void __launch_bounds__(COS_EMB_THREADS) cos_emb_forward_kernel(const 
   const int r0 = blockIdx.z * a.rows_per_block, r1 = min(a.B, r0 + a.rows_per_block);
   for (int r = r0; r < r1; ++r) {
     const float x = cos_emb_x(a, m, r, c.f);
-    const float cat = c.k == 0 ? x : cosf(c.b2 + c.w2 * x);
+    const float cat = c.k == 0 ? x : __cosf(cos_emb_reduce(c.b2 + c.w2 * x));
     const float v = c.ab + c.aw * cat;
     const size_t o = ((size_t)m * a.B + r) * a.out_ld + j;
     if (a.out_bf16)
@@ -108,7 +117,7 @@ __global__ void __launch_bounds__(COS_EMB_THREADS) cos_emb_backward_kernel(const
       s_aw += (double)g * (double)x;
     } else {
       float sn, cs;
-      sincosf(c.b2 + c.w2 * x, &sn, &cs);
+      __sincosf(cos_emb_reduce(c.b2 + c.w2 * x), &sn, &cs);
       s_aw += (double)g * (double)cs;
       const double dz = -(double)g * (double)c.aw * (double)sn;
       s_w += dz * (double)x;
