@@ -79,70 +79,108 @@ __device__ __forceinline__ float cos_emb_x(const CosEmbArgs& a, int m, int r, in
   return a.x[(a.x_shared ? (size_t)r : ((size_t)m * a.B + r)) * a.F + f];
 }
 
-// Grid: (ceil(F * D / COS_EMB_THREADS), P, ceil(B / rows_per_block)).
-__global__ void __launch_bounds__(COS_EMB_THREADS) cos_emb_forward_kernel(const CosEmbArgs a) {
-  const int m = blockIdx.y;
-  const int j = blockIdx.x * COS_EMB_THREADS + threadIdx.x;
-  const CosEmbCol c = cos_emb_col(a, m, j);
-  if (!c.valid) return;
-  const int r0 = blockIdx.z * a.rows_per_block, r1 = min(a.B, r0 + a.rows_per_block);
-  for (int r = r0; r < r1; ++r) {
-    const float x = cos_emb_x(a, m, r, c.f);
-    const float cat = c.k == 0 ? x : __cosf(cos_emb_reduce(c.b2 + c.w2 * x));
-    const float v = c.ab + c.aw * cat;
-    const size_t o = ((size_t)m * a.B + r) * a.out_ld + j;
-    if (a.out_bf16)
-      reinterpret_cast<__nv_bfloat16*>(a.out)[o] = __float2bfloat16_rn(v);
-    else
-      reinterpret_cast<float*>(a.out)[o] = v;
+// The forward: a thread owns two adjacent columns (j0 = 2 t, j0 + 1) so that its stores are
+// 4- or 8-byte pairs when the row stride is even.
+__device__ __forceinline__ void cos_emb_store2(const CosEmbArgs& a, size_t o, bool v1, float y0, float y1) {
+  if (a.out_bf16) {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+    if (v1 && (a.out_ld & 1) == 0) {
+      *reinterpret_cast<uint32_t*>(out + o) = pack_bf16x2(y0, y1);
+    } else {
+      out[o] = __float2bfloat16_rn(y0);
+      if (v1) out[o + 1] = __float2bfloat16_rn(y1);
+    }
+  } else {
+    float* out = reinterpret_cast<float*>(a.out);
+    if (v1 && (a.out_ld & 1) == 0) {
+      *reinterpret_cast<float2*>(out + o) = make_float2(y0, y1);
+    } else {
+      out[o] = y0;
+      if (v1) out[o + 1] = y1;
+    }
   }
 }
 
-// Grid as the forward.  One block row segment per z; with gridDim.z == 1 the sums are final,
-// otherwise they go to `partial` and cos_emb_finish_kernel adds the segments in order.
+__device__ __forceinline__ float cos_emb_value(const CosEmbCol& c, float x) {
+  return c.ab + c.aw * (c.k == 0 ? x : __cosf(cos_emb_reduce(c.b2 + c.w2 * x)));
+}
+
+// Grid: (ceil(F * D / (2 COS_EMB_THREADS)), P, ceil(B / rows_per_block)).
+__global__ void __launch_bounds__(COS_EMB_THREADS) cos_emb_forward_kernel(const CosEmbArgs a) {
+  const int m = blockIdx.y;
+  const int j0 = 2 * (blockIdx.x * COS_EMB_THREADS + threadIdx.x);
+  const CosEmbCol c0 = cos_emb_col(a, m, j0), c1 = cos_emb_col(a, m, j0 + 1);
+  if (!c0.valid) return;
+  const int r0 = blockIdx.z * a.rows_per_block, r1 = min(a.B, r0 + a.rows_per_block);
+  for (int r = r0; r < r1; ++r) {
+    const float x0 = cos_emb_x(a, m, r, c0.f);
+    const float x1 = c1.f == c0.f ? x0 : cos_emb_x(a, m, r, c1.f);
+    const float y0 = cos_emb_value(c0, x0);
+    const float y1 = c1.valid ? cos_emb_value(c1, x1) : 0.0f;
+    cos_emb_store2(a, ((size_t)m * a.B + r) * a.out_ld + j0, c1.valid, y0, y1);
+  }
+}
+
+// Sums of one column over rows: sa = sum g, sw = sum g cat, s1 = sum dz x, s2 = sum dz.
+struct CosEmbSums {
+  double ab, aw, w, b;
+};
+
+__device__ __forceinline__ void cos_emb_accumulate(const CosEmbCol& c, float g, float x, CosEmbSums& s) {
+  s.ab += (double)g;
+  if (c.k == 0) {
+    s.aw += (double)g * (double)x;
+  } else {
+    float sn, cs;
+    __sincosf(cos_emb_reduce(c.b2 + c.w2 * x), &sn, &cs);
+    s.aw += (double)g * (double)cs;
+    const double dz = -(double)g * (double)c.aw * (double)sn;
+    s.w += dz * (double)x;
+    s.b += dz;
+  }
+}
+
+__device__ __forceinline__ void cos_emb_write_sums(const CosEmbArgs& a, int m, int j, const CosEmbCol& c,
+                                                   const CosEmbSums& s) {
+  const size_t FD = (size_t)a.F * a.D;
+  if (gridDim.z > 1) {
+    const size_t slot = ((size_t)blockIdx.z * a.P + m) * FD + j;
+    const size_t plane = (size_t)gridDim.z * a.P * FD;
+    a.partial[slot] = s.ab;
+    a.partial[plane + slot] = s.aw;
+    a.partial[2 * plane + slot] = s.w;
+    a.partial[3 * plane + slot] = s.b;
+    return;
+  }
+  const bool on = a.d_emb == nullptr || c.k < a.d_emb[m];
+  const size_t pa = ((size_t)m * a.F + c.f) * a.D + c.k;
+  a.dab[pa] = on ? (float)s.ab : 0.0f;
+  a.daw[pa] = on ? (float)s.aw : 0.0f;
+  if (c.k > 0) {
+    const size_t pw = ((size_t)m * a.F + c.f) * (a.D - 1) + (c.k - 1);
+    a.dw[pw] = (float)s.w * COS_EMB_TWO_PI;
+    a.db[pw] = (float)s.b * COS_EMB_TWO_PI;
+  }
+}
+
+// Grid: (ceil(F * D / COS_EMB_THREADS), P, segments), one column a thread (two columns a thread
+// measured slower: twice the fp64 accumulation chains per thread).  One block row segment per
+// z; with gridDim.z == 1 the sums are final, otherwise they go to `partial` and
+// cos_emb_finish_kernel adds the segments in order.
 __global__ void __launch_bounds__(COS_EMB_THREADS) cos_emb_backward_kernel(const CosEmbArgs a) {
   const int m = blockIdx.y;
   const int j = blockIdx.x * COS_EMB_THREADS + threadIdx.x;
   const CosEmbCol c = cos_emb_col(a, m, j);
   if (!c.valid) return;
   const int r0 = blockIdx.z * a.rows_per_block, r1 = min(a.B, r0 + a.rows_per_block);
-  double s_ab = 0.0, s_aw = 0.0, s_w = 0.0, s_b = 0.0;
+  CosEmbSums sums{0.0, 0.0, 0.0, 0.0};
   for (int r = r0; r < r1; ++r) {
     const size_t gi = ((size_t)m * a.B + r) * a.g_ld + j;
     const float g = a.g_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.g)[gi])
                              : reinterpret_cast<const float*>(a.g)[gi];
-    const float x = cos_emb_x(a, m, r, c.f);
-    s_ab += (double)g;
-    if (c.k == 0) {
-      s_aw += (double)g * (double)x;
-    } else {
-      float sn, cs;
-      __sincosf(cos_emb_reduce(c.b2 + c.w2 * x), &sn, &cs);
-      s_aw += (double)g * (double)cs;
-      const double dz = -(double)g * (double)c.aw * (double)sn;
-      s_w += dz * (double)x;
-      s_b += dz;
-    }
+    cos_emb_accumulate(c, g, cos_emb_x(a, m, r, c.f), sums);
   }
-  const size_t FD = (size_t)a.F * a.D;
-  if (gridDim.z > 1) {
-    const size_t slot = ((size_t)blockIdx.z * a.P + m) * FD + j;
-    const size_t plane = (size_t)gridDim.z * a.P * FD;
-    a.partial[slot] = s_ab;
-    a.partial[plane + slot] = s_aw;
-    a.partial[2 * plane + slot] = s_w;
-    a.partial[3 * plane + slot] = s_b;
-    return;
-  }
-  const bool on = a.d_emb == nullptr || c.k < a.d_emb[m];
-  const size_t pa = ((size_t)m * a.F + c.f) * a.D + c.k;
-  a.dab[pa] = on ? (float)s_ab : 0.0f;
-  a.daw[pa] = on ? (float)s_aw : 0.0f;
-  if (c.k > 0) {
-    const size_t pw = ((size_t)m * a.F + c.f) * (a.D - 1) + (c.k - 1);
-    a.dw[pw] = (float)s_w * COS_EMB_TWO_PI;
-    a.db[pw] = (float)s_b * COS_EMB_TWO_PI;
-  }
+  cos_emb_write_sums(a, m, j, c, sums);
 }
 
 // Adds the row segments' partial sums in segment order (deterministic).  Grid:
