@@ -388,10 +388,10 @@ def run_b200(args) -> None:
 # DRAM bytes (read + write) per full-size launch, from the ncu captures summarised in
 # profiles/linear_block_fwd_bwd_256x4096x512.md (32-member case scaled by 256/32).
 TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
-    'fwd': (25.804544e6 + 211.742720e6) * 8,
-    'act': (293.636608e6 + 98.083072e6) * 8,
-    'dgrad': (173.277184e6 + 100.588032e6) * 8,
-    'wgrad': (179.476736e6 + 45.408256e6) * 8,
+    'fwd': (25.796096e6 + 212.714752e6) * 8,
+    'act': (293.625344e6 + 94.327552e6) * 8,
+    'dgrad': (173.594624e6 + 100.386560e6) * 8,
+    'wgrad': (180.835072e6 + 42.455808e6) * 8,
 }
 
 
