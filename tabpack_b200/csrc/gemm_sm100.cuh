@@ -459,6 +459,9 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
       const int m = ti.member;
       const int row = ti.mt * Cfg::TILE_M + row_in_tile;
       const int cbase = ti.nt * BN + half * WCOLS;
+      // a ZERO / COPY / SKIP tile stages no bias: prefetch the next tile's slice here, so the
+      // MMA tile after it does not stage this tile's (zero) slice
+      if (Cfg::FWDK && ti.kind != KIND_MMA && t_next < total_tiles) load_bias(nti);
       if (ti.kind == KIND_MMA) {
         uint32_t thr = 65536u;
         float scale = 1.0f;  // 1 / (1 - p): kept elements are (acc + b) * scale

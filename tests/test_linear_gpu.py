@@ -7,12 +7,14 @@ relative, far inside the 2e-2 bar).  fp32 runs on CUDA cores and must agree with
 the oracle to 1e-5 relative (the bar is 1e-4).
 """
 
+import math
+
 import numpy as np
 import pytest
 import torch
 
 from oracle import layers as ol
-from oracle.philox import dropout_keep_mask
+from oracle.philox import dropout_keep_mask, keep_scale
 
 pytestmark = pytest.mark.gpu
 
@@ -166,6 +168,74 @@ def test_backward(dtype, case):
     if in_f is not None:
         dx_ref = dx_ref * ol.col_mask(in_f, max_in, np.float64)
     _close(_host(dx), dx_ref, tol, 'dx')
+
+
+def _close_dev(got, want, rtol, what):
+    """`_close` on the device: |got - want| <= rtol |want| + rtol / 4 * max |want|."""
+    got, want = got.float(), want.float()
+    scale = want.abs().max().clamp_min(1e-30)
+    err = (got - want).abs()
+    n = int((err > rtol * want.abs() + rtol * 0.25 * scale).sum())
+    assert n == 0, f'{what}: {n} / {err.numel()} mismatches, max err {float(err.max()):.3e} (scale {float(scale):.3e})'
+
+
+def test_full_size_layer_against_torch_fp32():
+    """The benchmarked layer at full size: 256 members sharing a 4096 x 512 bf16 batch, output
+    widths U{64..1024 step 16}, bias + ReLU + dropout p ~ U[0, 0.5].  Every member's output,
+    input gradient, weight gradient and bias gradient against plain PyTorch fp32 arithmetic on
+    the same bf16 values (TF32 off), with the ReLU mask taken from the kernel's own output as in
+    `test_backward`; exact zeros in every member's padding; and the keep masks of sampled
+    members (first, last, narrowest, widest) bit-exact against the oracle's Philox."""
+    from tabpack_b200 import ops
+
+    P, B, K, N = 256, 4096, 512, 1024
+    rng = np.random.default_rng(2024)
+    out_np = rng.integers(4, 65, P) * 16
+    p_np = rng.uniform(0, 0.5, P).astype(np.float32)
+    outf = torch.from_numpy(out_np.astype(np.int32)).cuda()
+    p = torch.from_numpy(p_np).cuda()
+    g = torch.Generator(device='cuda').manual_seed(2024)
+    bound = 1.0 / math.sqrt(K)
+    x = torch.randn(B, K, device='cuda', generator=g).bfloat16()
+    w = ((torch.rand(P, N, K, device='cuda', generator=g) * 2 - 1) * bound).bfloat16()
+    b = (torch.rand(P, N, device='cuda', generator=g) * 2 - 1) * bound
+    seed, offset, base = 0x123456789ABC, 7, 0
+    kw = dict(out_features=outf, relu=True, dropout_p=p, seed=seed, offset=offset, member_base=base)
+    y = ops.linear_forward(x, w, b, **kw)
+    dy = torch.randn(P, B, N, device='cuda', generator=g).bfloat16()
+    dx, dW, db = ops.linear_backward(dy, x, w, y, **kw)
+    keep = ops.dropout_mask(seed=seed, offset=offset, member_base=base, p=p, rows=B, cols=N)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+
+    for m in sorted({0, P - 1, int(np.argmin(out_np)), int(np.argmax(out_np))}):
+        want = dropout_keep_mask(seed=seed, offset=offset, members=np.array([m + base]), n_rows=B, n_cols=N,
+                                 p=p_np[m:m + 1])[0]
+        assert np.array_equal(keep[m].cpu().numpy().astype(bool), want), f'keep mask of member {m}'
+
+    scale = torch.from_numpy(keep_scale(p_np)).cuda()
+    col = torch.arange(N, device='cuda')
+    xf = x.float()
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for c in range(0, P, 32):
+            s = slice(c, c + 32)
+            valid = (col[None, :] < outf[s, None])[:, None, :]
+            mv = keep[s].float() * scale[s, None, None] * valid
+            pre = torch.matmul(xf, w[s].float().transpose(1, 2)) + b[s, None, :]
+            _close_dev(y[s], torch.relu(pre) * mv, BF16_RTOL, f'y members {c}..{c + 31}')
+            assert int(torch.count_nonzero(y[s] * ~valid)) == 0
+            gm = dy[s].float() * mv * (y[s] > 0)
+            _close_dev(db[s], gm.sum(1), 1e-4, f'db members {c}..{c + 31}')
+            gq = gm.bfloat16().float()
+            _close_dev(dW[s], torch.matmul(gq.transpose(1, 2), xf), BF16_RTOL, f'dW members {c}..{c + 31}')
+            _close_dev(dx[s], torch.matmul(gq, w[s].float()), BF16_RTOL, f'dx members {c}..{c + 31}')
+            rows_pad = (col[None, :] >= outf[s, None])
+            assert int(torch.count_nonzero(dW[s] * rows_pad[:, :, None])) == 0
+            assert int(torch.count_nonzero(db[s] * rows_pad)) == 0
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = tf32
 
 
 @pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
