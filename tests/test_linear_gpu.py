@@ -179,9 +179,11 @@ def _close_dev(got, want, rtol, what):
     assert n == 0, f'{what}: {n} / {err.numel()} mismatches, max err {float(err.max()):.3e} (scale {float(scale):.3e})'
 
 
-def test_full_size_layer_against_torch_fp32():
+@pytest.mark.parametrize('dropout', [True, False])
+def test_full_size_layer_against_torch_fp32(dropout):
     """The benchmarked layer at full size: 256 members sharing a 4096 x 512 bf16 batch, output
-    widths U{64..1024 step 16}, bias + ReLU + dropout p ~ U[0, 0.5].  Every member's output,
+    widths U{64..1024 step 16}, bias + ReLU + dropout p ~ U[0, 0.5] (without dropout the
+    forward runs on CTA pairs).  Every member's output,
     input gradient, weight gradient and bias gradient against plain PyTorch fp32 arithmetic on
     the same bf16 values (TF32 off), with the ReLU mask taken from the kernel's own output as in
     `test_backward`; exact zeros in every member's padding; and the keep masks of sampled
@@ -200,15 +202,20 @@ def test_full_size_layer_against_torch_fp32():
     w = ((torch.rand(P, N, K, device='cuda', generator=g) * 2 - 1) * bound).bfloat16()
     b = (torch.rand(P, N, device='cuda', generator=g) * 2 - 1) * bound
     seed, offset, base = 0x123456789ABC, 7, 0
-    kw = dict(out_features=outf, relu=True, dropout_p=p, seed=seed, offset=offset, member_base=base)
+    kw = dict(out_features=outf, relu=True, dropout_p=p if dropout else None, seed=seed, offset=offset,
+              member_base=base)
     y = ops.linear_forward(x, w, b, **kw)
     dy = torch.randn(P, B, N, device='cuda', generator=g).bfloat16()
     dx, dW, db = ops.linear_backward(dy, x, w, y, **kw)
-    keep = ops.dropout_mask(seed=seed, offset=offset, member_base=base, p=p, rows=B, cols=N)
+    if dropout:
+        keep = ops.dropout_mask(seed=seed, offset=offset, member_base=base, p=p, rows=B, cols=N)
+    else:
+        p_np = np.zeros_like(p_np)
+        keep = torch.ones(P, B, N, dtype=torch.uint8, device='cuda')
     torch.cuda.synchronize()
     assert ops.device_error() == 0
 
-    for m in sorted({0, P - 1, int(np.argmin(out_np)), int(np.argmax(out_np))}):
+    for m in sorted({0, P - 1, int(np.argmin(out_np)), int(np.argmax(out_np))}) if dropout else []:
         want = dropout_keep_mask(seed=seed, offset=offset, members=np.array([m + base]), n_rows=B, n_cols=N,
                                  p=p_np[m:m + 1])[0]
         assert np.array_equal(keep[m].cpu().numpy().astype(bool), want), f'keep mask of member {m}'
