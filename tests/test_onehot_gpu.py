@@ -119,6 +119,28 @@ def test_gathered_first_layer_with_cosine_embeddings():
     assert any(k.startswith('num_module') for k in grads)
 
 
+def test_gathered_first_layer_at_benchmark_shapes():
+    """64 members, 1024 rows, 100 numerical features and 10 categorical features with
+    cardinalities log-uniform in [2, 1000] (the one-hot block of the benchmarked model), widths
+    U{128..1024 step 8}: each CTA runs several gathered tiles, and outputs and gradients must
+    agree with the dense one-hot path."""
+    from tabpack_b200 import nn as bnn
+
+    torch.manual_seed(4)
+    rng = np.random.default_rng(4)
+    P, B = 64, 1024
+    cards = [int(c) for c in np.exp(rng.uniform(np.log(2), np.log(1000), 10)).astype(int)]
+    widths = [int(w) for w in rng.integers(16, 129, P) * 8]
+    model = bnn.TabPack(n_numerical_features=100, categorical_cardinalities=cards, d_out=1,
+                        n_blocks=[int(v) for v in rng.integers(1, 3, P)], d_block=widths,
+                        dropout=[float(v) for v in rng.uniform(0, 0.5, P)], pack_size=P,
+                        max_d_block=max(widths)).cuda().train()
+    g = torch.Generator(device='cuda').manual_seed(8)
+    x_num = torch.randn(B, 100, device='cuda', generator=g)
+    x_cat = torch.stack([torch.randint(0, c + 1, (B,), device='cuda', generator=g) for c in cards], -1)
+    _compare(model, x_num, x_cat)
+
+
 def test_onehot_wgrad_is_the_segmented_sum():
     """dW over the one-hot columns equals sum over each category's rows of the
     pre-activation gradient, exactly as fp32 sums in ascending row order (no dropout, no
