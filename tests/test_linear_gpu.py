@@ -245,6 +245,51 @@ def test_full_size_layer_against_torch_fp32(dropout):
         torch.backends.cuda.matmul.allow_tf32 = tf32
 
 
+def test_depth_gating_many_tiles_per_cta():
+    """128 members x 2048 rows x 512, a third of them past their depth (COPY tiles mixed with
+    MMA tiles on every CTA): gated members pass x and dy through bit for bit, the others match
+    plain PyTorch fp32 on the same bf16 values (TF32 off)."""
+    from tabpack_b200 import ops
+
+    P, B, W = 128, 2048, 512
+    rng = np.random.default_rng(21)
+    nb = rng.integers(1, 4, P).astype(np.int32)
+    p_np = rng.uniform(0, 0.5, P).astype(np.float32)
+    g = torch.Generator(device='cuda').manual_seed(21)
+    x = torch.randn(P, B, W, device='cuda', generator=g).bfloat16()
+    bound = 1.0 / math.sqrt(W)
+    w = ((torch.rand(P, W, W, device='cuda', generator=g) * 2 - 1) * bound).bfloat16()
+    b = (torch.rand(P, W, device='cuda', generator=g) * 2 - 1) * bound
+    p = torch.from_numpy(p_np).cuda()
+    seed, offset = 77, 3
+    kw = dict(n_blocks=torch.from_numpy(nb).cuda(), block_index=1, relu=True, dropout_p=p, seed=seed, offset=offset)
+    y = ops.linear_forward(x, w, b, **kw)
+    dy = torch.randn(P, B, W, device='cuda', generator=g).bfloat16()
+    dx, dW, db = ops.linear_backward(dy, x, w, y, **kw)
+    keep = ops.dropout_mask(seed=seed, offset=offset, member_base=0, p=p, rows=B, cols=W)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    gated = torch.from_numpy(nb <= 1).cuda()
+    assert torch.equal(y[gated], x[gated]) and torch.equal(dx[gated], dy[gated])
+    assert int(torch.count_nonzero(dW[gated])) == 0 and int(torch.count_nonzero(db[gated])) == 0
+    act = ~gated
+    scale = torch.from_numpy(keep_scale(p_np)).cuda()[act][:, None, None]
+    mv = keep[act].float() * scale
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        xa, wa = x[act].float(), w[act].float()
+        pre = torch.matmul(xa, wa.transpose(1, 2)) + b[act][:, None, :]
+        _close_dev(y[act], torch.relu(pre) * mv, BF16_RTOL, 'y of active members')
+        gm = dy[act].float() * mv * (y[act] > 0)
+        _close_dev(db[act], gm.sum(1), 1e-4, 'db of active members')
+        gq = gm.bfloat16().float()
+        _close_dev(dW[act], torch.matmul(gq.transpose(1, 2), xa), BF16_RTOL, 'dW of active members')
+        _close_dev(dx[act], torch.matmul(gq, wa), BF16_RTOL, 'dx of active members')
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+
+
 @pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
 def test_depth_gating(dtype):
     """Members with n_blocks <= block_index pass x through (forward) and dy through (dgrad)."""
