@@ -245,16 +245,18 @@ def test_full_size_layer_against_torch_fp32(dropout):
         torch.backends.cuda.matmul.allow_tf32 = tf32
 
 
-def test_depth_gating_many_tiles_per_cta():
+@pytest.mark.parametrize('dropout', [True, False])
+def test_depth_gating_many_tiles_per_cta(dropout):
     """128 members x 2048 rows x 512, a third of them past their depth (COPY tiles mixed with
-    MMA tiles on every CTA): gated members pass x and dy through bit for bit, the others match
-    plain PyTorch fp32 on the same bf16 values (TF32 off)."""
+    MMA tiles on every CTA; without dropout the forward runs on CTA pairs): gated members pass
+    x and dy through bit for bit, the others match plain PyTorch fp32 on the same bf16 values
+    (TF32 off)."""
     from tabpack_b200 import ops
 
     P, B, W = 128, 2048, 512
     rng = np.random.default_rng(21)
     nb = rng.integers(1, 4, P).astype(np.int32)
-    p_np = rng.uniform(0, 0.5, P).astype(np.float32)
+    p_np = rng.uniform(0, 0.5, P).astype(np.float32) if dropout else np.zeros(P, np.float32)
     g = torch.Generator(device='cuda').manual_seed(21)
     x = torch.randn(P, B, W, device='cuda', generator=g).bfloat16()
     bound = 1.0 / math.sqrt(W)
@@ -262,7 +264,8 @@ def test_depth_gating_many_tiles_per_cta():
     b = (torch.rand(P, W, device='cuda', generator=g) * 2 - 1) * bound
     p = torch.from_numpy(p_np).cuda()
     seed, offset = 77, 3
-    kw = dict(n_blocks=torch.from_numpy(nb).cuda(), block_index=1, relu=True, dropout_p=p, seed=seed, offset=offset)
+    kw = dict(n_blocks=torch.from_numpy(nb).cuda(), block_index=1, relu=True, dropout_p=p if dropout else None,
+              seed=seed, offset=offset)
     y = ops.linear_forward(x, w, b, **kw)
     dy = torch.randn(P, B, W, device='cuda', generator=g).bfloat16()
     dx, dW, db = ops.linear_backward(dy, x, w, y, **kw)
