@@ -14,6 +14,8 @@
 // thread and the loads / stores of a warp are contiguous along the columns.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace tp {
@@ -79,45 +81,61 @@ __device__ __forceinline__ float cos_emb_x(const CosEmbArgs& a, int m, int r, in
   return a.x[(a.x_shared ? (size_t)r : ((size_t)m * a.B + r)) * a.F + f];
 }
 
-// The forward: a thread owns two adjacent columns (j0 = 2 t, j0 + 1) so that its stores are
-// 4- or 8-byte pairs when the row stride is even.
-__device__ __forceinline__ void cos_emb_store2(const CosEmbArgs& a, size_t o, bool v1, float y0, float y1) {
-  if (a.out_bf16) {
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
-    if (v1 && (a.out_ld & 1) == 0) {
-      *reinterpret_cast<uint32_t*>(out + o) = pack_bf16x2(y0, y1);
-    } else {
-      out[o] = __float2bfloat16_rn(y0);
-      if (v1) out[o + 1] = __float2bfloat16_rn(y1);
-    }
-  } else {
-    float* out = reinterpret_cast<float*>(a.out);
-    if (v1 && (a.out_ld & 1) == 0) {
-      *reinterpret_cast<float2*>(out + o) = make_float2(y0, y1);
-    } else {
-      out[o] = y0;
-      if (v1) out[o + 1] = y1;
-    }
-  }
-}
-
 __device__ __forceinline__ float cos_emb_value(const CosEmbCol& c, float x) {
   return c.ab + c.aw * (c.k == 0 ? x : __cosf(cos_emb_reduce(c.b2 + c.w2 * x)));
 }
 
-// Grid: (ceil(F * D / (2 COS_EMB_THREADS)), P, ceil(B / rows_per_block)).
+// Grid: (ceil(F * D / (2 COS_EMB_THREADS)), P, ceil(B / rows_per_block)).  A thread owns two
+// adjacent columns (j0 = 2 t, j0 + 1), stored as one 4- or 8-byte pair when the row stride is
+// even.  The output type is
+// a template parameter and the row pointers advance by increments, so the loop body is the
+// embedding arithmetic and the stores; four rows' x values are loaded (read-only path) before
+// their stores, which the compiler could not move them past otherwise (x and out may alias).
+template <bool BF16>
 __global__ void __launch_bounds__(COS_EMB_THREADS) cos_emb_forward_kernel(const CosEmbArgs a) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, float>::type;
   const int m = blockIdx.y;
   const int j0 = 2 * (blockIdx.x * COS_EMB_THREADS + threadIdx.x);
   const CosEmbCol c0 = cos_emb_col(a, m, j0), c1 = cos_emb_col(a, m, j0 + 1);
   if (!c0.valid) return;
   const int r0 = blockIdx.z * a.rows_per_block, r1 = min(a.B, r0 + a.rows_per_block);
-  for (int r = r0; r < r1; ++r) {
-    const float x0 = cos_emb_x(a, m, r, c0.f);
-    const float x1 = c1.f == c0.f ? x0 : cos_emb_x(a, m, r, c1.f);
-    const float y0 = cos_emb_value(c0, x0);
-    const float y1 = c1.valid ? cos_emb_value(c1, x1) : 0.0f;
-    cos_emb_store2(a, ((size_t)m * a.B + r) * a.out_ld + j0, c1.valid, y0, y1);
+  const bool pair = c1.valid && (a.out_ld & 1) == 0;  // one 4- or 8-byte store for both columns
+  const int F = a.F;
+  const size_t ld = (size_t)a.out_ld;
+  const float* xp = a.x + (a.x_shared ? (size_t)r0 : (size_t)m * a.B + r0) * F;
+  const int f0 = c0.f, f1 = c1.f;  // f1 = 0 for an invalid second column: in bounds
+  T* o = reinterpret_cast<T*>(a.out) + ((size_t)m * a.B + r0) * ld + j0;
+  auto store = [&](T* q, float y0, float y1) {
+    if constexpr (BF16) {
+      if (pair) {
+        *reinterpret_cast<uint32_t*>(q) = pack_bf16x2(y0, y1);
+      } else {
+        q[0] = __float2bfloat16_rn(y0);
+        if (c1.valid) q[1] = __float2bfloat16_rn(y1);
+      }
+    } else {
+      if (pair) {
+        *reinterpret_cast<float2*>(q) = make_float2(y0, y1);
+      } else {
+        q[0] = y0;
+        if (c1.valid) q[1] = y1;
+      }
+    }
+  };
+  int r = r0;
+  for (; r + 4 <= r1; r += 4, xp += 4 * F, o += 4 * ld) {
+    float xa[4], xb[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      xa[i] = __ldg(xp + i * F + f0);
+      xb[i] = __ldg(xp + i * F + f1);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) store(o + i * ld, cos_emb_value(c0, xa[i]), c1.valid ? cos_emb_value(c1, xb[i]) : 0.0f);
+  }
+  for (; r < r1; ++r, xp += F, o += ld) {
+    const float x0 = __ldg(xp + f0), x1 = __ldg(xp + f1);
+    store(o, cos_emb_value(c0, x0), c1.valid ? cos_emb_value(c1, x1) : 0.0f);
   }
 }
 

@@ -893,7 +893,10 @@ int tp_cos_emb_forward(const tp_cos_emb_args* a, void* stream) {
   k.rows_per_block = 64;
   const dim3 grid((a->F * a->D + 2 * COS_EMB_THREADS - 1) / (2 * COS_EMB_THREADS), a->P, (a->B + 63) / 64);
   if (grid.z > 65535) return fail(TP_EINVAL, "batch too large for one embedding call");
-  cos_emb_forward_kernel<<<grid, COS_EMB_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(k);
+  if (k.out_bf16)
+    cos_emb_forward_kernel<true><<<grid, COS_EMB_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(k);
+  else
+    cos_emb_forward_kernel<false><<<grid, COS_EMB_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(k);
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;
 }
