@@ -26,9 +26,13 @@ constexpr int COS_EMB_THREADS = 128;
 // z reduced to about [-pi, pi] by z - k 2pi, k = rint(z / 2pi), with 2pi split into a head of
 // 12 significant bits (3217 / 512, so that k * head is exact for |k| < 4096) and an fp32 tail
 // (Cody and Waite's argument reduction); the hardware cosine and sine are accurate to about
-// 4e-7 absolute on that range.
+// 4e-7 absolute on that range.  k = rint(z / 2pi) is formed by adding and subtracting 1.5 * 2^23, which rounds to the nearest
+// integer (ties to even) exactly like rintf for |z / 2pi| < 2^22, on the FMA pipe instead of
+// the conversion unit that the cosine and sine already keep busy; the _rn intrinsics keep the
+// product and the sums separately rounded.
 __device__ __forceinline__ float cos_emb_reduce(float z) {
-  const float k = rintf(z * 0.159154936671f);
+  const float t = __fmul_rn(z, 0.159154936671f);
+  const float k = __fsub_rn(__fadd_rn(t, 12582912.0f), 12582912.0f);
   return fmaf(-k, -1.781781975e-05f, fmaf(-k, 6.283203125f, z));
 }
 
