@@ -81,10 +81,6 @@ __device__ __forceinline__ CosEmbCol cos_emb_col(const CosEmbArgs& a, int m, int
   return c;
 }
 
-__device__ __forceinline__ float cos_emb_x(const CosEmbArgs& a, int m, int r, int f) {
-  return a.x[(a.x_shared ? (size_t)r : ((size_t)m * a.B + r)) * a.F + f];
-}
-
 __device__ __forceinline__ float cos_emb_value(const CosEmbCol& c, float x) {
   return c.ab + c.aw * (c.k == 0 ? x : __cosf(cos_emb_reduce(c.b2 + c.w2 * x)));
 }
@@ -189,19 +185,39 @@ __device__ __forceinline__ void cos_emb_write_sums(const CosEmbArgs& a, int m, i
 // measured slower: twice the fp64 accumulation chains per thread).  One block row segment per
 // z; with gridDim.z == 1 the sums are final, otherwise they go to `partial` and
 // cos_emb_finish_kernel adds the segments in order.
+// The gradient's type is a template parameter and the row pointers advance by increments;
+// rows are accumulated in order, four loaded at a time.
+template <bool G_BF16>
 __global__ void __launch_bounds__(COS_EMB_THREADS) cos_emb_backward_kernel(const CosEmbArgs a) {
+  using T = typename std::conditional<G_BF16, __nv_bfloat16, float>::type;
   const int m = blockIdx.y;
   const int j = blockIdx.x * COS_EMB_THREADS + threadIdx.x;
   const CosEmbCol c = cos_emb_col(a, m, j);
   if (!c.valid) return;
   const int r0 = blockIdx.z * a.rows_per_block, r1 = min(a.B, r0 + a.rows_per_block);
+  const int F = a.F;
+  const size_t ld = (size_t)a.g_ld;
+  const float* xp = a.x + (a.x_shared ? (size_t)r0 : (size_t)m * a.B + r0) * F + c.f;
+  const T* gp = reinterpret_cast<const T*>(a.g) + ((size_t)m * a.B + r0) * ld + j;
+  auto gval = [](T v) -> float {
+    if constexpr (G_BF16)
+      return __bfloat162float(v);
+    else
+      return v;
+  };
   CosEmbSums sums{0.0, 0.0, 0.0, 0.0};
-  for (int r = r0; r < r1; ++r) {
-    const size_t gi = ((size_t)m * a.B + r) * a.g_ld + j;
-    const float g = a.g_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.g)[gi])
-                             : reinterpret_cast<const float*>(a.g)[gi];
-    cos_emb_accumulate(c, g, cos_emb_x(a, m, r, c.f), sums);
+  int r = r0;
+  for (; r + 4 <= r1; r += 4, xp += 4 * F, gp += 4 * ld) {
+    float gv[4], xv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      gv[i] = gval(gp[i * ld]);
+      xv[i] = xp[i * F];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) cos_emb_accumulate(c, gv[i], xv[i], sums);
   }
+  for (; r < r1; ++r, xp += F, gp += ld) cos_emb_accumulate(c, gval(*gp), *xp, sums);
   cos_emb_write_sums(a, m, j, c, sums);
 }
 

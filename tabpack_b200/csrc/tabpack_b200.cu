@@ -920,7 +920,10 @@ int tp_cos_emb_backward(const tp_cos_emb_args* a, void* stream) {
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned cols = (a->F * a->D + COS_EMB_THREADS - 1) / COS_EMB_THREADS;
-  cos_emb_backward_kernel<<<dim3(cols, a->P, s), COS_EMB_THREADS, 0, st>>>(k);
+  if (k.g_bf16)
+    cos_emb_backward_kernel<true><<<dim3(cols, a->P, s), COS_EMB_THREADS, 0, st>>>(k);
+  else
+    cos_emb_backward_kernel<false><<<dim3(cols, a->P, s), COS_EMB_THREADS, 0, st>>>(k);
   if (s > 1) cos_emb_finish_kernel<<<dim3(cols, a->P), COS_EMB_THREADS, 0, st>>>(k, s);
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;
