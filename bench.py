@@ -385,8 +385,8 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
-# DRAM bytes (read + write) per full-size launch, from the ncu captures summarised in
-# profiles/linear_block_fwd_bwd_256x4096x512.md (32-member case scaled by 256/32).
+# DRAM bytes (read + write) per full-size launch, from the ncu capture of the layer kernels
+# (32-member case scaled by 256/32).
 TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
     'fwd': (25.796096e6 + 212.714752e6) * 8,
     'act': (293.625344e6 + 94.327552e6) * 8,

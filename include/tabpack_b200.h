@@ -110,10 +110,13 @@ int tp_linear_backward(const tp_linear_grad_args* a, void* stream);
  *  - the workspace needs P * B * max_out elements (2 bytes in BF16 mode,
  *    4 bytes in F32 mode); larger calls are rejected with TP_EINVAL before any
  *    kernel runs;
- *  - every GPU that loads the library holds the TP_NOALLOC_SCRATCH_BYTES array
- *    until the process exits;
- *  - the first call on each device looks up the array's device address (set-up)
- *    and should come before any CUDA stream capture;
+ *  - the TP_NOALLOC_SCRATCH_BYTES array is reserved on a device the first time
+ *    the library's module is used there (its first kernel launch or its first
+ *    no-alloc call; at library load when CUDA_MODULE_LOADING=EAGER) and stays
+ *    reserved until the process exits;
+ *  - the first call in each CUDA context (the primary context of each device,
+ *    or a context the caller created) looks up the array's device address in
+ *    that context (set-up) and should come before any CUDA stream capture;
  *  - all calls share the one array and it keeps the last call's contents; calls
  *    whose kernels overlap on the GPU (different streams, no ordering) race;
  *  - `g_ready` is ignored: the activation gradient is always recomputed. */
@@ -212,7 +215,7 @@ int tp_metric_pack(const tp_metric_args* a, void* stream);
  * (maximize = 1) or -metric, top-k initialisation, forward selection with or
  * without replacement, stop at no improvement or the size limit.  The whole loop
  * runs on the device; `counts[c]` receives how often prediction c was selected, and
- * `status` (host memory) {iterations, distinct members, error} once the stream
+ * `status` (device memory) {iterations, distinct members, error} once the stream
  * reaches the end of the call.  error = 1 means a NaN score (the reference raises). */
 typedef struct tp_greedy_args {
   int32_t metric;

@@ -18,7 +18,8 @@ PKG = os.path.dirname(HERE)
 ROOT = os.path.dirname(PKG)
 LIB = os.path.join(PKG, 'libtabpack_b200.so')
 SOURCES = ['tabpack_b200.cu']
-HEADERS = ['common.cuh', 'linear_problem.cuh', 'gemm_sm100.cuh', 'gemm_simt.cuh', 'elementwise.cuh', 'muon.cuh', 'metrics.cuh', 'roc_auc.cuh', 'embeddings.cuh']
+# every header beside the translation unit, so that an edit to any of them triggers a rebuild
+HEADERS = sorted(f for f in os.listdir(HERE) if f.endswith('.cuh'))
 
 
 def nvcc_path() -> str:

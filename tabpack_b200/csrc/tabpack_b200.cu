@@ -106,21 +106,55 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 static __device__ __align__(256) unsigned char g_noalloc_scratch[TP_NOALLOC_SCRATCH_BYTES];
 
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};
+// (context, device address) pairs: a module's symbol has one address per CUDA context, so a
+// caller that drives a device through a non-primary context gets that context's copy.
+struct NoallocEntry {
+  CUcontext ctx;
+  void* addr;
+};
+NoallocEntry g_noalloc_addr[64] = {};
+int g_noalloc_n = 0;
 
-// Device address of g_noalloc_scratch on the current device (looked up once per device).
-int noalloc_scratch(void** out) {
-  int dev = 0;
-  TP_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return fail(TP_EUNSUPPORTED, "device index %d out of range", dev);
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
+PFN_cuCtxGetCurrent_v4000 ctx_current_fn() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
-    g_noalloc_addr[dev] = p;
-  }
-  *out = g_noalloc_addr[dev];
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  });
+  return fn;
+}
+
+// Device address of g_noalloc_scratch in the current context (looked up once per context).
+int noalloc_scratch(void** out) {
+  auto cur = ctx_current_fn();
+  if (!cur) return fail(TP_EUNSUPPORTED, "cuCtxGetCurrent is unavailable");
+  CUcontext ctx = nullptr;
+  if (cur(&ctx) != CUDA_SUCCESS) return fail(TP_EUNSUPPORTED, "cuCtxGetCurrent failed");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  for (int i = 0; ctx != nullptr && i < g_noalloc_n; ++i)
+    if (g_noalloc_addr[i].ctx == ctx) {
+      *out = g_noalloc_addr[i].addr;
+      return TP_OK;
+    }
+  // the first lookup in a context; with no context current, the runtime makes the current
+  // device's primary context current here
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+  if (ctx == nullptr && (cur(&ctx) != CUDA_SUCCESS || ctx == nullptr))
+    return fail(TP_EUNSUPPORTED, "no current CUDA context after the symbol lookup");
+  for (int i = 0; i < g_noalloc_n; ++i)
+    if (g_noalloc_addr[i].ctx == ctx) {
+      *out = g_noalloc_addr[i].addr;
+      return TP_OK;
+    }
+  if (g_noalloc_n == 64) return fail(TP_EUNSUPPORTED, "more than 64 CUDA contexts used the no-alloc entry point");
+  g_noalloc_addr[g_noalloc_n++] = NoallocEntry{ctx, p};
+  *out = p;
   return TP_OK;
 }
 

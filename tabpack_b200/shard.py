@@ -21,7 +21,9 @@ def member_ranges(n_members: int, world: int, cost: list[float] | None = None) -
 
     With `cost` (one number per member, e.g. its FLOPs per step) the cut points follow
     the cost prefix sums so that every rank gets about the same work; otherwise the
-    counts differ by at most one.
+    counts differ by at most one.  Whenever `n_members >= world` every rank gets at
+    least one member, however skewed the costs (a cut is clamped between one past the
+    previous cut and the last position that still leaves a member for each later rank).
     """
     if world <= 0 or n_members < 0:
         raise ValueError('world must be positive and n_members non-negative')
@@ -36,14 +38,17 @@ def member_ranges(n_members: int, world: int, cost: list[float] | None = None) -
     if len(cost) != n_members:
         raise ValueError('one cost per member is required')
     total = float(sum(cost))
-    cuts, acc, r = [0], 0.0, 1
-    for i, c in enumerate(cost):
+    prefix, acc = [], 0.0
+    for c in cost:
         acc += float(c)
-        while r < world and acc >= total * r / world and len(cuts) <= r:
-            cuts.append(i + 1)
-            r += 1
-    while len(cuts) < world:
-        cuts.append(n_members)
+        prefix.append(acc)
+    cuts = [0]
+    for k in range(1, world):
+        # first position whose prefix cost reaches the k-th share of the total
+        i = next((j + 1 for j, s in enumerate(prefix) if s >= total * k / world), n_members)
+        if n_members >= world:
+            i = min(max(i, cuts[-1] + 1), n_members - (world - k))
+        cuts.append(max(i, cuts[-1]))
     cuts.append(n_members)
     return [(cuts[k], cuts[k + 1]) for k in range(world)]
 

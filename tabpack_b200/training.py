@@ -139,6 +139,8 @@ class PackTrainer:
         self.world = dist.get_world_size(group) if (dist.is_initialized() and member_range is None) else 1
         self.rank = dist.get_rank(group) if (dist.is_initialized() and member_range is None) else 0
         self.ranges = member_ranges(n_members, self.world, cost)
+        if member_range is None:
+            self._check_ranges(self.ranges)
         lo, hi = self.ranges[self.rank] if member_range is None else member_range
         if hi <= lo:
             raise ValueError('every rank needs at least one member')
@@ -170,6 +172,14 @@ class PackTrainer:
             self.opt = AdamWPack([{'params': nd, 'weight_decay': 0.0}, {'params': wd}], pack_size=hi - lo, **okw)
         else:
             raise ValueError("optimizer type must be 'muon' or 'adamw'")
+
+    @staticmethod
+    def _check_ranges(ranges: list[tuple[int, int]]) -> None:
+        """Every rank computes the same ranges, so all ranks raise together here, before
+        any collective, instead of one rank leaving the others waiting in one."""
+        if any(b <= a for a, b in ranges):
+            raise ValueError(f'every rank needs at least one member ({ranges[-1][1]} members over '
+                             f'{len(ranges)} ranks)')
 
     # ------------------------------------------------------------------ training
     def _batches(self, n_rows: int, batch_size: int, epoch: int):

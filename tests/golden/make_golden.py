@@ -3,7 +3,7 @@
 Run from the repository root, in a container where the reference's sources are
 available (they are pure Python on top of PyTorch):
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /root/reference/src
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py PATH/TO/tabpack/src [FIXTURE ...]
 
 The reference (Abusagit/tabpack, package `tabpackage` 0.0.1) is imported
 unmodified.  Its only source of nondeterminism on the hot path is the dropout
@@ -410,22 +410,37 @@ def make_ensemble(tp):
     np.savez_compressed(os.path.join(HERE, 'ensemble.npz'), **arrays)
 
 
+FIXTURES = {
+    'block': lambda tp: (make_block(tp, torch.float64, 'block_fp64.npz'),
+                         make_block(tp, torch.float32, 'block_fp32.npz')),
+    'tabpack': lambda tp: (make_tabpack(tp, torch.float64, 'tabpack_fp64.npz'),
+                           make_tabpack(tp, torch.float64, 'tabpack_indexed_fp64.npz', forward_impl='indexed'),
+                           make_tabpack_large(tp, 'tabpack_large.npz')),
+    'cosine': lambda tp: (make_cosine(tp, torch.float64, 'cosine_fp64.npz'),
+                          make_cosine(tp, torch.float32, 'cosine_fp32.npz'),
+                          make_tabpack_cosine(tp, torch.float64, 'tabpack_cosine_fp64.npz')),
+    'adamw': lambda tp: make_adamw(tp),
+    'newton_schulz': lambda tp: make_newton_schulz(tp),
+    'muon': lambda tp: make_muon(tp),
+    'metrics': lambda tp: make_metrics(tp),
+    'ensemble': lambda tp: make_ensemble(tp),
+}
+
+
 def main():
-    src = sys.argv[1] if len(sys.argv) > 1 else '/root/reference/src'
+    """`make_golden.py SRC [FIXTURE ...]`: SRC is the reference's `src` directory (or set
+    TABPACK_REFERENCE_SRC); with no FIXTURE names every fixture is written."""
+    args = sys.argv[1:]
+    src = args.pop(0) if args else os.environ.get('TABPACK_REFERENCE_SRC')
+    if not src:
+        sys.exit('usage: make_golden.py REFERENCE_SRC [FIXTURE ...] (or set TABPACK_REFERENCE_SRC); '
+                 f'fixtures: {", ".join(FIXTURES)}')
+    unknown = [a for a in args if a not in FIXTURES]
+    if unknown:
+        sys.exit(f'unknown fixtures {unknown}; choose from {", ".join(FIXTURES)}')
     tp = _import_reference(src)
-    make_block(tp, torch.float64, 'block_fp64.npz')
-    make_block(tp, torch.float32, 'block_fp32.npz')
-    make_tabpack(tp, torch.float64, 'tabpack_fp64.npz')
-    make_tabpack(tp, torch.float64, 'tabpack_indexed_fp64.npz', forward_impl='indexed')
-    make_tabpack_large(tp, 'tabpack_large.npz')
-    make_cosine(tp, torch.float64, 'cosine_fp64.npz')
-    make_cosine(tp, torch.float32, 'cosine_fp32.npz')
-    make_tabpack_cosine(tp, torch.float64, 'tabpack_cosine_fp64.npz')
-    make_adamw(tp)
-    make_newton_schulz(tp)
-    make_muon(tp)
-    make_metrics(tp)
-    make_ensemble(tp)
+    for name in args or FIXTURES:
+        FIXTURES[name](tp)
     print('fixtures written to', HERE)
 
 

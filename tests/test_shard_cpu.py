@@ -25,6 +25,30 @@ def test_member_ranges_cover_members_in_order():
     assert max(loads) - min(loads) <= max(cost)
 
 
+@pytest.mark.parametrize('n,world,cost', [
+    (4, 4, [10.0, 1.0, 1.0, 1.0]),
+    (8, 4, [100.0] + [1.0] * 7),
+    (8, 4, [1.0] * 7 + [100.0]),
+    (9, 8, [1.0, 1.0, 1.0, 1.0, 50.0, 1.0, 1.0, 1.0, 1.0]),
+    (512, 8, [1e6] + [1.0] * 511),
+])
+def test_member_ranges_skewed_cost_leaves_no_rank_empty(n, world, cost):
+    r = member_ranges(n, world, cost)
+    assert r[0][0] == 0 and r[-1][1] == n
+    assert all(r[k][1] == r[k + 1][0] for k in range(world - 1))
+    assert all(b > a for a, b in r), r
+
+
+def test_member_ranges_fewer_members_than_ranks_raises_on_every_rank():
+    from tabpack_b200.training import PackTrainer
+
+    r = member_ranges(2, 4, [1.0, 5.0])
+    assert r[0][0] == 0 and r[-1][1] == 2 and sum(b - a for a, b in r) == 2
+    # the check runs on the ranges every rank computes alike, before any collective
+    with pytest.raises(ValueError, match='every rank needs at least one member'):
+        PackTrainer._check_ranges(r)
+
+
 def test_permutation_keys_depend_only_on_global_member():
     full = permutation_keys(seed=123, epoch=4, members=np.arange(10), n_rows=257)
     part = permutation_keys(seed=123, epoch=4, members=np.arange(6, 10), n_rows=257)

@@ -67,6 +67,46 @@ def test_noalloc_backward_matches_allocating_backward(dtype):
     assert lib.tp_device_error() == 0
 
 
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
+def test_noalloc_backward_plain_linear_uses_no_scratch(dtype):
+    """A plain linear layer (no ReLU, no dropout, no per-member widths or depths): dY is the
+    activation gradient itself, so the entry point passes it straight to dgrad / wgrad and
+    leaves the built-in scratch alone.  Its size limit does not apply either: this case is
+    larger than the scratch."""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+    from tabpack_b200 import _lib, ops
+
+    lib = _lib.load()
+    torch.manual_seed(11)
+    # P * B * max_out = 3 * 2048 * 1536 elements: 18 MiB in bf16, more than the 16 MiB scratch
+    P, B, max_in, max_out = 3, 2048, 96, 1536
+    dev = 'cuda'
+    x = torch.randn(P, B, max_in, device=dev).to(dtype)
+    w = (torch.randn(P, max_out, max_in, device=dev) / max_in ** 0.5).to(dtype)
+    b = torch.randn(P, max_out, device=dev) * 0.1
+    y = ops.linear_forward(x, w, b)
+    rtol = 2.0 ** -7 if dtype == torch.bfloat16 else 1e-5
+    for call in range(2):
+        dy = torch.randn(P, B, max_out, device=dev).to(dtype)
+        dx_ref, dw_ref, db_ref = ops.linear_backward(dy, x, w, y)
+        dx = torch.full((P, B, max_in), float('nan'), device=dev, dtype=dtype)
+        dw = torch.full((P, max_out, max_in), float('nan'), device=dev)
+        db = torch.full((P, max_out), float('nan'), device=dev)
+        ga = _lib.LinearGradArgs()
+        ga.fwd = ops._linear_args(x, w, None, None, None, None, 0, False, None, 0, 0, 0, None)
+        ga.dy, ga.y, ga.g = dy.data_ptr(), y.data_ptr(), None
+        ga.dbias, ga.dx, ga.dw = db.data_ptr(), dx.data_ptr(), dw.data_ptr()
+        ga.dw_rows, ga.dw_cols, ga.db_cols = max_out, max_in, max_out
+        rc = lib.tp_linear_backward_noalloc(ctypes.byref(ga), torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, lib.tp_last_error_string()
+        torch.cuda.synchronize()
+        _close(dx, dx_ref, rtol)
+        _close(dw, dw_ref, rtol)
+        _close(db, db_ref, rtol)
+    assert lib.tp_device_error() == 0
+
+
 def test_noalloc_rejects_oversized_and_caller_workspace():
     if not torch.cuda.is_available():
         pytest.skip('needs a GPU')
