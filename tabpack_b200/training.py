@@ -10,13 +10,22 @@ member id (initialisation, batch order, dropout), so a member trains identically
 (`_training.py:1909-2018`): every member's transformed prediction plus ensemble heads
 that average selected members, summed across ranks with one all-reduce.
 
-The reference's checkpoint store, early stopping and model-replacement queue are host
-bookkeeping around this loop and are not part of this module.
+`PackTrainer.fit` runs the reference's epoch loop end to end (`_training.py:2643-2960`):
+per-member best checkpoints by the validation metric with early-stopping patience
+(`update_training_state`, `_training.py:754-821`), and an online greedy ensemble rebuilt
+after every epoch from the current members, the best checkpoints of finished members and
+the latest checkpoints of running ones, accepted only when its validation score improves
+(`Ensemble.update`, `_training.py:1061-1183`).  A member that stops keeps its place in the
+pack with a zero learning rate (its parameters no longer change) where the reference removes
+it from the pack; the model-replacement queue of `max_pack_size < n_models` is not part of
+this module.
 """
 
 from __future__ import annotations
 
 import dataclasses
+import math
+from typing import Callable
 
 import torch
 import torch.distributed as dist
@@ -24,7 +33,7 @@ import torch.nn.functional as F
 from torch import Tensor
 
 from tabpack_b200 import ops
-from tabpack_b200.ensemble import greedy_ensemble
+from tabpack_b200.ensemble import compute_unsanitized_ensemble_predictions, greedy_ensemble
 from tabpack_b200.metrics import PackScore
 from tabpack_b200.nn import CosineEmbeddingsPack, LinearPack, TabPack
 from tabpack_b200.optim import AdamWPack, MuonAdamWPack, split_weight_decay
@@ -43,19 +52,26 @@ def _mix(*xs: int) -> int:
 
 
 @torch.no_grad()
-def init_member_parameters_(model: torch.nn.Module, *, seed: int, member_ids: list[int]) -> None:
+def init_member_parameters_(model: torch.nn.Module, *, seed: int, member_ids: list[int],
+                            generator_device: str | torch.device | None = None) -> None:
     """Re-initialise every LinearPack (and CosineEmbeddingsPack) member from its own generator.
 
     Same distribution as `LinearPack.reset_parameters` (`nn.py:702-747`), U(+-1/sqrt(in_i))
     for weights and biases, but member m of the j-th LinearPack draws from a generator
     seeded by (seed, global member id, j): initial weights do not depend on sharding.
+    The generators live on the parameters' device unless `generator_device` names another
+    one (e.g. 'cpu': the same numbers on any machine, drawn on the host and copied over).
     """
+    def gen(dev, key):
+        d = torch.device(generator_device) if generator_device is not None else dev
+        return torch.Generator(device=d).manual_seed(key), d
+
     for j, emb in enumerate(m for m in model.modules() if isinstance(m, CosineEmbeddingsPack)):
         # CosineEmbeddingsPack.reset_parameters (`nn.py:1706-1753`): truncated N(0, 1) on
         # [-3, 3] times the member's init scale, the affine parts zero
         for m, gid in enumerate(member_ids):
-            g = torch.Generator(device=emb.weight.device).manual_seed(_mix(seed, gid, 0xE0 + j))
-            w = torch.empty(emb.weight.shape[1:], device=emb.weight.device, dtype=emb.weight.dtype)
+            g, d = gen(emb.weight.device, _mix(seed, gid, 0xE0 + j))
+            w = torch.empty(emb.weight.shape[1:], device=d, dtype=emb.weight.dtype)
             torch.nn.init.trunc_normal_(w, a=-3.0, b=3.0, generator=g)
             scale = emb.init_scale if isinstance(emb.init_scale, float) else float(emb.init_scale[m])
             emb.weight[m].copy_(w * scale)
@@ -65,12 +81,12 @@ def init_member_parameters_(model: torch.nn.Module, *, seed: int, member_ids: li
     for j, lin in enumerate(linears):
         inf = lin.in_features.tolist() if lin.in_features is not None else [lin.max_in_features] * lin.pack_size
         for m, gid in enumerate(member_ids):
-            g = torch.Generator(device=lin.weight.device).manual_seed(_mix(seed, gid, j))
+            g, d = gen(lin.weight.device, _mix(seed, gid, j))
             b = inf[m] ** -0.5
             for p in (lin.weight, lin.bias):
                 if p is None:
                     continue
-                u = torch.rand(p.shape[1:], generator=g, device=p.device, dtype=p.dtype)
+                u = torch.rand(p.shape[1:], generator=g, device=d, dtype=p.dtype)
                 p[m].copy_(torch.lerp(torch.full_like(u, -b), torch.full_like(u, b), u))
 
 
@@ -124,15 +140,98 @@ class EpochResult:
     ensemble_score: float         # the ensemble's validation metric
 
 
+CheckpointKey = tuple[int, int]
+"""(global member id, training step) of an evaluated checkpoint (`ModelCheckpointKey`,
+`_training.py:531-540`)."""
+
+
+class OnlineEnsemble:
+    """The reference's `Ensemble` in online mode with an evaluation criterion
+    (`_training.py:978-1183`), over checkpoint keys.
+
+    After every epoch the candidates are the current members first, then the best
+    checkpoints of finished members and the latest checkpoints of running members that are
+    not members already (current members first: selection breaks ties by candidate order);
+    greedy selection (`greedy_ensemble`, `ensemble.py:95-263`) picks from their validation
+    predictions, and the rebuilt ensemble -- the mean of its members' predictions -- replaces
+    the current one only when its score is higher.  A pool that holds exactly the current
+    members counts as an update without improvement."""
+
+    def __init__(self, score: PackScore, *, max_ensemble_size: int | None = 32, init_top_k: int = 1,
+                 with_replacement: bool = False, early_stopping_patience: int | None = None) -> None:
+        if early_stopping_patience is not None and early_stopping_patience < 0:
+            raise ValueError('The early stopping patience must be non-negative')
+        self.score = score
+        self.max_ensemble_size = max_ensemble_size
+        self.init_top_k = init_top_k
+        self.with_replacement = with_replacement
+        self.early_stopping_patience = early_stopping_patience
+        self.member_keys: list[CheckpointKey] | None = None
+        self.member_weights: Tensor | None = None
+        self.best_score: float | None = None
+        self.n_consecutive_bad_updates = 0
+
+    def is_running(self) -> bool:
+        return self.early_stopping_patience is None or self.n_consecutive_bad_updates <= self.early_stopping_patience
+
+    def update(self, predictions: Callable[[CheckpointKey], Tensor], finished_best: list[CheckpointKey],
+               running_latest: list[CheckpointKey]) -> bool:
+        """`Ensemble.update` (`_training.py:1061-1183`); `predictions(key)` returns a
+        checkpoint's validation predictions.  Returns whether the ensemble was replaced."""
+        if not self.is_running():
+            raise RuntimeError('the ensemble is finalized')
+        candidates = list(finished_best) + list(running_latest)
+        if not candidates or len(set(candidates)) != len(candidates):
+            raise ValueError('candidate checkpoints must be non-empty and distinct')
+        if self.member_keys is not None:
+            current = set(self.member_keys)
+            candidates = list(self.member_keys) + [k for k in candidates if k not in current]
+            if set(candidates) == current:
+                self.n_consecutive_bad_updates += 1
+                return False
+        pool = torch.stack([predictions(k) for k in candidates])
+        idx, weights = greedy_ensemble(pool, score_fn=self.score, init_top_k=self.init_top_k,
+                                       max_ensemble_size=self.max_ensemble_size,
+                                       with_replacement=self.with_replacement)
+        keys = [candidates[i] for i in idx.tolist()]
+        if len(set(keys)) != len(keys):
+            raise ValueError('The ensemble algorithm selected the same model checkpoint more than once')
+        blend = compute_unsanitized_ensemble_predictions(pool[idx], weights)
+        score = float(self.score(blend[None])[0])
+        improved = not math.isnan(score) and (self.best_score is None or self.best_score < score)
+        if improved:
+            self.member_keys, self.member_weights, self.best_score = keys, weights, score
+            self.n_consecutive_bad_updates = 0
+        else:
+            self.n_consecutive_bad_updates += 1
+        return improved
+
+
+@dataclasses.dataclass
+class FitResult:
+    """What `PackTrainer.fit` leaves behind (cf. `TrainedTabPack`, `_training.py:2021-2364`).
+    Metrics are the validation criterion (lower is better for every loss here)."""
+    history: list[dict]            # per epoch: 'step' (training loop step), 'val_metric' (P,) of the
+                                   # members trained that epoch (NaN for stopped ones), 'train_loss' (P,)
+    best_step: Tensor              # (P,) step of each member's best checkpoint
+    best_metric: Tensor            # (P,) its validation metric
+    ensemble_keys: list[CheckpointKey]
+    ensemble_weights: Tensor | None
+    ensemble_metric: float
+    ensemble_history: list[dict]   # accepted updates: 'step', 'keys', 'metric'
+
+
 class PackTrainer:
     """Trains a pack of TabPack MLPs, members sharded over the process group."""
 
     def __init__(self, *, n_members: int, model: dict, per_member_model: list[dict], optimizer: dict,
                  per_member_optimizer: list[dict] | None = None, loss: str, seed: int, device,
                  autocast_bf16: bool = True, group=None, cost: list[float] | None = None,
-                 member_range: tuple[int, int] | None = None) -> None:
+                 member_range: tuple[int, int] | None = None, init_on_host: bool = False) -> None:
         """`member_range` pins this trainer to global members [lo, hi) without a process
-        group (several shards on one device); otherwise the group's rank picks its range."""
+        group (several shards on one device); otherwise the group's rank picks its range.
+        `init_on_host` draws the initial parameters with host generators (the same values on
+        every machine and device; slower for large packs)."""
         if loss not in _LOSSES:
             raise ValueError(f'loss must be one of {_LOSSES}')
         self.group = group
@@ -146,6 +245,8 @@ class PackTrainer:
             raise ValueError('every rank needs at least one member')
         self.lo, self.hi = lo, hi
         self.counts = [b - a for a, b in self.ranges] if member_range is None else [hi - lo]
+        # global ids of the rows that gather_members returns (this shard's alone with member_range)
+        self.gathered_ids = list(range(n_members)) if member_range is None else list(range(lo, hi))
         self.loss = loss
         self.seed = int(seed)
         self.autocast = autocast_bf16
@@ -155,7 +256,8 @@ class PackTrainer:
         self.model = TabPack(pack_size=hi - lo, **kw).to(self.device)
         self.model.backbone.set_member_base(lo)
         self.model.backbone._stream.seed = _mix(self.seed, 0xD0)  # one Philox key on every rank
-        init_member_parameters_(self.model, seed=self.seed, member_ids=list(range(lo, hi)))
+        init_member_parameters_(self.model, seed=self.seed, member_ids=list(range(lo, hi)),
+                                generator_device='cpu' if init_on_host else None)
         okw = dict(optimizer)
         otype = okw.pop('type')
         if per_member_optimizer is not None:
@@ -235,6 +337,118 @@ class PackTrainer:
     def _score(self, y_val: Tensor) -> PackScore:
         return PackScore({'mse': 'mse', 'bce': 'bce', 'ce': 'ce'}[self.loss], y_val, maximize=False)
 
+    def predict(self, data: dict, *, eval_batch_size: int = 32768) -> Tensor:
+        """Transformed predictions of every member (gathered over ranks when sharded)."""
+        local = self.predict_local(data, eval_batch_size=eval_batch_size)
+        return gather_members(local, self.counts, self.group) if self.world > 1 else local
+
+    def _freeze(self, local_idx: list[int]) -> None:
+        """Stop updating these members: a zero learning rate makes every optimizer update of
+        theirs (weight decay included, p * (1 - lr * wd)) leave the parameters unchanged."""
+        if not local_idx:
+            return
+        idx = torch.tensor(local_idx, device=self.device)
+        P = self.hi - self.lo
+        for g in self.opt.param_groups:
+            for key in ('lr', 'adamw_lr', 'muon_lr'):
+                if key not in g:
+                    continue
+                v = g[key]
+                if not isinstance(v, Tensor):
+                    v = torch.full((P,), float(v), device=self.device)
+                v = v.to(self.device, torch.float32).clone()
+                v[idx] = 0.0
+                g[key] = v
+
+    def fit(self, train: dict, val: dict, *, batch_size: int, max_epochs: int,
+            early_stopping_patience: int | None = None, ensemble: OnlineEnsemble | None = None,
+            eval_batch_size: int = 32768) -> FitResult:
+        """The reference's training loop (`_training.py:2643-2960`) for a pack whose members
+        all start together: train an epoch, evaluate every member on `val`, update each
+        member's best checkpoint (`update_training_state`, `_training.py:754-821`), stop the
+        members that reached `max_epochs` or ran out of patience (their best checkpoints are
+        then final), and update `ensemble` (by default an `OnlineEnsemble` over the validation
+        criterion, at most 32 members).  Ends when every member has finished."""
+        if max_epochs <= 0:
+            raise ValueError('max_epochs must be positive')
+        score = self._score(val['y'])
+        if ensemble is None:
+            ensemble = OnlineEnsemble(score)
+        ids = self.gathered_ids
+        P = len(ids)
+        pos = {g: i for i, g in enumerate(ids)}
+        steps_per_epoch = math.ceil(len(train['y']) / batch_size)
+        max_steps = max_epochs * steps_per_epoch
+        steps = [0] * P
+        n_bad = [0] * P
+        active = [True] * P
+        best_metric: list[float] | None = None
+        best_step = [0] * P
+        best_pred: Tensor | None = None
+        finished: list[CheckpointKey] = []
+        store: dict[CheckpointKey, Tensor] = {}
+        history: list[dict] = []
+        ensemble_history: list[dict] = []
+        loop_step = 0
+        for epoch in range(max_epochs):
+            loss = self.fit_epoch(train, batch_size=batch_size, epoch=epoch)
+            loop_step += steps_per_epoch
+            for i in range(P):
+                if active[i]:
+                    steps[i] += steps_per_epoch
+            preds = self.predict(val, eval_batch_size=eval_batch_size)
+            latest = (-score(preds)).double().cpu().tolist()
+            if best_metric is None:
+                best_metric = list(latest)
+                best_step = list(steps)
+                best_pred = preds.clone()
+                for i in range(P):
+                    n_bad[i] += int(math.isnan(latest[i]))
+            else:
+                better = [active[i] and not math.isnan(latest[i])
+                          and (math.isnan(best_metric[i]) or latest[i] < best_metric[i]) for i in range(P)]
+                rows = [i for i in range(P) if better[i]]
+                for i in range(P):
+                    if active[i]:
+                        n_bad[i] = 0 if better[i] else n_bad[i] + 1
+                for i in rows:
+                    best_metric[i], best_step[i] = latest[i], steps[i]
+                if rows:
+                    r = torch.tensor(rows, device=preds.device)
+                    best_pred[r] = preds[r]
+            running = [active[i] and steps[i] < max_steps
+                       and (early_stopping_patience is None or n_bad[i] <= early_stopping_patience) for i in range(P)]
+            stopped = [i for i in range(P) if active[i] and not running[i]]
+            finished += [(ids[i], best_step[i]) for i in stopped]
+            running_latest = [(ids[i], steps[i]) for i in range(P) if running[i]]
+
+            def lookup(key: CheckpointKey) -> Tensor:
+                i = pos[key[0]]
+                if active[i] and key[1] == steps[i]:
+                    return preds[i]
+                if key[1] == best_step[i]:
+                    return best_pred[i]
+                return store[key]
+
+            if ensemble.is_running() and (finished or running_latest):
+                if ensemble.update(lookup, finished, running_latest):
+                    ensemble_history.append({'step': loop_step, 'keys': list(ensemble.member_keys),
+                                             'metric': -ensemble.best_score})
+            # keep the predictions that later updates may need: finished members' best
+            # checkpoints and the current ensemble members (`rebuild_checkpoint_store`)
+            required = set(finished) | set(ensemble.member_keys or [])
+            store = {k: (store[k] if k in store else lookup(k).clone()) for k in required}
+            history.append({'step': loop_step, 'val_metric': torch.tensor(
+                [latest[i] if active[i] else math.nan for i in range(P)], dtype=torch.float64), 'train_loss': loss})
+            self._freeze([ids[i] - self.lo for i in stopped if self.lo <= ids[i] < self.hi])
+            active = running
+            if not any(active):
+                break
+        return FitResult(history=history, best_step=torch.tensor(best_step), best_metric=torch.tensor(best_metric),
+                         ensemble_keys=list(ensemble.member_keys or []), ensemble_weights=ensemble.member_weights,
+                         ensemble_metric=math.nan if ensemble.best_score is None else -ensemble.best_score,
+                         ensemble_history=ensemble_history)
+
     def evaluate_and_ensemble(self, data: dict, *, epoch: int, train_loss: Tensor, eval_batch_size: int = 32768,
                               max_ensemble_size: int | None = 32) -> EpochResult:
         """Validation predictions of all members (all-gathered over NVLink when sharded),
@@ -286,5 +500,5 @@ def assert_finite(x: Tensor, what: str) -> None:
         raise FloatingPointError(f'{what} is not finite')
 
 
-__all__ = ['PackTrainer', 'PackPredictor', 'EpochResult', 'init_member_parameters_', 'member_loss', 'transform',
-           'assert_finite']
+__all__ = ['PackTrainer', 'PackPredictor', 'EpochResult', 'FitResult', 'OnlineEnsemble', 'CheckpointKey',
+           'init_member_parameters_', 'member_loss', 'transform', 'assert_finite']

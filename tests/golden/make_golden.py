@@ -410,6 +410,172 @@ def make_ensemble(tp):
     np.savez_compressed(os.path.join(HERE, 'ensemble.npz'), **arrays)
 
 
+def make_init(tp):
+    """`LinearPack.reset_parameters` (`nn.py:702-747`) from a seeded global RNG: ragged
+    per-member input widths, a shared width, and a re-initialisation of selected members."""
+    arrays = {}
+    torch.manual_seed(12)
+    lin = tp.nn.LinearPack([40, 16, 33], [48, 16, 20], max_in_features=40, max_out_features=48, pack_size=3)
+    arrays['ragged.weight'], arrays['ragged.bias'] = _np(lin.weight), _np(lin.bias)
+    torch.manual_seed(13)
+    lin.reset_parameters(pack_idx=torch.tensor([2, 0]))
+    arrays['ragged.reset.weight'], arrays['ragged.reset.bias'] = _np(lin.weight), _np(lin.bias)
+    torch.manual_seed(14)
+    shared = tp.nn.LinearPack(24, 12, pack_size=4)
+    arrays['shared.weight'], arrays['shared.bias'] = _np(shared.weight), _np(shared.bias)
+    torch.manual_seed(15)
+    shared.reset_parameters(pack_idx=torch.tensor([1]))
+    arrays['shared.reset.weight'], arrays['shared.reset.bias'] = _np(shared.weight), _np(shared.bias)
+    np.savez_compressed(os.path.join(HERE, 'init.npz'), **arrays)
+
+
+def make_training(tp, dtype=torch.float32, name='train_config1.npz'):
+    """The reference's own `train` (`_training.py:3068-3296`) on the 16-member CPU plumbing
+    run (`synthetic.py`): AdamW, 20 epochs, per-member best checkpoints by validation
+    MSE and an online greedy ensemble (at most 32 members) built and scored on validation
+    MSE after every epoch.  Three inputs are injected so that a run of this package can be
+    compared with it on the same footing:
+
+    * the initial parameters: this package's `init_member_parameters_` drawn on host
+      generators (the same distribution as `LinearPack.reset_parameters`), loaded into the
+      reference's `TabPack` right after it is built;
+    * the batch order: the stable argsort of the Philox permutation keys
+      (`oracle.philox.permutation_keys`) in place of `make_shuffled_batch_indices_pack`'s
+      `torch.rand(...).argsort()` (`_training.py:323-338`);
+    * the dropout masks: the Philox keep mask (`oracle.layers.dropout_mask_values`) in place
+      of `bernoulli_` (`nn.py:897-901`), block i of the k-th training forward at offset
+      k * max_n_blocks + i, members keyed by their model id.
+
+    Everything else -- forward, loss, backward, `AdamWPack.step`, evaluation, best-checkpoint
+    bookkeeping, `Ensemble.update` and `greedy_ensemble` -- is the reference's code.
+
+    With dtype=float64 the model (parameters, activations, optimizer state) runs in fp64;
+    the data stay fp32 as `train` requires and the model's output is cast to fp32 by the
+    reference's `forward` (`_training.py:154-167`).  That run is the yardstick for how far
+    rounding alone moves this training: the fp32 run's distance from it is the reference's
+    own rounding drift.
+    """
+    sys.path.insert(0, HERE)
+    import synthetic
+
+    from oracle.layers import dropout_mask_values
+    from oracle.philox import permutation_keys
+    from tabpack_b200.nn import TabPack as OwnTabPack
+    from tabpack_b200.training import _mix, init_member_parameters_
+
+    seed = 0
+    data = synthetic.datasets(0)
+    hp = synthetic.hyperparameters(1)
+    P = len(hp)
+    nb = [h['model']['n_blocks'] for h in hp]
+    db = [h['model']['d_block'] for h in hp]
+    dp = [h['model']['dropout'] for h in hp]
+    lr = [h['optimizer']['lr'] for h in hp]
+    max_nb, max_db = max(nb), max(db)
+    own = OwnTabPack(n_numerical_features=synthetic.N_NUM, categorical_cardinalities=synthetic.CARDS, d_out=1,
+                     n_blocks=nb, d_block=db, dropout=dp, pack_size=P, max_n_blocks=max_nb, max_d_block=max_db)
+    init_member_parameters_(own, seed=seed, member_ids=list(range(P)), generator_device='cpu')
+    init_state = {k: v.clone() for k, v in own.state_dict().items()}
+
+    ref_tabpack = tp.nn.TabPack
+    ref_shuffle = tp._training.make_shuffled_batch_indices_pack
+    ref_dropout = tp.nn.DropoutPack.forward
+    block_of = {}
+    state = {'epoch': 0, 'forwards': 0}
+
+    class InitialisedTabPack(ref_tabpack):
+        def __init__(self, **kw):
+            # built in fp32 (the reference's initialisation mixes fp32 bounds into the
+            # parameters' dtype), then cast; the forward's one-hot block follows the default
+            # dtype, which stays `dtype` for the whole run
+            prev = torch.get_default_dtype()
+            torch.set_default_dtype(torch.float32)
+            try:
+                super().__init__(**kw)
+            finally:
+                torch.set_default_dtype(prev)
+            self.load_state_dict(init_state, strict=True)
+            self.to(dtype)
+            for i, b in enumerate(self.backbone.blocks):
+                block_of[id(b.dropout)] = i
+
+        def forward(self, x_num=None, x_cat=None, *args, **kw):
+            return super().forward(None if x_num is None else x_num.to(dtype), x_cat, *args, **kw)
+
+    def shuffled(*, total_size, batch_size, pack_size, generator=None, device=None):
+        keys = permutation_keys(seed=_mix(seed, 0xBA), epoch=state['epoch'], members=np.arange(pack_size),
+                                n_rows=total_size)
+        state['epoch'] += 1
+        order = torch.from_numpy(np.argsort(keys, axis=1, kind='stable')).to(device)
+        return list(order.split(batch_size, dim=1))
+
+    def dropout(mod, x, pack_idx=None):
+        if not mod.training:
+            return ref_dropout(mod, x, pack_idx)
+        assert pack_idx is None
+        i = block_of[id(mod)]
+        if i == 0:
+            state['forwards'] += 1
+        offset = (state['forwards'] - 1) * max_nb + i
+        mv = dropout_mask_values(seed=_mix(seed, 0xD0), offset=offset, members=np.arange(x.shape[0]),
+                                 n_rows=x.shape[1], n_cols=x.shape[2], p=_np(mod.p), dtype=np.float32)
+        return torch.from_numpy(mv).to(x.dtype) * x
+
+    def mse_loss(y_pred, y):
+        return ((y_pred.squeeze(-1) - y) ** 2).mean(1)
+
+    def ensemble_mse(*, y_true, y_pred):
+        # an ensemble's metric is a scalar: the pack metric of a one-member pack, as the
+        # reference's sklearn layer wraps it (`sklearn/_config.py:221`)
+        return tp.metrics.mse_pack(y_true=y_true, y_pred=y_pred.unsqueeze(0))[0]
+
+    torch_data = {k: {n: torch.from_numpy(a) for n, a in v.items()} for k, v in data.items()}
+    crit = tp.EvalCriterionConfig(dataset='val', metric='mse', metric_direction='minimize')
+    ens = tp.EnsembleConfig(
+        algorithm={'type': tp.ensemble.greedy_ensemble, 'max_ensemble_size': 32}, online=True,
+        prediction_transform=None, early_stopping_patience=None, algorithm_metric=tp.metrics.mse_pack,
+        algorithm_metric_direction='minimize', algorithm_dataset='val', algorithm_device=torch.device('cpu'))
+    tp.nn.TabPack = InitialisedTabPack
+    tp._training.make_shuffled_batch_indices_pack = shuffled
+    tp.nn.DropoutPack.forward = dropout
+    torch.set_default_dtype(dtype)
+    try:
+        res = tp.train(
+            datasets=torch_data, model={'d_out': 1, 'categorical_cardinalities': synthetic.CARDS},
+            prediction_transform=functools.partial(torch.squeeze, dim=-1), loss_fn=mse_loss,
+            optimizer={'type': tp.optim.AdamWPack, 'weight_decay': synthetic.WEIGHT_DECAY},
+            batch_size=synthetic.BATCH, max_epochs=20, early_stopping_patience=None, per_model_hyperparameters=hp,
+            eval_metrics={'val': {'mse': tp.metrics.mse_pack}}, eval_criterion=crit, ensembles={'greedy': ens},
+            ensemble_eval_metrics={'val': {'mse': ensemble_mse}}, ensemble_eval_criterion=crit,
+            stop_when_all_ensembles_are_finalized=False, seed=seed, device='cpu', aux_device='cpu',
+            autocast_dtype=None, print_progress=False, show_progress_bar=False)
+    finally:
+        torch.set_default_dtype(torch.float32)
+        tp.nn.TabPack = ref_tabpack
+        tp._training.make_shuffled_batch_indices_pack = ref_shuffle
+        tp.nn.DropoutPack.forward = ref_dropout
+    hist = res.load_model_history()
+    ids = torch.arange(P)
+    arrays = {
+        'n_blocks': np.array(nb, np.int32), 'd_block': np.array(db, np.int32), 'dropout': np.array(dp, np.float32),
+        'lr': np.array(lr, np.float64), 'seed': np.int64(seed), 'max_epochs': np.int32(20),
+        'epoch_step': np.array([h['training_loop_step'] for h in hist], np.int64),
+        'epoch_val_mse': np.stack([_np(h['metrics']['val']['mse']) for h in hist]),
+        'best_step': _np(res.load_model_steps(ids)),
+        'best_val_mse': _np(res.load_model_metrics(ids)['val']['mse']),
+        'ensemble_ids': _np(res.load_ensemble_member_ids('greedy')),
+        'ensemble_steps': _np(res.load_ensemble_member_steps('greedy')),
+        'ensemble_val_mse': np.float64(res.load_ensemble_metrics('greedy')['val']['mse']),
+    }
+    eh = res.load_ensemble_history('greedy')
+    arrays['update_step'] = np.array([u['training_loop_step'] for u in eh], np.int64)
+    arrays['update_val_mse'] = np.array([float(u['metrics']['val']['mse']) for u in eh], np.float64)
+    arrays['update_sizes'] = np.array([len(u['members']['ids']) for u in eh], np.int32)
+    arrays['update_ids'] = np.concatenate([_np(u['members']['ids']) for u in eh])
+    arrays['update_steps'] = np.concatenate([_np(u['members']['steps']) for u in eh])
+    np.savez_compressed(os.path.join(HERE, name), **arrays)
+
+
 FIXTURES = {
     'block': lambda tp: (make_block(tp, torch.float64, 'block_fp64.npz'),
                          make_block(tp, torch.float32, 'block_fp32.npz')),
@@ -424,6 +590,9 @@ FIXTURES = {
     'muon': lambda tp: make_muon(tp),
     'metrics': lambda tp: make_metrics(tp),
     'ensemble': lambda tp: make_ensemble(tp),
+    'init': lambda tp: make_init(tp),
+    'training': lambda tp: make_training(tp),
+    'training_fp64': lambda tp: make_training(tp, torch.float64, 'train_config1_fp64.npz'),
 }
 
 
