@@ -1,23 +1,28 @@
-"""Benchmark of the packed-ensemble hot path on B200: the ragged grouped GEMM layer.
+"""Benchmarks of the packed-ensemble hot path on B200.
 
-Workload (per GPU): a pack of 256 members sharing one 4096 x 512 bf16 input
-batch; member i has its own output width out_i ~ U{64, 80, ..., 1024}, weights
-U(+-1/sqrt(512)), a bias, ReLU and dropout with p_i ~ U[0, 0.5].  One step is
-the forward pass (one fused launch: GEMM + bias + ReLU + Philox dropout) and the
-backward pass (activation/bias gradient, dgrad, wgrad) of that layer, i.e.
-3 x sum_i 2 * 4096 * 512 * out_i ragged FLOPs.  Members are sharded over GPUs
-(weak scaling: every rank owns its own 256 members, keyed by global member id);
-the layer has no cross-member exchange, so the timed region has no collective.
+Default workload (`--workload train`): full TabPack training of the full-training
+configuration -- a global pack of 512 members (depth U{1..4}, width U{128..1024}, dropout
+U[0, 0.5]) on 1 000 000 synthetic rows with 100 numerical and 10 categorical features,
+batch 1024, BCE, Muon + AdamW, bf16 autocast -- with the members sharded over the GPUs
+(contiguous ranges balanced by FLOPs per step; strong scaling).  The timed region is an
+epoch scaled to K steps: K training steps over the first K x 1024 rows, then the epoch end
+over the first K / 977 of the 100 000 validation rows (every member's predictions
+all-gathered over NCCL, a greedy ensemble built from them).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload ...]
 
-Prints one JSON line (rank 0).  `value` is whole-job member-samples/s with all
-inputs resident in HBM; `e2e` repeats the measurement through the same C-ABI
-calls with the input batch copied from pinned host memory and the bias
-gradient read back every step; `roofline` covers the kernel with the largest
-share of the step; `cpu_baseline` times the numpy restatement of the same layer
-on a bounded member sample on this host.  `--impl reference` times that CPU
-restatement alone, with all host threads.
+Prints one JSON line (rank 0).  `value` is whole-job member-samples/s with the data resident
+in HBM; `e2e` repeats the region through the same public calls with the step inputs copied
+from pinned host memory and the losses and gathered predictions read back; `roofline` covers
+the kernel family with the largest share of the step (per-launch CUDA-event times from the
+library's profiler, `tp_profile_start` / `tp_profile_stop`); `config.checksum` hashes the
+trained pack's gathered validation predictions (equal at every N when sharding does not change
+the arithmetic); `cpu_baseline` and `--impl reference` time the reference's training step
+restated with the reference's own torch ops on the host cores, on a member sample.
+
+Other workloads (`--workload`): `layer` (one packed MLP block forward + backward: 256
+members per GPU over a shared 4096 x 512 bf16 batch), `optimizer`, `metrics`, `inference`,
+`onehot`; each prints its own JSON line.
 """
 
 from __future__ import annotations
@@ -25,6 +30,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -57,6 +63,14 @@ def member_dropout(base: int, n: int) -> np.ndarray:
     return np.array([np.random.default_rng(7_000_001 * (base + i) + 3).uniform(0, 0.5) for i in range(n)], np.float32)
 
 
+def peak_key(clk: dict) -> str:
+    """The bf16 peak that applies to a timed region: the sustained figure when the SM clock ran
+    below 90 % of its maximum there (the power cap held it down), the burst figure otherwise."""
+    if clk.get('sm_mhz') and clk.get('sm_max_mhz') and clk['sm_mhz'] < 0.9 * clk['sm_max_mhz']:
+        return 'bf16_tflops_sustained'
+    return 'bf16_tflops'
+
+
 def load_peaks() -> tuple[dict, str]:
     path = os.path.join(ROOT, 'MEASURED_PEAKS.json')
     if os.path.exists(path):
@@ -68,56 +82,45 @@ def load_peaks() -> tuple[dict, str]:
 # ----------------------------------------------------------------------------- CPU legs
 
 
-def cpu_layer_step(x, w, b, out_f, p, dy, seed, offset):
-    """numpy restatement (oracle) of one forward+backward of the layer."""
-    from oracle import layers as ol
-
-    P = w.shape[0]
-    mv = ol.dropout_mask_values(seed=seed, offset=offset, members=np.arange(P), n_rows=x.shape[0],
-                                n_cols=w.shape[1], p=p, dtype=np.float32)
-    y, pre = ol.block_forward(x, w, b, out_f, mask_values=mv)
-    ol.block_backward(x, w, out_f, pre, dy, mask_values=mv)
-    return y
-
-
 def cpu_sample(members: int, budget_s: float, steps: int | None = None):
-    """Times the CPU restatement on `members` members; returns (member-samples/s, threads, sample)."""
-    rng = np.random.default_rng(0)
-    out_f = member_widths(0, members)
+    """The reference's block forward+backward on the host (`oracle.torch_step.block_step`: padded
+    baddbmm, bernoulli_ dropout, autograd; all host threads) on `members` members of the layer
+    workload; returns (member-samples/s, threads, sample)."""
+    import torch
+
+    from oracle.torch_step import block_step
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    out_f = torch.from_numpy(member_widths(0, members))
     max_out = int(out_f.max())
-    x = rng.standard_normal((ROWS, D_IN)).astype(np.float32)
-    w = (rng.uniform(-1, 1, (members, max_out, D_IN)) / np.sqrt(D_IN)).astype(np.float32)
-    b = (rng.uniform(-1, 1, (members, max_out)) / np.sqrt(D_IN)).astype(np.float32)
-    p = member_dropout(0, members)
-    dy = rng.standard_normal((members, ROWS, max_out)).astype(np.float32)
-    cpu_layer_step(x, w, b, out_f, p, dy, 1, 0)  # warm-up
+    x = torch.randn(ROWS, D_IN, generator=g)
+    w = (torch.rand(members, max_out, D_IN, generator=g) * 2 - 1) / D_IN ** 0.5
+    b = (torch.rand(members, max_out, generator=g) * 2 - 1) / D_IN ** 0.5
+    p = torch.from_numpy(member_dropout(0, members))
+    dy = torch.randn(members, ROWS, max_out, generator=g)
+    block_step(x, w, b, out_f, p, dy)  # warm-up
     n, t0 = 0, time.perf_counter()
     while True:
-        cpu_layer_step(x, w, b, out_f, p, dy, 1, n + 1)
+        block_step(x, w, b, out_f, p, dy)
         n += 1
         el = time.perf_counter() - t0
         if (steps is not None and n >= steps) or (steps is None and el >= budget_s):
             break
-    try:
-        from threadpoolctl import threadpool_info
-
-        threads = max([i.get('num_threads', 1) for i in threadpool_info()] or [1])
-    except Exception:  # pragma: no cover
-        threads = os.cpu_count() or 1
-    sample = f'{members} members x {ROWS} rows x {D_IN} in (out widths {int(out_f.sum())} total), {n} fwd+bwd steps'
-    return members * ROWS * n / el, threads, sample
+    sample = (f'{members} members x {ROWS} rows x {D_IN} in (out widths {int(out_f.sum())} total), {n} fwd+bwd steps '
+              '(torch CPU restatement of the reference block: padded baddbmm, bernoulli_ dropout, autograd, fp32)')
+    return members * ROWS * n / el, torch.get_num_threads(), sample
 
 
 def run_reference(args) -> None:
-    rank = int(os.environ.get('RANK', '0'))
-    if rank != 0:
+    """The reference arm of the layer workload (rank 0 only)."""
+    if int(os.environ.get('RANK', '0')) != 0:
         return
     members = 4
-    vals = []
-    threads = 1
-    sample = ''
     for _ in range(max(args.warmup, 0)):
         cpu_sample(members, 0, steps=1)
+    vals = []
+    threads, sample = 1, ''
     for _ in range(args.steps):
         v, threads, sample = cpu_sample(members, 0, steps=1)
         vals.append(v)
@@ -129,7 +132,7 @@ def run_reference(args) -> None:
         'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic', 'impl': 'reference',
         'config': {'workload': WORKLOAD, 'sample_members': members},
         'cpu_baseline': {'value': value, 'unit': 'member-samples/s', 'cores': threads, 'kind': 'port',
-                         'sample': sample + ' per step (numpy restatement of the reference layer)'},
+                         'sample': sample + ', one per timed step'},
         'e2e': {'value': value, 'unit': 'member-samples/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line), flush=True)
@@ -334,6 +337,7 @@ def run_b200(args) -> None:
     e2e_value = samples / (e2e_ms / 1e3)
 
     peaks, peak_kind = load_peaks()
+    clk = clocks.summary()
     flops = 2.0 * ROWS * D_IN * float(out_f.sum())
     # activation-gradient kernel: reads dy and y and writes g over each member's
     # 64-column strips below out_i, bf16
@@ -345,11 +349,12 @@ def run_b200(args) -> None:
         roof = {'bound': 'hbm', 'achieved': ach, 'peak': peaks['hbm_gbs'], 'unit': 'GB/s'}
     else:
         ach = work[dominant] / (per_phase[dominant] / 1e3) / 1e12
-        roof = {'bound': 'tensor', 'achieved': ach, 'peak': peaks['bf16_tflops_sustained'], 'unit': 'TFLOP/s'}
+        roof = {'bound': 'tensor', 'achieved': ach, 'peak': peaks[peak_key(clk)], 'unit': 'TFLOP/s'}
     roof['frac'] = roof['achieved'] / roof['peak']
     roof['kernel'] = dominant
     roof['traffic'] = TRAFFIC_BYTES_PER_LAUNCH.get(dominant)
-    roof['peak_source'] = f'{peak_kind} ({"sustained" if roof["bound"] == "tensor" else "copy"})'
+    roof['peak_source'] = (f'{peak_kind} (copy)' if roof['bound'] == 'hbm' else
+                           f'{peak_kind} ({peak_key(clk)}: median SM clock {clk["sm_mhz"]} of {clk["sm_max_mhz"]} MHz)')
 
     if rank != 0:
         if world > 1:
@@ -359,8 +364,7 @@ def run_b200(args) -> None:
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         v, threads, sample = cpu_sample(4, args.cpu_seconds)
-        cpu = {'value': v, 'unit': 'member-samples/s', 'cores': threads, 'kind': 'port',
-               'sample': sample + ' (numpy restatement of the reference layer, fp32)'}
+        cpu = {'value': v, 'unit': 'member-samples/s', 'cores': threads, 'kind': 'port', 'sample': sample}
 
     tflops_step = 3 * flops * world / (elapsed_ms / args.steps / 1e3) / 1e12
     line = {
@@ -378,7 +382,7 @@ def run_b200(args) -> None:
         'e2e': {'value': e2e_value, 'unit': 'member-samples/s', 'h2d_bytes_per_step': x.numel() * 2,
                 'd2h_bytes_per_step': db.numel() * 4},
         'gpu_launches': 4 * args.steps,
-        'clocks': clocks.summary(),
+        'clocks': clk,
     }
     print(json.dumps(line), flush=True)
     if world > 1:
@@ -548,73 +552,302 @@ def run_metrics(args) -> None:
         'clocks': clocks.summary()}), flush=True)
 
 
-def run_train(args) -> None:
-    """Training steps of the full-training configuration: binary classification over
-    1 000 000 synthetic rows (100 numerical features N(0, 1), 10 % of rows heavy-tailed
-    Student-t(3); 10 categorical features with cardinalities log-U[2, 1000]; labels
-    Bernoulli(sigmoid(random teacher MLP))); `members` members per GPU with depth U{1..4},
-    width U{128..1024 step 8}, dropout U[0, 0.5], Muon + AdamW, batch 1024, bf16 autocast.
-    One step = batch gather, one-hot encoding, forward, loss, backward and optimizer step of
-    every member; value = member-samples/s (members x 1024 / step time)."""
+# ----------------------------------------------------------------------------- full training
+
+TRAIN_ROWS, VAL_ROWS, N_NUM, N_CAT, BATCH = 1_000_000, 100_000, 100, 10, 1024
+STEPS_PER_EPOCH = -(-TRAIN_ROWS // BATCH)  # 977
+
+
+def train_data(seed: int = 21):
+    """The full-training configuration's synthetic data, identical on every rank: 1 000 000 train
+    and 100 000 validation rows; 100 numerical features N(0, 1), 10 % of rows heavy-tailed
+    (Student-t, 3 degrees of freedom); 10 categorical features with cardinalities log-U[2, 1000];
+    labels Bernoulli(sigmoid(random teacher MLP)).  Drawn on the host from fixed seeds."""
     import torch
 
-    from tabpack_b200.training import PackTrainer
+    cards = train_cards(seed)
+    n = TRAIN_ROWS + VAL_ROWS
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(n, N_NUM, generator=g)
+    heavy = torch.rand(n, generator=g) < 0.1
+    # Student-t(3) = N(0, 1) / sqrt(chi2(3) / 3)
+    z = torch.randn(int(heavy.sum()), N_NUM, generator=g)
+    chi2 = torch.randn(int(heavy.sum()), N_NUM, 3, generator=g).square().sum(-1)
+    x[heavy] = z / torch.sqrt(chi2 / 3)
+    xc = torch.stack([torch.randint(0, c, (n,), generator=g) for c in cards], 1)
+    w1 = torch.randn(N_NUM, 64, generator=g) / N_NUM ** 0.5
+    w2 = torch.randn(64, generator=g) / 8
+    y = (torch.rand(n, generator=g) < torch.sigmoid(torch.relu(x @ w1) @ w2 - 0.5)).to(torch.int64)
+    split = {'train': slice(0, TRAIN_ROWS), 'val': slice(TRAIN_ROWS, n)}
+    return cards, {k: {'x_num': x[s], 'x_cat': xc[s], 'y': y[s]} for k, s in split.items()}
 
-    dev = torch.device('cuda', 0)
-    torch.cuda.set_device(dev)
-    rng = np.random.default_rng(21)
-    N, n_num, batch = 1_000_000, 100, 1024
-    cards = [int(c) for c in np.exp(rng.uniform(np.log(2), np.log(1000), 10)).round()]
-    g = torch.Generator(device=dev).manual_seed(21)
-    x = torch.randn(N, n_num, device=dev, generator=g)
-    heavy = torch.rand(N, device=dev, generator=g) < 0.1
-    t3 = torch.distributions.StudentT(3.0).sample((int(heavy.sum()), n_num)).to(dev)
-    x[heavy] = t3
-    xc = torch.stack([torch.randint(0, c, (N,), device=dev, generator=g) for c in cards], 1)
-    w1 = torch.randn(n_num, 64, device=dev, generator=g) / n_num ** 0.5
-    y = (torch.rand(N, device=dev, generator=g) < torch.sigmoid(torch.relu(x @ w1).sum(1) / 8 - 1)).to(torch.int64)
-    data = {'x_num': x, 'x_cat': xc, 'y': y}
-    P = args.members
-    per = [dict(n_blocks=int(rng.integers(1, 5)), d_block=int(rng.integers(16, 129)) * 8,
-                dropout=float(rng.uniform(0, 0.5))) for _ in range(P)]
-    model = dict(n_numerical_features=n_num, categorical_cardinalities=cards, d_out=1, max_d_block=1024,
-                 max_n_blocks=4)
+
+def train_cards(seed: int = 21) -> list[int]:
+    """Cardinalities of the 10 categorical features, log-U[2, 1000]."""
+    rng = np.random.default_rng(seed)
+    return [int(c) for c in np.exp(rng.uniform(np.log(2), np.log(1000), N_CAT)).round()]
+
+
+def train_members(n: int, seed: int = 21) -> list[dict]:
+    """Per-member hyperparameters of the full-training pack: depth U{1..4}, width U{128..1024
+    step 8}, dropout U[0, 0.5]."""
+    rng = np.random.default_rng(seed + 1)
+    return [dict(n_blocks=int(rng.integers(1, 5)), d_block=int(rng.integers(16, 129)) * 8,
+                 dropout=float(rng.uniform(0, 0.5))) for _ in range(n)]
+
+
+def train_work(per: list[dict], d_in: int, batch: int = BATCH) -> dict[str, float]:
+    """Algorithmic FLOPs per training step by kernel family (ragged shapes, active blocks only):
+    forward / dgrad / wgrad GEMMs of the blocks and the 1-wide head (the first layer takes no
+    input gradient), and the Newton-Schulz GEMMs of Muon (5 iterations of 4 r^2 c + 2 r^3 per
+    block weight, r = min and c = max of its shape)."""
+    fwd = dgrad = wgrad = ns = 0.0
+    for pm in per:
+        w, nb = pm['d_block'], pm['n_blocks']
+        mm = d_in * w + (nb - 1) * w * w + w
+        fwd += 2.0 * batch * mm
+        wgrad += 2.0 * batch * mm
+        dgrad += 2.0 * batch * ((nb - 1) * w * w + w)
+        for j in range(nb):
+            r, c = min(w, d_in if j == 0 else w), max(w, d_in if j == 0 else w)
+            ns += 5.0 * (4.0 * r * r * c + 2.0 * r ** 3)
+    return {'fwd': fwd, 'dgrad': dgrad, 'wgrad': wgrad, 'newton_schulz': ns}
+
+
+def member_cost(pm: dict, d_in: int) -> float:
+    """A member's FLOPs per training step (the sharding weight)."""
+    return sum(train_work([pm], d_in).values())
+
+
+def run_train(args) -> None:
+    """Full TabPack training of the full-training configuration, members sharded over the GPUs.
+
+    The global pack (512 members by default) is split into contiguous member ranges balanced by
+    FLOPs per step (strong scaling: the pack is fixed, each rank trains its share).  The timed
+    region is an epoch scaled down to K steps: K training steps (batch gather, one-hot first-layer
+    input, forward, BCE loss, backward, Muon + AdamW) over the first K x 1024 training rows, then
+    the epoch end over the first K / 977 of the validation rows -- every member's predictions,
+    all-gathered over NCCL, and a greedy ensemble built from them -- so training and evaluation
+    stand in the same ratio as in a full epoch.  value = member-samples/s of the whole job."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from tabpack_b200 import ops
+    from tabpack_b200.training import OnlineEnsemble, PackTrainer
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        dist.init_process_group('nccl', device_id=dev, timeout=datetime.timedelta(seconds=300))
+    P, K, W = args.members, args.steps, args.warmup
+    cards, data = train_data()
+    d_in = N_NUM + sum(cards)
+    per = train_members(P)
     if args.embeddings == 'cosine':
-        # the reference's default model: cosine numerical embeddings of per-member size
-        from tabpack_b200.nn import CosineEmbeddingsPack
-
-        model['numerical_embeddings'] = {'type': CosineEmbeddingsPack, 'max_d_embedding': 32}
+        rng = np.random.default_rng(23)
         for pm in per:
             pm['numerical_embeddings'] = {'d_embedding': int(rng.integers(8, 33)),
                                           'init_scale': float(np.exp(rng.uniform(np.log(0.01), np.log(1.0))))}
+    model = dict(n_numerical_features=N_NUM, categorical_cardinalities=cards, d_out=1, max_d_block=1024,
+                 max_n_blocks=4)
+    if args.embeddings == 'cosine':
+        from tabpack_b200.nn import CosineEmbeddingsPack
+
+        model['numerical_embeddings'] = {'type': CosineEmbeddingsPack, 'max_d_embedding': 32}
     trainer = PackTrainer(n_members=P, model=model, per_member_model=per,
-                          optimizer=dict(type='muon', adamw_lr=1e-3, weight_decay=1e-5, muon_lr=2e-2),
-                          loss='bce', seed=0, device=dev, autocast_bf16=True, member_range=(0, P))
-    steps = args.steps
-    # backward on the calling thread (kernels are asynchronous either way), so that the NVTX
-    # range below also holds the backward launches
-    torch.autograd.set_multithreading_enabled(False)
-    trainer.fit_epoch({k: v[: batch * args.warmup] for k, v in data.items()}, batch_size=batch, epoch=0)
-    torch.cuda.synchronize()
-    sub = {k: v[: batch * steps] for k, v in data.items()}
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(0) as clocks:
-        torch.cuda.nvtx.range_push('timed')  # lets a profiler keep only the timed steps
-        e0.record()
-        loss = trainer.fit_epoch(sub, batch_size=batch, epoch=1)
-        e1.record()
-        torch.cuda.nvtx.range_pop()
+                          optimizer=dict(type='muon', adamw_lr=1e-3, weight_decay=1e-5, muon_lr=2e-2), loss='bce',
+                          seed=0, device=dev, autocast_bf16=True, cost=[member_cost(pm, d_in) for pm in per])
+    val_rows = min(VAL_ROWS, (math.ceil(VAL_ROWS * K / STEPS_PER_EPOCH) + 255) // 256 * 256)
+    host = {'train': {k: v[: K * BATCH] for k, v in data['train'].items()},
+            'val': {k: v[:val_rows] for k, v in data['val'].items()}}
+    dev_data = {s: {k: v.to(dev) for k, v in d.items()} for s, d in host.items()}
+    warm = {k: v.to(dev) for k, v in (
+        (k, data['train'][k][K * BATCH: (K + max(W, 1)) * BATCH]) for k in data['train'])}
+    del data
+
+    def epoch(train, val, ep, on_step=None):
+        loss = trainer.fit_epoch(train, batch_size=BATCH, epoch=ep, on_step=on_step)
+        preds = trainer.predict(val)  # (P_total, rows), all-gathered over NCCL
+        ens = OnlineEnsemble(trainer._score(val['y']))
+        ens.update(lambda key: preds[key[0]], [], [(g, K) for g in trainer.gathered_ids])
+        return loss, preds, ens
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
-    print(json.dumps({
-        'metric': 'member-samples/sec train (full TabPack training step)', 'value': P * batch / (ms / 1e3),
-        'unit': 'member-samples/s', 'n_gpus': 1, 'steps': steps, 'warmup': args.warmup, 'ms_per_step': ms,
-        'higher_is_better': True, 'dtype': 'bf16', 'data': 'synthetic',
-        'config': {'workload': f'{P} members, depth U{{1..4}}, width U{{128..1024}}, 100 numerical + 10 categorical '
-                               f'(sum of cardinalities {sum(cards)}), batch 1024, Muon + AdamW, bf16'
-                               + (', cosine numerical embeddings d U{8..32}' if args.embeddings == 'cosine' else ''),
+
+    torch.autograd.set_multithreading_enabled(False)  # backward launches from the calling thread
+    epoch(warm, dev_data['val'], 0)  # warm-up: W steps and one epoch end
+    barrier()
+    stream = torch.cuda.current_stream(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    with ClockSampler(local) as clocks:
+        ev[0].record(stream)
+        loss = trainer.fit_epoch(dev_data['train'], batch_size=BATCH, epoch=1)
+        ev[1].record(stream)
+        preds = trainer.predict(dev_data['val'])
+        ens = OnlineEnsemble(trainer._score(dev_data['val']['y']))
+        ens.update(lambda key: preds[key[0]], [], [(g, K) for g in trainer.gathered_ids])
+        ev[2].record(stream)
+        barrier()
+    region_ms, train_ms = ev[0].elapsed_time(ev[2]), ev[0].elapsed_time(ev[1])
+
+    # end to end through the same public calls: the step inputs (the epoch's training and
+    # validation rows) copied from pinned host memory inside the region, each step's
+    # per-member losses and the gathered validation predictions read back to the host
+    pinned = {s: {k: v.pin_memory() for k, v in d.items()} for s, d in host.items()}
+    loss_host = torch.empty(K, trainer.hi - trainer.lo).pin_memory()
+    pred_host = torch.empty(P, val_rows).pin_memory()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    up = {s: {k: v.to(dev, non_blocking=True) for k, v in d.items()} for s, d in pinned.items()}
+    _, preds_e2e, _ = epoch(up['train'], up['val'], 2,
+                            on_step=lambda i, l: loss_host[i].copy_(l, non_blocking=True))
+    pred_host.copy_(preds_e2e, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    # per-family kernel time over one more scaled epoch, launch by launch (CUDA events)
+    with ops.KernelTimes() as kt:
+        epoch(dev_data['train'], dev_data['val'], 3)
+    barrier()
+
+    t = torch.tensor([region_ms, train_ms, e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    region_ms, train_ms, e2e_ms = (float(v) for v in t)
+    # shard-invariance checksum: the trained pack's gathered validation predictions
+    final = trainer.predict(dev_data['val']).float().cpu().numpy()
+    import hashlib
+
+    checksum = {'sha256_16': hashlib.sha256(final.tobytes()).hexdigest()[:16], 'sum': float(final.astype(np.float64).sum())}
+    local_work = train_work(per[trainer.lo: trainer.hi], d_in)
+    fam_ms = {k: kt.ms[k] / K for k in kt.ms if kt.launches[k]}
+    fam_ms['newton_schulz'] = fam_ms.pop('newton_schulz_gram', 0.0) + fam_ms.pop('newton_schulz_update', 0.0)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks, peak_kind = load_peaks()
+    clk = clocks.summary()
+    sustained = peak_key(clk) == 'bf16_tflops_sustained'
+    peak = peaks[peak_key(clk)]
+    gemm = {}
+    for fam in ('fwd', 'dgrad', 'wgrad', 'newton_schulz'):
+        if fam_ms.get(fam):
+            ach = local_work[fam] / (fam_ms[fam] / 1e3) / 1e12
+            gemm[fam] = {'ms_per_step': fam_ms[fam], 'tflop_per_step': local_work[fam] / 1e12, 'tflops': ach,
+                         'frac': ach / peak}
+    dominant = max(gemm, key=lambda f: gemm[f]['ms_per_step'])
+    roof = {'bound': 'tensor', 'achieved': gemm[dominant]['tflops'], 'peak': peak, 'unit': 'TFLOP/s',
+            'frac': gemm[dominant]['frac'], 'kernel': dominant,
+            'traffic': TRAIN_TRAFFIC_BYTES_PER_STEP.get(dominant),
+            'peak_source': f'{peak_kind} ({"sustained" if sustained else "burst"}: median SM clock '
+                           f'{clk["sm_mhz"]} of {clk["sm_max_mhz"]} MHz in the region)'}
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu, _ = train_cpu_sample(cards, per, budget_s=args.cpu_seconds)
+    samples = P * BATCH * K
+    launches = sum(kt.launches.values())
+    line = {
+        'metric': 'member-samples/sec train (full TabPack training, Muon + AdamW)', 'value': samples / (region_ms / 1e3),
+        'unit': 'member-samples/s', 'n_gpus': world, 'steps': K, 'warmup': W, 'ms_per_step': region_ms / K,
+        'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
+        'config': {'workload': f'full TabPack training: {P} members (depth U{{1..4}}, width U{{128..1024}}, '
+                               f'dropout U[0,0.5]), {N_NUM} numerical + {N_CAT} categorical features '
+                               f'({sum(cards)} one-hot columns), batch {BATCH}, BCE, Muon + AdamW, bf16; '
+                               f'timed: {K} steps + the epoch end over {val_rows} validation rows (all-gather + '
+                               f'greedy ensemble)' + (', cosine numerical embeddings' if args.embeddings == 'cosine'
+                                                      else ''),
+                   'members': P, 'members_per_rank': [b - a for a, b in trainer.ranges],
+                   'parallelism': f'member-sharded x{world} (ranges balanced by FLOPs per step)',
+                   'train_ms_per_step': train_ms / K, 'epoch_end_ms': region_ms - train_ms,
+                   'l2': 'weights and optimizer state exceed L2 (about 40 GB at 512 members)',
+                   'per_kernel_ms_per_step': fam_ms, 'gemm': gemm, 'checksum': checksum,
                    'mean_train_loss': float(loss.mean())},
-        'clocks': clocks.summary()}), flush=True)
+        'roofline': roof,
+        'cpu_baseline': cpu,
+        'e2e': {'value': samples / (e2e_ms / 1e3), 'unit': 'member-samples/s',
+                'h2d_bytes_per_step': sum(v.numel() * v.element_size() for d in host.values() for v in d.values()) / K,
+                'd2h_bytes_per_step': loss_host.numel() * 4 / K + pred_host.numel() * 4 / K},
+        'gpu_launches': launches,
+        'clocks': clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# DRAM bytes (read + write) per training step of the dominant kernel family, from the ncu
+# capture of the training workload's launches (64-member case scaled to 512 members).
+TRAIN_TRAFFIC_BYTES_PER_STEP: dict[str, float | None] = {}
+
+
+def train_cpu_sample(cards: list[int], per: list[dict], *, budget_s: float, steps: int | None = None,
+                     members: int = 16):
+    """The reference's training step on the host (`oracle.torch_step`, all host threads) on the
+    first `members` members of the pack; returns the cpu_baseline dict and the per-step values."""
+    import torch
+
+    from oracle.torch_step import TrainingStep, sample_batch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    sub = per[:members]
+    step = TrainingStep(n_num=N_NUM, cards=cards, widths=[p['d_block'] for p in sub],
+                        depths=[p['n_blocks'] for p in sub], dropout=[p['dropout'] for p in sub])
+    rng = np.random.default_rng(5)
+    g = torch.Generator().manual_seed(5)
+    n = 65536
+    x = torch.randn(n, N_NUM, generator=g)
+    xc = torch.stack([torch.randint(0, c, (n,), generator=g) for c in cards], 1)
+    y = (torch.rand(n, generator=g) < 0.3).to(torch.int64)
+    step.step(*sample_batch(rng, x, xc, y, members, BATCH))  # warm-up
+    vals, t_all = [], time.perf_counter()
+    while True:
+        b = sample_batch(rng, x, xc, y, members, BATCH)
+        t0 = time.perf_counter()
+        step.step(*b)
+        vals.append(members * BATCH / (time.perf_counter() - t0))
+        if (steps is not None and len(vals) >= steps) or (steps is None and time.perf_counter() - t_all >= budget_s):
+            break
+    return {'value': statistics.median(vals), 'unit': 'member-samples/s', 'cores': torch.get_num_threads(),
+            'kind': 'port', 'sample': f'the first {members} members of the pack, batch {BATCH}, {len(vals)} training '
+                                      'steps (torch CPU restatement of the reference step: padded baddbmm, '
+                                      'bernoulli_ dropout, BCE, autograd, Muon with bf16 Newton-Schulz + AdamW, '
+                                      'bf16 autocast)'}, vals
+
+
+def run_train_reference(args) -> None:
+    """The reference arm of the full-training workload: its CPU step on the host cores (rank 0
+    only; other ranks exit), K timed steps of a 16-member sample after W warm-up steps."""
+    if int(os.environ.get('RANK', '0')) != 0:
+        return
+    cards = train_cards()
+    per = train_members(args.members)
+    cpu, vals = train_cpu_sample(cards, per, budget_s=0.0, steps=args.warmup + args.steps)
+    vals = vals[args.warmup:]
+    value = statistics.median(vals)
+    cpu['value'] = value
+    cpu['sample'] = cpu['sample'].replace(f'{args.warmup + args.steps} training steps',
+                                          f'{args.steps} timed training steps after {args.warmup}')
+    line = {
+        'metric': 'member-samples/sec train (full TabPack training, Muon + AdamW)', 'value': value,
+        'unit': 'member-samples/s', 'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+        'ms_per_step': 16 * BATCH / value * 1e3, 'higher_is_better': True, 'scaling': 'strong',
+        'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic', 'impl': 'reference',
+        'config': {'workload': 'full TabPack training (the pack of the default workload), reference step on the '
+                               'host cores', 'sample_members': 16},
+        'cpu_baseline': cpu,
+        'e2e': {'value': value, 'unit': 'member-samples/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
 
 
 def run_inference(args) -> None:
@@ -800,43 +1033,42 @@ def main() -> None:
     global MEMBERS
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=300)
-    ap.add_argument('--warmup', type=int, default=10)
+    ap.add_argument('--steps', type=int, default=None, help='timed steps (default 20; 300 for the layer workload)')
+    ap.add_argument('--warmup', type=int, default=None, help='warm-up steps (default 5; 10 for the layer workload)')
     ap.add_argument('--impl', choices=['b200', 'reference'], default='b200')
-    ap.add_argument('--cpu-seconds', type=float, default=10.0)
+    ap.add_argument('--cpu-seconds', type=float, default=15.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--members', type=int, default=None,
-                    help='members per GPU (default 256 for the layer workload, 1024 for the optimizer)')
-    ap.add_argument('--workload', choices=['layer', 'optimizer', 'metrics', 'train', 'inference', 'onehot'],
-                    default='layer',
-                    help='layer: the packed-block fwd+bwd benchmark (default); optimizer: grouped Muon step; '
-                         'metrics: validation metrics, ROC AUC and greedy selection')
+                    help='members: of the whole pack for train (512) and inference (1024), per GPU for the layer '
+                         'workload (256), of the optimizer (1024), metrics (512) and onehot (512) workloads')
+    ap.add_argument('--workload', choices=['train', 'layer', 'optimizer', 'metrics', 'inference', 'onehot'],
+                    default='train',
+                    help='train: full TabPack training steps and the epoch end, members sharded over the GPUs '
+                         '(default); layer: one packed MLP block forward+backward; optimizer: grouped Muon step; '
+                         'metrics: validation metrics, ROC AUC and greedy selection; inference: packed predictor; '
+                         'onehot: the one-hot first layer piece by piece')
     ap.add_argument('--embeddings', choices=['none', 'cosine'], default='none',
                     help='train workload: numerical features raw or through cosine embeddings')
     args = ap.parse_args()
     if args.members is None:
         args.members = {'optimizer': 1024, 'metrics': 512, 'train': 512, 'inference': 1024,
                         'onehot': 512}.get(args.workload, MEMBERS)
+    if args.steps is None:
+        args.steps = 300 if args.workload == 'layer' else 20
+    if args.warmup is None:
+        args.warmup = 10 if args.workload == 'layer' else 5
     MEMBERS = args.members
-    if args.workload == 'optimizer':
-        run_optimizer(args)
-        return
-    if args.workload == 'metrics':
-        run_metrics(args)
-        return
-    if args.workload == 'train':
-        run_train(args)
-        return
-    if args.workload == 'inference':
-        run_inference(args)
-        return
-    if args.workload == 'onehot':
-        run_onehot(args)
-        return
     if args.impl == 'reference':
-        run_reference(args)
-    else:
-        run_b200(args)
+        if args.workload == 'train':
+            run_train_reference(args)
+        elif args.workload == 'layer':
+            run_reference(args)
+        elif int(os.environ.get('RANK', '0')) == 0:
+            print(json.dumps({'impl': 'reference', 'unavailable': f'no CPU reference arm for the {args.workload} '
+                                                                  'workload (train and layer have one)'}), flush=True)
+        return
+    {'train': run_train, 'layer': run_b200, 'optimizer': run_optimizer, 'metrics': run_metrics,
+     'inference': run_inference, 'onehot': run_onehot}[args.workload](args)
 
 
 if __name__ == '__main__':

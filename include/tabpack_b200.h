@@ -122,10 +122,50 @@ int tp_linear_backward(const tp_linear_grad_args* a, void* stream);
  *  - `g_ready` is ignored: the activation gradient is always recomputed. */
 int tp_linear_backward_noalloc(const tp_linear_grad_args* a, void* stream);
 
+/* No counterpart in the reference: per-launch timing of this library's kernels.
+ *
+ * tp_profile_start(capacity) creates 2 * capacity CUDA events on the current device and
+ * brackets each following kernel launch (for the GEMMs and the Muon kernels) or call (for
+ * the other entry points) with two of them, until `capacity` launches are recorded (later
+ * ones are counted in `dropped`).  tp_profile_stop waits for the recorded events, writes the
+ * summed milliseconds and launch counts per family into ms / launches (n_kinds entries,
+ * indexed by TP_PROF_*), destroys the events and turns the recording off.  Off by default,
+ * where it costs one atomic load per launch; start / stop must not overlap other calls into
+ * the library. */
+#define TP_PROF_FWD 0              /* tensor-core forward GEMMs (all forward variants) */
+#define TP_PROF_DGRAD 1            /* tensor-core dX GEMMs */
+#define TP_PROF_WGRAD 2            /* tensor-core dW GEMMs */
+#define TP_PROF_NS 3               /* Newton-Schulz A = X X^T and B = b A + c A^2 */
+#define TP_PROF_NS_BMN 4           /* Newton-Schulz X <- a X + B X */
+#define TP_PROF_GEMM_F32 5         /* fp32 CUDA-core GEMMs */
+#define TP_PROF_ACT_BACKWARD 6     /* activation / bias gradient */
+#define TP_PROF_MUON_ELEMENTWISE 7 /* Muon momentum, packing, norm, normalisation, update */
+#define TP_PROF_ADAMW 8
+#define TP_PROF_WEIGHT_CAST 9
+#define TP_PROF_INPUT 10           /* first-layer input build (tp_tabpack_input) */
+#define TP_PROF_EMBEDDING 11       /* cosine embeddings */
+#define TP_PROF_ONEHOT 12          /* one-hot sort, gather and weight gradient */
+#define TP_PROF_METRIC 13
+#define TP_PROF_GREEDY 14
+#define TP_PROF_ROC_AUC 15
+#define TP_PROF_OTHER 16
+#define TP_PROF_KINDS 17
+int tp_profile_start(int32_t capacity);
+int tp_profile_stop(double* ms, int64_t* launches, int32_t n_kinds, int32_t* dropped);
+
 /* Test hook: the Philox keep mask of the dropout above, (P, B, cols) uint8. */
 int tp_dropout_mask(uint64_t seed, uint32_t offset, uint32_t member_base,
                     const float* dropout_p, int32_t P, int32_t B, int32_t cols,
                     uint8_t* mask, void* stream);
+
+/* Test hook: the Muon normalisation's quotient (x * (1/den) with one fused correction,
+ * Markstein's method) against CUDA's correctly rounded division, exhaustively over bf16
+ * operands: divisors with bit patterns den_first .. den_first + den_count - 1 (positive finite),
+ * every finite bf16 dividend with |x| <= 2 den.  Adds to counts (device, 4 x uint64): fp32
+ * quotients differing in any bit, quotients differing after rounding to bf16 (what the
+ * normalisation stores), pairs checked, and the fp32 differences where the exact quotient or
+ * the reciprocal is subnormal. */
+int tp_quotient_check(int32_t den_first, int32_t den_count, unsigned long long* counts, void* stream);
 
 /* One tensor of a grouped optimizer step.  Element e of the tensor belongs to
  * member e / inner. */

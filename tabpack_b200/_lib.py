@@ -140,6 +140,10 @@ class GreedyArgs(ctypes.Structure):
     ]
 
 
+# kernel families of tp_profile_stop, in TP_PROF_* order
+TP_PROF_KINDS = ('fwd', 'dgrad', 'wgrad', 'newton_schulz_gram', 'newton_schulz_update', 'gemm_f32', 'act_backward',
+                 'muon_elementwise', 'adamw', 'weight_cast', 'input', 'embedding', 'onehot', 'metric', 'greedy',
+                 'roc_auc', 'other')
 TP_METRIC = {'mse': 0, 'mae': 1, 'accuracy': 2, 'bce': 3, 'ce': 4, 'accuracy_argmax': 5, 'r2': 6}
 
 
@@ -148,6 +152,10 @@ SIGNATURES = {
     'tp_linear_forward': (ctypes.c_int, [ctypes.POINTER(LinearArgs), ctypes.c_void_p]),
     'tp_linear_backward': (ctypes.c_int, [ctypes.POINTER(LinearGradArgs), ctypes.c_void_p]),
     'tp_linear_backward_noalloc': (ctypes.c_int, [ctypes.POINTER(LinearGradArgs), ctypes.c_void_p]),
+    'tp_profile_start': (ctypes.c_int, [ctypes.c_int32]),
+    'tp_profile_stop': (ctypes.c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64), ctypes.c_int32,
+                                       ctypes.POINTER(ctypes.c_int32)]),
+    'tp_quotient_check': (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]),
     'tp_dropout_mask': (ctypes.c_int, [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
                                        ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
                                        ctypes.c_void_p]),

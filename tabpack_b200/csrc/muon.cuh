@@ -194,6 +194,57 @@ __global__ void __launch_bounds__(256) muon_norm_kernel(MuonArgs a, int tiles_x)
 // on [0, R_s-tile) x [0, C_s-tile) around it (the Newton-Schulz GEMMs read those pads
 // along K).  Grid: (ceil(C_s / 256), ceil(R_s / 32), P), 256 threads; a warp covers rows
 // w, w + 8, w + 16, w + 24 of the block's 32, a lane 8 columns (16 bytes) of each.
+// x / den from rcp = 1 / den (correctly rounded) with one fused correction step: q = x * rcp,
+// then q + (x - q den) * rcp.  Markstein's method (P. Markstein, "Computation of elementary
+// functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): the
+// residual x - q den is exact in one FMA, and the corrected fp32 quotient is within one ulp of
+// x / den (it differs from the correctly rounded one for about 0.24 % of bf16 operand pairs).
+// The normalisation stores the quotient in bf16, and there the results equal bf16(x / den) bit
+// for bit: `tp_quotient_check` compares them with CUDA's correctly rounded division for every
+// bf16 operand pair the normalisation can see.
+__device__ __forceinline__ float quotient_from_reciprocal(float x, float den, float rcp) {
+  const float q = x * rcp;
+  // a zero dividend keeps its sign, as in x / den (the correction would add +0 to -0)
+  return x == 0.0f ? x : fmaf(fmaf(-q, den, x), rcp, q);
+}
+
+// Exhaustive check of quotient_from_reciprocal against __fdiv_rn: block (bx, by) takes the
+// positive bf16 divisor with bit pattern den_first + by and a stride of the 65536 bf16
+// dividend patterns; pairs with a non-finite dividend or |x| > 2 den (outside what the
+// normalisation divides: an element by its matrix's norm) are skipped.  counts[0] += fp32
+// results that differ in any bit, counts[1] += results that differ after rounding to bf16,
+// counts[2] += pairs checked, counts[3] += fp32 differences where the exact quotient or the
+// reciprocal is subnormal.
+__global__ void __launch_bounds__(256) quotient_check_kernel(int den_first, unsigned long long* counts) {
+  const unsigned short dbits = (unsigned short)(den_first + blockIdx.y);
+  const float den = __uint_as_float((unsigned)dbits << 16);
+  const float rcp = 1.0f / den;
+  unsigned long long m32 = 0, m16 = 0, n = 0, sub = 0;
+  for (unsigned xb = blockIdx.x * blockDim.x + threadIdx.x; xb < 65536u; xb += gridDim.x * blockDim.x) {
+    const float x = __uint_as_float(xb << 16);
+    if (!isfinite(x) || fabsf(x) > 2.0f * den) continue;
+    const float a = quotient_from_reciprocal(x, den, rcp);
+    const float b = __fdiv_rn(x, den);
+    m32 += __float_as_uint(a) != __float_as_uint(b);
+    sub += (__float_as_uint(a) != __float_as_uint(b)) && (fabsf(b) < 1.17549435e-38f || fabsf(rcp) < 1.17549435e-38f);
+    m16 += __bfloat16_as_ushort(__float2bfloat16_rn(a)) != __bfloat16_as_ushort(__float2bfloat16_rn(b));
+    ++n;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    m32 += __shfl_xor_sync(0xffffffffu, m32, o);
+    m16 += __shfl_xor_sync(0xffffffffu, m16, o);
+    n += __shfl_xor_sync(0xffffffffu, n, o);
+    sub += __shfl_xor_sync(0xffffffffu, sub, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    if (m32) atomicAdd(counts + 0, m32);
+    if (m16) atomicAdd(counts + 1, m16);
+    atomicAdd(counts + 2, n);
+    if (sub) atomicAdd(counts + 3, sub);
+  }
+}
+
 __global__ void __launch_bounds__(256) muon_normalize_kernel(MuonArgs a, int row_pad, int col_pad) {
   const int mem = blockIdx.z;
   const int r = a.rows[mem], c = a.cols[mem];
@@ -206,9 +257,7 @@ __global__ void __launch_bounds__(256) muon_normalize_kernel(MuonArgs a, int row
   if (nrm2 == 0.0f) return;  // all-zero update: Newton-Schulz is skipped for this member
   const float nrm = __bfloat162float(__float2bfloat16_rn(sqrtf(nrm2)));
   const float den = __bfloat162float(__float2bfloat16_rn(nrm + 1e-7f));
-  // x / den per element from one division per thread: q = x * (1 / den) and one correction
-  // step q + (x - q den) / den with fused multiply-adds (Markstein's method for a correctly
-  // rounded quotient from the correctly rounded reciprocal)
+  // x / den per element from one division per thread (quotient_from_reciprocal)
   const float rcp = 1.0f / den;
   uint4 u[4];
 #pragma unroll
@@ -226,10 +275,7 @@ __global__ void __launch_bounds__(256) muon_normalize_kernel(MuonArgs a, int row
 #pragma unroll
       for (int e = 0; e < 8; ++e)
         if (col + e < c) {
-          const float xv = __bfloat162float(h[e]);
-          float q = xv * rcp;
-          q = fmaf(fmaf(-q, den, xv), rcp, q);
-          h[e] = __float2bfloat16_rn(q);
+          h[e] = __float2bfloat16_rn(quotient_from_reciprocal(__bfloat162float(h[e]), den, rcp));
         } else {
           h[e] = __float2bfloat16_rn(0.0f);
         }

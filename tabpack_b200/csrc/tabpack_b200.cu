@@ -9,7 +9,9 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <atomic>
 #include <mutex>
+#include <vector>
 #include <string>
 
 #include "elementwise.cuh"
@@ -45,6 +47,43 @@ int cuda_fail(cudaError_t e, const char* what) {
     cudaError_t e_ = (expr);                        \
     if (e_ != cudaSuccess) return cuda_fail(e_, #expr); \
   } while (0)
+
+// ---- optional per-launch timing (tp_profile_start / tp_profile_stop) -----------------
+// Off by default (one relaxed atomic load per launch).  When on, each kernel launch (or, for
+// entry points without a GEMM inside, each call) is bracketed by two CUDA events taken from a
+// pool that tp_profile_start creates on the current device; tp_profile_stop waits for them and
+// adds up the elapsed time per kernel family.
+std::atomic<int> g_prof_on{0};
+std::mutex g_prof_mu;
+std::vector<cudaEvent_t> g_prof_events;  // two per slot
+std::vector<int> g_prof_kind;            // family of each slot
+int g_prof_used = 0;
+int g_prof_dropped = 0;
+
+struct ProfScope {
+  cudaStream_t st;
+  int slot = -1;
+  ProfScope(int kind, cudaStream_t s) : st(s) {
+    if (!g_prof_on.load(std::memory_order_relaxed)) return;
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (g_prof_used >= (int)g_prof_kind.size()) {
+      ++g_prof_dropped;
+      return;
+    }
+    slot = g_prof_used++;
+    g_prof_kind[slot] = kind;
+    cudaEventRecord(g_prof_events[2 * slot], st);
+  }
+  ~ProfScope() {
+    if (slot >= 0) cudaEventRecord(g_prof_events[2 * slot + 1], st);
+  }
+  ProfScope(const ProfScope&) = delete;
+  ProfScope& operator=(const ProfScope&) = delete;
+};
+
+#define TP_PROF_CAT2(a, b) a##b
+#define TP_PROF_CAT(a, b) TP_PROF_CAT2(a, b)
+#define TP_PROF(kind, stream) ProfScope TP_PROF_CAT(prof_scope_, __LINE__)((kind), (stream))
 
 struct DeviceInfo {
   int sms = 0;
@@ -211,6 +250,12 @@ int launch_sm100(const LinearProblem& pr_in, const CUtensorMap& a, const CUtenso
     }
   }
   cfg.gridDim = dim3(Cfg::PAIR ? 2 * grid : grid);
+  constexpr int kind = (MODE == MODE_DGRAD) ? TP_PROF_DGRAD
+                       : (MODE == MODE_WGRAD || MODE == MODE_WGRAD_T) ? TP_PROF_WGRAD
+                       : (MODE == MODE_NS) ? TP_PROF_NS
+                       : (MODE == MODE_NS_BMN) ? TP_PROF_NS_BMN
+                                               : TP_PROF_FWD;
+  TP_PROF(kind, st);
   TP_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a, b, pr));
   return TP_OK;
 }
@@ -225,6 +270,7 @@ int launch_simt(LinearProblem pr, cudaStream_t st) {
   const long long total = (long long)pr.P * pr.m_tiles * pr.n_tiles;
   if (total > 0x7FFFFFFFLL) return fail(TP_EINVAL, "too many tiles");
   if (total == 0) return TP_OK;
+  TP_PROF(TP_PROF_GEMM_F32, st);
   linear_gemm_simt<T, MODE><<<(unsigned)total, 256, 0, st>>>(pr);
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;
@@ -383,6 +429,58 @@ int tp_linear_forward(const tp_linear_args* a, void* stream) {
   return linear_forward_impl(a, nullptr, 0, stream);
 }
 
+int tp_profile_start(int32_t capacity) {
+  if (capacity <= 0 || capacity > (1 << 20)) return fail(TP_EINVAL, "capacity must be in 1 .. 2^20 launches");
+  if (g_prof_on.load()) return fail(TP_EINVAL, "profiling is already on");
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  g_prof_events.assign(2 * (size_t)capacity, nullptr);
+  for (auto& e : g_prof_events) {
+    const cudaError_t err = cudaEventCreate(&e);
+    if (err != cudaSuccess) {
+      for (auto& f : g_prof_events)
+        if (f) cudaEventDestroy(f);
+      g_prof_events.clear();
+      return cuda_fail(err, "cudaEventCreate");
+    }
+  }
+  g_prof_kind.assign((size_t)capacity, 0);
+  g_prof_used = 0;
+  g_prof_dropped = 0;
+  g_prof_on.store(1);
+  return TP_OK;
+}
+
+int tp_profile_stop(double* ms, int64_t* launches, int32_t n_kinds, int32_t* dropped) {
+  if (!g_prof_on.load()) return fail(TP_EINVAL, "profiling is not on");
+  g_prof_on.store(0);
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  int rc = TP_OK;
+  for (int k = 0; k < n_kinds; ++k) {
+    if (ms) ms[k] = 0.0;
+    if (launches) launches[k] = 0;
+  }
+  for (int i = 0; i < g_prof_used && rc == TP_OK; ++i) {
+    float t = 0.0f;
+    cudaError_t err = cudaEventSynchronize(g_prof_events[2 * i + 1]);
+    if (err == cudaSuccess) err = cudaEventElapsedTime(&t, g_prof_events[2 * i], g_prof_events[2 * i + 1]);
+    if (err != cudaSuccess) {
+      rc = cuda_fail(err, "reading a profiling event");
+      break;
+    }
+    const int k = g_prof_kind[i];
+    if (k >= 0 && k < n_kinds) {
+      if (ms) ms[k] += t;
+      if (launches) ++launches[k];
+    }
+  }
+  if (dropped) *dropped = g_prof_dropped;
+  for (auto& e : g_prof_events) cudaEventDestroy(e);
+  g_prof_events.clear();
+  g_prof_kind.clear();
+  g_prof_used = 0;
+  return rc;
+}
+
 }  // extern "C"
 
 namespace tp {
@@ -485,6 +583,7 @@ int linear_backward_impl(const tp_linear_grad_args* ga, int dw_ld_in, void* stre
     aa.db_cols = ga->db_cols > 0 ? ga->db_cols : a->max_out;
     dim3 grid((a->max_out + 63) / 64, a->P);
     const bool vec = (a->max_out % 8) == 0 && aligned16(ga->dy) && aligned16(aa.y) && (!aa.g || aligned16(aa.g));
+    TP_PROF(TP_PROF_ACT_BACKWARD, st);
     if (bf16) {
       if (vec) act_backward_kernel<__nv_bfloat16, true><<<grid, 256, 0, st>>>(aa);
       else act_backward_kernel<__nv_bfloat16, false><<<grid, 256, 0, st>>>(aa);
@@ -665,15 +764,16 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
   void* Bm = ws + L.off_b;
   m.x = reinterpret_cast<__nv_bfloat16*>(x0);
 
-  muon_geometry_kernel<<<(a->P + 255) / 256, 256, 0, st>>>(m);
-  TP_CUDA_TRY(cudaGetLastError());
   if (a->P > 65535) return fail(TP_EINVAL, "at most 65535 members per Muon call");
   dim3 tiles((a->max_in + MUON_TN - 1) / MUON_TN, (a->max_out + MUON_TM - 1) / MUON_TM, a->P);
-  muon_prologue_kernel<<<tiles, 256, 0, st>>>(m);
-  muon_norm_kernel<<<a->P, 256, 0, st>>>(m, (int)tiles.x);
-  TP_CUDA_TRY(cudaGetLastError());
   dim3 ngrid((L.C_s + 255) / 256, (L.R_s + 31) / 32, a->P);
-  muon_normalize_kernel<<<ngrid, 256, 0, st>>>(m, 128, 256);
+  {
+    TP_PROF(TP_PROF_MUON_ELEMENTWISE, st);
+    muon_geometry_kernel<<<(a->P + 255) / 256, 256, 0, st>>>(m);
+    muon_prologue_kernel<<<tiles, 256, 0, st>>>(m);
+    muon_norm_kernel<<<a->P, 256, 0, st>>>(m, (int)tiles.x);
+    muon_normalize_kernel<<<ngrid, 256, 0, st>>>(m, 128, 256);
+  }
   TP_CUDA_TRY(cudaGetLastError());
   // quintic Newton-Schulz, coefficients of optim.py:477
   const float ca = 3.4445f, cb = -4.7750f, cc = 2.0315f;
@@ -700,12 +800,14 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
     std::swap(X, Xn);
   }
   m.x = reinterpret_cast<__nv_bfloat16*>(X);
+  TP_PROF(TP_PROF_MUON_ELEMENTWISE, st);
   muon_apply_kernel<<<tiles, 256, 0, st>>>(m);
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;
 }
 
 int tp_metric_pack(const tp_metric_args* a, void* stream) {
+  TP_PROF(TP_PROF_METRIC, static_cast<cudaStream_t>(stream));
   if (!a || a->P <= 0 || a->N <= 0 || !a->y_pred || !a->y_true || !a->out) return fail(TP_EINVAL, "bad metric arguments");
   if (a->metric < TP_METRIC_MSE || a->metric > TP_METRIC_R2) return fail(TP_EINVAL, "unknown metric %d", a->metric);
   MetricSrc s{};
@@ -757,6 +859,7 @@ size_t tp_greedy_workspace_size(int32_t n_pred, int64_t N, int32_t C) {
 }
 
 int tp_greedy_ensemble(const tp_greedy_args* a, void* stream) {
+  TP_PROF(TP_PROF_GREEDY, static_cast<cudaStream_t>(stream));
   if (!a || a->n_pred <= 0 || a->N <= 0 || !a->predictions || !a->y_true || !a->counts || !a->workspace || !a->status)
     return fail(TP_EINVAL, "bad greedy arguments");
   if (a->metric == TP_METRIC_ACCURACY || a->metric == TP_METRIC_R2 || a->metric < 0 || a->metric > TP_METRIC_R2)
@@ -827,6 +930,7 @@ int tp_greedy_ensemble(const tp_greedy_args* a, void* stream) {
 
 int tp_ensemble_mean(const float* pred, const int32_t* idx, const float* weights, int32_t K, int64_t n, float* out,
                      void* stream) {
+  TP_PROF(TP_PROF_OTHER, static_cast<cudaStream_t>(stream));
   if (!pred || !idx || !out || K <= 0 || n <= 0) return fail(TP_EINVAL, "bad ensemble-mean arguments");
   const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4096);
   ensemble_mean_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(pred, idx, weights, K, n, out);
@@ -835,6 +939,7 @@ int tp_ensemble_mean(const float* pred, const int32_t* idx, const float* weights
 }
 
 int tp_softmax_rows(const float* x, int64_t rows, int32_t C, float* out, void* stream) {
+  TP_PROF(TP_PROF_OTHER, static_cast<cudaStream_t>(stream));
   if (!x || !out || rows <= 0 || C <= 0) return fail(TP_EINVAL, "bad softmax arguments");
   const int64_t threads = rows * 32;
   const int blocks = (int)std::min<int64_t>((threads + 255) / 256, 1 << 20);
@@ -896,6 +1001,7 @@ size_t tp_cos_emb_workspace_size(int32_t P, int32_t B, int32_t F, int32_t D) {
 }
 
 int tp_tabpack_input(const tp_input_args* a, void* stream) {
+  TP_PROF(TP_PROF_INPUT, static_cast<cudaStream_t>(stream));
   if (!a || a->rows <= 0 || a->n_num < 0 || a->n_cat < 0 || !a->out) return fail(TP_EINVAL, "bad input arguments");
   if (a->n_num > 0 && !a->x_num) return fail(TP_EINVAL, "x_num is null");
   if (a->n_cat > 0 && (!a->x_cat || !a->cat_offsets)) return fail(TP_EINVAL, "x_cat or cat_offsets is null");
@@ -919,6 +1025,7 @@ int tp_tabpack_input(const tp_input_args* a, void* stream) {
 }
 
 int tp_cos_emb_forward(const tp_cos_emb_args* a, void* stream) {
+  TP_PROF(TP_PROF_EMBEDDING, static_cast<cudaStream_t>(stream));
   int rc = check_cos_emb(a);
   if (rc) return rc;
   if (!a->out || a->out_ld < a->F * a->D) return fail(TP_EINVAL, "embedding output needs out_ld >= F * D");
@@ -936,6 +1043,7 @@ int tp_cos_emb_forward(const tp_cos_emb_args* a, void* stream) {
 }
 
 int tp_cos_emb_backward(const tp_cos_emb_args* a, void* stream) {
+  TP_PROF(TP_PROF_EMBEDDING, static_cast<cudaStream_t>(stream));
   int rc = check_cos_emb(a);
   if (rc) return rc;
   if (!a->grad_out || a->grad_ld < a->F * a->D) return fail(TP_EINVAL, "embedding gradient needs grad_ld >= F * D");
@@ -970,6 +1078,7 @@ size_t tp_roc_auc_workspace_size(int32_t P, int64_t N, int32_t dtype) {
 
 int tp_binary_roc_auc(const void* scores, const int64_t* labels, int32_t P, int64_t N, int32_t dtype, void* out,
                       void* workspace, size_t workspace_bytes, void* stream) {
+  TP_PROF(TP_PROF_ROC_AUC, static_cast<cudaStream_t>(stream));
   if (!scores || !labels || !out || !workspace) return fail(TP_EINVAL, "null ROC AUC argument");
   if (P <= 0 || N <= 0) return fail(TP_EINVAL, "ROC AUC needs P > 0 and N > 0 (got %d, %lld)", P, (long long)N);
   if (N >= (int64_t)1 << 31) return fail(TP_EINVAL, "ROC AUC supports N < 2^31");
@@ -989,6 +1098,7 @@ int tp_binary_roc_auc(const void* scores, const int64_t* labels, int32_t P, int6
 
 int tp_permutation_keys(uint64_t seed, uint32_t epoch, uint32_t member_base, int32_t P, int64_t N, int32_t* keys,
                         void* stream) {
+  TP_PROF(TP_PROF_OTHER, static_cast<cudaStream_t>(stream));
   if (!keys || P <= 0 || N <= 0) return fail(TP_EINVAL, "bad permutation-key arguments");
   const int blocks = (int)std::min<int64_t>(((int64_t)P * N + 255) / 256, 8192);
   permutation_keys_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
@@ -1008,7 +1118,17 @@ int tp_dropout_mask(uint64_t seed, uint32_t offset, uint32_t member_base, const 
   return TP_OK;
 }
 
+int tp_quotient_check(int32_t den_first, int32_t den_count, unsigned long long* counts, void* stream) {
+  if (!counts || den_count <= 0 || den_first <= 0 || den_first + den_count > 0x7F80)
+    return fail(TP_EINVAL, "divisor patterns must be positive finite bf16 values (0x0001 .. 0x7F7F)");
+  if (den_count > 65535) return fail(TP_EINVAL, "at most 65535 divisors a call");
+  quotient_check_kernel<<<dim3(16, den_count), 256, 0, static_cast<cudaStream_t>(stream)>>>(den_first, counts);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
 int tp_weight_cast(const tp_weight_cast_args* a, void* stream) {
+  TP_PROF(TP_PROF_WEIGHT_CAST, static_cast<cudaStream_t>(stream));
   if (!a || a->P <= 0 || a->src_rows <= 0 || a->src_cols <= 0 || !a->src || !a->dst)
     return fail(TP_EINVAL, "bad weight cast arguments");
   if (a->dst_rows < a->src_rows || a->dst_cols < a->src_cols || a->dst_cols % 8 != 0)
@@ -1027,6 +1147,7 @@ int tp_weight_cast(const tp_weight_cast_args* a, void* stream) {
 }
 
 int tp_weight_cast_transposed(const tp_weight_cast_t_args* a, void* stream) {
+  TP_PROF(TP_PROF_WEIGHT_CAST, static_cast<cudaStream_t>(stream));
   if (!a || a->P <= 0 || a->src_rows <= 0 || a->ncols <= 0 || a->col0 < 0 || !a->src || !a->dst)
     return fail(TP_EINVAL, "bad transposed weight cast arguments");
   if (a->src_ld < a->col0 + a->ncols) return fail(TP_EINVAL, "column block beyond the source rows");
@@ -1101,6 +1222,8 @@ int tp_onehot_linear_forward(const tp_linear_args* a, const tp_onehot_args* oh, 
     return fail(TP_EINVAL, "addend must be 16-byte aligned with addend_ld a multiple of 16 covering max_out");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const OneHotArgs k = onehot_args(a, oh);
+  {
+  TP_PROF(TP_PROF_ONEHOT, st);
   if (oh->sorted_keys) {  // the category sort the backward reads
     int pow2 = 1;
     while (pow2 < a->B) pow2 <<= 1;
@@ -1111,6 +1234,7 @@ int tp_onehot_linear_forward(const tp_linear_args* a, const tp_onehot_args* oh, 
   }
   onehot_gather_kernel<<<dim3((a->B + 7) / 8, a->P), 256, 0, st>>>(k);
   TP_CUDA_TRY(cudaGetLastError());
+  }
   return linear_forward_impl(a, oh->addend, oh->addend_ld, stream);
 }
 
@@ -1144,12 +1268,14 @@ int tp_onehot_linear_backward(const tp_linear_grad_args* ga, const tp_onehot_arg
   const int nb_count = (dw_rows + ONEHOT_WG_N - 1) / ONEHOT_WG_N;
   const long long blocks = ((long long)a->P * nb_count + ONEHOT_WG_WARPS - 1) / ONEHOT_WG_WARPS;
   if (blocks > 0x7FFFFFFFLL) return fail(TP_EINVAL, "too many one-hot gradient tasks");
+  TP_PROF(TP_PROF_ONEHOT, static_cast<cudaStream_t>(stream));
   onehot_wgrad_kernel<<<(unsigned)blocks, 32 * ONEHOT_WG_WARPS, 0, static_cast<cudaStream_t>(stream)>>>(k, nb_count);
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;
 }
 
 int tp_adamw_step(const tp_adamw_args* a, void* stream) {
+  TP_PROF(TP_PROF_ADAMW, static_cast<cudaStream_t>(stream));
   if (!a || a->n_tensors <= 0 || a->n_tensors > TP_MAX_OPT_TENSORS) return fail(TP_EINVAL, "bad tensor count");
   AdamWTensors ts{};
   int64_t max_numel = 0;

@@ -17,6 +17,33 @@ from tabpack_b200 import _lib
 from tabpack_b200._lib import TP_DTYPE_BF16, TP_DTYPE_F32, check, load
 
 
+class KernelTimes:
+    """Per-family device time of this library's kernel launches (`tp_profile_start` /
+    `tp_profile_stop`): `with KernelTimes() as kt: ...` then `kt.ms` and `kt.launches`, dicts
+    keyed by family name (`_lib.TP_PROF_KINDS`).  Each launch is bracketed by two CUDA events
+    on its stream; the totals are read once the block ends (a synchronisation)."""
+
+    def __init__(self, capacity: int = 1 << 16) -> None:
+        self.capacity = capacity
+        self.ms: dict[str, float] = {}
+        self.launches: dict[str, int] = {}
+        self.dropped = 0
+
+    def __enter__(self) -> 'KernelTimes':
+        check(load().tp_profile_start(self.capacity), 'tp_profile_start')
+        return self
+
+    def __exit__(self, *exc) -> None:
+        n = len(_lib.TP_PROF_KINDS)
+        ms = (ctypes.c_double * n)()
+        cnt = (ctypes.c_int64 * n)()
+        dropped = ctypes.c_int32(0)
+        check(load().tp_profile_stop(ms, cnt, n, ctypes.byref(dropped)), 'tp_profile_stop')
+        self.ms = {k: ms[i] for i, k in enumerate(_lib.TP_PROF_KINDS)}
+        self.launches = {k: cnt[i] for i, k in enumerate(_lib.TP_PROF_KINDS)}
+        self.dropped = dropped.value
+
+
 def _ptr(t: Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 

@@ -193,9 +193,7 @@ class AdamWPack(OptimizerPack):
     @torch.no_grad()
     def step(self, closure=None):
         loss = closure() if closure is not None else None
-        for g in self.param_groups:
-            _adamw_group(self, g['params'], lr=g['lr'], beta1=g['beta1'], beta2=g['beta2'], eps=g['eps'],
-                         weight_decay=g['weight_decay'], support_replacement=self._support_replacement)
+        adamw_step(self, support_replacement=self._support_replacement)
         return loss
 
 
@@ -278,48 +276,71 @@ class MuonAdamWPack(OptimizerPack):
                 g['muon_update_scale'] = compute_muon_update_scale_pack(lin)
                 g['muon_out_features'], g['muon_in_features'] = _widths(lin)
 
-    def _workspace(self, p: Tensor) -> Tensor:
-        P, mo, mi = p.shape
-        n = ops.muon_workspace_size(P, mo, mi)
-        ws = self._workspaces.get(p.device)
-        if ws is None or ws.numel() < n:
-            ws = torch.empty(n, dtype=torch.uint8, device=p.device)
-            self._workspaces[p.device] = ws
-        return ws
-
-    def _step_muon(self, g) -> None:
-        p = g['params'][0]
-        if p.ndim != 3:
-            raise ValueError('Parameters optimized with Muon must have three dimensions')
-        if p.grad is None:
-            return
-        if p.grad.is_sparse:
-            raise RuntimeError('Sparse gradients are not supported')
-        st = self.state[p]
-        if len(st) == 0:
-            st['muon_momentum_buffer'] = torch.zeros_like(p)
-        grad = p.grad.data
-        if not self._allow_inplace_grad_mutation:
-            grad = grad.clone()
-        scale = g.get('muon_update_scale')
-        ops.muon_step(p, grad, st['muon_momentum_buffer'], out_features=g.get('muon_out_features'),
-                      in_features=g.get('muon_in_features'), lr=_hp(g['muon_lr']), momentum=_hp(g['muon_momentum']),
-                      weight_decay=_hp(g['weight_decay']),
-                      update_scale=None if scale is None else scale.to(torch.float32).contiguous(),
-                      nesterov=bool(g['muon_nesterov']), mutate_grad=True,
-                      ns_steps=int(g['muon_newton_schulz_steps']), workspace=self._workspace(p))
-
     @torch.no_grad()
     def step(self, closure=None):
         loss = closure() if closure is not None else None
-        for g in self.param_groups:
-            if g['muon']:
-                self._step_muon(g)
-            else:
-                _adamw_group(self, g['params'], lr=g['adamw_lr'], beta1=g['adamw_beta1'], beta2=g['adamw_beta2'],
-                             eps=g['adamw_eps'], weight_decay=g['weight_decay'],
-                             support_replacement=self._support_replacement)
+        muon_adamw_step(self, workspaces=self._workspaces, allow_inplace_grad_mutation=self._allow_inplace_grad_mutation,
+                        support_replacement=self._support_replacement)
         return loss
+
+
+def _muon_workspace(workspaces: dict, p: Tensor) -> Tensor:
+    """The Newton-Schulz workspace of `p`'s device, grown to fit `p` (one per optimizer)."""
+    P, mo, mi = p.shape
+    n = ops.muon_workspace_size(P, mo, mi)
+    ws = workspaces.get(p.device)
+    if ws is None or ws.numel() < n:
+        ws = torch.empty(n, dtype=torch.uint8, device=p.device)
+        workspaces[p.device] = ws
+    return ws
+
+
+def _muon_group(opt: torch.optim.Optimizer, g: dict, *, workspaces: dict, allow_inplace_grad_mutation: bool) -> None:
+    """`MuonAdamWPack._step_muon` (`optim.py:682-774`) for one single-parameter Muon group:
+    weight decay, momentum, Nesterov blend, batched Newton-Schulz and the scaled update in the
+    Muon kernels.  Per-member widths (`muon_out_features` / `muon_in_features`) keep each
+    member's Newton-Schulz on its own out x in block; without them it runs on the padded block
+    (the reference's arithmetic: zero padding rows and columns do not change the result)."""
+    p = g['params'][0]
+    if p.ndim != 3:
+        raise ValueError('Parameters optimized with Muon must have three dimensions')
+    if p.grad is None:
+        return
+    if p.grad.is_sparse:
+        raise RuntimeError('Sparse gradients are not supported')
+    st = opt.state[p]
+    if len(st) == 0:
+        st['muon_momentum_buffer'] = torch.zeros_like(p)
+    grad = p.grad.data
+    if not allow_inplace_grad_mutation:
+        grad = grad.clone()
+    scale = g.get('muon_update_scale')
+    ops.muon_step(p, grad, st['muon_momentum_buffer'], out_features=g.get('muon_out_features'),
+                  in_features=g.get('muon_in_features'), lr=_hp(g['muon_lr']), momentum=_hp(g['muon_momentum']),
+                  weight_decay=_hp(g['weight_decay']),
+                  update_scale=None if scale is None else scale.to(torch.float32).contiguous(),
+                  nesterov=bool(g['muon_nesterov']), mutate_grad=True,
+                  ns_steps=int(g['muon_newton_schulz_steps']), workspace=_muon_workspace(workspaces, p))
+
+
+def adamw_step(opt: torch.optim.Optimizer, *, support_replacement: bool) -> None:
+    """`AdamWPack.step` (`optim.py:347-427`) over every group of `opt` (keys `lr`, `beta1`,
+    `beta2`, `eps`, `weight_decay`), one grouped AdamW launch per group."""
+    for g in opt.param_groups:
+        _adamw_group(opt, g['params'], lr=g['lr'], beta1=g['beta1'], beta2=g['beta2'], eps=g['eps'],
+                     weight_decay=g['weight_decay'], support_replacement=support_replacement)
+
+
+def muon_adamw_step(opt: torch.optim.Optimizer, *, workspaces: dict, allow_inplace_grad_mutation: bool,
+                    support_replacement: bool) -> None:
+    """`MuonAdamWPack.step` (`optim.py:495-861`) over every group of `opt`: Muon groups through
+    the Muon kernels, the others through the grouped AdamW kernel (`adamw_*` keys)."""
+    for g in opt.param_groups:
+        if g['muon']:
+            _muon_group(opt, g, workspaces=workspaces, allow_inplace_grad_mutation=allow_inplace_grad_mutation)
+        else:
+            _adamw_group(opt, g['params'], lr=g['adamw_lr'], beta1=g['adamw_beta1'], beta2=g['adamw_beta2'],
+                         eps=g['adamw_eps'], weight_decay=g['weight_decay'], support_replacement=support_replacement)
 
 
 def optimizer_pack_remove(optimizer, *, pack_idx: Tensor, old_to_new_parameters) -> None:

@@ -290,9 +290,11 @@ class PackTrainer:
         order = torch.argsort(keys, dim=1, stable=True)
         return order.split(batch_size, dim=1)
 
-    def fit_epoch(self, data: dict, *, batch_size: int, epoch: int) -> Tensor:
+    def fit_epoch(self, data: dict, *, batch_size: int, epoch: int,
+                  on_step: Callable[[int, Tensor], None] | None = None) -> Tensor:
         """One epoch over `data` ({'x_num', 'x_cat', 'y'} on this device); returns the
-        mean training loss of every member (P_total,) (gathered when sharded)."""
+        mean training loss of every member (P_total,) (gathered when sharded).  `on_step(i,
+        losses)` sees each step's per-member losses of this rank (a device tensor)."""
         self.model.train()
         n = len(data['y'])
         total = torch.zeros(self.hi - self.lo, device=self.device)
@@ -307,6 +309,8 @@ class PackTrainer:
             self.opt.step()
             self.opt.zero_grad()
             total += losses.detach()
+            if on_step is not None:
+                on_step(steps, losses.detach())
             steps += 1
         mean = total / max(steps, 1)
         return gather_members(mean, self.counts, self.group) if self.world > 1 else mean

@@ -81,6 +81,38 @@ def test_tabpack_training_step_matches_reference(golden, name, autocast):
         assert err(got, want) < tol_for('grad.' + k), (k, err(got, want), tol_for('grad.' + k))
 
 
+def test_tabpack_bf16_matches_the_reference_bf16_path(golden):
+    """bf16 against the reference's own bf16 autocast run of the same step (`bf16ref.*`, the
+    reference's `TabPack` under `torch.autocast(bfloat16)` on the same inputs, weights and
+    masks).  The forward output must agree within 2e-2 relative Frobenius error, the bar for
+    bf16 with fp32 accumulation.  Parameter gradients are held to fp64 truth instead
+    (`test_tabpack_training_step_matches_reference`): three layers deep, each bf16
+    implementation is 3-5 % off fp64, rounding at different points (autocast after every op,
+    here once per fused block), so the two differ from each other by as much; that
+    difference is reported here."""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+    g = golden('tabpack_large.npz')
+    dev = torch.device('cuda')
+    model = _model_from_golden(g, dev)
+    model.train()
+    x_num = torch.from_numpy(g['x_num']).float().to(dev)
+    x_cat = torch.from_numpy(g['x_cat']).to(dev)
+    with torch.autocast('cuda', dtype=torch.bfloat16):
+        y = model(x_num, x_cat)
+    y = y.float()
+    err_y = _rel_fro(y.detach().cpu().numpy(), g['bf16ref.y'])
+    (y * torch.from_numpy(g['dy']).float().to(dev)).sum().backward()
+    grads = {}
+    for k, p in model.named_parameters():
+        got = p.grad.detach().cpu().numpy()
+        grads[k] = (_rel_fro(got, g['bf16ref.grad.' + k]), _rel_fro(got, g['grad.' + k]),
+                    _rel_fro(g['bf16ref.grad.' + k], g['grad.' + k]))
+    print('forward output against the reference bf16 path:', err_y)
+    print('gradients (against reference bf16, ours against fp64, reference bf16 against fp64):', grads)
+    assert err_y <= 2e-2
+
+
 def test_eval_forward_shared_input_and_state_dict_keys(golden):
     if not torch.cuda.is_available():
         pytest.skip('needs a GPU')

@@ -174,3 +174,29 @@ def test_adamw_pack_class_matches_reference(golden, case):
         torch.cuda.synchronize()
         np.testing.assert_allclose(w.detach().cpu().numpy(), g[f'c{case}.s{s}.w'], rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(b.detach().cpu().numpy(), g[f'c{case}.s{s}.b'], rtol=1e-5, atol=1e-6)
+
+
+def test_muon_normalisation_quotient_equals_cuda_division():
+    """The Muon normalisation divides every element by the matrix's bf16 norm through the
+    reciprocal and one fused correction step (Markstein's method).  Checked exhaustively
+    against CUDA's correctly rounded division (`__fdiv_rn`): every positive normal bf16
+    divisor, every finite bf16 dividend with |x| <= 2 * divisor -- every pair the normalisation
+    can meet, since an element never exceeds its matrix's norm and both are bf16 there.  The
+    stored bf16 quotients must agree bit for bit (the sign of zero included); the fp32
+    quotients before that rounding may differ in the last place, which is reported."""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+    from tabpack_b200 import _lib
+
+    lib = _lib.load()
+    counts = torch.zeros(4, dtype=torch.int64, device='cuda')
+    stream = torch.cuda.current_stream().cuda_stream
+    first, last = 0x0080, 0x7F7F  # smallest and largest positive normal bf16
+    rc = lib.tp_quotient_check(first, last - first + 1, counts.data_ptr(), stream)
+    assert rc == 0, lib.tp_last_error_string()
+    m32, m16, n, sub = counts.tolist()
+    print(f'quotient check: {n} pairs, {m32} fp32 results differ from x / den ({sub} of them with a subnormal '
+          f'quotient or reciprocal), {m16} differ after rounding to bf16')
+    assert n > 1_000_000_000
+    assert m16 == 0  # what the normalisation stores agrees bit for bit, the sign of zero included
+    assert m32 < 0.01 * n
