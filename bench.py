@@ -688,6 +688,7 @@ def run_train(args) -> None:
     stream = torch.cuda.current_stream(dev)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     with ClockSampler(local) as clocks:
+        torch.cuda.nvtx.range_push('timed')  # lets a profiler keep only the timed region
         ev[0].record(stream)
         loss = trainer.fit_epoch(dev_data['train'], batch_size=BATCH, epoch=1)
         ev[1].record(stream)
@@ -695,6 +696,7 @@ def run_train(args) -> None:
         ens = OnlineEnsemble(trainer._score(dev_data['val']['y']))
         ens.update(lambda key: preds[key[0]], [], [(g, K) for g in trainer.gathered_ids])
         ev[2].record(stream)
+        torch.cuda.nvtx.range_pop()
         barrier()
     region_ms, train_ms = ev[0].elapsed_time(ev[2]), ev[0].elapsed_time(ev[1])
 
