@@ -14,9 +14,11 @@
 //   MODE_NS / MODE_NS_BMN: C = alpha * A B^T + beta * D over each member's r x (r|c) block
 //                 (B K-major / MN-major); tiles claimed dynamically
 //
-// Warp roles: warp 0 = TMA producer (and, with a tile counter, the tile claimer), warp 1 =
-// TMEM owner + MMA issuer, warps 2.. = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31 and
-// column slice (w-2)/4).  The forward runs 16 epilogue warps (four per SM sub-partition: its
+// Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer, warp 2 = tile
+// scheduler (claims and decodes the CTA's tiles ahead of use and publishes them in a
+// shared-memory ring that the producer, the MMA thread and the epilogue warps read in order,
+// so no per-tile global load or division sits on their critical paths), warps 3.. = epilogue
+// (warp w reads TMEM lanes 32*(w%4) .. +31 and column slice (w-3)/4).  The forward runs 16 epilogue warps (four per SM sub-partition: its
 // bias + ReLU + Philox epilogue is latency-bound, so four warps per scheduler hide each
 // other's dependency stalls) over a 3-stage ring; the other modes run 8 epilogue warps.
 #pragma once
@@ -47,15 +49,20 @@ struct Sm100Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int EPI_WARPS = FWDK ? 16 : 8;
-  static constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
-  // stages + barriers (full, empty per stage; tfull, tempty x2; done) + tmem addr + abort
-  // + per-warp bias slice (BN / (EPI_WARPS / 4) floats per epilogue warp)
+  static constexpr int EPI_WARP0 = 3;  // first epilogue warp
+  static constexpr int NUM_THREADS = 32 * EPI_WARP0 + 32 * EPI_WARPS;
+  static constexpr int TRING = 4;      // slots of the decoded-tile ring
+  // control block: barriers (full, empty per stage; tfull, tempty x2; done; tile ring full,
+  // empty per slot), tmem address, abort flag (first 256 bytes), then the tile ring (8 ints
+  // per slot)
+  static constexpr int CTRL_BYTES = 512;
+  // stages + control block + per-warp bias slice (BN / (EPI_WARPS / 4) floats per epilogue warp)
   static constexpr int BIAS_FLOATS_PER_WARP = BN / (EPI_WARPS / 4);
   // + per-warp staging tile for coalesced bf16 stores (32 rows x 32 columns, rows padded to 80 B)
   static constexpr int STAGE_ROW_BYTES = 80;
   static constexpr int STORE_STAGE_BYTES = 32 * STAGE_ROW_BYTES;
   static constexpr int SMEM_BYTES =
-      1024 + STAGES * STAGE_BYTES + 256 + EPI_WARPS * BIAS_FLOATS_PER_WARP * 4 + EPI_WARPS * STORE_STAGE_BYTES;
+      1024 + STAGES * STAGE_BYTES + CTRL_BYTES + EPI_WARPS * BIAS_FLOATS_PER_WARP * 4 + EPI_WARPS * STORE_STAGE_BYTES;
 };
 
 // Forward epilogue of one 16-column chunk (columns col0.., col0 a multiple of 16) of one
@@ -210,11 +217,12 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
   uint64_t* tfull = bars + 2 * Cfg::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* done_bar = tempty + 2;
-  uint64_t* tr_full = done_bar + 1;   // tile-id ring (dynamic scheduling): published
-  uint64_t* tr_empty = tr_full + 4;   //   read by the MMA thread and every epilogue warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tr_empty + 4);
+  constexpr int TRING = Cfg::TRING;
+  uint64_t* tr_full = done_bar + 1;        // decoded-tile ring: published by the scheduler warp,
+  uint64_t* tr_empty = tr_full + TRING;    //   read by the producer, the MMA thread and every epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tr_empty + TRING);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* tile_ring = abort_flag + 1;
+  volatile int* tile_ring = reinterpret_cast<volatile int*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + 256);
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -224,20 +232,28 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
-  // Dynamic scheduling (single CTAs with a counter): the producer claims the k-th tile
-  // (k > 0) with an atomic on the counter and publishes its id in ring slot k % 4; the MMA
-  // thread and the epilogue warps read the ids in the same order.  Tiles of ragged members
+  // With a tile list (single CTAs), tiles are claimed dynamically: ragged members' tiles
   // differ a lot in cost, so claiming them as CTAs free up balances the launch.
-  const bool dyn = !PAIR && pr.tile_counter != nullptr;
-  // k-th tile of this CTA for a consumer (MMA thread or an epilogue warp); total_tiles ends
-  auto consume_tile = [&](int k, bool arrive) -> int {
-    if (!dyn) return tile0 + k * tile_step;
-    const int s = k & 3;
-    if (!mbar_wait(&tr_full[s], (uint32_t)(k >> 2) & 1u, abort_flag)) return total_tiles;
-    const int t = tile_ring[s];
+  // k-th tile of this CTA for a consumer warp (all its active lanes read; `arrive` frees the
+  // slot, once per consumer warp); KIND_END ends the sequence
+  auto ring_read = [&](int k, bool arrive) -> TileInfo {
+    TileInfo ti;
+    const int s = k & (TRING - 1);
+    if (!mbar_wait(&tr_full[s], (uint32_t)(k / TRING) & 1u, abort_flag)) {
+      ti.kind = KIND_END;
+      return ti;
+    }
+    const volatile int* e = tile_ring + 8 * s;
+    ti.member = e[0];
+    ti.mt = e[1];
+    ti.nt = e[2];
+    ti.kind = e[3];
+    ti.kblocks = e[4];
+    ti.m_valid = e[5];
+    ti.n_valid = e[6];
     __syncwarp(__activemask());
     if (arrive) mbar_arrive(&tr_empty[s]);
-    return t;
+    return ti;
   };
 
   if (threadIdx.x == 0) {
@@ -250,9 +266,10 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
       mbar_init(&tempty[i], PAIR ? 2 * Cfg::EPI_WARPS : Cfg::EPI_WARPS);  // the leader's counts both CTAs
     }
     mbar_init(done_bar, 1);
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < TRING; ++i) {
       mbar_init(&tr_full[i], 1);
-      mbar_init(&tr_empty[i], 1 + Cfg::EPI_WARPS);
+      // consumers: the producer, the epilogue warps and the MMA thread (a pair's leader only)
+      mbar_init(&tr_empty[i], 1 + Cfg::EPI_WARPS + ((!PAIR || rank == 0) ? 1 : 0));
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -277,16 +294,8 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int k = 0;; ++k) {
-        int t = tile0 + k * tile_step;
-        if (dyn) {  // claim and publish the k-th tile
-          if (k > 0) t = min(total_tiles, (int)gridDim.x + atomicAdd(pr.tile_counter, 1));
-          const int s = k & 3;
-          if (!mbar_wait(&tr_empty[s], ((uint32_t)(k >> 2) & 1u) ^ 1u, abort_flag)) goto producer_done;
-          tile_ring[s] = min(t, total_tiles);
-          mbar_arrive(&tr_full[s]);
-        }
-        if (t >= total_tiles) break;
-        const TileInfo ti = decode_tile(pr, t, Cfg::BK);
+        const TileInfo ti = ring_read(k, true);
+        if (ti.kind == KIND_END) break;
         if (ti.kind != KIND_MMA) continue;
         const int zA = ((Cfg::FWDK || MODE == MODE_WGRAD_T) && pr.x_shared) ? 0 : ti.member;  // NS operands are per member
         const int zB = ti.member;
@@ -349,9 +358,8 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int k = 0;; ++k) {
-        const int t = consume_tile(k, true);
-        if (t >= total_tiles) break;
-        const TileInfo ti = decode_tile(pr, t, Cfg::BK);
+        const TileInfo ti = ring_read(k, true);
+        if (ti.kind == KIND_END) break;
         if (ti.kind != KIND_MMA) continue;
         // the last column block of a member only multiplies its own columns (N multiple of
         // 16, of 32 for a pair so that each CTA's half is a multiple of 16)
@@ -409,18 +417,56 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
       volatile int no_abort = 0;
       mbar_wait(done_bar, 0, &no_abort);
     }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ tile scheduler
+    // Claims (tile list) or enumerates (slots c, c + grid, ...) this CTA's tiles, decodes
+    // them and publishes every tile that needs work, then KIND_END.
+    if (lane == 0) {
+      const int n_list = pr.tile_list != nullptr ? __ldg(pr.tile_count) : 0;
+      int pub = 0;
+      for (int k = 0;; ++k) {
+        TileInfo ti;
+        if (pr.tile_list != nullptr) {
+          const int i = (k == 0) ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(pr.tile_counter, 1);
+          if (i < n_list)
+            ti = decode_list_entry(pr, __ldg(pr.tile_list + i), Cfg::BK);
+          else
+            ti.kind = KIND_END;
+        } else {
+          const int t = tile0 + k * tile_step;
+          if (t < total_tiles)
+            ti = decode_tile(pr, t, Cfg::BK);
+          else
+            ti.kind = KIND_END;
+          if (ti.kind == KIND_SKIP) continue;
+        }
+        const int s = pub & (TRING - 1);
+        if (!mbar_wait(&tr_empty[s], ((uint32_t)(pub / TRING) & 1u) ^ 1u, abort_flag)) break;
+        volatile int* e = tile_ring + 8 * s;
+        e[0] = ti.member;
+        e[1] = ti.mt;
+        e[2] = ti.nt;
+        e[3] = ti.kind;
+        e[4] = ti.kblocks;
+        e[5] = ti.m_valid;
+        e[6] = ti.n_valid;
+        mbar_arrive(&tr_full[s]);
+        ++pub;
+        if (ti.kind == KIND_END) break;
+      }
+    }
   } else {
     // ------------------------------------------------------------------ epilogue
-    // Epilogue warp w drains TMEM lane quarter (w % 4) and column slice (w - 2) / 4
+    // Epilogue warp w drains TMEM lane quarter (w % 4) and column slice (w - 3) / 4
     // (EPI_WARPS / 4 slices of WCOLS columns).
-    const int ew = warp - 2;
+    const int ew = warp - Cfg::EPI_WARP0;
     const int q = warp & 3;
     const int half = ew >> 2;
     constexpr int WCOLS = BN / (Cfg::EPI_WARPS / 4);
     constexpr int NCH = WCOLS / 32;
-    float* sbias = reinterpret_cast<float*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + 256) + ew * WCOLS;
-    uint8_t* stage_warp = smem + Cfg::STAGES * Cfg::STAGE_BYTES + 256 + Cfg::EPI_WARPS * Cfg::BIAS_FLOATS_PER_WARP * 4 +
-                          ew * Cfg::STORE_STAGE_BYTES;
+    float* sbias = reinterpret_cast<float*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + Cfg::CTRL_BYTES) + ew * WCOLS;
+    uint8_t* stage_warp = smem + Cfg::STAGES * Cfg::STAGE_BYTES + Cfg::CTRL_BYTES +
+                          Cfg::EPI_WARPS * Cfg::BIAS_FLOATS_PER_WARP * 4 + ew * Cfg::STORE_STAGE_BYTES;
     uint8_t* stage_row = stage_warp + lane * Cfg::STAGE_ROW_BYTES;
     const int row_in_tile = (int)rank * Cfg::BM + q * 32 + lane;
     int acc = 0;
@@ -441,27 +487,23 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
                        : 0.0f;
       }
     };
-    int t = consume_tile(0, lane == 0);
-    if (t < total_tiles) {
-      nti = decode_tile(pr, t, Cfg::BK);
+    nti = ring_read(0, lane == 0);
+    if (nti.kind != KIND_END) {
       if (dropout_on) np = __ldg(pr.dropout_p + nti.member);
       if (Cfg::FWDK) load_bias(nti);
     }
-    int t_next = total_tiles;
-    for (int k = 0; t < total_tiles; ++k, t = t_next) {
+    for (int k = 0; nti.kind != KIND_END; ++k) {
       const TileInfo ti = nti;
       const float p_cur = np;
-      t_next = consume_tile(k + 1, lane == 0);
-      if (t_next < total_tiles) {
-        nti = decode_tile(pr, t_next, Cfg::BK);
-        if (dropout_on) np = __ldg(pr.dropout_p + nti.member);
-      }
+      nti = ring_read(k + 1, lane == 0);
+      const bool has_next = nti.kind != KIND_END;
+      if (has_next && dropout_on) np = __ldg(pr.dropout_p + nti.member);
       const int m = ti.member;
       const int row = ti.mt * Cfg::TILE_M + row_in_tile;
       const int cbase = ti.nt * BN + half * WCOLS;
       // a ZERO / COPY / SKIP tile stages no bias: prefetch the next tile's slice here, so the
       // MMA tile after it does not stage this tile's (zero) slice
-      if (Cfg::FWDK && ti.kind != KIND_MMA && t_next < total_tiles) load_bias(nti);
+      if (Cfg::FWDK && ti.kind != KIND_MMA && has_next) load_bias(nti);
       if (ti.kind == KIND_MMA) {
         uint32_t thr = 65536u;
         float scale = 1.0f;  // 1 / (1 - p): kept elements are (acc + b) * scale
@@ -476,7 +518,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < NCH; ++i) sbias[32 * i + lane] = bnext[i] * scale;
           __syncwarp();
-          if (t_next < total_tiles) load_bias(nti);
+          if (has_next) load_bias(nti);
         }
         // Newton-Schulz: the addend of the first chunk is loaded before the accumulator wait
         [[maybe_unused]] uint4 d_a[4], d_b[4];

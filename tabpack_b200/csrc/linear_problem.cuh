@@ -23,7 +23,8 @@ enum : int { MODE_FWD_ADD = 6 };
 // Kernel instantiation of the forward without dropout on CTA pairs (mode = MODE_FWD as well):
 // without the Philox draws its epilogue keeps up with the pair's faster k-blocks.
 enum : int { MODE_FWD_PAIR = 7 };
-enum : int { KIND_MMA = 0, KIND_ZERO = 1, KIND_COPY = 2, KIND_SKIP = 3 };
+// KIND_END marks the end of a CTA's tile sequence in the kernel's shared-memory tile ring.
+enum : int { KIND_MMA = 0, KIND_ZERO = 1, KIND_COPY = 2, KIND_SKIP = 3, KIND_END = 4 };
 
 struct LinearProblem {
   int mode;
@@ -54,8 +55,12 @@ struct LinearProblem {
   int BM, BN;
   FastDiv div_member;  // by m_tiles * n_tiles (tiles per member)
   FastDiv div_mt;      // by m_tiles
-  // zeroed counter for dynamic tile scheduling (single-CTA launches), or nullptr: CTA c
-  // takes tiles c, c + grid, ...
+  // Dynamic scheduling (single-CTA launches): a dense list of the launch's MMA tiles, entry
+  // member << 16 | n-tile << 8 | m-tile, its length (on the device) and a zeroed counter; CTA
+  // c takes entry c first and claims the next ones with the counter.  Without a list CTA c
+  // takes slots c, c + grid, ...
+  const uint32_t* tile_list;
+  const int* tile_count;
   int* tile_counter;
   // Newton-Schulz GEMMs: member m multiplies r = ns_rows[m], c = ns_cols[m] matrices;
   // ns_shape 1: (M, N, K) = (r, r, c), 2: (r, r, r), 3: (r, c, r); members with
@@ -131,6 +136,20 @@ __device__ __forceinline__ TileInfo decode_tile(const LinearProblem& p, int t, i
   } else {
     ti.kind = KIND_MMA;
   }
+  return ti;
+}
+
+// A Newton-Schulz tile-list entry (see LinearProblem::tile_list).
+__device__ __forceinline__ TileInfo decode_list_entry(const LinearProblem& p, uint32_t e, int BK) {
+  TileInfo ti;
+  ti.member = (int)(e >> 16);
+  ti.nt = (int)((e >> 8) & 0xFFu);
+  ti.mt = (int)(e & 0xFFu);
+  const int r = __ldg(p.ns_rows + ti.member), c = __ldg(p.ns_cols + ti.member);
+  ti.m_valid = r;
+  ti.n_valid = (p.ns_shape == 3) ? c : r;
+  ti.kblocks = ((p.ns_shape == 1 ? c : r) + BK - 1) / BK;
+  ti.kind = KIND_MMA;
   return ti;
 }
 

@@ -54,6 +54,75 @@ __global__ void muon_geometry_kernel(MuonArgs a) {
   a.trans[m] = o > n ? 1 : 0;
 }
 
+// Dense lists of the Newton-Schulz launches' MMA tiles (128 x 256 output tiles of the
+// tcgen05 kernel): list_rr for the r x r products (A = X X^T and B = b A + c A^2), list_rc for
+// the r x c update X <- a X + B X.  Entry = member << 16 | n-tile << 8 | m-tile; a member's
+// tiles go column block by column block, down the rows within one.  Members whose update is
+// zero (active == 0) have none.  One block of 1024 threads scans the members in chunks.
+constexpr int NS_TILE_M = 128, NS_TILE_N = 256;
+
+__global__ void __launch_bounds__(1024) ns_tile_list_kernel(MuonArgs a, uint32_t* list_rr, uint32_t* list_rc,
+                                                            int* counts) {
+  __shared__ int wsum[2][32];
+  __shared__ int base[2];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  if (tid == 0) base[0] = base[1] = 0;
+  __syncthreads();
+  for (int m0 = 0; m0 < a.P; m0 += 1024) {
+    const int m = m0 + tid;
+    int mt = 0, nrr = 0, nrc = 0;
+    if (m < a.P && a.active[m] != 0) {
+      const int r = a.rows[m], c = a.cols[m];
+      mt = (r + NS_TILE_M - 1) / NS_TILE_M;
+      nrr = (r + NS_TILE_N - 1) / NS_TILE_N;
+      nrc = (c + NS_TILE_N - 1) / NS_TILE_N;
+    }
+    int v[2] = {mt * nrr, mt * nrc};
+    int incl[2] = {v[0], v[1]};
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int o = __shfl_up_sync(0xFFFFFFFFu, incl[j], d);
+        if (lane >= d) incl[j] += o;
+      }
+    }
+    if (lane == 31) {
+      wsum[0][wid] = incl[0];
+      wsum[1][wid] = incl[1];
+    }
+    __syncthreads();
+    if (wid == 0) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        int x = wsum[j][lane];
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const int o = __shfl_up_sync(0xFFFFFFFFu, x, d);
+          if (lane >= d) x += o;
+        }
+        wsum[j][lane] = x;  // inclusive over warps
+      }
+    }
+    __syncthreads();
+    int off[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) off[j] = base[j] + (wid > 0 ? wsum[j][wid - 1] : 0) + incl[j] - v[j];
+    for (int i = 0; i < v[0]; ++i) list_rr[off[0] + i] = ((uint32_t)m << 16) | ((uint32_t)(i / mt) << 8) | (uint32_t)(i % mt);
+    for (int i = 0; i < v[1]; ++i) list_rc[off[1] + i] = ((uint32_t)m << 16) | ((uint32_t)(i / mt) << 8) | (uint32_t)(i % mt);
+    __syncthreads();
+    if (tid == 0) {
+      base[0] += wsum[0][31];
+      base[1] += wsum[1][31];
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    counts[0] = base[0];
+    counts[1] = base[1];
+  }
+}
+
 // Tiles of the Muon elementwise kernels: 32 weight rows (o) x 128 weight columns (n), 256
 // threads; warp w takes rows w, w + 8, w + 16, w + 24 and lane l columns l, l + 32, l + 64,
 // l + 96, so each load instruction covers 128 contiguous bytes and a thread has 16 elements

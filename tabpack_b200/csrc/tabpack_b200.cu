@@ -241,7 +241,7 @@ int launch_sm100(const LinearProblem& pr_in, const CUtensorMap& a, const CUtenso
   // grids for which that step leaves a CTA on a subset of the column blocks.
   const int spm = pr.m_tiles * pr.n_tiles;
   auto gcd = [](int x, int y) { while (y) { const int r = x % y; x = y; y = r; } return x; };
-  for (int g = grid; g > grid / 2 && pr.n_tiles > 1 && total > grid; --g) {
+  for (int g = grid; g > grid / 2 && pr.tile_list == nullptr && pr.n_tiles > 1 && total > grid; --g) {
     const int step = g % spm;
     const bool pinned = step == 0 || (step % pr.m_tiles == 0 && gcd(step / pr.m_tiles, pr.n_tiles) > 1);
     if (!pinned) {
@@ -319,7 +319,7 @@ LinearProblem base_problem(const tp_linear_args* a) {
 struct MuonLayout {
   int R_s, C_s, tiles;
   size_t off_x0, off_x1, off_a, off_b, off_norm, off_rows, off_cols, off_trans, off_active, off_partial, off_counter,
-      total;
+      off_list_rr, off_list_rc, off_list_n, total;
 };
 
 constexpr int MUON_COUNTERS = 64;
@@ -343,6 +343,11 @@ MuonLayout muon_layout(int P, int max_out, int max_in) {
   L.tiles = ((max_out + MUON_TM - 1) / MUON_TM) * ((max_in + MUON_TN - 1) / MUON_TN);
   L.off_partial = take((size_t)P * L.tiles * 4);
   L.off_counter = take(MUON_COUNTERS * 4);  // tile counters of the Newton-Schulz launches
+  // dense tile lists of the Newton-Schulz launches (r x r and r x c outputs) and their lengths
+  const size_t mtl = (size_t)L.R_s / NS_TILE_M;
+  L.off_list_rr = take((size_t)P * mtl * ((L.R_s + NS_TILE_N - 1) / NS_TILE_N) * 4);
+  L.off_list_rc = take((size_t)P * mtl * ((L.C_s + NS_TILE_N - 1) / NS_TILE_N) * 4);
+  L.off_list_n = take(2 * 4);
   L.total = o;
   return L;
 }
@@ -350,10 +355,14 @@ MuonLayout muon_layout(int P, int max_out, int max_in) {
 // One Newton-Schulz GEMM over the pack: out = alpha * A_op B_op^T + beta * D.
 template <int MODE>
 int ns_gemm(const MuonArgs& ma, int shape, const void* a_op, int a_cols, const void* b_op, int b_cols,
-            void* out, int out_cols, const void* d, float alpha, float beta, int* counter, cudaStream_t st) {
+            void* out, int out_cols, const void* d, float alpha, float beta, const uint32_t* list,
+            const int* list_n, int* counter, cudaStream_t st) {
   constexpr int BN = 256;
+  static_assert(BN == NS_TILE_N && Sm100Cfg<BN, MODE>::TILE_M == NS_TILE_M, "tile lists match the kernel's tiles");
   LinearProblem pr{};
-  pr.tile_counter = counter;  // zeroed: tiles of ragged members are claimed dynamically
+  pr.tile_list = list;  // the launch's MMA tiles, claimed dynamically (ragged members)
+  pr.tile_count = list_n;
+  pr.tile_counter = counter;  // zeroed
   pr.mode = MODE;
   pr.P = ma.P;
   pr.ns_rows = ma.rows;
@@ -765,6 +774,11 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
   m.x = reinterpret_cast<__nv_bfloat16*>(x0);
 
   if (a->P > 65535) return fail(TP_EINVAL, "at most 65535 members per Muon call");
+  if (L.R_s / NS_TILE_M > 255 || (L.C_s + NS_TILE_N - 1) / NS_TILE_N > 255)
+    return fail(TP_EINVAL, "Muon matrices of at most 32640 x 65280 elements (got %d x %d)", a->max_out, a->max_in);
+  uint32_t* list_rr = reinterpret_cast<uint32_t*>(ws + L.off_list_rr);
+  uint32_t* list_rc = reinterpret_cast<uint32_t*>(ws + L.off_list_rc);
+  int* list_n = reinterpret_cast<int*>(ws + L.off_list_n);
   dim3 tiles((a->max_in + MUON_TN - 1) / MUON_TN, (a->max_out + MUON_TM - 1) / MUON_TM, a->P);
   dim3 ngrid((L.C_s + 255) / 256, (L.R_s + 31) / 32, a->P);
   {
@@ -773,6 +787,7 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
     muon_prologue_kernel<<<tiles, 256, 0, st>>>(m);
     muon_norm_kernel<<<a->P, 256, 0, st>>>(m, (int)tiles.x);
     muon_normalize_kernel<<<ngrid, 256, 0, st>>>(m, 128, 256);
+    ns_tile_list_kernel<<<1, 1024, 0, st>>>(m, list_rr, list_rc, list_n);
   }
   TP_CUDA_TRY(cudaGetLastError());
   // quintic Newton-Schulz, coefficients of optim.py:477
@@ -794,9 +809,11 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
     int* c2 = counter();
     int* c3 = counter();
     if (!c1 || !c2 || !c3) return fail(TP_ECUDA, "cudaMemsetAsync of the tile counters failed");
-    if ((rc = ns_gemm<MODE_NS>(m, 1, X, L.C_s, X, L.C_s, A, L.R_s, nullptr, 1.0f, 0.0f, c1, st))) return rc;
-    if ((rc = ns_gemm<MODE_NS>(m, 2, A, L.R_s, A, L.R_s, Bm, L.R_s, A, cc, cb, c2, st))) return rc;
-    if ((rc = ns_gemm<MODE_NS_BMN>(m, 3, Bm, L.R_s, X, L.C_s, Xn, L.C_s, X, 1.0f, ca, c3, st))) return rc;
+    if ((rc = ns_gemm<MODE_NS>(m, 1, X, L.C_s, X, L.C_s, A, L.R_s, nullptr, 1.0f, 0.0f, list_rr, list_n, c1, st)))
+      return rc;
+    if ((rc = ns_gemm<MODE_NS>(m, 2, A, L.R_s, A, L.R_s, Bm, L.R_s, A, cc, cb, list_rr, list_n, c2, st))) return rc;
+    if ((rc = ns_gemm<MODE_NS_BMN>(m, 3, Bm, L.R_s, X, L.C_s, Xn, L.C_s, X, 1.0f, ca, list_rc, list_n + 1, c3, st)))
+      return rc;
     std::swap(X, Xn);
   }
   m.x = reinterpret_cast<__nv_bfloat16*>(X);
