@@ -6,7 +6,7 @@
 //
 //   MODE_FWD    : C[B x out_m] = X[B x in_m] * W^T, + bias, ReLU, Philox dropout; A, B K-major
 //   MODE_FWD_ADD: the forward with an fp32 addend E[B x out_m] summed before the bias
-//   MODE_FWD_PAIR: the forward without dropout, on CTA pairs
+//   MODE_FWD_PAIR: the forward on CTA pairs (without dropout, or with a long K loop)
 //   MODE_DGRAD  : C[B x in_m] = G[B x out_m] * W; A K-major, B MN-major; CTA pairs
 //   MODE_WGRAD_T: C^T[in_m x out_m] = X^T * G stored into C (K = batch rows), A and B MN-major;
 //                 a warp's 32 lanes hold 32 consecutive input features, so each output

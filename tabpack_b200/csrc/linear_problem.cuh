@@ -20,8 +20,9 @@ enum : int { MODE_FWD = 0, MODE_DGRAD = 1, MODE_WGRAD = 2, MODE_NS = 3, MODE_NS_
 // (the gathered one-hot columns of a TabPack's first layer); its problems carry
 // mode = MODE_FWD, so tiles decode as the forward's.
 enum : int { MODE_FWD_ADD = 6 };
-// Kernel instantiation of the forward without dropout on CTA pairs (mode = MODE_FWD as well):
-// without the Philox draws its epilogue keeps up with the pair's faster k-blocks.
+// Kernel instantiation of the forward on CTA pairs (mode = MODE_FWD as well): used without
+// dropout (no Philox draws, so the epilogue keeps up with the pair's faster k-blocks) and for
+// long K loops, where operand delivery rather than the epilogue bounds a tile.
 enum : int { MODE_FWD_PAIR = 7 };
 // KIND_END marks the end of a CTA's tile sequence in the kernel's shared-memory tile ring.
 enum : int { KIND_MMA = 0, KIND_ZERO = 1, KIND_COPY = 2, KIND_SKIP = 3, KIND_END = 4 };

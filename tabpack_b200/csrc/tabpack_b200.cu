@@ -529,7 +529,11 @@ int linear_forward_impl(const tp_linear_args* a, const float* addend, int add_ld
     static_assert(Sm100Cfg<BN, MODE_FWD_ADD>::TILE_M == Cfg::TILE_M && Sm100Cfg<BN, MODE_FWD_ADD>::B_ROWS == Cfg::B_ROWS,
                   "the forward with an addend shares the forward's tiling");
     if (addend != nullptr) return launch_sm100<BN, MODE_FWD_ADD>(pr, ma, mb, st);
-    if (a->dropout_p == nullptr) {  // no Philox draws: the forward on CTA pairs (256-row tiles)
+    // CTA pairs (256-row tiles: a third less operand traffic per SM, more k-blocks in flight)
+    // when there are no Philox draws, or when the K loop is long enough that operand delivery
+    // rather than the dropout epilogue bounds the tile (a TabPack's first layer over its one-hot
+    // columns); the keep mask depends only on (member, row, column), so it is the same either way
+    if (a->dropout_p == nullptr || a->max_in >= 2048) {
       using CfgP = Sm100Cfg<BN, MODE_FWD_PAIR>;
       pr.BM = CfgP::TILE_M;
       pr.m_tiles = (a->B + CfgP::TILE_M - 1) / CfgP::TILE_M;

@@ -311,15 +311,15 @@ def _muon_group(opt: torch.optim.Optimizer, g: dict, *, workspaces: dict, allow_
     st = opt.state[p]
     if len(st) == 0:
         st['muon_momentum_buffer'] = torch.zeros_like(p)
+    # without in-place mutation the kernel leaves the gradient as it is (the reference blends
+    # into a copy), so no copy is made here
     grad = p.grad.data
-    if not allow_inplace_grad_mutation:
-        grad = grad.clone()
     scale = g.get('muon_update_scale')
     ops.muon_step(p, grad, st['muon_momentum_buffer'], out_features=g.get('muon_out_features'),
                   in_features=g.get('muon_in_features'), lr=_hp(g['muon_lr']), momentum=_hp(g['muon_momentum']),
                   weight_decay=_hp(g['weight_decay']),
                   update_scale=None if scale is None else scale.to(torch.float32).contiguous(),
-                  nesterov=bool(g['muon_nesterov']), mutate_grad=True,
+                  nesterov=bool(g['muon_nesterov']), mutate_grad=allow_inplace_grad_mutation,
                   ns_steps=int(g['muon_newton_schulz_steps']), workspace=_muon_workspace(workspaces, p))
 
 

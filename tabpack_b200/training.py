@@ -268,7 +268,7 @@ class PackTrainer:
             decay, no_decay = split_weight_decay(self.model)
             groups.append({'params': [p for p in no_decay if id(p) not in muon_params], 'weight_decay': 0.0})
             groups.append({'params': [p for p in decay if id(p) not in muon_params]})
-            self.opt = MuonAdamWPack(groups, pack_size=hi - lo, allow_inplace_grad_mutation=True, **okw)
+            self.opt = MuonAdamWPack(groups, pack_size=hi - lo, allow_inplace_grad_mutation=False, **okw)
         elif otype == 'adamw':
             wd, nd = split_weight_decay(self.model)
             self.opt = AdamWPack([{'params': nd, 'weight_decay': 0.0}, {'params': wd}], pack_size=hi - lo, **okw)

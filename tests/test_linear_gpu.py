@@ -245,6 +245,52 @@ def test_full_size_layer_against_torch_fp32(dropout):
         torch.backends.cuda.matmul.allow_tf32 = tf32
 
 
+def test_long_k_forward_with_dropout_on_cta_pairs():
+    """A forward with dropout whose K loop is long (2544 padded inputs, 2538 valid, as in a
+    TabPack's first layer over its one-hot columns) runs on CTA pairs: every member's output
+    against plain PyTorch fp32 on the same bf16 values with the library's keep mask, that mask
+    bit-exact against the oracle's Philox for sampled members, exact zeros in the padding."""
+    from tabpack_b200 import ops
+
+    P, B, K, N = 24, 1024, 2544, 1024
+    rng = np.random.default_rng(77)
+    out_np = rng.integers(16, 129, P) * 8
+    p_np = rng.uniform(0, 0.5, P).astype(np.float32)
+    outf = torch.from_numpy(out_np.astype(np.int32)).cuda()
+    inf = torch.full((P,), 2538, dtype=torch.int32, device='cuda')
+    p = torch.from_numpy(p_np).cuda()
+    g = torch.Generator(device='cuda').manual_seed(77)
+    bound = 1.0 / math.sqrt(2538)
+    kin = (torch.arange(K, device='cuda') < 2538)
+    x = (torch.randn(P, B, K, device='cuda', generator=g) * kin).bfloat16()
+    w = ((torch.rand(P, N, K, device='cuda', generator=g) * 2 - 1) * bound * kin).bfloat16()
+    b = (torch.rand(P, N, device='cuda', generator=g) * 2 - 1) * bound
+    seed, offset, base = 99, 3, 5
+    y = ops.linear_forward(x, w, b, in_features=inf, out_features=outf, relu=True, dropout_p=p, seed=seed,
+                           offset=offset, member_base=base)
+    keep = ops.dropout_mask(seed=seed, offset=offset, member_base=base, p=p, rows=B, cols=N)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    for m in (0, P - 1, int(np.argmin(out_np))):
+        want = dropout_keep_mask(seed=seed, offset=offset, members=np.array([m + base]), n_rows=B, n_cols=N,
+                                 p=p_np[m:m + 1])[0]
+        assert np.array_equal(keep[m].cpu().numpy().astype(bool), want), f'keep mask of member {m}'
+    scale = torch.from_numpy(keep_scale(p_np)).cuda()
+    col = torch.arange(N, device='cuda')
+    tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for c in range(0, P, 8):
+            s = slice(c, c + 8)
+            valid = (col[None, :] < outf[s, None])[:, None, :]
+            mv = keep[s].float() * scale[s, None, None] * valid
+            pre = torch.matmul(x[s].float(), w[s].float().transpose(1, 2)) + b[s, None, :]
+            _close_dev(y[s], torch.relu(pre) * mv, BF16_RTOL, f'y members {c}..{c + 7}')
+            assert int(torch.count_nonzero(y[s] * ~valid)) == 0
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = tf32
+
+
 @pytest.mark.parametrize('dropout', [True, False])
 def test_depth_gating_many_tiles_per_cta(dropout):
     """128 members x 2048 rows x 512, a third of them past their depth (COPY tiles mixed with
