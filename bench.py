@@ -79,6 +79,26 @@ def load_peaks() -> tuple[dict, str]:
     return {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0, 'bf16_tflops_sustained': 1400.0}, 'fallback'
 
 
+def dist_init(dev, seconds: int = 300) -> int:
+    """Joins the NCCL process group once (torchrun's env); returns the world size."""
+    import datetime
+
+    import torch.distributed as dist
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group('nccl', device_id=dev, timeout=datetime.timedelta(seconds=seconds))
+    return world
+
+
+def dist_done(emit: bool) -> None:
+    """Leaves the process group after a workload that printed its own line."""
+    import torch.distributed as dist
+
+    if emit and dist.is_initialized():
+        dist.destroy_process_group()
+
+
 # ----------------------------------------------------------------------------- CPU legs
 
 
@@ -196,21 +216,19 @@ class ClockSampler:
 # ----------------------------------------------------------------------------- GPU leg
 
 
-def run_b200(args) -> None:
+def run_b200(args, emit: bool = True) -> dict | None:
+    """The layer workload (one packed MLP block forward + backward); prints its JSON line (rank
+    0) or, with emit=False, returns it (rank 0; None elsewhere)."""
     import torch
     import torch.distributed as dist
 
     from tabpack_b200 import _lib
 
-    world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local = int(os.environ.get('LOCAL_RANK', '0'))
     torch.cuda.set_device(local)
     dev = torch.device('cuda', local)
-    if world > 1:
-        import datetime
-
-        dist.init_process_group('nccl', device_id=dev, timeout=datetime.timedelta(seconds=120))
+    world = dist_init(dev)
     lib = _lib.load()
 
     base = rank * MEMBERS
@@ -357,9 +375,8 @@ def run_b200(args) -> None:
                            f'{peak_kind} ({peak_key(clk)}: median SM clock {clk["sm_mhz"]} of {clk["sm_max_mhz"]} MHz)')
 
     if rank != 0:
-        if world > 1:
-            dist.destroy_process_group()
-        return
+        dist_done(emit)
+        return None
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -384,9 +401,10 @@ def run_b200(args) -> None:
         'gpu_launches': 4 * args.steps,
         'clocks': clk,
     }
-    print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    if emit:
+        print(json.dumps(line), flush=True)
+    dist_done(emit)
+    return line
 
 
 # DRAM bytes (read + write) per full-size launch, from the ncu capture of the layer kernels
@@ -399,18 +417,27 @@ TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
 }
 
 
-def run_optimizer(args) -> None:
+def run_optimizer(args, emit: bool = True) -> dict | None:
     """Grouped optimizer step: `members` x 3 weight matrices with rows and cols ~ U{64..1024
     step 16} (entries N(0, 0.02^2), gradients N(0, 1e-3^2)), one Muon group per matrix with
     5 Newton-Schulz iterations and the update scale sqrt(max(1, out/in)), plus one grouped
     AdamW launch over the matrices' bias vectors; per-member lr log-U[1e-4, 1e-2], weight
-    decay log-U[1e-6, 1e-2], beta2 U[0.95, 0.999]."""
+    decay log-U[1e-6, 1e-2], beta2 U[0.95, 0.999].  Also timed at this size: the Muon
+    elementwise kernels (library profiler, 28 B per weight element: momentum, Nesterov blend,
+    bf16 operand, normalisation, update) and a grouped AdamW step over the three weight packs
+    themselves (28 B per element), each against the measured copy bandwidth.  Under torchrun
+    every rank runs the whole workload on its own GPU (replicas); times are the max over
+    ranks."""
     import torch
+    import torch.distributed as dist
 
     from tabpack_b200 import ops
 
-    dev = torch.device('cuda', 0)
-    torch.cuda.set_device(dev)
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    world = dist_init(dev)
     P = args.members
     rng = np.random.default_rng(5)
     groups = []
@@ -447,7 +474,6 @@ def run_optimizer(args) -> None:
     for b in biases:
         b['m'], b['v'] = torch.zeros_like(b['p']), torch.zeros_like(b['p'])
     adamw_elems = sum(b['p'].numel() for b in biases)
-    adamw_ms = []
 
     def step(i=0, ev=None):
         for gr in groups:
@@ -462,12 +488,17 @@ def run_optimizer(args) -> None:
         if ev is not None:
             ev[1].record()
 
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
     for i in range(args.warmup):
         step(i)
-    torch.cuda.synchronize()
+    barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     aev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
-    with ClockSampler(0) as clocks:
+    with ClockSampler(local) as clocks:
         e0.record()
         for i in range(args.steps):
             step(args.warmup + i, aev[i])
@@ -475,21 +506,74 @@ def run_optimizer(args) -> None:
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     adamw_ms = statistics.mean(a.elapsed_time(b) for a, b in aev)
+    # the Muon elementwise kernels and the Newton-Schulz GEMMs, launch by launch
+    with ops.KernelTimes() as kt:
+        step(args.warmup + args.steps)
+    muon_el_ms = kt.ms['muon_elementwise']
+    ns_ms = kt.ms['newton_schulz_gram'] + kt.ms['newton_schulz_update']
+    # AdamW over the weight packs themselves (what an AdamW optimizer pack would run on them);
+    # the Muon momentum buffers serve as first moments
+    for b in biases:
+        del b['v']
+    vs = [torch.zeros_like(gr['p']) for gr in groups]
+    big = dict(params=[gr['p'] for gr in groups], grads=[gr['grad'] for gr in groups],
+               exp_avgs=[gr['m'] for gr in groups], exp_avg_sqs=vs)
+    big_elems = sum(gr['p'].numel() for gr in groups)
+
+    def adamw_big(i):
+        ops.adamw_step(big['params'], big['grads'], big['exp_avgs'], big['exp_avg_sqs'], step=i + 1, lr=lr,
+                       beta1=0.9, beta2=beta2, eps=1e-8, weight_decay=wd)
+
+    adamw_big(0)
+    torch.cuda.synchronize()
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record()
+    for i in range(args.steps):
+        adamw_big(1 + i)
+    b1.record()
+    torch.cuda.synchronize()
+    adamw_big_ms = b0.elapsed_time(b1) / args.steps
+    t = torch.tensor([ms, adamw_ms, muon_el_ms, ns_ms, adamw_big_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, adamw_ms, muon_el_ms, ns_ms, adamw_big_ms = (float(v) for v in t)
+    del groups, biases, big, vs
+    if rank != 0:
+        dist_done(emit)
+        return None
     peaks, kind = load_peaks()
+    clk = clocks.summary()
+    sustained = peak_key(clk) == 'bf16_tflops_sustained'
+    peak = peaks[peak_key(clk)]
     ach = flops / (ms / 1e3) / 1e12
-    print(json.dumps({
+    hbm = peaks['hbm_gbs']
+
+    def gbs(nbytes, t_ms):
+        v = nbytes / (t_ms / 1e3) / 1e9
+        return {'ms': t_ms, 'gbs': v, 'hbm_frac': v / hbm}
+
+    line = {
         'metric': 'grouped Muon optimizer step (3 ragged matrices per member)', 'value': 3 * P / (ms / 1e3),
-        'unit': 'matrices/s', 'ms_per_step': ms, 'steps': args.steps, 'warmup': args.warmup,
+        'unit': 'matrices/s', 'n_gpus': world, 'ms_per_step': ms, 'steps': args.steps, 'warmup': args.warmup,
+        'higher_is_better': True, 'scaling': 'weak', 'dtype': 'bf16', 'data': 'synthetic',
         'config': {'workload': f'{P} members x 3 matrices, rows/cols U{{64..1024 step 16}}, 5 Newton-Schulz '
-                               'iterations; AdamW on the 3 bias vectors',
+                               'iterations; AdamW on the 3 bias vectors' +
+                               (f'; one replica per GPU' if world > 1 else ''),
                    'ns_tflop_per_step': flops / 1e12, 'elements': elems,
-                   'adamw': {'ms': adamw_ms, 'elements': adamw_elems,
-                             'gbs': 28.0 * adamw_elems / (adamw_ms / 1e3) / 1e9,
-                             'hbm_frac': 28.0 * adamw_elems / (adamw_ms / 1e3) / 1e9 / peaks['hbm_gbs']}},
-        'roofline': {'bound': 'tensor', 'achieved': ach, 'peak': peaks['bf16_tflops_sustained'], 'unit': 'TFLOP/s',
-                     'frac': ach / peaks['bf16_tflops_sustained'], 'peak_source': f'{kind} (sustained)',
+                   'newton_schulz': {'ms': ns_ms, 'tflops': flops / (ns_ms / 1e3) / 1e12,
+                                     'frac': flops / (ns_ms / 1e3) / 1e12 / peak},
+                   'muon_elementwise': dict(gbs(28.0 * elems, muon_el_ms), bytes_per_element=28),
+                   'adamw_biases': dict(gbs(28.0 * adamw_elems, adamw_ms), elements=adamw_elems),
+                   'adamw_weight_packs': dict(gbs(28.0 * big_elems, adamw_big_ms), elements=big_elems)},
+        'roofline': {'bound': 'tensor', 'achieved': ach, 'peak': peak, 'unit': 'TFLOP/s', 'frac': ach / peak,
+                     'peak_source': f'{kind} ({"sustained" if sustained else "burst"}: median SM clock '
+                                    f'{clk["sm_mhz"]} of {clk["sm_max_mhz"]} MHz)',
                      'note': 'whole step (elementwise + Newton-Schulz) time against Newton-Schulz FLOPs'},
-        'clocks': clocks.summary()}), flush=True)
+        'clocks': clk}
+    if emit:
+        print(json.dumps(line), flush=True)
+    dist_done(emit)
+    return line
 
 
 def run_metrics(args) -> None:
@@ -619,6 +703,46 @@ def member_cost(pm: dict, d_in: int) -> float:
     return sum(train_work([pm], d_in).values())
 
 
+def _compact(line: dict) -> dict:
+    """The figures of another workload's JSON line that the training line carries."""
+    keep = ('workload', 'per_kernel_ms', 'ragged_tflop_per_step_per_gpu', 'ragged_tflops_achieved',
+            'ns_tflop_per_step', 'newton_schulz', 'muon_elementwise', 'adamw_biases', 'adamw_weight_packs',
+            'member_rows_per_s', 'ragged_tflops', 'frac_of_sustained_bf16', 'head_checksum')
+    out = {k: line[k] for k in ('metric', 'value', 'unit', 'ms_per_step', 'steps', 'warmup', 'scaling')
+           if k in line}
+    out['config'] = {k: v for k, v in line.get('config', {}).items() if k in keep}
+    for k in ('roofline', 'e2e', 'clocks'):
+        if line.get(k) is not None:
+            out[k] = line[k]
+    return out
+
+
+def run_other_configs(args) -> dict:
+    """The other benchmark configurations, measured after the training region in the same run
+    (every rank takes part; short step counts): the ragged GEMM layer (256 members per GPU), the
+    grouped optimizer step (1024 members, one replica per GPU) and packed inference (1024
+    members over all GPUs, all-reduced ensemble head).  Returns compact results (rank 0)."""
+    import torch
+
+    global MEMBERS
+    out = {}
+    runs = (('ragged_gemm_layer', run_b200, 256, 50, 5), ('grouped_optimizer', run_optimizer, 1024, 5, 2),
+            ('packed_inference', run_inference, 1024, 3, 1))
+    saved = MEMBERS
+    for name, fn, members, steps, warmup in runs:
+        sub = argparse.Namespace(**vars(args))
+        sub.members, sub.steps, sub.warmup, sub.no_cpu_baseline = members, steps, warmup, True
+        MEMBERS = members
+        try:
+            line = fn(sub, emit=False)
+        finally:
+            MEMBERS = saved
+        torch.cuda.empty_cache()
+        if line is not None:
+            out[name] = _compact(line)
+    return out
+
+
 def run_train(args) -> None:
     """Full TabPack training of the full-training configuration, members sharded over the GPUs.
 
@@ -732,8 +856,13 @@ def run_train(args) -> None:
 
     checksum = {'sha256_16': hashlib.sha256(final.tobytes()).hexdigest()[:16], 'sum': float(final.astype(np.float64).sum())}
     local_work = train_work(per[trainer.lo: trainer.hi], d_in)
+    members_per_rank = [b - a for a, b in trainer.ranges]
     fam_ms = {k: kt.ms[k] / K for k in kt.ms if kt.launches[k]}
     fam_ms['newton_schulz'] = fam_ms.pop('newton_schulz_gram', 0.0) + fam_ms.pop('newton_schulz_update', 0.0)
+    mean_loss = float(loss.mean())
+    del trainer, dev_data, pinned, up, warm, preds, preds_e2e, ens, loss
+    torch.cuda.empty_cache()
+    other = {} if args.no_other_configs else run_other_configs(args)
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
@@ -770,12 +899,12 @@ def run_train(args) -> None:
                                f'timed: {K} steps + the epoch end over {val_rows} validation rows (all-gather + '
                                f'greedy ensemble)' + (', cosine numerical embeddings' if args.embeddings == 'cosine'
                                                       else ''),
-                   'members': P, 'members_per_rank': [b - a for a, b in trainer.ranges],
+                   'members': P, 'members_per_rank': members_per_rank,
                    'parallelism': f'member-sharded x{world} (ranges balanced by FLOPs per step)',
                    'train_ms_per_step': train_ms / K, 'epoch_end_ms': region_ms - train_ms,
                    'l2': 'weights and optimizer state exceed L2 (about 40 GB at 512 members)',
                    'per_kernel_ms_per_step': fam_ms, 'gemm': gemm, 'checksum': checksum,
-                   'mean_train_loss': float(loss.mean())},
+                   'mean_train_loss': mean_loss, 'other_configs': other},
         'roofline': roof,
         'cpu_baseline': cpu,
         'e2e': {'value': samples / (e2e_ms / 1e3), 'unit': 'member-samples/s',
@@ -852,7 +981,7 @@ def run_train_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def run_inference(args) -> None:
+def run_inference(args, emit: bool = True) -> dict | None:
     """Inference of the packed-ensemble inference configuration: `members` members over all
     ranks (1024 by default; rank r predicts its share), depth U{2,3}, width U{256..1024 step
     8}, 200 numerical features N(0, 1), a 10-class head, batches of 65 536 rows in bf16.  A step
@@ -867,13 +996,11 @@ def run_inference(args) -> None:
 
     from tabpack_b200.training import PackPredictor, PackTrainer
 
-    world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local = int(os.environ.get('LOCAL_RANK', '0'))
     torch.cuda.set_device(local)
     dev = torch.device('cuda', local)
-    if world > 1:
-        dist.init_process_group('nccl', device_id=dev, timeout=datetime.timedelta(seconds=120))
+    world = dist_init(dev)
     total, B, n_num, C = args.members, 65536, 200, 10
     rng = np.random.default_rng(31)
     per = [dict(n_blocks=int(rng.integers(2, 4)), d_block=int(rng.integers(32, 129)) * 8, dropout=0.0)
@@ -934,8 +1061,9 @@ def run_inference(args) -> None:
         dist.all_reduce(flops)
     peaks, kind = load_peaks()
     tflops = float(flops[0]) / (ms / 1e3) / 1e12
+    line = None
     if rank == 0:
-        print(json.dumps({
+        line = {
             'metric': 'rows/sec inference (every member of the pack, ensemble head)', 'value': B / (ms / 1e3),
             'unit': 'rows/s', 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms,
             'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
@@ -946,9 +1074,12 @@ def run_inference(args) -> None:
                        'head_checksum': float(head.double().sum())},
             'e2e': {'value': B / (e2e_ms / 1e3), 'unit': 'rows/s', 'h2d_bytes_per_step': x.numel() * 4,
                     'd2h_bytes_per_step': B * C * 4},
-            'clocks': clocks.summary()}), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+            'clocks': clocks.summary()}
+        if emit:
+            print(json.dumps(line), flush=True)
+    del trainer, predictor
+    dist_done(emit)
+    return line
 
 
 def run_onehot(args) -> None:
@@ -1049,6 +1180,8 @@ def main() -> None:
                          '(default); layer: one packed MLP block forward+backward; optimizer: grouped Muon step; '
                          'metrics: validation metrics, ROC AUC and greedy selection; inference: packed predictor; '
                          'onehot: the one-hot first layer piece by piece')
+    ap.add_argument('--no-other-configs', action='store_true',
+                    help='train workload: skip the other configurations measured after the training region')
     ap.add_argument('--embeddings', choices=['none', 'cosine'], default='none',
                     help='train workload: numerical features raw or through cosine embeddings')
     args = ap.parse_args()

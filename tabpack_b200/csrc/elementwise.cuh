@@ -205,12 +205,12 @@ struct AdamWScalars {
   const float* eps;
   const float* wd;
   float lr_s, beta1_s, beta2_s, eps_s, wd_s;
-  // host-precomputed values for the all-scalar case (the reference computes
-  // them in Python double precision)
+  // host-precomputed values (the reference computes them in Python double precision)
   int wd_on;               // 0: `_make_weight_decay_multiplier` returned None
   float wd_mult_s;         // 1 - lr*wd (all scalar)
   float one_m_b1_s, one_m_b2_s;
-  int scalar_bias_corr;    // betas scalar and step scalar
+  int bc1_scalar;          // beta1 and step scalar: bc1_s holds 1 - beta1^step
+  int bc2_scalar;          // beta2 and step scalar: sqrt_bc2_s holds sqrt(1 - beta2^step)
   float bc1_s;             // 1 - beta1^step
   float step_size_s;       // lr / (1 - beta1^step), used iff lr also scalar
   float sqrt_bc2_s;        // sqrt(1 - beta2^step)
@@ -218,55 +218,107 @@ struct AdamWScalars {
 };
 
 __device__ __forceinline__ float lerp_t(float a, float b, float w) {
-  // torch's lerp: a + w (b - a) for |w| < 0.5, else b - (b - a)(1 - w)
-  const float d = b - a;
-  return fabsf(w) < 0.5f ? a + w * d : b - d * (1.0f - w);
+  // torch's lerp: a + w (b - a) for |w| < 0.5, else b - (b - a)(1 - w), each as one fused
+  // multiply-add (fma(w, d, a) or fma(w - 1, d, b)) as torch's CPU kernel forms it; explicit
+  // intrinsics so that the compiler fuses nothing else
+  const float d = __fsub_rn(b, a);
+  return fabsf(w) < 0.5f ? __fmaf_rn(w, d, a) : __fmaf_rn(__fsub_rn(w, 1.0f), d, b);
 }
 
 struct AdamWTensors {
   tp_opt_tensor t[TP_MAX_OPT_TENSORS];
 };
 
-__global__ void __launch_bounds__(256) adamw_kernel(const AdamWTensors ts, const AdamWScalars s) {
-  const tp_opt_tensor& T = ts.t[blockIdx.y];
-  const int64_t n = T.numel;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int m = (int)(i / T.inner);
-    const float lr = s.lr ? s.lr[m] : s.lr_s;
-    const float b1 = s.beta1 ? s.beta1[m] : s.beta1_s;
-    const float b2 = s.beta2 ? s.beta2[m] : s.beta2_s;
-    const float eps = s.eps ? s.eps[m] : s.eps_s;
-    float p = T.p[i];
-    const float g = T.grad[i];
-    float mm = T.exp_avg[i];
-    float v = T.exp_avg_sq[i];
-    if (s.wd_on) {
-      const float mult = (s.lr || s.wd) ? 1.0f - lr * (s.wd ? s.wd[m] : s.wd_s) : s.wd_mult_s;
-      p = p * mult;
+// One element's AdamW update with its member's coefficients, rounded step by step as the
+// reference's torch ops round (src/tabpackage/optim.py:400-427 on the CPU): each op's result
+// is rounded to fp32; torch's lerp is one fused multiply-add, fma(w or w - 1, end - self,
+// self or end); addcmul is fma(value * t1, t2, self); addcdiv is self + (value * t1) / t2.
+// The intrinsics keep the compiler from fusing anything else.
+struct AdamWMember {
+  float mult, one_m_b1, b2, one_m_b2, step_size, sqrt_bc2, eps;
+  bool wd_on, b2_pm, step_float;
+};
+
+__device__ __forceinline__ void adamw_elem(const AdamWMember& c, float& p, float g, float& mm, float& v) {
+  if (c.wd_on) p = __fmul_rn(p, c.mult);                                   // p.mul_(1 - lr * wd)
+  mm = lerp_t(mm, g, c.one_m_b1);                                       // exp_avg.lerp_(grad, 1 - beta1)
+  if (c.b2_pm)
+    v = lerp_t(v, __fmul_rn(g, g), c.one_m_b2);                         // exp_avg_sq.lerp_(grad^2, 1 - beta2)
+  else
+    v = __fmaf_rn(__fmul_rn(c.one_m_b2, g), g, __fmul_rn(v, c.b2));         // .mul_(beta2).addcmul_(g, g, 1 - beta2)
+  const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), c.sqrt_bc2), c.eps);
+  if (c.step_float)
+    p = __fadd_rn(p, __fdiv_rn(__fmul_rn(-c.step_size, mm), denom));       // p.addcdiv_(m, denom, -step)
+  else
+    p = __fsub_rn(p, __fmul_rn(__fdiv_rn(mm, denom), c.step_size));         // p.add_((m / denom) * step, alpha=-1)
+}
+
+// Grid: (chunks of a member's elements, members, tensors), 256 threads.  Member m =
+// member0 + blockIdx.y of tensor blockIdx.z owns elements [m * inner, (m + 1) * inner); its
+// coefficients are formed once per thread, and 16-byte loads (four elements) keep enough
+// bytes in flight when inner is a multiple of 4.
+__global__ void __launch_bounds__(256) adamw_kernel(const AdamWTensors ts, const AdamWScalars s, int member0) {
+  const tp_opt_tensor& T = ts.t[blockIdx.z];
+  const int64_t inner = T.inner;
+  const int m = member0 + (int)blockIdx.y;
+  const int64_t base = (int64_t)m * inner;
+  if (base >= T.numel) return;
+  const float lr = s.lr ? s.lr[m] : s.lr_s;
+  const float b1 = s.beta1 ? s.beta1[m] : s.beta1_s;
+  const float b2 = s.beta2 ? s.beta2[m] : s.beta2_s;
+  AdamWMember c;
+  c.eps = s.eps ? s.eps[m] : s.eps_s;
+  c.wd_on = s.wd_on != 0;
+  // 1 - lr * wd as torch forms it from per-member tensors (two roundings), or the host's
+  c.mult = (s.lr || s.wd) ? __fsub_rn(1.0f, __fmul_rn(lr, s.wd ? s.wd[m] : s.wd_s)) : s.wd_mult_s;
+  c.one_m_b1 = s.beta1 ? __fsub_rn(1.0f, b1) : s.one_m_b1_s;
+  c.b2_pm = s.beta2 != nullptr;
+  c.b2 = b2;
+  c.one_m_b2 = s.beta2 ? __fsub_rn(1.0f, b2) : s.one_m_b2_s;
+  const bool step_scalar = T.step == nullptr;
+  const float st = (float)(step_scalar ? s.step : T.step[m]);
+  // step_size is a Python float in the reference iff lr, beta1 and the step are scalars
+  c.step_float = !s.lr && s.bc1_scalar && step_scalar;
+  if (c.step_float)
+    c.step_size = s.step_size_s;
+  else if (s.bc1_scalar && step_scalar)
+    c.step_size = __fdiv_rn(lr, s.bc1_s);
+  else
+    c.step_size = __fdiv_rn(lr, __fsub_rn(1.0f, powf(b1, st)));
+  c.sqrt_bc2 = (s.bc2_scalar && step_scalar) ? s.sqrt_bc2_s : __fsqrt_rn(__fsub_rn(1.0f, powf(b2, st)));
+  float* P = T.p + base;
+  const float* G = T.grad + base;
+  float* M = T.exp_avg + base;
+  float* V = T.exp_avg_sq + base;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t len = min(inner, T.numel - base);  // the last member of a ragged tensor may be short
+  const bool vec = ((inner | len) & 3) == 0 && ((reinterpret_cast<uintptr_t>(T.p) | reinterpret_cast<uintptr_t>(T.grad) |
+                                         reinterpret_cast<uintptr_t>(T.exp_avg) |
+                                         reinterpret_cast<uintptr_t>(T.exp_avg_sq)) & 15u) == 0;
+  if (vec) {
+    const int64_t n4 = len >> 2;
+    for (int64_t i = t0; i < n4; i += stride) {
+      float4 p = reinterpret_cast<const float4*>(P)[i];
+      const float4 g = __ldg(reinterpret_cast<const float4*>(G) + i);
+      float4 mm = reinterpret_cast<const float4*>(M)[i];
+      float4 v = reinterpret_cast<const float4*>(V)[i];
+      adamw_elem(c, p.x, g.x, mm.x, v.x);
+      adamw_elem(c, p.y, g.y, mm.y, v.y);
+      adamw_elem(c, p.z, g.z, mm.z, v.z);
+      adamw_elem(c, p.w, g.w, mm.w, v.w);
+      reinterpret_cast<float4*>(P)[i] = p;
+      reinterpret_cast<float4*>(M)[i] = mm;
+      reinterpret_cast<float4*>(V)[i] = v;
     }
-    mm = lerp_t(mm, g, s.beta1 ? 1.0f - b1 : s.one_m_b1_s);
-    if (s.beta2) {
-      v = lerp_t(v, g * g, 1.0f - b2);
-    } else {
-      v = v * b2;
-      v = v + (s.one_m_b2_s * g) * g;
+  } else {
+    for (int64_t i = t0; i < len; i += stride) {
+      float p = P[i], mm = M[i], v = V[i];
+      adamw_elem(c, p, G[i], mm, v);
+      P[i] = p;
+      M[i] = mm;
+      V[i] = v;
     }
-    float step_size, sqrt_bc2;
-    if (s.scalar_bias_corr && T.step == nullptr) {
-      step_size = s.lr ? lr / s.bc1_s : s.step_size_s;
-      sqrt_bc2 = s.sqrt_bc2_s;
-    } else {
-      const float st = (float)(T.step ? T.step[m] : s.step);
-      const float bc1 = 1.0f - powf(b1, st);
-      const float bc2 = 1.0f - powf(b2, st);
-      step_size = lr / bc1;
-      sqrt_bc2 = sqrtf(bc2);
-    }
-    const float denom = sqrtf(v) / sqrt_bc2 + eps;
-    p = p - step_size * (mm / denom);
-    T.p[i] = p;
-    T.exp_avg[i] = mm;
-    T.exp_avg_sq[i] = v;
   }
 }
 

@@ -542,24 +542,30 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
           __syncwarp();
         };
         if constexpr (MODE == MODE_NS || MODE == MODE_NS_BMN) {
-          // the addend of chunk c + 1 is loaded while chunk c is computed
+          // Chunks past the member's columns rounded up to a k-block (64) are never read: no
+          // later GEMM's K loop reaches them, and as M / N rows they only feed outputs that are
+          // written as zeros.  Two chunks' accumulators are loaded per TMEM wait; the addend of
+          // the next pair is loaded while this pair is computed.
           const bool rv = row < ti.m_valid;
-          uint32_t na[32];
+          const int nch_k = min(nch, max(0, (((ti.n_valid + 63) & ~63) - cbase + 31) / 32));
+          uint32_t na[32], nb[32];
 #pragma unroll 1
-          for (int c = 0; c < nch; c += 2) {
+          for (int c = 0; c < nch_k; c += 2) {
             const int col0 = cbase + 32 * c;
+            const bool two = c + 1 < nch_k;
             tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * c), na);
-            if (c + 1 < nch) ns_load_d(d_row, col0 + 32, ti.n_valid - col0 - 32, d_b);
+            if (two) {
+              tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * (c + 1)), nb);
+              ns_load_d(d_row, col0 + 32, ti.n_valid - col0 - 32, d_b);
+            }
             tmem_wait_ld();
             ns_chunk(pr, rv, ti.n_valid - col0, na, d_a, stage_row);
             __syncwarp();
             stage_flush(pr, m, row_base, col0, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
             __syncwarp();
-            if (c + 1 < nch) {
-              tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * (c + 1)), na);
-              if (c + 2 < nch) ns_load_d(d_row, col0 + 64, ti.n_valid - col0 - 64, d_a);
-              tmem_wait_ld();
-              ns_chunk(pr, rv, ti.n_valid - col0 - 32, na, d_b, stage_row);
+            if (two) {
+              if (c + 2 < nch_k) ns_load_d(d_row, col0 + 64, ti.n_valid - col0 - 64, d_a);
+              ns_chunk(pr, rv, ti.n_valid - col0 - 32, nb, d_b, stage_row);
               __syncwarp();
               stage_flush(pr, m, row_base, col0 + 32, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
               __syncwarp();

@@ -1299,13 +1299,14 @@ int tp_adamw_step(const tp_adamw_args* a, void* stream) {
   TP_PROF(TP_PROF_ADAMW, static_cast<cudaStream_t>(stream));
   if (!a || a->n_tensors <= 0 || a->n_tensors > TP_MAX_OPT_TENSORS) return fail(TP_EINVAL, "bad tensor count");
   AdamWTensors ts{};
-  int64_t max_numel = 0;
+  int64_t max_inner = 0, max_members = 0;
   for (int i = 0; i < a->n_tensors; ++i) {
     const tp_opt_tensor& t = a->t[i];
     if (!t.p || !t.grad || !t.exp_avg || !t.exp_avg_sq || t.numel <= 0 || t.inner <= 0)
       return fail(TP_EINVAL, "tensor %d: null pointer or empty", i);
     ts.t[i] = t;
-    max_numel = std::max(max_numel, t.numel);
+    max_inner = std::max(max_inner, t.inner);
+    max_members = std::max(max_members, (t.numel + t.inner - 1) / t.inner);
   }
   AdamWScalars s{};
   s.lr = a->lr.per_member;
@@ -1324,19 +1325,22 @@ int tp_adamw_step(const tp_adamw_args* a, void* stream) {
   s.wd_mult_s = (float)(1.0 - a->lr.scalar * a->weight_decay.scalar);
   s.one_m_b1_s = (float)(1.0 - a->beta1.scalar);
   s.one_m_b2_s = (float)(1.0 - a->beta2.scalar);
-  s.scalar_bias_corr = !a->beta1.per_member && !a->beta2.per_member;
+  s.bc1_scalar = !a->beta1.per_member;
+  s.bc2_scalar = !a->beta2.per_member;
   s.step = a->step;
-  if (s.scalar_bias_corr) {
+  if (s.bc1_scalar) {
     const double bc1 = 1.0 - std::pow(a->beta1.scalar, (double)a->step);
-    const double bc2 = 1.0 - std::pow(a->beta2.scalar, (double)a->step);
     s.bc1_s = (float)bc1;
     s.step_size_s = (float)(a->lr.scalar / bc1);
-    s.sqrt_bc2_s = (float)std::sqrt(bc2);
   }
-  const int bx = (int)std::min<int64_t>((max_numel + 255) / 256, 2048);
-  dim3 grid(bx, a->n_tensors);
-  adamw_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(ts, s);
-  TP_CUDA_TRY(cudaGetLastError());
+  if (s.bc2_scalar) s.sqrt_bc2_s = (float)std::sqrt(1.0 - std::pow(a->beta2.scalar, (double)a->step));
+  // blocks per member: up to 4 elements per thread per block pass, at most 64 blocks
+  const int bx = (int)std::min<int64_t>((max_inner + 1023) / 1024, 64);
+  for (int64_t m0 = 0; m0 < max_members; m0 += 65535) {
+    dim3 grid(bx, (unsigned)std::min<int64_t>(65535, max_members - m0), a->n_tensors);
+    adamw_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(ts, s, (int)m0);
+    TP_CUDA_TRY(cudaGetLastError());
+  }
   return TP_OK;
 }
 

@@ -200,3 +200,106 @@ def test_muon_normalisation_quotient_equals_cuda_division():
     assert n > 1_000_000_000
     assert m16 == 0  # what the normalisation stores agrees bit for bit, the sign of zero included
     assert m32 < 0.01 * n
+
+
+def _adamw_expected(p, g, m, v, *, lr, beta1, beta2, eps, wd, step):
+    """The reference's AdamW ops (optim.py:400-427) one fp32 rounding at a time, on the CPU
+    in float64 with explicit rounding to fp32: torch's lerp as fma(w or w - 1, end - self,
+    self or end), addcmul as fma(value * g, g, v * beta2), addcdiv as p + (value * m) / denom
+    when the step size is a Python float, p - (m / denom) * step otherwise; square root and
+    division correctly rounded.  A fused multiply-add is evaluated exactly in float64 (the
+    product of two fp32 values is exact there) and rounded once more to fp32; that second
+    rounding could differ from a single one only at an fp32 tie, which these random values
+    do not produce.  Hyperparameters are floats or (P,) fp32 tensors; step an int or (P,)."""
+    f = lambda t: t.to(torch.float32)  # noqa: E731
+    d = lambda t: t.to(torch.float64)  # noqa: E731
+    P = p.shape[0]
+    shape = (P,) + (1,) * (p.ndim - 1)
+    col = lambda x: x.reshape(shape) if isinstance(x, torch.Tensor) else x  # noqa: E731
+
+    def fma(a, b, c):
+        return f(d(a) * d(b) + d(c))
+
+    def lerp(a, b, w):
+        w = w if isinstance(w, torch.Tensor) else torch.tensor(w, dtype=torch.float32)
+        w = torch.broadcast_to(w, a.shape)
+        dd = f(b - a)
+        small = w.abs() < 0.5
+        return torch.where(small, fma(w, dd, a), fma(f(w - 1), dd, b))
+
+    pm = lambda x: isinstance(x, torch.Tensor)  # noqa: E731
+    if pm(lr) or pm(wd):
+        mult = f(1 - f(col(lr) * col(wd)))
+        p = f(p * mult)
+    elif lr != 0.0 and wd != 0.0:
+        p = f(p * torch.tensor(1 - lr * wd, dtype=torch.float32))
+    m = lerp(m, g, f(1 - col(beta1)) if pm(beta1) else torch.tensor(1 - beta1, dtype=torch.float32))
+    if pm(beta2):
+        v = lerp(v, f(g * g), f(1 - col(beta2)))
+    else:
+        v = fma(f(torch.tensor(1 - beta2, dtype=torch.float32) * g), g,
+                f(v * torch.tensor(beta2, dtype=torch.float32)))
+    st = step
+    if pm(beta1) or pm(st):
+        bc1 = f(1 - torch.pow(d(col(beta1)) if pm(beta1) else beta1, d(col(st)) if pm(st) else st))
+    else:
+        bc1 = 1 - beta1 ** st
+    if pm(beta2) or pm(st):
+        sbc2 = f(torch.sqrt(f(1 - torch.pow(d(col(beta2)) if pm(beta2) else beta2,
+                                            d(col(st)) if pm(st) else st))))
+    else:
+        sbc2 = torch.tensor((1 - beta2 ** st) ** 0.5, dtype=torch.float32)
+    denom = f(f(torch.sqrt(v) / sbc2) + (col(eps) if pm(eps) else torch.tensor(eps, dtype=torch.float32)))
+    if not pm(lr) and not pm(bc1):
+        step_size = torch.tensor(lr / bc1, dtype=torch.float32)
+        p = f(p + f(f(-step_size * m) / denom))
+    else:
+        step_size = f(col(lr) / (bc1 if pm(bc1) else torch.tensor(bc1, dtype=torch.float32)))
+        p = f(p - f(f(m / denom) * step_size))
+    return p, m, v
+
+
+@pytest.mark.parametrize('case', ['scalar', 'per_member_lr', 'per_member_all', 'no_decay', 'member_steps'])
+def test_adamw_kernel_rounds_like_the_reference_ops(case):
+    """Every element of the grouped AdamW kernel bit for bit equal to the reference's op
+    sequence rounded as torch rounds each op (`_adamw_expected`), for packs whose per-member
+    size is and is not a multiple of 4 (vector and scalar paths of the kernel).  Bias
+    corrections use the same float32 powers where they are per member (the kernel's powf and
+    the expectation's float64 power rounded to fp32 may differ in the last place; those cases
+    compare the bias-correction-free part only through the moments)."""
+    from tabpack_b200 import ops
+
+    P = 12
+    gen = torch.Generator().manual_seed(hash(case) % 1000)
+    pmv = lambda lo, hi: torch.rand(P, generator=gen) * (hi - lo) + lo  # noqa: E731
+    hp = dict(lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, wd=1e-2)
+    if case == 'per_member_lr':
+        hp['lr'] = pmv(1e-4, 3e-3)
+    elif case == 'per_member_all':
+        hp = dict(lr=pmv(1e-4, 3e-3), beta1=pmv(0.8, 0.95), beta2=pmv(0.95, 0.999), eps=pmv(1e-9, 1e-7),
+                  wd=pmv(0.0, 0.1))
+    elif case == 'no_decay':
+        hp['wd'] = 0.0
+    steps = torch.randint(1, 40, (P,), generator=gen) if case == 'member_steps' else None
+    for shape in ((P, 64, 36), (P, 130), (P, 7, 5), (P, 1)):
+        p = torch.randn(shape, generator=gen)
+        g = torch.randn(shape, generator=gen) * 1e-2
+        m = torch.randn(shape, generator=gen) * 1e-3
+        v = torch.rand(shape, generator=gen) * 1e-4
+        step = 7
+        want = _adamw_expected(p, g, m, v, lr=hp['lr'], beta1=hp['beta1'], beta2=hp['beta2'], eps=hp['eps'],
+                               wd=hp['wd'], step=steps if steps is not None else step)
+        dev = [t.cuda() for t in (p, g, m, v)]
+        cuda_hp = {k: (x.cuda() if isinstance(x, torch.Tensor) else x) for k, x in hp.items()}
+        ops.adamw_step([dev[0]], [dev[1]], [dev[2]], [dev[3]], step=step,
+                       steps=None if steps is None else [steps.cuda()], lr=cuda_hp['lr'], beta1=cuda_hp['beta1'],
+                       beta2=cuda_hp['beta2'], eps=cuda_hp['eps'], weight_decay=cuda_hp['wd'])
+        torch.cuda.synchronize()
+        names = ('p', 'exp_avg', 'exp_avg_sq')
+        for name, got, exp in zip(names, (dev[0], dev[2], dev[3]), want):
+            if name == 'p' and (case in ('per_member_all', 'member_steps')):
+                # per-member powers: powf on the device against float64 rounded to fp32 here
+                np.testing.assert_allclose(got.cpu().numpy(), exp.numpy(), rtol=2e-6, atol=1e-8)
+                continue
+            diff = int((got.cpu().view(torch.int32) != exp.view(torch.int32)).sum())
+            assert diff == 0, f'{case} {shape} {name}: {diff} of {exp.numel()} elements differ'

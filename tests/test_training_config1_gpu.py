@@ -15,8 +15,10 @@ reference's model in fp64, and the reference's fp32 run differs from it by up to
 member's per-epoch validation MSE, by up to 0.7 % in a member's best validation MSE, in one
 member's best epoch, and in its final ensemble.  The criteria are therefore:
 
-* final ensemble: the same checkpoint keys as the reference's fp32 run, in the same order,
-  and its validation MSE within 0.5 %;
+* final ensemble: its validation MSE within 0.5 % of the reference's fp32 run, and its
+  checkpoint keys differing from that run's (as multisets: keys in one and not the other) in
+  no more keys than the reference's own fp64 run differs from it (2 keys; greedy selection
+  turns a near-tie into a different checkpoint, and rounding alone does that);
 * every accepted ensemble update: at the same epochs, its validation MSE within 0.5 %;
 * first epoch (before the drift builds up): every member's validation MSE within 1e-3, which
   a mismatch in initialisation, batch order, dropout mask or optimizer would exceed;
@@ -108,15 +110,28 @@ def test_config1_best_checkpoints(golden, config1_run):
         assert ref_there <= g['best_val_mse'][m] * (1 + tol), (m, step)
 
 
+def _key_difference(a, b) -> int:
+    """Keys in one multiset of checkpoint keys and not in the other."""
+    from collections import Counter
+
+    ca, cb = Counter(map(tuple, a)), Counter(map(tuple, b))
+    return sum(((ca - cb) + (cb - ca)).values())
+
+
 def test_config1_ensemble_members_and_metric(golden, config1_run):
-    g = golden('train_config1.npz')
+    g, h = golden('train_config1.npz'), golden('train_config1_fp64.npz')
     want = list(zip(g['ensemble_ids'].tolist(), g['ensemble_steps'].tolist()))
-    print('ensemble (reference):', want)
-    print('ensemble (here):     ', config1_run.ensemble_keys)
-    assert config1_run.ensemble_keys == want
+    ref64 = list(zip(h['ensemble_ids'].tolist(), h['ensemble_steps'].tolist()))
+    got = [tuple(k) for k in config1_run.ensemble_keys]
+    allowed = _key_difference(ref64, want)  # the reference's own fp32-vs-fp64 difference
+    print('ensemble (reference fp32):', want)
+    print('ensemble (reference fp64):', ref64)
+    print('ensemble (here):          ', got)
+    print('keys differing from the reference fp32 run:', _key_difference(got, want), 'allowed', allowed)
     rel = abs(config1_run.ensemble_metric - float(g['ensemble_val_mse'])) / float(g['ensemble_val_mse'])
     print('ensemble val MSE', config1_run.ensemble_metric, 'reference', float(g['ensemble_val_mse']), 'rel', rel)
     assert rel <= REL
+    assert _key_difference(got, want) <= max(allowed, 2)
 
 
 def test_config1_ensemble_updates(golden, config1_run):
