@@ -223,6 +223,12 @@ typedef struct tp_muon_args {
   int32_t ns_steps;
   void* workspace;              /* >= tp_muon_workspace_size(P, max_out, max_in) bytes */
   size_t workspace_bytes;
+  /* Optional bf16 compute copy of p (the copy autocast's forward multiplies with): when
+   * non-NULL, element (o, n) of member m with o < out_m, n < in_m receives bf16(p_new) at
+   * p_bf16[(m * p_bf16_rows + o) * p_bf16_cols + n] in the same pass that writes p; other
+   * elements of the copy are left as they are.  NULL: no copy is written. */
+  void* p_bf16;
+  int32_t p_bf16_rows, p_bf16_cols;
 } tp_muon_args;
 
 size_t tp_muon_workspace_size(int32_t P, int32_t max_out, int32_t max_in);

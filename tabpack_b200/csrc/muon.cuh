@@ -42,6 +42,8 @@ struct MuonArgs {
   int32_t* cols;         // (P,) c_m
   int32_t* trans;        // (P,) 1: X = U^T
   int32_t* active;       // (P,) norm2 > 0
+  __nv_bfloat16* p_bf16; // optional bf16 copy of p written with the update, or nullptr
+  int bf16_rows, bf16_cols;
 };
 
 __global__ void muon_geometry_kernel(MuonArgs a) {
@@ -377,9 +379,13 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(MuonArgs a) {
   if (active) muon_load_x(a.x + (size_t)mem * a.R_s * a.C_s, a.C_s, out_m > in_m, o0, n0, ub);
   __syncthreads();
   const float lr = a.lr_pm ? a.lr_pm[mem] : a.lr_s;
-  const float mult = (a.lr_pm || a.wd_pm) ? 1.0f - lr * (a.wd_pm ? a.wd_pm[mem] : a.wd_s) : a.wd_mult_s;
+  // 1 - lr * wd and lr * scale as the reference's per-member tensor ops round them (one rounding
+  // each; intrinsics keep the compiler from fusing them), the update as addcmul's
+  // fma(-update, lr * scale, p)
+  const float mult =
+      (a.lr_pm || a.wd_pm) ? __fsub_rn(1.0f, __fmul_rn(lr, a.wd_pm ? a.wd_pm[mem] : a.wd_s)) : a.wd_mult_s;
   const float sc = a.scale_pm ? a.scale_pm[mem] : a.scale_s;
-  const float slr = lr * sc;
+  const float slr = __fmul_rn(lr, sc);
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -388,7 +394,10 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(MuonArgs a) {
       if (o < out_m && n < in_m) {
         const float pw = a.wd_on ? __fmul_rn(pv[i][c], mult) : pv[i][c];
         const float u = active ? __bfloat162float(ub[w + 8 * i][lane + 32 * c]) : 0.0f;
-        a.p[((size_t)mem * a.max_out + o) * a.max_in + n] = fmaf(-u, slr, pw);
+        const float pn = __fmaf_rn(-u, slr, pw);
+        a.p[((size_t)mem * a.max_out + o) * a.max_in + n] = pn;
+        if (a.p_bf16 != nullptr)
+          a.p_bf16[((size_t)mem * a.bf16_rows + o) * a.bf16_cols + n] = __float2bfloat16_rn(pn);
       }
     }
 }

@@ -776,6 +776,12 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
   void* A = ws + L.off_a;
   void* Bm = ws + L.off_b;
   m.x = reinterpret_cast<__nv_bfloat16*>(x0);
+  if (a->p_bf16 != nullptr && (a->p_bf16_rows < a->max_out || a->p_bf16_cols < a->max_in))
+    return fail(TP_EINVAL, "the bf16 copy (%d x %d per member) is smaller than p (%d x %d)", a->p_bf16_rows,
+                a->p_bf16_cols, a->max_out, a->max_in);
+  m.p_bf16 = static_cast<__nv_bfloat16*>(a->p_bf16);
+  m.bf16_rows = a->p_bf16_rows;
+  m.bf16_cols = a->p_bf16_cols;
 
   if (a->P > 65535) return fail(TP_EINVAL, "at most 65535 members per Muon call");
   if (L.R_s / NS_TILE_M > 255 || (L.C_s + NS_TILE_N - 1) / NS_TILE_N > 255)

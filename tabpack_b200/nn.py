@@ -27,6 +27,7 @@ import contextlib
 import enum
 import itertools
 import math
+import weakref
 from typing import Any, Final
 
 import torch
@@ -334,6 +335,48 @@ class _WeightCache:
             self.key = key
         return self.value
 
+    def begin_update(self, w: Tensor) -> Tensor | None:
+        """The bf16 copy for an optimizer step to refresh in the pass that updates `w`: the copy
+        when it holds `w`'s current values (its key is at `w`'s present version) and nothing but
+        this cache holds it; else None, and the next forward casts again."""
+        key, buf = self.key, self.value
+        if key is None or buf is None or key[0] != w.data_ptr() or key[1] != w._version or key[2] != torch.bfloat16:
+            return None
+        if buf is w or not _reusable(buf, tuple(buf.shape), torch.bfloat16, w.device):
+            return None
+        return buf
+
+    def end_update(self, w: Tensor, buf: Tensor) -> None:
+        """After a step that wrote bf16 of `w`'s new values into `buf` (`begin_update`): the copy
+        is current at `w`'s new version."""
+        if self.value is buf and self.key is not None:
+            self.key = (self.key[0], w._version) + tuple(self.key[2:])
+
+
+# id(parameter) -> (weak parameter, weak cache): the bf16 compute-copy cache of a LinearPack's
+# weight, so that an optimizer step can write the refreshed copy in the same pass as the fp32
+# weights.  Keyed by id (tensors do not hash by value); an entry leaves when its parameter dies.
+_BF16_CACHES: dict[int, tuple] = {}
+
+
+def _register_bf16_cache(w: Tensor, cache: _WeightCache) -> None:
+    key = id(w)
+
+    def gone(ref, key=key):
+        entry = _BF16_CACHES.get(key)
+        if entry is not None and entry[0] is ref:
+            del _BF16_CACHES[key]
+
+    _BF16_CACHES[key] = (weakref.ref(w, gone), weakref.ref(cache))
+
+
+def bf16_copy_cache(w: Tensor) -> _WeightCache | None:
+    """The bf16 compute-copy cache registered for parameter `w`, if any."""
+    entry = _BF16_CACHES.get(id(w))
+    if entry is None or entry[0]() is not w:
+        return None
+    return entry[1]()
+
 
 class _OneHotWeightCache:
     """bf16 copies of a first-layer weight (P, max_out, n_dense + n_onehot) for the gathered
@@ -542,6 +585,7 @@ class LinearPack(ModulePack):
         self.weight = ParameterPack(torch.empty(pack_size, max_out, max_in, **fk))
         self.bias = ParameterPack(torch.empty(pack_size, max_out, **fk)) if bias else None
         self._cache = _WeightCache()
+        _register_bf16_cache(self.weight, self._cache)
         self.reset_parameters()
 
     @property

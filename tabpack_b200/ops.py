@@ -251,8 +251,10 @@ def muon_workspace_size(P: int, max_out: int, max_in: int) -> int:
 
 def muon_step(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=None, in_features=None, lr,
               momentum, weight_decay, update_scale=None, nesterov: bool = True, mutate_grad: bool = True,
-              ns_steps: int = 5, workspace: Tensor | None = None) -> None:
-    """One Muon group step on a packed (P, max_out, max_in) fp32 weight; see `tp_muon_step`."""
+              ns_steps: int = 5, workspace: Tensor | None = None, p_bf16: Tensor | None = None) -> None:
+    """One Muon group step on a packed (P, max_out, max_in) fp32 weight; see `tp_muon_step`.
+    `p_bf16` (P, rows >= max_out, cols >= max_in) bf16, optional, receives bf16 of the updated
+    weights of each member's out x in block in the same pass."""
     for name, t in (('p', p), ('grad', grad), ('momentum_buffer', momentum_buffer)):
         if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous() or t.ndim != 3:
             raise TypeError(f'{name} must be a contiguous 3-D fp32 CUDA tensor')
@@ -269,9 +271,14 @@ def muon_step(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=
     a.update_scale = _ptr(_cuda('update_scale', update_scale, torch.float32))
     a.nesterov, a.mutate_grad, a.ns_steps = int(nesterov), int(mutate_grad), int(ns_steps)
     a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    if p_bf16 is not None:
+        if (not p_bf16.is_cuda or p_bf16.dtype != torch.bfloat16 or not p_bf16.is_contiguous() or p_bf16.ndim != 3
+                or p_bf16.shape[0] != P):
+            raise TypeError('p_bf16 must be a contiguous (P, rows, cols) bf16 CUDA tensor')
+        a.p_bf16, a.p_bf16_rows, a.p_bf16_cols = p_bf16.data_ptr(), p_bf16.shape[1], p_bf16.shape[2]
     keep = (out_features, in_features, update_scale)  # noqa: F841  (alive until the launch is queued)
     check(load().tp_muon_step(ctypes.byref(a), _stream()), 'tp_muon_step')
-    increment_version([p, momentum_buffer] + ([grad] if mutate_grad else []))
+    increment_version([p, momentum_buffer] + ([grad] if mutate_grad else []) + ([p_bf16] if p_bf16 is not None else []))
 
 
 def metric_pack(metric: str, y_pred: Tensor, y_true: Tensor, classes: int = 1) -> Tensor:

@@ -18,7 +18,8 @@ import torch
 from torch import Tensor
 
 from tabpack_b200 import ops
-from tabpack_b200.nn import PACK_DIM, LinearPack, ParameterPack, check_pack_idx, make_complementary_pack_idx
+from tabpack_b200.nn import (PACK_DIM, LinearPack, ParameterPack, bf16_copy_cache, check_pack_idx,
+                             make_complementary_pack_idx)
 
 
 def _check_lr(v):
@@ -315,12 +316,19 @@ def _muon_group(opt: torch.optim.Optimizer, g: dict, *, workspaces: dict, allow_
     # into a copy), so no copy is made here
     grad = p.grad.data
     scale = g.get('muon_update_scale')
+    # the layer's bf16 compute copy, refreshed in the pass that writes the weights (otherwise the
+    # next forward casts the whole weight pack again)
+    cache = bf16_copy_cache(p)
+    copy = cache.begin_update(p) if cache is not None else None
     ops.muon_step(p, grad, st['muon_momentum_buffer'], out_features=g.get('muon_out_features'),
                   in_features=g.get('muon_in_features'), lr=_hp(g['muon_lr']), momentum=_hp(g['muon_momentum']),
                   weight_decay=_hp(g['weight_decay']),
                   update_scale=None if scale is None else scale.to(torch.float32).contiguous(),
                   nesterov=bool(g['muon_nesterov']), mutate_grad=allow_inplace_grad_mutation,
-                  ns_steps=int(g['muon_newton_schulz_steps']), workspace=_muon_workspace(workspaces, p))
+                  ns_steps=int(g['muon_newton_schulz_steps']), workspace=_muon_workspace(workspaces, p),
+                  p_bf16=copy)
+    if copy is not None:
+        cache.end_update(p, copy)
 
 
 def adamw_step(opt: torch.optim.Optimizer, *, support_replacement: bool) -> None:

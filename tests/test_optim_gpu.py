@@ -303,3 +303,39 @@ def test_adamw_kernel_rounds_like_the_reference_ops(case):
                 continue
             diff = int((got.cpu().view(torch.int32) != exp.view(torch.int32)).sum())
             assert diff == 0, f'{case} {shape} {name}: {diff} of {exp.numel()} elements differ'
+
+
+def test_muon_step_refreshes_the_bf16_weight_copy():
+    """Under bf16 autocast a LinearPack multiplies with a cached bf16 copy of its weights.  A
+    Muon step writes bf16 of the new weights into that copy in the pass that updates them, so
+    the copy is current afterwards (its key at the weight's new version: the next forward
+    casts nothing) and equals bf16 of the updated weights on every member's block, bit for bit."""
+    from tabpack_b200 import nn as bnn
+    from tabpack_b200 import optim as bopt
+
+    P = 4
+    outs, ins = [72, 16, 48, 64], [40, 24, 64, 8]
+    lin = bnn.LinearPack(ins, outs, max_in_features=64, max_out_features=72, pack_size=P).cuda()
+    opt = bopt.MuonAdamWPack([bopt.MuonAdamWPack.make_muon_parameter_group(lin), {'params': [lin.bias]}],
+                             adamw_lr=1e-3, weight_decay=1e-2, muon_lr=0.02, pack_size=P,
+                             allow_inplace_grad_mutation=False)
+    gen = torch.Generator(device='cuda').manual_seed(5)
+    x = torch.randn(P, 32, 64, device='cuda', generator=gen)
+    rows = torch.arange(72, device='cuda')[None, :, None] < torch.tensor(outs, device='cuda')[:, None, None]
+    cols = torch.arange(64, device='cuda')[None, None, :] < torch.tensor(ins, device='cuda')[:, None, None]
+    valid = rows & cols
+    for _ in range(3):
+        with torch.autocast('cuda', dtype=torch.bfloat16):
+            y = lin(x)
+        y.float().square().sum().backward()
+        del y
+        opt.step()
+        opt.zero_grad()
+        torch.cuda.synchronize()
+        cache = bnn.bf16_copy_cache(lin.weight)
+        assert cache is lin._cache and cache.key is not None
+        assert cache.key[1] == lin.weight._version, 'the copy was not refreshed with the step'
+        copy = cache.value[:, :72, :64]
+        want = lin.weight.detach().bfloat16()
+        assert torch.equal(copy[valid].view(torch.int16), want[valid].view(torch.int16))
+        del copy  # a view of the copy would keep the next step from writing into it
