@@ -207,7 +207,8 @@ def _adamw_expected(p, g, m, v, *, lr, beta1, beta2, eps, wd, step):
     in float64 with explicit rounding to fp32: torch's lerp as fma(w or w - 1, end - self,
     self or end), addcmul as fma(value * g, g, v * beta2), addcdiv as p + (value * m) / denom
     when the step size is a Python float, p - (m / denom) * step otherwise; square root and
-    division correctly rounded.  A fused multiply-add is evaluated exactly in float64 (the
+    division correctly rounded (the reference's CPU fp32 square root is not: it is 1 ulp off for
+    about 0.6 % of values, which no CUDA kernel reproduces).  A fused multiply-add is evaluated exactly in float64 (the
     product of two fp32 values is exact there) and rounded once more to fp32; that second
     rounding could differ from a single one only at an fp32 tie, which these random values
     do not produce.  Hyperparameters are floats or (P,) fp32 tensors; step an int or (P,)."""
@@ -245,11 +246,12 @@ def _adamw_expected(p, g, m, v, *, lr, beta1, beta2, eps, wd, step):
     else:
         bc1 = 1 - beta1 ** st
     if pm(beta2) or pm(st):
-        sbc2 = f(torch.sqrt(f(1 - torch.pow(d(col(beta2)) if pm(beta2) else beta2,
-                                            d(col(st)) if pm(st) else st))))
+        sbc2 = f(torch.sqrt(d(f(1 - torch.pow(d(col(beta2)) if pm(beta2) else beta2,
+                                              d(col(st)) if pm(st) else st)))))
     else:
         sbc2 = torch.tensor((1 - beta2 ** st) ** 0.5, dtype=torch.float32)
-    denom = f(f(torch.sqrt(v) / sbc2) + (col(eps) if pm(eps) else torch.tensor(eps, dtype=torch.float32)))
+    # a correctly rounded fp32 square root (float64 then fp32; torch's CPU fp32 sqrt is not)
+    denom = f(f(f(torch.sqrt(d(v))) / sbc2) + (col(eps) if pm(eps) else torch.tensor(eps, dtype=torch.float32)))
     if not pm(lr) and not pm(bc1):
         step_size = torch.tensor(lr / bc1, dtype=torch.float32)
         p = f(p + f(f(-step_size * m) / denom))
@@ -270,7 +272,7 @@ def test_adamw_kernel_rounds_like_the_reference_ops(case):
     from tabpack_b200 import ops
 
     P = 12
-    gen = torch.Generator().manual_seed(hash(case) % 1000)
+    gen = torch.Generator().manual_seed(sum(map(ord, case)))
     pmv = lambda lo, hi: torch.rand(P, generator=gen) * (hi - lo) + lo  # noqa: E731
     hp = dict(lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, wd=1e-2)
     if case == 'per_member_lr':
