@@ -60,6 +60,11 @@ typedef struct tp_linear_args {
   const void* w;               /* (P, max_out, max_in) */
   const float* bias;           /* (P, max_out) fp32, or NULL */
   void* y;                     /* (P, B, max_out) */
+  int32_t y_pad_zero;          /* 1: y's padding already holds zeros (the columns at or beyond
+                                  each member's out_features, in every row), e.g. a buffer that
+                                  an earlier call with the same widths wrote: the forward writes
+                                  each member's columns rounded up to a multiple of 32 and skips
+                                  the rest.  0: it writes every column. */
 } tp_linear_args;
 
 /* Backward of tp_linear_forward with the same `fwd` arguments. */

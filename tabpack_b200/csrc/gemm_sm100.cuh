@@ -438,7 +438,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
             ti = decode_tile(pr, t, Cfg::BK);
           else
             ti.kind = KIND_END;
-          if (ti.kind == KIND_SKIP) continue;
+          if (ti.kind == KIND_SKIP || (ti.kind == KIND_ZERO && pr.skip_zero)) continue;
         }
         const int s = pub & (TRING - 1);
         if (!mbar_wait(&tr_empty[s], ((uint32_t)(pub / TRING) & 1u) ^ 1u, abort_flag)) break;
@@ -633,7 +633,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
             }
           }
           const int z0 = cbase + 32 * ncomp, z1 = min(cbase + WCOLS, pr.out_cols);
-          if (z0 < z1) zero_fill_bf16(pr, m, row_base, z0, z1, lane);
+          if (z0 < z1 && !pr.skip_zero) zero_fill_bf16(pr, m, row_base, z0, z1, lane);
         } else {
         uint32_t ra[32], rb[32];
         if (nch > 0) tmem_ld_32x32b_x32(t_row, ra);

@@ -54,6 +54,7 @@ struct LinearProblem {
   const void* b_ptr;
   int m_tiles, n_tiles;
   int BM, BN;
+  int skip_zero;       // the output's padding already holds zeros: ZERO tiles are not written
   FastDiv div_member;  // by m_tiles * n_tiles (tiles per member)
   FastDiv div_mt;      // by m_tiles
   // Dynamic scheduling (single-CTA launches): a dense list of the launch's MMA tiles, entry

@@ -506,6 +506,7 @@ int linear_forward_impl(const tp_linear_args* a, const float* addend, int add_ld
   pr.addend = addend;
   pr.add_ld = add_ld;
   pr.mode = MODE_FWD;
+  pr.skip_zero = a->y_pad_zero != 0;
   pr.out = a->y;
   pr.out_rows = a->B;
   pr.out_cols = a->max_out;

@@ -416,3 +416,40 @@ def test_adamw_golden(golden, case):
         np.testing.assert_allclose(ms[0].cpu().numpy(), g[f'c{case}.s{s}.m_w'], rtol=1e-5, atol=1e-9)
         np.testing.assert_allclose(vs[0].cpu().numpy(), g[f'c{case}.s{s}.v_w'], rtol=1e-5, atol=1e-12)
     assert ops.device_error() == 0
+
+
+def test_forward_into_zero_padded_buffer_skips_the_padding():
+    """`y_pad_zero = 1`: the forward writes only each member's block, rounded up to 32
+    columns (the caller states that y's padding already holds zeros).  Into a zeroed buffer the
+    result equals the normal forward bit for bit; a sentinel planted in the padding past that is
+    left as it is."""
+    import ctypes
+
+    from tabpack_b200 import _lib, ops
+
+    P, B, K, N = 6, 640, 256, 520
+    rng = np.random.default_rng(8)
+    out_np = (rng.integers(2, 66, P) * 8).astype(np.int32)
+    outf = torch.from_numpy(out_np).cuda()
+    p = torch.from_numpy(rng.uniform(0, 0.5, P).astype(np.float32)).cuda()
+    g = torch.Generator(device='cuda').manual_seed(8)
+    x = torch.randn(P, B, K, device='cuda', generator=g).bfloat16()
+    w = (torch.randn(P, N, K, device='cuda', generator=g) / 16).bfloat16()
+    b = torch.randn(P, N, device='cuda', generator=g) / 16
+    kw = dict(out_features=outf, relu=True, dropout_p=p, seed=3, offset=1)
+    want = ops.linear_forward(x, w, b, **kw)
+    lib = _lib.load()
+    col = torch.arange(N, device='cuda')[None, None, :]
+    pad = col >= outf[:, None, None]
+    far = col >= ((outf[:, None, None] + 31) // 32) * 32  # beyond the chunk that holds the last column
+    for fill in (0.0, 7.0):
+        y = torch.zeros(P, B, N, device='cuda', dtype=torch.bfloat16).masked_fill_(pad, fill)
+        a = _lib.LinearArgs()
+        a.P, a.B, a.max_in, a.max_out, a.dtype = P, B, K, N, _lib.TP_DTYPE_BF16
+        a.out_features, a.relu, a.dropout_p, a.seed, a.offset = outf.data_ptr(), 1, p.data_ptr(), 3, 1
+        a.x, a.w, a.bias, a.y, a.y_pad_zero = x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), 1
+        assert lib.tp_linear_forward(ctypes.byref(a), torch.cuda.current_stream().cuda_stream) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(y[~pad.expand_as(y)].view(torch.int16), want[~pad.expand_as(want)].view(torch.int16))
+        assert bool((y[far.expand_as(y)] == fill).all())
+        assert bool((y[(pad & ~far).expand_as(y)] == 0).all())
