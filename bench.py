@@ -414,7 +414,7 @@ def run_b200(args, emit: bool = True) -> dict | None:
 # DRAM bytes (read + write) per full-size launch, from the ncu capture of the layer kernels
 # (32-member case scaled by 256/32).
 TRAFFIC_BYTES_PER_LAUNCH: dict[str, float | None] = {
-    'fwd': (25.796096e6 + 212.714752e6) * 8,
+    'fwd': (25.810688e6 + 91.443712e6) * 8,
     'act': (293.625344e6 + 94.327552e6) * 8,
     'dgrad': (173.594624e6 + 100.386560e6) * 8,
     'wgrad': (180.835072e6 + 42.455808e6) * 8,
