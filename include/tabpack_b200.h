@@ -65,6 +65,14 @@ typedef struct tp_linear_args {
                                   an earlier call with the same widths wrote: the forward writes
                                   each member's columns rounded up to a multiple of 32 and skips
                                   the rest.  0: it writes every column. */
+  const int32_t* row_index;    /* device (P, B) dataset rows, or NULL.  With it, x is a
+                                  (x_rows, max_in) table shared by every member and member m's
+                                  row b is x[row_index[m * B + b]]: the training loop's per-step
+                                  batch gather (src/tabpackage/_training.py:2667-2669) done by
+                                  the GEMMs' operand loads (TMA gather4) instead of a gathered
+                                  copy.  BF16 tensor-core path only; no depth gating and no
+                                  input gradient (the table takes none). */
+  int32_t x_rows;              /* rows of the table x when row_index is set */
 } tp_linear_args;
 
 /* Backward of tp_linear_forward with the same `fwd` arguments. */

@@ -32,6 +32,7 @@ class LinearArgs(ctypes.Structure):
         ('dropout_p', ctypes.c_void_p), ('seed', ctypes.c_uint64), ('offset', ctypes.c_uint32),
         ('member_base', ctypes.c_uint32), ('x', ctypes.c_void_p), ('w', ctypes.c_void_p),
         ('bias', ctypes.c_void_p), ('y', ctypes.c_void_p), ('y_pad_zero', ctypes.c_int32),
+        ('row_index', ctypes.c_void_p), ('x_rows', ctypes.c_int32),
     ]
 
 

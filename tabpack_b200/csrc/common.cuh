@@ -178,6 +178,19 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Four rows of a 2-D table (tensor map box: 64 columns x 1 row) at column x into 512 consecutive
+// bytes of shared memory, completing on `bar`: TMA gather4.  The shared-memory destination keeps
+// the map's 128-byte swizzle, so four gathers at 512-byte steps fill a tile as one tiled load of
+// those rows would.
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int4 rows) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(rows.x), "r"(rows.y), "r"(rows.z),
+      "r"(rows.w)
+      : "memory");
+}
+
 // CTA-pair form (cta_group::2): the data lands in this CTA's shared memory and the
 // transaction bytes are counted on `bar_cluster`, a shared::cluster address that may
 // name the mbarrier of the pair's leader CTA; the data goes to this CTA only.

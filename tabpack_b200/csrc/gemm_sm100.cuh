@@ -8,6 +8,7 @@
 //   MODE_FWD_ADD: the forward with an fp32 addend E[B x out_m] summed before the bias
 //   MODE_FWD_PAIR: the forward on CTA pairs (without dropout, or with a long K loop)
 //   MODE_DGRAD  : C[B x in_m] = G[B x out_m] * W; A K-major, B MN-major; CTA pairs
+//   MODE_WGRAD_TG: MODE_WGRAD_T on single CTAs with X gathered from a table by row index
 //   MODE_WGRAD_T: C^T[in_m x out_m] = X^T * G stored into C (K = batch rows), A and B MN-major;
 //                 a warp's 32 lanes hold 32 consecutive input features, so each output
 //                 feature's column is one coalesced 128-byte fp32 store; CTA pairs
@@ -41,8 +42,8 @@ struct Sm100Cfg {
   static constexpr bool FWDK = (MODE == MODE_FWD || MODE == MODE_FWD_ADD || MODE == MODE_FWD_PAIR);  // forward epilogue
   static constexpr int TILE_M = PAIR ? 2 * BM : BM;
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B columns staged per CTA
-  static constexpr bool A_MN = (MODE == MODE_WGRAD_T);
-  static constexpr bool B_MN = (MODE == MODE_DGRAD || MODE == MODE_WGRAD_T || MODE == MODE_NS_BMN);
+  static constexpr bool A_MN = is_wgrad_t(MODE);
+  static constexpr bool B_MN = (MODE == MODE_DGRAD || is_wgrad_t(MODE) || MODE == MODE_NS_BMN);
   static constexpr int STAGES = PAIR ? (FWDK ? 5 : 6) : (BN == 256) ? (FWDK ? 3 : 4) : 6;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = B_ROWS * BK * 2;
@@ -288,7 +289,63 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp == 0 && !PAIR && pr.row_index != nullptr) {
+    // ------------------------------------------------------------------ producer, gathered A
+    // A's rows come from a shared table by row index: each lane gathers four rows per k-block
+    // (32 TMA gather4 loads fill the 128 x 64 stage), lane 0 loads B as usual.  Forward (A
+    // K-major): lane l takes the tile's rows 4l..4l+3, the same for every k-block.  Transposed
+    // weight gradient (A = X^T, MN-major, two 64-feature boxes of 64 batch rows): lane l takes
+    // box l / 16 and batch rows 4 (l % 16)..+3 of the k-block.  Rows past the batch gather
+    // table row 0: forward outputs of those rows are not stored, and in the weight gradient G
+    // is zero there (its rows past the batch load as zeros).
+    int stage = 0;
+    uint32_t phase = 0;
+    auto rows4 = [&](int m, int b0) -> int4 {
+      const int32_t* ri = pr.row_index + (size_t)m * pr.B;
+      int4 r;
+      r.x = b0 < pr.B ? __ldg(ri + b0) : 0;
+      r.y = b0 + 1 < pr.B ? __ldg(ri + b0 + 1) : 0;
+      r.z = b0 + 2 < pr.B ? __ldg(ri + b0 + 2) : 0;
+      r.w = b0 + 3 < pr.B ? __ldg(ri + b0 + 3) : 0;
+      return r;
+    };
+    for (int k = 0;; ++k) {
+      const TileInfo ti = ring_read(k, lane == 0);
+      if (ti.kind == KIND_END) break;
+      if (ti.kind != KIND_MMA) continue;
+      int4 fr = make_int4(0, 0, 0, 0);
+      if constexpr (!Cfg::A_MN) fr = rows4(ti.member, ti.mt * Cfg::BM + 4 * lane);
+      const int a_col = ti.mt * Cfg::BM;  // transposed: the tile's first input feature
+      const int b_col = ti.nt * BN;
+      for (int kb = 0; kb < ti.kblocks; ++kb) {
+        const int k0 = kb * Cfg::BK;
+        int4 wr = make_int4(0, 0, 0, 0);
+        if constexpr (Cfg::A_MN) wr = rows4(ti.member, k0 + 4 * (lane & 15));
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto gather_done;
+        if (lane == 0) mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+        __syncwarp();
+        uint8_t* a = smA + stage * Cfg::A_BYTES;
+        uint8_t* b = smB + stage * Cfg::B_BYTES;
+        if constexpr (!Cfg::A_MN)
+          tma_gather4(a + lane * 512, &tmA, &full[stage], k0, fr);
+        else
+          tma_gather4(a + (lane >> 4) * 64 * 128 + (lane & 15) * 512, &tmA, &full[stage], a_col + (lane >> 4) * 64, wr);
+        if (lane == 0) {
+          if (!Cfg::B_MN) {
+            tma_load_3d(b, &tmB, &full[stage], k0, b_col, ti.member);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c) tma_load_3d(b + c * 64 * 128, &tmB, &full[stage], b_col + c * 64, k0, ti.member);
+          }
+        }
+        if (++stage == Cfg::STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  gather_done:;
+  } else if (warp == 0) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
       int stage = 0;
@@ -297,7 +354,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
         const TileInfo ti = ring_read(k, true);
         if (ti.kind == KIND_END) break;
         if (ti.kind != KIND_MMA) continue;
-        const int zA = ((Cfg::FWDK || MODE == MODE_WGRAD_T) && pr.x_shared) ? 0 : ti.member;  // NS operands are per member
+        const int zA = ((Cfg::FWDK || is_wgrad_t(MODE)) && pr.x_shared) ? 0 : ti.member;  // NS operands are per member
         const int zB = ti.member;
         // this CTA's A rows and B columns: in a pair the leader takes rows 0..127 and the
         // first half of the (trimmed) columns, the peer rows 128..255 and the second half
@@ -571,7 +628,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
               __syncwarp();
             }
           }
-        } else if constexpr (MODE == MODE_WGRAD_T) {
+        } else if constexpr (is_wgrad_t(MODE)) {
           // lane = input feature `row`, register j = output feature col0 + j:
           // dW[o][row] for fixed o is 32 consecutive floats across the warp
           float* base = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms;
@@ -663,7 +720,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
         // ZERO or COPY block: this warp's 32 rows x column slice, lanes along the columns
         const int row_base = ti.mt * Cfg::TILE_M + (int)rank * Cfg::BM + q * 32;
         const int c_end = min(cbase + WCOLS, pr.out_cols);
-        if (MODE == MODE_WGRAD_T) {
+        if (is_wgrad_t(MODE)) {
           // zero block, transposed: output features cbase.. x input features row_base + lane
           float* base = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms;
           const int i = row_base + lane;

@@ -24,6 +24,10 @@ enum : int { MODE_FWD_ADD = 6 };
 // dropout (no Philox draws, so the epilogue keeps up with the pair's faster k-blocks) and for
 // long K loops, where operand delivery rather than the epilogue bounds a tile.
 enum : int { MODE_FWD_PAIR = 7 };
+// Kernel instantiation of the transposed weight gradient (problems carry MODE_WGRAD_T) on single
+// CTAs whose A operand (X^T) is gathered from a table by row index.
+enum : int { MODE_WGRAD_TG = 9 };
+__host__ __device__ constexpr bool is_wgrad_t(int mode) { return mode == MODE_WGRAD_T || mode == MODE_WGRAD_TG; }
 // KIND_END marks the end of a CTA's tile sequence in the kernel's shared-memory tile ring.
 enum : int { KIND_MMA = 0, KIND_ZERO = 1, KIND_COPY = 2, KIND_SKIP = 3, KIND_END = 4 };
 
@@ -55,6 +59,9 @@ struct LinearProblem {
   int m_tiles, n_tiles;
   int BM, BN;
   int skip_zero;       // the output's padding already holds zeros: ZERO tiles are not written
+  // gathered input (x is a shared table): member m's row b is x row row_index[m * B + b]; the
+  // producer warp loads the A operand with TMA gather4 (4 table rows per load)
+  const int32_t* row_index;
   FastDiv div_member;  // by m_tiles * n_tiles (tiles per member)
   FastDiv div_mt;      // by m_tiles
   // Dynamic scheduling (single-CTA launches): a dense list of the launch's MMA tiles, entry

@@ -137,6 +137,24 @@ int make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t rows, u
   return TP_OK;
 }
 
+// 2-D map over a (rows, inner) bf16 table for TMA gather4: a box of 64 columns x 1 row (gather4
+// loads take one-row boxes), 128-byte swizzle like the tiled operand maps.
+int make_gather_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t rows) {
+  auto enc = encode_fn();
+  if (!enc) return fail(TP_EUNSUPPORTED, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {64, 1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(TP_EINVAL, "cuTensorMapEncodeTiled failed (%d) for a %llu x %llu gather table", (int)r,
+                (unsigned long long)rows, (unsigned long long)inner);
+  return TP_OK;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Workspace of tp_linear_backward_noalloc (device memory reserved at module load).
@@ -251,7 +269,7 @@ int launch_sm100(const LinearProblem& pr_in, const CUtensorMap& a, const CUtenso
   }
   cfg.gridDim = dim3(Cfg::PAIR ? 2 * grid : grid);
   constexpr int kind = (MODE == MODE_DGRAD) ? TP_PROF_DGRAD
-                       : (MODE == MODE_WGRAD || MODE == MODE_WGRAD_T) ? TP_PROF_WGRAD
+                       : (MODE == MODE_WGRAD || is_wgrad_t(MODE)) ? TP_PROF_WGRAD
                        : (MODE == MODE_NS) ? TP_PROF_NS
                        : (MODE == MODE_NS_BMN) ? TP_PROF_NS_BMN
                                                : TP_PROF_FWD;
@@ -285,6 +303,13 @@ int check_linear(const tp_linear_args* a) {
   if (a->n_blocks && a->max_in != a->max_out)
     return fail(TP_EINVAL, "depth gating needs max_in == max_out (inactive members pass their input through)");
   if (!a->w) return fail(TP_EINVAL, "w is null");
+  if (a->row_index) {
+    if (a->x_rows <= 0) return fail(TP_EINVAL, "a gathered input needs the table's row count (x_rows > 0)");
+    if (a->x_shared || a->n_blocks)
+      return fail(TP_EINVAL, "a gathered input is a shared table: no x_shared flag and no depth gating");
+    if (a->dtype != TP_DTYPE_BF16 || device_info().major != 10 || (a->max_in % 8) != 0 || (a->max_out % 8) != 0)
+      return fail(TP_EUNSUPPORTED, "a gathered input runs on the sm_100 bf16 tensor-core path only");
+  }
   return TP_OK;
 }
 
@@ -530,6 +555,11 @@ int linear_forward_impl(const tp_linear_args* a, const float* addend, int add_ld
     static_assert(Sm100Cfg<BN, MODE_FWD_ADD>::TILE_M == Cfg::TILE_M && Sm100Cfg<BN, MODE_FWD_ADD>::B_ROWS == Cfg::B_ROWS,
                   "the forward with an addend shares the forward's tiling");
     if (addend != nullptr) return launch_sm100<BN, MODE_FWD_ADD>(pr, ma, mb, st);
+    if (a->row_index) {  // A gathered from the table by row index, on single CTAs
+      if ((rc = make_gather_map(&ma, a->x, a->max_in, a->x_rows))) return rc;
+      pr.row_index = a->row_index;
+      return launch_sm100<BN, MODE_FWD>(pr, ma, mb, st);
+    }
     // CTA pairs (256-row tiles: a third less operand traffic per SM, more k-blocks in flight)
     // when there are no Philox draws, or when the K loop is long enough that operand delivery
     // rather than the dropout epilogue bounds the tile (a TabPack's first layer over its one-hot
@@ -611,6 +641,7 @@ int linear_backward_impl(const tp_linear_grad_args* ga, int dw_ld_in, void* stre
   const bool tc = use_tensor_cores(a);
   // 2. dx = g w   (dx = dy for depth-inactive members); with dx_cols, the input columns from
   // dx_cols on are written as zeros without their GEMM tiles
+  if (ga->dx && a->row_index) return fail(TP_EINVAL, "a gathered input (a table) takes no input gradient");
   if (ga->dx) {
     if (ga->dx_cols < 0 || (ga->dx_cols > 0 && (a->in_features || a->n_blocks)))
       return fail(TP_EINVAL, "dx_cols needs a layer without per-member input widths or depth gating");
@@ -681,9 +712,18 @@ int linear_backward_impl(const tp_linear_grad_args* ga, int dw_ld_in, void* stre
       pr.m_tiles = (dw_cols + Cfg::TILE_M - 1) / Cfg::TILE_M;
       pr.n_tiles = (dw_rows + BN - 1) / BN;
       CUtensorMap ma, mb;
-      if ((rc = make_map(&ma, a->x, a->max_in, a->B, a->x_shared ? 1 : a->P, 64, 64))) return rc;
       if ((rc = make_map(&mb, G, a->max_out, a->B, a->P, 64, 64))) return rc;
-      if ((rc = launch_sm100<BN, MODE_WGRAD_T>(pr, ma, mb, st))) return rc;
+      if (a->row_index) {  // X gathered from the table by row index, on single CTAs
+        using CfgG = Sm100Cfg<BN, MODE_WGRAD_TG>;
+        pr.BM = CfgG::TILE_M;
+        pr.m_tiles = (dw_cols + CfgG::TILE_M - 1) / CfgG::TILE_M;
+        pr.row_index = a->row_index;
+        if ((rc = make_gather_map(&ma, a->x, a->max_in, a->x_rows))) return rc;
+        if ((rc = launch_sm100<BN, MODE_WGRAD_TG>(pr, ma, mb, st))) return rc;
+      } else {
+        if ((rc = make_map(&ma, a->x, a->max_in, a->B, a->x_shared ? 1 : a->P, 64, 64))) return rc;
+        if ((rc = launch_sm100<BN, MODE_WGRAD_T>(pr, ma, mb, st))) return rc;
+      }
     } else {
       rc = bf16 ? launch_simt<__nv_bfloat16, MODE_WGRAD>(pr, st) : launch_simt<float, MODE_WGRAD>(pr, st);
       if (rc) return rc;

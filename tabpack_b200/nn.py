@@ -453,9 +453,12 @@ class _PackedLinearFn(torch.autograd.Function):
 
 def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features=None, out_features=None,
                   n_blocks=None, block_index=0, relu=False, dropout_p=None, seed=0, offset=0,
-                  member_base=0, cache: _WeightCache | None = None, dx_cols: int = 0) -> Tensor:
+                  member_base=0, cache: _WeightCache | None = None, dx_cols: int = 0,
+                  row_index: Tensor | None = None) -> Tensor:
     """Functional form of the fused packed linear layer (see module docstring).  `dx_cols` > 0:
-    the input's gradient is needed in its first dx_cols columns only (zeros beyond)."""
+    the input's gradient is needed in its first dx_cols columns only (zeros beyond).
+    `row_index` (pack_size, batch): `x` is a (rows, in) table and member m's input row b is
+    x[row_index[m, b]], gathered by the GEMMs' operand loads (the table takes no gradient)."""
     if not x.is_cuda:
         raise RuntimeError('tabpack_b200 packs run on CUDA devices only')
     dtype = _compute_dtype(x)
@@ -479,6 +482,10 @@ def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features
         bc = nn.functional.pad(bias.detach(), (0, rows - max_out))
     kw = dict(in_features=in_features, out_features=out_features, n_blocks=n_blocks, block_index=block_index,
               relu=relu, dropout_p=dropout_p, seed=seed, offset=offset, member_base=member_base)
+    if row_index is not None:
+        if x.requires_grad:
+            raise ValueError('a gathered input (a table) takes no gradient')
+        kw['row_index'] = row_index
     cfg = {'kw': kw, 'w_shape': tuple(weight.shape), 'in_cols': in_cols, 'dx_cols': int(dx_cols)}
     with torch.autocast(x.device.type, enabled=False):
         y = _PackedLinearFn.apply(xc, weight, bias, wc, bc, cfg)
@@ -651,8 +658,10 @@ class LinearPack(ModulePack):
 
 
 def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stream, n_blocks, block_index,
-                 offset_stride: int = 1, offset_add: int = 0, dx_cols: int = 0):
+                 offset_stride: int = 1, offset_add: int = 0, dx_cols: int = 0, row_index: Tensor | None = None):
     w, b = linear.weight, linear.bias
+    if row_index is not None and pack_idx is not None:
+        raise ValueError('a gathered input runs on the whole pack')
     inf, outf = linear.in_features, linear.out_features
     member_base = 0 if stream is None else stream.member_base
     if pack_idx is not None:
@@ -662,7 +671,9 @@ def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stre
         if dropout is not None:
             raise NotImplementedError('pack_idx with training-mode dropout is not supported; '
                                       'use temporarily_select or remove')
-    if x.ndim == 3 and x.shape[0] == 1 and w.shape[0] != 1:
+    if row_index is not None:
+        pass  # x is the gathered table
+    elif x.ndim == 3 and x.shape[0] == 1 and w.shape[0] != 1:
         x = x[0]
     elif x.ndim == 3 and x.stride(0) == 0:
         x = x[0]
@@ -679,7 +690,7 @@ def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stre
     return packed_linear(x, w, b, in_features=inf, out_features=outf, n_blocks=n_blocks,
                          block_index=block_index, relu=relu, dropout_p=dropout, seed=seed, offset=offset,
                          member_base=member_base, cache=linear._cache if pack_idx is None else None,
-                         dx_cols=dx_cols)
+                         dx_cols=dx_cols, row_index=row_index)
 
 
 class DropoutPack(ModulePack):
@@ -777,7 +788,7 @@ class MLPBackbonePack(ModulePack):
 
         def forward(self, x: Tensor, pack_idx: Tensor | None = None, *, n_blocks: Tensor | None = None,
                     block_index: int = 0, stream: _DropoutStream | None = None, offset_stride: int = 1,
-                    onehot: dict | None = None, dx_cols: int = 0) -> Tensor:
+                    onehot: dict | None = None, dx_cols: int = 0, row_index: Tensor | None = None) -> Tensor:
             drop = None
             if self.training:
                 drop = self.dropout.probabilities(self.pack_size, x.device).contiguous()
@@ -789,7 +800,8 @@ class MLPBackbonePack(ModulePack):
                                            offset_add=block_index)
             return _linear_call(self.linear, x, pack_idx, relu=self._fused_relu(), dropout=drop,
                                 stream=stream or self.dropout._stream, n_blocks=n_blocks, block_index=block_index,
-                                offset_stride=offset_stride, offset_add=block_index, dx_cols=dx_cols)
+                                offset_stride=offset_stride, offset_add=block_index, dx_cols=dx_cols,
+                                row_index=row_index)
 
     @enum.unique
     class ForwardImpl(enum.StrEnum):
@@ -875,10 +887,11 @@ class MLPBackbonePack(ModulePack):
         return self._nb_cache[1]
 
     def forward(self, x: Tensor, pack_idx: Tensor | None = None, *, onehot: dict | None = None,
-                dx_cols: int = 0) -> Tensor:
+                dx_cols: int = 0, row_index: Tensor | None = None) -> Tensor:
         """`onehot`: the first block's one-hot columns, gathered instead of multiplied (`x` then
         holds only the dense columns; see `_onehot_linear_call`).  `dx_cols`: the input's
-        gradient is needed in its first dx_cols columns only."""
+        gradient is needed in its first dx_cols columns only.  `row_index` (pack_size, batch):
+        `x` is a (rows, in) table whose rows the first block's GEMMs gather."""
         if pack_idx is not None:
             check_pack_idx(pack_idx, self.pack_size)
             if onehot is not None:
@@ -895,6 +908,8 @@ class MLPBackbonePack(ModulePack):
                 first['onehot'] = onehot
             if i == 0 and dx_cols:
                 first['dx_cols'] = dx_cols
+            if i == 0 and row_index is not None:
+                first['row_index'] = row_index
             x = block(x, pack_idx, n_blocks=nb if i > 0 else None, block_index=i, stream=sub, **first)
         return x
 
@@ -1170,6 +1185,41 @@ class TabPack(ModulePack):
             return None
         return ops.tabpack_input(x_num, x_cat, self._cat_offsets, width, dtype, row_index=row_index)
 
+    # The per-step batch gather (`_training.py:2667-2669`) inside the first block's GEMM operand
+    # loads: the dataset's first-layer input ([x_num | one-hot(x_cat)], bf16, padded width) is
+    # built once and kept, and every step's rows are gathered from it by the forward and weight-
+    # gradient GEMMs (TMA gather4, 4 table rows per load) instead of being copied into a
+    # (pack, batch, width) tensor.  Off by default: on a B200 the gathered GEMMs (single CTAs,
+    # 32 gather loads per 16 KB operand stage) measured 2.7 ms (forward) and 3.7 ms (weight
+    # gradient) slower per step of the 512-member training configuration than the copied batch
+    # on CTA pairs, against 0.47 ms saved by not building the copy.
+    gather_batch_in_gemm = False
+
+    def _input_table(self, x_num: Tensor | None, x_cat: Tensor | None, row_index: Tensor,
+                     pack_idx: Tensor | None) -> Tensor | None:
+        """The dataset's encoded first-layer input for `forward_rows` to gather from, or None when
+        the other paths apply (no one-hot features, numerical embeddings, a member subset,
+        fp32 compute, per-member input datasets)."""
+        if not self.gather_batch_in_gemm or pack_idx is not None or x_cat is None or row_index.ndim != 2:
+            return None
+        if not (torch.is_autocast_enabled('cuda') and torch.get_autocast_dtype('cuda') == torch.bfloat16):
+            return None
+        # the cache holds the datasets weakly and keys on their identity and version counters, so
+        # a new or modified dataset (even one at a freed dataset's address) builds a new table
+        versions = tuple(None if t is None else t._version for t in (x_num, x_cat))
+        cached = self.__dict__.get('_table_cache')
+        if cached is not None:
+            refs, vers, offsets, table = cached
+            same = all((r is None and t is None) or (r is not None and r() is t) for r, t in zip(refs, (x_num, x_cat)))
+            if same and vers == versions and offsets is self._cat_offsets:
+                return table
+        table = self._fused_input(x_num, x_cat)  # every dataset row, no gather
+        if table is None or table.dtype != torch.bfloat16 or table.ndim != 2:
+            return None
+        refs = tuple(None if t is None else weakref.ref(t) for t in (x_num, x_cat))
+        self.__dict__['_table_cache'] = (refs, versions, self._cat_offsets, table)
+        return table
+
     # batch rows one gathered first-layer call sorts in shared memory (tp_onehot_linear_forward)
     _GATHER_MAX_ROWS = 16384
 
@@ -1283,6 +1333,9 @@ class TabPack(ModulePack):
         emb = self._embedded_input(x_num, x_cat, row_index, pack_idx)
         if emb is not None:
             return self.output(self.backbone(emb[0], pack_idx, dx_cols=emb[1]), pack_idx)
+        table = self._input_table(x_num, x_cat, row_index, pack_idx)
+        if table is not None:
+            return self.output(self.backbone(table, pack_idx, row_index=row_index), pack_idx)
         fused = None if x_cat is None else self._fused_input(x_num, x_cat, row_index)
         if fused is None:
             return self(None if x_num is None else x_num[row_index], None if x_cat is None else x_cat[row_index],

@@ -79,14 +79,16 @@ def _i32(name: str, t: Tensor | None) -> Tensor | None:
 
 
 def _linear_args(x, weight, bias, in_features, out_features, n_blocks, block_index, relu,
-                 dropout_p, seed, offset, member_base, y) -> _lib.LinearArgs:
+                 dropout_p, seed, offset, member_base, y, row_index=None) -> _lib.LinearArgs:
     P, max_out, max_in = weight.shape
-    shared = x.ndim == 2
-    B = x.shape[0] if shared else x.shape[1]
+    shared = x.ndim == 2 and row_index is None
+    B = row_index.shape[1] if row_index is not None else x.shape[0] if shared else x.shape[1]
     a = _lib.LinearArgs()
     a.P, a.B, a.max_in, a.max_out = P, B, max_in, max_out
     a.dtype = _dtype_code(x.dtype)
     a.x_shared = 1 if shared else 0
+    if row_index is not None:
+        a.row_index, a.x_rows = row_index.data_ptr(), x.shape[0]
     a.in_features = _ptr(in_features)
     a.out_features = _ptr(out_features)
     a.n_blocks = _ptr(n_blocks)
@@ -103,6 +105,17 @@ def _linear_args(x, weight, bias, in_features, out_features, n_blocks, block_ind
     return a
 
 
+def _row_index(row_index: Tensor | None, P: int) -> Tensor | None:
+    """(P, B) int32 CUDA row indices of a gathered input, or None."""
+    if row_index is None:
+        return None
+    if row_index.ndim != 2 or row_index.shape[0] != P:
+        raise ValueError(f'row_index must be (pack_size={P}, batch), got {tuple(row_index.shape)}')
+    if not row_index.is_cuda:
+        raise RuntimeError('row_index must be a CUDA tensor (tabpack_b200 has no CPU path)')
+    return row_index.to(torch.int32).contiguous()
+
+
 def linear_forward(
     x: Tensor,
     weight: Tensor,
@@ -117,19 +130,23 @@ def linear_forward(
     seed: int = 0,
     offset: int = 0,
     member_base: int = 0,
+    row_index: Tensor | None = None,
 ) -> Tensor:
-    """Packed linear (+ReLU +dropout +depth gating) forward; see `tp_linear_forward`."""
+    """Packed linear (+ReLU +dropout +depth gating) forward; see `tp_linear_forward`.  With
+    `row_index` (P, B), x is a (rows, in) table and member m's input row b is
+    x[row_index[m, b]] (gathered by the GEMM's operand loads)."""
     weight = _cuda('weight', weight)
     x = _cuda('x', x, weight.dtype)
+    row_index = _row_index(row_index, weight.shape[0])
     bias = _cuda('bias', bias, torch.float32)
     dropout_p = _cuda('dropout_p', dropout_p, torch.float32)
     in_features, out_features, n_blocks = (_i32(n, t) for n, t in (
         ('in_features', in_features), ('out_features', out_features), ('n_blocks', n_blocks)))
     P, max_out, _ = weight.shape
-    B = x.shape[-2]
+    B = x.shape[-2] if row_index is None else row_index.shape[1]
     y = torch.empty((P, B, max_out), dtype=x.dtype, device=x.device)
     a = _linear_args(x, weight, bias, in_features, out_features, n_blocks, block_index, relu,
-                     dropout_p, seed, offset, member_base, y)
+                     dropout_p, seed, offset, member_base, y, row_index)
     check(load().tp_linear_forward(ctypes.byref(a), _stream()), 'tp_linear_forward')
     return y
 
@@ -155,18 +172,23 @@ def linear_backward(
     dw_shape: tuple[int, int] | None = None,
     db_cols: int | None = None,
     dx_cols: int = 0,
+    row_index: Tensor | None = None,
 ) -> tuple[Tensor | None, Tensor | None, Tensor | None]:
     """Backward of `linear_forward`: returns (dx, dw, db); dw/db are fp32.  With dx_cols > 0
-    only dx's first dx_cols columns are computed (the rest are zeros)."""
+    only dx's first dx_cols columns are computed (the rest are zeros).  With `row_index`, x is
+    the forward's table (no dx)."""
     weight = _cuda('weight', weight)
     x = _cuda('x', x, weight.dtype)
+    row_index = _row_index(row_index, weight.shape[0])
+    if row_index is not None and need_dx:
+        raise ValueError('a gathered input (a table) takes no input gradient')
     dy = _cuda('dy', dy, weight.dtype)
     y = _cuda('y', y, weight.dtype)
     dropout_p = _cuda('dropout_p', dropout_p, torch.float32)
     in_features, out_features, n_blocks = (_i32(n, t) for n, t in (
         ('in_features', in_features), ('out_features', out_features), ('n_blocks', n_blocks)))
     P, max_out, max_in = weight.shape
-    B = x.shape[-2]
+    B = x.shape[-2] if row_index is None else row_index.shape[1]
     need_g = relu or dropout_p is not None or out_features is not None or n_blocks is not None
     g = torch.empty_like(dy) if need_g else None
     dx = torch.empty((P, B, max_in), dtype=dy.dtype, device=dy.device) if need_dx else None
@@ -176,7 +198,7 @@ def linear_backward(
     db = torch.empty((P, dbc), dtype=torch.float32, device=dy.device) if need_db else None
     ga = _lib.LinearGradArgs()
     ga.fwd = _linear_args(x, weight, None, in_features, out_features, n_blocks, block_index, relu,
-                          dropout_p, seed, offset, member_base, None)
+                          dropout_p, seed, offset, member_base, None, row_index)
     ga.dy, ga.y, ga.g = _ptr(dy), _ptr(y), _ptr(g)
     ga.dbias, ga.dx, ga.dw = _ptr(db), _ptr(dx), _ptr(dw)
     ga.dw_rows, ga.dw_cols, ga.db_cols = rows, cols, dbc

@@ -453,3 +453,44 @@ def test_forward_into_zero_padded_buffer_skips_the_padding():
         assert torch.equal(y[~pad.expand_as(y)].view(torch.int16), want[~pad.expand_as(want)].view(torch.int16))
         assert bool((y[far.expand_as(y)] == fill).all())
         assert bool((y[(pad & ~far).expand_as(y)] == 0).all())
+
+
+@pytest.mark.parametrize('B', [1000, 258])
+def test_gathered_input_matches_the_materialised_batch(B):
+    """The first layer with its batch gathered by the GEMMs' operand loads (a (rows, 2544)
+    bf16 table and per-member row indices, TMA gather4) against the same layer on the
+    materialised per-member batch table[row_index]: forward output (ReLU + dropout, ragged
+    widths), weight and bias gradients.  Rows past the batch (B not a multiple of the tiles)
+    included."""
+    from tabpack_b200 import ops
+
+    P, N, K, O = 12, 4099, 2544, 1024
+    rng = np.random.default_rng(B)
+    out_np = (rng.integers(16, 129, P) * 8).astype(np.int32)
+    outf = torch.from_numpy(out_np).cuda()
+    inf = torch.full((P,), 2538, dtype=torch.int32, device='cuda')
+    p = torch.from_numpy(rng.uniform(0, 0.5, P).astype(np.float32)).cuda()
+    g = torch.Generator(device='cuda').manual_seed(B)
+    kin = torch.arange(K, device='cuda') < 2538
+    table = (torch.randn(N, K, device='cuda', generator=g) * kin).bfloat16()
+    ri = torch.randint(0, N, (P, B), device='cuda', generator=g)
+    w = ((torch.rand(P, O, K, device='cuda', generator=g) * 2 - 1) / 50 * kin).bfloat16()
+    b = (torch.rand(P, O, device='cuda', generator=g) * 2 - 1) / 50
+    kw = dict(in_features=inf, out_features=outf, relu=True, dropout_p=p, seed=11, offset=2)
+    x = table[ri]  # (P, B, K) materialised
+    y_g = ops.linear_forward(table, w, b, row_index=ri, **kw)
+    y_m = ops.linear_forward(x, w, b, **kw)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    _close_dev(y_g, y_m, BF16_RTOL, 'gathered forward')
+    print('forward: bit-equal fraction', float((y_g.view(torch.int16) == y_m.view(torch.int16)).float().mean()))
+    dy = torch.randn(P, B, O, device='cuda', generator=g).bfloat16()
+    _, dw_g, db_g = ops.linear_backward(dy, table, w, y_g, row_index=ri, need_dx=False, **kw)
+    _, dw_m, db_m = ops.linear_backward(dy, x, w, y_m, need_dx=False, **kw)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    _close_dev(db_g, db_m, 1e-4, 'gathered bias gradient')
+    _close_dev(dw_g, dw_m, BF16_RTOL, 'gathered weight gradient')
+    pad = torch.arange(O, device='cuda')[None, :, None] >= outf[:, None, None]
+    assert int(torch.count_nonzero(dw_g * pad)) == 0
+    print('weight gradient: bit-equal fraction', float((dw_g == dw_m).float().mean()))

@@ -183,6 +183,48 @@ def test_forward_rows_equals_gathered_forward():
         assert torch.equal(a, b), autocast
 
 
+def test_forward_rows_with_the_gemm_gather_matches_the_copied_batch():
+    """TabPack.forward_rows under bf16 autocast gathers each step's rows inside the first block's
+    GEMM loads from a table of the whole dataset (`gather_batch_in_gemm`): output and every
+    parameter gradient against the same step with the batch copied into a (pack, batch,
+    width) input first; the table is built once and reused while the dataset is unchanged."""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+    from tabpack_b200 import nn as bnn
+
+    torch.manual_seed(3)
+    P, N, B = 6, 3000, 300
+    cards = [300, 7, 500, 120]
+    model = bnn.TabPack(n_numerical_features=20, categorical_cardinalities=cards, d_out=1, n_blocks=[1, 2, 3, 2, 1, 3],
+                        d_block=[256, 128, 512, 64, 384, 200], dropout=[0.1, 0.2, 0.0, 0.3, 0.25, 0.05], pack_size=P,
+                        max_d_block=512).cuda().train()
+    g = torch.Generator(device='cuda').manual_seed(4)
+    x_num = torch.randn(N, 20, device='cuda', generator=g)
+    x_cat = torch.stack([torch.randint(0, c + 1, (N,), device='cuda', generator=g) for c in cards], 1)
+    grads = []
+    for gather in (True, False):
+        model.gather_batch_in_gemm = gather
+        for rep in range(2):
+            idx = torch.randint(0, N, (P, B), device='cuda', generator=torch.Generator(device='cuda').manual_seed(rep))
+            model.zero_grad(set_to_none=True)
+            with torch.autocast('cuda', dtype=torch.bfloat16):
+                model.backbone._stream.seed, model.backbone._stream.calls = 9, 0
+                y = model.forward_rows(x_num, x_cat, idx)
+            y.float().square().mean().backward()
+            if rep == 1:
+                grads.append((y.detach(), {n: q.grad.clone() for n, q in model.named_parameters() if q.grad is not None}))
+        if gather:
+            table = model.__dict__['_table_cache'][3]
+            assert table.shape == (N, (20 + sum(cards) + 7) // 8 * 8)
+    (ya, ga), (yb, gb) = grads
+    assert torch.equal(ya, yb)
+    assert ga.keys() == gb.keys()
+    for n in ga:
+        a, b = ga[n].float(), gb[n].float()
+        err = float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+        assert err <= 2 ** -7, (n, err)
+
+
 def test_weight_cast_writes_active_rows_only():
     """tp_weight_cast: bf16 (round to nearest even, as torch's cast) over rows < out_features
     of active members, zeros from in_features to the padded width; the other rows and the
