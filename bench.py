@@ -689,7 +689,7 @@ def train_work(per: list[dict], d_in: int, batch: int = BATCH) -> dict[str, floa
     forward / dgrad / wgrad GEMMs of the blocks and the 1-wide head (the first layer takes no
     input gradient), and the Newton-Schulz GEMMs of Muon (5 iterations of 4 r^2 c + 2 r^3 per
     block weight, r = min and c = max of its shape)."""
-    fwd = dgrad = wgrad = ns = 0.0
+    fwd = dgrad = wgrad = ns = ns_exec = 0.0
     for pm in per:
         w, nb = pm['d_block'], pm['n_blocks']
         mm = d_in * w + (nb - 1) * w * w + w
@@ -699,12 +699,27 @@ def train_work(per: list[dict], d_in: int, batch: int = BATCH) -> dict[str, floa
         for j in range(nb):
             r, c = min(w, d_in if j == 0 else w), max(w, d_in if j == 0 else w)
             ns += 5.0 * (4.0 * r * r * c + 2.0 * r ** 3)
-    return {'fwd': fwd, 'dgrad': dgrad, 'wgrad': wgrad, 'newton_schulz': ns}
+            ns_exec += 5.0 * (2.0 * r * r * c * ns_symmetric_fraction(r) + 2.0 * r ** 3 * ns_symmetric_fraction(r)
+                              + 2.0 * r * r * c)
+    return {'fwd': fwd, 'dgrad': dgrad, 'wgrad': wgrad, 'newton_schulz': ns, 'newton_schulz_executed': ns_exec}
+
+
+def ns_symmetric_fraction(r: int) -> float:
+    """Fraction of an r x r symmetric Newton-Schulz product (A = X X^T, B = b A + c A^2) that
+    the kernels compute directly: the 128 x 256 tiles not entirely below the diagonal (the rest
+    are written as transposes), counted over the matrix's r x r elements."""
+    done = 0
+    for nt in range((r + 255) // 256):
+        cols = min(256, r - 256 * nt)
+        for mt in range(min((r + 127) // 128, 2 * nt + 2)):
+            done += min(128, r - 128 * mt) * cols
+    return done / float(r * r)
 
 
 def member_cost(pm: dict, d_in: int) -> float:
-    """A member's FLOPs per training step (the sharding weight)."""
-    return sum(train_work([pm], d_in).values())
+    """A member's FLOPs per training step as the kernels execute them (the sharding weight)."""
+    w = train_work([pm], d_in)
+    return w['fwd'] + w['dgrad'] + w['wgrad'] + w['newton_schulz_executed']
 
 
 def _compact(line: dict) -> dict:
@@ -863,6 +878,7 @@ def run_train(args) -> None:
     members_per_rank = [b - a for a, b in trainer.ranges]
     fam_ms = {k: kt.ms[k] / K for k in kt.ms if kt.launches[k]}
     fam_ms['newton_schulz'] = fam_ms.pop('newton_schulz_gram', 0.0) + fam_ms.pop('newton_schulz_update', 0.0)
+    ns_exec = local_work.pop('newton_schulz_executed')
     mean_loss = float(loss.mean())
     del trainer, dev_data, pinned, up, warm, preds, preds_e2e, ens, loss
     torch.cuda.empty_cache()
@@ -882,6 +898,12 @@ def run_train(args) -> None:
             ach = local_work[fam] / (fam_ms[fam] / 1e3) / 1e12
             gemm[fam] = {'ms_per_step': fam_ms[fam], 'tflop_per_step': local_work[fam] / 1e12, 'tflops': ach,
                          'frac': ach / peak}
+    if 'newton_schulz' in gemm:
+        # the symmetric products compute only the tiles on or above the diagonal: the FLOPs
+        # the kernels execute, beside the reference iteration's algorithmic count above
+        ex = ns_exec / (fam_ms['newton_schulz'] / 1e3) / 1e12
+        gemm['newton_schulz'].update({'executed_tflop_per_step': ns_exec / 1e12, 'executed_tflops': ex,
+                                      'executed_frac': ex / peak})
     dominant = max(gemm, key=lambda f: gemm[f]['ms_per_step'])
     roof = {'bound': 'tensor', 'achieved': gemm[dominant]['tflops'], 'peak': peak, 'unit': 'TFLOP/s',
             'frac': gemm[dominant]['frac'], 'kernel': dominant,

@@ -164,6 +164,30 @@ __device__ __forceinline__ void dgrad_chunk(const TileInfo& ti, int col0, const 
   }
 }
 
+// The transpose of a warp's staged 32 x 32 bf16 chunk (rows row_base.., columns col0..): row
+// col0 + j of member m's output receives the chunk's column j in its columns row_base..+31 (a
+// symmetric product's tile below the diagonal, which is not computed).  Four lanes per output
+// row, 16 bytes each: lane l writes rows (l / 4) + 8k, k = 0..3, columns row_base + 8 (l % 4)..+7.
+__device__ __forceinline__ void mirror_flush(const LinearProblem& pr, int m, int row_base, int col0,
+                                             const uint8_t* stage_warp, int lane, int row_bytes) {
+  const int c = lane & 3;
+  if (row_base + 8 * c >= pr.out_cols) return;
+  __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms + row_base + 8 * c;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int jj = (lane >> 2) + 8 * k;
+    if (col0 + jj >= pr.out_rows) continue;
+    uint32_t v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t lo = *reinterpret_cast<const unsigned short*>(stage_warp + (8 * c + 2 * e) * row_bytes + 2 * jj);
+      const uint32_t hi = *reinterpret_cast<const unsigned short*>(stage_warp + (8 * c + 2 * e + 1) * row_bytes + 2 * jj);
+      v[e] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint4*>(base + (size_t)(col0 + jj) * pr.out_ld) = make_uint4(v[0], v[1], v[2], v[3]);
+  }
+}
+
 // Writes a warp's staged 32 x 32 bf16 chunk (rows row_base.., columns col0..) to global
 // memory with 4 lanes per row (64 contiguous bytes), so one store instruction covers
 // 8 rows instead of 32 scattered 16-byte pieces.
@@ -605,6 +629,9 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
           // the next pair is loaded while this pair is computed.
           const bool rv = row < ti.m_valid;
           const int nch_k = min(nch, max(0, (((ti.n_valid + 63) & ~63) - cbase + 31) / 32));
+          // symmetric product: this warp's half is also written transposed into a tile below
+          // the diagonal (one that the tile list leaves out) when that tile lies entirely there
+          const bool mirror = pr.ns_sym && ((ti.mt >> 1) * 2 + 2 <= 2 * ti.nt + half);
           uint32_t na[32], nb[32];
 #pragma unroll 1
           for (int c = 0; c < nch_k; c += 2) {
@@ -619,12 +646,14 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
             ns_chunk(pr, rv, ti.n_valid - col0, na, d_a, stage_row);
             __syncwarp();
             stage_flush(pr, m, row_base, col0, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
+            if (mirror) mirror_flush(pr, m, row_base, col0, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
             __syncwarp();
             if (two) {
               if (c + 2 < nch_k) ns_load_d(d_row, col0 + 64, ti.n_valid - col0 - 64, d_a);
               ns_chunk(pr, rv, ti.n_valid - col0 - 32, nb, d_b, stage_row);
               __syncwarp();
               stage_flush(pr, m, row_base, col0 + 32, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
+              if (mirror) mirror_flush(pr, m, row_base, col0 + 32, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
               __syncwarp();
             }
           }

@@ -78,6 +78,7 @@ struct LinearProblem {
   const int32_t* ns_cols;
   const int32_t* active;
   int ns_shape;
+  int ns_sym;  // symmetric output (A = X X^T): tiles below the diagonal come as transposes
   float alpha, beta;
   const void* D;  // (optional) addend with the output's geometry
   // MODE_FWD_ADD: fp32 addend (P, B, add_ld) added to the accumulator before the bias

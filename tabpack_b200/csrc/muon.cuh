@@ -57,46 +57,53 @@ __global__ void muon_geometry_kernel(MuonArgs a) {
 }
 
 // Dense lists of the Newton-Schulz launches' MMA tiles (128 x 256 output tiles of the
-// tcgen05 kernel): list_rr for the r x r products (A = X X^T and B = b A + c A^2), list_rc for
-// the r x c update X <- a X + B X.  Entry = member << 16 | n-tile << 8 | m-tile; a member's
+// tcgen05 kernel): list_rr for the r x r product B = b A + c A^2, list_rc for the r x c update
+// X <- a X + B X, and list_sym for the symmetric r x r product A = X X^T: only the tiles not
+// entirely below the diagonal (n-tile nt, m-tile mt with 256 nt + 256 > 128 mt); the epilogue
+// writes the others as transposes.  Entry = member << 16 | n-tile << 8 | m-tile; a member's
 // tiles go column block by column block, down the rows within one.  Members whose update is
-// zero (active == 0) have none.  One block of 1024 threads scans the members in chunks.
+// zero (active == 0) have none.  One block of 1024 threads scans the members in chunks;
+// counts[0..2] receive the three lengths.
 constexpr int NS_TILE_M = 128, NS_TILE_N = 256;
+constexpr int NS_LISTS = 3;
+
+__device__ __forceinline__ int ns_sym_mtiles(int nt, int mt_all) { return min(mt_all, 2 * nt + 2); }
 
 __global__ void __launch_bounds__(1024) ns_tile_list_kernel(MuonArgs a, uint32_t* list_rr, uint32_t* list_rc,
-                                                            int* counts) {
-  __shared__ int wsum[2][32];
-  __shared__ int base[2];
+                                                            uint32_t* list_sym, int* counts) {
+  __shared__ int wsum[NS_LISTS][32];
+  __shared__ int base[NS_LISTS];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  if (tid == 0) base[0] = base[1] = 0;
+  if (tid < NS_LISTS) base[tid] = 0;
   __syncthreads();
   for (int m0 = 0; m0 < a.P; m0 += 1024) {
     const int m = m0 + tid;
-    int mt = 0, nrr = 0, nrc = 0;
+    int mt = 0, nrr = 0, nrc = 0, nsym = 0;
     if (m < a.P && a.active[m] != 0) {
       const int r = a.rows[m], c = a.cols[m];
       mt = (r + NS_TILE_M - 1) / NS_TILE_M;
       nrr = (r + NS_TILE_N - 1) / NS_TILE_N;
       nrc = (c + NS_TILE_N - 1) / NS_TILE_N;
+      for (int nt = 0; nt < nrr; ++nt) nsym += ns_sym_mtiles(nt, mt);
     }
-    int v[2] = {mt * nrr, mt * nrc};
-    int incl[2] = {v[0], v[1]};
+    const int v[NS_LISTS] = {mt * nrr, mt * nrc, nsym};
+    int incl[NS_LISTS] = {v[0], v[1], v[2]};
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < NS_LISTS; ++j) {
         const int o = __shfl_up_sync(0xFFFFFFFFu, incl[j], d);
         if (lane >= d) incl[j] += o;
       }
     }
     if (lane == 31) {
-      wsum[0][wid] = incl[0];
-      wsum[1][wid] = incl[1];
+#pragma unroll
+      for (int j = 0; j < NS_LISTS; ++j) wsum[j][wid] = incl[j];
     }
     __syncthreads();
     if (wid == 0) {
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < NS_LISTS; ++j) {
         int x = wsum[j][lane];
 #pragma unroll
         for (int d = 1; d < 32; d <<= 1) {
@@ -107,22 +114,19 @@ __global__ void __launch_bounds__(1024) ns_tile_list_kernel(MuonArgs a, uint32_t
       }
     }
     __syncthreads();
-    int off[2];
+    int off[NS_LISTS];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) off[j] = base[j] + (wid > 0 ? wsum[j][wid - 1] : 0) + incl[j] - v[j];
-    for (int i = 0; i < v[0]; ++i) list_rr[off[0] + i] = ((uint32_t)m << 16) | ((uint32_t)(i / mt) << 8) | (uint32_t)(i % mt);
-    for (int i = 0; i < v[1]; ++i) list_rc[off[1] + i] = ((uint32_t)m << 16) | ((uint32_t)(i / mt) << 8) | (uint32_t)(i % mt);
+    for (int j = 0; j < NS_LISTS; ++j) off[j] = base[j] + (wid > 0 ? wsum[j][wid - 1] : 0) + incl[j] - v[j];
+    const uint32_t mk = (uint32_t)m << 16;
+    for (int i = 0; i < v[0]; ++i) list_rr[off[0] + i] = mk | ((uint32_t)(i / mt) << 8) | (uint32_t)(i % mt);
+    for (int i = 0; i < v[1]; ++i) list_rc[off[1] + i] = mk | ((uint32_t)(i / mt) << 8) | (uint32_t)(i % mt);
+    for (int nt = 0, o = off[2]; nt < nrr; ++nt)
+      for (int t = 0; t < ns_sym_mtiles(nt, mt); ++t) list_sym[o++] = mk | ((uint32_t)nt << 8) | (uint32_t)t;
     __syncthreads();
-    if (tid == 0) {
-      base[0] += wsum[0][31];
-      base[1] += wsum[1][31];
-    }
+    if (tid < NS_LISTS) base[tid] += wsum[tid][31];
     __syncthreads();
   }
-  if (tid == 0) {
-    counts[0] = base[0];
-    counts[1] = base[1];
-  }
+  if (tid < NS_LISTS) counts[tid] = base[tid];
 }
 
 // Tiles of the Muon elementwise kernels: 32 weight rows (o) x 128 weight columns (n), 256

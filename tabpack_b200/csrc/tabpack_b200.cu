@@ -344,7 +344,7 @@ LinearProblem base_problem(const tp_linear_args* a) {
 struct MuonLayout {
   int R_s, C_s, tiles;
   size_t off_x0, off_x1, off_a, off_b, off_norm, off_rows, off_cols, off_trans, off_active, off_partial, off_counter,
-      off_list_rr, off_list_rc, off_list_n, total;
+      off_list_rr, off_list_rc, off_list_sym, off_list_n, total;
 };
 
 constexpr int MUON_COUNTERS = 64;
@@ -372,7 +372,8 @@ MuonLayout muon_layout(int P, int max_out, int max_in) {
   const size_t mtl = (size_t)L.R_s / NS_TILE_M;
   L.off_list_rr = take((size_t)P * mtl * ((L.R_s + NS_TILE_N - 1) / NS_TILE_N) * 4);
   L.off_list_rc = take((size_t)P * mtl * ((L.C_s + NS_TILE_N - 1) / NS_TILE_N) * 4);
-  L.off_list_n = take(2 * 4);
+  L.off_list_sym = take((size_t)P * mtl * ((L.R_s + NS_TILE_N - 1) / NS_TILE_N) * 4);
+  L.off_list_n = take(NS_LISTS * 4);
   L.total = o;
   return L;
 }
@@ -381,12 +382,13 @@ MuonLayout muon_layout(int P, int max_out, int max_in) {
 template <int MODE>
 int ns_gemm(const MuonArgs& ma, int shape, const void* a_op, int a_cols, const void* b_op, int b_cols,
             void* out, int out_cols, const void* d, float alpha, float beta, const uint32_t* list,
-            const int* list_n, int* counter, cudaStream_t st) {
+            const int* list_n, int* counter, cudaStream_t st, int sym = 0) {
   constexpr int BN = 256;
   static_assert(BN == NS_TILE_N && Sm100Cfg<BN, MODE>::TILE_M == NS_TILE_M, "tile lists match the kernel's tiles");
   LinearProblem pr{};
   pr.tile_list = list;  // the launch's MMA tiles, claimed dynamically (ragged members)
   pr.tile_count = list_n;
+  pr.ns_sym = sym;
   pr.tile_counter = counter;  // zeroed
   pr.mode = MODE;
   pr.P = ma.P;
@@ -829,6 +831,7 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
     return fail(TP_EINVAL, "Muon matrices of at most 32640 x 65280 elements (got %d x %d)", a->max_out, a->max_in);
   uint32_t* list_rr = reinterpret_cast<uint32_t*>(ws + L.off_list_rr);
   uint32_t* list_rc = reinterpret_cast<uint32_t*>(ws + L.off_list_rc);
+  uint32_t* list_sym = reinterpret_cast<uint32_t*>(ws + L.off_list_sym);
   int* list_n = reinterpret_cast<int*>(ws + L.off_list_n);
   dim3 tiles((a->max_in + MUON_TN - 1) / MUON_TN, (a->max_out + MUON_TM - 1) / MUON_TM, a->P);
   dim3 ngrid((L.C_s + 255) / 256, (L.R_s + 31) / 32, a->P);
@@ -838,7 +841,7 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
     muon_prologue_kernel<<<tiles, 256, 0, st>>>(m);
     muon_norm_kernel<<<a->P, 256, 0, st>>>(m, (int)tiles.x);
     muon_normalize_kernel<<<ngrid, 256, 0, st>>>(m, 128, 256);
-    ns_tile_list_kernel<<<1, 1024, 0, st>>>(m, list_rr, list_rc, list_n);
+    ns_tile_list_kernel<<<1, 1024, 0, st>>>(m, list_rr, list_rc, list_sym, list_n);
   }
   TP_CUDA_TRY(cudaGetLastError());
   // quintic Newton-Schulz, coefficients of optim.py:477
@@ -860,9 +863,13 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
     int* c2 = counter();
     int* c3 = counter();
     if (!c1 || !c2 || !c3) return fail(TP_ECUDA, "cudaMemsetAsync of the tile counters failed");
-    if ((rc = ns_gemm<MODE_NS>(m, 1, X, L.C_s, X, L.C_s, A, L.R_s, nullptr, 1.0f, 0.0f, list_rr, list_n, c1, st)))
+    // A = X X^T is symmetric: only the tiles not below the diagonal, the rest written as transposes
+    if ((rc = ns_gemm<MODE_NS>(m, 1, X, L.C_s, X, L.C_s, A, L.R_s, nullptr, 1.0f, 0.0f, list_sym, list_n + 2, c1, st,
+                               1)))
       return rc;
-    if ((rc = ns_gemm<MODE_NS>(m, 2, A, L.R_s, A, L.R_s, Bm, L.R_s, A, cc, cb, list_rr, list_n, c2, st))) return rc;
+    // B = b A + c A^2 is symmetric as well
+    if ((rc = ns_gemm<MODE_NS>(m, 2, A, L.R_s, A, L.R_s, Bm, L.R_s, A, cc, cb, list_sym, list_n + 2, c2, st, 1)))
+      return rc;
     if ((rc = ns_gemm<MODE_NS_BMN>(m, 3, Bm, L.R_s, X, L.C_s, Xn, L.C_s, X, 1.0f, ca, list_rc, list_n + 1, c3, st)))
       return rc;
     std::swap(X, Xn);
