@@ -92,6 +92,11 @@ typedef struct tp_linear_grad_args {
   int32_t dx_cols;    /* > 0: dx only for input columns < dx_cols (zeros beyond), e.g. the
                          embedding columns of a first layer whose one-hot columns take no
                          gradient; 0: every column */
+  int32_t dw_pad_zero; /* 1: dw already holds zeros outside each active member's
+                          out_features x in_features block and for every depth-inactive member
+                          (a buffer that an earlier call with the same widths and depths wrote):
+                          the weight gradient writes the active members' blocks only (output
+                          features rounded up to a multiple of 32).  0: it writes every element. */
 } tp_linear_grad_args;
 
 /* LinearPack.forward (src/tabpackage/nn.py:792-816) fused with the ReLU and

@@ -41,7 +41,7 @@ class LinearGradArgs(ctypes.Structure):
         ('fwd', LinearArgs), ('dy', ctypes.c_void_p), ('y', ctypes.c_void_p), ('g', ctypes.c_void_p),
         ('dbias', ctypes.c_void_p), ('dx', ctypes.c_void_p), ('dw', ctypes.c_void_p),
         ('dw_rows', ctypes.c_int32), ('dw_cols', ctypes.c_int32), ('db_cols', ctypes.c_int32),
-        ('g_ready', ctypes.c_int32), ('dx_cols', ctypes.c_int32),
+        ('g_ready', ctypes.c_int32), ('dx_cols', ctypes.c_int32), ('dw_pad_zero', ctypes.c_int32),
     ]
 
 

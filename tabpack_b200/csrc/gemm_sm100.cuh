@@ -663,7 +663,8 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
           float* base = reinterpret_cast<float*>(pr.out) + (size_t)m * pr.out_ms;
           const bool in_store = row < pr.out_cols;
           const bool in_valid = row < ti.m_valid;
-          const int nco = min(NCH, max(0, (pr.out_rows - cbase + 31) / 32));
+          // with the padding known zero, only the chunks that hold the member's output features
+          const int nco = min(NCH, max(0, ((pr.skip_zero ? min(pr.out_rows, ti.n_valid) : pr.out_rows) - cbase + 31) / 32));
           uint32_t wa[32];
 #pragma unroll 1
           for (int c = 0; c < nco; ++c) {

@@ -693,6 +693,7 @@ int linear_backward_impl(const tp_linear_grad_args* ga, int dw_ld_in, void* stre
     if (dw_ld < dw_cols) return fail(TP_EINVAL, "dw row stride below its columns");
     LinearProblem pr = base_problem(a);
     pr.mode = MODE_WGRAD;
+    pr.skip_zero = ga->dw_pad_zero != 0;
     pr.out = ga->dw;
     pr.out_rows = dw_rows;
     pr.out_cols = dw_cols;

@@ -422,6 +422,20 @@ def _round8(n: int) -> int:
     return (n + 7) // 8 * 8
 
 
+def _weight_gradient_buffer(slot: dict, shape: tuple, device, key) -> Tensor:
+    """The weight gradient's buffer for a layer whose gradients the trainer owns: the previous
+    step's storage again once nothing holds that step's gradient any more (its padding and the
+    depth-inactive members' blocks are still zero, so the kernel writes the active blocks only),
+    else a zeroed new one.  `key` (widths and depths) must match the previous step's."""
+    st, ref = slot.get('storage'), slot.get('ref')
+    if (st is not None and slot.get('shape') == shape and slot.get('key') == key and st.device == device
+            and (ref is None or ref() is None)):
+        return torch.empty(0, dtype=torch.float32, device=device).set_(st, 0, shape)
+    t = torch.zeros(shape, dtype=torch.float32, device=device)
+    slot.update(storage=t.untyped_storage(), shape=shape, key=key, ref=None)
+    return t
+
+
 class _PackedLinearFn(torch.autograd.Function):
     """One fused launch forward, three in backward (activation grad + bias grad,
     dgrad, wgrad); `cfg` carries the non-tensor configuration."""
@@ -439,10 +453,17 @@ class _PackedLinearFn(torch.autograd.Function):
         x, w_compute, y = ctx.saved_tensors
         cfg = ctx.cfg
         need_dx, need_dw, need_db = ctx.needs_input_grad[0], ctx.needs_input_grad[1], ctx.needs_input_grad[2]
+        slot = cfg.get('dw_slot')
+        dw_out = None
+        if slot is not None and need_dw:
+            dw_out = _weight_gradient_buffer(slot, tuple(cfg['w_shape']), dy.device, cfg['dw_key'])
         dx, dw, db = ops.linear_backward(
             dy.contiguous().to(w_compute.dtype), x, w_compute, y, **cfg['kw'],
             need_dx=need_dx, need_dw=need_dw, need_db=need_db,
-            dw_shape=cfg['w_shape'][1:], db_cols=cfg['w_shape'][1], dx_cols=cfg.get('dx_cols', 0))
+            dw_shape=cfg['w_shape'][1:], db_cols=cfg['w_shape'][1], dx_cols=cfg.get('dx_cols', 0),
+            dw_out=dw_out, dw_pad_zero=dw_out is not None)
+        if dw_out is not None:
+            slot['ref'] = weakref.ref(dw)  # reusable once the optimizer has dropped this gradient
         if dx is not None:
             if len(ctx.x_shape) == 2:
                 dx = dx.sum(PACK_DIM)
@@ -454,7 +475,7 @@ class _PackedLinearFn(torch.autograd.Function):
 def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features=None, out_features=None,
                   n_blocks=None, block_index=0, relu=False, dropout_p=None, seed=0, offset=0,
                   member_base=0, cache: _WeightCache | None = None, dx_cols: int = 0,
-                  row_index: Tensor | None = None) -> Tensor:
+                  row_index: Tensor | None = None, dw_slot: dict | None = None) -> Tensor:
     """Functional form of the fused packed linear layer (see module docstring).  `dx_cols` > 0:
     the input's gradient is needed in its first dx_cols columns only (zeros beyond).
     `row_index` (pack_size, batch): `x` is a (rows, in) table and member m's input row b is
@@ -487,6 +508,10 @@ def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features
             raise ValueError('a gathered input (a table) takes no gradient')
         kw['row_index'] = row_index
     cfg = {'kw': kw, 'w_shape': tuple(weight.shape), 'in_cols': in_cols, 'dx_cols': int(dx_cols)}
+    if dw_slot is not None:
+        tag = lambda t: None if t is None else (t.data_ptr(), t._version, tuple(t.shape))  # noqa: E731
+        cfg['dw_slot'] = dw_slot
+        cfg['dw_key'] = (tag(out_features), tag(in_features), tag(n_blocks), int(block_index))
     with torch.autocast(x.device.type, enabled=False):
         y = _PackedLinearFn.apply(xc, weight, bias, wc, bc, cfg)
     return y if rows == max_out else y[..., :max_out]
@@ -579,6 +604,13 @@ def _widths_cached(module: nn.Module, name: str, buf: Tensor | None) -> Tensor |
 class LinearPack(ModulePack):
     """`LinearPack` (`nn.py:598-816`) on the fused ragged grouped GEMM."""
 
+    # Set by a training loop that owns the gradients (PackTrainer): each backward writes the
+    # weight gradient into the previous step's storage once nothing holds that step's gradient
+    # (the optimizer has stepped and the gradients were set to None); its padding and the
+    # depth-inactive members' blocks are still zero there, so only the active blocks are
+    # written.  Code that modifies a weight gradient's padding in place must leave it off.
+    reuse_weight_gradient = False
+
     def __init__(self, in_features, out_features, bias: bool = True, *, max_in_features=None,
                  max_out_features=None, pack_size: int, dtype=None, device=None) -> None:
         if pack_size <= 0:
@@ -593,6 +625,7 @@ class LinearPack(ModulePack):
         self.bias = ParameterPack(torch.empty(pack_size, max_out, **fk)) if bias else None
         self._cache = _WeightCache()
         _register_bf16_cache(self.weight, self._cache)
+        self._dw_slot = {}
         self.reset_parameters()
 
     @property
@@ -690,7 +723,8 @@ def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stre
     return packed_linear(x, w, b, in_features=inf, out_features=outf, n_blocks=n_blocks,
                          block_index=block_index, relu=relu, dropout_p=dropout, seed=seed, offset=offset,
                          member_base=member_base, cache=linear._cache if pack_idx is None else None,
-                         dx_cols=dx_cols, row_index=row_index)
+                         dx_cols=dx_cols, row_index=row_index,
+                         dw_slot=linear._dw_slot if (pack_idx is None and linear.reuse_weight_gradient) else None)
 
 
 class DropoutPack(ModulePack):

@@ -173,10 +173,13 @@ def linear_backward(
     db_cols: int | None = None,
     dx_cols: int = 0,
     row_index: Tensor | None = None,
+    dw_out: Tensor | None = None,
+    dw_pad_zero: bool = False,
 ) -> tuple[Tensor | None, Tensor | None, Tensor | None]:
     """Backward of `linear_forward`: returns (dx, dw, db); dw/db are fp32.  With dx_cols > 0
     only dx's first dx_cols columns are computed (the rest are zeros).  With `row_index`, x is
-    the forward's table (no dx)."""
+    the forward's table (no dx).  `dw_out`: the weight gradient's buffer (else a new one);
+    `dw_pad_zero`: it already holds zeros outside the active members' blocks (`tp_linear_grad_args`)."""
     weight = _cuda('weight', weight)
     x = _cuda('x', x, weight.dtype)
     row_index = _row_index(row_index, weight.shape[0])
@@ -193,7 +196,15 @@ def linear_backward(
     g = torch.empty_like(dy) if need_g else None
     dx = torch.empty((P, B, max_in), dtype=dy.dtype, device=dy.device) if need_dx else None
     rows, cols = dw_shape if dw_shape is not None else (max_out, max_in)
-    dw = torch.empty((P, rows, cols), dtype=torch.float32, device=dy.device) if need_dw else None
+    dw = None
+    if need_dw:
+        if dw_out is not None:
+            if (tuple(dw_out.shape) != (P, rows, cols) or dw_out.dtype != torch.float32 or not dw_out.is_contiguous()
+                    or dw_out.device != dy.device):
+                raise ValueError('dw_out must be a contiguous fp32 (P, rows, cols) tensor on the gradient device')
+            dw = dw_out
+        else:
+            dw = torch.empty((P, rows, cols), dtype=torch.float32, device=dy.device)
     dbc = db_cols if db_cols is not None else max_out
     db = torch.empty((P, dbc), dtype=torch.float32, device=dy.device) if need_db else None
     ga = _lib.LinearGradArgs()
@@ -203,6 +214,7 @@ def linear_backward(
     ga.dbias, ga.dx, ga.dw = _ptr(db), _ptr(dx), _ptr(dw)
     ga.dw_rows, ga.dw_cols, ga.db_cols = rows, cols, dbc
     ga.dx_cols = int(dx_cols)
+    ga.dw_pad_zero = 1 if (dw_pad_zero and dw_out is not None) else 0
     check(load().tp_linear_backward(ctypes.byref(ga), _stream()), 'tp_linear_backward')
     return dx, dw, db
 

@@ -254,6 +254,11 @@ class PackTrainer:
         local = per_member_model[lo:hi]
         kw = _merge(model, _transpose(local))
         self.model = TabPack(pack_size=hi - lo, **kw).to(self.device)
+        # this loop owns the gradients (the optimizer consumes them and sets them to None), so
+        # each layer's weight gradient reuses the previous step's storage
+        for mod in self.model.modules():
+            if isinstance(mod, LinearPack):
+                mod.reuse_weight_gradient = True
         self.model.backbone.set_member_base(lo)
         self.model.backbone._stream.seed = _mix(self.seed, 0xD0)  # one Philox key on every rank
         init_member_parameters_(self.model, seed=self.seed, member_ids=list(range(lo, hi)),

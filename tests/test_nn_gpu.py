@@ -312,3 +312,62 @@ def test_pack_idx_forward_selects_members():
         for idx in ([4, 1], [3], [2, 0, 4]):
             part = model(x_num, x_cat, torch.tensor(idx, device='cuda'))
             assert torch.equal(part, whole[idx]), idx
+
+
+def test_reused_weight_gradient_storage_gives_the_same_training():
+    """With `reuse_weight_gradient` (set by PackTrainer) each step's weight gradient is written
+    into the previous step's storage, active blocks only: three bf16 Muon training steps of a
+    ragged, depth-gated TabPack give bit-identical parameters to the same steps with fresh,
+    fully written gradients, and the storage is indeed reused; after the layer's widths change
+    (`replace`) the buffer is rebuilt."""
+    if not torch.cuda.is_available():
+        pytest.skip('needs a GPU')
+    import copy
+
+    from tabpack_b200 import nn as bnn
+    from tabpack_b200 import optim as bopt
+
+    torch.manual_seed(5)
+    P, N, B = 5, 2000, 256
+    cards = [40, 9, 70]
+    base = bnn.TabPack(n_numerical_features=12, categorical_cardinalities=cards, d_out=1, n_blocks=[1, 3, 2, 3, 1],
+                       d_block=[128, 256, 64, 200, 96], dropout=[0.1, 0.0, 0.3, 0.2, 0.05], pack_size=P,
+                       max_d_block=256).cuda().train()
+    g = torch.Generator(device='cuda').manual_seed(6)
+    x_num = torch.randn(N, 12, device='cuda', generator=g)
+    x_cat = torch.stack([torch.randint(0, c + 1, (N,), device='cuda', generator=g) for c in cards], 1)
+    y = torch.randn(N, device='cuda', generator=g)
+    runs = []
+    for reuse in (False, True):
+        model = copy.deepcopy(base)
+        for m in model.modules():
+            if isinstance(m, bnn.LinearPack):
+                m.reuse_weight_gradient = reuse
+        groups = [bopt.MuonAdamWPack.make_muon_parameter_group(b.linear) for b in model.backbone.blocks]
+        muon = {id(gr['params'][0]) for gr in groups}
+        groups.append({'params': [q for q in model.parameters() if id(q) not in muon]})
+        opt = bopt.MuonAdamWPack(groups, adamw_lr=1e-3, weight_decay=1e-4, muon_lr=0.02, pack_size=P,
+                                 allow_inplace_grad_mutation=False)
+        ptrs = []
+        for step in range(3):
+            idx = torch.randint(0, N, (P, B), device='cuda', generator=torch.Generator(device='cuda').manual_seed(step))
+            with torch.autocast('cuda', dtype=torch.bfloat16):
+                model.backbone._stream.seed, model.backbone._stream.calls = 13, step
+                out = model.forward_rows(x_num, x_cat, idx)
+            ((out.float().squeeze(-1) - y[idx]) ** 2).mean(1).sum().backward()
+            ptrs.append(model.backbone.blocks[1].linear.weight.grad.data_ptr())
+            opt.step()
+            opt.zero_grad()
+        runs.append(({n: q.detach().clone() for n, q in model.named_parameters()}, ptrs, model))
+    (pa, _, _), (pb, ptrs, model) = runs
+    for n in pa:
+        assert torch.equal(pa[n], pb[n]), n
+    assert ptrs[0] == ptrs[1] == ptrs[2]
+    slot = model.backbone.blocks[1].linear._dw_slot
+    key = slot['key']
+    model.backbone.blocks[1].linear.replace(pack_idx=torch.tensor([1], device='cuda'), out_features=[64])
+    idx = torch.randint(0, N, (P, B), device='cuda', generator=g)
+    with torch.autocast('cuda', dtype=torch.bfloat16):
+        out = model.forward_rows(x_num, x_cat, idx)
+    out.float().sum().backward()
+    assert slot['key'] != key
