@@ -247,6 +247,13 @@ typedef struct tp_muon_args {
    * elements of the copy are left as they are.  NULL: no copy is written. */
   void* p_bf16;
   int32_t p_bf16_rows, p_bf16_cols;
+  /* Optional depth gating of the block this weight belongs to: members with
+   * n_blocks[m] <= block_index pass their input through the block, so their gradient is
+   * exactly zero; the step reads it as zero (their momentum still decays and, where it is
+   * nonzero, they take the full update) and leaves their rows of the bf16 copy alone.
+   * NULL: every member is stepped from its gradient. */
+  const int32_t* n_blocks;
+  int32_t block_index;
 } tp_muon_args;
 
 size_t tp_muon_workspace_size(int32_t P, int32_t max_out, int32_t max_in);

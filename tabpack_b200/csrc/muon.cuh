@@ -44,7 +44,13 @@ struct MuonArgs {
   int32_t* active;       // (P,) norm2 > 0
   __nv_bfloat16* p_bf16; // optional bf16 copy of p written with the update, or nullptr
   int bf16_rows, bf16_cols;
+  const int32_t* n_blocks;  // (P,) depths, or nullptr: members with n_blocks <= block_index have
+  int block_index;          //   an exactly zero gradient (depth-gated)
 };
+
+__device__ __forceinline__ bool muon_gated(const MuonArgs& a, int mem) {
+  return a.n_blocks != nullptr && __ldg(a.n_blocks + mem) <= a.block_index;
+}
 
 __global__ void muon_geometry_kernel(MuonArgs a) {
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
@@ -197,6 +203,9 @@ __global__ void __launch_bounds__(256) muon_prologue_kernel(MuonArgs a) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const float mu = a.mu_pm ? a.mu_pm[mem] : a.mu_s;
   const float one_m_mu = a.mu_pm ? 1.0f - mu : a.one_m_mu_s;
+  // a depth-gated member's gradient is exactly zero: it is not read, and its momentum is
+  // written back only where it changes (nowhere once it is zero)
+  const bool gated = muon_gated(a, mem);
   float gv[4][4], mv[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -205,7 +214,7 @@ __global__ void __launch_bounds__(256) muon_prologue_kernel(MuonArgs a) {
       const int o = o0 + w + 8 * i, n = n0 + lane + 32 * c;
       const bool ok = o < out_m && n < in_m;
       const size_t idx = ((size_t)mem * a.max_out + o) * a.max_in + n;
-      gv[i][c] = ok ? a.g[idx] : 0.0f;
+      gv[i][c] = (ok && !gated) ? a.g[idx] : 0.0f;
       mv[i][c] = ok ? a.m[idx] : 0.0f;
     }
   float ss = 0.0f;
@@ -219,8 +228,8 @@ __global__ void __launch_bounds__(256) muon_prologue_kernel(MuonArgs a) {
         const size_t idx = ((size_t)mem * a.max_out + o) * a.max_in + n;
         const float m = lerp_t(mv[i][c], gv[i][c], one_m_mu);
         const float u = a.nesterov ? lerp_t(gv[i][c], m, mu) : m;
-        a.m[idx] = m;
-        if (a.nesterov && a.mutate_grad) a.g[idx] = u;
+        if (!gated || __float_as_uint(m) != __float_as_uint(mv[i][c])) a.m[idx] = m;
+        if (a.nesterov && a.mutate_grad && (!gated || __float_as_uint(u) != 0u)) a.g[idx] = u;
         ubv = __float2bfloat16_rn(u);
         const float ub_f = __bfloat162float(ubv);
         ss += ub_f * ub_f;
@@ -372,6 +381,7 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(MuonArgs a) {
   if (o0 >= out_m || n0 >= in_m) return;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const bool active = a.active[mem] != 0;
+  const bool gated = muon_gated(a, mem);  // its rows of the bf16 copy are not read (depth-gated)
   float pv[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -400,7 +410,7 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(MuonArgs a) {
         const float u = active ? __bfloat162float(ub[w + 8 * i][lane + 32 * c]) : 0.0f;
         const float pn = __fmaf_rn(-u, slr, pw);
         a.p[((size_t)mem * a.max_out + o) * a.max_in + n] = pn;
-        if (a.p_bf16 != nullptr)
+        if (a.p_bf16 != nullptr && !gated)
           a.p_bf16[((size_t)mem * a.bf16_rows + o) * a.bf16_cols + n] = __float2bfloat16_rn(pn);
       }
     }

@@ -824,6 +824,8 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
     return fail(TP_EINVAL, "the bf16 copy (%d x %d per member) is smaller than p (%d x %d)", a->p_bf16_rows,
                 a->p_bf16_cols, a->max_out, a->max_in);
   m.p_bf16 = static_cast<__nv_bfloat16*>(a->p_bf16);
+  m.n_blocks = a->n_blocks;
+  m.block_index = a->block_index;
   m.bf16_rows = a->p_bf16_rows;
   m.bf16_cols = a->p_bf16_cols;
 

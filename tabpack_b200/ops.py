@@ -285,10 +285,13 @@ def muon_workspace_size(P: int, max_out: int, max_in: int) -> int:
 
 def muon_step(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=None, in_features=None, lr,
               momentum, weight_decay, update_scale=None, nesterov: bool = True, mutate_grad: bool = True,
-              ns_steps: int = 5, workspace: Tensor | None = None, p_bf16: Tensor | None = None) -> None:
+              ns_steps: int = 5, workspace: Tensor | None = None, p_bf16: Tensor | None = None,
+              n_blocks: Tensor | None = None, block_index: int = 0) -> None:
     """One Muon group step on a packed (P, max_out, max_in) fp32 weight; see `tp_muon_step`.
     `p_bf16` (P, rows >= max_out, cols >= max_in) bf16, optional, receives bf16 of the updated
-    weights of each member's out x in block in the same pass."""
+    weights of each member's out x in block in the same pass.  `n_blocks` / `block_index`: the
+    weight's block is depth-gated for members with n_blocks <= block_index (their gradient is
+    exactly zero and is not read)."""
     for name, t in (('p', p), ('grad', grad), ('momentum_buffer', momentum_buffer)):
         if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous() or t.ndim != 3:
             raise TypeError(f'{name} must be a contiguous 3-D fp32 CUDA tensor')
@@ -310,7 +313,12 @@ def muon_step(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=
                 or p_bf16.shape[0] != P):
             raise TypeError('p_bf16 must be a contiguous (P, rows, cols) bf16 CUDA tensor')
         a.p_bf16, a.p_bf16_rows, a.p_bf16_cols = p_bf16.data_ptr(), p_bf16.shape[1], p_bf16.shape[2]
-    keep = (out_features, in_features, update_scale)  # noqa: F841  (alive until the launch is queued)
+    nb = _i32('n_blocks', n_blocks)
+    if nb is not None:
+        if nb.shape != (P,):
+            raise ValueError(f'n_blocks must be ({P},), got {tuple(nb.shape)}')
+        a.n_blocks, a.block_index = nb.data_ptr(), int(block_index)
+    keep = (out_features, in_features, update_scale, nb)  # noqa: F841  (alive until the launch is queued)
     check(load().tp_muon_step(ctypes.byref(a), _stream()), 'tp_muon_step')
     increment_version([p, momentum_buffer] + ([grad] if mutate_grad else []) + ([p_bf16] if p_bf16 is not None else []))
 

@@ -326,7 +326,7 @@ def _muon_group(opt: torch.optim.Optimizer, g: dict, *, workspaces: dict, allow_
                   update_scale=None if scale is None else scale.to(torch.float32).contiguous(),
                   nesterov=bool(g['muon_nesterov']), mutate_grad=allow_inplace_grad_mutation,
                   ns_steps=int(g['muon_newton_schulz_steps']), workspace=_muon_workspace(workspaces, p),
-                  p_bf16=copy)
+                  p_bf16=copy, n_blocks=g.get('muon_n_blocks'), block_index=int(g.get('muon_block_index', 0)))
     if copy is not None:
         cache.end_update(p, copy)
 

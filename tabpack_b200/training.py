@@ -269,6 +269,11 @@ class PackTrainer:
             okw.update(_transpose(per_member_optimizer[lo:hi]))
         if otype == 'muon':
             groups = [MuonAdamWPack.make_muon_parameter_group(b.linear) for b in self.model.backbone.blocks]
+            # the blocks a member's depth leaves out get an exactly zero gradient: the Muon step
+            # does not read it (a key of this package's groups; the reference has no such key)
+            for i, gr in enumerate(groups):
+                if i > 0:
+                    gr['muon_n_blocks'], gr['muon_block_index'] = self.model.backbone.n_blocks, i
             muon_params = {id(g['params'][0]) for g in groups}
             decay, no_decay = split_weight_decay(self.model)
             groups.append({'params': [p for p in no_decay if id(p) not in muon_params], 'weight_decay': 0.0})

@@ -341,3 +341,41 @@ def test_muon_step_refreshes_the_bf16_weight_copy():
         want = lin.weight.detach().bfloat16()
         assert torch.equal(copy[valid].view(torch.int16), want[valid].view(torch.int16))
         del copy  # a view of the copy would keep the next step from writing into it
+
+
+def test_muon_step_with_depth_gated_members():
+    """Members whose depth leaves the block out (n_blocks <= block_index) have an exactly zero
+    gradient, which the step then does not read: weights and momentum bit-identical to the
+    same step reading the zero gradient, also for a gated member whose momentum is still
+    nonzero (it takes the full update); the bf16 copy is written for the other members."""
+    from tabpack_b200 import ops
+
+    P, O, I = 6, 200, 136
+    gen = torch.Generator(device='cuda').manual_seed(17)
+    outf = torch.tensor([200, 64, 128, 200, 96, 8], dtype=torch.int32, device='cuda')
+    inf = torch.tensor([136, 40, 136, 72, 136, 16], dtype=torch.int32, device='cuda')
+    nb = torch.tensor([3, 1, 2, 4, 1, 2], dtype=torch.int32, device='cuda')  # block 1: members 1, 4 gated
+    valid = ((torch.arange(O, device='cuda')[None, :, None] < outf[:, None, None])
+             & (torch.arange(I, device='cuda')[None, None, :] < inf[:, None, None]))
+    p0 = torch.randn(P, O, I, device='cuda', generator=gen) * 0.05
+    g = torch.randn(P, O, I, device='cuda', generator=gen) * 1e-3 * valid
+    g[1] = 0.0
+    g[4] = 0.0
+    m0 = torch.zeros(P, O, I, device='cuda')
+    m0[4] = torch.randn(O, I, device='cuda', generator=gen) * 1e-3 * valid[4]  # still nonzero
+    lr = torch.full((P,), 0.02, device='cuda')
+    out = []
+    for gated in (False, True):
+        p, m = p0.clone(), m0.clone()
+        copy = torch.zeros(P, O, I, dtype=torch.bfloat16, device='cuda')
+        for _ in range(2):
+            ops.muon_step(p, g.clone(), m, out_features=outf, in_features=inf, lr=lr, momentum=0.95,
+                          weight_decay=1e-2, nesterov=True, mutate_grad=False, ns_steps=5, p_bf16=copy,
+                          n_blocks=nb if gated else None, block_index=1)
+        torch.cuda.synchronize()
+        out.append((p, m, copy))
+    (pa, ma, ca), (pb, mb, cb) = out
+    assert torch.equal(pa, pb) and torch.equal(ma, mb)
+    live = (nb > 1)[:, None, None] & valid
+    assert torch.equal(ca[live.expand_as(ca)], cb[live.expand_as(cb)])
+    assert not torch.equal(pa[4], p0[4] * (1 - 0.02 * 1e-2))  # the nonzero momentum still moved it
