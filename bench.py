@@ -717,9 +717,14 @@ def ns_symmetric_fraction(r: int) -> float:
 
 
 def member_cost(pm: dict, d_in: int) -> float:
-    """A member's FLOPs per training step as the kernels execute them (the sharding weight)."""
+    """A member's estimated device time per training step (the sharding weight): its tensor-core
+    FLOPs as the kernels execute them at ~800 TFLOP/s plus the bytes its weights move through
+    the Muon elementwise kernels and the bf16 copies (~30 B per weight element) at ~5 TB/s."""
     w = train_work([pm], d_in)
-    return w['fwd'] + w['dgrad'] + w['wgrad'] + w['newton_schulz_executed']
+    flops = w['fwd'] + w['dgrad'] + w['wgrad'] + w['newton_schulz_executed']
+    wd = pm['d_block']
+    elements = d_in * wd + (pm['n_blocks'] - 1) * wd * wd
+    return flops / 800e12 + 30.0 * elements / 5e12
 
 
 def _compact(line: dict) -> dict:
@@ -860,10 +865,13 @@ def run_train(args) -> None:
     barrier()
     e2e_ms = e0.elapsed_time(e1)
 
-    # per-family kernel time over one more scaled epoch, launch by launch (CUDA events)
+    # per-family kernel time over one more scaled epoch, launch by launch (CUDA events; the
+    # Muon groups one after another so that no launch's time includes another's)
+    trainer.opt.concurrent_muon_groups = False
     with ops.KernelTimes() as kt:
         epoch(dev_data['train'], dev_data['val'], 3)
     barrier()
+    trainer.opt.concurrent_muon_groups = True
 
     t = torch.tensor([region_ms, train_ms, e2e_ms], device=dev, dtype=torch.float64)
     if world > 1:

@@ -285,18 +285,21 @@ class MuonAdamWPack(OptimizerPack):
         return loss
 
 
-def _muon_workspace(workspaces: dict, p: Tensor) -> Tensor:
-    """The Newton-Schulz workspace of `p`'s device, grown to fit `p` (one per optimizer)."""
+def _muon_workspace(workspaces: dict, p: Tensor, slot: int = 0) -> Tensor:
+    """Newton-Schulz workspace `slot` of `p`'s device, grown to fit `p` (groups that run
+    concurrently use different slots)."""
     P, mo, mi = p.shape
     n = ops.muon_workspace_size(P, mo, mi)
-    ws = workspaces.get(p.device)
+    key = (p.device, slot)
+    ws = workspaces.get(key)
     if ws is None or ws.numel() < n:
         ws = torch.empty(n, dtype=torch.uint8, device=p.device)
-        workspaces[p.device] = ws
+        workspaces[key] = ws
     return ws
 
 
-def _muon_group(opt: torch.optim.Optimizer, g: dict, *, workspaces: dict, allow_inplace_grad_mutation: bool) -> None:
+def _muon_group(opt: torch.optim.Optimizer, g: dict, *, workspaces: dict, allow_inplace_grad_mutation: bool,
+                slot: int = 0) -> None:
     """`MuonAdamWPack._step_muon` (`optim.py:682-774`) for one single-parameter Muon group:
     weight decay, momentum, Nesterov blend, batched Newton-Schulz and the scaled update in the
     Muon kernels.  Per-member widths (`muon_out_features` / `muon_in_features`) keep each
@@ -325,7 +328,7 @@ def _muon_group(opt: torch.optim.Optimizer, g: dict, *, workspaces: dict, allow_
                   weight_decay=_hp(g['weight_decay']),
                   update_scale=None if scale is None else scale.to(torch.float32).contiguous(),
                   nesterov=bool(g['muon_nesterov']), mutate_grad=allow_inplace_grad_mutation,
-                  ns_steps=int(g['muon_newton_schulz_steps']), workspace=_muon_workspace(workspaces, p),
+                  ns_steps=int(g['muon_newton_schulz_steps']), workspace=_muon_workspace(workspaces, p, slot),
                   p_bf16=copy, n_blocks=g.get('muon_n_blocks'), block_index=int(g.get('muon_block_index', 0)))
     if copy is not None:
         cache.end_update(p, copy)
@@ -342,13 +345,48 @@ def adamw_step(opt: torch.optim.Optimizer, *, support_replacement: bool) -> None
 def muon_adamw_step(opt: torch.optim.Optimizer, *, workspaces: dict, allow_inplace_grad_mutation: bool,
                     support_replacement: bool) -> None:
     """`MuonAdamWPack.step` (`optim.py:495-861`) over every group of `opt`: Muon groups through
-    the Muon kernels, the others through the grouped AdamW kernel (`adamw_*` keys)."""
-    for g in opt.param_groups:
-        if g['muon']:
+    the Muon kernels, the others through the grouped AdamW kernel (`adamw_*` keys).
+
+    The Muon groups of one device are independent, so they run concurrently, each on a side
+    stream of its own (after the current stream's work so far, which the current stream then
+    waits for): one group's Newton-Schulz launches fill the SMs that another's leave idle at
+    its ramp and tail.  Each concurrent group has its own workspace."""
+    muon = [g for g in opt.param_groups if g['muon'] and g['params'][0].grad is not None]
+    streams = _side_streams(opt, muon)
+    if streams:
+        main = torch.cuda.current_stream(muon[0]['params'][0].device)
+        ready = torch.cuda.Event()
+        ready.record(main)
+        for i, (g, s) in enumerate(zip(muon, streams)):
+            s.wait_event(ready)
+            with torch.cuda.stream(s):
+                _muon_group(opt, g, workspaces=workspaces, allow_inplace_grad_mutation=allow_inplace_grad_mutation,
+                            slot=i)
+    else:
+        for g in muon:
             _muon_group(opt, g, workspaces=workspaces, allow_inplace_grad_mutation=allow_inplace_grad_mutation)
-        else:
+    for g in opt.param_groups:
+        if not g['muon']:
             _adamw_group(opt, g['params'], lr=g['adamw_lr'], beta1=g['adamw_beta1'], beta2=g['adamw_beta2'],
                          eps=g['adamw_eps'], weight_decay=g['weight_decay'], support_replacement=support_replacement)
+    if streams:
+        for s in streams:
+            main.wait_stream(s)
+
+
+def _side_streams(opt: torch.optim.Optimizer, groups: list) -> list:
+    """One side stream per Muon group when there are several on one CUDA device (kept on the
+    optimizer), else [] (also when the optimizer's `concurrent_muon_groups` is False, e.g. to
+    time each launch on its own)."""
+    if len(groups) < 2 or not getattr(opt, 'concurrent_muon_groups', True):
+        return []
+    dev = groups[0]['params'][0].device
+    if dev.type != 'cuda' or any(g['params'][0].device != dev for g in groups):
+        return []
+    pool = opt.__dict__.setdefault('_side_streams', {}).setdefault(dev, [])
+    while len(pool) < len(groups):
+        pool.append(torch.cuda.Stream(device=dev))
+    return pool[:len(groups)]
 
 
 def optimizer_pack_remove(optimizer, *, pack_idx: Tensor, old_to_new_parameters) -> None:
