@@ -6,7 +6,8 @@ exchange: rank r owns the contiguous global member range `ranges[r]`, dropout ma
 and batch orders are keyed by global member id (shard-invariant), and the only
 exchanges are the once-per-epoch all-gather of per-member validation predictions
 (before greedy selection) and, at inference, a sum all-reduce of ensemble
-probabilities.
+probabilities.  When more models than pack slots are trained, freed slots take new
+model ids in a fixed global order (`assign_replacements`).
 """
 
 from __future__ import annotations
@@ -70,13 +71,38 @@ def gather_members(local: Tensor, counts: list[int], group=None) -> Tensor:
         dist.all_gather_into_tensor(out, padded.contiguous(), group=group)
         parts = [out[r * maxc: r * maxc + counts[r]] for r in range(world)]
     else:
-        bufs = [torch.empty_like(padded) for _ in range(world)]
-        dist.all_gather(bufs, padded.contiguous(), group=group)
-        parts = [bufs[r][: counts[r]] for r in range(world)]
+        # host-side groups (gloo): device tensors are staged through host memory
+        src = padded.cpu() if padded.is_cuda else padded.contiguous()
+        bufs = [torch.empty_like(src) for _ in range(world)]
+        dist.all_gather(bufs, src, group=group)
+        parts = [bufs[r][: counts[r]].to(local.device) for r in range(world)]
     return torch.cat(parts, 0)
 
 
 def allreduce_sum_(t: Tensor, group=None) -> Tensor:
     """In-place sum over ranks (ensemble probability partial sums)."""
+    if t.is_cuda and dist.get_backend(group) != 'nccl':
+        h = t.cpu()
+        dist.all_reduce(h, op=dist.ReduceOp.SUM, group=group)
+        t.copy_(h)
+        return t
     dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
     return t
+
+
+def assign_replacements(stopped_slots: list[int], *, next_model_id: int, n_pending: int) -> list[tuple[int, int]]:
+    """The replacement queue of a sharded pack (`src/tabpackage/_training.py:2891-2927`):
+    (global slot, model id) pairs that refill the slots freed this epoch.
+
+    As in the reference, the first `min(len(stopped_slots), n_pending)` freed slots in pack
+    order take the next model ids in increasing order (`get_next_models`); the other freed
+    slots stay empty.  Every rank derives `stopped_slots` from the same gathered validation
+    metrics, so every rank computes the same pairs, and slot -- hence rank -- of a model does
+    not depend on the number of GPUs."""
+    if n_pending < 0 or next_model_id < 0:
+        raise ValueError('n_pending and next_model_id must be non-negative')
+    slots = sorted(stopped_slots)
+    if len(set(slots)) != len(slots):
+        raise ValueError('stopped slots must be distinct')
+    n = min(len(slots), n_pending)
+    return [(slots[i], next_model_id + i) for i in range(n)]

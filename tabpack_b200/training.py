@@ -15,10 +15,12 @@ per-member best checkpoints by the validation metric with early-stopping patienc
 (`update_training_state`, `_training.py:754-821`), and an online greedy ensemble rebuilt
 after every epoch from the current members, the best checkpoints of finished members and
 the latest checkpoints of running ones, accepted only when its validation score improves
-(`Ensemble.update`, `_training.py:1061-1183`).  A member that stops keeps its place in the
-pack with a zero learning rate (its parameters no longer change) where the reference removes
-it from the pack; the model-replacement queue of `max_pack_size < n_models` is not part of
-this module.
+(`Ensemble.update`, `_training.py:1061-1183`).  With more models than pack slots
+(`n_models`, the reference's `max_pack_size < n_models`), the slots of finished models take
+the next model ids (`_training.py:2891-2927`, `pack_replace` `_training.py:860-924`) in one
+global order that every rank computes alike (`shard.assign_replacements`).  A finished model
+that no new model replaces keeps its slot with a zero learning rate (its parameters no longer
+change) where the reference removes it from the pack.
 """
 
 from __future__ import annotations
@@ -37,7 +39,7 @@ from tabpack_b200.ensemble import compute_unsanitized_ensemble_predictions, gree
 from tabpack_b200.metrics import PackScore
 from tabpack_b200.nn import CosineEmbeddingsPack, LinearPack, TabPack
 from tabpack_b200.optim import AdamWPack, MuonAdamWPack, split_weight_decay
-from tabpack_b200.shard import allreduce_sum_, gather_members, member_ranges
+from tabpack_b200.shard import allreduce_sum_, assign_replacements, gather_members, member_ranges
 
 _LOSSES = ('mse', 'bce', 'ce')
 
@@ -53,7 +55,8 @@ def _mix(*xs: int) -> int:
 
 @torch.no_grad()
 def init_member_parameters_(model: torch.nn.Module, *, seed: int, member_ids: list[int],
-                            generator_device: str | torch.device | None = None) -> None:
+                            generator_device: str | torch.device | None = None,
+                            pack_idx: list[int] | None = None) -> None:
     """Re-initialise every LinearPack (and CosineEmbeddingsPack) member from its own generator.
 
     Same distribution as `LinearPack.reset_parameters` (`nn.py:702-747`), U(+-1/sqrt(in_i))
@@ -61,7 +64,12 @@ def init_member_parameters_(model: torch.nn.Module, *, seed: int, member_ids: li
     seeded by (seed, global member id, j): initial weights do not depend on sharding.
     The generators live on the parameters' device unless `generator_device` names another
     one (e.g. 'cpu': the same numbers on any machine, drawn on the host and copied over).
+    `pack_idx` names the pack positions that take `member_ids` (default: 0, 1, ...).
     """
+    slots = list(range(len(member_ids))) if pack_idx is None else list(pack_idx)
+    if len(slots) != len(member_ids):
+        raise ValueError('one pack position per member id is required')
+
     def gen(dev, key):
         d = torch.device(generator_device) if generator_device is not None else dev
         return torch.Generator(device=d).manual_seed(key), d
@@ -69,7 +77,7 @@ def init_member_parameters_(model: torch.nn.Module, *, seed: int, member_ids: li
     for j, emb in enumerate(m for m in model.modules() if isinstance(m, CosineEmbeddingsPack)):
         # CosineEmbeddingsPack.reset_parameters (`nn.py:1706-1753`): truncated N(0, 1) on
         # [-3, 3] times the member's init scale, the affine parts zero
-        for m, gid in enumerate(member_ids):
+        for m, gid in zip(slots, member_ids):
             g, d = gen(emb.weight.device, _mix(seed, gid, 0xE0 + j))
             w = torch.empty(emb.weight.shape[1:], device=d, dtype=emb.weight.dtype)
             torch.nn.init.trunc_normal_(w, a=-3.0, b=3.0, generator=g)
@@ -80,7 +88,7 @@ def init_member_parameters_(model: torch.nn.Module, *, seed: int, member_ids: li
     linears = [m for m in model.modules() if isinstance(m, LinearPack)]
     for j, lin in enumerate(linears):
         inf = lin.in_features.tolist() if lin.in_features is not None else [lin.max_in_features] * lin.pack_size
-        for m, gid in enumerate(member_ids):
+        for m, gid in zip(slots, member_ids):
             g, d = gen(lin.weight.device, _mix(seed, gid, j))
             b = inf[m] ** -0.5
             for p in (lin.weight, lin.bias):
@@ -141,7 +149,7 @@ class EpochResult:
 
 
 CheckpointKey = tuple[int, int]
-"""(global member id, training step) of an evaluated checkpoint (`ModelCheckpointKey`,
+"""(model id, the model's training step) of an evaluated checkpoint (`ModelCheckpointKey`,
 `_training.py:531-540`)."""
 
 
@@ -210,11 +218,13 @@ class OnlineEnsemble:
 @dataclasses.dataclass
 class FitResult:
     """What `PackTrainer.fit` leaves behind (cf. `TrainedTabPack`, `_training.py:2021-2364`).
-    Metrics are the validation criterion (lower is better for every loss here)."""
-    history: list[dict]            # per epoch: 'step' (training loop step), 'val_metric' (P,) of the
-                                   # members trained that epoch (NaN for stopped ones), 'train_loss' (P,)
-    best_step: Tensor              # (P,) step of each member's best checkpoint
-    best_metric: Tensor            # (P,) its validation metric
+    Metrics are the validation criterion (lower is better for every loss here); checkpoint
+    keys are (model id, model step)."""
+    history: list[dict]            # per epoch: 'step' (training loop step), 'val_metric' and 'train_loss'
+                                   # (n_models,) of the models trained that epoch (NaN for the others),
+                                   # 'slot_model' (the model id each gathered slot trained, -1: none)
+    best_step: Tensor              # (n_models,) model step of each model's best checkpoint
+    best_metric: Tensor            # (n_models,) its validation metric
     ensemble_keys: list[CheckpointKey]
     ensemble_weights: Tensor | None
     ensemble_metric: float
@@ -227,13 +237,32 @@ class PackTrainer:
     def __init__(self, *, n_members: int, model: dict, per_member_model: list[dict], optimizer: dict,
                  per_member_optimizer: list[dict] | None = None, loss: str, seed: int, device,
                  autocast_bf16: bool = True, group=None, cost: list[float] | None = None,
-                 member_range: tuple[int, int] | None = None, init_on_host: bool = False) -> None:
+                 member_range: tuple[int, int] | None = None, init_on_host: bool = False,
+                 n_models: int | None = None) -> None:
         """`member_range` pins this trainer to global members [lo, hi) without a process
         group (several shards on one device); otherwise the group's rank picks its range.
         `init_on_host` draws the initial parameters with host generators (the same values on
-        every machine and device; slower for large packs)."""
+        every machine and device; slower for large packs).
+
+        `n_models` (default `n_members`): models trained over the run through a pack of
+        `n_members` slots.  `per_member_model` and `per_member_optimizer` then hold one entry
+        per model id; slot s starts with model s, and `fit` gives the slots of finished
+        models to the next ids.  The pack's maximum shapes (`model`) must fit every model."""
         if loss not in _LOSSES:
             raise ValueError(f'loss must be one of {_LOSSES}')
+        self.n_models = n_members if n_models is None else int(n_models)
+        if self.n_models < n_members:
+            raise ValueError('n_models must be at least the number of pack slots')
+        if len(per_member_model) != self.n_models or (per_member_optimizer is not None
+                                                      and len(per_member_optimizer) != self.n_models):
+            raise ValueError('one hyperparameter dict per model is required')
+        if self.n_models > n_members and member_range is not None and tuple(member_range) != (0, n_members):
+            raise ValueError('the replacement queue needs the whole pack: a process group or member_range '
+                             '(0, n_members)')
+        self.per_model = list(per_member_model)
+        self.per_model_optimizer = None if per_member_optimizer is None else list(per_member_optimizer)
+        self.slot_model = list(range(n_members))  # global slot -> model id it trains (-1: none)
+        replacement = self.n_models > n_members
         self.group = group
         self.world = dist.get_world_size(group) if (dist.is_initialized() and member_range is None) else 1
         self.rank = dist.get_rank(group) if (dist.is_initialized() and member_range is None) else 0
@@ -261,8 +290,9 @@ class PackTrainer:
                 mod.reuse_weight_gradient = True
         self.model.backbone.set_member_base(lo)
         self.model.backbone._stream.seed = _mix(self.seed, 0xD0)  # one Philox key on every rank
+        self._init_device = 'cpu' if init_on_host else None
         init_member_parameters_(self.model, seed=self.seed, member_ids=list(range(lo, hi)),
-                                generator_device='cpu' if init_on_host else None)
+                                generator_device=self._init_device)
         okw = dict(optimizer)
         otype = okw.pop('type')
         if per_member_optimizer is not None:
@@ -278,10 +308,12 @@ class PackTrainer:
             decay, no_decay = split_weight_decay(self.model)
             groups.append({'params': [p for p in no_decay if id(p) not in muon_params], 'weight_decay': 0.0})
             groups.append({'params': [p for p in decay if id(p) not in muon_params]})
-            self.opt = MuonAdamWPack(groups, pack_size=hi - lo, allow_inplace_grad_mutation=False, **okw)
+            self.opt = MuonAdamWPack(groups, pack_size=hi - lo, allow_inplace_grad_mutation=False,
+                                     support_replacement=replacement, **okw)
         elif otype == 'adamw':
             wd, nd = split_weight_decay(self.model)
-            self.opt = AdamWPack([{'params': nd, 'weight_decay': 0.0}, {'params': wd}], pack_size=hi - lo, **okw)
+            self.opt = AdamWPack([{'params': nd, 'weight_decay': 0.0}, {'params': wd}], pack_size=hi - lo,
+                                 support_replacement=replacement, **okw)
         else:
             raise ValueError("optimizer type must be 'muon' or 'adamw'")
 
@@ -374,73 +406,97 @@ class PackTrainer:
                 v[idx] = 0.0
                 g[key] = v
 
-    def fit(self, train: dict, val: dict, *, batch_size: int, max_epochs: int,
+    def _replace_local(self, pairs: list[tuple[int, int]]) -> None:
+        """`pack_replace` (`_training.py:860-924`) on this rank's slots: (local slot, model id)
+        pairs take the models' shapes and hyperparameters, fresh optimizer state (the Muon
+        update scales follow the new shapes) and parameters initialised from the model ids."""
+        if not pairs:
+            return
+        slots = [sl for sl, _ in pairs]
+        models = [m for _, m in pairs]
+        idx = torch.tensor(slots, device=self.device)
+        self.model.replace(pack_idx=idx, **_transpose([self.per_model[m] for m in models]))
+        okw = {} if self.per_model_optimizer is None else _transpose([self.per_model_optimizer[m] for m in models])
+        if isinstance(self.opt, MuonAdamWPack):
+            self.opt.replace(pack_idx=idx, module=self.model, **okw)
+        else:
+            self.opt.replace(pack_idx=idx, **okw)
+        init_member_parameters_(self.model, seed=self.seed, member_ids=models, pack_idx=slots,
+                                generator_device=self._init_device)
+
+    def fit(self, train: dict, val: dict, *, batch_size: int, max_epochs: int | list[int],
             early_stopping_patience: int | None = None, ensemble: OnlineEnsemble | None = None,
             eval_batch_size: int = 32768) -> FitResult:
-        """The reference's training loop (`_training.py:2643-2960`) for a pack whose members
-        all start together: train an epoch, evaluate every member on `val`, update each
-        member's best checkpoint (`update_training_state`, `_training.py:754-821`), stop the
-        members that reached `max_epochs` or ran out of patience (their best checkpoints are
-        then final), and update `ensemble` (by default an `OnlineEnsemble` over the validation
-        criterion, at most 32 members).  Ends when every member has finished."""
-        if max_epochs <= 0:
-            raise ValueError('max_epochs must be positive')
+        """The reference's training loop (`_training.py:2643-2960`): train an epoch, evaluate
+        every slot's model on `val`, update each model's best checkpoint
+        (`update_training_state`, `_training.py:754-821`; a model's first evaluation is its
+        first best checkpoint even when NaN), stop the models that reached their `max_epochs`
+        (one value, or one per model id) or ran out of patience (their best checkpoints are then
+        final), update `ensemble` (by default an `OnlineEnsemble` over the validation criterion,
+        at most 32 members), then give the freed slots to the next model ids while any are left
+        (`shard.assign_replacements`).  Ends when every model has finished."""
+        M = self.n_models
+        max_ep = [max_epochs] * M if isinstance(max_epochs, int) else list(max_epochs)
+        if len(max_ep) != M or any(int(v) <= 0 for v in max_ep):
+            raise ValueError('max_epochs must be positive (one value, or one per model)')
         score = self._score(val['y'])
         if ensemble is None:
             ensemble = OnlineEnsemble(score)
-        ids = self.gathered_ids
-        P = len(ids)
-        pos = {g: i for i, g in enumerate(ids)}
+        ids = self.gathered_ids                   # global slots whose predictions predict() returns
+        S = len(ids)
+        occ = [self.slot_model[g] for g in ids]   # model id each slot trains (-1: none)
         steps_per_epoch = math.ceil(len(train['y']) / batch_size)
-        max_steps = max_epochs * steps_per_epoch
-        steps = [0] * P
-        n_bad = [0] * P
-        active = [True] * P
-        best_metric: list[float] | None = None
-        best_step = [0] * P
-        best_pred: Tensor | None = None
+        max_steps = [int(v) * steps_per_epoch for v in max_ep]
+        steps, n_bad, best_step = [0] * M, [0] * M, [0] * M
+        best_metric = [math.nan] * M
+        active = [m >= 0 for m in occ]
+        fresh = list(active)                      # the slot's model has not been evaluated yet
+        next_model = 1 + max(self.slot_model)
+        best_pred: Tensor | None = None           # (S, ...) best predictions of each slot's model
         finished: list[CheckpointKey] = []
         store: dict[CheckpointKey, Tensor] = {}
         history: list[dict] = []
         ensemble_history: list[dict] = []
         loop_step = 0
-        for epoch in range(max_epochs):
+        epoch = 0
+        while any(active):
             loss = self.fit_epoch(train, batch_size=batch_size, epoch=epoch)
+            epoch += 1
             loop_step += steps_per_epoch
-            for i in range(P):
+            for i in range(S):
                 if active[i]:
-                    steps[i] += steps_per_epoch
+                    steps[occ[i]] += steps_per_epoch
             preds = self.predict(val, eval_batch_size=eval_batch_size)
             latest = (-score(preds)).double().cpu().tolist()
-            if best_metric is None:
-                best_metric = list(latest)
-                best_step = list(steps)
+            if best_pred is None:
                 best_pred = preds.clone()
-                for i in range(P):
-                    n_bad[i] += int(math.isnan(latest[i]))
-            else:
-                better = [active[i] and not math.isnan(latest[i])
-                          and (math.isnan(best_metric[i]) or latest[i] < best_metric[i]) for i in range(P)]
-                rows = [i for i in range(P) if better[i]]
-                for i in range(P):
-                    if active[i]:
-                        n_bad[i] = 0 if better[i] else n_bad[i] + 1
-                for i in rows:
-                    best_metric[i], best_step[i] = latest[i], steps[i]
-                if rows:
-                    r = torch.tensor(rows, device=preds.device)
-                    best_pred[r] = preds[r]
-            running = [active[i] and steps[i] < max_steps
-                       and (early_stopping_patience is None or n_bad[i] <= early_stopping_patience) for i in range(P)]
-            stopped = [i for i in range(P) if active[i] and not running[i]]
-            finished += [(ids[i], best_step[i]) for i in stopped]
-            running_latest = [(ids[i], steps[i]) for i in range(P) if running[i]]
+            rows = []
+            for i in range(S):
+                if not active[i]:
+                    continue
+                m, x = occ[i], latest[i]
+                improved = not math.isnan(x) and (fresh[i] or math.isnan(best_metric[m]) or x < best_metric[m])
+                n_bad[m] = 0 if improved else n_bad[m] + 1
+                if improved or fresh[i]:
+                    best_metric[m], best_step[m] = x, steps[m]
+                    rows.append(i)
+                fresh[i] = False
+            if rows:
+                r = torch.tensor(rows, device=preds.device)
+                best_pred[r] = preds[r]
+            running = [active[i] and steps[occ[i]] < max_steps[occ[i]]
+                       and (early_stopping_patience is None or n_bad[occ[i]] <= early_stopping_patience)
+                       for i in range(S)]
+            stopped = [i for i in range(S) if active[i] and not running[i]]
+            finished += [(occ[i], best_step[occ[i]]) for i in stopped]
+            running_latest = [(occ[i], steps[occ[i]]) for i in range(S) if running[i]]
+            slot_of = {occ[i]: i for i in range(S) if active[i]}
 
             def lookup(key: CheckpointKey) -> Tensor:
-                i = pos[key[0]]
-                if active[i] and key[1] == steps[i]:
+                i = slot_of.get(key[0])
+                if i is not None and key[1] == steps[key[0]]:
                     return preds[i]
-                if key[1] == best_step[i]:
+                if i is not None and key[1] == best_step[key[0]]:
                     return best_pred[i]
                 return store[key]
 
@@ -448,17 +504,40 @@ class PackTrainer:
                 if ensemble.update(lookup, finished, running_latest):
                     ensemble_history.append({'step': loop_step, 'keys': list(ensemble.member_keys),
                                              'metric': -ensemble.best_score})
-            # keep the predictions that later updates may need: finished members' best
+            # keep the predictions that later updates may need: finished models' best
             # checkpoints and the current ensemble members (`rebuild_checkpoint_store`)
             required = set(finished) | set(ensemble.member_keys or [])
             store = {k: (store[k] if k in store else lookup(k).clone()) for k in required}
-            history.append({'step': loop_step, 'val_metric': torch.tensor(
-                [latest[i] if active[i] else math.nan for i in range(P)], dtype=torch.float64), 'train_loss': loss})
-            self._freeze([ids[i] - self.lo for i in stopped if self.lo <= ids[i] < self.hi])
-            active = running
-            if not any(active):
-                break
-        return FitResult(history=history, best_step=torch.tensor(best_step), best_metric=torch.tensor(best_metric),
+            vm = [math.nan] * M
+            tl = torch.full((M,), math.nan, dtype=loss.dtype)
+            loss_h = loss.cpu()
+            for i in range(S):
+                if active[i]:
+                    vm[occ[i]] = latest[i]
+                    tl[occ[i]] = loss_h[i]
+            history.append({'step': loop_step, 'val_metric': torch.tensor(vm, dtype=torch.float64),
+                            'train_loss': tl, 'slot_model': list(occ)})
+            # the replacement queue: freed slots take the next model ids, the rest stop training
+            pending = M - len(finished) - sum(running)
+            pairs = assign_replacements([ids[i] for i in stopped], next_model_id=next_model, n_pending=pending)
+            next_model += len(pairs)
+            refilled = {g for g, _ in pairs}
+            self._freeze([ids[i] - self.lo for i in stopped
+                          if ids[i] not in refilled and self.lo <= ids[i] < self.hi])
+            self._replace_local([(g - self.lo, m) for g, m in pairs if self.lo <= g < self.hi])
+            pos = {g: i for i, g in enumerate(ids)}
+            for i in stopped:
+                occ[i] = -1
+                self.slot_model[ids[i]] = -1
+            for g, m in pairs:
+                self.slot_model[g] = m
+                if g in pos:
+                    occ[pos[g]] = m
+                    fresh[pos[g]] = True
+            was_stopped = set(stopped)
+            active = [running[i] or (occ[i] >= 0 and i in was_stopped) for i in range(S)]
+        return FitResult(history=history, best_step=torch.tensor(best_step),
+                         best_metric=torch.tensor(best_metric, dtype=torch.float64),
                          ensemble_keys=list(ensemble.member_keys or []), ensemble_weights=ensemble.member_weights,
                          ensemble_metric=math.nan if ensemble.best_score is None else -ensemble.best_score,
                          ensemble_history=ensemble_history)

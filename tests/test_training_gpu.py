@@ -40,6 +40,11 @@ def _data(n, seed, dev):
 MODEL = dict(n_numerical_features=12, categorical_cardinalities=[3, 3], d_out=1, max_d_block=96, max_n_blocks=3)
 PER_MEMBER = [dict(n_blocks=nb, d_block=db, dropout=p) for nb, db, p in
               [(1, 64, 0.1), (3, 96, 0.2), (2, 32, 0.0), (3, 48, 0.3), (2, 96, 0.1), (1, 16, 0.05)]]
+# nine models through six slots (the replacement queue): shapes, dropout, Muon learning rate
+REPLACE_MODELS = PER_MEMBER + [dict(n_blocks=2, d_block=80, dropout=0.15), dict(n_blocks=1, d_block=96, dropout=0.0),
+                               dict(n_blocks=3, d_block=24, dropout=0.25)]
+REPLACE_OPT = [dict(muon_lr=lr) for lr in (1e-2, 2e-2, 5e-3, 1e-2, 3e-2, 2e-2, 1.5e-2, 2.5e-2, 8e-3)]
+REPLACE_MAX_EPOCHS = [2, 1, 3, 2, 1, 2, 1, 2, 1]
 
 
 def _trainer(member_range, opt='muon'):
@@ -147,3 +152,61 @@ def test_member_chunked_prediction_equals_whole_pack():
     y_pack, heads = pred(val['x_num'], val['x_cat'], member_chunk=4)
     assert torch.equal(y_pack, one)
     torch.testing.assert_close(heads['h'], one[[1, 4, 5]].mean(0), rtol=1e-6, atol=1e-6)
+
+
+def _replace_trainer():
+    from tabpack_b200.training import PackTrainer
+
+    return PackTrainer(n_members=6, model=MODEL, per_member_model=REPLACE_MODELS,
+                       optimizer=dict(type='muon', adamw_lr=3e-3, weight_decay=1e-4, muon_lr=2e-2),
+                       per_member_optimizer=REPLACE_OPT, loss='mse', seed=99, device='cuda', n_models=9)
+
+
+def test_replacement_gives_the_slot_a_fresh_model():
+    """A slot taken over by a new model (`pack_replace`, `_training.py:860-924`): the model's
+    shapes, dropout and learning rate, parameters keyed by model id (the same in any slot),
+    zeroed optimizer state and the Muon update scale of the new shape; the other slots are
+    untouched, and the layers' bf16 compute copies follow the new weights."""
+    import math
+
+    data, val = _data(640, 0, 'cuda'), _data(300, 1, 'cuda')
+    a, b = _replace_trainer(), _replace_trainer()
+    for t in (a, b):
+        t.fit_epoch(data, batch_size=64, epoch=0)
+    before = {n: p.detach().clone() for n, p in a.model.named_parameters()}
+    pred_before = a.predict_local(val)
+    a._replace_local([(2, 7)])
+    b._replace_local([(4, 7)])
+    hp = REPLACE_MODELS[7]
+    bb = a.model.backbone
+    assert int(bb.n_blocks[2]) == hp['n_blocks']
+    assert all(int(blk.linear.out_features[2]) == hp['d_block'] for blk in bb.blocks)
+    assert int(a.model.output.in_features[2]) == hp['d_block']
+    assert all(abs(float(blk.dropout.p[2]) - hp['dropout']) < 1e-7 for blk in bb.blocks)
+    params_b = dict(b.model.named_parameters())
+    for n, p in a.model.named_parameters():
+        keep = torch.ones(p.shape[0], dtype=torch.bool, device=p.device)
+        keep[2] = False
+        assert torch.equal(p[keep], before[n][keep]), n
+        assert torch.equal(p[2], params_b[n][4]), n  # initialisation keyed by model id, not slot
+    for g in a.opt.param_groups:
+        if g['muon']:
+            assert abs(float(g['muon_lr'][2]) / REPLACE_OPT[7]['muon_lr'] - 1) < 1e-6
+            lin = next(blk.linear for blk in bb.blocks if blk.linear.weight is g['params'][0])
+            o = int(lin.out_features[2])
+            i = lin.max_in_features if lin.in_features is None else int(lin.in_features[2])
+            assert abs(float(g['muon_update_scale'][2]) - math.sqrt(max(1.0, o / i))) < 1e-6
+        for p in g['params']:
+            for v in a.opt.state[p].values():
+                if isinstance(v, torch.Tensor) and v.ndim > 0:
+                    assert not v[2].any()
+    pred = a.predict_local(val)
+    assert torch.equal(pred[[0, 1, 3, 4, 5]], pred_before[[0, 1, 3, 4, 5]])
+    assert not torch.equal(pred[2], pred_before[2])
+    with torch.no_grad():  # every weight's version moves: the compute copies are cast again
+        for p in a.model.parameters():
+            p.add_(0.0)
+    assert torch.equal(a.predict_local(val), pred)
+    # the replaced slot trains on
+    loss = a.fit_epoch(data, batch_size=64, epoch=1)
+    assert torch.isfinite(loss).all()
