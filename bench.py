@@ -865,13 +865,11 @@ def run_train(args) -> None:
     barrier()
     e2e_ms = e0.elapsed_time(e1)
 
-    # per-family kernel time over one more scaled epoch, launch by launch (CUDA events; the
-    # Muon groups one after another so that no launch's time includes another's)
-    trainer.opt.concurrent_muon_groups = False
+    # per-family kernel time over one more scaled epoch, launch by launch (CUDA events on the
+    # one stream every launch of the step runs on)
     with ops.KernelTimes() as kt:
         epoch(dev_data['train'], dev_data['val'], 3)
     barrier()
-    trainer.opt.concurrent_muon_groups = True
 
     t = torch.tensor([region_ms, train_ms, e2e_ms], device=dev, dtype=torch.float64)
     if world > 1:

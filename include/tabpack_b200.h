@@ -259,6 +259,17 @@ typedef struct tp_muon_args {
 size_t tp_muon_workspace_size(int32_t P, int32_t max_out, int32_t max_in);
 int tp_muon_step(const tp_muon_args* a, void* stream);
 
+/* Several Muon parameter groups in one call (MuonAdamWPack.step's loop over its Muon groups,
+ * src/tabpackage/optim.py:682-774 per group): each group's momentum, normalisation and
+ * update as tp_muon_step computes them, bit for bit, with the Newton-Schulz GEMMs of all
+ * groups in shared launches (their tiles in one dynamically claimed list; fewer, fuller
+ * launches than one set per group).  The groups' own workspace fields are ignored; the
+ * call's workspace (256-byte aligned) holds every group's operands at common strides.  All
+ * groups take the same ns_steps; at most 65535 members over all groups. */
+size_t tp_muon_grouped_workspace_size(const tp_muon_args* groups, int32_t n_groups);
+int tp_muon_step_grouped(const tp_muon_args* groups, int32_t n_groups, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
 #define TP_METRIC_MSE 0
 #define TP_METRIC_MAE 1
 #define TP_METRIC_ACCURACY 2        /* int64 predicted labels (P, N) vs int64 labels */

@@ -165,6 +165,9 @@ SIGNATURES = {
     'tp_adamw_step': (ctypes.c_int, [ctypes.POINTER(AdamWArgs), ctypes.c_void_p]),
     'tp_muon_workspace_size': (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]),
     'tp_muon_step': (ctypes.c_int, [ctypes.POINTER(MuonArgs), ctypes.c_void_p]),
+    'tp_muon_grouped_workspace_size': (ctypes.c_size_t, [ctypes.POINTER(MuonArgs), ctypes.c_int32]),
+    'tp_muon_step_grouped': (ctypes.c_int, [ctypes.POINTER(MuonArgs), ctypes.c_int32, ctypes.c_void_p,
+                                            ctypes.c_size_t, ctypes.c_void_p]),
     'tp_metric_pack': (ctypes.c_int, [ctypes.POINTER(MetricArgs), ctypes.c_void_p]),
     'tp_greedy_workspace_size': (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int64, ctypes.c_int32]),
     'tp_greedy_ensemble': (ctypes.c_int, [ctypes.POINTER(GreedyArgs), ctypes.c_void_p]),

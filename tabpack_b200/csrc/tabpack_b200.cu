@@ -349,11 +349,13 @@ struct MuonLayout {
 
 constexpr int MUON_COUNTERS = 64;
 
-MuonLayout muon_layout(int P, int max_out, int max_in) {
+// Workspace of Newton-Schulz operands for P members with (R_s, C_s) strides and
+// `partials` per-tile norm partials.
+MuonLayout muon_layout_rc(int P, int R_s, int C_s, size_t partials) {
   auto up = [](size_t v, size_t a) { return (v + a - 1) / a * a; };
   MuonLayout L{};
-  L.R_s = (int)up((size_t)std::min(max_out, max_in), 128);
-  L.C_s = (int)up((size_t)std::max(max_out, max_in), 256);
+  L.R_s = R_s;
+  L.C_s = C_s;
   size_t o = 0;
   auto take = [&](size_t bytes) { const size_t at = o; o = up(o + bytes, 256); return at; };
   L.off_x0 = take((size_t)P * L.R_s * L.C_s * 2);
@@ -365,8 +367,7 @@ MuonLayout muon_layout(int P, int max_out, int max_in) {
   L.off_cols = take((size_t)P * 4);
   L.off_trans = take((size_t)P * 4);
   L.off_active = take((size_t)P * 4);
-  L.tiles = ((max_out + MUON_TM - 1) / MUON_TM) * ((max_in + MUON_TN - 1) / MUON_TN);
-  L.off_partial = take((size_t)P * L.tiles * 4);
+  L.off_partial = take(partials * 4);
   L.off_counter = take(MUON_COUNTERS * 4);  // tile counters of the Newton-Schulz launches
   // dense tile lists of the Newton-Schulz launches (r x r and r x c outputs) and their lengths
   const size_t mtl = (size_t)L.R_s / NS_TILE_M;
@@ -375,6 +376,21 @@ MuonLayout muon_layout(int P, int max_out, int max_in) {
   L.off_list_sym = take((size_t)P * mtl * ((L.R_s + NS_TILE_N - 1) / NS_TILE_N) * 4);
   L.off_list_n = take(NS_LISTS * 4);
   L.total = o;
+  return L;
+}
+
+// Operand strides of one group: r rounded to the 128-row tiles, c to the 256-column tiles.
+int muon_rows_stride(int max_out, int max_in) { return (std::min(max_out, max_in) + 127) / 128 * 128; }
+int muon_cols_stride(int max_out, int max_in) { return (std::max(max_out, max_in) + 255) / 256 * 256; }
+int muon_prologue_tiles(int max_out, int max_in) {
+  return ((max_out + MUON_TM - 1) / MUON_TM) * ((max_in + MUON_TN - 1) / MUON_TN);
+}
+
+MuonLayout muon_layout(int P, int max_out, int max_in) {
+  const int tiles = muon_prologue_tiles(max_out, max_in);
+  MuonLayout L = muon_layout_rc(P, muon_rows_stride(max_out, max_in), muon_cols_stride(max_out, max_in),
+                                (size_t)P * tiles);
+  L.tiles = tiles;
   return L;
 }
 
@@ -770,18 +786,21 @@ size_t tp_muon_workspace_size(int32_t P, int32_t max_out, int32_t max_in) {
   return muon_layout(P, max_out, max_in).total;
 }
 
-int tp_muon_step(const tp_muon_args* a, void* stream) {
+}  // extern "C"
+
+namespace tp {
+namespace {
+
+// Checks one group's arguments and fills the per-group fields of m (hyperparameters, tensors,
+// the bf16 copy, depth gating); the workspace fields are set by the caller.
+int muon_group_args(const tp_muon_args* a, MuonArgs* out) {
   if (!a || a->P <= 0 || a->max_out <= 0 || a->max_in <= 0) return fail(TP_EINVAL, "bad Muon shapes");
-  if (!a->p || !a->grad || !a->momentum_buffer || !a->workspace) return fail(TP_EINVAL, "null Muon tensor");
+  if (!a->p || !a->grad || !a->momentum_buffer) return fail(TP_EINVAL, "null Muon tensor");
   if (a->ns_steps < 0) return fail(TP_EINVAL, "negative Newton-Schulz step count");
-  const DeviceInfo dinfo = device_info();
-  if (dinfo.major != 10) return fail(TP_EUNSUPPORTED, "Newton-Schulz GEMMs need an sm_100 device");
-  const MuonLayout L = muon_layout(a->P, a->max_out, a->max_in);
-  if (a->workspace_bytes < L.total)
-    return fail(TP_EINVAL, "Muon workspace holds %zu bytes, needs %zu", a->workspace_bytes, L.total);
-  if ((reinterpret_cast<uintptr_t>(a->workspace) & 255u) != 0) return fail(TP_EALIGN, "workspace must be 256-byte aligned");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  if (a->P > 65535) return fail(TP_EINVAL, "at most 65535 members per Muon call");
+  if (a->p_bf16 != nullptr && (a->p_bf16_rows < a->max_out || a->p_bf16_cols < a->max_in))
+    return fail(TP_EINVAL, "the bf16 copy (%d x %d per member) is smaller than p (%d x %d)", a->p_bf16_rows,
+                a->p_bf16_cols, a->max_out, a->max_in);
   MuonArgs m{};
   m.P = a->P;
   m.max_out = a->max_out;
@@ -806,51 +825,72 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
   m.scale_s = (float)std::sqrt(std::max(1.0, (double)a->max_out / (double)a->max_in));
   m.nesterov = a->nesterov;
   m.mutate_grad = a->mutate_grad;
-  m.R_s = L.R_s;
-  m.C_s = L.C_s;
-  m.norm2 = reinterpret_cast<float*>(ws + L.off_norm);
-  m.rows = reinterpret_cast<int32_t*>(ws + L.off_rows);
-  m.cols = reinterpret_cast<int32_t*>(ws + L.off_cols);
-  m.trans = reinterpret_cast<int32_t*>(ws + L.off_trans);
-  m.active = reinterpret_cast<int32_t*>(ws + L.off_active);
-  m.partial = reinterpret_cast<float*>(ws + L.off_partial);
-  m.tiles = L.tiles;
-  void* x0 = ws + L.off_x0;
-  void* x1 = ws + L.off_x1;
-  void* A = ws + L.off_a;
-  void* Bm = ws + L.off_b;
-  m.x = reinterpret_cast<__nv_bfloat16*>(x0);
-  if (a->p_bf16 != nullptr && (a->p_bf16_rows < a->max_out || a->p_bf16_cols < a->max_in))
-    return fail(TP_EINVAL, "the bf16 copy (%d x %d per member) is smaller than p (%d x %d)", a->p_bf16_rows,
-                a->p_bf16_cols, a->max_out, a->max_in);
   m.p_bf16 = static_cast<__nv_bfloat16*>(a->p_bf16);
   m.n_blocks = a->n_blocks;
   m.block_index = a->block_index;
   m.bf16_rows = a->p_bf16_rows;
   m.bf16_cols = a->p_bf16_cols;
+  *out = m;
+  return TP_OK;
+}
 
-  if (a->P > 65535) return fail(TP_EINVAL, "at most 65535 members per Muon call");
+// Points a group's MuonArgs at members [first, first + P) of a workspace laid out by L, whose
+// per-tile norm partials start at partial element `partial_first`.
+void muon_bind(MuonArgs& m, const MuonLayout& L, uint8_t* ws, int first, size_t partial_first, int tiles) {
+  m.R_s = L.R_s;
+  m.C_s = L.C_s;
+  m.x = reinterpret_cast<__nv_bfloat16*>(ws + L.off_x0) + (size_t)first * L.R_s * L.C_s;
+  m.norm2 = reinterpret_cast<float*>(ws + L.off_norm) + first;
+  m.rows = reinterpret_cast<int32_t*>(ws + L.off_rows) + first;
+  m.cols = reinterpret_cast<int32_t*>(ws + L.off_cols) + first;
+  m.trans = reinterpret_cast<int32_t*>(ws + L.off_trans) + first;
+  m.active = reinterpret_cast<int32_t*>(ws + L.off_active) + first;
+  m.partial = reinterpret_cast<float*>(ws + L.off_partial) + partial_first;
+  m.tiles = tiles;
+}
+
+// Momentum, the oriented bf16 operand and its Frobenius normalisation for one bound group;
+// (rows_ext, cols_ext) bound the normalisation grid (the group's own operand extent).
+void muon_prepare(const MuonArgs& m, int rows_ext, int cols_ext, cudaStream_t st) {
+  dim3 tiles((m.max_in + MUON_TN - 1) / MUON_TN, (m.max_out + MUON_TM - 1) / MUON_TM, m.P);
+  dim3 ngrid((cols_ext + 255) / 256, (rows_ext + 31) / 32, m.P);
+  TP_PROF(TP_PROF_MUON_ELEMENTWISE, st);
+  muon_geometry_kernel<<<(m.P + 255) / 256, 256, 0, st>>>(m);
+  muon_prologue_kernel<<<tiles, 256, 0, st>>>(m);
+  muon_norm_kernel<<<m.P, 256, 0, st>>>(m, (int)tiles.x);
+  muon_normalize_kernel<<<ngrid, 256, 0, st>>>(m, 128, 256);
+}
+
+// The scaled update (and bf16 copy) of one bound group from the Newton-Schulz result x.
+void muon_finish(MuonArgs m, __nv_bfloat16* x, cudaStream_t st) {
+  m.x = x;
+  dim3 tiles((m.max_in + MUON_TN - 1) / MUON_TN, (m.max_out + MUON_TM - 1) / MUON_TM, m.P);
+  TP_PROF(TP_PROF_MUON_ELEMENTWISE, st);
+  muon_apply_kernel<<<tiles, 256, 0, st>>>(m);
+}
+
+// ns_steps quintic Newton-Schulz iterations over every member of the workspace (mu: the
+// workspace-wide view: P, rows, cols, active, R_s); *result receives the final operand.
+int muon_newton_schulz(const MuonArgs& mu, const MuonLayout& L, uint8_t* ws, int ns_steps, cudaStream_t st,
+                       void** result) {
   if (L.R_s / NS_TILE_M > 255 || (L.C_s + NS_TILE_N - 1) / NS_TILE_N > 255)
-    return fail(TP_EINVAL, "Muon matrices of at most 32640 x 65280 elements (got %d x %d)", a->max_out, a->max_in);
+    return fail(TP_EINVAL, "Muon matrices of at most 32640 x 65280 elements (operand strides %d x %d)", L.R_s,
+                L.C_s);
   uint32_t* list_rr = reinterpret_cast<uint32_t*>(ws + L.off_list_rr);
   uint32_t* list_rc = reinterpret_cast<uint32_t*>(ws + L.off_list_rc);
   uint32_t* list_sym = reinterpret_cast<uint32_t*>(ws + L.off_list_sym);
   int* list_n = reinterpret_cast<int*>(ws + L.off_list_n);
-  dim3 tiles((a->max_in + MUON_TN - 1) / MUON_TN, (a->max_out + MUON_TM - 1) / MUON_TM, a->P);
-  dim3 ngrid((L.C_s + 255) / 256, (L.R_s + 31) / 32, a->P);
   {
     TP_PROF(TP_PROF_MUON_ELEMENTWISE, st);
-    muon_geometry_kernel<<<(a->P + 255) / 256, 256, 0, st>>>(m);
-    muon_prologue_kernel<<<tiles, 256, 0, st>>>(m);
-    muon_norm_kernel<<<a->P, 256, 0, st>>>(m, (int)tiles.x);
-    muon_normalize_kernel<<<ngrid, 256, 0, st>>>(m, 128, 256);
-    ns_tile_list_kernel<<<1, 1024, 0, st>>>(m, list_rr, list_rc, list_sym, list_n);
+    ns_tile_list_kernel<<<1, 1024, 0, st>>>(mu, list_rr, list_rc, list_sym, list_n);
   }
   TP_CUDA_TRY(cudaGetLastError());
   // quintic Newton-Schulz, coefficients of optim.py:477
   const float ca = 3.4445f, cb = -4.7750f, cc = 2.0315f;
-  void* X = x0;
-  void* Xn = x1;
+  void* X = ws + L.off_x0;
+  void* Xn = ws + L.off_x1;
+  void* A = ws + L.off_a;
+  void* Bm = ws + L.off_b;
   int rc;
   // one zeroed tile counter per Newton-Schulz launch (the block is re-zeroed when it wraps;
   // stream order keeps the earlier launches' use of a counter before its memset)
@@ -861,25 +901,119 @@ int tp_muon_step(const tp_muon_args* a, void* stream) {
       return nullptr;
     return counters + (launch++ % MUON_COUNTERS);
   };
-  for (int it = 0; it < a->ns_steps; ++it) {
+  for (int it = 0; it < ns_steps; ++it) {
     int* c1 = counter();
     int* c2 = counter();
     int* c3 = counter();
     if (!c1 || !c2 || !c3) return fail(TP_ECUDA, "cudaMemsetAsync of the tile counters failed");
     // A = X X^T is symmetric: only the tiles not below the diagonal, the rest written as transposes
-    if ((rc = ns_gemm<MODE_NS>(m, 1, X, L.C_s, X, L.C_s, A, L.R_s, nullptr, 1.0f, 0.0f, list_sym, list_n + 2, c1, st,
-                               1)))
+    if ((rc = ns_gemm<MODE_NS>(mu, 1, X, L.C_s, X, L.C_s, A, L.R_s, nullptr, 1.0f, 0.0f, list_sym, list_n + 2, c1,
+                               st, 1)))
       return rc;
     // B = b A + c A^2 is symmetric as well
-    if ((rc = ns_gemm<MODE_NS>(m, 2, A, L.R_s, A, L.R_s, Bm, L.R_s, A, cc, cb, list_sym, list_n + 2, c2, st, 1)))
+    if ((rc = ns_gemm<MODE_NS>(mu, 2, A, L.R_s, A, L.R_s, Bm, L.R_s, A, cc, cb, list_sym, list_n + 2, c2, st, 1)))
       return rc;
-    if ((rc = ns_gemm<MODE_NS_BMN>(m, 3, Bm, L.R_s, X, L.C_s, Xn, L.C_s, X, 1.0f, ca, list_rc, list_n + 1, c3, st)))
+    if ((rc = ns_gemm<MODE_NS_BMN>(mu, 3, Bm, L.R_s, X, L.C_s, Xn, L.C_s, X, 1.0f, ca, list_rc, list_n + 1, c3,
+                                   st)))
       return rc;
     std::swap(X, Xn);
   }
-  m.x = reinterpret_cast<__nv_bfloat16*>(X);
-  TP_PROF(TP_PROF_MUON_ELEMENTWISE, st);
-  muon_apply_kernel<<<tiles, 256, 0, st>>>(m);
+  *result = X;
+  return TP_OK;
+}
+
+int muon_check_device_and_workspace(const void* workspace, size_t have, size_t need) {
+  if (device_info().major != 10) return fail(TP_EUNSUPPORTED, "Newton-Schulz GEMMs need an sm_100 device");
+  if (!workspace) return fail(TP_EINVAL, "null Muon workspace");
+  if (have < need) return fail(TP_EINVAL, "Muon workspace holds %zu bytes, needs %zu", have, need);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return fail(TP_EALIGN, "workspace must be 256-byte aligned");
+  return TP_OK;
+}
+
+// Layout of a grouped call: every group's members one after another, common operand strides
+// (the largest group's), each group's norm partials after the previous group's.
+MuonLayout muon_grouped_layout(const tp_muon_args* g, int n) {
+  int P = 0, R = 0, C = 0;
+  size_t partials = 0;
+  for (int i = 0; i < n; ++i) {
+    P += g[i].P;
+    R = std::max(R, muon_rows_stride(g[i].max_out, g[i].max_in));
+    C = std::max(C, muon_cols_stride(g[i].max_out, g[i].max_in));
+    partials += (size_t)g[i].P * muon_prologue_tiles(g[i].max_out, g[i].max_in);
+  }
+  return muon_layout_rc(P, R, C, partials);
+}
+
+}  // namespace
+}  // namespace tp
+
+extern "C" {
+
+int tp_muon_step(const tp_muon_args* a, void* stream) {
+  MuonArgs m{};
+  int rc;
+  if ((rc = muon_group_args(a, &m))) return rc;
+  const MuonLayout L = muon_layout(a->P, a->max_out, a->max_in);
+  if ((rc = muon_check_device_and_workspace(a->workspace, a->workspace_bytes, L.total))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  muon_bind(m, L, ws, 0, 0, L.tiles);
+  muon_prepare(m, L.R_s, L.C_s, st);
+  TP_CUDA_TRY(cudaGetLastError());
+  void* X = nullptr;
+  if ((rc = muon_newton_schulz(m, L, ws, a->ns_steps, st, &X))) return rc;
+  muon_finish(m, static_cast<__nv_bfloat16*>(X), st);
+  TP_CUDA_TRY(cudaGetLastError());
+  return TP_OK;
+}
+
+size_t tp_muon_grouped_workspace_size(const tp_muon_args* groups, int32_t n_groups) {
+  if (!groups || n_groups <= 0) return 0;
+  for (int i = 0; i < n_groups; ++i)
+    if (groups[i].P <= 0 || groups[i].max_out <= 0 || groups[i].max_in <= 0) return 0;
+  return muon_grouped_layout(groups, n_groups).total;
+}
+
+int tp_muon_step_grouped(const tp_muon_args* groups, int32_t n_groups, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (!groups || n_groups <= 0) return fail(TP_EINVAL, "no Muon groups");
+  std::vector<MuonArgs> ms((size_t)n_groups);
+  int rc;
+  long long P = 0;
+  for (int i = 0; i < n_groups; ++i) {
+    if ((rc = muon_group_args(&groups[i], &ms[(size_t)i]))) return rc;
+    if (groups[i].ns_steps != groups[0].ns_steps)
+      return fail(TP_EINVAL, "grouped Muon steps share one Newton-Schulz step count (group %d: %d, group 0: %d)", i,
+                  groups[i].ns_steps, groups[0].ns_steps);
+    P += groups[i].P;
+  }
+  if (P > 65535) return fail(TP_EINVAL, "at most 65535 members over the groups of one grouped Muon call");
+  const MuonLayout L = muon_grouped_layout(groups, n_groups);
+  if ((rc = muon_check_device_and_workspace(workspace, workspace_bytes, L.total))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int first = 0;
+  size_t partial_first = 0;
+  for (int i = 0; i < n_groups; ++i) {
+    const tp_muon_args& g = groups[i];
+    const int tiles = muon_prologue_tiles(g.max_out, g.max_in);
+    muon_bind(ms[(size_t)i], L, ws, first, partial_first, tiles);
+    muon_prepare(ms[(size_t)i], muon_rows_stride(g.max_out, g.max_in), muon_cols_stride(g.max_out, g.max_in), st);
+    first += g.P;
+    partial_first += (size_t)g.P * tiles;
+  }
+  TP_CUDA_TRY(cudaGetLastError());
+  // the Newton-Schulz launches run over the members of every group at once
+  MuonArgs mu{};
+  muon_bind(mu, L, ws, 0, 0, 0);
+  mu.P = (int)P;
+  void* X = nullptr;
+  if ((rc = muon_newton_schulz(mu, L, ws, groups[0].ns_steps, st, &X))) return rc;
+  first = 0;
+  for (int i = 0; i < n_groups; ++i) {
+    muon_finish(ms[(size_t)i], static_cast<__nv_bfloat16*>(X) + (size_t)first * L.R_s * L.C_s, st);
+    first += groups[i].P;
+  }
   TP_CUDA_TRY(cudaGetLastError());
   return TP_OK;
 }

@@ -283,31 +283,25 @@ def muon_workspace_size(P: int, max_out: int, max_in: int) -> int:
     return int(load().tp_muon_workspace_size(P, max_out, max_in))
 
 
-def muon_step(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=None, in_features=None, lr,
-              momentum, weight_decay, update_scale=None, nesterov: bool = True, mutate_grad: bool = True,
-              ns_steps: int = 5, workspace: Tensor | None = None, p_bf16: Tensor | None = None,
-              n_blocks: Tensor | None = None, block_index: int = 0) -> None:
-    """One Muon group step on a packed (P, max_out, max_in) fp32 weight; see `tp_muon_step`.
-    `p_bf16` (P, rows >= max_out, cols >= max_in) bf16, optional, receives bf16 of the updated
-    weights of each member's out x in block in the same pass.  `n_blocks` / `block_index`: the
-    weight's block is depth-gated for members with n_blocks <= block_index (their gradient is
-    exactly zero and is not read)."""
+def _muon_args(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=None, in_features=None, lr,
+               momentum, weight_decay, update_scale=None, nesterov: bool = True, mutate_grad: bool = True,
+               ns_steps: int = 5, p_bf16: Tensor | None = None, n_blocks: Tensor | None = None,
+               block_index: int = 0):
+    """`tp_muon_args` of one group (workspace unset), the tensors that must stay alive until
+    the launch is queued, and the tensors the step writes."""
     for name, t in (('p', p), ('grad', grad), ('momentum_buffer', momentum_buffer)):
         if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous() or t.ndim != 3:
             raise TypeError(f'{name} must be a contiguous 3-D fp32 CUDA tensor')
     P, mo, mi = p.shape
-    need = muon_workspace_size(P, mo, mi)
-    if workspace is None or workspace.numel() * workspace.element_size() < need:
-        workspace = torch.empty(need, dtype=torch.uint8, device=p.device)
     a = _lib.MuonArgs()
     a.P, a.max_out, a.max_in = P, mo, mi
     a.p, a.grad, a.momentum_buffer = p.data_ptr(), grad.data_ptr(), momentum_buffer.data_ptr()
-    a.out_features = _ptr(_i32('out_features', out_features))
-    a.in_features = _ptr(_i32('in_features', in_features))
+    of, inf = _i32('out_features', out_features), _i32('in_features', in_features)
+    a.out_features, a.in_features = _ptr(of), _ptr(inf)
     a.lr, a.momentum, a.weight_decay = _hparam(lr), _hparam(momentum), _hparam(weight_decay)
-    a.update_scale = _ptr(_cuda('update_scale', update_scale, torch.float32))
+    us = _cuda('update_scale', update_scale, torch.float32)
+    a.update_scale = _ptr(us)
     a.nesterov, a.mutate_grad, a.ns_steps = int(nesterov), int(mutate_grad), int(ns_steps)
-    a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     if p_bf16 is not None:
         if (not p_bf16.is_cuda or p_bf16.dtype != torch.bfloat16 or not p_bf16.is_contiguous() or p_bf16.ndim != 3
                 or p_bf16.shape[0] != P):
@@ -318,9 +312,69 @@ def muon_step(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=
         if nb.shape != (P,):
             raise ValueError(f'n_blocks must be ({P},), got {tuple(nb.shape)}')
         a.n_blocks, a.block_index = nb.data_ptr(), int(block_index)
-    keep = (out_features, in_features, update_scale, nb)  # noqa: F841  (alive until the launch is queued)
+    keep = (of, inf, us, nb, lr, momentum, weight_decay)
+    written = [p, momentum_buffer] + ([grad] if mutate_grad else []) + ([p_bf16] if p_bf16 is not None else [])
+    return a, keep, written
+
+
+def muon_step(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=None, in_features=None, lr,
+              momentum, weight_decay, update_scale=None, nesterov: bool = True, mutate_grad: bool = True,
+              ns_steps: int = 5, workspace: Tensor | None = None, p_bf16: Tensor | None = None,
+              n_blocks: Tensor | None = None, block_index: int = 0) -> None:
+    """One Muon group step on a packed (P, max_out, max_in) fp32 weight; see `tp_muon_step`.
+    `p_bf16` (P, rows >= max_out, cols >= max_in) bf16, optional, receives bf16 of the updated
+    weights of each member's out x in block in the same pass.  `n_blocks` / `block_index`: the
+    weight's block is depth-gated for members with n_blocks <= block_index (their gradient is
+    exactly zero and is not read)."""
+    a, keep, written = _muon_args(p, grad, momentum_buffer, out_features=out_features, in_features=in_features,
+                                  lr=lr, momentum=momentum, weight_decay=weight_decay, update_scale=update_scale,
+                                  nesterov=nesterov, mutate_grad=mutate_grad, ns_steps=ns_steps, p_bf16=p_bf16,
+                                  n_blocks=n_blocks, block_index=block_index)
+    P, mo, mi = p.shape
+    need = muon_workspace_size(P, mo, mi)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=p.device)
+    a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     check(load().tp_muon_step(ctypes.byref(a), _stream()), 'tp_muon_step')
-    increment_version([p, momentum_buffer] + ([grad] if mutate_grad else []) + ([p_bf16] if p_bf16 is not None else []))
+    del keep
+    increment_version(written)
+
+
+def muon_grouped_workspace_size(shapes: list[tuple[int, int, int]]) -> int:
+    """Bytes of the workspace of a grouped Muon call over weights of these (P, max_out, max_in)."""
+    arr = (_lib.MuonArgs * len(shapes))()
+    for a, (P, mo, mi) in zip(arr, shapes):
+        a.P, a.max_out, a.max_in = P, mo, mi
+    return int(load().tp_muon_grouped_workspace_size(arr, len(shapes)))
+
+
+def muon_step_grouped(steps: list[dict], *, workspace: Tensor | None = None) -> None:
+    """Several Muon groups of one device in one call (`tp_muon_step_grouped`): each entry of
+    `steps` holds `muon_step`'s arguments for one group (`p`, `grad`, `momentum_buffer`, ...,
+    without `workspace`).  Each group's result equals its own `muon_step` bit for bit; the
+    Newton-Schulz GEMMs of all groups share launches."""
+    if not steps:
+        return
+    built = [_muon_args(**kw) for kw in steps]
+    arr = (_lib.MuonArgs * len(built))(*[b[0] for b in built])
+    need = muon_grouped_workspace_size([tuple(kw['p'].shape) for kw in steps])
+    dev = steps[0]['p'].device
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    check(load().tp_muon_step_grouped(arr, len(built), workspace.data_ptr(),
+                                      workspace.numel() * workspace.element_size(), _stream()),
+          'tp_muon_step_grouped')
+    del built
+    increment_version([t for kw in steps for t in _muon_written(kw)])
+
+
+def _muon_written(kw: dict) -> list:
+    out = [kw['p'], kw['momentum_buffer']]
+    if kw.get('mutate_grad', True):
+        out.append(kw['grad'])
+    if kw.get('p_bf16') is not None:
+        out.append(kw['p_bf16'])
+    return out
 
 
 def metric_pack(metric: str, y_pred: Tensor, y_true: Tensor, classes: int = 1) -> Tensor:

@@ -285,12 +285,11 @@ class MuonAdamWPack(OptimizerPack):
         return loss
 
 
-def _muon_workspace(workspaces: dict, p: Tensor, slot: int = 0) -> Tensor:
-    """Newton-Schulz workspace `slot` of `p`'s device, grown to fit `p` (groups that run
-    concurrently use different slots)."""
+def _muon_workspace(workspaces: dict, p: Tensor) -> Tensor:
+    """Newton-Schulz workspace of `p`'s device, grown to fit `p`."""
     P, mo, mi = p.shape
     n = ops.muon_workspace_size(P, mo, mi)
-    key = (p.device, slot)
+    key = (p.device, 'single')
     ws = workspaces.get(key)
     if ws is None or ws.numel() < n:
         ws = torch.empty(n, dtype=torch.uint8, device=p.device)
@@ -298,40 +297,82 @@ def _muon_workspace(workspaces: dict, p: Tensor, slot: int = 0) -> Tensor:
     return ws
 
 
-def _muon_group(opt: torch.optim.Optimizer, g: dict, *, workspaces: dict, allow_inplace_grad_mutation: bool,
-                slot: int = 0) -> None:
-    """`MuonAdamWPack._step_muon` (`optim.py:682-774`) for one single-parameter Muon group:
-    weight decay, momentum, Nesterov blend, batched Newton-Schulz and the scaled update in the
-    Muon kernels.  Per-member widths (`muon_out_features` / `muon_in_features`) keep each
+def _muon_kwargs(opt: torch.optim.Optimizer, g: dict, *, allow_inplace_grad_mutation: bool):
+    """`MuonAdamWPack._step_muon` (`optim.py:682-774`) for one single-parameter Muon group, as
+    the arguments of `ops.muon_step` (weight decay, momentum, Nesterov blend, batched
+    Newton-Schulz and the scaled update run in the Muon kernels), or None when the parameter
+    has no gradient.  Per-member widths (`muon_out_features` / `muon_in_features`) keep each
     member's Newton-Schulz on its own out x in block; without them it runs on the padded block
-    (the reference's arithmetic: zero padding rows and columns do not change the result)."""
+    (the reference's arithmetic: zero padding rows and columns do not change the result).  The
+    second value is the bf16 compute-copy cache to close after the step."""
     p = g['params'][0]
     if p.ndim != 3:
         raise ValueError('Parameters optimized with Muon must have three dimensions')
     if p.grad is None:
-        return
+        return None, None
     if p.grad.is_sparse:
         raise RuntimeError('Sparse gradients are not supported')
     st = opt.state[p]
     if len(st) == 0:
         st['muon_momentum_buffer'] = torch.zeros_like(p)
-    # without in-place mutation the kernel leaves the gradient as it is (the reference blends
-    # into a copy), so no copy is made here
-    grad = p.grad.data
     scale = g.get('muon_update_scale')
     # the layer's bf16 compute copy, refreshed in the pass that writes the weights (otherwise the
     # next forward casts the whole weight pack again)
     cache = bf16_copy_cache(p)
     copy = cache.begin_update(p) if cache is not None else None
-    ops.muon_step(p, grad, st['muon_momentum_buffer'], out_features=g.get('muon_out_features'),
-                  in_features=g.get('muon_in_features'), lr=_hp(g['muon_lr']), momentum=_hp(g['muon_momentum']),
-                  weight_decay=_hp(g['weight_decay']),
-                  update_scale=None if scale is None else scale.to(torch.float32).contiguous(),
-                  nesterov=bool(g['muon_nesterov']), mutate_grad=allow_inplace_grad_mutation,
-                  ns_steps=int(g['muon_newton_schulz_steps']), workspace=_muon_workspace(workspaces, p, slot),
-                  p_bf16=copy, n_blocks=g.get('muon_n_blocks'), block_index=int(g.get('muon_block_index', 0)))
+    # without in-place mutation the kernel leaves the gradient as it is (the reference blends
+    # into a copy), so no copy is made here
+    kw = dict(p=p, grad=p.grad.data, momentum_buffer=st['muon_momentum_buffer'],
+              out_features=g.get('muon_out_features'), in_features=g.get('muon_in_features'),
+              lr=_hp(g['muon_lr']), momentum=_hp(g['muon_momentum']), weight_decay=_hp(g['weight_decay']),
+              update_scale=None if scale is None else scale.to(torch.float32).contiguous(),
+              nesterov=bool(g['muon_nesterov']), mutate_grad=allow_inplace_grad_mutation,
+              ns_steps=int(g['muon_newton_schulz_steps']), p_bf16=copy, n_blocks=g.get('muon_n_blocks'),
+              block_index=int(g.get('muon_block_index', 0)))
+    return kw, (cache, copy)
+
+
+def _close_copy(kw: dict, closing) -> None:
+    cache, copy = closing
     if copy is not None:
-        cache.end_update(p, copy)
+        cache.end_update(kw['p'], copy)
+
+
+def _muon_group(opt: torch.optim.Optimizer, g: dict, *, workspaces: dict, allow_inplace_grad_mutation: bool) -> None:
+    """One Muon group in its own call (`tp_muon_step`)."""
+    kw, closing = _muon_kwargs(opt, g, allow_inplace_grad_mutation=allow_inplace_grad_mutation)
+    if kw is None:
+        return
+    ops.muon_step(**kw, workspace=_muon_workspace(workspaces, kw['p']))
+    _close_copy(kw, closing)
+
+
+def _muon_groups(opt: torch.optim.Optimizer, groups: list, *, workspaces: dict,
+                 allow_inplace_grad_mutation: bool) -> None:
+    """The Muon groups of one device in one grouped call (`tp_muon_step_grouped`): the same
+    results as one call per group, with the Newton-Schulz GEMMs of all groups in shared
+    launches (fewer and fuller launches: the tails of one group's launches no longer leave
+    SMs idle)."""
+    built = [_muon_kwargs(opt, g, allow_inplace_grad_mutation=allow_inplace_grad_mutation) for g in groups]
+    built = [(kw, c) for kw, c in built if kw is not None]
+    if not built:
+        return
+    steps = [kw for kw, _ in built]
+    if len({kw['ns_steps'] for kw in steps}) > 1:
+        for kw, closing in built:
+            ops.muon_step(**kw, workspace=_muon_workspace(workspaces, kw['p']))
+            _close_copy(kw, closing)
+        return
+    need = ops.muon_grouped_workspace_size([tuple(kw['p'].shape) for kw in steps])
+    dev = steps[0]['p'].device
+    key = (dev, 'grouped')
+    ws = workspaces.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        workspaces[key] = ws
+    ops.muon_step_grouped(steps, workspace=ws)
+    for kw, closing in built:
+        _close_copy(kw, closing)
 
 
 def adamw_step(opt: torch.optim.Optimizer, *, support_replacement: bool) -> None:
@@ -347,46 +388,22 @@ def muon_adamw_step(opt: torch.optim.Optimizer, *, workspaces: dict, allow_inpla
     """`MuonAdamWPack.step` (`optim.py:495-861`) over every group of `opt`: Muon groups through
     the Muon kernels, the others through the grouped AdamW kernel (`adamw_*` keys).
 
-    The Muon groups of one device are independent, so they run concurrently, each on a side
-    stream of its own (after the current stream's work so far, which the current stream then
-    waits for): one group's Newton-Schulz launches fill the SMs that another's leave idle at
-    its ramp and tail.  Each concurrent group has its own workspace."""
-    muon = [g for g in opt.param_groups if g['muon'] and g['params'][0].grad is not None]
-    streams = _side_streams(opt, muon)
-    if streams:
-        main = torch.cuda.current_stream(muon[0]['params'][0].device)
-        ready = torch.cuda.Event()
-        ready.record(main)
-        for i, (g, s) in enumerate(zip(muon, streams)):
-            s.wait_event(ready)
-            with torch.cuda.stream(s):
-                _muon_group(opt, g, workspaces=workspaces, allow_inplace_grad_mutation=allow_inplace_grad_mutation,
-                            slot=i)
-    else:
-        for g in muon:
-            _muon_group(opt, g, workspaces=workspaces, allow_inplace_grad_mutation=allow_inplace_grad_mutation)
+    The Muon groups of one device go to one grouped call when there are several (unless the
+    optimizer's `grouped_muon` is False, e.g. to time each group's launches on their own)."""
+    by_device: dict = {}
+    for g in opt.param_groups:
+        if g['muon'] and g['params'][0].grad is not None:
+            by_device.setdefault(g['params'][0].device, []).append(g)
+    for dev, groups in by_device.items():
+        if len(groups) > 1 and dev.type == 'cuda' and getattr(opt, 'grouped_muon', True):
+            _muon_groups(opt, groups, workspaces=workspaces, allow_inplace_grad_mutation=allow_inplace_grad_mutation)
+        else:
+            for g in groups:
+                _muon_group(opt, g, workspaces=workspaces, allow_inplace_grad_mutation=allow_inplace_grad_mutation)
     for g in opt.param_groups:
         if not g['muon']:
             _adamw_group(opt, g['params'], lr=g['adamw_lr'], beta1=g['adamw_beta1'], beta2=g['adamw_beta2'],
                          eps=g['adamw_eps'], weight_decay=g['weight_decay'], support_replacement=support_replacement)
-    if streams:
-        for s in streams:
-            main.wait_stream(s)
-
-
-def _side_streams(opt: torch.optim.Optimizer, groups: list) -> list:
-    """One side stream per Muon group when there are several on one CUDA device (kept on the
-    optimizer), else [] (also when the optimizer's `concurrent_muon_groups` is False, e.g. to
-    time each launch on its own)."""
-    if len(groups) < 2 or not getattr(opt, 'concurrent_muon_groups', True):
-        return []
-    dev = groups[0]['params'][0].device
-    if dev.type != 'cuda' or any(g['params'][0].device != dev for g in groups):
-        return []
-    pool = opt.__dict__.setdefault('_side_streams', {}).setdefault(dev, [])
-    while len(pool) < len(groups):
-        pool.append(torch.cuda.Stream(device=dev))
-    return pool[:len(groups)]
 
 
 def optimizer_pack_remove(optimizer, *, pack_idx: Tensor, old_to_new_parameters) -> None:

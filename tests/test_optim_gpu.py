@@ -379,3 +379,49 @@ def test_muon_step_with_depth_gated_members():
     live = (nb > 1)[:, None, None] & valid
     assert torch.equal(ca[live.expand_as(ca)], cb[live.expand_as(cb)])
     assert not torch.equal(pa[4], p0[4] * (1 - 0.02 * 1e-2))  # the nonzero momentum still moved it
+
+
+def test_grouped_muon_equals_one_call_per_group():
+    """`tp_muon_step_grouped` over three groups of different shapes (a transposed one, ragged
+    widths, a member with an all-zero update, per-member and scalar hyperparameters, a bf16
+    copy, depth gating, a mutated gradient) gives each group exactly its own `tp_muon_step`
+    result: weights, momentum, gradient and bf16 copy bit for bit, over two steps."""
+    from tabpack_b200 import ops
+
+    gen = torch.Generator(device='cuda').manual_seed(23)
+
+    def group(P, O, I, *, ragged, gated, copy, per_member, mutate):
+        outf = torch.randint(8, O + 1, (P,), generator=gen, device='cuda', dtype=torch.int32) if ragged else None
+        inf = torch.randint(8, I + 1, (P,), generator=gen, device='cuda', dtype=torch.int32) if ragged else None
+        p = torch.randn(P, O, I, device='cuda', generator=gen) * 0.05
+        g = torch.randn(P, O, I, device='cuda', generator=gen) * 1e-3
+        g[1] = 0.0  # all-zero update: skips the iterations
+        lr = torch.rand(P, device='cuda', generator=gen) * 0.02 + 1e-3 if per_member else 0.02
+        nb = torch.tensor([1, 3, 2] * P, dtype=torch.int32, device='cuda')[:P] if gated else None
+        return dict(p=p, grad=g, momentum_buffer=torch.zeros_like(p), out_features=outf, in_features=inf, lr=lr,
+                    momentum=0.95, weight_decay=1e-2, nesterov=True, mutate_grad=mutate, ns_steps=5,
+                    p_bf16=torch.zeros(P, O, I, dtype=torch.bfloat16, device='cuda') if copy else None,
+                    n_blocks=nb, block_index=1)
+
+    groups = [group(5, 300, 136, ragged=True, gated=False, copy=True, per_member=True, mutate=False),
+              group(7, 96, 520, ragged=True, gated=True, copy=False, per_member=False, mutate=True),
+              group(3, 128, 128, ragged=False, gated=False, copy=True, per_member=False, mutate=False)]
+    groups[1]['grad'][groups[1]['n_blocks'] <= 1] = 0.0  # gated members' gradients are exactly zero
+
+    def clone(gr):
+        return {k: (v.clone() if isinstance(v, torch.Tensor) and k in ('p', 'grad', 'momentum_buffer', 'p_bf16')
+                    else v) for k, v in gr.items()}
+
+    sep, grp = [clone(g) for g in groups], [clone(g) for g in groups]
+    for _ in range(2):
+        for gr in sep:
+            ops.muon_step(**gr)
+        ops.muon_step_grouped(grp)
+    torch.cuda.synchronize()
+    for i, (a, b) in enumerate(zip(sep, grp)):
+        for k in ('p', 'momentum_buffer', 'grad', 'p_bf16'):
+            if a[k] is None:
+                continue
+            assert torch.equal(a[k].view(torch.int16) if a[k].dtype == torch.bfloat16 else a[k].view(torch.int32),
+                               b[k].view(torch.int16) if b[k].dtype == torch.bfloat16 else b[k].view(torch.int32)), (i, k)
+        assert not torch.equal(a['p'], groups[i]['p'])
