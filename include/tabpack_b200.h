@@ -49,7 +49,10 @@ typedef struct tp_linear_args {
   const int32_t* in_features;  /* device (P,) real input widths, or NULL (= max_in) */
   const int32_t* out_features; /* device (P,) real output widths, or NULL (= max_out) */
   const int32_t* n_blocks;     /* device (P,) depths, or NULL: member m is active
-                                  iff n_blocks == NULL || n_blocks[m] > block_index */
+                                  iff n_blocks == NULL || n_blocks[m] > block_index; an
+                                  inactive member's y is its x over its out_features columns
+                                  (dx = dy over in_features in the backward) and zero beyond,
+                                  where its x (dy) holds zeros as a pack's activations do */
   int32_t block_index;
   int32_t relu;                /* 1: ReLU after the bias */
   const float* dropout_p;      /* device (P,) dropout probabilities, or NULL (eval) */

@@ -761,13 +761,24 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
           __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(pr.out) + (size_t)m * pr.out_ms;
           const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(pr.copy_src) + (size_t)m * pr.out_ms;
           const int nq = (c_end - cbase) / 8;  // 16-byte pieces per row (out_cols multiple of 8)
-          for (int i = lane; i < 32 * nq; i += 32) {
-            const int r = (nq == WCOLS / 8) ? i / (WCOLS / 8) : i / nq;
-            const int cc = cbase + 8 * (i - r * nq);
-            if (row_base + r >= pr.out_rows) continue;
-            const size_t off = (size_t)(row_base + r) * pr.out_ld + cc;
-            *reinterpret_cast<uint4*>(base + off) =
-                ti.kind == KIND_ZERO ? make_uint4(0, 0, 0, 0) : *reinterpret_cast<const uint4*>(src + off);
+          const int npieces = 32 * nq;
+          const bool copy = ti.kind == KIND_COPY;
+          // batches of 8 pieces per lane: every load of a batch is in flight before its stores
+          constexpr int UNR = 8;
+          for (int i0 = 0; i0 < npieces; i0 += 32 * UNR) {
+            uint4 v[UNR];
+            int off[UNR];  // element offsets within the member's block (-1: outside), below 2^31
+#pragma unroll
+            for (int u = 0; u < UNR; ++u) {
+              const int i = i0 + 32 * u + lane;
+              const int r = (nq == WCOLS / 8) ? i / (WCOLS / 8) : i / max(nq, 1);
+              const int cc = cbase + 8 * (i - r * nq);
+              off[u] = (i < npieces && row_base + r < pr.out_rows) ? (row_base + r) * pr.out_ld + cc : -1;
+              v[u] = (copy && off[u] >= 0) ? __ldg(reinterpret_cast<const uint4*>(src + off[u])) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < UNR; ++u)
+              if (off[u] >= 0) *reinterpret_cast<uint4*>(base + off[u]) = v[u];
           }
         }
       }

@@ -140,7 +140,11 @@ __device__ __forceinline__ TileInfo decode_tile(const LinearProblem& p, int t, i
   }
   ti.kblocks = (k_len + BK - 1) / BK;
   if (!active) {
-    ti.kind = (p.mode == MODE_WGRAD || p.mode == MODE_WGRAD_T) ? KIND_ZERO : KIND_COPY;
+    // a depth-gated member passes its input through (y = x, dx = dy) over its valid columns;
+    // the source's padding columns beyond them are zeros, so those tiles are ZERO tiles
+    // (nothing to read)
+    ti.kind = (p.mode == MODE_WGRAD || p.mode == MODE_WGRAD_T || ti.nt * p.BN >= ti.n_valid) ? KIND_ZERO
+                                                                                               : KIND_COPY;
   } else if (ti.mt * p.BM >= ti.m_valid || ti.nt * p.BN >= ti.n_valid || ti.kblocks == 0) {
     ti.kind = KIND_ZERO;
   } else {

@@ -339,6 +339,33 @@ def test_depth_gating_many_tiles_per_cta(dropout):
         torch.backends.cuda.matmul.allow_tf32 = tf32
 
 
+def test_depth_gating_with_widths_copies_only_valid_columns():
+    """Depth-gated members with their own widths (a hidden block: in = out = width): y = x and
+    dx = dy bit for bit, where x and dy hold zeros beyond the member's width as a pack's
+    activations do; the copy reads only the valid column tiles and writes zeros beyond."""
+    from tabpack_b200 import ops
+
+    P, B, W = 8, 300, 768
+    gen = torch.Generator(device='cuda').manual_seed(8)
+    widths = torch.tensor([64, 768, 200, 512, 256, 8, 520, 384], dtype=torch.int32, device='cuda')
+    nb = torch.tensor([1, 2, 1, 3, 1, 1, 2, 1], dtype=torch.int32, device='cuda')
+    cols = torch.arange(W, device='cuda')[None, None, :] < widths[:, None, None]
+    x = (torch.randn(P, B, W, device='cuda', generator=gen) * cols).bfloat16()
+    w = (torch.randn(P, W, W, device='cuda', generator=gen) * 0.03).bfloat16()
+    b = torch.randn(P, W, device='cuda', generator=gen) * 0.01
+    p = torch.full((P,), 0.2, device='cuda')
+    kw = dict(in_features=widths, out_features=widths, n_blocks=nb, block_index=1, relu=True, dropout_p=p,
+              seed=3, offset=1)
+    y = ops.linear_forward(x, w, b, **kw)
+    dy = (torch.randn(P, B, W, device='cuda', generator=gen) * cols).bfloat16()
+    dx, dW, db = ops.linear_backward(dy, x, w, y, **kw)
+    torch.cuda.synchronize()
+    gated = nb <= 1
+    assert torch.equal(y[gated], x[gated])
+    assert torch.equal(dx[gated], dy[gated])
+    assert int(torch.count_nonzero(y * ~cols)) == 0 and int(torch.count_nonzero(dx * ~cols)) == 0
+
+
 @pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
 def test_depth_gating(dtype):
     """Members with n_blocks <= block_index pass x through (forward) and dy through (dgrad)."""
