@@ -38,12 +38,13 @@ struct Sm100Cfg {
   // a CTA loads and its tensor core reads per MMA drop by a third.  The forward, whose
   // time goes to its bias / ReLU / dropout epilogue rather than to operand traffic, runs
   // on single CTAs (measured a few percent faster than on pairs).
-  static constexpr bool PAIR = (MODE == MODE_DGRAD || MODE == MODE_WGRAD_T || MODE == MODE_FWD_PAIR) && BN_ == 256;
+  static constexpr bool PAIR = (MODE == MODE_DGRAD || MODE == MODE_WGRAD_T || MODE == MODE_FWD_PAIR ||
+                                MODE == MODE_NS_P || MODE == MODE_NS_BMN_P) && BN_ == 256;
   static constexpr bool FWDK = (MODE == MODE_FWD || MODE == MODE_FWD_ADD || MODE == MODE_FWD_PAIR);  // forward epilogue
   static constexpr int TILE_M = PAIR ? 2 * BM : BM;
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // B columns staged per CTA
   static constexpr bool A_MN = is_wgrad_t(MODE);
-  static constexpr bool B_MN = (MODE == MODE_DGRAD || is_wgrad_t(MODE) || MODE == MODE_NS_BMN);
+  static constexpr bool B_MN = (MODE == MODE_DGRAD || is_wgrad_t(MODE) || MODE == MODE_NS_BMN || MODE == MODE_NS_BMN_P);
   static constexpr int STAGES = PAIR ? (FWDK ? 5 : 6) : (BN == 256) ? (FWDK ? 3 : 4) : 6;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = B_ROWS * BK * 2;
@@ -248,6 +249,14 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tr_empty + TRING);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* tile_ring = reinterpret_cast<volatile int*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + 256);
+  // a pair's claimed tile-list indices, handed from the leader's scheduler to the peer's: CRING
+  // slots after the tile ring, with a full barrier (arrived by the leader) and an empty barrier
+  // (arrived by the peer) per slot
+  constexpr int CRING = 4;
+  volatile int* claim_val = tile_ring + 8 * TRING;
+  uint64_t* claim_full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + 256 + 32 * TRING + 16);
+  uint64_t* claim_empty = claim_full + CRING;
+  static_assert(256 + 32 * TRING + 16 + 16 * CRING <= Cfg::CTRL_BYTES, "control block holds the claim ring");
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -291,6 +300,12 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
       mbar_init(&tempty[i], PAIR ? 2 * Cfg::EPI_WARPS : Cfg::EPI_WARPS);  // the leader's counts both CTAs
     }
     mbar_init(done_bar, 1);
+    if constexpr (PAIR) {
+      for (int i = 0; i < CRING; ++i) {
+        mbar_init(&claim_full[i], 1);
+        mbar_init(&claim_empty[i], 1);
+      }
+    }
     for (int i = 0; i < TRING; ++i) {
       mbar_init(&tr_full[i], 1);
       // consumers: the producer, the epilogue warps and the MMA thread (a pair's leader only)
@@ -507,7 +522,27 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
       int pub = 0;
       for (int k = 0;; ++k) {
         TileInfo ti;
-        if (pr.tile_list != nullptr) {
+        if (PAIR && pr.tile_list != nullptr) {
+          // a pair claims each tile once: the leader's scheduler claims it and hands the index
+          // to the peer's through the peer's shared memory; both decode and publish it
+          const int cs = k & (CRING - 1);
+          const uint32_t cph = (uint32_t)(k / CRING) & 1u;
+          int i;
+          if (rank == 0) {
+            i = (k == 0) ? (int)tile0 : tile_step + atomicAdd(pr.tile_counter, 1);
+            if (!mbar_wait<true>(&claim_empty[cs], cph ^ 1u, abort_flag)) break;
+            st_shared_cluster_u32(mapa_shared(smem_u32((const void*)(claim_val + cs)), 1), (uint32_t)i);
+            mbar_arrive_release_cluster(mapa_shared(smem_u32(&claim_full[cs]), 1));
+          } else {
+            if (!mbar_wait<true>(&claim_full[cs], cph, abort_flag)) break;
+            i = claim_val[cs];
+            mbar_arrive_release_cluster(mapa_shared(smem_u32(&claim_empty[cs]), 0));
+          }
+          if (i < n_list)
+            ti = decode_list_entry(pr, __ldg(pr.tile_list + i), Cfg::BK);
+          else
+            ti.kind = KIND_END;
+        } else if (pr.tile_list != nullptr) {
           const int i = (k == 0) ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(pr.tile_counter, 1);
           if (i < n_list)
             ti = decode_list_entry(pr, __ldg(pr.tile_list + i), Cfg::BK);
@@ -604,7 +639,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
         // Newton-Schulz: the addend of the first chunk is loaded before the accumulator wait
         [[maybe_unused]] uint4 d_a[4], d_b[4];
         [[maybe_unused]] const __nv_bfloat16* d_row = nullptr;
-        if constexpr (MODE == MODE_NS || MODE == MODE_NS_BMN) {
+        if constexpr (is_ns(MODE)) {
           if (pr.D != nullptr && row < ti.m_valid)
             d_row = reinterpret_cast<const __nv_bfloat16*>(pr.D) + (size_t)m * pr.out_ms + (size_t)row * pr.out_ld;
           ns_load_d(d_row, cbase, ti.n_valid - cbase, d_a);
@@ -622,7 +657,7 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
           stage_flush(pr, m, row_base, col0, stage_warp, lane, Cfg::STAGE_ROW_BYTES);
           __syncwarp();
         };
-        if constexpr (MODE == MODE_NS || MODE == MODE_NS_BMN) {
+        if constexpr (is_ns(MODE)) {
           // Chunks past the member's columns rounded up to a k-block (64) are never read: no
           // later GEMM's K loop reaches them, and as M / N rows they only feed outputs that are
           // written as zeros.  Two chunks' accumulators are loaded per TMEM wait; the addend of
@@ -631,7 +666,9 @@ __global__ void __launch_bounds__(Sm100Cfg<BN, MODE>::NUM_THREADS, 1)
           const int nch_k = min(nch, max(0, (((ti.n_valid + 63) & ~63) - cbase + 31) / 32));
           // symmetric product: this warp's half is also written transposed into a tile below
           // the diagonal (one that the tile list leaves out) when that tile lies entirely there
-          const bool mirror = pr.ns_sym && ((ti.mt >> 1) * 2 + 2 <= 2 * ti.nt + half);
+          // (a pair's 256 x 256 tile: every tile above the diagonal; the diagonal tiles compute
+          // both of their triangles)
+          const bool mirror = pr.ns_sym && (PAIR ? ti.mt < ti.nt : ((ti.mt >> 1) * 2 + 2 <= 2 * ti.nt + half));
           uint32_t na[32], nb[32];
 #pragma unroll 1
           for (int c = 0; c < nch_k; c += 2) {

@@ -28,6 +28,12 @@ enum : int { MODE_FWD_PAIR = 7 };
 // CTAs whose A operand (X^T) is gathered from a table by row index.
 enum : int { MODE_WGRAD_TG = 9 };
 __host__ __device__ constexpr bool is_wgrad_t(int mode) { return mode == MODE_WGRAD_T || mode == MODE_WGRAD_TG; }
+// Kernel instantiations of the Newton-Schulz GEMMs on CTA pairs (256-row tiles claimed from
+// 256-row tile lists; problems carry MODE_NS / MODE_NS_BMN).
+enum : int { MODE_NS_P = 10, MODE_NS_BMN_P = 11 };
+__host__ __device__ constexpr bool is_ns(int mode) {
+  return mode == MODE_NS || mode == MODE_NS_BMN || mode == MODE_NS_P || mode == MODE_NS_BMN_P;
+}
 // KIND_END marks the end of a CTA's tile sequence in the kernel's shared-memory tile ring.
 enum : int { KIND_MMA = 0, KIND_ZERO = 1, KIND_COPY = 2, KIND_SKIP = 3, KIND_END = 4 };
 

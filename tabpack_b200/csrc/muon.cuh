@@ -62,21 +62,27 @@ __global__ void muon_geometry_kernel(MuonArgs a) {
   a.trans[m] = o > n ? 1 : 0;
 }
 
-// Dense lists of the Newton-Schulz launches' MMA tiles (128 x 256 output tiles of the
-// tcgen05 kernel): list_rr for the r x r product B = b A + c A^2, list_rc for the r x c update
-// X <- a X + B X, and list_sym for the symmetric r x r product A = X X^T: only the tiles not
-// entirely below the diagonal (n-tile nt, m-tile mt with 256 nt + 256 > 128 mt); the epilogue
-// writes the others as transposes.  Entry = member << 16 | n-tile << 8 | m-tile; a member's
-// tiles go column block by column block, down the rows within one.  Members whose update is
-// zero (active == 0) have none.  One block of 1024 threads scans the members in chunks;
-// counts[0..2] receive the three lengths.
+// Dense lists of the Newton-Schulz launches' MMA tiles (BN = 256 columns by TM = 128 rows on
+// single CTAs, 256 rows on CTA pairs): rr for the r x r product B = b A + c A^2, rc for the
+// r x c update X <- a X + B X, and sym for the symmetric r x r product A = X X^T: only the tiles
+// not entirely below the diagonal (n-tile nt, m-tile mt with TM mt < 256 nt + 256); the epilogue
+// writes the others as transposes.  Entry = member << 16 | n-tile << 8 | m-tile (in TM rows); a
+// member's tiles go column block by column block, down the rows within one.  Members whose
+// update is zero (active == 0) have none.  One block of 1024 threads scans the members in
+// chunks; list j (j = 0..5: rr, rc, sym with TM = 128, then with TM = 256) gets counts[j].
 constexpr int NS_TILE_M = 128, NS_TILE_N = 256;
-constexpr int NS_LISTS = 3;
+constexpr int NS_LISTS = 6;
 
-__device__ __forceinline__ int ns_sym_mtiles(int nt, int mt_all) { return min(mt_all, 2 * nt + 2); }
+struct NsTileLists {
+  uint32_t* list[NS_LISTS];
+  int* counts;
+};
 
-__global__ void __launch_bounds__(1024) ns_tile_list_kernel(MuonArgs a, uint32_t* list_rr, uint32_t* list_rc,
-                                                            uint32_t* list_sym, int* counts) {
+__device__ __forceinline__ int ns_sym_mtiles(int nt, int mt_all, int tm) {
+  return min(mt_all, (nt + 1) * (NS_TILE_N / tm));
+}
+
+__global__ void __launch_bounds__(1024) ns_tile_list_kernel(MuonArgs a, NsTileLists L) {
   __shared__ int wsum[NS_LISTS][32];
   __shared__ int base[NS_LISTS];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -84,16 +90,24 @@ __global__ void __launch_bounds__(1024) ns_tile_list_kernel(MuonArgs a, uint32_t
   __syncthreads();
   for (int m0 = 0; m0 < a.P; m0 += 1024) {
     const int m = m0 + tid;
-    int mt = 0, nrr = 0, nrc = 0, nsym = 0;
+    int v[NS_LISTS] = {0, 0, 0, 0, 0, 0};
+    int mt[2] = {0, 0}, nrr = 0;
     if (m < a.P && a.active[m] != 0) {
       const int r = a.rows[m], c = a.cols[m];
-      mt = (r + NS_TILE_M - 1) / NS_TILE_M;
       nrr = (r + NS_TILE_N - 1) / NS_TILE_N;
-      nrc = (c + NS_TILE_N - 1) / NS_TILE_N;
-      for (int nt = 0; nt < nrr; ++nt) nsym += ns_sym_mtiles(nt, mt);
+      const int nrc = (c + NS_TILE_N - 1) / NS_TILE_N;
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        const int tm = NS_TILE_M << g;
+        mt[g] = (r + tm - 1) / tm;
+        v[3 * g] = mt[g] * nrr;
+        v[3 * g + 1] = mt[g] * nrc;
+        for (int nt = 0; nt < nrr; ++nt) v[3 * g + 2] += ns_sym_mtiles(nt, mt[g], tm);
+      }
     }
-    const int v[NS_LISTS] = {mt * nrr, mt * nrc, nsym};
-    int incl[NS_LISTS] = {v[0], v[1], v[2]};
+    int incl[NS_LISTS];
+#pragma unroll
+    for (int j = 0; j < NS_LISTS; ++j) incl[j] = v[j];
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
 #pragma unroll
@@ -124,15 +138,23 @@ __global__ void __launch_bounds__(1024) ns_tile_list_kernel(MuonArgs a, uint32_t
 #pragma unroll
     for (int j = 0; j < NS_LISTS; ++j) off[j] = base[j] + (wid > 0 ? wsum[j][wid - 1] : 0) + incl[j] - v[j];
     const uint32_t mk = (uint32_t)m << 16;
-    for (int i = 0; i < v[0]; ++i) list_rr[off[0] + i] = mk | ((uint32_t)(i / mt) << 8) | (uint32_t)(i % mt);
-    for (int i = 0; i < v[1]; ++i) list_rc[off[1] + i] = mk | ((uint32_t)(i / mt) << 8) | (uint32_t)(i % mt);
-    for (int nt = 0, o = off[2]; nt < nrr; ++nt)
-      for (int t = 0; t < ns_sym_mtiles(nt, mt); ++t) list_sym[o++] = mk | ((uint32_t)nt << 8) | (uint32_t)t;
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      const int tm = NS_TILE_M << g, mtg = max(mt[g], 1);
+      uint32_t* rr = L.list[3 * g];
+      uint32_t* rc = L.list[3 * g + 1];
+      uint32_t* sym = L.list[3 * g + 2];
+      for (int i = 0; i < v[3 * g]; ++i) rr[off[3 * g] + i] = mk | ((uint32_t)(i / mtg) << 8) | (uint32_t)(i % mtg);
+      for (int i = 0; i < v[3 * g + 1]; ++i)
+        rc[off[3 * g + 1] + i] = mk | ((uint32_t)(i / mtg) << 8) | (uint32_t)(i % mtg);
+      for (int nt = 0, o = off[3 * g + 2]; nt < nrr && v[3 * g + 2] > 0; ++nt)
+        for (int t = 0; t < ns_sym_mtiles(nt, mt[g], tm); ++t) sym[o++] = mk | ((uint32_t)nt << 8) | (uint32_t)t;
+    }
     __syncthreads();
     if (tid < NS_LISTS) base[tid] += wsum[tid][31];
     __syncthreads();
   }
-  if (tid < NS_LISTS) counts[tid] = base[tid];
+  if (tid < NS_LISTS) L.counts[tid] = base[tid];
 }
 
 // Tiles of the Muon elementwise kernels: 32 weight rows (o) x 128 weight columns (n), 256

@@ -7,6 +7,7 @@
 #include <type_traits>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstdarg>
 #include <cstdio>
 #include <atomic>
@@ -270,8 +271,8 @@ int launch_sm100(const LinearProblem& pr_in, const CUtensorMap& a, const CUtenso
   cfg.gridDim = dim3(Cfg::PAIR ? 2 * grid : grid);
   constexpr int kind = (MODE == MODE_DGRAD) ? TP_PROF_DGRAD
                        : (MODE == MODE_WGRAD || is_wgrad_t(MODE)) ? TP_PROF_WGRAD
-                       : (MODE == MODE_NS) ? TP_PROF_NS
-                       : (MODE == MODE_NS_BMN) ? TP_PROF_NS_BMN
+                       : (MODE == MODE_NS || MODE == MODE_NS_P) ? TP_PROF_NS
+                       : (MODE == MODE_NS_BMN || MODE == MODE_NS_BMN_P) ? TP_PROF_NS_BMN
                                                : TP_PROF_FWD;
   TP_PROF(kind, st);
   TP_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a, b, pr));
@@ -344,7 +345,7 @@ LinearProblem base_problem(const tp_linear_args* a) {
 struct MuonLayout {
   int R_s, C_s, tiles;
   size_t off_x0, off_x1, off_a, off_b, off_norm, off_rows, off_cols, off_trans, off_active, off_partial, off_counter,
-      off_list_rr, off_list_rc, off_list_sym, off_list_n, total;
+      off_list[NS_LISTS], off_list_n, total;
 };
 
 constexpr int MUON_COUNTERS = 64;
@@ -370,10 +371,14 @@ MuonLayout muon_layout_rc(int P, int R_s, int C_s, size_t partials) {
   L.off_partial = take(partials * 4);
   L.off_counter = take(MUON_COUNTERS * 4);  // tile counters of the Newton-Schulz launches
   // dense tile lists of the Newton-Schulz launches (r x r and r x c outputs) and their lengths
-  const size_t mtl = (size_t)L.R_s / NS_TILE_M;
-  L.off_list_rr = take((size_t)P * mtl * ((L.R_s + NS_TILE_N - 1) / NS_TILE_N) * 4);
-  L.off_list_rc = take((size_t)P * mtl * ((L.C_s + NS_TILE_N - 1) / NS_TILE_N) * 4);
-  L.off_list_sym = take((size_t)P * mtl * ((L.R_s + NS_TILE_N - 1) / NS_TILE_N) * 4);
+  // (rr, rc, sym with 128-row tiles, then with 256-row tiles for CTA pairs)
+  for (int g = 0; g < 2; ++g) {
+    const size_t tm = (size_t)NS_TILE_M << g;
+    const size_t mtl = ((size_t)L.R_s + tm - 1) / tm;
+    L.off_list[3 * g] = take((size_t)P * mtl * ((L.R_s + NS_TILE_N - 1) / NS_TILE_N) * 4);
+    L.off_list[3 * g + 1] = take((size_t)P * mtl * ((L.C_s + NS_TILE_N - 1) / NS_TILE_N) * 4);
+    L.off_list[3 * g + 2] = take((size_t)P * mtl * ((L.R_s + NS_TILE_N - 1) / NS_TILE_N) * 4);
+  }
   L.off_list_n = take(NS_LISTS * 4);
   L.total = o;
   return L;
@@ -400,13 +405,14 @@ int ns_gemm(const MuonArgs& ma, int shape, const void* a_op, int a_cols, const v
             void* out, int out_cols, const void* d, float alpha, float beta, const uint32_t* list,
             const int* list_n, int* counter, cudaStream_t st, int sym = 0) {
   constexpr int BN = 256;
-  static_assert(BN == NS_TILE_N && Sm100Cfg<BN, MODE>::TILE_M == NS_TILE_M, "tile lists match the kernel's tiles");
+  static_assert(BN == NS_TILE_N && (Sm100Cfg<BN, MODE>::TILE_M == NS_TILE_M || Sm100Cfg<BN, MODE>::TILE_M == 2 * NS_TILE_M),
+                "tile lists match the kernel's tiles");
   LinearProblem pr{};
   pr.tile_list = list;  // the launch's MMA tiles, claimed dynamically (ragged members)
   pr.tile_count = list_n;
   pr.ns_sym = sym;
   pr.tile_counter = counter;  // zeroed
-  pr.mode = MODE;
+  pr.mode = (MODE == MODE_NS_P) ? MODE_NS : (MODE == MODE_NS_BMN_P) ? MODE_NS_BMN : MODE;
   pr.P = ma.P;
   pr.ns_rows = ma.rows;
   pr.ns_cols = ma.cols;
@@ -428,7 +434,7 @@ int ns_gemm(const MuonArgs& ma, int shape, const void* a_op, int a_cols, const v
   CUtensorMap mapA, mapB;
   int rc;
   if ((rc = make_map(&mapA, a_op, a_cols, ma.R_s, ma.P, 64, Cfg::BM))) return rc;
-  if (MODE == MODE_NS) {
+  if (!Cfg::B_MN) {
     if ((rc = make_map(&mapB, b_op, b_cols, ma.R_s, ma.P, 64, Cfg::B_ROWS))) return rc;
   } else {
     if ((rc = make_map(&mapB, b_op, b_cols, ma.R_s, ma.P, 64, 64))) return rc;
@@ -871,18 +877,31 @@ void muon_finish(MuonArgs m, __nv_bfloat16* x, cudaStream_t st) {
 
 // ns_steps quintic Newton-Schulz iterations over every member of the workspace (mu: the
 // workspace-wide view: P, rows, cols, active, R_s); *result receives the final operand.
+// Bit mask of the Newton-Schulz products that run on CTA pairs (bit 0: A = X X^T, bit 1:
+// B = b A + c A^2, bit 2: X <- a X + B X); the environment variable TP_NS_PAIRS (read once)
+// overrides the default.  Both kernels compute every tile the same way, so the choice does not
+// change the results.
+int ns_pair_products() {
+  static const int mask = [] {
+    const char* e = std::getenv("TP_NS_PAIRS");
+    if (e == nullptr || *e == 0) return 7;
+    return (int)(std::strtol(e, nullptr, 0) & 7);
+  }();
+  return mask;
+}
+
 int muon_newton_schulz(const MuonArgs& mu, const MuonLayout& L, uint8_t* ws, int ns_steps, cudaStream_t st,
                        void** result) {
   if (L.R_s / NS_TILE_M > 255 || (L.C_s + NS_TILE_N - 1) / NS_TILE_N > 255)
     return fail(TP_EINVAL, "Muon matrices of at most 32640 x 65280 elements (operand strides %d x %d)", L.R_s,
                 L.C_s);
-  uint32_t* list_rr = reinterpret_cast<uint32_t*>(ws + L.off_list_rr);
-  uint32_t* list_rc = reinterpret_cast<uint32_t*>(ws + L.off_list_rc);
-  uint32_t* list_sym = reinterpret_cast<uint32_t*>(ws + L.off_list_sym);
-  int* list_n = reinterpret_cast<int*>(ws + L.off_list_n);
+  NsTileLists lists{};
+  for (int j = 0; j < NS_LISTS; ++j) lists.list[j] = reinterpret_cast<uint32_t*>(ws + L.off_list[j]);
+  lists.counts = reinterpret_cast<int*>(ws + L.off_list_n);
+  const int* list_n = lists.counts;
   {
     TP_PROF(TP_PROF_MUON_ELEMENTWISE, st);
-    ns_tile_list_kernel<<<1, 1024, 0, st>>>(mu, list_rr, list_rc, list_sym, list_n);
+    ns_tile_list_kernel<<<1, 1024, 0, st>>>(mu, lists);
   }
   TP_CUDA_TRY(cudaGetLastError());
   // quintic Newton-Schulz, coefficients of optim.py:477
@@ -901,21 +920,31 @@ int muon_newton_schulz(const MuonArgs& mu, const MuonLayout& L, uint8_t* ws, int
       return nullptr;
     return counters + (launch++ % MUON_COUNTERS);
   };
+  // which of the three products run on CTA pairs (256-row tiles)
+  const int pairs = ns_pair_products();
+  const int sym_l = (pairs & 1) ? 5 : 2, b_l = (pairs & 2) ? 5 : 2, x_l = (pairs & 4) ? 4 : 1;
   for (int it = 0; it < ns_steps; ++it) {
     int* c1 = counter();
     int* c2 = counter();
     int* c3 = counter();
     if (!c1 || !c2 || !c3) return fail(TP_ECUDA, "cudaMemsetAsync of the tile counters failed");
     // A = X X^T is symmetric: only the tiles not below the diagonal, the rest written as transposes
-    if ((rc = ns_gemm<MODE_NS>(mu, 1, X, L.C_s, X, L.C_s, A, L.R_s, nullptr, 1.0f, 0.0f, list_sym, list_n + 2, c1,
-                               st, 1)))
-      return rc;
+    rc = (pairs & 1) ? ns_gemm<MODE_NS_P>(mu, 1, X, L.C_s, X, L.C_s, A, L.R_s, nullptr, 1.0f, 0.0f, lists.list[sym_l],
+                                          list_n + sym_l, c1, st, 1)
+                     : ns_gemm<MODE_NS>(mu, 1, X, L.C_s, X, L.C_s, A, L.R_s, nullptr, 1.0f, 0.0f, lists.list[sym_l],
+                                        list_n + sym_l, c1, st, 1);
+    if (rc) return rc;
     // B = b A + c A^2 is symmetric as well
-    if ((rc = ns_gemm<MODE_NS>(mu, 2, A, L.R_s, A, L.R_s, Bm, L.R_s, A, cc, cb, list_sym, list_n + 2, c2, st, 1)))
-      return rc;
-    if ((rc = ns_gemm<MODE_NS_BMN>(mu, 3, Bm, L.R_s, X, L.C_s, Xn, L.C_s, X, 1.0f, ca, list_rc, list_n + 1, c3,
-                                   st)))
-      return rc;
+    rc = (pairs & 2) ? ns_gemm<MODE_NS_P>(mu, 2, A, L.R_s, A, L.R_s, Bm, L.R_s, A, cc, cb, lists.list[b_l],
+                                          list_n + b_l, c2, st, 1)
+                     : ns_gemm<MODE_NS>(mu, 2, A, L.R_s, A, L.R_s, Bm, L.R_s, A, cc, cb, lists.list[b_l], list_n + b_l,
+                                        c2, st, 1);
+    if (rc) return rc;
+    rc = (pairs & 4) ? ns_gemm<MODE_NS_BMN_P>(mu, 3, Bm, L.R_s, X, L.C_s, Xn, L.C_s, X, 1.0f, ca, lists.list[x_l],
+                                              list_n + x_l, c3, st)
+                     : ns_gemm<MODE_NS_BMN>(mu, 3, Bm, L.R_s, X, L.C_s, Xn, L.C_s, X, 1.0f, ca, lists.list[x_l],
+                                            list_n + x_l, c3, st);
+    if (rc) return rc;
     std::swap(X, Xn);
   }
   *result = X;

@@ -436,13 +436,36 @@ def _weight_gradient_buffer(slot: dict, shape: tuple, device, key) -> Tensor:
     return t
 
 
+def _activation_buffer(slot: dict, shape: tuple, dtype: torch.dtype, device, key) -> Tensor | None:
+    """The output buffer of a layer whose activations the trainer owns: the previous call's
+    storage again once nothing else holds it (a finished step's autograd graph has released
+    it), else a zeroed new one.  Its padding columns stay zero (the kernels then write only
+    the members' column tiles, `y_pad_zero`); `key` (widths and depths) must match the
+    previous call's.  None (no reuse) where storage use counts are not available."""
+    use_count = getattr(torch._C, '_storage_Use_Count', None)
+    if use_count is None:
+        return None
+    st = slot.get('storage')
+    if (st is not None and slot.get('shape') == shape and slot.get('dtype') == dtype and slot.get('key') == key
+            and st.device == device and use_count(st._cdata) == 1):
+        return torch.empty(0, dtype=dtype, device=device).set_(st, 0, shape)
+    t = torch.zeros(shape, dtype=dtype, device=device)
+    slot.update(storage=t.untyped_storage(), shape=shape, dtype=dtype, key=key)
+    return t
+
+
 class _PackedLinearFn(torch.autograd.Function):
     """One fused launch forward, three in backward (activation grad + bias grad,
     dgrad, wgrad); `cfg` carries the non-tensor configuration."""
 
     @staticmethod
     def forward(ctx, x, weight, bias, w_compute, b_compute, cfg):
-        y = ops.linear_forward(x, w_compute, b_compute, **cfg['kw'])
+        y_buf = None
+        if cfg.get('y_slot') is not None:
+            rows = cfg['kw']['row_index'].shape[1] if 'row_index' in cfg['kw'] else x.shape[-2]
+            y_buf = _activation_buffer(cfg['y_slot'], (w_compute.shape[0], rows, w_compute.shape[1]), x.dtype,
+                                       x.device, cfg['y_key'])
+        y = ops.linear_forward(x, w_compute, b_compute, **cfg['kw'], y=y_buf)
         ctx.cfg = cfg
         ctx.x_shape = x.shape
         ctx.save_for_backward(x, w_compute, y if (cfg['kw']['relu'] or cfg['kw']['dropout_p'] is not None) else None)
@@ -475,11 +498,14 @@ class _PackedLinearFn(torch.autograd.Function):
 def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features=None, out_features=None,
                   n_blocks=None, block_index=0, relu=False, dropout_p=None, seed=0, offset=0,
                   member_base=0, cache: _WeightCache | None = None, dx_cols: int = 0,
-                  row_index: Tensor | None = None, dw_slot: dict | None = None) -> Tensor:
+                  row_index: Tensor | None = None, dw_slot: dict | None = None,
+                  y_slot: dict | None = None) -> Tensor:
     """Functional form of the fused packed linear layer (see module docstring).  `dx_cols` > 0:
     the input's gradient is needed in its first dx_cols columns only (zeros beyond).
     `row_index` (pack_size, batch): `x` is a (rows, in) table and member m's input row b is
-    x[row_index[m, b]], gathered by the GEMMs' operand loads (the table takes no gradient)."""
+    x[row_index[m, b]], gathered by the GEMMs' operand loads (the table takes no gradient).
+    `dw_slot` / `y_slot`: storage that the weight gradient / the output reuse from the
+    previous call (a trainer that owns them; the output only while autograd records)."""
     if not x.is_cuda:
         raise RuntimeError('tabpack_b200 packs run on CUDA devices only')
     dtype = _compute_dtype(x)
@@ -512,6 +538,10 @@ def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features
         tag = lambda t: None if t is None else (t.data_ptr(), t._version, tuple(t.shape))  # noqa: E731
         cfg['dw_slot'] = dw_slot
         cfg['dw_key'] = (tag(out_features), tag(in_features), tag(n_blocks), int(block_index))
+    if y_slot is not None and dtype == torch.bfloat16 and rows == max_out and torch.is_grad_enabled():
+        tag = lambda t: None if t is None else (t.data_ptr(), t._version, tuple(t.shape))  # noqa: E731
+        cfg['y_slot'] = y_slot
+        cfg['y_key'] = (tag(out_features), tag(in_features), tag(n_blocks), int(block_index))
     with torch.autocast(x.device.type, enabled=False):
         y = _PackedLinearFn.apply(xc, weight, bias, wc, bc, cfg)
     return y if rows == max_out else y[..., :max_out]
@@ -610,6 +640,10 @@ class LinearPack(ModulePack):
     # depth-inactive members' blocks are still zero there, so only the active blocks are
     # written.  Code that modifies a weight gradient's padding in place must leave it off.
     reuse_weight_gradient = False
+    # When set (a trainer whose layer outputs feed only the next layer), a training-mode
+    # forward writes its output into the previous step's storage once autograd has released it;
+    # the padding columns stay zero there, so only the members' column tiles are written.
+    reuse_activation_buffer = False
 
     def __init__(self, in_features, out_features, bias: bool = True, *, max_in_features=None,
                  max_out_features=None, pack_size: int, dtype=None, device=None) -> None:
@@ -626,6 +660,7 @@ class LinearPack(ModulePack):
         self._cache = _WeightCache()
         _register_bf16_cache(self.weight, self._cache)
         self._dw_slot = {}
+        self._y_slot = {}
         self.reset_parameters()
 
     @property
@@ -724,7 +759,8 @@ def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stre
                          block_index=block_index, relu=relu, dropout_p=dropout, seed=seed, offset=offset,
                          member_base=member_base, cache=linear._cache if pack_idx is None else None,
                          dx_cols=dx_cols, row_index=row_index,
-                         dw_slot=linear._dw_slot if (pack_idx is None and linear.reuse_weight_gradient) else None)
+                         dw_slot=linear._dw_slot if (pack_idx is None and linear.reuse_weight_gradient) else None,
+                         y_slot=linear._y_slot if (pack_idx is None and linear.reuse_activation_buffer) else None)
 
 
 class DropoutPack(ModulePack):

@@ -131,10 +131,13 @@ def linear_forward(
     offset: int = 0,
     member_base: int = 0,
     row_index: Tensor | None = None,
+    y: Tensor | None = None,
 ) -> Tensor:
     """Packed linear (+ReLU +dropout +depth gating) forward; see `tp_linear_forward`.  With
     `row_index` (P, B), x is a (rows, in) table and member m's input row b is
-    x[row_index[m, b]] (gathered by the GEMM's operand loads)."""
+    x[row_index[m, b]] (gathered by the GEMM's operand loads).  `y`: an output buffer whose
+    padding columns already hold zeros (`y_pad_zero`: only the members' column tiles are
+    written); by default a new one."""
     weight = _cuda('weight', weight)
     x = _cuda('x', x, weight.dtype)
     row_index = _row_index(row_index, weight.shape[0])
@@ -144,10 +147,17 @@ def linear_forward(
         ('in_features', in_features), ('out_features', out_features), ('n_blocks', n_blocks)))
     P, max_out, _ = weight.shape
     B = x.shape[-2] if row_index is None else row_index.shape[1]
-    y = torch.empty((P, B, max_out), dtype=x.dtype, device=x.device)
+    pad_zero = y is not None
+    if y is None:
+        y = torch.empty((P, B, max_out), dtype=x.dtype, device=x.device)
+    elif tuple(y.shape) != (P, B, max_out) or y.dtype != x.dtype or not y.is_contiguous() or y.device != x.device:
+        raise ValueError(f'y must be a contiguous ({P}, {B}, {max_out}) {x.dtype} tensor on {x.device}')
     a = _linear_args(x, weight, bias, in_features, out_features, n_blocks, block_index, relu,
                      dropout_p, seed, offset, member_base, y, row_index)
+    a.y_pad_zero = 1 if pad_zero else 0
     check(load().tp_linear_forward(ctypes.byref(a), _stream()), 'tp_linear_forward')
+    if pad_zero:
+        increment_version([y])
     return y
 
 

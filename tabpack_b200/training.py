@@ -288,6 +288,10 @@ class PackTrainer:
         for mod in self.model.modules():
             if isinstance(mod, LinearPack):
                 mod.reuse_weight_gradient = True
+        # the backbone blocks' outputs feed only the next block (and the head): a training step
+        # writes them into the previous step's storage, whose padding is still zero
+        for blk in self.model.backbone.blocks:
+            blk.linear.reuse_activation_buffer = True
         self.model.backbone.set_member_base(lo)
         self.model.backbone._stream.seed = _mix(self.seed, 0xD0)  # one Philox key on every rank
         self._init_device = 'cpu' if init_on_host else None
