@@ -100,6 +100,10 @@ typedef struct tp_linear_grad_args {
                           (a buffer that an earlier call with the same widths and depths wrote):
                           the weight gradient writes the active members' blocks only (output
                           features rounded up to a multiple of 32).  0: it writes every element. */
+  int32_t dx_pad_zero; /* 1: dx already holds zeros beyond each member's input columns rounded
+                          up to the GEMM's 256-column tiles (a buffer that an earlier call with
+                          the same widths and depths wrote): the input gradient writes only the
+                          column tiles that hold a member's columns.  0: every element. */
 } tp_linear_grad_args;
 
 /* LinearPack.forward (src/tabpackage/nn.py:792-816) fused with the ReLU and
@@ -257,6 +261,11 @@ typedef struct tp_muon_args {
    * NULL: every member is stepped from its gradient. */
   const int32_t* n_blocks;
   int32_t block_index;
+  /* 1: the momentum of every depth-gated member is zero (a caller that zeroes a member's state
+   * whenever its depth changes): such a member's update is zero, so its gradient, momentum and
+   * Newton-Schulz operand are neither read nor written, and only its weight decay is applied.
+   * 0: a gated member's momentum is read (it decays and, where nonzero, updates the weights). */
+  int32_t gated_momentum_zero;
 } tp_muon_args;
 
 size_t tp_muon_workspace_size(int32_t P, int32_t max_out, int32_t max_in);

@@ -42,6 +42,7 @@ class LinearGradArgs(ctypes.Structure):
         ('dbias', ctypes.c_void_p), ('dx', ctypes.c_void_p), ('dw', ctypes.c_void_p),
         ('dw_rows', ctypes.c_int32), ('dw_cols', ctypes.c_int32), ('db_cols', ctypes.c_int32),
         ('g_ready', ctypes.c_int32), ('dx_cols', ctypes.c_int32), ('dw_pad_zero', ctypes.c_int32),
+        ('dx_pad_zero', ctypes.c_int32),
     ]
 
 
@@ -74,7 +75,7 @@ class MuonArgs(ctypes.Structure):
         ('update_scale', ctypes.c_void_p), ('nesterov', ctypes.c_int32), ('mutate_grad', ctypes.c_int32),
         ('ns_steps', ctypes.c_int32), ('workspace', ctypes.c_void_p), ('workspace_bytes', ctypes.c_size_t),
         ('p_bf16', ctypes.c_void_p), ('p_bf16_rows', ctypes.c_int32), ('p_bf16_cols', ctypes.c_int32),
-        ('n_blocks', ctypes.c_void_p), ('block_index', ctypes.c_int32),
+        ('n_blocks', ctypes.c_void_p), ('block_index', ctypes.c_int32), ('gated_momentum_zero', ctypes.c_int32),
     ]
 
 

@@ -46,6 +46,7 @@ struct MuonArgs {
   int bf16_rows, bf16_cols;
   const int32_t* n_blocks;  // (P,) depths, or nullptr: members with n_blocks <= block_index have
   int block_index;          //   an exactly zero gradient (depth-gated)
+  int gated_zero;           // 1: depth-gated members' momentum is zero as well (their update is zero)
 };
 
 __device__ __forceinline__ bool muon_gated(const MuonArgs& a, int mem) {
@@ -228,6 +229,12 @@ __global__ void __launch_bounds__(256) muon_prologue_kernel(MuonArgs a) {
   // a depth-gated member's gradient is exactly zero: it is not read, and its momentum is
   // written back only where it changes (nowhere once it is zero)
   const bool gated = muon_gated(a, mem);
+  if (gated && a.gated_zero) {
+    // its momentum is zero too, so its update is: nothing to read or write but this tile's
+    // (zero) norm partial; the member stays inactive and its operand is never read
+    if (threadIdx.x == 0) a.partial[(size_t)mem * a.tiles + blockIdx.y * gridDim.x + blockIdx.x] = 0.0f;
+    return;
+  }
   float gv[4][4], mv[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)

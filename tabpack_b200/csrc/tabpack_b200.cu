@@ -674,6 +674,7 @@ int linear_backward_impl(const tp_linear_grad_args* ga, int dw_ld_in, void* stre
     // tensor cores: the members' input width (tiles past it are zero tiles)
     if (dx_part && tc) pr.max_in = ga->dx_cols;
     pr.mode = MODE_DGRAD;
+    pr.skip_zero = ga->dx_pad_zero != 0;
     pr.out = ga->dx;
     pr.out_rows = a->B;
     pr.out_cols = a->max_in;
@@ -834,6 +835,7 @@ int muon_group_args(const tp_muon_args* a, MuonArgs* out) {
   m.p_bf16 = static_cast<__nv_bfloat16*>(a->p_bf16);
   m.n_blocks = a->n_blocks;
   m.block_index = a->block_index;
+  m.gated_zero = a->n_blocks != nullptr && a->gated_momentum_zero != 0;
   m.bf16_rows = a->p_bf16_rows;
   m.bf16_cols = a->p_bf16_cols;
   *out = m;

@@ -480,11 +480,14 @@ class _PackedLinearFn(torch.autograd.Function):
         dw_out = None
         if slot is not None and need_dw:
             dw_out = _weight_gradient_buffer(slot, tuple(cfg['w_shape']), dy.device, cfg['dw_key'])
+        dx_out = None
+        if cfg.get('dx_slot') is not None and need_dx and len(ctx.x_shape) == 3 and x.shape == ctx.x_shape:
+            dx_out = _activation_buffer(cfg['dx_slot'], tuple(x.shape), w_compute.dtype, dy.device, cfg['x_key'])
         dx, dw, db = ops.linear_backward(
             dy.contiguous().to(w_compute.dtype), x, w_compute, y, **cfg['kw'],
             need_dx=need_dx, need_dw=need_dw, need_db=need_db,
             dw_shape=cfg['w_shape'][1:], db_cols=cfg['w_shape'][1], dx_cols=cfg.get('dx_cols', 0),
-            dw_out=dw_out, dw_pad_zero=dw_out is not None)
+            dw_out=dw_out, dw_pad_zero=dw_out is not None, dx_out=dx_out)
         if dw_out is not None:
             slot['ref'] = weakref.ref(dw)  # reusable once the optimizer has dropped this gradient
         if dx is not None:
@@ -538,10 +541,13 @@ def packed_linear(x: Tensor, weight: Tensor, bias: Tensor | None, *, in_features
         tag = lambda t: None if t is None else (t.data_ptr(), t._version, tuple(t.shape))  # noqa: E731
         cfg['dw_slot'] = dw_slot
         cfg['dw_key'] = (tag(out_features), tag(in_features), tag(n_blocks), int(block_index))
-    if y_slot is not None and dtype == torch.bfloat16 and rows == max_out and torch.is_grad_enabled():
+    if y_slot is not None and dtype == torch.bfloat16 and torch.is_grad_enabled():
         tag = lambda t: None if t is None else (t.data_ptr(), t._version, tuple(t.shape))  # noqa: E731
-        cfg['y_slot'] = y_slot
-        cfg['y_key'] = (tag(out_features), tag(in_features), tag(n_blocks), int(block_index))
+        key = (tag(out_features), tag(in_features), tag(n_blocks), int(block_index))
+        if rows == max_out:
+            cfg['y_slot'], cfg['y_key'] = y_slot.setdefault('y', {}), key
+        if x.ndim == 3 and cols == in_cols and row_index is None and not dx_cols:
+            cfg['dx_slot'], cfg['x_key'] = y_slot.setdefault('dx', {}), key
     with torch.autocast(x.device.type, enabled=False):
         y = _PackedLinearFn.apply(xc, weight, bias, wc, bc, cfg)
     return y if rows == max_out else y[..., :max_out]

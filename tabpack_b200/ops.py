@@ -185,11 +185,14 @@ def linear_backward(
     row_index: Tensor | None = None,
     dw_out: Tensor | None = None,
     dw_pad_zero: bool = False,
+    dx_out: Tensor | None = None,
 ) -> tuple[Tensor | None, Tensor | None, Tensor | None]:
     """Backward of `linear_forward`: returns (dx, dw, db); dw/db are fp32.  With dx_cols > 0
     only dx's first dx_cols columns are computed (the rest are zeros).  With `row_index`, x is
     the forward's table (no dx).  `dw_out`: the weight gradient's buffer (else a new one);
-    `dw_pad_zero`: it already holds zeros outside the active members' blocks (`tp_linear_grad_args`)."""
+    `dw_pad_zero`: it already holds zeros outside the active members' blocks (`tp_linear_grad_args`).
+    `dx_out`: the input gradient's buffer, whose columns beyond each member's input column tiles
+    already hold zeros (`dx_pad_zero`); by default a new one."""
     weight = _cuda('weight', weight)
     x = _cuda('x', x, weight.dtype)
     row_index = _row_index(row_index, weight.shape[0])
@@ -204,7 +207,15 @@ def linear_backward(
     B = x.shape[-2] if row_index is None else row_index.shape[1]
     need_g = relu or dropout_p is not None or out_features is not None or n_blocks is not None
     g = torch.empty_like(dy) if need_g else None
-    dx = torch.empty((P, B, max_in), dtype=dy.dtype, device=dy.device) if need_dx else None
+    dx = None
+    if need_dx:
+        if dx_out is not None:
+            if (tuple(dx_out.shape) != (P, B, max_in) or dx_out.dtype != dy.dtype or not dx_out.is_contiguous()
+                    or dx_out.device != dy.device):
+                raise ValueError(f'dx_out must be a contiguous ({P}, {B}, {max_in}) {dy.dtype} tensor on {dy.device}')
+            dx = dx_out
+        else:
+            dx = torch.empty((P, B, max_in), dtype=dy.dtype, device=dy.device)
     rows, cols = dw_shape if dw_shape is not None else (max_out, max_in)
     dw = None
     if need_dw:
@@ -225,7 +236,10 @@ def linear_backward(
     ga.dw_rows, ga.dw_cols, ga.db_cols = rows, cols, dbc
     ga.dx_cols = int(dx_cols)
     ga.dw_pad_zero = 1 if (dw_pad_zero and dw_out is not None) else 0
+    ga.dx_pad_zero = 1 if (dx is not None and dx_out is not None) else 0
     check(load().tp_linear_backward(ctypes.byref(ga), _stream()), 'tp_linear_backward')
+    if ga.dx_pad_zero:
+        increment_version([dx])
     return dx, dw, db
 
 
@@ -296,7 +310,7 @@ def muon_workspace_size(P: int, max_out: int, max_in: int) -> int:
 def _muon_args(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=None, in_features=None, lr,
                momentum, weight_decay, update_scale=None, nesterov: bool = True, mutate_grad: bool = True,
                ns_steps: int = 5, p_bf16: Tensor | None = None, n_blocks: Tensor | None = None,
-               block_index: int = 0):
+               block_index: int = 0, gated_momentum_zero: bool = False):
     """`tp_muon_args` of one group (workspace unset), the tensors that must stay alive until
     the launch is queued, and the tensors the step writes."""
     for name, t in (('p', p), ('grad', grad), ('momentum_buffer', momentum_buffer)):
@@ -322,6 +336,7 @@ def _muon_args(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features
         if nb.shape != (P,):
             raise ValueError(f'n_blocks must be ({P},), got {tuple(nb.shape)}')
         a.n_blocks, a.block_index = nb.data_ptr(), int(block_index)
+        a.gated_momentum_zero = 1 if gated_momentum_zero else 0
     keep = (of, inf, us, nb, lr, momentum, weight_decay)
     written = [p, momentum_buffer] + ([grad] if mutate_grad else []) + ([p_bf16] if p_bf16 is not None else [])
     return a, keep, written
@@ -330,16 +345,18 @@ def _muon_args(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features
 def muon_step(p: Tensor, grad: Tensor, momentum_buffer: Tensor, *, out_features=None, in_features=None, lr,
               momentum, weight_decay, update_scale=None, nesterov: bool = True, mutate_grad: bool = True,
               ns_steps: int = 5, workspace: Tensor | None = None, p_bf16: Tensor | None = None,
-              n_blocks: Tensor | None = None, block_index: int = 0) -> None:
+              n_blocks: Tensor | None = None, block_index: int = 0, gated_momentum_zero: bool = False) -> None:
     """One Muon group step on a packed (P, max_out, max_in) fp32 weight; see `tp_muon_step`.
     `p_bf16` (P, rows >= max_out, cols >= max_in) bf16, optional, receives bf16 of the updated
     weights of each member's out x in block in the same pass.  `n_blocks` / `block_index`: the
     weight's block is depth-gated for members with n_blocks <= block_index (their gradient is
-    exactly zero and is not read)."""
+    exactly zero and is not read); `gated_momentum_zero`: their momentum is zero as well (not
+    read either)."""
     a, keep, written = _muon_args(p, grad, momentum_buffer, out_features=out_features, in_features=in_features,
                                   lr=lr, momentum=momentum, weight_decay=weight_decay, update_scale=update_scale,
                                   nesterov=nesterov, mutate_grad=mutate_grad, ns_steps=ns_steps, p_bf16=p_bf16,
-                                  n_blocks=n_blocks, block_index=block_index)
+                                  n_blocks=n_blocks, block_index=block_index,
+                                  gated_momentum_zero=gated_momentum_zero)
     P, mo, mi = p.shape
     need = muon_workspace_size(P, mo, mi)
     if workspace is None or workspace.numel() * workspace.element_size() < need:

@@ -328,7 +328,8 @@ def _muon_kwargs(opt: torch.optim.Optimizer, g: dict, *, allow_inplace_grad_muta
               update_scale=None if scale is None else scale.to(torch.float32).contiguous(),
               nesterov=bool(g['muon_nesterov']), mutate_grad=allow_inplace_grad_mutation,
               ns_steps=int(g['muon_newton_schulz_steps']), p_bf16=copy, n_blocks=g.get('muon_n_blocks'),
-              block_index=int(g.get('muon_block_index', 0)))
+              block_index=int(g.get('muon_block_index', 0)),
+              gated_momentum_zero=bool(g.get('muon_gated_momentum_zero', False)))
     return kw, (cache, copy)
 
 

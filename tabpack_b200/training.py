@@ -288,10 +288,12 @@ class PackTrainer:
         for mod in self.model.modules():
             if isinstance(mod, LinearPack):
                 mod.reuse_weight_gradient = True
-        # the backbone blocks' outputs feed only the next block (and the head): a training step
-        # writes them into the previous step's storage, whose padding is still zero
+        # the backbone blocks' outputs feed only the next block (and the head), and their input
+        # gradients only the previous block: a training step writes both into the previous
+        # step's storage, whose padding is still zero
         for blk in self.model.backbone.blocks:
             blk.linear.reuse_activation_buffer = True
+        self.model.output.reuse_activation_buffer = True
         self.model.backbone.set_member_base(lo)
         self.model.backbone._stream.seed = _mix(self.seed, 0xD0)  # one Philox key on every rank
         self._init_device = 'cpu' if init_on_host else None
@@ -308,6 +310,9 @@ class PackTrainer:
             for i, gr in enumerate(groups):
                 if i > 0:
                     gr['muon_n_blocks'], gr['muon_block_index'] = self.model.backbone.n_blocks, i
+                    # a gated member's momentum is zero as well: its gradient has always been
+                    # zero, and `replace` zeroes the state of a member whose depth changes
+                    gr['muon_gated_momentum_zero'] = True
             muon_params = {id(g['params'][0]) for g in groups}
             decay, no_decay = split_weight_decay(self.model)
             groups.append({'params': [p for p in no_decay if id(p) not in muon_params], 'weight_decay': 0.0})

@@ -316,8 +316,8 @@ def test_pack_idx_forward_selects_members():
 
 def test_reused_weight_gradient_storage_gives_the_same_training():
     """With `reuse_weight_gradient` and `reuse_activation_buffer` (set by PackTrainer) each
-    step's weight gradients and block outputs are written into the previous step's storage,
-    active blocks / member columns only: three bf16 Muon training steps of a ragged,
+    step's weight gradients, block outputs and input gradients are written into the previous
+    step's storage, active blocks / member column tiles only: three bf16 Muon training steps of a ragged,
     depth-gated TabPack give bit-identical parameters to the same steps with fresh, fully
     written tensors, and the storage is indeed reused; after the layer's widths change
     (`replace`) the buffers are rebuilt."""
@@ -346,6 +346,7 @@ def test_reused_weight_gradient_storage_gives_the_same_training():
                 m.reuse_weight_gradient = reuse
         for blk in model.backbone.blocks:
             blk.linear.reuse_activation_buffer = reuse
+        model.output.reuse_activation_buffer = reuse  # its input gradient
         groups = [bopt.MuonAdamWPack.make_muon_parameter_group(b.linear) for b in model.backbone.blocks]
         muon = {id(gr['params'][0]) for gr in groups}
         groups.append({'params': [q for q in model.parameters() if id(q) not in muon]})
@@ -358,18 +359,19 @@ def test_reused_weight_gradient_storage_gives_the_same_training():
                 model.backbone._stream.seed, model.backbone._stream.calls = 13, step
                 out = model.forward_rows(x_num, x_cat, idx)
             ((out.float().squeeze(-1) - y[idx]) ** 2).mean(1).sum().backward()
-            y_slot = model.backbone.blocks[2].linear._y_slot
+            slots = model.backbone.blocks[2].linear._y_slot
             ptrs.append((model.backbone.blocks[1].linear.weight.grad.data_ptr(),
-                         y_slot['storage'].data_ptr() if y_slot else None))
+                         slots['y']['storage'].data_ptr() if slots else None,
+                         slots['dx']['storage'].data_ptr() if slots else None))
             opt.step()
             opt.zero_grad()
         runs.append(({n: q.detach().clone() for n, q in model.named_parameters()}, ptrs, model))
     (pa, _, _), (pb, ptrs, model) = runs
     for n in pa:
         assert torch.equal(pa[n], pb[n]), n
-    assert ptrs[0] == ptrs[1] == ptrs[2] and ptrs[0][1] is not None
+    assert ptrs[0] == ptrs[1] == ptrs[2] and ptrs[0][1] is not None and ptrs[0][2] is not None
     slot = model.backbone.blocks[1].linear._dw_slot
-    y_slot = model.backbone.blocks[1].linear._y_slot
+    y_slot = model.backbone.blocks[1].linear._y_slot['y']
     key, y_key = slot['key'], y_slot['key']
     model.backbone.blocks[1].linear.replace(pack_idx=torch.tensor([1], device='cuda'), out_features=[64])
     idx = torch.randint(0, N, (P, B), device='cuda', generator=g)

@@ -425,3 +425,35 @@ def test_grouped_muon_equals_one_call_per_group():
             assert torch.equal(a[k].view(torch.int16) if a[k].dtype == torch.bfloat16 else a[k].view(torch.int32),
                                b[k].view(torch.int16) if b[k].dtype == torch.bfloat16 else b[k].view(torch.int32)), (i, k)
         assert not torch.equal(a['p'], groups[i]['p'])
+
+
+def test_muon_step_skips_gated_members_with_zero_momentum():
+    """`gated_momentum_zero`: depth-gated members whose momentum is zero take only the weight
+    decay; the step reads neither their gradient nor their momentum and gives exactly the
+    results of the step that reads both (two steps, a bf16 copy, Nesterov)."""
+    from tabpack_b200 import ops
+
+    P, O, I = 7, 160, 96
+    gen = torch.Generator(device='cuda').manual_seed(31)
+    outf = torch.tensor([160, 64, 128, 8, 96, 160, 40], dtype=torch.int32, device='cuda')
+    inf = torch.tensor([96, 40, 96, 16, 72, 8, 96], dtype=torch.int32, device='cuda')
+    nb = torch.tensor([3, 1, 2, 1, 1, 4, 2], dtype=torch.int32, device='cuda')  # block 1: members 1, 3, 4 gated
+    valid = ((torch.arange(O, device='cuda')[None, :, None] < outf[:, None, None])
+             & (torch.arange(I, device='cuda')[None, None, :] < inf[:, None, None]))
+    p0 = torch.randn(P, O, I, device='cuda', generator=gen) * 0.05
+    g = torch.randn(P, O, I, device='cuda', generator=gen) * 1e-3 * valid
+    g[nb <= 1] = 0.0
+    lr = torch.rand(P, device='cuda', generator=gen) * 0.02 + 1e-3
+    out = []
+    for skip in (False, True):
+        p, m = p0.clone(), torch.zeros(P, O, I, device='cuda')
+        copy = torch.zeros(P, O, I, dtype=torch.bfloat16, device='cuda')
+        for _ in range(2):
+            ops.muon_step(p, g.clone(), m, out_features=outf, in_features=inf, lr=lr, momentum=0.95,
+                          weight_decay=1e-2, nesterov=True, mutate_grad=False, ns_steps=5, p_bf16=copy,
+                          n_blocks=nb, block_index=1, gated_momentum_zero=skip)
+        torch.cuda.synchronize()
+        out.append((p, m, copy))
+    (pa, ma, ca), (pb, mb, cb) = out
+    assert torch.equal(pa, pb) and torch.equal(ma, mb) and torch.equal(ca, cb)
+    assert not torch.equal(pa[0], p0[0])
