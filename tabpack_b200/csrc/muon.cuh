@@ -77,6 +77,7 @@ constexpr int NS_LISTS = 6;
 struct NsTileLists {
   uint32_t* list[NS_LISTS];
   int* counts;
+  int build[2];  // write the lists of 128-row (build[0]) / 256-row (build[1]) tiles (lengths always)
 };
 
 __device__ __forceinline__ int ns_sym_mtiles(int nt, int mt_all, int tm) {
@@ -141,6 +142,7 @@ __global__ void __launch_bounds__(1024) ns_tile_list_kernel(MuonArgs a, NsTileLi
     const uint32_t mk = (uint32_t)m << 16;
 #pragma unroll
     for (int g = 0; g < 2; ++g) {
+      if (!L.build[g]) continue;
       const int tm = NS_TILE_M << g, mtg = max(mt[g], 1);
       uint32_t* rr = L.list[3 * g];
       uint32_t* rc = L.list[3 * g + 1];
@@ -163,6 +165,7 @@ __global__ void __launch_bounds__(1024) ns_tile_list_kernel(MuonArgs a, NsTileLi
 // l + 96, so each load instruction covers 128 contiguous bytes and a thread has 16 elements
 // (32 loads in the prologue) in flight.
 constexpr int MUON_TM = 32, MUON_TN = 128;
+constexpr int MUON_NORM_ROWS = 64;  // rows of a normalisation block
 constexpr int MUON_UB_LD = MUON_TN + 8;  // bf16 staging row (16-byte aligned rows)
 
 // The oriented operand X of the tile (o0, n0) from / to the staged bf16 update ub[o][n]:
@@ -305,8 +308,8 @@ __global__ void __launch_bounds__(256) muon_norm_kernel(MuonArgs a, int tiles_x)
 
 // X <- bf16(X / bf16(bf16(||X||_F) + 1e-7)) on the member's r x c block and exact zeros
 // on [0, R_s-tile) x [0, C_s-tile) around it (the Newton-Schulz GEMMs read those pads
-// along K).  Grid: (ceil(C_s / 256), ceil(R_s / 32), P), 256 threads; a warp covers rows
-// w, w + 8, w + 16, w + 24 of the block's 32, a lane 8 columns (16 bytes) of each.
+// along K).  Grid: (ceil(C_s / 256), ceil(R_s / MUON_NORM_ROWS), P), 256 threads; warp w covers
+// rows w, w + 8, ... of the block's MUON_NORM_ROWS, a lane 8 columns (16 bytes) of each.
 // x / den from rcp = 1 / den (correctly rounded) with one fused correction step: q = x * rcp,
 // then q + (x - q den) * rcp.  Markstein's method (P. Markstein, "Computation of elementary
 // functions on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): the
@@ -363,7 +366,7 @@ __global__ void __launch_bounds__(256) muon_normalize_kernel(MuonArgs a, int row
   const int r = a.rows[mem], c = a.cols[mem];
   const int rr = min(a.R_s, (r + row_pad - 1) / row_pad * row_pad);
   const int cc = min(a.C_s, (c + col_pad - 1) / col_pad * col_pad);
-  const int row0 = blockIdx.y * 32;
+  const int row0 = blockIdx.y * MUON_NORM_ROWS;
   const int col = blockIdx.x * 256 + (threadIdx.x & 31) * 8;
   if (row0 >= rr || col >= cc) return;
   const float nrm2 = a.norm2[mem];
@@ -372,15 +375,16 @@ __global__ void __launch_bounds__(256) muon_normalize_kernel(MuonArgs a, int row
   const float den = __bfloat162float(__float2bfloat16_rn(nrm + 1e-7f));
   // x / den per element from one division per thread (quotient_from_reciprocal)
   const float rcp = 1.0f / den;
-  uint4 u[4];
+  constexpr int RPT = MUON_NORM_ROWS / 8;  // rows per thread, all loaded before any is written
+  uint4 u[RPT];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < RPT; ++i) {
     const int row = row0 + (threadIdx.x >> 5) + 8 * i;
     u[i] = make_uint4(0, 0, 0, 0);
     if (row < r && col < c) u[i] = *reinterpret_cast<const uint4*>(a.x + (size_t)mem * a.R_s * a.C_s + (size_t)row * a.C_s + col);
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < RPT; ++i) {
     const int row = row0 + (threadIdx.x >> 5) + 8 * i;
     if (row >= rr) continue;
     __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&u[i]);

@@ -861,7 +861,7 @@ void muon_bind(MuonArgs& m, const MuonLayout& L, uint8_t* ws, int first, size_t 
 // (rows_ext, cols_ext) bound the normalisation grid (the group's own operand extent).
 void muon_prepare(const MuonArgs& m, int rows_ext, int cols_ext, cudaStream_t st) {
   dim3 tiles((m.max_in + MUON_TN - 1) / MUON_TN, (m.max_out + MUON_TM - 1) / MUON_TM, m.P);
-  dim3 ngrid((cols_ext + 255) / 256, (rows_ext + 31) / 32, m.P);
+  dim3 ngrid((cols_ext + 255) / 256, (rows_ext + MUON_NORM_ROWS - 1) / MUON_NORM_ROWS, m.P);
   TP_PROF(TP_PROF_MUON_ELEMENTWISE, st);
   muon_geometry_kernel<<<(m.P + 255) / 256, 256, 0, st>>>(m);
   muon_prologue_kernel<<<tiles, 256, 0, st>>>(m);
@@ -901,6 +901,10 @@ int muon_newton_schulz(const MuonArgs& mu, const MuonLayout& L, uint8_t* ws, int
   for (int j = 0; j < NS_LISTS; ++j) lists.list[j] = reinterpret_cast<uint32_t*>(ws + L.off_list[j]);
   lists.counts = reinterpret_cast<int*>(ws + L.off_list_n);
   const int* list_n = lists.counts;
+  // which of the three products run on CTA pairs (256-row tiles)
+  const int pairs = ns_pair_products();
+  lists.build[0] = (pairs & 7) != 7;
+  lists.build[1] = (pairs & 7) != 0;
   {
     TP_PROF(TP_PROF_MUON_ELEMENTWISE, st);
     ns_tile_list_kernel<<<1, 1024, 0, st>>>(mu, lists);
@@ -922,8 +926,6 @@ int muon_newton_schulz(const MuonArgs& mu, const MuonLayout& L, uint8_t* ws, int
       return nullptr;
     return counters + (launch++ % MUON_COUNTERS);
   };
-  // which of the three products run on CTA pairs (256-row tiles)
-  const int pairs = ns_pair_products();
   const int sym_l = (pairs & 1) ? 5 : 2, b_l = (pairs & 2) ? 5 : 2, x_l = (pairs & 4) ? 4 : 1;
   for (int it = 0; it < ns_steps; ++it) {
     int* c1 = counter();
