@@ -7,7 +7,7 @@
 // written at column f * D + k of the member's output row, so the flattened embedding lands
 // directly in the first layer's input (the one-hot block can follow in the same buffer).
 //
-// Backward, per (m, f, k), sums over the batch rows in fp64:
+// Backward, per (m, f, k), sums over the batch rows (fp32 runs of 16 rows added in fp64):
 //   dab_k = [k < d] sum g,  daw_k = [k < d] sum g cat_k,
 //   dz_k = g aw'_k (-sin z_k),  dw[k-1] = 2pi sum dz_k x,  db[k-1] = 2pi sum dz_k.
 // Threads own one column (f, k) each and walk the rows, so parameter loads happen once per
@@ -144,18 +144,34 @@ struct CosEmbSums {
   double ab, aw, w, b;
 };
 
-__device__ __forceinline__ void cos_emb_accumulate(const CosEmbCol& c, float g, float x, CosEmbSums& s) {
-  s.ab += (double)g;
+// The same four sums over a run of at most COS_EMB_RUN rows in fp32, added to the fp64 sums
+// at the end of the run: one conversion per sum and run instead of one per product (the
+// conversions share the conversion unit with the sine and cosine).
+struct CosEmbRun {
+  float ab, aw, w, b;
+};
+constexpr int COS_EMB_RUN = 16;
+
+__device__ __forceinline__ void cos_emb_accumulate(const CosEmbCol& c, float g, float x, CosEmbRun& s) {
+  s.ab += g;
   if (c.k == 0) {
-    s.aw += (double)g * (double)x;
+    s.aw = fmaf(g, x, s.aw);
   } else {
     float sn, cs;
     __sincosf(cos_emb_reduce(c.b2 + c.w2 * x), &sn, &cs);
-    s.aw += (double)g * (double)cs;
-    const double dz = -(double)g * (double)c.aw * (double)sn;
-    s.w += dz * (double)x;
+    s.aw = fmaf(g, cs, s.aw);
+    const float dz = -(g * c.aw) * sn;
+    s.w = fmaf(dz, x, s.w);
     s.b += dz;
   }
+}
+
+__device__ __forceinline__ void cos_emb_flush(CosEmbRun& run, CosEmbSums& s) {
+  s.ab += (double)run.ab;
+  s.aw += (double)run.aw;
+  s.w += (double)run.w;
+  s.b += (double)run.b;
+  run = CosEmbRun{0.0f, 0.0f, 0.0f, 0.0f};
 }
 
 __device__ __forceinline__ void cos_emb_write_sums(const CosEmbArgs& a, int m, int j, const CosEmbCol& c,
@@ -182,11 +198,12 @@ __device__ __forceinline__ void cos_emb_write_sums(const CosEmbArgs& a, int m, i
 }
 
 // Grid: (ceil(F * D / COS_EMB_THREADS), P, segments), one column a thread (two columns a thread
-// measured slower: twice the fp64 accumulation chains per thread).  One block row segment per
+// measured slower: twice the accumulation chains per thread).  One block row segment per
 // z; with gridDim.z == 1 the sums are final, otherwise they go to `partial` and
 // cos_emb_finish_kernel adds the segments in order.
 // The gradient's type is a template parameter and the row pointers advance by increments;
-// rows are accumulated in order, four loaded at a time.
+// rows are accumulated in order, eight loaded at a time, in fp32 runs of COS_EMB_RUN rows whose
+// sums are added in fp64.
 template <bool G_BF16>
 __global__ void __launch_bounds__(COS_EMB_THREADS) cos_emb_backward_kernel(const CosEmbArgs a) {
   using T = typename std::conditional<G_BF16, __nv_bfloat16, float>::type;
@@ -206,18 +223,23 @@ __global__ void __launch_bounds__(COS_EMB_THREADS) cos_emb_backward_kernel(const
       return v;
   };
   CosEmbSums sums{0.0, 0.0, 0.0, 0.0};
+  CosEmbRun run{0.0f, 0.0f, 0.0f, 0.0f};
   int r = r0;
-  for (; r + 4 <= r1; r += 4, xp += 4 * F, gp += 4 * ld) {
-    float gv[4], xv[4];
+  constexpr int NR = 8;  // rows loaded ahead
+  static_assert(COS_EMB_RUN % NR == 0, "runs hold whole row groups");
+  for (; r + NR <= r1; r += NR, xp += NR * F, gp += NR * ld) {
+    float gv[NR], xv[NR];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < NR; ++i) {
       gv[i] = gval(gp[i * ld]);
       xv[i] = xp[i * F];
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) cos_emb_accumulate(c, gv[i], xv[i], sums);
+    for (int i = 0; i < NR; ++i) cos_emb_accumulate(c, gv[i], xv[i], run);
+    if (((r + NR - r0) % COS_EMB_RUN) == 0) cos_emb_flush(run, sums);
   }
-  for (; r < r1; ++r, xp += F, gp += ld) cos_emb_accumulate(c, gval(*gp), *xp, sums);
+  for (; r < r1; ++r, xp += F, gp += ld) cos_emb_accumulate(c, gval(*gp), *xp, run);
+  cos_emb_flush(run, sums);
   cos_emb_write_sums(a, m, j, c, sums);
 }
 

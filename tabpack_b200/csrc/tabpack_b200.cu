@@ -1199,7 +1199,8 @@ int tp_softmax_rows(const float* x, int64_t rows, int32_t C, float* out, void* s
 static int cos_emb_segments(int P, int B, int F, int D) {
   const long long cols = ((long long)F * D + COS_EMB_THREADS - 1) / COS_EMB_THREADS;
   const long long base = cols * P;
-  long long s = (148 * 16 + base - 1) / base;
+  // about four waves of 128-thread blocks (16 per SM): a single wave left a third of it as tail
+  long long s = (148 * 16 * 4 + base - 1) / base;
   s = std::min<long long>(s, (B + 63) / 64);
   return (int)std::max<long long>(1, s);
 }
