@@ -732,7 +732,11 @@ class LinearPack(ModulePack):
 
 
 def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stream, n_blocks, block_index,
-                 offset_stride: int = 1, offset_add: int = 0, dx_cols: int = 0, row_index: Tensor | None = None):
+                 offset_stride: int = 1, offset_add: int = 0, dx_cols: int = 0, row_index: Tensor | None = None,
+                 narrow: tuple[int | None, int | None] | None = None):
+    """`narrow` = (out, in): with a member selection, the selected weights are cut to their
+    first `out` rows / `in` columns (None: all), so the selected members' layer runs with
+    those maximum widths (they must cover every selected member's widths)."""
     w, b = linear.weight, linear.bias
     if row_index is not None and pack_idx is not None:
         raise ValueError('a gathered input runs on the whole pack')
@@ -745,6 +749,16 @@ def _linear_call(linear: LinearPack, x: Tensor, pack_idx, *, relu, dropout, stre
         if dropout is not None:
             raise NotImplementedError('pack_idx with training-mode dropout is not supported; '
                                       'use temporarily_select or remove')
+        if narrow is not None:
+            n_out, n_in = narrow
+            if n_out is not None:
+                w = w[:, :n_out]
+                b = None if b is None else b[:, :n_out].contiguous()
+            if n_in is not None:
+                w = w[:, :, :n_in]
+            w = w.contiguous()
+    elif narrow is not None:
+        raise ValueError('narrowed widths need a member selection')
     if row_index is not None:
         pass  # x is the gathered table
     elif x.ndim == 3 and x.shape[0] == 1 and w.shape[0] != 1:
@@ -864,7 +878,8 @@ class MLPBackbonePack(ModulePack):
 
         def forward(self, x: Tensor, pack_idx: Tensor | None = None, *, n_blocks: Tensor | None = None,
                     block_index: int = 0, stream: _DropoutStream | None = None, offset_stride: int = 1,
-                    onehot: dict | None = None, dx_cols: int = 0, row_index: Tensor | None = None) -> Tensor:
+                    onehot: dict | None = None, dx_cols: int = 0, row_index: Tensor | None = None,
+                    narrow: tuple[int | None, int | None] | None = None) -> Tensor:
             drop = None
             if self.training:
                 drop = self.dropout.probabilities(self.pack_size, x.device).contiguous()
@@ -877,7 +892,7 @@ class MLPBackbonePack(ModulePack):
             return _linear_call(self.linear, x, pack_idx, relu=self._fused_relu(), dropout=drop,
                                 stream=stream or self.dropout._stream, n_blocks=n_blocks, block_index=block_index,
                                 offset_stride=offset_stride, offset_add=block_index, dx_cols=dx_cols,
-                                row_index=row_index)
+                                row_index=row_index, narrow=narrow)
 
     @enum.unique
     class ForwardImpl(enum.StrEnum):
@@ -963,11 +978,13 @@ class MLPBackbonePack(ModulePack):
         return self._nb_cache[1]
 
     def forward(self, x: Tensor, pack_idx: Tensor | None = None, *, onehot: dict | None = None,
-                dx_cols: int = 0, row_index: Tensor | None = None) -> Tensor:
+                dx_cols: int = 0, row_index: Tensor | None = None, max_width: int | None = None) -> Tensor:
         """`onehot`: the first block's one-hot columns, gathered instead of multiplied (`x` then
         holds only the dense columns; see `_onehot_linear_call`).  `dx_cols`: the input's
         gradient is needed in its first dx_cols columns only.  `row_index` (pack_size, batch):
-        `x` is a (rows, in) table whose rows the first block's GEMMs gather."""
+        `x` is a (rows, in) table whose rows the first block's GEMMs gather.  `max_width`
+        (with `pack_idx`): the selected members' blocks run with this maximum width (at least
+        every selected member's), so their activations are no wider."""
         if pack_idx is not None:
             check_pack_idx(pack_idx, self.pack_size)
             if onehot is not None:
@@ -986,6 +1003,8 @@ class MLPBackbonePack(ModulePack):
                 first['dx_cols'] = dx_cols
             if i == 0 and row_index is not None:
                 first['row_index'] = row_index
+            if max_width is not None:
+                first['narrow'] = (max_width, None if i == 0 else max_width)
             x = block(x, pack_idx, n_blocks=nb if i > 0 else None, block_index=i, stream=sub, **first)
         return x
 
@@ -1430,9 +1449,23 @@ class TabPack(ModulePack):
         self.backbone.replace(pack_idx=pack_idx, d_in=d_in, d_block=d_block, **kwargs)
         self.output.replace(pack_idx=pack_idx, in_features=d_block)
 
-    def forward(self, x_num: Tensor | None, x_cat: Tensor | None, pack_idx: Tensor | None = None) -> Tensor:
+    def _head(self, h: Tensor, pack_idx: Tensor | None, max_width: int | None) -> Tensor:
+        if max_width is None:
+            return self.output(h, pack_idx)
+        return _linear_call(self.output, h, pack_idx, relu=False, dropout=None, stream=None, n_blocks=None,
+                            block_index=0, narrow=(None, max_width))
+
+    def forward(self, x_num: Tensor | None, x_cat: Tensor | None, pack_idx: Tensor | None = None, *,
+                max_width: int | None = None) -> Tensor:
+        """`max_width` (evaluation with `pack_idx`): the selected members' hidden width bound; the
+        backbone and the head then run with that maximum width instead of `max_d_block`, which
+        leaves every member's output unchanged and its activations narrower."""
         if x_num is None and x_cat is None:
             raise ValueError('Provide at least one of `x_num` and `x_cat`')
+        if max_width is not None:
+            if pack_idx is None or self.training:
+                raise ValueError('max_width applies to an evaluation-mode forward of selected members')
+            max_width = min(int(max_width), self.backbone.blocks[0].linear.max_out_features)
         # per-member batches are a training-time input (PackView, `nn.py:88-131`); a shared batch
         # may still become per-member inside (numerical embeddings)
         if not self.training and any(t is not None and t.ndim == 3 for t in (x_num, x_cat)):
@@ -1442,10 +1475,11 @@ class TabPack(ModulePack):
             return y
         emb = self._embedded_input(x_num, x_cat, None, pack_idx)
         if emb is not None:
-            return self.output(self.backbone(emb[0], pack_idx, dx_cols=emb[1]), pack_idx)
+            return self._head(self.backbone(emb[0], pack_idx, dx_cols=emb[1], max_width=max_width), pack_idx,
+                              max_width)
         fused = None if x_cat is None else self._fused_input(x_num, x_cat)
         if fused is not None:
-            return self.output(self.backbone(fused, pack_idx), pack_idx)
+            return self._head(self.backbone(fused, pack_idx, max_width=max_width), pack_idx, max_width)
         parts = []
         if x_num is not None:
             if self.num_module is None:
@@ -1465,5 +1499,5 @@ class TabPack(ModulePack):
                 oh = oh.expand(parts[0].shape[0], *oh.shape)
             parts.append(oh)
         x = torch.cat(parts, -1) if len(parts) > 1 else parts[0]
-        x = self.backbone(x, pack_idx)
-        return self.output(x, pack_idx)
+        x = self.backbone(x, pack_idx, max_width=max_width)
+        return self._head(x, pack_idx, max_width)

@@ -367,26 +367,49 @@ class PackTrainer:
         return gather_members(mean, self.counts, self.group) if self.world > 1 else mean
 
     # ------------------------------------------------------------------ evaluation
+    def _width_chunks(self, member_chunk: int) -> list[tuple[Tensor, int]]:
+        """Member groups of `member_chunk` members in order of hidden width, each with its
+        widest member's width (rounded up to 8): a group then runs with that maximum width
+        instead of the pack's, so its activations are only as wide as its members need."""
+        P = self.hi - self.lo
+        outf = self.model.backbone.blocks[0].linear.out_features
+        widths = outf.tolist() if outf is not None else [self.model.backbone.blocks[0].linear.max_out_features] * P
+        order = sorted(range(P), key=lambda m: (widths[m], m))
+        chunks = []
+        for c in range(0, P, member_chunk):
+            members = order[c: c + member_chunk]
+            mw = -(-max(widths[m] for m in members) // 8) * 8
+            chunks.append((torch.tensor(members, device=self.device), mw))
+        return chunks
+
     @torch.no_grad()
     def predict_local(self, data: dict, *, eval_batch_size: int = 32768, member_chunk: int | None = None) -> Tensor:
         """Transformed predictions of this rank's members on a shared dataset.  `member_chunk`
         runs the members in groups of that size (bounds the activations of wide packs on large
-        batches: each group is a `pack_idx` selection of the pack)."""
+        batches: each group is a `pack_idx` selection of the pack, of members of similar width
+        that run with their own maximum width)."""
         self.model.eval()
         n = len(data['y']) if 'y' in data else len(next(iter(data.values())))
         P = self.hi - self.lo
-        chunks = [None] if member_chunk is None or member_chunk >= P else [
-            torch.arange(c, min(P, c + member_chunk), device=self.device) for c in range(0, P, member_chunk)]
+        chunks = None if member_chunk is None or member_chunk >= P else self._width_chunks(member_chunk)
         parts = []
         for i in range(0, n, eval_batch_size):
             xn = data['x_num'][i: i + eval_batch_size] if 'x_num' in data else None
             xc = data['x_cat'][i: i + eval_batch_size] if 'x_cat' in data else None
-            outs = []
-            for idx in chunks:
-                with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16, enabled=self.autocast):
-                    out = self.model(xn, xc, idx)
-                outs.append(transform(self.loss, out.float()))
-            parts.append(outs[0] if len(outs) == 1 else torch.cat(outs, 0))
+            if chunks is None:
+                with torch.autocast('cuda', dtype=torch.bfloat16, enabled=self.autocast):
+                    out = self.model(xn, xc)
+                parts.append(transform(self.loss, out.float()))
+                continue
+            full = None
+            for idx, mw in chunks:
+                with torch.autocast('cuda', dtype=torch.bfloat16, enabled=self.autocast):
+                    out = self.model(xn, xc, idx, max_width=mw)
+                out = transform(self.loss, out.float())
+                if full is None:
+                    full = out.new_empty((P, *out.shape[1:]))
+                full.index_copy_(0, idx, out)
+            parts.append(full)
         return torch.cat(parts, 1)
 
     def _score(self, y_val: Tensor) -> PackScore:
