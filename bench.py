@@ -913,7 +913,9 @@ def run_train(args) -> None:
     dominant = max(gemm, key=lambda f: gemm[f]['ms_per_step'])
     roof = {'bound': 'tensor', 'achieved': gemm[dominant]['tflops'], 'peak': peak, 'unit': 'TFLOP/s',
             'frac': gemm[dominant]['frac'], 'kernel': dominant,
-            'traffic': TRAIN_TRAFFIC_BYTES_PER_STEP.get(dominant),
+            'traffic': (TRAIN_TRAFFIC_BYTES_PER_MEMBER_STEP[dominant] * (trainer.hi - trainer.lo)
+                        if dominant in TRAIN_TRAFFIC_BYTES_PER_MEMBER_STEP else None),
+            'traffic_per': 'step (all launches of the family on this rank)',
             'peak_source': f'{peak_kind} ({"sustained" if sustained else "burst"}: median SM clock '
                            f'{clk["sm_mhz"]} of {clk["sm_max_mhz"]} MHz in the region)'}
     cpu = None
@@ -948,9 +950,11 @@ def run_train(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-# DRAM bytes (read + write) per training step of the dominant kernel family, from the ncu
-# capture of the training workload's launches (64-member case scaled to 512 members).
-TRAIN_TRAFFIC_BYTES_PER_STEP: dict[str, float | None] = {}
+# DRAM bytes (read + write) per training step and member of a kernel family, from an ncu
+# capture of the training workload's launches at 64 members (the 15 Newton-Schulz launches of
+# one step: 7.528 GB, `dram__bytes_read.sum + dram__bytes_write.sum`), scaled by the members a
+# rank trains.
+TRAIN_TRAFFIC_BYTES_PER_MEMBER_STEP: dict[str, float] = {'newton_schulz': 7.528e9 / 64}
 
 
 def train_cpu_sample(cards: list[int], per: list[dict], *, budget_s: float, steps: int | None = None,
