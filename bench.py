@@ -882,6 +882,7 @@ def run_train(args) -> None:
     checksum = {'sha256_16': hashlib.sha256(final.tobytes()).hexdigest()[:16], 'sum': float(final.astype(np.float64).sum())}
     local_work = train_work(per[trainer.lo: trainer.hi], d_in)
     members_per_rank = [b - a for a, b in trainer.ranges]
+    local_members = trainer.hi - trainer.lo
     fam_ms = {k: kt.ms[k] / K for k in kt.ms if kt.launches[k]}
     fam_ms['newton_schulz'] = fam_ms.pop('newton_schulz_gram', 0.0) + fam_ms.pop('newton_schulz_update', 0.0)
     ns_exec = local_work.pop('newton_schulz_executed')
@@ -913,7 +914,7 @@ def run_train(args) -> None:
     dominant = max(gemm, key=lambda f: gemm[f]['ms_per_step'])
     roof = {'bound': 'tensor', 'achieved': gemm[dominant]['tflops'], 'peak': peak, 'unit': 'TFLOP/s',
             'frac': gemm[dominant]['frac'], 'kernel': dominant,
-            'traffic': (TRAIN_TRAFFIC_BYTES_PER_MEMBER_STEP[dominant] * (trainer.hi - trainer.lo)
+            'traffic': (TRAIN_TRAFFIC_BYTES_PER_MEMBER_STEP[dominant] * local_members
                         if dominant in TRAIN_TRAFFIC_BYTES_PER_MEMBER_STEP else None),
             'traffic_per': 'step (all launches of the family on this rank)',
             'peak_source': f'{peak_kind} ({"sustained" if sustained else "burst"}: median SM clock '
